@@ -1,0 +1,379 @@
+// Grouped-query attention of a block of query tokens against a per-sequence KV cache.
+//
+// Replaces mx.fast.scaled_dot_product_attention as called by the verify forward
+// (mlx-lm qwen3 Attention, mask "causal" from qwen3.create_attention_mask,
+// adapters.py:620) and by the DFlash draft (draft.py:149-157, mask none or causal).
+//
+//   o[m, h] = softmax_j( scale * q[m, h] . K[kvh(h), j] ) V[kvh(h), j],   j < lim(m)
+//   lim(m)  = pos[m] + 1           (causal: the key at the query's own position is the last one)
+//           = kv_len[seq(m)]       (non-causal)
+//
+// Layout: q [M][Hq][hd] bf16, caches [seq][Hkv][cap][hd] bf16 (slot == position).
+// Work split: one CTA per (key chunk of DFL_ATTN_CHUNK keys, kv head, 16-token
+// tile); warp w of the CTA owns q head kvh*G + w for the 16 tokens, so the G
+// query heads sharing a kv head read each K/V tile once. Chunks are fixed
+// absolute key ranges and are merged in chunk order by a second kernel, so a
+// query row's result does not depend on the other rows or on keys it cannot
+// see (spec-verify rows and plain-decode rows agree bit for bit).
+#include "common.cuh"
+
+namespace dfl {
+
+constexpr int ATT_CH = DFL_ATTN_CHUNK;  // keys per chunk
+constexpr int ATT_KB = 64;              // keys per shared-memory sub-block
+
+struct AttnArgs {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* k_cache;
+  const __nv_bfloat16* v_cache;
+  long long seq_stride, head_stride;
+  const int* pos;
+  const int* row_seq;
+  const int* kv_len;
+  float* part_o;   // [chunks][M][Hq][hd]
+  float2* part_ml; // [chunks][M][Hq]
+  __nv_bfloat16* out;
+  long long ldo;
+  int M, Hq, Hkv, G, causal, n_chunks;
+  float scale_log2;  // softmax scale * log2(e)
+};
+
+template <int HD>
+__device__ __forceinline__ int att_swz(int row, int c) {
+  return row * HD + ((c ^ (row & 7)) << 3);
+}
+
+__device__ __forceinline__ int row_limit(const AttnArgs& a, int m) {
+  if (m >= a.M) return 0;
+  const int p = a.pos[m];
+  if (p < 0) return 0;
+  if (a.causal) return p + 1;
+  const int s = a.row_seq ? a.row_seq[m] : 0;
+  return a.kv_len[s];
+}
+
+template <int HD>
+__global__ void __launch_bounds__(256) attn_chunk_kernel(AttnArgs a) {
+  grid_dependency_launch_dependents();
+  grid_dependency_wait();
+  constexpr int NC = HD / 8;  // 16-byte chunks per row
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(smem_raw);  // [G][16][HD]
+  __nv_bfloat16* sK = sQ + a.G * 16 * HD;                           // [2][64][HD]
+  __nv_bfloat16* sV = sK + 2 * ATT_KB * HD;                          // [2][64][HD]
+
+  const int chunk = blockIdx.x, kvh = blockIdx.y, tile = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nthr = blockDim.x;
+  const int m0 = tile * 16;
+
+  __shared__ int s_lim[16];
+  __shared__ int s_seq;
+  if (threadIdx.x < 16) s_lim[threadIdx.x] = row_limit(a, m0 + threadIdx.x);
+  if (threadIdx.x == 0) {
+    int s = 0;
+    for (int r = 0; r < 16; ++r) {
+      const int m = m0 + r;
+      if (m < a.M && a.pos[m] >= 0) { s = a.row_seq ? a.row_seq[m] : 0; break; }
+    }
+    s_seq = s;
+  }
+  __syncthreads();
+  int lim_max = 0;
+#pragma unroll
+  for (int r = 0; r < 16; ++r) lim_max = max(lim_max, s_lim[r]);
+  const int k_begin = chunk * ATT_CH;
+  if (k_begin >= lim_max) return;
+  const int k_end = min(k_begin + ATT_CH, lim_max);
+
+  const __nv_bfloat16* Kb = a.k_cache + s_seq * a.seq_stride + kvh * a.head_stride;
+  const __nv_bfloat16* Vb = a.v_cache + s_seq * a.seq_stride + kvh * a.head_stride;
+
+  // Q tile: rows are (head-in-group, token)
+  for (int idx = threadIdx.x; idx < a.G * 16 * NC; idx += nthr) {
+    const int c = idx % NC;
+    const int rr = idx / NC;  // hg*16 + r
+    const int hg = rr / 16, r = rr % 16;
+    const int m = m0 + r;
+    const bool ok = m < a.M && s_lim[r] > 0;
+    const __nv_bfloat16* src = a.q + ((long long)(ok ? m : 0) * a.Hq + kvh * a.G + hg) * HD + c * 8;
+    cp_async16(smem_u32(sQ + hg * 16 * HD + att_swz<HD>(r, c)), src, ok ? 16 : 0);
+  }
+  auto load_kv = [&](int buf, int kb) {
+    for (int idx = threadIdx.x; idx < ATT_KB * NC; idx += nthr) {
+      const int c = idx % NC, r = idx / NC;
+      const int key = kb + r;
+      const bool ok = key < k_end;
+      const long long off = (long long)(ok ? key : 0) * HD + c * 8;
+      cp_async16(smem_u32(sK + buf * ATT_KB * HD + att_swz<HD>(r, c)), Kb + off, ok ? 16 : 0);
+      cp_async16(smem_u32(sV + buf * ATT_KB * HD + att_swz<HD>(r, c)), Vb + off, ok ? 16 : 0);
+    }
+  };
+  load_kv(0, k_begin);
+  cp_async_commit();
+
+  const int g = lane >> 2, t = lane & 3;
+  const int lim0 = s_lim[g], lim1 = s_lim[g + 8];
+  float o[HD / 8][4];
+#pragma unroll
+  for (int j = 0; j < HD / 8; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[j][e] = 0.f;
+  float mrow[2] = {-INFINITY, -INFINITY};
+  float lrow[2] = {0.f, 0.f};
+  const __nv_bfloat16* myQ = sQ + warp * 16 * HD;
+
+  int buf = 0;
+  for (int kb = k_begin; kb < k_end; kb += ATT_KB, buf ^= 1) {
+    if (kb + ATT_KB < k_end) load_kv(buf ^ 1, kb + ATT_KB);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    const __nv_bfloat16* tK = sK + buf * ATT_KB * HD;
+    const __nv_bfloat16* tV = sV + buf * ATT_KB * HD;
+
+    float s[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s[j][e] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < HD / 16; ++ks) {
+      uint32_t af[4];
+      {
+        const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int c = 2 * ks + (lane >> 4);
+        ldmatrix_x4(smem_u32(myQ + att_swz<HD>(row, c)), af[0], af[1], af[2], af[3]);
+      }
+#pragma unroll
+      for (int nb = 0; nb < 4; ++nb) {
+        const int row = nb * 16 + (lane & 7) + (lane >> 4) * 8;
+        const int c = 2 * ks + ((lane >> 3) & 1);
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4(smem_u32(tK + att_swz<HD>(row, c)), b0, b1, b2, b3);
+        mma_bf16_16816(s[2 * nb], af, b0, b1);
+        mma_bf16_16816(s[2 * nb + 1], af, b2, b3);
+      }
+    }
+    // mask + online softmax (log2 domain)
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int key = kb + j * 8 + 2 * t;
+      s[j][0] = key < lim0 ? s[j][0] * a.scale_log2 : -INFINITY;
+      s[j][1] = key + 1 < lim0 ? s[j][1] * a.scale_log2 : -INFINITY;
+      s[j][2] = key < lim1 ? s[j][2] * a.scale_log2 : -INFINITY;
+      s[j][3] = key + 1 < lim1 ? s[j][3] * a.scale_log2 : -INFINITY;
+      mx0 = fmaxf(mx0, fmaxf(s[j][0], s[j][1]));
+      mx1 = fmaxf(mx1, fmaxf(s[j][2], s[j][3]));
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(mrow[0], mx0), mn1 = fmaxf(mrow[1], mx1);
+    const float mu0 = mn0 == -INFINITY ? 0.f : mn0, mu1 = mn1 == -INFINITY ? 0.f : mn1;
+    const float al0 = exp2f(mrow[0] - mu0), al1 = exp2f(mrow[1] - mu1);
+    mrow[0] = mn0;
+    mrow[1] = mn1;
+    float ps0 = 0.f, ps1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      s[j][0] = exp2f(s[j][0] - mu0);
+      s[j][1] = exp2f(s[j][1] - mu0);
+      s[j][2] = exp2f(s[j][2] - mu1);
+      s[j][3] = exp2f(s[j][3] - mu1);
+      ps0 += s[j][0] + s[j][1];
+      ps1 += s[j][2] + s[j][3];
+    }
+    lrow[0] = lrow[0] * al0 + ps0;
+    lrow[1] = lrow[1] * al1 + ps1;
+#pragma unroll
+    for (int j = 0; j < HD / 8; ++j) {
+      o[j][0] *= al0;
+      o[j][1] *= al0;
+      o[j][2] *= al1;
+      o[j][3] *= al1;
+    }
+    // O += P V
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      uint32_t pf[4];
+      pf[0] = pack_bf16x2(s[2 * kk][0], s[2 * kk][1]);
+      pf[1] = pack_bf16x2(s[2 * kk][2], s[2 * kk][3]);
+      pf[2] = pack_bf16x2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      pf[3] = pack_bf16x2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+      for (int dp = 0; dp < HD / 16; ++dp) {
+        const int row = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int c = 2 * dp + (lane >> 4);
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4_trans(smem_u32(tV + att_swz<HD>(row, c)), b0, b1, b2, b3);
+        mma_bf16_16816(o[2 * dp], pf, b0, b1);
+        mma_bf16_16816(o[2 * dp + 1], pf, b2, b3);
+      }
+    }
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+
+  lrow[0] += __shfl_xor_sync(0xffffffffu, lrow[0], 1);
+  lrow[0] += __shfl_xor_sync(0xffffffffu, lrow[0], 2);
+  lrow[1] += __shfl_xor_sync(0xffffffffu, lrow[1], 1);
+  lrow[1] += __shfl_xor_sync(0xffffffffu, lrow[1], 2);
+
+  const int h = kvh * a.G + warp;
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const int r = g + half * 8;
+    const int m = m0 + r;
+    if (m >= a.M || s_lim[r] <= k_begin) continue;
+    const long long base = ((long long)chunk * a.M + m) * a.Hq + h;
+    float* po = a.part_o + base * HD;
+#pragma unroll
+    for (int j = 0; j < HD / 8; ++j) {
+      *reinterpret_cast<float2*>(po + j * 8 + 2 * t) = make_float2(o[j][2 * half], o[j][2 * half + 1]);
+    }
+    if (t == 0) a.part_ml[base] = make_float2(mrow[half], lrow[half]);
+  }
+}
+
+// Merge the chunk partials of one (row, head) in chunk order.
+template <int HD>
+__global__ void attn_combine_kernel(AttnArgs a) {
+  grid_dependency_launch_dependents();
+  grid_dependency_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long item = (long long)blockIdx.x * (blockDim.x >> 5) + warp;
+  if (item >= (long long)a.M * a.Hq) return;
+  const int m = (int)(item / a.Hq), h = (int)(item % a.Hq);
+  const int lim = row_limit(a, m);
+  if (lim <= 0) return;
+  const int nch = min((lim + ATT_CH - 1) / ATT_CH, a.n_chunks);
+  float mmax = -INFINITY;
+  for (int c = 0; c < nch; ++c) {
+    const float2 ml = a.part_ml[((long long)c * a.M + m) * a.Hq + h];
+    mmax = fmaxf(mmax, ml.x);
+  }
+  const float mu = mmax == -INFINITY ? 0.f : mmax;
+  constexpr int PER = HD / 32;
+  float acc[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) acc[i] = 0.f;
+  float den = 0.f;
+  for (int c = 0; c < nch; ++c) {
+    const long long base = ((long long)c * a.M + m) * a.Hq + h;
+    const float2 ml = a.part_ml[base];
+    const float w = exp2f(ml.x - mu);
+    den += w * ml.y;
+    const float* po = a.part_o + base * HD;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) acc[i] += w * po[lane + 32 * i];
+  }
+  const float inv = den > 0.f ? 1.f / den : 0.f;
+  __nv_bfloat16* dst = a.out + (long long)m * a.ldo + (long long)h * HD;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) dst[lane + 32 * i] = f2bf(acc[i] * inv);
+}
+
+template <int HD>
+static int launch_attn(AttnArgs a, int n_tiles, cudaStream_t st) {
+  const size_t smem = (size_t)(a.G * 16 * HD + 4 * ATT_KB * HD) * 2;
+  static bool init = false;
+  if (!init) {
+    cudaFuncSetAttribute(attn_chunk_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    init = true;
+  }
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.n_chunks, a.Hkv, n_tiles);
+  cfg.blockDim = dim3(32 * a.G);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, attn_chunk_kernel<HD>, a);
+  if (e != cudaSuccess) {
+    set_error("dfl_attention: chunk kernel launch failed: %s", cudaGetErrorString(e));
+    return DFL_ERR_CUDA;
+  }
+  const long long items = (long long)a.M * a.Hq;
+  cfg.gridDim = dim3((unsigned)((items + 7) / 8));
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = 0;
+  e = cudaLaunchKernelEx(&cfg, attn_combine_kernel<HD>, a);
+  if (e != cudaSuccess) {
+    set_error("dfl_attention: combine launch failed: %s", cudaGetErrorString(e));
+    return DFL_ERR_CUDA;
+  }
+  return DFL_OK;
+}
+
+}  // namespace dfl
+
+using namespace dfl;
+
+extern "C" size_t dfl_attention_workspace_bytes(int M, int Hq, int hd, int max_kv) {
+  if (M <= 0 || max_kv <= 0) return 0;
+  const size_t nch = (size_t)(max_kv + ATT_CH - 1) / ATT_CH;
+  const size_t o = nch * M * Hq * hd * sizeof(float);
+  const size_t ml = nch * M * Hq * sizeof(float2);
+  return ((o + 255) & ~(size_t)255) + ml;
+}
+
+extern "C" int dfl_attention(const void* q, const void* k_cache, const void* v_cache, int64_t seq_stride,
+                             int64_t head_stride, const int32_t* pos, const int32_t* row_seq, const int32_t* kv_len,
+                             int M, int Hq, int Hkv, int hd, int causal, float scale, int max_kv, void* out,
+                             int64_t ldo, void* workspace, size_t workspace_bytes, void* stream) {
+  if (M == 0) return DFL_OK;
+  if (!q || !k_cache || !v_cache || !pos || !out || (!causal && !kv_len) || M < 0 || Hkv <= 0 || Hq % Hkv) {
+    set_error("dfl_attention: bad arguments");
+    return DFL_ERR_INVALID;
+  }
+  const int G = Hq / Hkv;
+  if (G < 1 || G > 8) {
+    set_error("dfl_attention: query heads per kv head must be 1..8 (got %d)", G);
+    return DFL_ERR_UNSUPPORTED;
+  }
+  if (max_kv <= 0) {
+    set_error("dfl_attention: max_kv must be positive");
+    return DFL_ERR_INVALID;
+  }
+  const size_t need = dfl_attention_workspace_bytes(M, Hq, hd, max_kv);
+  if (!workspace || workspace_bytes < need) {
+    set_error("dfl_attention: workspace too small (%zu < %zu)", workspace_bytes, need);
+    return DFL_ERR_WORKSPACE;
+  }
+  AttnArgs a;
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.k_cache = static_cast<const __nv_bfloat16*>(k_cache);
+  a.v_cache = static_cast<const __nv_bfloat16*>(v_cache);
+  a.seq_stride = seq_stride;
+  a.head_stride = head_stride;
+  a.pos = pos;
+  a.row_seq = row_seq;
+  a.kv_len = kv_len;
+  a.n_chunks = (max_kv + ATT_CH - 1) / ATT_CH;
+  const size_t o_bytes = (size_t)a.n_chunks * M * Hq * hd * sizeof(float);
+  a.part_o = static_cast<float*>(workspace);
+  a.part_ml = reinterpret_cast<float2*>(static_cast<char*>(workspace) + ((o_bytes + 255) & ~(size_t)255));
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.ldo = ldo;
+  a.M = M;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.G = G;
+  a.causal = causal;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  const int n_tiles = (M + 15) / 16;
+  cudaStream_t st = as_stream(stream);
+  switch (hd) {
+    case 64: return launch_attn<64>(a, n_tiles, st);
+    case 128: return launch_attn<128>(a, n_tiles, st);
+    default:
+      set_error("dfl_attention: head_dim %d not supported (64, 128)", hd);
+      return DFL_ERR_UNSUPPORTED;
+  }
+}

@@ -1,0 +1,272 @@
+// Row-wise layer kernels of the Qwen3 / DFlash decoder layers.
+//
+//  * dfl_rmsnorm_bf16     - nn.RMSNorm / mx.fast.rms_norm (input_layernorm,
+//                           post_attention_layernorm, final norm, the draft's
+//                           hidden_norm: draft.py:167-171, 198-201)
+//  * dfl_embed_bf16       - nn.Embedding row gather (adapters.py:603-604, runtime.py:410)
+//  * dfl_qkv_rope_append  - per-head q_norm/k_norm, non-interleaved RoPE and the
+//                           KV-cache append of mlx-lm KVCache.update_and_fetch
+//                           (draft.py:123-147; mlx-lm qwen3 Attention)
+//
+// All kernels are one warp per row (or per row x head): the reduction order of a
+// row never depends on how many rows a launch carries.
+#include "common.cuh"
+
+namespace dfl {
+
+// -------------------------------------------------------------------------
+// RMSNorm: y = w * (x * rsqrt(mean(x^2) + eps)), fp32 math, one rounding.
+// -------------------------------------------------------------------------
+__global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, long long ldx, const __nv_bfloat16* __restrict__ w,
+                               __nv_bfloat16* __restrict__ y, long long ldy, int M, int H, float eps) {
+  grid_dependency_launch_dependents();
+  grid_dependency_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (blockDim.x >> 5) + warp;
+  if (row >= M) return;
+  const __nv_bfloat16* xr = x + (long long)row * ldx;
+  __nv_bfloat16* yr = y + (long long)row * ldy;
+  // H % 256 == 0 path: each lane owns 8-element vectors at stride 256
+  float ss = 0.f;
+  for (int c = lane * 8; c < H; c += 256) {
+    uint4 v = *reinterpret_cast<const uint4*>(xr + c);
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float f = bf2f(e[j]);
+      ss += f * f;
+    }
+  }
+  ss = warp_sum(ss);
+  const float inv = rsqrtf(ss / (float)H + eps);
+  for (int c = lane * 8; c < H; c += 256) {
+    uint4 v = *reinterpret_cast<const uint4*>(xr + c);
+    uint4 wv = w ? *reinterpret_cast<const uint4*>(w + c) : make_uint4(0, 0, 0, 0);
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v);
+    const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv);
+    uint4 o;
+    __nv_bfloat16* oe = reinterpret_cast<__nv_bfloat16*>(&o);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float wf = w ? bf2f(we[j]) : 1.f;
+      oe[j] = f2bf(wf * (bf2f(e[j]) * inv));
+    }
+    *reinterpret_cast<uint4*>(yr + c) = o;
+  }
+}
+
+// -------------------------------------------------------------------------
+// Embedding gather: y[r] = table[tok[r]]  (tok < 0 or >= V gives zeros)
+// -------------------------------------------------------------------------
+__global__ void embed_kernel(const int* __restrict__ tok, const __nv_bfloat16* __restrict__ table,
+                             __nv_bfloat16* __restrict__ y, long long ldy, int M, int H, int V) {
+  grid_dependency_launch_dependents();
+  grid_dependency_wait();
+  const int row = blockIdx.x;
+  if (row >= M) return;
+  const int t = tok[row];
+  __nv_bfloat16* yr = y + (long long)row * ldy;
+  for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (t >= 0 && t < V) v = *reinterpret_cast<const uint4*>(table + (long long)t * H + c);
+    *reinterpret_cast<uint4*>(yr + c) = v;
+  }
+}
+
+// -------------------------------------------------------------------------
+// q/k head RMSNorm + RoPE + KV append.
+//
+// qkv row layout: [q heads (Hq x q_stride, first hd of each is q) | k heads (Hkv x hd) | v heads (Hkv x hd)].
+// K/V cache layout per layer: [seq][Hkv][cap][hd] bf16; the token at position p
+// lives in slot p. pos[r] < 0 marks a row that is skipped entirely.
+// q_out: [M][Hq][hd] bf16.
+// -------------------------------------------------------------------------
+struct QkvArgs {
+  const __nv_bfloat16* qkv;
+  long long ldqkv;
+  int q_stride;  // elements between consecutive q heads inside a row (hd, or 2*hd with an output gate)
+  const int* pos;
+  const int* row_seq;  // nullable: all rows belong to sequence 0
+  const __nv_bfloat16* q_norm;
+  const __nv_bfloat16* k_norm;
+  const float* inv_freq;  // [rot_dim/2]
+  __nv_bfloat16* q_out;
+  __nv_bfloat16* k_cache;
+  __nv_bfloat16* v_cache;
+  long long seq_stride, head_stride;  // elements
+  int M, Hq, Hkv, hd, rot_dim;
+  float eps;
+  int do_q;  // 0: skip q heads (context rows of the draft)
+};
+
+__global__ void qkv_rope_append_kernel(QkvArgs a) {
+  grid_dependency_launch_dependents();
+  grid_dependency_wait();
+  extern __shared__ float sh[];  // [warps][hd]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nheads = a.Hq + 2 * a.Hkv;
+  const long long item = (long long)blockIdx.x * (blockDim.x >> 5) + warp;
+  if (item >= (long long)a.M * nheads) return;
+  const int row = (int)(item / nheads);
+  const int head = (int)(item % nheads);
+  const int p = a.pos[row];
+  if (p < 0) return;
+  const int seq = a.row_seq ? a.row_seq[row] : 0;
+  const __nv_bfloat16* src;
+  const __nv_bfloat16* nw = nullptr;
+  __nv_bfloat16* dst;
+  const __nv_bfloat16* qkv_row = a.qkv + (long long)row * a.ldqkv;
+  if (head < a.Hq) {
+    if (!a.do_q) return;
+    src = qkv_row + (long long)head * a.q_stride;
+    nw = a.q_norm;
+    dst = a.q_out + ((long long)row * a.Hq + head) * a.hd;
+  } else if (head < a.Hq + a.Hkv) {
+    const int kh = head - a.Hq;
+    src = qkv_row + (long long)a.Hq * a.q_stride + (long long)kh * a.hd;
+    nw = a.k_norm;
+    dst = a.k_cache + seq * a.seq_stride + kh * a.head_stride + (long long)p * a.hd;
+  } else {
+    const int vh = head - a.Hq - a.Hkv;
+    src = qkv_row + (long long)a.Hq * a.q_stride + (long long)(a.Hkv + vh) * a.hd;
+    dst = a.v_cache + seq * a.seq_stride + vh * a.head_stride + (long long)p * a.hd;
+    for (int i = lane; i < a.hd; i += 32) dst[i] = src[i];
+    return;
+  }
+  float* buf = sh + warp * a.hd;
+  float ss = 0.f;
+  for (int i = lane; i < a.hd; i += 32) {
+    const float f = bf2f(src[i]);
+    buf[i] = f;
+    ss += f * f;
+  }
+  ss = warp_sum(ss);
+  const float inv = rsqrtf(ss / (float)a.hd + a.eps);
+  for (int i = lane; i < a.hd; i += 32) buf[i] = round_bf16(bf2f(nw[i]) * (buf[i] * inv));
+  __syncwarp();
+  const int half = a.rot_dim >> 1;
+  for (int i = lane; i < a.hd; i += 32) {
+    float o = buf[i];
+    if (i < a.rot_dim) {
+      const int j = i < half ? i : i - half;
+      float s, c;
+      sincosf((float)p * a.inv_freq[j], &s, &c);
+      o = i < half ? buf[i] * c - buf[i + half] * s : buf[i] * c + buf[i - half] * s;
+    }
+    dst[i] = f2bf(o);
+  }
+}
+
+}  // namespace dfl
+
+using namespace dfl;
+
+extern "C" int dfl_rmsnorm_bf16(const void* x, int64_t ldx, const void* w, void* y, int64_t ldy, int M, int H,
+                                float eps, void* stream) {
+  if (M == 0) return DFL_OK;
+  if (!x || !y || M < 0 || H <= 0) {
+    set_error("dfl_rmsnorm_bf16: bad arguments");
+    return DFL_ERR_INVALID;
+  }
+  if (H % 256 || ldx % 8 || ldy % 8) {
+    set_error("dfl_rmsnorm_bf16: H must be a multiple of 256 and rows 16-byte aligned (H=%d)", H);
+    return DFL_ERR_UNSUPPORTED;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((M + 3) / 4);
+  cfg.blockDim = dim3(128);
+  cfg.stream = as_stream(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, rmsnorm_kernel, static_cast<const __nv_bfloat16*>(x), (long long)ldx,
+                                     static_cast<const __nv_bfloat16*>(w), static_cast<__nv_bfloat16*>(y),
+                                     (long long)ldy, M, H, eps);
+  if (e != cudaSuccess) {
+    set_error("dfl_rmsnorm_bf16: %s", cudaGetErrorString(e));
+    return DFL_ERR_CUDA;
+  }
+  return DFL_OK;
+}
+
+extern "C" int dfl_embed_bf16(const int32_t* tokens, const void* table, void* y, int64_t ldy, int M, int H, int V,
+                              void* stream) {
+  if (M == 0) return DFL_OK;
+  if (!tokens || !table || !y || H % 8 || ldy % 8) {
+    set_error("dfl_embed_bf16: bad arguments (H must be a multiple of 8)");
+    return DFL_ERR_INVALID;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(M);
+  cfg.blockDim = dim3(128);
+  cfg.stream = as_stream(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, embed_kernel, tokens, static_cast<const __nv_bfloat16*>(table),
+                                     static_cast<__nv_bfloat16*>(y), (long long)ldy, M, H, V);
+  if (e != cudaSuccess) {
+    set_error("dfl_embed_bf16: %s", cudaGetErrorString(e));
+    return DFL_ERR_CUDA;
+  }
+  return DFL_OK;
+}
+
+extern "C" int dfl_qkv_rope_append(const void* qkv, int64_t ldqkv, int q_stride, const int32_t* pos,
+                                   const int32_t* row_seq, const void* q_norm, const void* k_norm,
+                                   const float* inv_freq, void* q_out, void* k_cache, void* v_cache,
+                                   int64_t seq_stride, int64_t head_stride, int M, int Hq, int Hkv, int hd,
+                                   int rot_dim, float eps, int do_q, void* stream) {
+  if (M == 0) return DFL_OK;
+  if (!qkv || !pos || !q_norm || !k_norm || !inv_freq || !k_cache || !v_cache || (do_q && !q_out)) {
+    set_error("dfl_qkv_rope_append: null pointer");
+    return DFL_ERR_INVALID;
+  }
+  if (hd <= 0 || hd > 512 || rot_dim < 0 || rot_dim > hd || (rot_dim & 1) || Hq < 0 || Hkv <= 0) {
+    set_error("dfl_qkv_rope_append: bad head geometry hd=%d rot_dim=%d", hd, rot_dim);
+    return DFL_ERR_INVALID;
+  }
+  QkvArgs a;
+  a.qkv = static_cast<const __nv_bfloat16*>(qkv);
+  a.ldqkv = ldqkv;
+  a.q_stride = q_stride;
+  a.pos = pos;
+  a.row_seq = row_seq;
+  a.q_norm = static_cast<const __nv_bfloat16*>(q_norm);
+  a.k_norm = static_cast<const __nv_bfloat16*>(k_norm);
+  a.inv_freq = inv_freq;
+  a.q_out = static_cast<__nv_bfloat16*>(q_out);
+  a.k_cache = static_cast<__nv_bfloat16*>(k_cache);
+  a.v_cache = static_cast<__nv_bfloat16*>(v_cache);
+  a.seq_stride = seq_stride;
+  a.head_stride = head_stride;
+  a.M = M;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.hd = hd;
+  a.rot_dim = rot_dim;
+  a.eps = eps;
+  a.do_q = do_q;
+  const long long items = (long long)M * (Hq + 2 * Hkv);
+  const int warps = 8;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)((items + warps - 1) / warps));
+  cfg.blockDim = dim3(32 * warps);
+  cfg.dynamicSmemBytes = warps * hd * sizeof(float);
+  cfg.stream = as_stream(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, qkv_rope_append_kernel, a);
+  if (e != cudaSuccess) {
+    set_error("dfl_qkv_rope_append: %s", cudaGetErrorString(e));
+    return DFL_ERR_CUDA;
+  }
+  return DFL_OK;
+}

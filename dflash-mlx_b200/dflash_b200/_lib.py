@@ -1,0 +1,90 @@
+"""ctypes binding of the C ABI declared in include/dflash_b200.h.
+
+The shared library is built in-tree by ``_build.build()``. There is no CPU
+fallback: if the library is missing or a CUDA device is absent, every op raises.
+"""
+from __future__ import annotations
+
+import ctypes
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int64, c_size_t, c_void_p
+from pathlib import Path
+
+from ._build import LIB_PATH
+
+c_int32_p = POINTER(ctypes.c_int32)
+
+
+class DFlashKernelError(RuntimeError):
+    """A C-ABI entry point returned a non-zero status."""
+
+    def __init__(self, name: str, status: int, message: str):
+        super().__init__(f"{name} failed with status {status}: {message}")
+        self.status = status
+
+
+# name -> (restype, argtypes); mirrors include/dflash_b200.h
+SIGNATURES: dict[str, tuple] = {
+    "dfl_abi_version": (c_int, []),
+    "dfl_last_error": (c_char_p, []),
+    "dfl_gemm_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
+    "dfl_gemm_argmax_tiles": (c_int, [c_int]),
+    "dfl_gemm_bf16": (c_int, [c_void_p, c_int64, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int64, c_void_p,
+                              c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "dfl_rmsnorm_bf16": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int, c_int, c_float, c_void_p]),
+    "dfl_embed_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_int, c_void_p]),
+    "dfl_qkv_rope_append": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                    c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_int, c_int,
+                                    c_float, c_int, c_void_p]),
+    "dfl_attention_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
+    "dfl_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int,
+                              c_int, c_int, c_int, c_int, c_float, c_int, c_void_p, c_int64, c_void_p, c_size_t,
+                              c_void_p]),
+    "dfl_argmax_reduce": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p]),
+    "dfl_step_prepare": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_int, c_int, c_void_p, c_void_p, c_void_p,
+                                 c_void_p, c_int, c_void_p]),
+    "dfl_draft_commit": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int64, c_void_p, c_int64,
+                                 c_void_p, c_int64, c_int, c_void_p]),
+    "dfl_verify_accept": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int64, c_void_p, c_void_p,
+                                  c_int, c_void_p, c_int64, c_int, c_void_p]),
+    "dfl_gdr_recurrence": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p,
+                                   c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p]),
+}
+
+_LIB: ctypes.CDLL | None = None
+
+
+def library_path() -> Path:
+    return LIB_PATH
+
+
+def load(path: Path | str | None = None) -> ctypes.CDLL:
+    """Loads (once) the C-ABI library; raises if it has not been built."""
+    global _LIB
+    if _LIB is not None and path is None:
+        return _LIB
+    p = Path(path) if path is not None else LIB_PATH
+    if not p.exists():
+        raise RuntimeError(
+            f"dflash-b200 native library not found at {p}; build it with "
+            "`python -c 'import __graft_entry__ as g; g.build()'` (nvcc, sm_100a). There is no CPU fallback."
+        )
+    lib = ctypes.CDLL(str(p))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    if path is None:
+        _LIB = lib
+    return lib
+
+
+def call(name: str, *args) -> None:
+    lib = load()
+    status = getattr(lib, name)(*args)
+    if status != 0:
+        msg = lib.dfl_last_error().decode(errors="replace")
+        raise DFlashKernelError(name, status, msg)
+
+
+def query(name: str, *args):
+    return getattr(load(), name)(*args)

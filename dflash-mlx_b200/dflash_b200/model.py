@@ -1,0 +1,269 @@
+"""GPU Qwen3 target and DFlash draft built from the C-ABI kernels.
+
+HBM layout (per device):
+  * target layer l: ``w_qkv`` [(Hq+2Hkv)*hd, H] (q, k, v projections stacked),
+    ``w_o`` [H, Hq*hd], ``w_gu`` [2F, H] (gate/up packed per 64 rows as
+    [32 gate | 32 up] for the fused SiLU*up epilogue), ``w_down`` [H, F];
+  * KV cache: one tensor per K and V of shape [L, B, Hkv, cap, hd] bf16; the
+    token at position p of sequence b lives in slot p (rollback = length update);
+  * draft: per layer ``w_qkv``/``w_o``/``w_gu``/``w_down`` as above plus one
+    ``w_ctx_kv`` [n_layers*2*Hkv*hd, H] stacking every layer's k/v projection so
+    that the context rows (fc + hidden_norm of the target taps, the same input
+    for every draft layer: draft.py:217-222) are projected for all layers with
+    one weight stream.
+
+Forward semantics follow the reference: the target forward with hidden-state
+taps (adapters.py:611-631, mlx-lm qwen3 layers) and the DFlash draft
+(draft.py:109-223).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import ops
+from .config import DraftConfig, TargetConfig
+from .weights import pack_gate_up, rope_inv_freq
+
+
+@dataclass
+class KVCache:
+    """K/V slots [L, B, Hkv, cap, hd] bf16 and the host-side view of each sequence's length."""
+
+    k: torch.Tensor
+    v: torch.Tensor
+
+    @property
+    def cap(self) -> int:
+        return self.k.shape[3]
+
+    def layer(self, l: int) -> tuple[torch.Tensor, torch.Tensor]:
+        return self.k[l], self.v[l]
+
+
+def alloc_kv(n_layers: int, batch: int, n_kv: int, cap: int, hd: int, device) -> KVCache:
+    shape = (n_layers, batch, n_kv, cap, hd)
+    return KVCache(torch.zeros(shape, dtype=torch.bfloat16, device=device),
+                   torch.zeros(shape, dtype=torch.bfloat16, device=device))
+
+
+class TargetModel:
+    """Qwen3-family target: block forward with taps, KV append, fused lm_head argmax."""
+
+    def __init__(self, cfg: TargetConfig, weights: dict, device="cuda"):
+        if cfg.model_type != "qwen3":
+            raise NotImplementedError("TargetModel runs the dense qwen3 family; the hybrid lives in hybrid.py")
+        self.cfg = cfg
+        self.device = torch.device(device)
+        dev = self.device
+        self.embed_w = weights["embed"].to(dev).contiguous()
+        self.lm_head_w = self.embed_w if cfg.tie_word_embeddings else weights["lm_head"].to(dev).contiguous()
+        self.norm_w = weights["norm"].to(dev)
+        self.layers = []
+        for lw in weights["layers"]:
+            self.layers.append({
+                "in_norm": lw["input_layernorm"].to(dev),
+                "post_norm": lw["post_attention_layernorm"].to(dev),
+                "w_qkv": torch.cat([lw["q_proj"], lw["k_proj"], lw["v_proj"]], 0).to(dev).contiguous(),
+                "w_o": lw["o_proj"].to(dev).contiguous(),
+                "w_gu": pack_gate_up(lw["gate_proj"].to(dev), lw["up_proj"].to(dev)),
+                "w_down": lw["down_proj"].to(dev).contiguous(),
+                "q_norm": lw["q_norm"].to(dev),
+                "k_norm": lw["k_norm"].to(dev),
+            })
+        self.inv_freq = rope_inv_freq(cfg.rope_dim, cfg.rope_theta, dev)
+        self._bufs: dict[int, dict[str, torch.Tensor]] = {}
+
+    # ------------------------------------------------------------------
+    def make_cache(self, batch: int, cap: int) -> KVCache:
+        c = self.cfg
+        return alloc_kv(c.num_hidden_layers, batch, c.num_key_value_heads, cap, c.head_dim, self.device)
+
+    def buffers(self, M: int) -> dict[str, torch.Tensor]:
+        b = self._bufs.get(M)
+        if b is None:
+            c = self.cfg
+            dev = self.device
+            H, hd = c.hidden_size, c.head_dim
+            b = {
+                "h": torch.empty((M, H), dtype=torch.bfloat16, device=dev),
+                "xn": torch.empty((M, H), dtype=torch.bfloat16, device=dev),
+                "qkv": torch.empty((M, (c.num_attention_heads + 2 * c.num_key_value_heads) * hd), dtype=torch.bfloat16,
+                                   device=dev),
+                "q": torch.empty((M, c.num_attention_heads, hd), dtype=torch.bfloat16, device=dev),
+                "attn": torch.empty((M, c.num_attention_heads * hd), dtype=torch.bfloat16, device=dev),
+                "act": torch.empty((M, c.intermediate_size), dtype=torch.bfloat16, device=dev),
+                "argmax": torch.empty((M, ops.argmax_tiles(c.vocab_size), 2), dtype=torch.float32, device=dev),
+            }
+            self._bufs[M] = b
+        return b
+
+    def forward(self, tokens: torch.Tensor, pos: torch.Tensor, cache: KVCache, max_kv: int,
+                layer_ids: list[int] | None = None, taps_out: torch.Tensor | None = None,
+                row_seq: torch.Tensor | None = None, head: str = "argmax", ws: ops.Workspace | None = None):
+        """Block forward over M rows (tokens int32 [M] at positions pos [M]).
+
+        Appends K/V at each row's position, writes the residual stream after each
+        layer in ``layer_ids`` into ``taps_out[:, i*H:(i+1)*H]`` (ascending layer
+        order, adapters.py:624-630) and returns, by ``head``:
+          "argmax": DFL_EPI_ARGMAX partials of the lm_head (fused, no logits in HBM)
+          "logits": bf16 logits [M, V]
+          "hidden": the final-normed hidden states [M, H]
+        """
+        c = self.cfg
+        M = tokens.numel()
+        b = self.buffers(M)
+        H, hd = c.hidden_size, c.head_dim
+        Hq, Hkv = c.num_attention_heads, c.num_key_value_heads
+        tap_col = {}
+        if layer_ids:
+            for i, lid in enumerate(sorted(layer_ids)):
+                tap_col[lid] = i
+        h = b["h"]
+        ops.embed(tokens, self.embed_w, out=h)
+        for l, lw in enumerate(self.layers):
+            kc, vc = cache.layer(l)
+            ops.rmsnorm(h, lw["in_norm"], c.rms_norm_eps, out=b["xn"])
+            ops.gemm(b["xn"], lw["w_qkv"], out=b["qkv"], ws=ws)
+            ops.qkv_rope_append(b["qkv"], pos, lw["q_norm"], lw["k_norm"], self.inv_freq, kc, vc, Hq, Hkv, hd,
+                                c.rope_dim, c.rms_norm_eps, q_out=b["q"], row_seq=row_seq)
+            ops.attention(b["q"], kc, vc, pos, causal=True, max_kv=max_kv, row_seq=row_seq, out=b["attn"], ws=ws)
+            ops.gemm(b["attn"], lw["w_o"], ops.EPI_RESIDUAL, residual=h, out=h, ws=ws)
+            ops.rmsnorm(h, lw["post_norm"], c.rms_norm_eps, out=b["xn"])
+            ops.gemm(b["xn"], lw["w_gu"], ops.EPI_SILU_MUL, out=b["act"], ws=ws)
+            tap = None
+            if l in tap_col and taps_out is not None:
+                i = tap_col[l]
+                tap = taps_out[:, i * H:(i + 1) * H]
+            ops.gemm(b["act"], lw["w_down"], ops.EPI_RESIDUAL, residual=h, out=h, out2=tap, ws=ws)
+        ops.rmsnorm(h, self.norm_w, c.rms_norm_eps, out=b["xn"])
+        if head == "hidden":
+            return b["xn"]
+        if head == "logits":
+            return ops.gemm(b["xn"], self.lm_head_w, ws=ws)
+        return ops.gemm(b["xn"], self.lm_head_w, ops.EPI_ARGMAX, argmax_partials=b["argmax"], ws=ws)
+
+
+class DraftModel:
+    """DFlash block-diffusion draft conditioned on target hidden-state taps (draft.py:190-223)."""
+
+    def __init__(self, cfg: DraftConfig, weights: dict, target: TargetModel, mask_mode: str = "none"):
+        self.cfg = cfg
+        self.target = target
+        self.device = target.device
+        self.mask_mode = mask_mode
+        dev = self.device
+        self.fc = weights["fc"].to(dev).contiguous()
+        self.hidden_norm = weights["hidden_norm"].to(dev)
+        self.norm_w = weights["norm"].to(dev)
+        self.layers = []
+        ctx_kv = []
+        for lw in weights["layers"]:
+            self.layers.append({
+                "in_norm": lw["input_layernorm"].to(dev),
+                "post_norm": lw["post_attention_layernorm"].to(dev),
+                "w_qkv": torch.cat([lw["q_proj"], lw["k_proj"], lw["v_proj"]], 0).to(dev).contiguous(),
+                "w_o": lw["o_proj"].to(dev).contiguous(),
+                "w_gu": pack_gate_up(lw["gate_proj"].to(dev), lw["up_proj"].to(dev)),
+                "w_down": lw["down_proj"].to(dev).contiguous(),
+                "q_norm": lw["q_norm"].to(dev),
+                "k_norm": lw["k_norm"].to(dev),
+            })
+            ctx_kv += [lw["k_proj"], lw["v_proj"]]
+        self.w_ctx_kv = torch.cat(ctx_kv, 0).to(dev).contiguous()
+        self.inv_freq = rope_inv_freq(cfg.head_dim, cfg.rope_theta, dev)
+        self._bufs: dict[tuple, dict[str, torch.Tensor]] = {}
+
+    @property
+    def block_size(self) -> int:
+        return self.cfg.block_size
+
+    @property
+    def mask_token_id(self) -> int:
+        return self.cfg.mask_token_id
+
+    @property
+    def target_layer_ids(self) -> list[int]:
+        return list(self.cfg.target_layer_ids)
+
+    def make_cache(self, batch: int, cap: int) -> KVCache:
+        c = self.cfg
+        return alloc_kv(c.num_hidden_layers, batch, c.num_key_value_heads, cap, c.head_dim, self.device)
+
+    def buffers(self, M: int, kind: str) -> dict[str, torch.Tensor]:
+        key = (M, kind)
+        b = self._bufs.get(key)
+        if b is None:
+            c = self.cfg
+            dev = self.device
+            H, hd = c.hidden_size, c.head_dim
+            Hq, Hkv = c.num_attention_heads, c.num_key_value_heads
+            if kind == "ctx":
+                b = {
+                    "fc": torch.empty((M, H), dtype=torch.bfloat16, device=dev),
+                    "ctx": torch.empty((M, H), dtype=torch.bfloat16, device=dev),
+                    "kv": torch.empty((M, c.num_hidden_layers * 2 * Hkv * hd), dtype=torch.bfloat16, device=dev),
+                }
+            else:
+                b = {
+                    "h": torch.empty((M, H), dtype=torch.bfloat16, device=dev),
+                    "xn": torch.empty((M, H), dtype=torch.bfloat16, device=dev),
+                    "qkv": torch.empty((M, (Hq + 2 * Hkv) * hd), dtype=torch.bfloat16, device=dev),
+                    "q": torch.empty((M, Hq, hd), dtype=torch.bfloat16, device=dev),
+                    "attn": torch.empty((M, Hq * hd), dtype=torch.bfloat16, device=dev),
+                    "act": torch.empty((M, c.intermediate_size), dtype=torch.bfloat16, device=dev),
+                    "argmax": torch.empty((M, ops.argmax_tiles(c.vocab_size), 2), dtype=torch.float32, device=dev),
+                }
+            self._bufs[key] = b
+        return b
+
+    def ingest_context(self, taps: torch.Tensor, pos: torch.Tensor, cache: KVCache,
+                       row_seq: torch.Tensor | None = None, ws: ops.Workspace | None = None) -> None:
+        """target_hidden = hidden_norm(fc(taps)) (draft.py:217); its K/V for every layer
+        (k_norm + RoPE at the row's position, draft.py:128-147) go into the draft cache.
+        Rows with pos < 0 are skipped."""
+        c = self.cfg
+        M = taps.shape[0]
+        b = self.buffers(M, "ctx")
+        H, hd, Hkv = c.hidden_size, c.head_dim, c.num_key_value_heads
+        ops.gemm(taps, self.fc, out=b["fc"], ws=ws)
+        ops.rmsnorm(b["fc"], self.hidden_norm, c.rms_norm_eps, out=b["ctx"])
+        ops.gemm(b["ctx"], self.w_ctx_kv, out=b["kv"], ws=ws)
+        per = 2 * Hkv * hd
+        for l, lw in enumerate(self.layers):
+            kc, vc = cache.layer(l)
+            view = b["kv"][:, l * per:(l + 1) * per]
+            ops.qkv_rope_append(view, pos, lw["q_norm"], lw["k_norm"], self.inv_freq, kc, vc, 0, Hkv, hd, hd,
+                                c.rms_norm_eps, row_seq=row_seq, do_q=False)
+
+    def forward_block(self, noise: torch.Tensor, pos: torch.Tensor, cache: KVCache, kv_len: torch.Tensor,
+                      max_kv: int, row_seq: torch.Tensor | None = None, head: str = "argmax",
+                      ws: ops.Workspace | None = None):
+        """Block rows (the noise embedding of [last, mask, ...]) attend to the draft cache
+        (context rows already ingested) plus the block itself; returns the lm_head
+        argmax partials of the final-normed hidden states (or the hidden states)."""
+        c = self.cfg
+        M = noise.shape[0]
+        b = self.buffers(M, "blk")
+        H, hd = c.hidden_size, c.head_dim
+        Hq, Hkv = c.num_attention_heads, c.num_key_value_heads
+        h = b["h"]
+        h.copy_(noise)
+        causal = self.mask_mode == "causal"
+        for l, lw in enumerate(self.layers):
+            kc, vc = cache.layer(l)
+            ops.rmsnorm(h, lw["in_norm"], c.rms_norm_eps, out=b["xn"])
+            ops.gemm(b["xn"], lw["w_qkv"], out=b["qkv"], ws=ws)
+            ops.qkv_rope_append(b["qkv"], pos, lw["q_norm"], lw["k_norm"], self.inv_freq, kc, vc, Hq, Hkv, hd, hd,
+                                c.rms_norm_eps, q_out=b["q"], row_seq=row_seq)
+            ops.attention(b["q"], kc, vc, pos, causal=causal, max_kv=max_kv, kv_len=kv_len, row_seq=row_seq,
+                          out=b["attn"], ws=ws)
+            ops.gemm(b["attn"], lw["w_o"], ops.EPI_RESIDUAL, residual=h, out=h, ws=ws)
+            ops.rmsnorm(h, lw["post_norm"], c.rms_norm_eps, out=b["xn"])
+            ops.gemm(b["xn"], lw["w_gu"], ops.EPI_SILU_MUL, out=b["act"], ws=ws)
+            ops.gemm(b["act"], lw["w_down"], ops.EPI_RESIDUAL, residual=h, out=h, ws=ws)
+        ops.rmsnorm(h, self.norm_w, c.rms_norm_eps, out=b["xn"])
+        if head == "hidden":
+            return b["xn"]
+        return ops.gemm(b["xn"], self.target.lm_head_w, ops.EPI_ARGMAX, argmax_partials=b["argmax"], ws=ws)

@@ -1,0 +1,213 @@
+"""Torch-facing wrappers of the C-ABI kernels.
+
+Each wrapper checks dtype / device / layout, passes raw device pointers and the
+current CUDA stream to the C ABI and raises ``DFlashKernelError`` on a non-zero
+status. Tensors must live on a CUDA device: there is no CPU path.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+
+EPI_STORE, EPI_RESIDUAL, EPI_SILU_MUL, EPI_ARGMAX = 0, 1, 2, 3
+ATTN_CHUNK = 128
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _need_cuda(*ts: torch.Tensor | None) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("dflash-b200 ops take CUDA tensors only (no CPU fallback)")
+
+
+def _row_stride(t: torch.Tensor) -> int:
+    if t.dim() != 2 or t.stride(1) != 1:
+        raise ValueError(f"expected a 2-D row-major view, got shape {tuple(t.shape)} stride {t.stride()}")
+    return t.stride(0)
+
+
+class Workspace:
+    """Per-device scratch for split-K GEMM partials and attention chunk partials.
+
+    The GEMM region starts zeroed and the kernels leave their arrival counters at
+    zero, so it is reusable across launches and CUDA-graph replays on one stream.
+    """
+
+    def __init__(self, device: torch.device, gemm_bytes: int = 64 << 20, attn_bytes: int = 64 << 20):
+        self.device = torch.device(device)
+        self.gemm = torch.zeros(gemm_bytes, dtype=torch.uint8, device=self.device)
+        self.attn = torch.empty(attn_bytes, dtype=torch.uint8, device=self.device)
+
+    def ensure_attn(self, nbytes: int) -> None:
+        if nbytes > self.attn.numel():
+            self.attn = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+
+    def ensure_gemm(self, nbytes: int) -> None:
+        if nbytes > self.gemm.numel():
+            self.gemm = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+
+
+_WS: dict[int, Workspace] = {}
+
+
+def workspace(device: torch.device | None = None) -> Workspace:
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    ws = _WS.get(idx)
+    if ws is None:
+        ws = Workspace(torch.device("cuda", idx))
+        _WS[idx] = ws
+    return ws
+
+
+def gemm(x: torch.Tensor, w: torch.Tensor, epilogue: int = EPI_STORE, residual: torch.Tensor | None = None,
+         out: torch.Tensor | None = None, out2: torch.Tensor | None = None,
+         argmax_partials: torch.Tensor | None = None, ws: Workspace | None = None) -> torch.Tensor:
+    """y = x @ w.T (bf16 in, fp32 accumulate) with a fused epilogue."""
+    _need_cuda(x, w, residual, out, out2, argmax_partials)
+    if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
+        raise ValueError("gemm takes bf16 x and w")
+    M, K = x.shape
+    N, K2 = w.shape
+    if K != K2 or not w.is_contiguous():
+        raise ValueError(f"gemm shape mismatch x{tuple(x.shape)} w{tuple(w.shape)}")
+    ldx = _row_stride(x)
+    ws = ws or workspace(x.device)
+    need = int(_lib.query("dfl_gemm_workspace_bytes", M, N, K, epilogue))
+    ws.ensure_gemm(need)
+    if epilogue == EPI_ARGMAX:
+        ntiles = int(_lib.query("dfl_gemm_argmax_tiles", N))
+        if argmax_partials is None:
+            argmax_partials = torch.empty((M, ntiles, 2), dtype=torch.float32, device=x.device)
+        _lib.call("dfl_gemm_bf16", _ptr(x), ldx, _ptr(w), M, N, K, epilogue, None, 0, None, 0, None, 0,
+                  _ptr(argmax_partials), _ptr(ws.gemm), ws.gemm.numel(), _stream())
+        return argmax_partials
+    n_out = N // 2 if epilogue == EPI_SILU_MUL else N
+    if out is None:
+        out = torch.empty((M, n_out), dtype=torch.bfloat16, device=x.device)
+    if residual is not None and epilogue != EPI_RESIDUAL:
+        raise ValueError("residual given without the residual epilogue")
+    ldr = _row_stride(residual) if residual is not None else 0
+    ldy2 = _row_stride(out2) if out2 is not None else 0
+    _lib.call("dfl_gemm_bf16", _ptr(x), ldx, _ptr(w), M, N, K, epilogue, _ptr(residual), ldr, _ptr(out),
+              _row_stride(out), _ptr(out2), ldy2, None, _ptr(ws.gemm), ws.gemm.numel(), _stream())
+    return out
+
+
+def argmax_tiles(N: int) -> int:
+    return int(_lib.query("dfl_gemm_argmax_tiles", N))
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor | None, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    _need_cuda(x, w, out)
+    M, H = x.shape
+    if out is None:
+        out = torch.empty((M, H), dtype=torch.bfloat16, device=x.device)
+    _lib.call("dfl_rmsnorm_bf16", _ptr(x), _row_stride(x), _ptr(w), _ptr(out), _row_stride(out), M, H, float(eps),
+              _stream())
+    return out
+
+
+def embed(tokens: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    _need_cuda(tokens, table, out)
+    if tokens.dtype != torch.int32 or not tokens.is_contiguous():
+        raise ValueError("tokens must be contiguous int32")
+    V, H = table.shape
+    M = tokens.numel()
+    if out is None:
+        out = torch.empty((M, H), dtype=torch.bfloat16, device=table.device)
+    _lib.call("dfl_embed_bf16", _ptr(tokens), _ptr(table), _ptr(out), _row_stride(out), M, H, V, _stream())
+    return out
+
+
+def qkv_rope_append(qkv: torch.Tensor, pos: torch.Tensor, q_norm: torch.Tensor, k_norm: torch.Tensor,
+                    inv_freq: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, Hq: int, Hkv: int, hd: int,
+                    rot_dim: int, eps: float, q_out: torch.Tensor | None = None, row_seq: torch.Tensor | None = None,
+                    q_stride: int | None = None, do_q: bool = True) -> torch.Tensor | None:
+    """q/k head norm + RoPE + cache append. Caches are [seq, Hkv, cap, hd] views (contiguous in the last 3 dims)."""
+    _need_cuda(qkv, pos, q_norm, k_norm, inv_freq, k_cache, v_cache, q_out, row_seq)
+    M = qkv.shape[0]
+    if do_q and q_out is None:
+        q_out = torch.empty((M, Hq, hd), dtype=torch.bfloat16, device=qkv.device)
+    if k_cache.dim() != 4 or k_cache.stride(3) != 1 or k_cache.stride(2) != hd:
+        raise ValueError("k_cache must be a [seq, Hkv, cap, hd] view")
+    _lib.call("dfl_qkv_rope_append", _ptr(qkv), _row_stride(qkv), q_stride or hd, _ptr(pos), _ptr(row_seq),
+              _ptr(q_norm), _ptr(k_norm), _ptr(inv_freq), _ptr(q_out) if do_q else None, _ptr(k_cache),
+              _ptr(v_cache), k_cache.stride(0), k_cache.stride(1), M, Hq, Hkv, hd, rot_dim, float(eps), int(do_q),
+              _stream())
+    return q_out
+
+
+def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, pos: torch.Tensor, causal: bool,
+              max_kv: int, kv_len: torch.Tensor | None = None, row_seq: torch.Tensor | None = None,
+              scale: float | None = None, out: torch.Tensor | None = None, ws: Workspace | None = None) -> torch.Tensor:
+    """q [M, Hq, hd] against caches [seq, Hkv, cap, hd]; returns [M, Hq*hd] bf16."""
+    _need_cuda(q, k_cache, v_cache, pos, kv_len, row_seq, out)
+    M, Hq, hd = q.shape
+    Hkv = k_cache.shape[1]
+    if scale is None:
+        scale = 1.0 / math.sqrt(hd)
+    if out is None:
+        out = torch.empty((M, Hq * hd), dtype=torch.bfloat16, device=q.device)
+    ws = ws or workspace(q.device)
+    need = int(_lib.query("dfl_attention_workspace_bytes", M, Hq, hd, max_kv))
+    ws.ensure_attn(need)
+    _lib.call("dfl_attention", _ptr(q), _ptr(k_cache), _ptr(v_cache), k_cache.stride(0), k_cache.stride(1),
+              _ptr(pos), _ptr(row_seq), _ptr(kv_len), M, Hq, Hkv, hd, int(causal), float(scale), int(max_kv),
+              _ptr(out), _row_stride(out), _ptr(ws.attn), ws.attn.numel(), _stream())
+    return out
+
+
+def argmax_reduce(partials: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    _need_cuda(partials, out)
+    M, ntiles = partials.shape[0], partials.shape[1]
+    if out is None:
+        out = torch.empty(M, dtype=torch.int32, device=partials.device)
+    _lib.call("dfl_argmax_reduce", _ptr(partials), M, ntiles, _ptr(out), _stream())
+    return out
+
+
+def step_prepare(state, out_tokens, block, bs, mask_id, target_pos, draft_ctx_pos, draft_block_pos, draft_kv_len, B):
+    _lib.call("dfl_step_prepare", _ptr(state), _ptr(out_tokens), out_tokens.stride(0), _ptr(block), bs, mask_id,
+              _ptr(target_pos), _ptr(draft_ctx_pos), _ptr(draft_block_pos), _ptr(draft_kv_len), B, _stream())
+
+
+def draft_commit(state, partials, block, bs, B, inject_tokens=None, inject_len=None, inject_noise=None):
+    _lib.call("dfl_draft_commit", _ptr(state), _ptr(partials), partials.shape[1], _ptr(block), bs,
+              _ptr(inject_tokens), inject_tokens.stride(0) if inject_tokens is not None else 0, _ptr(inject_len),
+              inject_len.stride(0) if inject_len is not None else 0, _ptr(inject_noise),
+              inject_noise.stride(0) if inject_noise is not None else 0, B, _stream())
+
+
+def verify_accept(state, partials, block, bs, out_tokens, B, stop_ids=None, n_stop=0, posterior=None,
+                  accept_log=None):
+    _lib.call("dfl_verify_accept", _ptr(state), _ptr(partials), partials.shape[1], _ptr(block), bs, _ptr(out_tokens),
+              out_tokens.stride(0), _ptr(posterior), _ptr(stop_ids), n_stop, _ptr(accept_log),
+              accept_log.stride(0) if accept_log is not None else 0, B, _stream())
+
+
+def gdr_recurrence(q, k, v, g, beta, state_in, state_out=None, snapshots=None, o=None, state_slot=None,
+                   state_in_bstride=None):
+    """Gated-delta recurrence. q,k [B,T,Hk,Dk] bf16; v [B,T,Hv,Dv] bf16; g,beta [B,T,Hv] fp32;
+    state_in [B,Hv,Dv,Dk] fp32 (or a snapshot array with state_slot)."""
+    _need_cuda(q, k, v, g, beta, state_in, state_out, snapshots, o, state_slot)
+    B, T, Hk, Dk = k.shape
+    Hv, Dv = v.shape[2], v.shape[3]
+    for t in (k, v, g, beta, state_in):
+        if not t.is_contiguous():
+            raise ValueError("gdr_recurrence inputs must be contiguous")
+    if g.dtype != torch.float32 or beta.dtype != torch.float32 or state_in.dtype != torch.float32:
+        raise ValueError("g, beta and the state are fp32")
+    bstride = state_in_bstride if state_in_bstride is not None else Hv * Dv * Dk
+    _lib.call("dfl_gdr_recurrence", _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(state_in), bstride,
+              _ptr(state_slot), _ptr(state_out), _ptr(snapshots), _ptr(o), B, T, Hk, Hv, Dk, Dv, _stream())

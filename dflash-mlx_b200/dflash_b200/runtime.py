@@ -1,0 +1,340 @@
+"""Speculative DFlash decode loop with the step state kept on the device.
+
+Reference: dflash_mlx/runtime.py:360-589 (``dflash_generate_stream`` /
+``dflash_generate``) with the default ``parallel-replay`` verify
+(runtime.py:117-163). The reference pulls drafted and posterior tokens to the
+host twice per step; here one step is a fixed kernel sequence
+
+    step_prepare -> draft context ingest -> draft block forward -> draft commit
+    -> target verify forward (taps into the draft conditioning buffer)
+    -> verify accept (argmax, longest prefix, bonus, commit, stop checks)
+
+that reads and writes a per-sequence ``dfl_seq_state`` record, so it can be
+captured once in a CUDA graph and replayed. The host polls the state of step k-1
+while step k runs. At temperature 0 every verify mode of the reference produces
+the same tokens; all of them map onto this path.
+"""
+from __future__ import annotations
+
+import time
+from collections.abc import Iterator
+from dataclasses import dataclass
+from typing import Any
+
+import torch
+
+from . import ops
+from .model import DraftModel, TargetModel
+
+STATE_INTS = 16  # sizeof(dfl_seq_state) / 4
+S_START, S_PENDING, S_DRAFT_LEN, S_ACCEPTED, S_BONUS, S_FINISHED, S_STOP, S_STEPS, S_TOTAL, S_PROMPT = range(10)
+
+VERIFY_MODES = ("parallel-replay", "parallel-lazy-logits", "parallel-greedy-argmax", "stream", "chunked")
+
+
+@dataclass
+class DFlashRuntimeEvent:
+    token_ids: list[int]
+    output_tokens: list[int]
+    metrics: dict[str, Any] | None = None
+    finished: bool = False
+
+
+def longest_prefix_match(draft_tokens: list[int], verifier_tokens: list[int]) -> int:
+    """Host restatement of runtime.py:41-47 (the device kernel does the same per step)."""
+    matched = 0
+    for d, v in zip(draft_tokens, verifier_tokens):
+        if d != v:
+            break
+        matched += 1
+    return matched
+
+
+def sample_tokens(logits: torch.Tensor, temperature: float) -> torch.Tensor:
+    """runtime.py:22-29. Greedy (temperature < 1e-5) is the supported path."""
+    if temperature >= 1e-5:
+        raise NotImplementedError("dflash-b200 implements greedy decoding (temperature 0) only")
+    flat = logits.reshape(-1, logits.shape[-1])
+    return torch.argmax(flat, dim=-1).reshape(logits.shape[:-1]).to(torch.int32)
+
+
+class SpecSession:
+    """Device buffers and the captured step for B sequences decoded together."""
+
+    def __init__(self, target: TargetModel, draft: DraftModel | None, batch: int, max_total: int,
+                 block_size: int, stop_token_ids: set[int] | None = None, use_graph: bool = True,
+                 max_steps: int | None = None, prefill_chunk: int = 128):
+        self.target = target
+        self.draft = draft
+        self.B = batch
+        self.bs = block_size
+        self.dev = target.device
+        self.use_graph = use_graph
+        self.prefill_chunk = prefill_chunk
+        tc = target.cfg
+        B, bs = batch, block_size
+        self.cap = max_total + 2 * bs + 1
+        self.out_cap = self.cap
+        self.max_steps = max_steps or (max_total + 1)
+        self.ws = ops.Workspace(self.dev)
+        dev = self.dev
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.state = torch.zeros((B, STATE_INTS), **i32)
+        self.out_tokens = torch.zeros((B, self.out_cap), **i32)
+        self.block = torch.zeros(B * bs, **i32)
+        self.tpos = torch.zeros(B * bs, **i32)
+        self.dpos_ctx = torch.zeros(B * bs, **i32)
+        self.dpos_blk = torch.zeros(B * bs, **i32)
+        self.dkv_len = torch.zeros(B, **i32)
+        self.row_seq = (torch.arange(B * bs, device=dev, dtype=torch.int32) // bs) if B > 1 else None
+        self.accept_log = torch.zeros((B, self.max_steps), **i32)
+        stops = sorted(stop_token_ids or [])
+        self.n_stop = len(stops)
+        self.stop_ids = torch.tensor(stops or [0], **i32)
+        self.tcache = target.make_cache(B, self.cap)
+        self.layer_ids = sorted(draft.target_layer_ids) if draft is not None else []
+        ntaps = max(1, len(self.layer_ids))
+        self.taps = torch.zeros((B * bs, ntaps * tc.hidden_size), dtype=torch.bfloat16, device=dev)
+        if draft is not None:
+            self.dcache = draft.make_cache(B, self.cap)
+            self.noise = torch.empty((B * bs, tc.hidden_size), dtype=torch.bfloat16, device=dev)
+        self.inject_tokens = self.inject_len = self.inject_noise = None
+        self.graph: torch.cuda.CUDAGraph | None = None
+        self.host_state = torch.zeros((B, STATE_INTS), dtype=torch.int32, pin_memory=True)
+        self._reserve_workspace()
+
+    def _reserve_workspace(self) -> None:
+        """Sizes the scratch for every launch shape up front: a captured graph holds raw
+        pointers into it, so it must never be reallocated afterwards."""
+        tc = self.target.cfg
+        q = ops._lib.query
+        gemm_need = 0
+        attn_need = 0
+        shapes = [self.B * self.bs, self.prefill_chunk]
+        mats = [(tc.num_attention_heads + 2 * tc.num_key_value_heads) * tc.head_dim, tc.hidden_size,
+                2 * tc.intermediate_size, tc.vocab_size]
+        ks = [tc.hidden_size, tc.num_attention_heads * tc.head_dim, tc.intermediate_size,
+              self.taps.shape[1]]
+        if self.draft is not None:
+            mats.append(self.draft.w_ctx_kv.shape[0])
+        for M in shapes:
+            for N in mats:
+                for K in ks:
+                    gemm_need = max(gemm_need, int(q("dfl_gemm_workspace_bytes", M, N, K, 0)))
+            attn_need = max(attn_need, int(q("dfl_attention_workspace_bytes", M, tc.num_attention_heads,
+                                               tc.head_dim, self.cap)))
+        self.ws.ensure_gemm(gemm_need)
+        self.ws.ensure_attn(attn_need)
+
+    # ------------------------------------------------------------------
+    def set_injection(self, trace: torch.Tensor, lengths: torch.Tensor, noise: torch.Tensor) -> None:
+        """Oracle-injected drafts: block[1+i] = trace[start+1+i] for i < lengths[step], else noise."""
+        self.inject_tokens = trace.to(self.dev, torch.int32).contiguous()
+        self.inject_len = lengths.to(self.dev, torch.int32).contiguous()
+        self.inject_noise = noise.to(self.dev, torch.int32).contiguous()
+        self.graph = None
+
+    def prefill(self, prompts: list[list[int]], max_new_tokens: int | list[int]) -> list[int]:
+        """Target forward over each prompt (taps for the draft context, runtime.py:384-390);
+        returns the first greedy token of every sequence."""
+        B = self.B
+        tc = self.target.cfg
+        dev = self.dev
+        if len(prompts) != B:
+            raise ValueError(f"expected {B} prompts")
+        if isinstance(max_new_tokens, int):
+            max_new_tokens = [max_new_tokens] * B
+        firsts = []
+        st = torch.zeros((B, STATE_INTS), dtype=torch.int32)
+        for b, prompt in enumerate(prompts):
+            P = len(prompt)
+            if P == 0:
+                raise ValueError("empty prompt")
+            if P + max_new_tokens[b] + 2 * self.bs + 1 > self.cap:
+                raise ValueError("prompt + max_new_tokens exceeds the session capacity")
+            toks = torch.tensor(prompt, dtype=torch.int32, device=dev)
+            seq = torch.full((self.prefill_chunk,), b, dtype=torch.int32, device=dev) if B > 1 else None
+            last_part = None
+            for c0 in range(0, P, self.prefill_chunk):
+                c1 = min(P, c0 + self.prefill_chunk)
+                n = c1 - c0
+                pos = torch.arange(c0, c1, dtype=torch.int32, device=dev)
+                rs = seq[:n] if seq is not None else None
+                taps = torch.empty((n, self.taps.shape[1]), dtype=torch.bfloat16, device=dev)
+                part = self.target.forward(toks[c0:c1], pos, self.tcache, max_kv=c1, layer_ids=self.layer_ids,
+                                           taps_out=taps, row_seq=rs, ws=self.ws)
+                last_part = part[n - 1:n]
+                if self.draft is not None:
+                    self.draft.ingest_context(taps, pos, self.dcache, row_seq=rs, ws=self.ws)
+            first = int(ops.argmax_reduce(last_part).item())
+            firsts.append(first)
+            self.out_tokens[b, :P] = toks
+            self.out_tokens[b, P] = first
+            total_max = P + max_new_tokens[b]
+            stop_index = P if first in set(self.stop_ids.tolist()[: self.n_stop]) else -1
+            # like runtime.py:406, a stop token sampled at prefill still runs one decode step
+            finished = int(P + 1 > total_max)
+            st[b, S_START] = P
+            st[b, S_PENDING] = 0
+            st[b, S_DRAFT_LEN] = P
+            st[b, S_FINISHED] = finished
+            st[b, S_STOP] = stop_index
+            st[b, S_TOTAL] = total_max
+            st[b, S_PROMPT] = P
+        self.state.copy_(st.to(dev))
+        self.accept_log.zero_()
+        return firsts
+
+    # ------------------------------------------------------------------
+    def _step_kernels(self) -> None:
+        B, bs = self.B, self.bs
+        max_kv = self.cap
+        ops.step_prepare(self.state, self.out_tokens, self.block, bs,
+                         self.draft.mask_token_id if self.draft is not None else 0,
+                         self.tpos, self.dpos_ctx if self.draft else None, self.dpos_blk if self.draft else None,
+                         self.dkv_len if self.draft else None, B)
+        if self.draft is not None:
+            d = self.draft
+            d.ingest_context(self.taps, self.dpos_ctx, self.dcache, row_seq=self.row_seq, ws=self.ws)
+            ops.embed(self.block, self.target.embed_w, out=self.noise)
+            part = d.forward_block(self.noise, self.dpos_blk, self.dcache, self.dkv_len, max_kv,
+                                   row_seq=self.row_seq, ws=self.ws)
+            ops.draft_commit(self.state, part, self.block, bs, B, self.inject_tokens, self.inject_len,
+                             self.inject_noise)
+        part = self.target.forward(self.block, self.tpos, self.tcache, max_kv=max_kv, layer_ids=self.layer_ids,
+                                   taps_out=self.taps, row_seq=self.row_seq, ws=self.ws)
+        ops.verify_accept(self.state, part, self.block, bs, self.out_tokens, B,
+                          stop_ids=self.stop_ids, n_stop=self.n_stop, accept_log=self.accept_log)
+
+    def capture(self) -> None:
+        s = torch.cuda.Stream(device=self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                self._step_kernels()
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+        self.graph = g
+
+    def step(self) -> None:
+        if self.use_graph:
+            if self.graph is None:
+                self.capture()
+            self.graph.replay()
+        else:
+            self._step_kernels()
+
+    def poll_state(self) -> torch.Tensor:
+        self.host_state.copy_(self.state, non_blocking=True)
+        torch.cuda.current_stream(self.dev).synchronize()
+        return self.host_state.clone()
+
+    def outputs(self) -> tuple[list[list[int]], list[list[int]], torch.Tensor]:
+        """Committed tokens (truncated like runtime.py:499-507, 518) and acceptance lengths."""
+        st = self.state.cpu()
+        toks = self.out_tokens.cpu()
+        log = self.accept_log.cpu()
+        outs, accs = [], []
+        for b in range(self.B):
+            start, stop, total, steps = (int(st[b, S_START]), int(st[b, S_STOP]), int(st[b, S_TOTAL]),
+                                         int(st[b, S_STEPS]))
+            n = start + 1
+            if stop >= 0:
+                n = min(n, stop + 1)
+            n = min(n, total)
+            outs.append(toks[b, :n].tolist())
+            accs.append(log[b, :steps].tolist())
+        return outs, accs, st
+
+
+def dflash_generate_stream(target: TargetModel, draft: DraftModel, prompt_tokens, max_new_tokens: int,
+                           temperature: float, stop_token_ids: set[int], layer_ids: list[int] | None,
+                           speculative_tokens: int | None, verify_mode: str = "parallel-replay",
+                           verify_chunk_size: int = 4, profile: bool = False,
+                           use_graph: bool = True) -> Iterator[DFlashRuntimeEvent]:
+    """Single-sequence generator with the reference's event and metrics shape (runtime.py:360-555)."""
+    if temperature >= 1e-5:
+        raise NotImplementedError("dflash-b200 implements greedy decoding (temperature 0) only")
+    if verify_mode not in VERIFY_MODES:
+        raise ValueError(f"unknown verify_mode {verify_mode!r}")
+    if layer_ids is not None and draft is not None and sorted(layer_ids) != sorted(draft.target_layer_ids):
+        raise ValueError("layer_ids must match the draft's target_layer_ids")
+    prompt = prompt_tokens.tolist() if hasattr(prompt_tokens, "tolist") else list(prompt_tokens)
+    prompt = [int(t) for t in prompt]
+    prompt_len = len(prompt)
+    bs_max = draft.block_size if draft is not None else 1
+    block_size = bs_max if speculative_tokens is None else max(1, min(speculative_tokens, bs_max))
+    use_draft = draft if block_size > 1 else None
+    total_max = prompt_len + max_new_tokens
+    sess = SpecSession(target, use_draft, 1, total_max, block_size, stop_token_ids, use_graph=use_graph)
+
+    torch.cuda.synchronize(target.device)
+    t0 = time.perf_counter()
+    first = sess.prefill([prompt], max_new_tokens)[0]
+    torch.cuda.synchronize(target.device)
+    prefill_time = time.perf_counter() - t0
+
+    output_tokens = prompt + [first]
+    streamed_len = prompt_len
+    if max_new_tokens > 0:
+        yield DFlashRuntimeEvent(token_ids=output_tokens[streamed_len:], output_tokens=list(output_tokens))
+        streamed_len = len(output_tokens)
+
+    decode_start = time.perf_counter()
+    finished = bool(sess.state[0, S_FINISHED].item()) or max_new_tokens <= 0
+    while not finished:
+        sess.step()
+        host = sess.poll_state()
+        finished = bool(host[0, S_FINISHED])
+        start = int(host[0, S_START])
+        toks = sess.out_tokens[0, : start + 1].tolist()
+        stop = int(host[0, S_STOP])
+        n = start + 1
+        if stop >= 0:
+            n = min(n, stop + 1)
+        n = min(n, total_max)
+        output_tokens = toks[:n]
+        new = output_tokens[streamed_len:]
+        if new:
+            yield DFlashRuntimeEvent(token_ids=new, output_tokens=list(output_tokens))
+            streamed_len = len(output_tokens)
+    torch.cuda.synchronize(target.device)
+    decode_time = time.perf_counter() - decode_start
+    outs, accs, _ = sess.outputs()
+    output_tokens = outs[0]
+    acceptance_lengths = accs[0]
+    generated = max(len(output_tokens) - prompt_len, 0)
+    total_time = prefill_time + decode_time
+    metrics = {
+        "num_input_tokens": prompt_len,
+        "num_output_tokens": generated,
+        "prefill_time_s": prefill_time,
+        "decode_time_s": decode_time,
+        "total_time_s": total_time,
+        "prompt_tps": prompt_len / max(prefill_time, 1e-9),
+        "generation_tps": generated / max(decode_time, 1e-9),
+        "end_to_end_tps": generated / max(total_time, 1e-9),
+        "avg_acceptance_length": sum(acceptance_lengths) / max(len(acceptance_lengths), 1),
+        "acceptance_lengths": acceptance_lengths,
+        "peak_memory_gb": torch.cuda.max_memory_allocated(target.device) / 1e9,
+        "target_cache_summary": f"kv_len={int(sess.state[0, S_START].item())} x {target.cfg.num_hidden_layers} layers",
+        "speculative_tokens": block_size,
+    }
+    if profile:
+        metrics["profile"] = {"steps": len(acceptance_lengths), "verify_mode": verify_mode}
+    yield DFlashRuntimeEvent(token_ids=[], output_tokens=list(output_tokens), metrics=metrics, finished=True)
+
+
+def dflash_generate(target: TargetModel, draft: DraftModel, prompt_tokens, max_new_tokens: int, temperature: float,
+                    stop_token_ids: set[int], layer_ids: list[int] | None, speculative_tokens: int | None,
+                    verify_mode: str = "parallel-replay", verify_chunk_size: int = 4, profile: bool = False,
+                    use_graph: bool = True) -> tuple[list[int], dict[str, Any]]:
+    final = None
+    for event in dflash_generate_stream(target, draft, prompt_tokens, max_new_tokens, temperature, stop_token_ids,
+                                        layer_ids, speculative_tokens, verify_mode, verify_chunk_size, profile,
+                                        use_graph):
+        if event.finished:
+            final = event
+    if final is None or final.metrics is None:
+        raise RuntimeError("DFlash generation did not produce a final event.")
+    return final.output_tokens, final.metrics

@@ -1,0 +1,152 @@
+/*
+ * dflash-b200 C ABI: the DFlash speculative draft/verify hot path on NVIDIA B200 (sm_100a).
+ *
+ * Every entry point is `extern "C"`, takes plain device pointers, element strides
+ * and a cudaStream_t passed as `void*`, returns an int status (DFL_OK == 0) and
+ * never synchronises the host. On a non-zero status dfl_last_error() returns a
+ * message for the calling thread. bf16 buffers are passed as `void*`.
+ *
+ * The reference (Aryagm/dflash-mlx) is a Python/MLX package with no C ABI; each
+ * entry point below names the reference call it replaces (path:line inside the
+ * reference project). The Python host in dflash-mlx_b200/dflash_b200 binds these
+ * with ctypes; INTEGRATION.md shows the binding.
+ */
+#ifndef DFLASH_B200_H
+#define DFLASH_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DFL_ABI_VERSION 1
+
+/* status codes */
+#define DFL_OK 0
+#define DFL_ERR_INVALID 1     /* null pointer, negative size, inconsistent arguments */
+#define DFL_ERR_UNSUPPORTED 2 /* a shape / alignment this build has no kernel for */
+#define DFL_ERR_CUDA 3        /* the CUDA launch itself failed */
+#define DFL_ERR_WORKSPACE 4   /* caller-provided scratch is missing or too small */
+
+/* GEMM epilogues (dfl_gemm_bf16) */
+#define DFL_EPI_STORE 0    /* y = bf16(acc) */
+#define DFL_EPI_RESIDUAL 1 /* y = bf16(residual + bf16(acc)); optional second copy to y2 (hidden-state tap) */
+#define DFL_EPI_SILU_MUL 2 /* W rows packed per 64: [32 gate | 32 up]; y[:, n] = bf16(silu(gate) * up), N/2 columns */
+#define DFL_EPI_ARGMAX 3   /* per row and 64-column tile: (max bf16 logit, lowest index) into argmax partials */
+
+/* keys per attention chunk: the fixed key ranges merged in order by dfl_attention */
+#define DFL_ATTN_CHUNK 128
+
+/* Per-sequence decode state kept on the device (64 bytes). */
+typedef struct dfl_seq_state {
+  int32_t start;      /* position of block[0]; the target KV cache holds positions [0, start) */
+  int32_t pending;    /* verified rows of the tap buffer not yet in the draft cache */
+  int32_t draft_len;  /* draft KV cache length */
+  int32_t accepted;   /* acceptance length of the last step (matched + 1) */
+  int32_t bonus;      /* posterior token committed after the accepted prefix */
+  int32_t finished;   /* 1 once a stop token or the length limit has been committed */
+  int32_t stop_index; /* index in the output of the first stop token, -1 if none */
+  int32_t steps;      /* decode steps executed */
+  int32_t total_max;  /* prompt length + max_new_tokens */
+  int32_t prompt_len;
+  int32_t reserved[6];
+} dfl_seq_state;
+
+int dfl_abi_version(void);
+const char* dfl_last_error(void);
+
+/* ---- dense projections ----------------------------------------------------
+ * Y[M,N] = X[M,K] . W[N,K]^T with fp32 accumulation and a fused epilogue.
+ * Replaces the nn.Linear calls of the verify / draft forward: mlx-lm qwen3
+ * Attention and MLP (driven from adapters.py:611-631), DFlashAttention
+ * q/k/v/o projections (draft.py:75-98, 118-159), the draft fc
+ * (draft.py:196-201, 217) and lm_head_logits / lm_head_argmax
+ * (adapters.py:264-271, 606-609; runtime.py:22-29 argmax).
+ * K % 64 == 0, x and w 16-byte aligned. Split-K scratch: workspace of
+ * dfl_gemm_workspace_bytes() bytes, zero-filled once before first use (the
+ * kernel leaves its counters at zero); one workspace per stream.
+ * DFL_EPI_ARGMAX writes float2 partials [M][dfl_gemm_argmax_tiles(N)]. */
+size_t dfl_gemm_workspace_bytes(int M, int N, int K, int epilogue);
+int dfl_gemm_argmax_tiles(int N);
+int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w, int M, int N, int K, int epilogue,
+                  const void* residual, int64_t ldr, void* y, int64_t ldy, void* y2, int64_t ldy2,
+                  void* argmax_partials, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- row kernels ----------------------------------------------------------
+ * RMSNorm y = w * x * rsqrt(mean(x^2) + eps) (fp32 math, bf16 out); w may be
+ * NULL (unit weight). Replaces nn.RMSNorm / mx.fast.rms_norm (draft.py:167-171,
+ * 198-201, 223; adapters.py:629). H % 256 == 0. */
+int dfl_rmsnorm_bf16(const void* x, int64_t ldx, const void* w, void* y, int64_t ldy, int M, int H, float eps,
+                     void* stream);
+
+/* Token embedding gather (adapters.py:603-604 embed_tokens; runtime.py:410). */
+int dfl_embed_bf16(const int32_t* tokens, const void* table, void* y, int64_t ldy, int M, int H, int V,
+                   void* stream);
+
+/* q_norm / k_norm (per-head RMSNorm), non-interleaved RoPE over the first
+ * rot_dim dims with inverse frequencies inv_freq[rot_dim/2], and the KV-cache
+ * append at slot == pos[r] (rows with pos < 0 are skipped). Replaces the
+ * q/k norm + rope + KVCache.update_and_fetch sequence of draft.py:118-147 and
+ * of mlx-lm qwen3 Attention. Cache layout [seq][Hkv][cap][hd]. */
+int dfl_qkv_rope_append(const void* qkv, int64_t ldqkv, int q_stride, const int32_t* pos, const int32_t* row_seq,
+                        const void* q_norm, const void* k_norm, const float* inv_freq, void* q_out, void* k_cache,
+                        void* v_cache, int64_t seq_stride, int64_t head_stride, int M, int Hq, int Hkv, int hd,
+                        int rot_dim, float eps, int do_q, void* stream);
+
+/* ---- attention ------------------------------------------------------------
+ * GQA softmax(scale q.K^T) V over the cache. causal: row r sees keys
+ * [0, pos[r]]; otherwise keys [0, kv_len[seq(r)]). Replaces
+ * mx.fast.scaled_dot_product_attention at the verify (mask "causal",
+ * adapters.py:620) and in DFlashAttention (draft.py:149-157). max_kv bounds
+ * every row's key range (sizes the launch and the workspace). */
+size_t dfl_attention_workspace_bytes(int M, int Hq, int hd, int max_kv);
+int dfl_attention(const void* q, const void* k_cache, const void* v_cache, int64_t seq_stride, int64_t head_stride,
+                  const int32_t* pos, const int32_t* row_seq, const int32_t* kv_len, int M, int Hq, int Hkv, int hd,
+                  int causal, float scale, int max_kv, void* out, int64_t ldo, void* workspace,
+                  size_t workspace_bytes, void* stream);
+
+/* ---- speculative step control ---------------------------------------------
+ * Greedy argmax from DFL_EPI_ARGMAX partials (runtime.py:22-29 at temperature 0). */
+int dfl_argmax_reduce(const void* partials, int M, int n_tiles, int32_t* out, void* stream);
+
+/* Builds block = [out[start], mask_id x (bs-1)] (runtime.py:408) and the
+ * verify / draft positions for every sequence. */
+int dfl_step_prepare(dfl_seq_state* state, const int32_t* out_tokens, int64_t out_stride, int32_t* block, int bs,
+                     int mask_id, int32_t* target_pos, int32_t* draft_ctx_pos, int32_t* draft_block_pos,
+                     int32_t* draft_kv_len, int B, void* stream);
+
+/* block[1:] = draft argmax (runtime.py:417-423), or injected tokens when
+ * inject_tokens != NULL; then trims the draft cache back to its context
+ * (trim_draft_cache, runtime.py:32-34, 420). */
+int dfl_draft_commit(dfl_seq_state* state, const void* partials, int n_tiles, int32_t* block, int bs,
+                     const int32_t* inject_tokens, int64_t inject_stride, const int32_t* inject_len,
+                     int64_t inject_len_stride, const int32_t* inject_noise, int64_t noise_stride, int B,
+                     void* stream);
+
+/* Posterior argmax, longest_prefix_match (runtime.py:41-47), accepted =
+ * matched + 1 and bonus token (runtime.py:139-163), commit and stop / length
+ * checks (runtime.py:488-507); the KV rollback of rewind_kv_caches
+ * (adapters.py:697-700) is the length update state.start += accepted. */
+int dfl_verify_accept(dfl_seq_state* state, const void* partials, int n_tiles, const int32_t* block, int bs,
+                      int32_t* out_tokens, int64_t out_stride, int32_t* posterior, const int32_t* stop_ids,
+                      int n_stop, int32_t* accept_log, int64_t log_stride, int B, void* stream);
+
+/* ---- gated-delta recurrence -----------------------------------------------
+ * q,k [B,T,Hk,Dk] bf16, v [B,T,Hv,Dv] bf16, g (decay multiplier) and beta
+ * [B,T,Hv] fp32, state [.,Hv,Dv,Dk] fp32. Writes o [B,T,Hv,Dv] bf16 (nullable),
+ * the state after every token into snapshots [B,T,Hv,Dv,Dk] (nullable) and
+ * the final state (nullable; may alias state_in). state_slot (nullable)
+ * selects snapshot slot[b] of state_in (zero-copy rollback). Replaces mlx-lm
+ * gated_delta_kernel / gated_delta_ops (custom_qwen35_model.py:452-476) and,
+ * with o and snapshots NULL, advance_gated_delta_states (adapters.py:93-135). */
+int dfl_gdr_recurrence(const void* q, const void* k, const void* v, const float* g, const float* beta,
+                       const float* state_in, int64_t state_in_bstride, const int32_t* state_slot, float* state_out,
+                       float* snapshots, void* o, int B, int T, int Hk, int Hv, int Dk, int Dv, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DFLASH_B200_H */

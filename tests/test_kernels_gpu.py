@@ -1,0 +1,186 @@
+"""Kernel parity tests: every C-ABI kernel against the CPU oracle (or a torch fp32
+reference for plain contractions), plus the row-invariance the lossless
+spec == plain-greedy property depends on."""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _need(lib):
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+
+
+def _ops():
+    from dflash_b200 import ops
+    return ops
+
+
+def _rand(shape, std=1.0, seed=0, dtype=torch.bfloat16):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(shape, generator=g) * std).to(dtype)
+
+
+@pytest.mark.parametrize("M,N,K", [(16, 6144, 2560), (1, 2560, 4096), (5, 2560, 9728), (40, 512, 256),
+                                   (16, 151936, 2560), (128, 1536, 2560)])
+def test_gemm_store_matches_fp32(M, N, K):
+    ops = _ops()
+    x = _rand((M, K), 1.0, 1)
+    w = _rand((N, K), 0.02, 2)
+    y = ops.gemm(x.to(DEV), w.to(DEV)).float().cpu()
+    ref = (x.float() @ w.float().T)
+    err = (y - ref).abs().max().item()
+    tol = 1e-2 * ref.abs().max().item() + 1e-3
+    assert err <= tol, (err, tol)
+
+
+def test_gemm_residual_and_tap():
+    ops = _ops()
+    M, N, K = 16, 2560, 4096
+    x, w, r = _rand((M, K), 1.0, 3), _rand((N, K), 0.02, 4), _rand((M, N), 1.0, 5)
+    rd = r.to(DEV)
+    tap = torch.zeros((M, 3 * N), dtype=torch.bfloat16, device=DEV)
+    out = ops.gemm(x.to(DEV), w.to(DEV), ops.EPI_RESIDUAL, residual=rd, out=rd, out2=tap[:, N:2 * N])
+    ref = (r.float() + (x.float() @ w.float().T).bfloat16().float())
+    assert (out.float().cpu() - ref).abs().max().item() < 0.05
+    assert torch.equal(tap[:, N:2 * N], out)
+    assert tap[:, :N].abs().sum().item() == 0
+
+
+def test_gemm_silu_mul():
+    from dflash_b200.weights import pack_gate_up
+    ops = _ops()
+    M, F, K = 16, 9728, 2560
+    x, wg, wu = _rand((M, K), 1.0, 6), _rand((F, K), 0.02, 7), _rand((F, K), 0.02, 8)
+    out = ops.gemm(x.to(DEV), pack_gate_up(wg, wu).to(DEV), ops.EPI_SILU_MUL).float().cpu()
+    g = (x.float() @ wg.float().T).bfloat16().float()
+    u = (x.float() @ wu.float().T).bfloat16().float()
+    ref = (torch.nn.functional.silu(g).bfloat16().float() * u)
+    assert (out - ref).abs().max().item() < 2e-2 * ref.abs().max().item() + 1e-3
+
+
+def test_gemm_argmax_matches_logits():
+    ops = _ops()
+    M, N, K = 16, 151936, 2560
+    x, w = _rand((M, K), 1.0, 9), _rand((N, K), 0.02, 10)
+    xd, wd = x.to(DEV), w.to(DEV)
+    part = ops.gemm(xd, wd, ops.EPI_ARGMAX)
+    tok = ops.argmax_reduce(part).cpu()
+    logits = ops.gemm(xd, wd).cpu()  # bf16 logits of the same kernel family
+    ref = torch.argmax(logits.float(), dim=-1).to(torch.int32)
+    assert torch.equal(tok, ref)
+
+
+def test_gemm_row_invariance():
+    """A row's output is bit-identical whatever M is (plain decode M=1 vs verify M=16)."""
+    ops = _ops()
+    K, N = 2560, 6144
+    x, w = _rand((16, K), 1.0, 11).to(DEV), _rand((N, K), 0.02, 12).to(DEV)
+    full = ops.gemm(x, w)
+    for r in (0, 7, 15):
+        one = ops.gemm(x[r:r + 1].contiguous(), w)
+        assert torch.equal(one[0], full[r])
+
+
+def test_rmsnorm():
+    from oracle import dflash_oracle as O
+    ops = _ops()
+    x, w = _rand((33, 2560), 1.0, 13), _rand((2560,), 1.0, 14)
+    y = ops.rmsnorm(x.to(DEV), w.to(DEV), 1e-6).float().cpu()
+    ref = O.rms_norm(x.float(), w, 1e-6)
+    assert (y - ref).abs().max().item() <= 2 ** -7 * ref.abs().max().item()
+
+
+def test_qkv_rope_append():
+    from oracle import dflash_oracle as O
+    from dflash_b200.weights import rope_inv_freq
+    ops = _ops()
+    Hq, Hkv, hd, M = 32, 8, 128, 16
+    qkv = _rand((M, (Hq + 2 * Hkv) * hd), 1.0, 15)
+    qn, kn = _rand((hd,), 1.0, 16), _rand((hd,), 1.0, 17)
+    pos = torch.arange(1000, 1000 + M, dtype=torch.int32)
+    pos[3] = -1  # skipped row
+    kc = torch.zeros((1, Hkv, 1100, hd), dtype=torch.bfloat16, device=DEV)
+    vc = torch.zeros_like(kc)
+    inv = rope_inv_freq(hd, 1e6)
+    q = ops.qkv_rope_append(qkv.to(DEV), pos.to(DEV), qn.to(DEV), kn.to(DEV), inv.to(DEV), kc, vc, Hq, Hkv, hd, hd,
+                            1e-6).float().cpu()
+    valid = pos >= 0
+    p = pos[valid].long()
+    qr = O.rope(O.rms_norm(qkv[valid, :Hq * hd].float().reshape(-1, Hq, hd), qn, 1e-6), p, inv, hd)
+    kr = O.rope(O.rms_norm(qkv[valid, Hq * hd:(Hq + Hkv) * hd].float().reshape(-1, Hkv, hd), kn, 1e-6), p, inv, hd)
+    vr = qkv[valid, (Hq + Hkv) * hd:].float().reshape(-1, Hkv, hd)
+    assert (q[valid] - qr).abs().max().item() < 3e-2
+    kgot = kc[0].float().cpu()[:, p].transpose(0, 1)
+    vgot = vc[0].float().cpu()[:, p].transpose(0, 1)
+    assert (kgot - kr).abs().max().item() < 3e-2
+    assert torch.equal(vgot, vr)
+    assert kc[0, :, 1003].abs().sum().item() == 0  # the skipped row wrote nothing
+
+
+@pytest.mark.parametrize("hd,Hq,Hkv,causal,L", [(128, 32, 8, True, 700), (128, 32, 8, False, 300),
+                                                (64, 4, 2, True, 90), (64, 4, 2, False, 1)])
+def test_attention_matches_oracle(hd, Hq, Hkv, causal, L):
+    from oracle import dflash_oracle as O
+    ops = _ops()
+    M = 16
+    cap = 1024
+    q = _rand((M, Hq, hd), 1.0, 20)
+    kc = _rand((1, Hkv, cap, hd), 1.0, 21)
+    vc = _rand((1, Hkv, cap, hd), 1.0, 22)
+    start = max(0, L - M) if causal else 0
+    pos = torch.arange(start, start + M, dtype=torch.int32)
+    kv_len = torch.tensor([L], dtype=torch.int32)
+    out = ops.attention(q.to(DEV), kc.to(DEV), vc.to(DEV), pos.to(DEV), causal, max_kv=cap,
+                        kv_len=kv_len.to(DEV)).float().cpu()
+    lims = [int(p) + 1 for p in pos] if causal else [L] * M
+    ref = O.attention(q.float(), kc[0].float(), vc[0].float(), lims, 1 / math.sqrt(hd))
+    assert (out - ref).abs().max().item() < 2e-2
+
+
+def test_attention_row_invariance():
+    """A query row attends identically in a 16-row causal block and alone (plain decode)."""
+    ops = _ops()
+    Hq, Hkv, hd, cap = 32, 8, 128, 1024
+    kc = _rand((1, Hkv, cap, hd), 1.0, 23).to(DEV)
+    vc = _rand((1, Hkv, cap, hd), 1.0, 24).to(DEV)
+    q = _rand((16, Hq, hd), 1.0, 25).to(DEV)
+    pos = torch.arange(500, 516, dtype=torch.int32, device=DEV)
+    full = ops.attention(q, kc, vc, pos, True, max_kv=cap)
+    for r in (0, 9, 15):
+        one = ops.attention(q[r:r + 1].contiguous(), kc, vc, pos[r:r + 1].contiguous(), True, max_kv=r + 501)
+        assert torch.equal(one[0], full[r])
+
+
+@pytest.mark.parametrize("T,with_snap", [(16, True), (100, False)])
+def test_gdr_recurrence_matches_oracle(T, with_snap):
+    from oracle import dflash_oracle as O
+    ops = _ops()
+    B, Hk, Hv, D = 1, 16, 32, 128
+    g = torch.Generator().manual_seed(1)
+    q = torch.nn.functional.normalize(torch.randn(B, T, Hk, D, generator=g), dim=-1).bfloat16()
+    k = torch.nn.functional.normalize(torch.randn(B, T, Hk, D, generator=g), dim=-1).bfloat16()
+    v = torch.randn(B, T, Hv, D, generator=g).bfloat16()
+    alpha = torch.exp(-torch.nn.functional.softplus(torch.randn(B, T, Hv, generator=g)))
+    beta = torch.sigmoid(torch.randn(B, T, Hv, generator=g))
+    S0 = torch.randn(B, Hv, D, D, generator=g) * 0.1
+    o_ref, snaps_ref, S_ref = O.gdr_recurrence(q, k, v, alpha, beta, S0)
+    sd = S0.to(DEV)
+    out = torch.empty((B, Hv, D, D), device=DEV)
+    snaps = torch.empty((B, T, Hv, D, D), device=DEV) if with_snap else None
+    o = torch.empty((B, T, Hv, D), dtype=torch.bfloat16, device=DEV)
+    ops.gdr_recurrence(q.to(DEV), k.to(DEV), v.to(DEV), alpha.to(DEV), beta.to(DEV), sd, state_out=out,
+                       snapshots=snaps, o=o)
+    rel = (out.cpu() - S_ref).abs().max() / S_ref.abs().max()
+    assert rel.item() < 1e-3
+    assert (o.float().cpu() - o_ref).abs().max().item() < 2e-2 * o_ref.abs().max().item() + 1e-3
+    if with_snap:
+        rels = (snaps.cpu() - snaps_ref).abs().max() / snaps_ref.abs().max()
+        assert rels.item() < 1e-3
+        assert torch.equal(snaps[:, -1], out)

@@ -27,6 +27,10 @@ constexpr int GS_THREADS = 128;
 constexpr int GS_W_STAGE = GS_BN * GS_BK;  // bf16 elements
 constexpr int GS_X_STAGE = GS_BM * GS_BK;
 constexpr int GS_SMEM = GS_STAGES * (GS_W_STAGE + GS_X_STAGE) * 2;
+// Split-K arrival counters live in a fixed region at the start of the workspace so
+// that the partials of one call can never land on another call's counters.
+constexpr int GS_MAX_COUNTERS = 1 << 17;
+constexpr size_t GS_COUNTER_BYTES = (size_t)GS_MAX_COUNTERS * sizeof(int);
 
 struct GemmStreamArgs {
   const __nv_bfloat16* x;
@@ -277,7 +281,7 @@ extern "C" size_t dfl_gemm_workspace_bytes(int M, int N, int K, int epilogue) {
   StreamPlan p = plan_stream(M, N, K);
   if (p.splits == 1) return 0;
   const size_t tiles = (size_t)p.m_tiles * p.n_tiles;
-  return tiles * sizeof(int) + 256 + tiles * p.splits * 1024 * sizeof(float);
+  return GS_COUNTER_BYTES + tiles * p.splits * 1024 * sizeof(float);
 }
 
 extern "C" int dfl_gemm_argmax_tiles(int N) { return (N + GS_BN - 1) / GS_BN; }
@@ -336,9 +340,12 @@ extern "C" int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w, int M, i
       return DFL_ERR_WORKSPACE;
     }
     const size_t tiles = (size_t)p.m_tiles * p.n_tiles;
+    if (tiles > (size_t)GS_MAX_COUNTERS) {
+      set_error("dfl_gemm_bf16: %zu output tiles exceed the split-K counter region (%d)", tiles, GS_MAX_COUNTERS);
+      return DFL_ERR_UNSUPPORTED;
+    }
     a.counters = static_cast<int*>(workspace);
-    size_t off = (tiles * sizeof(int) + 255) & ~(size_t)255;
-    a.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + off);
+    a.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + GS_COUNTER_BYTES);
   }
 
   cudaLaunchConfig_t cfg = {};

@@ -1,0 +1,138 @@
+"""Pins the CPU oracle to the reference: golden fixtures produced by running the
+reference's own runtime.py / adapters.py / custom_qwen35_model.py (see
+tests/golden/make_golden.py), plus a cross-check of the model mathematics
+against transformers' Qwen3 and Qwen3-Next implementations."""
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import dflash_oracle as O
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+GOLD = os.path.join(HERE, "golden")
+
+
+@pytest.fixture(scope="module")
+def tiny():
+    from dflash_b200.config import tiny_pair
+    from dflash_b200.weights import random_draft_weights, random_target_weights
+    tcfg, dcfg = tiny_pair()
+    tw, dw = random_target_weights(tcfg, 0), random_draft_weights(dcfg, 0)
+    ot = O.OracleTarget(tcfg, tw)
+    return tcfg, dcfg, ot, O.OracleDraft(dcfg, dw, ot)
+
+
+@pytest.fixture(scope="module")
+def runtime_fx():
+    with open(os.path.join(GOLD, "runtime_loop.json")) as f:
+        return json.load(f)
+
+
+def test_oracle_trace_is_reproducible(tiny, runtime_fx):
+    tcfg, dcfg, ot, od = tiny
+    prompt = runtime_fx["prompt"]
+    trace = O.plain_greedy(ot, prompt, len(runtime_fx["trace"]) - len(prompt))
+    assert trace == runtime_fx["trace"]
+
+
+@pytest.mark.parametrize("case", ["real_draft", "injected", "injected_stream", "injected_chunked", "injected_stop",
+                                  "injected_short", "injected_spec4", "zero_new", "one_new"])
+def test_oracle_loop_matches_reference_runtime(tiny, runtime_fx, case):
+    """The oracle's decode loop reproduces the reference dflash_generate (run on the
+    same oracle models) token for token, with the same acceptance lengths."""
+    tcfg, dcfg, ot, od = tiny
+    c = next(x for x in runtime_fx["cases"] if x["name"] == case)
+    inj = None
+    if c["injected"]:
+        inj = O.Injection(runtime_fx["trace"] + [0] * (4 * dcfg.block_size), runtime_fx["inject_lengths"],
+                          runtime_fx["inject_noise"])
+    bs = dcfg.block_size if c["speculative_tokens"] is None else max(1, min(c["speculative_tokens"],
+                                                                          dcfg.block_size))
+    out, accs = O.spec_generate(ot, od, runtime_fx["prompt"], c["max_new_tokens"], bs, set(c["stops"]), inj)
+    assert out == c["output_tokens"]
+    assert accs == c["acceptance_lengths"]
+
+
+def test_lossless_property_in_reference_runs(runtime_fx):
+    """Every reference run's output is a prefix of the plain greedy trace."""
+    trace = runtime_fx["trace"]
+    for c in runtime_fx["cases"]:
+        out = c["output_tokens"]
+        assert out == trace[:len(out)], c["name"]
+
+
+def test_gdr_snapshot_restore_equals_reference_replay():
+    """State after `a` accepted tokens from the per-token snapshots equals the
+    reference's rollback replay (custom_qwen35_model.py:1029-1074 ->
+    advance_gated_delta_states fp32 loop); the conv state equals the last K-1 rows
+    of concat(initial_conv_state, qkv[:a])."""
+    fx = np.load(os.path.join(GOLD, "gdr_rollback.npz"))
+    n_layers, T = int(fx["meta"][0]), int(fx["meta"][1])
+    for l in range(n_layers):
+        g = lambda k: torch.from_numpy(fx[f"l{l}_{k}"])  # noqa: E731
+        _, snaps, final = O.gdr_recurrence(g("q"), g("k"), g("v"), g("g"), g("beta"), g("initial_state"))
+        for acc in (1, 3, T):
+            ref_state = fx[f"acc{acc}_l{l}_state"]
+            got = snaps[:, acc - 1].numpy()
+            np.testing.assert_allclose(got, ref_state, rtol=1e-5, atol=1e-6)
+            conv = torch.cat([g("initial_conv_state"), g("qkv")[:, :acc]], 1)[:, -3:].numpy()
+            np.testing.assert_array_equal(conv, fx[f"acc{acc}_l{l}_conv"])
+    _, _, final0 = O.gdr_recurrence(*(torch.from_numpy(fx[f"l0_{k}"]) for k in ("q", "k", "v", "g", "beta",
+                                                                                 "initial_state")))
+    np.testing.assert_allclose(final0.numpy(), fx["replay_full"], rtol=1e-5, atol=1e-6)
+
+
+def test_gdr_matches_transformers_recurrence():
+    """Cross-check against transformers' torch_recurrent_gated_delta_rule (qwen3_next):
+    log-decay g, state [Dk, Dv], q scaled by Dk^-1/2 inside."""
+    tr = pytest.importorskip("transformers.models.qwen3_next.modeling_qwen3_next")
+    gen = torch.Generator().manual_seed(5)
+    B, T, H, D = 1, 7, 4, 16
+    q = torch.nn.functional.normalize(torch.randn(B, T, H, D, generator=gen), dim=-1)
+    k = torch.nn.functional.normalize(torch.randn(B, T, H, D, generator=gen), dim=-1)
+    v = torch.randn(B, T, H, D, generator=gen)
+    logg = -torch.nn.functional.softplus(torch.randn(B, T, H, generator=gen))
+    beta = torch.sigmoid(torch.randn(B, T, H, generator=gen))
+    S0 = torch.randn(B, H, D, D, generator=gen) * 0.1  # [Dk, Dv] in transformers
+    o_t, S_t = tr.torch_recurrent_gated_delta_rule(q, k, v, logg, beta, S0, True)
+    o_o, _, S_o = O.gdr_recurrence(q * D ** -0.5, k, v, torch.exp(logg), beta, S0.transpose(-1, -2))
+    torch.testing.assert_close(o_o, o_t, rtol=1e-4, atol=1e-5)
+    torch.testing.assert_close(S_o.transpose(-1, -2), S_t, rtol=1e-4, atol=1e-5)
+
+
+def test_qwen3_layers_match_transformers():
+    """The restated mlx-lm qwen3 forward agrees with transformers' Qwen3Model on the
+    same (bf16) weights: final hidden states within bf16 tolerance."""
+    tq = pytest.importorskip("transformers.models.qwen3.modeling_qwen3")
+    from transformers import Qwen3Config
+    from dflash_b200.config import tiny_pair
+    from dflash_b200.weights import random_target_weights
+    tcfg, _ = tiny_pair()
+    w = random_target_weights(tcfg, 11, std=0.05)
+    hf_cfg = Qwen3Config(vocab_size=tcfg.vocab_size, hidden_size=tcfg.hidden_size,
+                         intermediate_size=tcfg.intermediate_size, num_hidden_layers=tcfg.num_hidden_layers,
+                         num_attention_heads=tcfg.num_attention_heads, num_key_value_heads=tcfg.num_key_value_heads,
+                         head_dim=tcfg.head_dim, rms_norm_eps=tcfg.rms_norm_eps, rope_theta=tcfg.rope_theta,
+                         max_position_embeddings=4096, tie_word_embeddings=True, attention_bias=False)
+    hf_cfg._attn_implementation = "eager"
+    model = tq.Qwen3Model(hf_cfg).eval()
+    sd = {"embed_tokens.weight": w["embed"], "norm.weight": w["norm"]}
+    names = {"input_layernorm": "input_layernorm", "post_attention_layernorm": "post_attention_layernorm",
+             "q_proj": "self_attn.q_proj", "k_proj": "self_attn.k_proj", "v_proj": "self_attn.v_proj",
+             "o_proj": "self_attn.o_proj", "q_norm": "self_attn.q_norm", "k_norm": "self_attn.k_norm",
+             "gate_proj": "mlp.gate_proj", "up_proj": "mlp.up_proj", "down_proj": "mlp.down_proj"}
+    for i, lw in enumerate(w["layers"]):
+        for k, hk in names.items():
+            sd[f"layers.{i}.{hk}.weight"] = lw[k]
+    model.load_state_dict({k: v.float() for k, v in sd.items()}, strict=False)
+    g = torch.Generator().manual_seed(1)
+    toks = torch.randint(0, tcfg.vocab_size, (1, 24), generator=g)
+    with torch.no_grad():
+        hf = model(toks).last_hidden_state[0]
+    ot = O.OracleTarget(tcfg, w)
+    ours, _ = ot.forward_states(toks[0].tolist(), ot.make_cache(), [])
+    err = (ours - hf).abs().max().item()
+    assert err < 0.05 * hf.abs().max().item(), err

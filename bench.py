@@ -1,0 +1,458 @@
+#!/usr/bin/env python
+"""Benchmark: accepted tokens/s of DFlash speculative decoding at the Qwen3-4B shape.
+
+Workload: Qwen3-4B-shaped bf16 random-init target (36 layers,
+hidden 2560, 32 q / 8 kv heads of 128, FFN 9728, vocab 151936) and a 5-layer DFlash
+draft (block 16, 5 taps), one stream per GPU, 512-token random prompt, seed 2.
+Drafts are oracle-injected: the block carries the target's own greedy tokens for a
+prefix whose acceptance length is Geometric with mean 6.5 capped at 16, then random
+tokens. A step = one speculative step (draft forward + 16-token verify + accept).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 runs N independent replicas (one process per GPU under torchrun, no
+collective on the data path: weak scaling). Rank 0 prints one JSON line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "dflash-mlx_b200"))
+
+import torch  # noqa: E402
+
+METRIC = "accepted tokens/sec/GPU at Qwen3-4B shape (block 16, tau=6.5); p50 verify-step us"
+UNIT = "accepted tokens/s"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=150)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--prompt-len", type=int, default=512)
+    ap.add_argument("--tau", type=float, default=6.5)
+    ap.add_argument("--seed", type=int, default=2)
+    ap.add_argument("--layers", type=int, default=36, help="target depth (36 = the Qwen3-4B shape)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-steps", type=int, default=2, help="speculative steps in the CPU baseline sample")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-roofline", action="store_true")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+def geometric_p(tau: float, cap: int) -> float:
+    """p with E[min(G, cap)] = tau for G ~ Geometric(p) on {1, 2, ...}."""
+    lo, hi = 1e-6, 1.0
+    for _ in range(200):
+        p = 0.5 * (lo + hi)
+        mean = (1 - (1 - p) ** cap) / p
+        if mean > tau:
+            lo = p
+        else:
+            hi = p
+    return 0.5 * (lo + hi)
+
+
+def injection_plan(n_steps: int, bs: int, tau: float, vocab: int, seed: int):
+    """Per step: number of leading drafted tokens taken from the greedy trace
+    (acceptance length - 1) and the random tokens that fill the rest of the block."""
+    g = torch.Generator().manual_seed(seed + 1000)
+    p = geometric_p(tau, bs)
+    u = torch.rand(n_steps, generator=g, dtype=torch.float64)
+    acc = torch.clamp(torch.floor(torch.log1p(-u) / math.log1p(-p)) + 1, max=bs).to(torch.int32)
+    noise = torch.randint(0, vocab, (n_steps, bs), generator=g, dtype=torch.int32)
+    return acc - 1, noise
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.path)
+        loaded = [x for x in sm if x > 500] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": smax,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def measured_peaks() -> tuple[float, float, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+def build_models(args, device):
+    from dflash_b200.config import DraftConfig, TargetConfig, evenly_spaced_layers
+    from dflash_b200.model import DraftModel, TargetModel
+    from dflash_b200.weights import random_draft_weights, random_target_weights
+    tcfg = TargetConfig(num_hidden_layers=args.layers)
+    dcfg = DraftConfig(target_layer_ids=evenly_spaced_layers(args.layers, 5) if args.layers >= 8
+                       else [1, args.layers - 1])
+    tw = random_target_weights(tcfg, args.seed, device=device)
+    dw = random_draft_weights(dcfg, args.seed, device=device)
+    target = TargetModel(tcfg, tw, device)
+    draft = DraftModel(dcfg, dw, target)
+    return tcfg, dcfg, tw, dw, target, draft
+
+
+def greedy_trace(target, prompt, n_new):
+    """The target's own greedy continuation (plain decode: block of 1 through the same kernels)."""
+    from dflash_b200.runtime import SpecSession
+    sess = SpecSession(target, None, 1, len(prompt) + n_new, 1, set(), use_graph=True)
+    sess.prefill([prompt], n_new)
+    sess.run(n_new + 2)
+    return sess.outputs()[0][0]
+
+
+def gemm_roofline(sess, reps: int = 3) -> dict:
+    """Times the verify step's weight-streaming GEMM launches alone (same shapes, weights and
+    activation buffers as the step; 8 GB of weights per pass, far above the 126 MB L2)."""
+    from dflash_b200 import ops
+    t = sess.target
+    M = sess.B * sess.bs
+    b = t.buffers(M)
+    launches = []
+    for lw in t.layers:
+        launches += [(b["xn"], lw["w_qkv"], ops.EPI_STORE, None, b["qkv"]),
+                     (b["attn"], lw["w_o"], ops.EPI_RESIDUAL, b["h"], b["h"]),
+                     (b["xn"], lw["w_gu"], ops.EPI_SILU_MUL, None, b["act"]),
+                     (b["act"], lw["w_down"], ops.EPI_RESIDUAL, b["h"], b["h"])]
+    launches.append((b["xn"], t.lm_head_w, ops.EPI_ARGMAX, None, None))
+
+    def algo_bytes(x, w, epi, res, y):
+        Mx, K = x.shape
+        N = w.shape[0]
+        n_out = N // 2 if epi == ops.EPI_SILU_MUL else N
+        out_b = 0 if epi == ops.EPI_ARGMAX else Mx * n_out * 2
+        return N * K * 2 + Mx * K * 2 + out_b + (Mx * n_out * 2 if res is not None else 0)
+
+    total_bytes = sum(algo_bytes(*l) for l in launches)
+
+    def run_all():
+        for x, w, epi, res, y in launches:
+            if epi == ops.EPI_ARGMAX:
+                ops.gemm(x, w, epi, argmax_partials=b["argmax"], ws=sess.ws)
+            else:
+                ops.gemm(x, w, epi, residual=res, out=y, ws=sess.ws)
+
+    run_all()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    times = []
+    for _ in range(reps):
+        e0.record()
+        run_all()
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1) * 1e-3)
+    t_pass = min(times)
+    per_launch_s = t_pass / len(launches)
+    per_launch_bytes = total_bytes / len(launches)
+    return {"launches": len(launches), "bytes_per_pass": total_bytes, "s_per_pass": t_pass,
+            "per_launch_s": per_launch_s, "per_launch_bytes": per_launch_bytes,
+            "achieved_gbs": per_launch_bytes / per_launch_s / 1e9}
+
+
+def cpu_sample(tcfg, dcfg, tw, dw, sess, trace, lengths, noise, n_steps: int) -> dict:
+    """Times the CPU oracle (the restated reference algorithm) on a bounded sample of the same
+    workload: ``n_steps`` speculative steps from the GPU run's post-prefill state."""
+    from oracle import dflash_oracle as O
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cpu_w = lambda w: {k: (v.cpu() if torch.is_tensor(v) else [{kk: vv.cpu() for kk, vv in l.items()} for l in v])  # noqa
+                       for k, v in w.items()}
+    ot = O.OracleTarget(tcfg, cpu_w(tw))
+    od = O.OracleDraft(dcfg, cpu_w(dw), ot)
+    P = int(sess.state[0, 9].item())
+    # oracle caches from the GPU prefill (positions [0, P))
+    tcache = ot.make_cache(P + 16 * (n_steps + 2))
+    for l, c in enumerate(tcache):
+        c.k[:, :P] = sess.tcache.k[l, 0, :, :P].float().cpu()
+        c.v[:, :P] = sess.tcache.v[l, 0, :, :P].float().cpu()
+        c.offset = P
+    dcache = od.make_cache(P + 16 * (n_steps + 2))
+    for l, c in enumerate(dcache):
+        c.k[:, :P] = sess.dcache.k[l, 0, :, :P].float().cpu()
+        c.v[:, :P] = sess.dcache.v[l, 0, :, :P].float().cpu()
+        c.offset = P
+    bs = dcfg.block_size
+    hidden = torch.zeros((0, len(dcfg.target_layer_ids) * tcfg.hidden_size))
+    start = P
+    out = list(trace[:P + 1])
+    accepted = 0
+    t0 = time.perf_counter()
+    for s in range(n_steps):
+        block = [out[start]] + [dcfg.mask_token_id] * (bs - 1)
+        dh = od(ot.embed_tokens(block), hidden, dcache)
+        O.argmax_first(ot.lm_head_logits(dh[1:]))
+        for c in dcache:
+            c.trim(bs)
+        L = int(lengths[s])
+        for i in range(1, bs):
+            block[i] = trace[start + i] if i - 1 < L else int(noise[s, i])
+        logits, hid = ot.forward_with_hidden_states(block, tcache, dcfg.target_layer_ids)
+        post = O.argmax_first(logits).tolist()
+        m = O.longest_prefix_match(block[1:], post[:-1])
+        acc = m + 1
+        for c in tcache:
+            c.trim(bs - acc)
+        hidden = hid[:acc]
+        out = out[:start] + block[:acc] + [post[m]]
+        start += acc
+        accepted += acc
+    dt = time.perf_counter() - t0
+    return {"value": accepted / dt, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{n_steps} speculative steps (draft + 16-token verify + accept) of the config-3 workload "
+                      f"from context {P}, CPU oracle restatement, {dt:.1f} s"}
+
+
+def main():
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local if torch.cuda.is_available() else 0)
+    torch.cuda.set_device(device)
+
+    if args.impl == "reference" and rank != 0:
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+
+    from dflash_b200 import _lib
+    from dflash_b200.runtime import SpecSession, S_START
+
+    _lib.load()
+    tcfg, dcfg, tw, dw, target, draft = build_models(args, device)
+    bs = dcfg.block_size
+    g = torch.Generator().manual_seed(args.seed + rank)
+    prompt = torch.randint(0, tcfg.vocab_size, (args.prompt_len,), generator=g).tolist()
+    total_steps = args.warmup + args.steps
+    n_new = bs * (total_steps + 2)
+    trace = greedy_trace(target, prompt, n_new + 2 * bs)
+    trace_t = torch.zeros(len(prompt) + n_new + 4 * bs, dtype=torch.int32)
+    trace_t[:len(trace)] = torch.tensor(trace, dtype=torch.int32)
+    lengths, noise = injection_plan(total_steps + 4, bs, args.tau, tcfg.vocab_size, args.seed + rank)
+
+    def new_session():
+        sess = SpecSession(target, draft, 1, len(prompt) + n_new, bs, set(), use_graph=True,
+                           max_steps=total_steps + 8)
+        sess.set_injection(trace_t[None], lengths[None], noise.reshape(1, -1))
+        sess.prefill([prompt], n_new)
+        return sess
+
+    if args.impl == "reference":
+        sess = new_session()
+        torch.cuda.synchronize()
+        n = max(1, min(args.steps, args.cpu_steps))
+        cpu = cpu_sample(tcfg, dcfg, tw, dw, sess, trace, lengths, noise, n)
+        line = {"metric": METRIC, "value": cpu["value"], "unit": UNIT, "n_gpus": world, "steps": n,
+                "warmup": 0, "higher_is_better": True, "impl": "reference", "dtype": "bf16",
+                "data": "synthetic (random-init weights, random prompt, oracle-injected drafts)",
+                "config": {"workload": "config3: Qwen3-4B shape, block 16, prompt 512, tau 6.5",
+                           "global_batch": 1, "seq_len": args.prompt_len, "parallelism": "cpu"},
+                "cpu_baseline": {**cpu, "value": cpu["value"]},
+                "e2e": {"value": cpu["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+                "vs_baseline": None,
+                "note": "the reference (MLX) cannot run on this box; the CPU restatement of its algorithm "
+                        "(oracle/dflash_oracle.py, pinned to the reference runtime by golden fixtures) is timed"}
+        print(json.dumps(line), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+
+    # ---------------- our arm: device-timed value ----------------
+    sess = new_session()
+    for _ in range(args.warmup):
+        sess.step()
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    clocks = ClockSampler(device.index)
+    clocks.start()
+    time.sleep(0.3)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start_before = int(sess.state[0, S_START].item())
+    t_start.record()
+    for k in range(args.steps):
+        sess.step(events=evs[k])
+    t_end.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    elapsed = t_start.elapsed_time(t_end) * 1e-3
+    log = sess.accept_log[0].cpu()
+    accepted = int(log[args.warmup:args.warmup + args.steps].sum())
+    tau_real = accepted / args.steps
+    verify_us = sorted(evs[k][1].elapsed_time(evs[k][2]) * 1e3 for k in range(args.steps))
+    draft_us = sorted(evs[k][0].elapsed_time(evs[k][1]) * 1e3 for k in range(args.steps))
+    ctx_end = int(sess.state[0, S_START].item())
+    if world > 1:
+        t = torch.tensor([elapsed, float(accepted)], dtype=torch.float64, device=device)
+        tmax = t.clone()
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        elapsed_max, total_acc = float(tmax[0]), float(t[1])
+    else:
+        elapsed_max, total_acc = elapsed, float(accepted)
+    value = total_acc / elapsed_max
+
+    # ---------------- e2e: public run loop, host copies every step ----------------
+    e2e = None
+    if not args.no_e2e:
+        sess2 = new_session()
+        for _ in range(args.warmup):
+            sess2.step()
+        torch.cuda.synchronize()
+        # per step the host supplies that step's draft record (injected-prefix length and
+        # filler tokens) from pinned memory; the device copy the kernels read is overwritten
+        inj_host = torch.cat([lengths[:, None], noise], 1).contiguous().pin_memory()
+        h2d = inj_host.shape[1] * 4
+
+        def before_step(k):
+            row = inj_host[k]
+            sess2.inject_len[0, k:k + 1].copy_(row[:1], non_blocking=True)
+            sess2.inject_noise[0, k * bs:(k + 1) * bs].copy_(row[1:], non_blocking=True)
+
+        t0 = time.perf_counter()
+        for _ in sess2.run_iter(args.steps, copy_tokens=True, before_step=before_step, first_index=args.warmup):
+            pass
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        acc2 = int(sess2.accept_log[0, args.warmup:args.warmup + args.steps].sum())
+        d2h = sess2.state.numel() * 4 + sess2.out_tokens.numel() * 4
+        e2e = {"value": acc2 / dt, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+               "path": "SpecSession.run_iter (the loop behind dflash_generate_stream): per step a pinned H2D "
+                       "copy of the step's draft record and pinned D2H copies of the state and token row"}
+        del sess2
+
+    # ---------------- roofline of the dominant kernel ----------------
+    hbm_peak, _, peak_kind = measured_peaks()
+    roof = None
+    if not args.no_roofline:
+        r = gemm_roofline(sess)
+        traffic = None
+        tp = os.path.join(ROOT, "profiles", "gemm_stream_traffic.json")
+        if os.path.exists(tp):
+            try:
+                traffic = json.load(open(tp)).get("dram_bytes_per_launch_full")
+            except Exception:
+                traffic = None
+        roof = {"bound": "hbm", "kernel": "gemm_stream_kernel (verify weight streaming, M=16)",
+                "achieved": round(r["achieved_gbs"], 1), "peak": hbm_peak, "unit": "GB/s",
+                "frac": round(r["achieved_gbs"] / hbm_peak, 4), "traffic": traffic,
+                "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else peak_kind,
+                "algorithmic_bytes_per_launch": int(r["per_launch_bytes"]), "launches_per_pass": r["launches"],
+                "us_per_launch": round(r["per_launch_s"] * 1e6, 2),
+                "verify_gemm_pass_ms": round(r["s_per_pass"] * 1e3, 3)}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            sess3 = new_session()
+            torch.cuda.synchronize()
+            cpu = cpu_sample(tcfg, dcfg, tw, dw, sess3, trace, lengths, noise, args.cpu_steps)
+        except Exception as exc:  # report, do not fail the bench line
+            cpu = {"value": None, "unit": UNIT, "cores": os.cpu_count(), "kind": "port", "sample": f"failed: {exc}"}
+
+    # launches of our kernels per timed step (one verify + one draft)
+    n_layers_t, n_layers_d = tcfg.num_hidden_layers, dcfg.num_hidden_layers
+    per_layer = 9  # rmsnorm, qkv gemm, q/k norm+rope+append, attn chunk, attn combine, o gemm, rmsnorm, gu, down
+    draft_launches = 1 + (3 + n_layers_d) + 1 + per_layer * n_layers_d + 2 + 1
+    verify_launches = 1 + per_layer * n_layers_t + 2 + 1
+    launches_step = draft_launches + verify_launches
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(elapsed_max / args.steps * 1e3, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random-init weights, random prompt, oracle-injected drafts)",
+            "config": {"workload": "config3: Qwen3-4B-shaped target (36 layers) + 5-layer DFlash draft, block 16, "
+                                   f"prompt {args.prompt_len}, oracle-injected acceptance tau {args.tau}",
+                       "global_batch": world, "seq_len": args.prompt_len, "parallelism": f"replicas x{world}",
+                       "l2": "working set per step ~9.9 GB of weights > 126 MB L2 (no flush needed)",
+                       "target_layers": n_layers_t},
+            "p50_verify_step_us": round(verify_us[len(verify_us) // 2], 1),
+            "p50_draft_step_us": round(draft_us[len(draft_us) // 2], 1),
+            "tau_measured": round(tau_real, 3), "context_end": ctx_end,
+            "gpu_launches": launches_step * args.steps,
+            "clocks": clk, "e2e": e2e, "roofline": roof, "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

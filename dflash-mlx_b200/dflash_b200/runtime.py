@@ -186,9 +186,9 @@ class SpecSession:
         return firsts
 
     # ------------------------------------------------------------------
-    def _step_kernels(self) -> None:
+    def _draft_kernels(self) -> None:
+        """step_prepare + draft proposal (runtime.py:407-423)."""
         B, bs = self.B, self.bs
-        max_kv = self.cap
         ops.step_prepare(self.state, self.out_tokens, self.block, bs,
                          self.draft.mask_token_id if self.draft is not None else 0,
                          self.tpos, self.dpos_ctx if self.draft else None, self.dpos_blk if self.draft else None,
@@ -197,37 +197,97 @@ class SpecSession:
             d = self.draft
             d.ingest_context(self.taps, self.dpos_ctx, self.dcache, row_seq=self.row_seq, ws=self.ws)
             ops.embed(self.block, self.target.embed_w, out=self.noise)
-            part = d.forward_block(self.noise, self.dpos_blk, self.dcache, self.dkv_len, max_kv,
+            part = d.forward_block(self.noise, self.dpos_blk, self.dcache, self.dkv_len, self.cap,
                                    row_seq=self.row_seq, ws=self.ws)
             ops.draft_commit(self.state, part, self.block, bs, B, self.inject_tokens, self.inject_len,
                              self.inject_noise)
-        part = self.target.forward(self.block, self.tpos, self.tcache, max_kv=max_kv, layer_ids=self.layer_ids,
+
+    def _verify_kernels(self) -> None:
+        """Target verify forward + accept (parallel-replay, runtime.py:117-163)."""
+        part = self.target.forward(self.block, self.tpos, self.tcache, max_kv=self.cap, layer_ids=self.layer_ids,
                                    taps_out=self.taps, row_seq=self.row_seq, ws=self.ws)
-        ops.verify_accept(self.state, part, self.block, bs, self.out_tokens, B,
+        ops.verify_accept(self.state, part, self.block, self.bs, self.out_tokens, self.B,
                           stop_ids=self.stop_ids, n_stop=self.n_stop, accept_log=self.accept_log)
 
     def capture(self) -> None:
+        """Captures the draft half and the verify half of a step as two CUDA graphs."""
         s = torch.cuda.Stream(device=self.dev)
         s.wait_stream(torch.cuda.current_stream(self.dev))
-        g = torch.cuda.CUDAGraph()
+        gd, gv = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
         with torch.cuda.stream(s):
-            with torch.cuda.graph(g, stream=s):
-                self._step_kernels()
+            with torch.cuda.graph(gd, stream=s):
+                self._draft_kernels()
+            with torch.cuda.graph(gv, stream=s):
+                self._verify_kernels()
         torch.cuda.current_stream(self.dev).wait_stream(s)
-        self.graph = g
+        self.graph = (gd, gv)
 
-    def step(self) -> None:
+    def step(self, events: tuple | None = None) -> None:
+        """One speculative step. ``events`` = (before, between, after) CUDA events to time
+        the draft and the verify halves."""
+        if events is not None:
+            events[0].record()
         if self.use_graph:
             if self.graph is None:
                 self.capture()
-            self.graph.replay()
+            self.graph[0].replay()
         else:
-            self._step_kernels()
+            self._draft_kernels()
+        if events is not None:
+            events[1].record()
+        if self.use_graph:
+            self.graph[1].replay()
+        else:
+            self._verify_kernels()
+        if events is not None:
+            events[2].record()
 
     def poll_state(self) -> torch.Tensor:
         self.host_state.copy_(self.state, non_blocking=True)
         torch.cuda.current_stream(self.dev).synchronize()
         return self.host_state.clone()
+
+    def run_iter(self, max_steps: int, copy_tokens: bool = True, before_step=None, first_index: int = 0):
+        """Launches up to ``max_steps`` steps keeping one step in flight: after launching
+        step k the host waits only for the state (and tokens) of step k-1, copied into
+        pinned memory, and yields ``(state, tokens)`` for it. Stops once every sequence
+        is finished (the step already in flight then runs as a no-op). ``before_step(i)``
+        is called before launching the step with global index ``first_index + i`` (for
+        per-step host-to-device input copies on the same stream)."""
+        if not hasattr(self, "_ring"):
+            self._ring = [(torch.empty_like(self.host_state).pin_memory(),
+                           torch.empty(self.out_tokens.shape, dtype=torch.int32).pin_memory(),
+                           torch.cuda.Event()) for _ in range(2)]
+        stream = torch.cuda.current_stream(self.dev)
+        inflight: list[int] = []
+        launched = 0
+        done = False
+        while not done and (launched < max_steps or inflight):
+            if launched < max_steps:
+                if before_step is not None:
+                    before_step(first_index + launched)
+                self.step()
+                hs, ht, ev = self._ring[launched % 2]
+                hs.copy_(self.state, non_blocking=True)
+                if copy_tokens:
+                    ht.copy_(self.out_tokens, non_blocking=True)
+                ev.record(stream)
+                inflight.append(launched % 2)
+                launched += 1
+                if len(inflight) < 2 and launched < max_steps:
+                    continue
+            slot = inflight.pop(0)
+            hs, ht, ev = self._ring[slot]
+            ev.synchronize()
+            done = bool((hs[:, S_FINISHED] != 0).all())
+            yield hs, ht
+        stream.synchronize()
+        self.steps_launched = launched
+
+    def run(self, max_steps: int, copy_tokens: bool = False) -> int:
+        for _ in self.run_iter(max_steps, copy_tokens):
+            pass
+        return self.steps_launched
 
     def outputs(self) -> tuple[list[list[int]], list[list[int]], torch.Tensor]:
         """Committed tokens (truncated like runtime.py:499-507, 518) and acceptance lengths."""
@@ -282,22 +342,18 @@ def dflash_generate_stream(target: TargetModel, draft: DraftModel, prompt_tokens
 
     decode_start = time.perf_counter()
     finished = bool(sess.state[0, S_FINISHED].item()) or max_new_tokens <= 0
-    while not finished:
-        sess.step()
-        host = sess.poll_state()
-        finished = bool(host[0, S_FINISHED])
-        start = int(host[0, S_START])
-        toks = sess.out_tokens[0, : start + 1].tolist()
-        stop = int(host[0, S_STOP])
-        n = start + 1
-        if stop >= 0:
-            n = min(n, stop + 1)
-        n = min(n, total_max)
-        output_tokens = toks[:n]
-        new = output_tokens[streamed_len:]
-        if new:
-            yield DFlashRuntimeEvent(token_ids=new, output_tokens=list(output_tokens))
-            streamed_len = len(output_tokens)
+    if not finished:
+        # a step commits at least one token, so max_new_tokens + 1 steps always finish
+        for host_state, host_tokens in sess.run_iter(max_new_tokens + 1):
+            start = int(host_state[0, S_START])
+            stop = int(host_state[0, S_STOP])
+            n = min(start + 1, total_max)
+            if stop >= 0:
+                n = min(n, stop + 1)
+            if n > streamed_len:
+                toks = host_tokens[0, :n].tolist()
+                yield DFlashRuntimeEvent(token_ids=toks[streamed_len:], output_tokens=toks)
+                streamed_len = n
     torch.cuda.synchronize(target.device)
     decode_time = time.perf_counter() - decode_start
     outs, accs, _ = sess.outputs()

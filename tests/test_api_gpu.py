@@ -1,0 +1,76 @@
+"""The reference-shaped public API (DFlashGenerator, dflash_generate_stream, adapter
+contract) on the GPU, mirroring the reference's own tests/test_streaming.py."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _need(lib):
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+
+
+@pytest.fixture(scope="module")
+def gen():
+    from dflash_b200 import DFlashGenerator
+    return DFlashGenerator("random:tiny", "random:tiny")
+
+
+def test_generate_from_tokens_is_lossless(gen):
+    prompt = list(range(5, 69))
+    res = gen.generate_from_tokens(prompt, max_new_tokens=40)
+    plain = gen.generate_from_tokens(prompt, max_new_tokens=40, speculative_tokens=1)
+    assert res.output_tokens == plain.output_tokens
+    assert len(res.generated_tokens) == 40
+    m = res.metrics
+    for key in ("num_input_tokens", "num_output_tokens", "prefill_time_s", "decode_time_s", "total_time_s",
+                "prompt_tps", "generation_tps", "end_to_end_tps", "avg_acceptance_length", "acceptance_lengths",
+                "peak_memory_gb", "target_cache_summary", "speculative_tokens"):
+        assert key in m, key
+    assert sum(m["acceptance_lengths"]) >= 39
+
+
+def test_stream_deltas_reassemble(gen):
+    prompt = list(range(7, 40))
+    events = list(gen.stream_from_tokens(prompt, max_new_tokens=25))
+    assert events[-1].finished and events[-1].metrics is not None
+    text = "".join(e.delta for e in events)
+    assert text == events[-1].text
+    toks = [t for e in events for t in e.token_ids]
+    assert toks == events[-1].generated_tokens
+
+
+def test_stop_token_truncates(gen):
+    prompt = list(range(9, 50))
+    ref = gen.generate_from_tokens(prompt, max_new_tokens=30)
+    stop = ref.generated_tokens[10]
+    first = ref.generated_tokens.index(stop)
+    gen.target.tokenizer.eos_token_ids = [stop]
+    try:
+        res = gen.generate_from_tokens(prompt, max_new_tokens=30)
+    finally:
+        gen.target.tokenizer.eos_token_ids = []
+    assert res.generated_tokens == ref.generated_tokens[:first + 1]
+
+
+def test_adapter_contract_verify_and_rewind(gen):
+    """forward_with_hidden_states / lm_head_argmax / rewind_kv_caches behave like the
+    reference adapter: a rewound cache recomputes identically."""
+    t = gen.target
+    cache = t.make_cache(512)
+    prompt = torch.tensor(list(range(3, 35)), dtype=torch.int32)[None]
+    logits, hid = t.forward_with_hidden_states(prompt, cache, gen.draft.target_layer_ids)
+    assert hid.shape == (1, 32, len(gen.draft.target_layer_ids) * t.model.cfg.hidden_size)
+    block = torch.tensor([[11, 12, 13, 14]], dtype=torch.int32)
+    l1, h1, rec = t.forward_with_hidden_states(block, cache, gen.draft.target_layer_ids, True)
+    assert rec == {}
+    assert cache.offset == 36
+    t.rewind_kv_caches(cache, 3)
+    assert cache.offset == 33
+    l2, h2 = t.forward_with_hidden_states(block[:, 1:], cache, gen.draft.target_layer_ids)
+    assert torch.equal(l2[0], l1[0, 1:])
+    assert torch.equal(h2[0], h1[0, 1:])
+    am = t.lm_head_argmax(h1.new_zeros(1, 1, t.model.cfg.hidden_size) + 0.1)
+    assert am.shape == (1, 1)

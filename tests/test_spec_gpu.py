@@ -82,10 +82,11 @@ def test_tiny_injected_acceptance_matches_oracle():
     # expected acceptance from the oracle loop run on the device's own greedy trace
     exp = []
     start = len(prompt)
+    trl = tr.tolist()
     for s in range(len(accs)):
         L = int(lengths[s])
-        blk = [trace[start]] + [trace[start + i] if i - 1 < L else int(noise[s, i]) for i in range(1, bs)]
-        m = O.longest_prefix_match(blk[1:], [trace[start + i] for i in range(1, bs)])
+        blk = [trl[start]] + [trl[start + i] if i - 1 < L else int(noise[s, i]) for i in range(1, bs)]
+        m = O.longest_prefix_match(blk[1:], [trl[start + i] for i in range(1, bs)])
         exp.append(m + 1)
         start += m + 1
         if start >= len(prompt) + max_new:
@@ -111,7 +112,15 @@ def test_qwen3_4b_layer_logits_parity():
     logits = target.forward(toks, pos, cache, max_kv=48, layer_ids=[0, 1], taps_out=taps, head="logits")
     ot = O.OracleTarget(tcfg, tw)
     ref_logits, ref_taps = ot.forward_with_hidden_states(prompt, ot.make_cache(128), [0, 1])
-    err = (logits.float().cpu() - ref_logits).abs().max().item()
-    print("max abs logit error", err)
-    assert err <= 2e-2
+    got = logits.float().cpu()
+    diff = (got - ref_logits).abs()
+    # 2e-2 absolute, widened to 2e-2 relative where |logit| > 1: a bf16 logit in [4, 8)
+    # has an ulp of 2^-5 = 0.031, so an absolute 2e-2 bound is below one ulp there.
+    bound = 2e-2 * ref_logits.abs().clamp_min(1.0)
+    print(f"logits: max|ref| {ref_logits.abs().max().item():.3f} max abs err {diff.max().item():.4f} "
+          f"mean abs err {diff.mean().item():.2e} exact {(diff == 0).float().mean().item():.3f}")
+    assert bool((diff <= bound).all()), (diff - bound).max().item()
+    agree = (got.argmax(-1) == ref_logits.argmax(-1)).float().mean().item()
+    print(f"greedy-token agreement {agree:.3f}")
+    assert agree >= 0.9
     assert (taps.float().cpu() - ref_taps).abs().max().item() < 5e-2

@@ -69,13 +69,15 @@ def test_tiny_injected_acceptance_matches_oracle():
     g = torch.Generator().manual_seed(3)
     prompt = torch.randint(0, tcfg.vocab_size, (64,), generator=g).tolist()
     max_new = 96
-    trace, _ = _run(target, None, prompt, max_new, 1)
     bs = dcfg.block_size
+    # the trace runs past the spec run's end so the last block's posterior is known
+    long_trace, _ = _run(target, None, prompt, max_new + 2 * bs, 1)
+    trace = long_trace[:len(prompt) + max_new]
     steps = max_new + 1
     lengths = torch.randint(0, bs, (steps,), generator=g)
     noise = torch.randint(0, tcfg.vocab_size, (steps, bs), generator=g)
     tr = torch.zeros(len(prompt) + max_new + 3 * bs, dtype=torch.int32)
-    tr[:len(trace)] = torch.tensor(trace, dtype=torch.int32)
+    tr[:len(long_trace)] = torch.tensor(long_trace, dtype=torch.int32)
     spec, accs = _run(target, draft, prompt, max_new, bs,
                       inject=(tr[None], lengths[None].to(torch.int32), noise.reshape(1, -1).to(torch.int32)))
     assert spec == trace
@@ -114,13 +116,15 @@ def test_qwen3_4b_layer_logits_parity():
     ref_logits, ref_taps = ot.forward_with_hidden_states(prompt, ot.make_cache(128), [0, 1])
     got = logits.float().cpu()
     diff = (got - ref_logits).abs()
-    # 2e-2 absolute, widened to 2e-2 relative where |logit| > 1: a bf16 logit in [4, 8)
-    # has an ulp of 2^-5 = 0.031, so an absolute 2e-2 bound is below one ulp there.
-    bound = 2e-2 * ref_logits.abs().clamp_min(1.0)
+    # The oracle computed in bf16 and the same oracle computed in fp32 differ by up to
+    # 0.062 (mean 0.009) on these logits: that is the model's own bf16 sensitivity, and
+    # no bf16 implementation (the reference's MLX path included) can beat it per logit.
+    # Bound: mean abs error <= 2e-2, max abs error <= 0.08.
     print(f"logits: max|ref| {ref_logits.abs().max().item():.3f} max abs err {diff.max().item():.4f} "
           f"mean abs err {diff.mean().item():.2e} exact {(diff == 0).float().mean().item():.3f}")
-    assert bool((diff <= bound).all()), (diff - bound).max().item()
+    assert diff.mean().item() <= 2e-2
+    assert diff.max().item() <= 0.08
     agree = (got.argmax(-1) == ref_logits.argmax(-1)).float().mean().item()
     print(f"greedy-token agreement {agree:.3f}")
-    assert agree >= 0.9
+    assert agree >= 0.95
     assert (taps.float().cpu() - ref_taps).abs().max().item() < 5e-2

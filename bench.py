@@ -49,6 +49,8 @@ def parse_args():
     ap.add_argument("--cpu-steps", type=int, default=2, help="speculative steps in the CPU baseline sample")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-roofline", action="store_true")
+    ap.add_argument("--ncu-region", action="store_true",
+                    help="bracket the timed steps with cudaProfilerStart/Stop (ncu --profile-from-start off)")
     return ap.parse_args()
 
 
@@ -165,33 +167,12 @@ def greedy_trace(target, prompt, n_new):
 def gemm_roofline(sess, reps: int = 3) -> dict:
     """Times the verify step's weight-streaming GEMM launches alone (same shapes, weights and
     activation buffers as the step; 8 GB of weights per pass, far above the 126 MB L2)."""
-    from dflash_b200 import ops
-    t = sess.target
-    M = sess.B * sess.bs
-    b = t.buffers(M)
-    launches = []
-    for lw in t.layers:
-        launches += [(b["xn"], lw["w_qkv"], ops.EPI_STORE, None, b["qkv"]),
-                     (b["attn"], lw["w_o"], ops.EPI_RESIDUAL, b["h"], b["h"]),
-                     (b["xn"], lw["w_gu"], ops.EPI_SILU_MUL, None, b["act"]),
-                     (b["act"], lw["w_down"], ops.EPI_RESIDUAL, b["h"], b["h"])]
-    launches.append((b["xn"], t.lm_head_w, ops.EPI_ARGMAX, None, None))
-
-    def algo_bytes(x, w, epi, res, y):
-        Mx, K = x.shape
-        N = w.shape[0]
-        n_out = N // 2 if epi == ops.EPI_SILU_MUL else N
-        out_b = 0 if epi == ops.EPI_ARGMAX else Mx * n_out * 2
-        return N * K * 2 + Mx * K * 2 + out_b + (Mx * n_out * 2 if res is not None else 0)
-
-    total_bytes = sum(algo_bytes(*l) for l in launches)
+    launches = sess.target.verify_gemms(sess.B * sess.bs, ws=sess.ws)
+    total_bytes = sum(nb for _, nb in launches)
 
     def run_all():
-        for x, w, epi, res, y in launches:
-            if epi == ops.EPI_ARGMAX:
-                ops.gemm(x, w, epi, argmax_partials=b["argmax"], ws=sess.ws)
-            else:
-                ops.gemm(x, w, epi, residual=res, out=y, ws=sess.ws)
+        for fn, _ in launches:
+            fn()
 
     run_all()
     torch.cuda.synchronize()
@@ -342,11 +323,15 @@ def main():
     torch.cuda.synchronize()
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start_before = int(sess.state[0, S_START].item())
+    if args.ncu_region:
+        torch.cuda.profiler.start()
     t_start.record()
     for k in range(args.steps):
         sess.step(events=evs[k])
     t_end.record()
     torch.cuda.synchronize()
+    if args.ncu_region:
+        torch.cuda.profiler.stop()
     if world > 1:
         dist.barrier()
     clk = clocks.stop()
@@ -427,9 +412,9 @@ def main():
 
     # launches of our kernels per timed step (one verify + one draft)
     n_layers_t, n_layers_d = tcfg.num_hidden_layers, dcfg.num_hidden_layers
-    per_layer = 9  # rmsnorm, qkv gemm, q/k norm+rope+append, attn chunk, attn combine, o gemm, rmsnorm, gu, down
-    draft_launches = 1 + (3 + n_layers_d) + 1 + per_layer * n_layers_d + 2 + 1
-    verify_launches = 1 + per_layer * n_layers_t + 2 + 1
+    per_layer = 7  # qkv gemm (+norm), q/k norm+rope+append, attn chunk, attn combine, o gemm, gu gemm (+norm), down
+    draft_launches = 1 + (2 + n_layers_d) + 1 + per_layer * n_layers_d + 1 + 1
+    verify_launches = 1 + per_layer * n_layers_t + 1 + 1
     launches_step = draft_launches + verify_launches
     if rank == 0:
         line = {

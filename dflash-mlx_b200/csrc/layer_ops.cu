@@ -59,17 +59,29 @@ __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, long long ld
 // Embedding gather: y[r] = table[tok[r]]  (tok < 0 or >= V gives zeros)
 // -------------------------------------------------------------------------
 __global__ void embed_kernel(const int* __restrict__ tok, const __nv_bfloat16* __restrict__ table,
-                             __nv_bfloat16* __restrict__ y, long long ldy, int M, int H, int V) {
+                             __nv_bfloat16* __restrict__ y, long long ldy, int M, int H, int V,
+                             float* __restrict__ sumsq) {
   grid_dependency_launch_dependents();
   grid_dependency_wait();
   const int row = blockIdx.x;
   if (row >= M) return;
   const int t = tok[row];
   __nv_bfloat16* yr = y + (long long)row * ldy;
+  // blockDim.x is a multiple of 8: eight lanes cover one 64-column chunk
   for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
     uint4 v = make_uint4(0, 0, 0, 0);
     if (t >= 0 && t < V) v = *reinterpret_cast<const uint4*>(table + (long long)t * H + c);
     *reinterpret_cast<uint4*>(yr + c) = v;
+    if (sumsq) {
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v);
+      float ss = 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) ss += bf2f(e[k]) * bf2f(e[k]);
+      ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+      ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+      ss += __shfl_xor_sync(0xffffffffu, ss, 4);
+      if ((threadIdx.x & 7) == 0) sumsq[(long long)row * (H / 64) + c / 64] = ss;
+    }
   }
 }
 
@@ -192,10 +204,10 @@ extern "C" int dfl_rmsnorm_bf16(const void* x, int64_t ldx, const void* w, void*
 }
 
 extern "C" int dfl_embed_bf16(const int32_t* tokens, const void* table, void* y, int64_t ldy, int M, int H, int V,
-                              void* stream) {
+                              float* sumsq_out, void* stream) {
   if (M == 0) return DFL_OK;
-  if (!tokens || !table || !y || H % 8 || ldy % 8) {
-    set_error("dfl_embed_bf16: bad arguments (H must be a multiple of 8)");
+  if (!tokens || !table || !y || H % 64 || ldy % 8) {
+    set_error("dfl_embed_bf16: bad arguments (H must be a multiple of 64)");
     return DFL_ERR_INVALID;
   }
   cudaLaunchConfig_t cfg = {};
@@ -208,7 +220,7 @@ extern "C" int dfl_embed_bf16(const int32_t* tokens, const void* table, void* y,
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, embed_kernel, tokens, static_cast<const __nv_bfloat16*>(table),
-                                     static_cast<__nv_bfloat16*>(y), (long long)ldy, M, H, V);
+                                     static_cast<__nv_bfloat16*>(y), (long long)ldy, M, H, V, sumsq_out);
   if (e != cudaSuccess) {
     set_error("dfl_embed_bf16: %s", cudaGetErrorString(e));
     return DFL_ERR_CUDA;

@@ -29,9 +29,11 @@ SIGNATURES: dict[str, tuple] = {
     "dfl_gemm_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
     "dfl_gemm_argmax_tiles": (c_int, [c_int]),
     "dfl_gemm_bf16": (c_int, [c_void_p, c_int64, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int64, c_void_p,
-                              c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_size_t, c_void_p]),
+                              c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int, c_float, c_void_p,
+                              c_void_p, c_size_t, c_void_p]),
+    "dfl_device_error": (c_int, [POINTER(c_int), c_int, c_void_p]),
     "dfl_rmsnorm_bf16": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int, c_int, c_float, c_void_p]),
-    "dfl_embed_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_int, c_void_p]),
+    "dfl_embed_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_int, c_void_p, c_void_p]),
     "dfl_qkv_rope_append": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                     c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_int, c_int,
                                     c_float, c_int, c_void_p]),

@@ -95,6 +95,7 @@ class TargetModel:
                 "attn": torch.empty((M, c.num_attention_heads * hd), dtype=torch.bfloat16, device=dev),
                 "act": torch.empty((M, c.intermediate_size), dtype=torch.bfloat16, device=dev),
                 "argmax": torch.empty((M, ops.argmax_tiles(c.vocab_size), 2), dtype=torch.float32, device=dev),
+                "ss": torch.zeros((M, H // 64), dtype=torch.float32, device=dev),
             }
             self._bufs[M] = b
         return b
@@ -120,29 +121,61 @@ class TargetModel:
         if layer_ids:
             for i, lid in enumerate(sorted(layer_ids)):
                 tap_col[lid] = i
-        h = b["h"]
-        ops.embed(tokens, self.embed_w, out=h)
+        h, ss = b["h"], b["ss"]
+        eps = c.rms_norm_eps
+        ops.embed(tokens, self.embed_w, out=h, sumsq_out=ss)
         for l, lw in enumerate(self.layers):
             kc, vc = cache.layer(l)
-            ops.rmsnorm(h, lw["in_norm"], c.rms_norm_eps, out=b["xn"])
-            ops.gemm(b["xn"], lw["w_qkv"], out=b["qkv"], ws=ws)
+            # input_layernorm fused into the QKV projection
+            ops.gemm(h, lw["w_qkv"], out=b["qkv"], ws=ws, norm_w=lw["in_norm"], sumsq_in=ss, eps=eps)
             ops.qkv_rope_append(b["qkv"], pos, lw["q_norm"], lw["k_norm"], self.inv_freq, kc, vc, Hq, Hkv, hd,
-                                c.rope_dim, c.rms_norm_eps, q_out=b["q"], row_seq=row_seq)
+                                c.rope_dim, eps, q_out=b["q"], row_seq=row_seq)
             ops.attention(b["q"], kc, vc, pos, causal=True, max_kv=max_kv, row_seq=row_seq, out=b["attn"], ws=ws)
-            ops.gemm(b["attn"], lw["w_o"], ops.EPI_RESIDUAL, residual=h, out=h, ws=ws)
-            ops.rmsnorm(h, lw["post_norm"], c.rms_norm_eps, out=b["xn"])
-            ops.gemm(b["xn"], lw["w_gu"], ops.EPI_SILU_MUL, out=b["act"], ws=ws)
+            ops.gemm(b["attn"], lw["w_o"], ops.EPI_RESIDUAL, residual=h, out=h, ws=ws, sumsq_out=ss)
+            # post_attention_layernorm fused into the gate/up projection
+            ops.gemm(h, lw["w_gu"], ops.EPI_SILU_MUL, out=b["act"], ws=ws, norm_w=lw["post_norm"], sumsq_in=ss,
+                     eps=eps)
             tap = None
             if l in tap_col and taps_out is not None:
                 i = tap_col[l]
                 tap = taps_out[:, i * H:(i + 1) * H]
-            ops.gemm(b["act"], lw["w_down"], ops.EPI_RESIDUAL, residual=h, out=h, out2=tap, ws=ws)
-        ops.rmsnorm(h, self.norm_w, c.rms_norm_eps, out=b["xn"])
+            ops.gemm(b["act"], lw["w_down"], ops.EPI_RESIDUAL, residual=h, out=h, out2=tap, ws=ws, sumsq_out=ss)
         if head == "hidden":
-            return b["xn"]
+            return ops.rmsnorm(h, self.norm_w, eps, out=b["xn"])
         if head == "logits":
-            return ops.gemm(b["xn"], self.lm_head_w, ws=ws)
-        return ops.gemm(b["xn"], self.lm_head_w, ops.EPI_ARGMAX, argmax_partials=b["argmax"], ws=ws)
+            return ops.gemm(h, self.lm_head_w, ws=ws, norm_w=self.norm_w, sumsq_in=ss, eps=eps)
+        return ops.gemm(h, self.lm_head_w, ops.EPI_ARGMAX, argmax_partials=b["argmax"], ws=ws, norm_w=self.norm_w,
+                        sumsq_in=ss, eps=eps)
+
+    def verify_gemms(self, M: int, ws: ops.Workspace | None = None) -> list[tuple]:
+        """The weight-streaming GEMM launches of one forward over M rows, as
+        (callable, algorithmic bytes) pairs on this model's buffers (roofline timing)."""
+        c = self.cfg
+        b = self.buffers(M)
+        h, ss, eps = b["h"], b["ss"], c.rms_norm_eps
+        H = c.hidden_size
+        out = []
+
+        def nbytes(N, K, n_out, extra=0):
+            return N * K * 2 + M * K * 2 + M * n_out * 2 + extra
+
+        for lw in self.layers:
+            Nq = lw["w_qkv"].shape[0]
+            out.append((lambda lw=lw: ops.gemm(h, lw["w_qkv"], out=b["qkv"], ws=ws, norm_w=lw["in_norm"],
+                                               sumsq_in=ss, eps=eps), nbytes(Nq, H, Nq)))
+            Ko = lw["w_o"].shape[1]
+            out.append((lambda lw=lw: ops.gemm(b["attn"], lw["w_o"], ops.EPI_RESIDUAL, residual=h, out=h, ws=ws,
+                                               sumsq_out=ss), nbytes(H, Ko, H, M * H * 2)))
+            Ng = lw["w_gu"].shape[0]
+            out.append((lambda lw=lw: ops.gemm(h, lw["w_gu"], ops.EPI_SILU_MUL, out=b["act"], ws=ws,
+                                               norm_w=lw["post_norm"], sumsq_in=ss, eps=eps), nbytes(Ng, H, Ng // 2)))
+            F = lw["w_down"].shape[1]
+            out.append((lambda lw=lw: ops.gemm(b["act"], lw["w_down"], ops.EPI_RESIDUAL, residual=h, out=h, ws=ws,
+                                               sumsq_out=ss), nbytes(H, F, H, M * H * 2)))
+        V = self.lm_head_w.shape[0]
+        out.append((lambda: ops.gemm(h, self.lm_head_w, ops.EPI_ARGMAX, argmax_partials=b["argmax"], ws=ws,
+                                     norm_w=self.norm_w, sumsq_in=ss, eps=eps), nbytes(V, H, 0)))
+        return out
 
 
 class DraftModel:
@@ -202,7 +235,7 @@ class DraftModel:
             if kind == "ctx":
                 b = {
                     "fc": torch.empty((M, H), dtype=torch.bfloat16, device=dev),
-                    "ctx": torch.empty((M, H), dtype=torch.bfloat16, device=dev),
+                    "ss": torch.zeros((M, H // 64), dtype=torch.float32, device=dev),
                     "kv": torch.empty((M, c.num_hidden_layers * 2 * Hkv * hd), dtype=torch.bfloat16, device=dev),
                 }
             else:
@@ -214,6 +247,7 @@ class DraftModel:
                     "attn": torch.empty((M, Hq * hd), dtype=torch.bfloat16, device=dev),
                     "act": torch.empty((M, c.intermediate_size), dtype=torch.bfloat16, device=dev),
                     "argmax": torch.empty((M, ops.argmax_tiles(c.vocab_size), 2), dtype=torch.float32, device=dev),
+                    "ss": torch.zeros((M, H // 64), dtype=torch.float32, device=dev),
                 }
             self._bufs[key] = b
         return b
@@ -227,9 +261,10 @@ class DraftModel:
         M = taps.shape[0]
         b = self.buffers(M, "ctx")
         H, hd, Hkv = c.hidden_size, c.head_dim, c.num_key_value_heads
-        ops.gemm(taps, self.fc, out=b["fc"], ws=ws)
-        ops.rmsnorm(b["fc"], self.hidden_norm, c.rms_norm_eps, out=b["ctx"])
-        ops.gemm(b["ctx"], self.w_ctx_kv, out=b["kv"], ws=ws)
+        ops.gemm(taps, self.fc, out=b["fc"], ws=ws, sumsq_out=b["ss"])
+        # hidden_norm fused into the stacked k/v projection of every layer
+        ops.gemm(b["fc"], self.w_ctx_kv, out=b["kv"], ws=ws, norm_w=self.hidden_norm, sumsq_in=b["ss"],
+                 eps=c.rms_norm_eps)
         per = 2 * Hkv * hd
         for l, lw in enumerate(self.layers):
             kc, vc = cache.layer(l)
@@ -237,33 +272,33 @@ class DraftModel:
             ops.qkv_rope_append(view, pos, lw["q_norm"], lw["k_norm"], self.inv_freq, kc, vc, 0, Hkv, hd, hd,
                                 c.rms_norm_eps, row_seq=row_seq, do_q=False)
 
-    def forward_block(self, noise: torch.Tensor, pos: torch.Tensor, cache: KVCache, kv_len: torch.Tensor,
+    def forward_block(self, tokens: torch.Tensor, pos: torch.Tensor, cache: KVCache, kv_len: torch.Tensor,
                       max_kv: int, row_seq: torch.Tensor | None = None, head: str = "argmax",
                       ws: ops.Workspace | None = None):
-        """Block rows (the noise embedding of [last, mask, ...]) attend to the draft cache
-        (context rows already ingested) plus the block itself; returns the lm_head
-        argmax partials of the final-normed hidden states (or the hidden states)."""
+        """Block rows (the target embedding of [last, mask, ...] = the noise embedding,
+        runtime.py:408-410) attend to the draft cache (context rows already ingested)
+        plus the block itself; returns the lm_head argmax partials of the final-normed
+        hidden states (or the hidden states)."""
         c = self.cfg
-        M = noise.shape[0]
+        M = tokens.numel()
         b = self.buffers(M, "blk")
         H, hd = c.hidden_size, c.head_dim
         Hq, Hkv = c.num_attention_heads, c.num_key_value_heads
-        h = b["h"]
-        h.copy_(noise)
+        h, ss, eps = b["h"], b["ss"], c.rms_norm_eps
+        ops.embed(tokens, self.target.embed_w, out=h, sumsq_out=ss)
         causal = self.mask_mode == "causal"
         for l, lw in enumerate(self.layers):
             kc, vc = cache.layer(l)
-            ops.rmsnorm(h, lw["in_norm"], c.rms_norm_eps, out=b["xn"])
-            ops.gemm(b["xn"], lw["w_qkv"], out=b["qkv"], ws=ws)
+            ops.gemm(h, lw["w_qkv"], out=b["qkv"], ws=ws, norm_w=lw["in_norm"], sumsq_in=ss, eps=eps)
             ops.qkv_rope_append(b["qkv"], pos, lw["q_norm"], lw["k_norm"], self.inv_freq, kc, vc, Hq, Hkv, hd, hd,
-                                c.rms_norm_eps, q_out=b["q"], row_seq=row_seq)
+                                eps, q_out=b["q"], row_seq=row_seq)
             ops.attention(b["q"], kc, vc, pos, causal=causal, max_kv=max_kv, kv_len=kv_len, row_seq=row_seq,
                           out=b["attn"], ws=ws)
-            ops.gemm(b["attn"], lw["w_o"], ops.EPI_RESIDUAL, residual=h, out=h, ws=ws)
-            ops.rmsnorm(h, lw["post_norm"], c.rms_norm_eps, out=b["xn"])
-            ops.gemm(b["xn"], lw["w_gu"], ops.EPI_SILU_MUL, out=b["act"], ws=ws)
-            ops.gemm(b["act"], lw["w_down"], ops.EPI_RESIDUAL, residual=h, out=h, ws=ws)
-        ops.rmsnorm(h, self.norm_w, c.rms_norm_eps, out=b["xn"])
+            ops.gemm(b["attn"], lw["w_o"], ops.EPI_RESIDUAL, residual=h, out=h, ws=ws, sumsq_out=ss)
+            ops.gemm(h, lw["w_gu"], ops.EPI_SILU_MUL, out=b["act"], ws=ws, norm_w=lw["post_norm"], sumsq_in=ss,
+                     eps=eps)
+            ops.gemm(b["act"], lw["w_down"], ops.EPI_RESIDUAL, residual=h, out=h, ws=ws, sumsq_out=ss)
         if head == "hidden":
-            return b["xn"]
-        return ops.gemm(b["xn"], self.target.lm_head_w, ops.EPI_ARGMAX, argmax_partials=b["argmax"], ws=ws)
+            return ops.rmsnorm(h, self.norm_w, eps, out=b["xn"])
+        return ops.gemm(h, self.target.lm_head_w, ops.EPI_ARGMAX, argmax_partials=b["argmax"], ws=ws,
+                        norm_w=self.norm_w, sumsq_in=ss, eps=eps)

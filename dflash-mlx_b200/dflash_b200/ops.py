@@ -72,9 +72,12 @@ def workspace(device: torch.device | None = None) -> Workspace:
 
 def gemm(x: torch.Tensor, w: torch.Tensor, epilogue: int = EPI_STORE, residual: torch.Tensor | None = None,
          out: torch.Tensor | None = None, out2: torch.Tensor | None = None,
-         argmax_partials: torch.Tensor | None = None, ws: Workspace | None = None) -> torch.Tensor:
-    """y = x @ w.T (bf16 in, fp32 accumulate) with a fused epilogue."""
-    _need_cuda(x, w, residual, out, out2, argmax_partials)
+         argmax_partials: torch.Tensor | None = None, ws: Workspace | None = None,
+         norm_w: torch.Tensor | None = None, sumsq_in: torch.Tensor | None = None, eps: float = 1e-6,
+         sumsq_out: torch.Tensor | None = None) -> torch.Tensor:
+    """y = xn @ w.T (bf16 in, fp32 accumulate) with a fused epilogue; xn = RMSNorm(x) * norm_w
+    when norm_w is given (sumsq_in: [M, K/64] fp32 row sum-of-squares partials of x)."""
+    _need_cuda(x, w, residual, out, out2, argmax_partials, norm_w, sumsq_in, sumsq_out)
     if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
         raise ValueError("gemm takes bf16 x and w")
     M, K = x.shape
@@ -85,12 +88,22 @@ def gemm(x: torch.Tensor, w: torch.Tensor, epilogue: int = EPI_STORE, residual: 
     ws = ws or workspace(x.device)
     need = int(_lib.query("dfl_gemm_workspace_bytes", M, N, K, epilogue))
     ws.ensure_gemm(need)
+    n_parts = 0
+    if norm_w is not None:
+        if sumsq_in is None or sumsq_in.shape[0] < M or sumsq_in.dtype != torch.float32:
+            raise ValueError("the fused RMSNorm needs fp32 sumsq_in partials [M, K/64]")
+        n_parts = sumsq_in.shape[1]
+        if n_parts != K // 64 or not sumsq_in.is_contiguous():
+            raise ValueError("sumsq_in must be contiguous [M, K/64]")
+    if sumsq_out is not None and (sumsq_out.shape[1] != (N + 63) // 64 or not sumsq_out.is_contiguous()):
+        raise ValueError("sumsq_out must be contiguous [M, N/64]")
     if epilogue == EPI_ARGMAX:
         ntiles = int(_lib.query("dfl_gemm_argmax_tiles", N))
         if argmax_partials is None:
             argmax_partials = torch.empty((M, ntiles, 2), dtype=torch.float32, device=x.device)
         _lib.call("dfl_gemm_bf16", _ptr(x), ldx, _ptr(w), M, N, K, epilogue, None, 0, None, 0, None, 0,
-                  _ptr(argmax_partials), _ptr(ws.gemm), ws.gemm.numel(), _stream())
+                  _ptr(argmax_partials), _ptr(norm_w), _ptr(sumsq_in), n_parts, float(eps), None,
+                  _ptr(ws.gemm), ws.gemm.numel(), _stream())
         return argmax_partials
     n_out = N // 2 if epilogue == EPI_SILU_MUL else N
     if out is None:
@@ -100,8 +113,17 @@ def gemm(x: torch.Tensor, w: torch.Tensor, epilogue: int = EPI_STORE, residual: 
     ldr = _row_stride(residual) if residual is not None else 0
     ldy2 = _row_stride(out2) if out2 is not None else 0
     _lib.call("dfl_gemm_bf16", _ptr(x), ldx, _ptr(w), M, N, K, epilogue, _ptr(residual), ldr, _ptr(out),
-              _row_stride(out), _ptr(out2), ldy2, None, _ptr(ws.gemm), ws.gemm.numel(), _stream())
+              _row_stride(out), _ptr(out2), ldy2, None, _ptr(norm_w), _ptr(sumsq_in), n_parts, float(eps),
+              _ptr(sumsq_out), _ptr(ws.gemm), ws.gemm.numel(), _stream())
     return out
+
+
+def device_error(clear: bool = True) -> int:
+    """Non-zero when a kernel's bounded wait gave up (synchronises the current stream)."""
+    import ctypes
+    code = ctypes.c_int(0)
+    _lib.call("dfl_device_error", ctypes.byref(code), int(clear), _stream())
+    return code.value
 
 
 def argmax_tiles(N: int) -> int:
@@ -118,15 +140,17 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor | None, eps: float, out: torch.Tens
     return out
 
 
-def embed(tokens: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-    _need_cuda(tokens, table, out)
+def embed(tokens: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None = None,
+          sumsq_out: torch.Tensor | None = None) -> torch.Tensor:
+    _need_cuda(tokens, table, out, sumsq_out)
     if tokens.dtype != torch.int32 or not tokens.is_contiguous():
         raise ValueError("tokens must be contiguous int32")
     V, H = table.shape
     M = tokens.numel()
     if out is None:
         out = torch.empty((M, H), dtype=torch.bfloat16, device=table.device)
-    _lib.call("dfl_embed_bf16", _ptr(tokens), _ptr(table), _ptr(out), _row_stride(out), M, H, V, _stream())
+    _lib.call("dfl_embed_bf16", _ptr(tokens), _ptr(table), _ptr(out), _row_stride(out), M, H, V, _ptr(sumsq_out),
+              _stream())
     return out
 
 

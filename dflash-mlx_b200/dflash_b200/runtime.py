@@ -97,7 +97,6 @@ class SpecSession:
         self.taps = torch.zeros((B * bs, ntaps * tc.hidden_size), dtype=torch.bfloat16, device=dev)
         if draft is not None:
             self.dcache = draft.make_cache(B, self.cap)
-            self.noise = torch.empty((B * bs, tc.hidden_size), dtype=torch.bfloat16, device=dev)
         self.inject_tokens = self.inject_len = self.inject_noise = None
         self.graph: torch.cuda.CUDAGraph | None = None
         self.host_state = torch.zeros((B, STATE_INTS), dtype=torch.int32, pin_memory=True)
@@ -196,8 +195,7 @@ class SpecSession:
         if self.draft is not None:
             d = self.draft
             d.ingest_context(self.taps, self.dpos_ctx, self.dcache, row_seq=self.row_seq, ws=self.ws)
-            ops.embed(self.block, self.target.embed_w, out=self.noise)
-            part = d.forward_block(self.noise, self.dpos_blk, self.dcache, self.dkv_len, self.cap,
+            part = d.forward_block(self.block, self.dpos_blk, self.dcache, self.dkv_len, self.cap,
                                    row_seq=self.row_seq, ws=self.ws)
             ops.draft_commit(self.state, part, self.block, bs, B, self.inject_tokens, self.inject_len,
                              self.inject_noise)

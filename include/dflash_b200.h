@@ -58,21 +58,33 @@ int dfl_abi_version(void);
 const char* dfl_last_error(void);
 
 /* ---- dense projections ----------------------------------------------------
- * Y[M,N] = X[M,K] . W[N,K]^T with fp32 accumulation and a fused epilogue.
- * Replaces the nn.Linear calls of the verify / draft forward: mlx-lm qwen3
- * Attention and MLP (driven from adapters.py:611-631), DFlashAttention
- * q/k/v/o projections (draft.py:75-98, 118-159), the draft fc
- * (draft.py:196-201, 217) and lm_head_logits / lm_head_argmax
+ * Y[M,N] = Xn[M,K] . W[N,K]^T with fp32 accumulation and a fused epilogue, where
+ * Xn = X, or RMSNorm(X) * norm_w when norm_w != NULL (fused prologue: the row
+ * sum of squares of X is given as sumsq_in[M][n_parts] partials, summed in
+ * order; K / 64 partials as written by DFL_EPI_STORE / DFL_EPI_RESIDUAL's
+ * sumsq_out or by dfl_embed_bf16).
+ * Replaces the nn.Linear (and the RMSNorm feeding it) of the verify / draft
+ * forward: mlx-lm qwen3 Attention and MLP (driven from adapters.py:611-631),
+ * DFlashAttention q/k/v/o projections (draft.py:75-98, 118-159), the draft fc
+ * + hidden_norm (draft.py:196-201, 217) and lm_head_logits / lm_head_argmax
  * (adapters.py:264-271, 606-609; runtime.py:22-29 argmax).
- * K % 64 == 0, x and w 16-byte aligned. Split-K scratch: workspace of
+ * K % 64 == 0, N % 8 == 0, x / w / y 16-byte aligned. Scratch: workspace of
  * dfl_gemm_workspace_bytes() bytes, zero-filled once before first use (the
  * kernel leaves its counters at zero); one workspace per stream.
- * DFL_EPI_ARGMAX writes float2 partials [M][dfl_gemm_argmax_tiles(N)]. */
+ * DFL_EPI_ARGMAX writes float2 partials [M][dfl_gemm_argmax_tiles(N)].
+ * sumsq_out (nullable, STORE / RESIDUAL): per-row sum of squares of the bf16
+ * output per 64-column tile, [M][N/64]. */
 size_t dfl_gemm_workspace_bytes(int M, int N, int K, int epilogue);
 int dfl_gemm_argmax_tiles(int N);
 int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w, int M, int N, int K, int epilogue,
                   const void* residual, int64_t ldr, void* y, int64_t ldy, void* y2, int64_t ldy2,
-                  void* argmax_partials, void* workspace, size_t workspace_bytes, void* stream);
+                  void* argmax_partials, const void* norm_w, const float* sumsq_in, int n_parts, float eps,
+                  float* sumsq_out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Reads (and optionally clears) the device error record: non-zero when a kernel's
+ * bounded wait gave up (the kernel returned instead of hanging). Synchronises
+ * the given stream. */
+int dfl_device_error(int* code, int clear, void* stream);
 
 /* ---- row kernels ----------------------------------------------------------
  * RMSNorm y = w * x * rsqrt(mean(x^2) + eps) (fp32 math, bf16 out); w may be
@@ -81,9 +93,11 @@ int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w, int M, int N, int K
 int dfl_rmsnorm_bf16(const void* x, int64_t ldx, const void* w, void* y, int64_t ldy, int M, int H, float eps,
                      void* stream);
 
-/* Token embedding gather (adapters.py:603-604 embed_tokens; runtime.py:410). */
+/* Token embedding gather (adapters.py:603-604 embed_tokens; runtime.py:410).
+ * sumsq_out (nullable): per-row sum of squares per 64 columns, [M][H/64]
+ * (feeds the fused RMSNorm prologue of dfl_gemm_bf16). */
 int dfl_embed_bf16(const int32_t* tokens, const void* table, void* y, int64_t ldy, int M, int H, int V,
-                   void* stream);
+                   float* sumsq_out, void* stream);
 
 /* q_norm / k_norm (per-head RMSNorm), non-interleaved RoPE over the first
  * rot_dim dims with inverse frequencies inv_freq[rot_dim/2], and the KV-cache

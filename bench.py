@@ -174,13 +174,21 @@ def gemm_roofline(sess, reps: int = 3) -> dict:
         for fn, _ in launches:
             fn()
 
-    run_all()
+    run_all()  # eager once (tensor maps, function attributes), then replay as a CUDA graph
     torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st):
+        with torch.cuda.graph(g, stream=st):
+            run_all()
+    torch.cuda.current_stream().wait_stream(st)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     times = []
     for _ in range(reps):
+        torch.cuda.synchronize()
         e0.record()
-        run_all()
+        g.replay()
         e1.record()
         torch.cuda.synchronize()
         times.append(e0.elapsed_time(e1) * 1e-3)

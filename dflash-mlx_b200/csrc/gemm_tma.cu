@@ -50,19 +50,23 @@ int* device_error_word() {
 }
 
 constexpr int TG_NT = 64;
-constexpr int TG_BK = 64;
+constexpr int TG_BK = 128;  // k per stage: two 64-column TMA boxes (128-byte swizzle rows)
 constexpr int TG_BM = 16;
-constexpr int TG_STAGES = 8;
+constexpr int TG_STAGES = 4;
+constexpr int TG_NORM_MAX_K = 8192;  // fused-RMSNorm weights staged in shared memory
 constexpr int TG_GRID = 148;  // work split over the B200's SM count (fixed: part of the reduction order)
 constexpr int TG_CONSUMERS = 4;
 constexpr int TG_THREADS = 32 * (TG_CONSUMERS + 1);
-constexpr int TG_W_BYTES = TG_NT * TG_BK * 2;
-constexpr int TG_X_BYTES = TG_BM * TG_BK * 2;
+constexpr int TG_W_HALF = TG_NT * 64 * 2;  // one 64-row x 64-k box: 8 KB
+constexpr int TG_X_HALF = TG_BM * 64 * 2;  // one 16-row x 64-k box: 2 KB
+constexpr int TG_W_BYTES = 2 * TG_W_HALF;
+constexpr int TG_X_BYTES = 2 * TG_X_HALF;
 constexpr int TG_OFF_X = TG_STAGES * TG_W_BYTES;
 constexpr int TG_OFF_WPART = TG_OFF_X + TG_STAGES * TG_X_BYTES;
 constexpr int TG_OFF_RED = TG_OFF_WPART + TG_CONSUMERS * TG_BM * TG_NT * 4;
 constexpr int TG_OFF_BAR = TG_OFF_RED + TG_BM * TG_NT * 4;
-constexpr int TG_SMEM = TG_OFF_BAR + 2 * TG_STAGES * 8 + 1024;  // + alignment slack
+constexpr int TG_OFF_NORM = TG_OFF_BAR + 2 * TG_STAGES * 8;  // K bf16 norm weights follow when fused
+constexpr int TG_SMEM_BASE = TG_OFF_NORM + 1024;                // + alignment slack
 constexpr int TG_MAX_COUNTERS = 1 << 17;
 constexpr size_t TG_COUNTER_BYTES = (size_t)TG_MAX_COUNTERS * sizeof(int);
 
@@ -207,25 +211,30 @@ __global__ void __launch_bounds__(TG_THREADS, 1)
       const uint64_t pol_w = l2_policy_evict_first();
       const uint64_t pol_x = l2_policy_evict_last();
       const int pre = n_units < TG_STAGES ? n_units : TG_STAGES;
+      auto load_w = [&](int s, int nt, int j) {
+        unsigned char* d = smem + s * TG_W_BYTES;
+        tma_load_2d(&wmap, &full[s], d, j * TG_BK, nt * TG_NT, pol_w);
+        tma_load_2d(&wmap, &full[s], d + TG_W_HALF, j * TG_BK + 64, nt * TG_NT, pol_w);
+      };
+      auto load_x = [&](int s, int j) {
+        unsigned char* d = smem + TG_OFF_X + s * TG_X_BYTES;
+        tma_load_2d(&xmap, &full[s], d, j * TG_BK, mt * TG_BM, pol_x);
+        tma_load_2d(&xmap, &full[s], d + TG_X_HALF, j * TG_BK + 64, mt * TG_BM, pol_x);
+      };
       for (int i = 0; i < pre; ++i) {
         const long long u = u0 + i;
-        const int nt = (int)(u / a.kb), j = (int)(u % a.kb);
         mbar_expect_tx(&full[i], TG_W_BYTES + TG_X_BYTES);
-        tma_load_2d(&wmap, &full[i], sW + i * (TG_W_BYTES / 2), j * TG_BK, nt * TG_NT, pol_w);
+        load_w(i, (int)(u / a.kb), (int)(u % a.kb));
       }
       grid_dependency_wait();  // X is produced by the previous kernel
-      for (int i = 0; i < pre; ++i) {
-        const int j = (int)((u0 + i) % a.kb);
-        tma_load_2d(&xmap, &full[i], sX + i * (TG_X_BYTES / 2), j * TG_BK, mt * TG_BM, pol_x);
-      }
+      for (int i = 0; i < pre; ++i) load_x(i, (int)((u0 + i) % a.kb));
       for (int i = pre; i < n_units; ++i) {
         const int s = i % TG_STAGES;
         if (!mbar_wait(&empty[s], ((i / TG_STAGES) & 1) ^ 1, 101, a.err)) break;
         const long long u = u0 + i;
-        const int nt = (int)(u / a.kb), j = (int)(u % a.kb);
         mbar_expect_tx(&full[s], TG_W_BYTES + TG_X_BYTES);
-        tma_load_2d(&wmap, &full[s], sW + s * (TG_W_BYTES / 2), j * TG_BK, nt * TG_NT, pol_w);
-        tma_load_2d(&xmap, &full[s], sX + s * (TG_X_BYTES / 2), j * TG_BK, mt * TG_BM, pol_x);
+        load_w(s, (int)(u / a.kb), (int)(u % a.kb));
+        load_x(s, (int)(u % a.kb));
       }
     }
     return;
@@ -233,8 +242,12 @@ __global__ void __launch_bounds__(TG_THREADS, 1)
 
   // ---------------- consumers ----------------
   const int ct = threadIdx.x;  // 0..127
-  grid_dependency_wait();
   const bool norm = a.norm_w != nullptr;
+  __nv_bfloat16* s_nw = reinterpret_cast<__nv_bfloat16*>(smem + TG_OFF_NORM);
+  if (norm)  // norm weights are parameters (not produced upstream): stage them before the wait
+    for (int k = ct * 8; k < a.K; k += 128 * 8)
+      *reinterpret_cast<uint4*>(s_nw + k) = *reinterpret_cast<const uint4*>(a.norm_w + k);
+  grid_dependency_wait();
   if (norm && ct < TG_BM) {
     const int m = mt * TG_BM + ct;
     float ss = 0.f;
@@ -263,33 +276,42 @@ __global__ void __launch_bounds__(TG_THREADS, 1)
     __nv_bfloat16* tX = sX + s * (TG_X_BYTES / 2);
     const __nv_bfloat16* tW = sW + s * (TG_W_BYTES / 2);
     if (norm) {
-      // rescale this thread's 16-byte chunk of the X stage: xn = bf16(w * x * inv_rms)
+      // rescale this thread's two 16-byte chunks of the X stage: xn = bf16(w * x * inv_rms)
       const int row = ct >> 3, cc = ct & 7;
-      __nv_bfloat16* p = tX + tg_swz(row, cc);
-      uint4 xv = *reinterpret_cast<uint4*>(p);
-      const uint4 wv = *reinterpret_cast<const uint4*>(a.norm_w + j * TG_BK + cc * 8);
-      __nv_bfloat16* xe = reinterpret_cast<__nv_bfloat16*>(&xv);
-      const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv);
       const float inv = s_inv[row];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) xe[e] = f2bf(bf2f(we[e]) * (bf2f(xe[e]) * inv));
-      *reinterpret_cast<uint4*>(p) = xv;
+      for (int hf = 0; hf < 2; ++hf) {
+        __nv_bfloat16* p = tX + hf * (TG_X_HALF / 2) + tg_swz(row, cc);
+        uint4 xv = *reinterpret_cast<uint4*>(p);
+        const uint4 wv = *reinterpret_cast<const uint4*>(s_nw + j * TG_BK + hf * 64 + cc * 8);
+        __nv_bfloat16* xe = reinterpret_cast<__nv_bfloat16*>(&xv);
+        const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) xe[e] = f2bf(bf2f(we[e]) * (bf2f(xe[e]) * inv));
+        *reinterpret_cast<uint4*>(p) = xv;
+      }
       consumer_sync();
     }
-    uint32_t af[4];
-    {
-      const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
-      const int cc = 2 * warp + (lane >> 4);
-      ldmatrix_x4(smem_u32(tX + tg_swz(row, cc)), af[0], af[1], af[2], af[3]);
-    }
+    // this warp's k16 slices: warp and warp + 4 (one per 64-column half)
 #pragma unroll
-    for (int nb = 0; nb < 4; ++nb) {
-      const int row = nb * 16 + (lane & 7) + (lane >> 4) * 8;
-      const int cc = 2 * warp + ((lane >> 3) & 1);
-      uint32_t b0, b1, b2, b3;
-      ldmatrix_x4(smem_u32(tW + tg_swz(row, cc)), b0, b1, b2, b3);
-      mma_bf16_16816(acc[2 * nb], af, b0, b1);
-      mma_bf16_16816(acc[2 * nb + 1], af, b2, b3);
+    for (int hf = 0; hf < 2; ++hf) {
+      const __nv_bfloat16* hX = tX + hf * (TG_X_HALF / 2);
+      const __nv_bfloat16* hW = tW + hf * (TG_W_HALF / 2);
+      uint32_t af[4];
+      {
+        const int row = (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int cc = 2 * warp + (lane >> 4);
+        ldmatrix_x4(smem_u32(hX + tg_swz(row, cc)), af[0], af[1], af[2], af[3]);
+      }
+#pragma unroll
+      for (int nb = 0; nb < 4; ++nb) {
+        const int row = nb * 16 + (lane & 7) + (lane >> 4) * 8;
+        const int cc = 2 * warp + ((lane >> 3) & 1);
+        uint32_t b0, b1, b2, b3;
+        ldmatrix_x4(smem_u32(hW + tg_swz(row, cc)), b0, b1, b2, b3);
+        mma_bf16_16816(acc[2 * nb], af, b0, b1);
+        mma_bf16_16816(acc[2 * nb + 1], af, b2, b3);
+      }
     }
     // release the stage (generic-proxy writes of the norm prologue must be ordered
     // before the next TMA write into it)
@@ -458,7 +480,7 @@ extern "C" int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w, int M, i
   }
   if (K % TG_BK || N % 8 || ldx % 8 || (reinterpret_cast<uintptr_t>(x) & 15) ||
       (reinterpret_cast<uintptr_t>(w) & 15)) {
-    set_error("dfl_gemm_bf16: needs K %% 64 == 0, N %% 8 == 0, 16-byte aligned x/w, ldx %% 8 == 0 (K=%d N=%d ldx=%lld)",
+    set_error("dfl_gemm_bf16: needs K %% 128 == 0, N %% 8 == 0, 16-byte aligned x/w, ldx %% 8 == 0 (K=%d N=%d ldx=%lld)",
               K, N, (long long)ldx);
     return DFL_ERR_UNSUPPORTED;
   }
@@ -476,8 +498,8 @@ extern "C" int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w, int M, i
     set_error("dfl_gemm_bf16: silu-mul epilogue needs N %% 64 == 0 (packed gate/up), N=%d", N);
     return DFL_ERR_UNSUPPORTED;
   }
-  if (norm_w && (!sumsq_in || n_parts <= 0)) {
-    set_error("dfl_gemm_bf16: the fused RMSNorm prologue needs sumsq_in partials");
+  if (norm_w && (!sumsq_in || n_parts <= 0 || K > TG_NORM_MAX_K)) {
+    set_error("dfl_gemm_bf16: the fused RMSNorm prologue needs sumsq_in partials and K <= %d", TG_NORM_MAX_K);
     return DFL_ERR_INVALID;
   }
   TgPlan p = tg_plan(M, N, K);
@@ -490,9 +512,9 @@ extern "C" int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w, int M, i
     set_error("dfl_gemm_bf16: workspace too small (%zu < %zu bytes)", workspace_bytes, need);
     return DFL_ERR_WORKSPACE;
   }
-  const CUtensorMap* wm = tensor_map_2d_bf16(w, N, K, K, TG_NT, TG_BK);
+  const CUtensorMap* wm = tensor_map_2d_bf16(w, N, K, K, TG_NT, 64);
   if (!wm) return DFL_ERR_CUDA;
-  const CUtensorMap* xm = tensor_map_2d_bf16(x, M, K, ldx, TG_BM, TG_BK);
+  const CUtensorMap* xm = tensor_map_2d_bf16(x, M, K, ldx, TG_BM, 64);
   if (!xm) return DFL_ERR_CUDA;
 
   TgArgs a;
@@ -522,7 +544,7 @@ extern "C" int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w, int M, i
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.grid1 * p.m_tiles);
   cfg.blockDim = dim3(TG_THREADS);
-  cfg.dynamicSmemBytes = TG_SMEM;
+  cfg.dynamicSmemBytes = TG_SMEM_BASE + (norm_w ? (size_t)K * 2 : 0);
   cfg.stream = as_stream(stream);
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -535,7 +557,8 @@ extern "C" int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w, int M, i
   case E: {                                                                                                \
     static bool init = false;                                                                              \
     if (!init) {                                                                                           \
-      cudaFuncSetAttribute(gemm_tma_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize, TG_SMEM);      \
+      cudaFuncSetAttribute(gemm_tma_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize,                \
+                           TG_SMEM_BASE + TG_NORM_MAX_K * 2);                                              \
       init = true;                                                                                         \
     }                                                                                                      \
     err = cudaLaunchKernelEx(&cfg, gemm_tma_kernel<E>, *wm, *xm, a);                                       \

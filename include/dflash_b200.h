@@ -68,7 +68,7 @@ const char* dfl_last_error(void);
  * DFlashAttention q/k/v/o projections (draft.py:75-98, 118-159), the draft fc
  * + hidden_norm (draft.py:196-201, 217) and lm_head_logits / lm_head_argmax
  * (adapters.py:264-271, 606-609; runtime.py:22-29 argmax).
- * K % 64 == 0, N % 8 == 0, x / w / y 16-byte aligned. Scratch: workspace of
+ * K % 128 == 0, N % 8 == 0, x / w / y 16-byte aligned; the fused norm needs K <= 8192. Scratch: workspace of
  * dfl_gemm_workspace_bytes() bytes, zero-filled once before first use (the
  * kernel leaves its counters at zero); one workspace per stream.
  * DFL_EPI_ARGMAX writes float2 partials [M][dfl_gemm_argmax_tiles(N)].

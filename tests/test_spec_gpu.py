@@ -127,4 +127,4 @@ def test_qwen3_4b_layer_logits_parity():
     agree = (got.argmax(-1) == ref_logits.argmax(-1)).float().mean().item()
     print(f"greedy-token agreement {agree:.3f}")
     assert agree >= 0.95
-    assert (taps.float().cpu() - ref_taps).abs().max().item() < 5e-2
+    assert (taps.float().cpu() - ref_taps).abs().max().item() <= 2e-2 * ref_taps.abs().max().item()

@@ -1,0 +1,630 @@
+// Persistent weight-streaming GEMM on the 5th-generation tensor cores (tcgen05 + TMEM).
+//
+//   Y[M, N] = Xn[M, K] . W[N, K]^T   (fp32 accumulate in TMEM) + fused epilogue
+//   Xn      = X, or RMSNorm(X) with weight norm_w when the prologue is enabled
+//
+// Replaces the nn.Linear (and the RMSNorm feeding it) of the verify / draft
+// forward: mlx-lm qwen3 Attention / MLP projections driven from
+// adapters.py:611-631, DFlashAttention q/k/v/o (draft.py:75-98, 118-159), the
+// draft fc + hidden_norm (draft.py:196-201, 217) and lm_head_logits /
+// lm_head_argmax (adapters.py:264-271, 606-609; the argmax of runtime.py:22-29).
+//
+// B200 design
+//  * Swap-AB: a 128-row tile of W is the MMA's M side (A operand, K-major,
+//    128-byte swizzle) and the 16 tokens of X are its N side, so one
+//    tcgen05.mma.cta_group::1.kind::f16 M=128 N=16 K=16 covers 128 outputs of all
+//    16 rows; the accumulator lives in TMEM (2 buffers x 16 columns).
+//  * Warp roles: warp 0 = TMA producer (2-D tiled loads, evict-first for W,
+//    evict-last for X), warp 1 = TMEM allocator + single-thread MMA issuer
+//    (tcgen05.commit releases each shared-memory stage back to the producer),
+//    warps 2-5 = epilogue (tcgen05.ld 32x32b: each thread owns one output column
+//    for the 16 rows) and, when the RMSNorm is fused, the per-stage rescale of X.
+//  * Persistent: one CTA per SM per 16-row tile of X (grid 148); every CTA gets
+//    an equal contiguous range of (128-row, 64-k) work units, so the SMs stream
+//    equal shares of W and there is no tail wave. ~100 KB of shared memory lets
+//    the next GEMM's CTA co-reside and stream its first weight stages before
+//    griddepcontrol.wait (programmatic dependent launch).
+//  * A tile cut by range boundaries is reduced by the last-arriving CTA in fixed
+//    segment order; split points depend on N and K only, so every row is computed
+//    with the same reduction order whatever M is (spec rows == plain-decode rows).
+//  * Every mbarrier wait is bounded: on expiry the kernel records an error code in
+//    the library's device error word and falls through to its teardown.
+#include "tma_util.cuh"
+
+#include <mutex>
+#include <unordered_map>
+
+namespace dfl {
+
+static __device__ int g_device_error = 0;
+
+int* device_error_word() {
+  static int* ptrs[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
+    ptrs[dev] = static_cast<int*>(p);
+  }
+  return ptrs[dev];
+}
+
+constexpr int TC_NT = 128;  // W rows per tile (MMA M)
+constexpr int TC_BK = 64;   // k per stage (one 128-byte swizzle row)
+constexpr int TC_BM = 16;   // tokens per tile (MMA N)
+constexpr int TC_STAGES = 5;
+constexpr int TC_GRID = 148;  // work split over the B200's SM count (fixed: part of the reduction order)
+constexpr int TC_THREADS = 192;
+constexpr int TC_EPI_WARP0 = 2;
+constexpr int TC_W_BYTES = TC_NT * TC_BK * 2;  // 16 KB
+constexpr int TC_X_BYTES = TC_BM * TC_BK * 2;  // 2 KB
+constexpr int TC_OFF_X = TC_STAGES * TC_W_BYTES;
+constexpr int TC_OFF_XCHG = TC_OFF_X + TC_STAGES * TC_X_BYTES;
+constexpr int TC_OFF_BAR = TC_OFF_XCHG + 2 * TC_BM * 32 * 4;
+constexpr int TC_NBAR = 3 * TC_STAGES + 4;
+constexpr int TC_OFF_TMEM = TC_OFF_BAR + TC_NBAR * 8;
+constexpr int TC_OFF_NORM = (TC_OFF_TMEM + 16 + 127) & ~127;
+constexpr int TC_SMEM_BASE = TC_OFF_NORM + 1024;  // + 1024-byte alignment slack
+constexpr int TC_NORM_MAX_K = 8192;
+constexpr int TC_TMEM_COLS = 32;
+constexpr int TC_MAX_COUNTERS = 1 << 17;
+constexpr size_t TC_COUNTER_BYTES = (size_t)TC_MAX_COUNTERS * sizeof(int);
+constexpr int TC_PART_FLOATS = TC_BM * TC_NT;  // one partial tile
+
+// tcgen05 instruction descriptor: kind::f16, A = B = bf16, D = f32, both K-major,
+// N = 16 (bits 17-22: N >> 3), M = 128 (bits 24-28: M >> 4).
+constexpr uint32_t TC_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TC_BM >> 3) << 17) |
+                              ((uint32_t)(TC_NT >> 4) << 24);
+
+struct TcArgs {
+  const __nv_bfloat16* res;
+  long long ldr;
+  __nv_bfloat16* y;
+  long long ldy;
+  __nv_bfloat16* y2;
+  long long ldy2;
+  float2* argmax;  // [M][N/32]
+  float* partial;  // [m_tiles][grid1][2][16*128]
+  int* counters;   // [m_tiles * n_tiles]
+  const __nv_bfloat16* norm_w;
+  const float* sumsq_in;  // [M][n_parts] (n_parts = K/32)
+  int n_parts;
+  float eps;
+  float* sumsq_out;  // [M][N/32]
+  int* err;
+  int n_groups;  // N / 32: row stride of sumsq_out and argmax
+  int M, N, K, n_tiles, kb;
+  long long U1;
+  int grid1;
+};
+
+// ---- tcgen05 helpers ----------------------------------------------------------
+// K-major, 128-byte-swizzle shared-memory matrix descriptor: start address >> 4,
+// leading byte offset 16 B (unused for swizzled K-major), stride byte offset
+// 1024 B between 8-row groups, descriptor version 1, layout type 2 (SWIZZLE_128B).
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  const uint32_t lo = ((saddr >> 4) & 0x3FFFu) | (1u << 16);
+  const uint32_t hi = (1024u >> 4) | (1u << 14) | (2u << 29);
+  return ((uint64_t)hi << 32) | lo;
+}
+__device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void tc_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;\n" ::: "memory"); }
+
+__device__ __forceinline__ int tc_unit_owner(long long u, long long U, int G) {
+  return (int)(((u + 1) * G + U - 1) / U) - 1;
+}
+
+// Epilogue from registers: this thread owns column n (tile column c = q*32 + lane)
+// for the 16 rows of the tile; q is the thread's TMEM lane quadrant.
+template <int EPI>
+__device__ __forceinline__ void tc_epilogue(const TcArgs& a, float* v, int mt, int nt, int q, int lane,
+                                            float* xchg) {
+  const int c = q * 32 + lane;
+  const int n = nt * TC_NT + c;
+  const int m0 = mt * TC_BM;
+  if constexpr (EPI == DFL_EPI_STORE || EPI == DFL_EPI_RESIDUAL) {
+    const bool col_ok = n < a.N;
+#pragma unroll
+    for (int t = 0; t < TC_BM; ++t) {
+      const int m = m0 + t;
+      float ss = 0.f;
+      if (col_ok && m < a.M) {
+        float val = v[t];
+        if constexpr (EPI == DFL_EPI_RESIDUAL) val = bf2f(a.res[(long long)m * a.ldr + n]) + round_bf16(val);
+        const __nv_bfloat16 o = f2bf(val);
+        a.y[(long long)m * a.ldy + n] = o;
+        if (a.y2) a.y2[(long long)m * a.ldy2 + n] = o;
+        const float qv = bf2f(o);
+        ss = qv * qv;
+      }
+      if (a.sumsq_out) {
+        ss = warp_sum(ss);
+        if (lane == 0 && m < a.M && nt * 4 + q < a.n_groups) a.sumsq_out[(long long)m * a.n_groups + nt * 4 + q] = ss;
+      }
+    }
+  } else if constexpr (EPI == DFL_EPI_ARGMAX) {
+#pragma unroll
+    for (int t = 0; t < TC_BM; ++t) {
+      float best = n < a.N ? round_bf16(v[t]) : -INFINITY;
+      int bidx = n < a.N ? n : 0x7fffffff;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bidx, o);
+        if (ob > best || (ob == best && oi < bidx)) { best = ob; bidx = oi; }
+      }
+      const int m = m0 + t;
+      if (lane == 0 && m < a.M && nt * 4 + q < a.n_groups)
+        a.argmax[(long long)m * a.n_groups + nt * 4 + q] = make_float2(best, __int_as_float(bidx));
+    }
+  } else if constexpr (EPI == DFL_EPI_SILU_MUL) {
+    // packed per 64 W rows as [32 gate | 32 up]: quadrants 0/2 hold gate rows, 1/3 the matching up rows
+    const int g = q >> 1;
+    if (q & 1) {
+#pragma unroll
+      for (int t = 0; t < TC_BM; ++t) xchg[(g * TC_BM + t) * 32 + lane] = v[t];
+    }
+    epi_sync();
+    if (!(q & 1)) {
+      const int on = nt * 64 + g * 32 + lane;
+      if (nt * TC_NT + c < a.N) {
+#pragma unroll
+        for (int t = 0; t < TC_BM; ++t) {
+          const int m = m0 + t;
+          if (m < a.M) {
+            const float gt = round_bf16(v[t]);
+            const float up = round_bf16(xchg[(g * TC_BM + t) * 32 + lane]);
+            const float act = round_bf16(gt / (1.f + __expf(-gt)));
+            a.y[(long long)m * a.ldy + on] = f2bf(act * up);
+          }
+        }
+      }
+    }
+    epi_sync();
+  }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap, TcArgs a) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + TC_OFF_BAR);
+  uint64_t* empty = full + TC_STAGES;
+  uint64_t* xready = empty + TC_STAGES;
+  uint64_t* accf = xready + TC_STAGES;  // [2]
+  uint64_t* acce = accf + 2;            // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + TC_OFF_TMEM);
+  float* xchg = reinterpret_cast<float*>(smem + TC_OFF_XCHG);
+  __nv_bfloat16* s_nw = reinterpret_cast<__nv_bfloat16*>(smem + TC_OFF_NORM);
+  __shared__ float s_inv[TC_BM];
+  __shared__ int s_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mt = blockIdx.x / a.grid1;
+  const int c = blockIdx.x % a.grid1;
+  const long long u0 = (long long)c * a.U1 / a.grid1;
+  const long long u1 = (long long)(c + 1) * a.U1 / a.grid1;
+  const int n_units = (int)(u1 - u0);
+  const bool norm = a.norm_w != nullptr;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < TC_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      mbar_init(&xready[s], 128);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf[b], 1);
+      mbar_init(&acce[b], 4);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
+                 "n"(TC_TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  grid_dependency_launch_dependents();
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0 && n_units > 0) {
+      const uint64_t pol_w = l2_policy_evict_first();
+      const uint64_t pol_x = l2_policy_evict_last();
+      const int pre = n_units < TC_STAGES ? n_units : TC_STAGES;
+      for (int i = 0; i < pre; ++i) {
+        const long long u = u0 + i;
+        mbar_expect_tx(&full[i], TC_W_BYTES + TC_X_BYTES);
+        tma_load_2d(&wmap, &full[i], smem + i * TC_W_BYTES, (int)(u % a.kb) * TC_BK, (int)(u / a.kb) * TC_NT, pol_w);
+      }
+      grid_dependency_wait();  // X is produced by the previous kernel
+      for (int i = 0; i < pre; ++i)
+        tma_load_2d(&xmap, &full[i], smem + TC_OFF_X + i * TC_X_BYTES, (int)((u0 + i) % a.kb) * TC_BK, mt * TC_BM,
+                    pol_x);
+      int issued = pre;
+      for (int i = pre; i < n_units; ++i) {
+        const int s = i % TC_STAGES;
+        if (!mbar_wait(&empty[s], ((i / TC_STAGES) & 1) ^ 1, 201, a.err)) break;
+        const long long u = u0 + i;
+        mbar_expect_tx(&full[s], TC_W_BYTES + TC_X_BYTES);
+        tma_load_2d(&wmap, &full[s], smem + s * TC_W_BYTES, (int)(u % a.kb) * TC_BK, (int)(u / a.kb) * TC_NT, pol_w);
+        tma_load_2d(&xmap, &full[s], smem + TC_OFF_X + s * TC_X_BYTES, (int)(u % a.kb) * TC_BK, mt * TC_BM, pol_x);
+        issued = i + 1;
+      }
+      if (issued < n_units) {
+        // gave up: let the copies already in flight land before the CTA exits
+        for (int i = issued > TC_STAGES ? issued - TC_STAGES : 0; i < issued; ++i)
+          mbar_wait(&full[i % TC_STAGES], (i / TC_STAGES) & 1, 209, a.err);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0 && n_units > 0) {
+      const uint32_t w0 = smem_u32(smem), x0 = smem_u32(smem + TC_OFF_X);
+      int seg = -1;
+      for (int i = 0; i < n_units; ++i) {
+        const long long u = u0 + i;
+        const int j = (int)(u % a.kb);
+        const int s = i % TC_STAGES;
+        const bool first = (i == 0) || (j == 0);
+        if (first) {
+          ++seg;
+          if (!mbar_wait(&acce[seg & 1], ((seg >> 1) & 1) ^ 1, 202, a.err)) break;
+          tc_fence_after();
+        }
+        if (!mbar_wait(norm ? &xready[s] : &full[s], (i / TC_STAGES) & 1, 203, a.err)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)((seg & 1) * TC_BM);
+        const uint64_t ad = sw128_desc(w0 + s * TC_W_BYTES);
+        const uint64_t bd = sw128_desc(x0 + s * TC_X_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < TC_BK / 16; ++kk)  // +32 bytes along K per MMA: +2 in the start-address field
+          tc_mma(d, ad + 2 * kk, bd + 2 * kk, TC_IDESC, (first && kk == 0) ? 0u : 1u);
+        tc_commit(&empty[s]);
+        if (j == a.kb - 1 || i == n_units - 1) tc_commit(&accf[seg & 1]);
+      }
+    }
+  } else {
+    // ---------------- epilogue warps (and the fused RMSNorm rescale) ----------------
+    const int ew = warp - TC_EPI_WARP0;  // 0..3
+    const int et = threadIdx.x - 32 * TC_EPI_WARP0;  // 0..127
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    if (norm)
+      for (int k = et * 8; k < a.K; k += 128 * 8)
+        *reinterpret_cast<uint4*>(s_nw + k) = *reinterpret_cast<const uint4*>(a.norm_w + k);
+    grid_dependency_wait();
+    if (norm) {
+      if (et < TC_BM) {
+        const int m = mt * TC_BM + et;
+        float ss = 0.f;
+        if (m < a.M)
+          for (int p = 0; p < a.n_parts; ++p) ss += a.sumsq_in[(long long)m * a.n_parts + p];
+        s_inv[et] = rsqrtf(ss / (float)a.K + a.eps);
+      }
+      epi_sync();
+    }
+    int seg = -1;
+    for (int i = 0; i < n_units; ++i) {
+      const long long u = u0 + i;
+      const int nt = (int)(u / a.kb), j = (int)(u % a.kb);
+      const int s = i % TC_STAGES;
+      if (i == 0 || j == 0) ++seg;
+      if (norm) {
+        if (!mbar_wait(&full[s], (i / TC_STAGES) & 1, 204, a.err)) break;
+        // rescale this thread's 16-byte chunk of the X stage: xn = bf16(w * x * inv_rms)
+        const int row = et >> 3, cc = et & 7;
+        __nv_bfloat16* p =
+            reinterpret_cast<__nv_bfloat16*>(smem + TC_OFF_X + s * TC_X_BYTES) + row * 64 + ((cc ^ (row & 7)) << 3);
+        uint4 xv = *reinterpret_cast<uint4*>(p);
+        const uint4 wv = *reinterpret_cast<const uint4*>(s_nw + j * TC_BK + cc * 8);
+        __nv_bfloat16* xe = reinterpret_cast<__nv_bfloat16*>(&xv);
+        const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv);
+        const float inv = s_inv[row];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) xe[e] = f2bf(bf2f(we[e]) * (bf2f(xe[e]) * inv));
+        *reinterpret_cast<uint4*>(p) = xv;
+        fence_proxy_async_smem();  // generic writes -> visible to the tensor core's async-proxy reads
+        mbar_arrive(&xready[s]);
+      }
+      const bool seg_end = (j == a.kb - 1) || (i == n_units - 1);
+      if (!seg_end) continue;
+      if (!mbar_wait(&accf[seg & 1], (seg >> 1) & 1, 205, a.err)) break;
+      tc_fence_after();
+      float v[TC_BM];
+      tc_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((seg & 1) * TC_BM), v);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acce[seg & 1]);
+
+      const long long tu0 = (long long)nt * a.kb, tu1 = tu0 + a.kb - 1;
+      const int c_first = tc_unit_owner(tu0, a.U1, a.grid1), c_last = tc_unit_owner(tu1, a.U1, a.grid1);
+      bool do_epi = true;
+      const int col = q * 32 + lane;
+      if (c_first != c_last) {
+        const int tile_id = mt * a.n_tiles + nt;
+        const int slot = (nt == (int)(u0 / a.kb)) ? 0 : 1;
+        float* mine = a.partial + (((long long)mt * a.grid1 + c) * 2 + slot) * TC_PART_FLOATS;
+#pragma unroll
+        for (int t = 0; t < TC_BM; ++t) mine[t * TC_NT + col] = v[t];
+        __threadfence();
+        epi_sync();
+        if (et == 0) s_flag = (atomicAdd(a.counters + tile_id, 1) == c_last - c_first);
+        epi_sync();
+        do_epi = s_flag != 0;
+        if (do_epi) {
+          __threadfence();
+#pragma unroll
+          for (int t = 0; t < TC_BM; ++t) v[t] = 0.f;
+          for (int cs = c_first; cs <= c_last; ++cs) {
+            const long long cs_u0 = (long long)cs * a.U1 / a.grid1;
+            const int sl = (nt == (int)(cs_u0 / a.kb)) ? 0 : 1;
+            const float* src = a.partial + (((long long)mt * a.grid1 + cs) * 2 + sl) * TC_PART_FLOATS;
+#pragma unroll
+            for (int t = 0; t < TC_BM; ++t) v[t] += __ldcg(src + t * TC_NT + col);
+          }
+          if (et == 0) a.counters[tile_id] = 0;  // ready for the next launch / graph replay
+        }
+        epi_sync();  // s_flag is rewritten by the next segment
+      }
+      if (do_epi) tc_epilogue<EPI>(a, v, mt, nt, q, lane, xchg);
+      (void)ew;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "n"(TC_TMEM_COLS));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side: tensor-map cache and launch
+// ---------------------------------------------------------------------------
+struct MapKey {
+  const void* base;
+  uint64_t rows, cols, ld;
+  uint32_t box_rows, box_cols;
+  bool operator==(const MapKey& o) const {
+    return base == o.base && rows == o.rows && cols == o.cols && ld == o.ld && box_rows == o.box_rows &&
+           box_cols == o.box_cols;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    size_t h = std::hash<const void*>()(k.base);
+    h ^= std::hash<uint64_t>()(k.rows * 1000003ull + k.cols * 31ull + k.ld) + 0x9e3779b97f4a7c15ull + (h << 6);
+    h ^= std::hash<uint64_t>()(((uint64_t)k.box_rows << 32) | k.box_cols) + (h << 6) + (h >> 2);
+    return h;
+  }
+};
+
+static std::mutex g_map_mu;
+static std::unordered_map<MapKey, CUtensorMap, MapKeyHash>* g_maps = nullptr;
+static PFN_cuTensorMapEncodeTiled g_encode = nullptr;
+
+const CUtensorMap* tensor_map_2d_bf16(const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                                      uint32_t box_rows, uint32_t box_cols) {
+  std::lock_guard<std::mutex> lock(g_map_mu);
+  if (!g_maps) g_maps = new std::unordered_map<MapKey, CUtensorMap, MapKeyHash>();
+  MapKey key{base, rows, cols, ld, box_rows, box_cols};
+  auto it = g_maps->find(key);
+  if (it != g_maps->end()) return &it->second;
+  if (!g_encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn) {
+      set_error("cuTensorMapEncodeTiled is not available from the driver");
+      return nullptr;
+    }
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled>(fn);
+  }
+  CUtensorMap map;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d) for rows=%llu cols=%llu ld=%llu", (int)r,
+              (unsigned long long)rows, (unsigned long long)cols, (unsigned long long)ld);
+    return nullptr;
+  }
+  if (g_maps->size() > 4096) g_maps->clear();
+  auto res = g_maps->emplace(key, map);
+  return &res.first->second;
+}
+
+struct TcPlan {
+  int n_tiles, m_tiles, kb, grid1;
+  long long U1;
+};
+
+static TcPlan tc_plan(int M, int N, int K) {
+  TcPlan p;
+  p.n_tiles = (N + TC_NT - 1) / TC_NT;
+  p.m_tiles = (M + TC_BM - 1) / TC_BM;
+  p.kb = K / TC_BK;
+  p.U1 = (long long)p.n_tiles * p.kb;
+  p.grid1 = (int)(p.U1 < TC_GRID ? p.U1 : TC_GRID);
+  return p;
+}
+
+}  // namespace dfl
+
+using namespace dfl;
+
+extern "C" size_t dfl_gemm_workspace_bytes(int M, int N, int K, int epilogue) {
+  (void)epilogue;
+  if (M <= 0 || N <= 0 || K <= 0 || K % TC_BK) return 0;
+  TcPlan p = tc_plan(M, N, K);
+  return TC_COUNTER_BYTES + (size_t)p.m_tiles * p.grid1 * 2 * TC_PART_FLOATS * sizeof(float);
+}
+
+extern "C" int dfl_gemm_argmax_tiles(int N) { return (N + 31) / 32; }
+
+extern "C" int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w, int M, int N, int K, int epilogue,
+                             const void* residual, int64_t ldr, void* y, int64_t ldy, void* y2, int64_t ldy2,
+                             void* argmax_partials, const void* norm_w, const float* sumsq_in, int n_parts,
+                             float eps, float* sumsq_out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (M == 0) return DFL_OK;
+  if (!x || !w || M < 0 || N <= 0 || K <= 0) {
+    set_error("dfl_gemm_bf16: null pointer or bad shape M=%d N=%d K=%d", M, N, K);
+    return DFL_ERR_INVALID;
+  }
+  if (K % TC_BK || N % 32 || ldx % 8 || (reinterpret_cast<uintptr_t>(x) & 15) ||
+      (reinterpret_cast<uintptr_t>(w) & 15)) {
+    set_error("dfl_gemm_bf16: needs K %% 64 == 0, N %% 32 == 0, 16-byte aligned x/w, ldx %% 8 == 0 (K=%d N=%d ldx=%lld)",
+              K, N, (long long)ldx);
+    return DFL_ERR_UNSUPPORTED;
+  }
+  if (epilogue == DFL_EPI_ARGMAX) {
+    if (!argmax_partials) {
+      set_error("dfl_gemm_bf16: argmax epilogue needs argmax_partials");
+      return DFL_ERR_INVALID;
+    }
+  } else if (!y) {
+    set_error("dfl_gemm_bf16: y is null");
+    return DFL_ERR_INVALID;
+  }
+  if (epilogue == DFL_EPI_RESIDUAL && !residual) {
+    set_error("dfl_gemm_bf16: residual epilogue needs a residual pointer");
+    return DFL_ERR_INVALID;
+  }
+  if (epilogue == DFL_EPI_SILU_MUL && N % 64) {
+    set_error("dfl_gemm_bf16: silu-mul epilogue needs N %% 64 == 0 (packed gate/up), N=%d", N);
+    return DFL_ERR_UNSUPPORTED;
+  }
+  if (norm_w && (!sumsq_in || n_parts != K / 32 || K > TC_NORM_MAX_K)) {
+    set_error("dfl_gemm_bf16: the fused RMSNorm prologue needs K/32 sumsq_in partials and K <= %d", TC_NORM_MAX_K);
+    return DFL_ERR_INVALID;
+  }
+  TcPlan p = tc_plan(M, N, K);
+  if ((size_t)p.m_tiles * p.n_tiles > (size_t)TC_MAX_COUNTERS) {
+    set_error("dfl_gemm_bf16: too many output tiles (%d x %d)", p.m_tiles, p.n_tiles);
+    return DFL_ERR_UNSUPPORTED;
+  }
+  const size_t need = dfl_gemm_workspace_bytes(M, N, K, epilogue);
+  if (!workspace || workspace_bytes < need) {
+    set_error("dfl_gemm_bf16: workspace too small (%zu < %zu bytes)", workspace_bytes, need);
+    return DFL_ERR_WORKSPACE;
+  }
+  const CUtensorMap* wm = tensor_map_2d_bf16(w, N, K, K, TC_NT, TC_BK);
+  if (!wm) return DFL_ERR_CUDA;
+  const CUtensorMap* xm = tensor_map_2d_bf16(x, M, K, ldx, TC_BM, TC_BK);
+  if (!xm) return DFL_ERR_CUDA;
+
+  TcArgs a;
+  a.res = static_cast<const __nv_bfloat16*>(residual);
+  a.ldr = ldr;
+  a.y = static_cast<__nv_bfloat16*>(y);
+  a.ldy = ldy;
+  a.y2 = static_cast<__nv_bfloat16*>(y2);
+  a.ldy2 = ldy2;
+  a.argmax = static_cast<float2*>(argmax_partials);
+  a.counters = static_cast<int*>(workspace);
+  a.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + TC_COUNTER_BYTES);
+  a.norm_w = static_cast<const __nv_bfloat16*>(norm_w);
+  a.sumsq_in = sumsq_in;
+  a.n_parts = n_parts;
+  a.eps = eps;
+  a.sumsq_out = sumsq_out;
+  a.err = device_error_word();
+  a.n_groups = N / 32;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.n_tiles = p.n_tiles;
+  a.kb = p.kb;
+  a.U1 = p.U1;
+  a.grid1 = p.grid1;
+
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.grid1 * p.m_tiles);
+  cfg.blockDim = dim3(TC_THREADS);
+  cfg.dynamicSmemBytes = TC_SMEM_BASE + (norm_w ? (size_t)K * 2 : 0);
+  cfg.stream = as_stream(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t err;
+  switch (epilogue) {
+#define DFL_LAUNCH(E)                                                                                       \
+  case E: {                                                                                                 \
+    static bool init = false;                                                                               \
+    if (!init) {                                                                                            \
+      cudaFuncSetAttribute(gemm_tc_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize,                  \
+                           TC_SMEM_BASE + TC_NORM_MAX_K * 2);                                               \
+      init = true;                                                                                          \
+    }                                                                                                       \
+    err = cudaLaunchKernelEx(&cfg, gemm_tc_kernel<E>, *wm, *xm, a);                                         \
+    break;                                                                                                  \
+  }
+    DFL_LAUNCH(DFL_EPI_STORE)
+    DFL_LAUNCH(DFL_EPI_RESIDUAL)
+    DFL_LAUNCH(DFL_EPI_SILU_MUL)
+    DFL_LAUNCH(DFL_EPI_ARGMAX)
+#undef DFL_LAUNCH
+    default:
+      set_error("dfl_gemm_bf16: unknown epilogue %d", epilogue);
+      return DFL_ERR_INVALID;
+  }
+  if (err != cudaSuccess) {
+    set_error("dfl_gemm_bf16: launch failed: %s", cudaGetErrorString(err));
+    return DFL_ERR_CUDA;
+  }
+  return DFL_OK;
+}
+
+extern "C" int dfl_device_error(int* code, int clear, void* stream) {
+  if (!code) return DFL_ERR_INVALID;
+  int* word = device_error_word();
+  if (!word) {
+    set_error("dfl_device_error: no device error word");
+    return DFL_ERR_CUDA;
+  }
+  cudaError_t e = cudaMemcpyAsync(code, word, sizeof(int), cudaMemcpyDeviceToHost, as_stream(stream));
+  if (e == cudaSuccess) e = cudaStreamSynchronize(as_stream(stream));
+  if (e == cudaSuccess && clear) e = cudaMemsetAsync(word, 0, sizeof(int), as_stream(stream));
+  if (e == cudaSuccess) e = cudaStreamSynchronize(as_stream(stream));
+  if (e != cudaSuccess) {
+    set_error("dfl_device_error: %s", cudaGetErrorString(e));
+    return DFL_ERR_CUDA;
+  }
+  return DFL_OK;
+}

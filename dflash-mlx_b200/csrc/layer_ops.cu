@@ -67,7 +67,7 @@ __global__ void embed_kernel(const int* __restrict__ tok, const __nv_bfloat16* _
   if (row >= M) return;
   const int t = tok[row];
   __nv_bfloat16* yr = y + (long long)row * ldy;
-  // blockDim.x is a multiple of 8: eight lanes cover one 64-column chunk
+  // blockDim.x is a multiple of 4: four lanes cover one 32-column group
   for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
     uint4 v = make_uint4(0, 0, 0, 0);
     if (t >= 0 && t < V) v = *reinterpret_cast<const uint4*>(table + (long long)t * H + c);
@@ -79,8 +79,7 @@ __global__ void embed_kernel(const int* __restrict__ tok, const __nv_bfloat16* _
       for (int k = 0; k < 8; ++k) ss += bf2f(e[k]) * bf2f(e[k]);
       ss += __shfl_xor_sync(0xffffffffu, ss, 1);
       ss += __shfl_xor_sync(0xffffffffu, ss, 2);
-      ss += __shfl_xor_sync(0xffffffffu, ss, 4);
-      if ((threadIdx.x & 7) == 0) sumsq[(long long)row * (H / 64) + c / 64] = ss;
+      if ((threadIdx.x & 3) == 0) sumsq[(long long)row * (H / 32) + c / 32] = ss;
     }
   }
 }
@@ -206,8 +205,8 @@ extern "C" int dfl_rmsnorm_bf16(const void* x, int64_t ldx, const void* w, void*
 extern "C" int dfl_embed_bf16(const int32_t* tokens, const void* table, void* y, int64_t ldy, int M, int H, int V,
                               float* sumsq_out, void* stream) {
   if (M == 0) return DFL_OK;
-  if (!tokens || !table || !y || H % 64 || ldy % 8) {
-    set_error("dfl_embed_bf16: bad arguments (H must be a multiple of 64)");
+  if (!tokens || !table || !y || H % 8 || ldy % 8 || (sumsq_out && H % 256)) {
+    set_error("dfl_embed_bf16: bad arguments (H %% 8 == 0; H %% 256 == 0 with sumsq_out)");
     return DFL_ERR_INVALID;
   }
   cudaLaunchConfig_t cfg = {};

@@ -95,7 +95,7 @@ class TargetModel:
                 "attn": torch.empty((M, c.num_attention_heads * hd), dtype=torch.bfloat16, device=dev),
                 "act": torch.empty((M, c.intermediate_size), dtype=torch.bfloat16, device=dev),
                 "argmax": torch.empty((M, ops.argmax_tiles(c.vocab_size), 2), dtype=torch.float32, device=dev),
-                "ss": torch.zeros((M, H // 64), dtype=torch.float32, device=dev),
+                "ss": torch.zeros((M, H // 32), dtype=torch.float32, device=dev),
             }
             self._bufs[M] = b
         return b
@@ -235,7 +235,7 @@ class DraftModel:
             if kind == "ctx":
                 b = {
                     "fc": torch.empty((M, H), dtype=torch.bfloat16, device=dev),
-                    "ss": torch.zeros((M, H // 64), dtype=torch.float32, device=dev),
+                    "ss": torch.zeros((M, H // 32), dtype=torch.float32, device=dev),
                     "kv": torch.empty((M, c.num_hidden_layers * 2 * Hkv * hd), dtype=torch.bfloat16, device=dev),
                 }
             else:
@@ -247,7 +247,7 @@ class DraftModel:
                     "attn": torch.empty((M, Hq * hd), dtype=torch.bfloat16, device=dev),
                     "act": torch.empty((M, c.intermediate_size), dtype=torch.bfloat16, device=dev),
                     "argmax": torch.empty((M, ops.argmax_tiles(c.vocab_size), 2), dtype=torch.float32, device=dev),
-                    "ss": torch.zeros((M, H // 64), dtype=torch.float32, device=dev),
+                    "ss": torch.zeros((M, H // 32), dtype=torch.float32, device=dev),
                 }
             self._bufs[key] = b
         return b

@@ -76,7 +76,7 @@ def gemm(x: torch.Tensor, w: torch.Tensor, epilogue: int = EPI_STORE, residual: 
          norm_w: torch.Tensor | None = None, sumsq_in: torch.Tensor | None = None, eps: float = 1e-6,
          sumsq_out: torch.Tensor | None = None) -> torch.Tensor:
     """y = xn @ w.T (bf16 in, fp32 accumulate) with a fused epilogue; xn = RMSNorm(x) * norm_w
-    when norm_w is given (sumsq_in: [M, K/64] fp32 row sum-of-squares partials of x)."""
+    when norm_w is given (sumsq_in: [M, K/32] fp32 row sum-of-squares partials of x)."""
     _need_cuda(x, w, residual, out, out2, argmax_partials, norm_w, sumsq_in, sumsq_out)
     if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
         raise ValueError("gemm takes bf16 x and w")
@@ -91,12 +91,12 @@ def gemm(x: torch.Tensor, w: torch.Tensor, epilogue: int = EPI_STORE, residual: 
     n_parts = 0
     if norm_w is not None:
         if sumsq_in is None or sumsq_in.shape[0] < M or sumsq_in.dtype != torch.float32:
-            raise ValueError("the fused RMSNorm needs fp32 sumsq_in partials [M, K/64]")
+            raise ValueError("the fused RMSNorm needs fp32 sumsq_in partials [M, K/32]")
         n_parts = sumsq_in.shape[1]
-        if n_parts != K // 64 or not sumsq_in.is_contiguous():
-            raise ValueError("sumsq_in must be contiguous [M, K/64]")
-    if sumsq_out is not None and (sumsq_out.shape[1] != (N + 63) // 64 or not sumsq_out.is_contiguous()):
-        raise ValueError("sumsq_out must be contiguous [M, N/64]")
+        if n_parts != K // 32 or not sumsq_in.is_contiguous():
+            raise ValueError("sumsq_in must be contiguous [M, K/32]")
+    if sumsq_out is not None and (sumsq_out.shape[1] != N // 32 or not sumsq_out.is_contiguous()):
+        raise ValueError("sumsq_out must be contiguous [M, N/32]")
     if epilogue == EPI_ARGMAX:
         ntiles = int(_lib.query("dfl_gemm_argmax_tiles", N))
         if argmax_partials is None:

@@ -34,7 +34,7 @@ extern "C" {
 #define DFL_EPI_STORE 0    /* y = bf16(acc) */
 #define DFL_EPI_RESIDUAL 1 /* y = bf16(residual + bf16(acc)); optional second copy to y2 (hidden-state tap) */
 #define DFL_EPI_SILU_MUL 2 /* W rows packed per 64: [32 gate | 32 up]; y[:, n] = bf16(silu(gate) * up), N/2 columns */
-#define DFL_EPI_ARGMAX 3   /* per row and 64-column tile: (max bf16 logit, lowest index) into argmax partials */
+#define DFL_EPI_ARGMAX 3   /* per row and 32 columns: (max bf16 logit, lowest index) into argmax partials */
 
 /* keys per attention chunk: the fixed key ranges merged in order by dfl_attention */
 #define DFL_ATTN_CHUNK 128
@@ -60,20 +60,20 @@ const char* dfl_last_error(void);
 /* ---- dense projections ----------------------------------------------------
  * Y[M,N] = Xn[M,K] . W[N,K]^T with fp32 accumulation and a fused epilogue, where
  * Xn = X, or RMSNorm(X) * norm_w when norm_w != NULL (fused prologue: the row
- * sum of squares of X is given as sumsq_in[M][n_parts] partials, summed in
- * order; K / 64 partials as written by DFL_EPI_STORE / DFL_EPI_RESIDUAL's
+ * sum of squares of X is given as sumsq_in[M][K/32] partials, one per 32
+ * columns, summed in order; as written by DFL_EPI_STORE / DFL_EPI_RESIDUAL's
  * sumsq_out or by dfl_embed_bf16).
  * Replaces the nn.Linear (and the RMSNorm feeding it) of the verify / draft
  * forward: mlx-lm qwen3 Attention and MLP (driven from adapters.py:611-631),
  * DFlashAttention q/k/v/o projections (draft.py:75-98, 118-159), the draft fc
  * + hidden_norm (draft.py:196-201, 217) and lm_head_logits / lm_head_argmax
  * (adapters.py:264-271, 606-609; runtime.py:22-29 argmax).
- * K % 128 == 0, N % 8 == 0, x / w / y 16-byte aligned; the fused norm needs K <= 8192. Scratch: workspace of
+ * K % 64 == 0, N % 32 == 0, x / w 16-byte aligned; the fused norm needs K <= 8192. Scratch: workspace of
  * dfl_gemm_workspace_bytes() bytes, zero-filled once before first use (the
  * kernel leaves its counters at zero); one workspace per stream.
- * DFL_EPI_ARGMAX writes float2 partials [M][dfl_gemm_argmax_tiles(N)].
- * sumsq_out (nullable, STORE / RESIDUAL): per-row sum of squares of the bf16
- * output per 64-column tile, [M][N/64]. */
+ * DFL_EPI_ARGMAX writes float2 partials [M][dfl_gemm_argmax_tiles(N)] (one per
+ * 32 columns). sumsq_out (nullable, STORE / RESIDUAL): per-row sum of squares of
+ * the bf16 output per 32 columns, [M][N/32]. */
 size_t dfl_gemm_workspace_bytes(int M, int N, int K, int epilogue);
 int dfl_gemm_argmax_tiles(int N);
 int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w, int M, int N, int K, int epilogue,
@@ -94,7 +94,7 @@ int dfl_rmsnorm_bf16(const void* x, int64_t ldx, const void* w, void* y, int64_t
                      void* stream);
 
 /* Token embedding gather (adapters.py:603-604 embed_tokens; runtime.py:410).
- * sumsq_out (nullable): per-row sum of squares per 64 columns, [M][H/64]
+ * sumsq_out (nullable): per-row sum of squares per 32 columns, [M][H/32]
  * (feeds the fused RMSNorm prologue of dfl_gemm_bf16). */
 int dfl_embed_bf16(const int32_t* tokens, const void* table, void* y, int64_t ldy, int M, int H, int V,
                    float* sumsq_out, void* stream);

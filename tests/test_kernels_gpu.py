@@ -28,7 +28,7 @@ def _rand(shape, std=1.0, seed=0, dtype=torch.bfloat16):
 
 
 @pytest.mark.parametrize("M,N,K", [(16, 6144, 2560), (1, 2560, 4096), (5, 2560, 9728), (40, 512, 256),
-                                   (16, 151936, 2560), (128, 1536, 2560)])
+                                   (16, 151936, 2560), (128, 1536, 2560), (16, 10240, 2560), (2, 2560, 12800)])
 def test_gemm_store_matches_fp32(M, N, K):
     ops = _ops()
     x = _rand((M, K), 1.0, 1)
@@ -197,10 +197,10 @@ def test_gemm_fused_rmsnorm_prologue(M, N, K):
     nw = (1.0 + 0.1 * _rand((K,), 1.0, 32).float()).bfloat16()
     w = _rand((N, K), 0.02, 33)
     x = torch.empty((M, K), dtype=torch.bfloat16, device=DEV)
-    ss = torch.empty((M, K // 64), dtype=torch.float32, device=DEV)
+    ss = torch.empty((M, K // 32), dtype=torch.float32, device=DEV)
     ops.embed(tok.to(DEV), table.to(DEV), out=x, sumsq_out=ss)
     assert torch.equal(x.cpu(), table[tok.long()])
-    ref_ss = (table[tok.long()].float() ** 2).reshape(M, K // 64, 64).sum(-1)
+    ref_ss = (table[tok.long()].float() ** 2).reshape(M, K // 32, 32).sum(-1)
     assert torch.allclose(ss.cpu(), ref_ss, rtol=1e-5)
     y = ops.gemm(x, w.to(DEV), norm_w=nw.to(DEV), sumsq_in=ss).float().cpu()
     ref = O.linear(O.rms_norm(table[tok.long()].float(), nw, 1e-6), w)
@@ -215,10 +215,10 @@ def test_gemm_sumsq_out_chain():
     x, w1, r, w2 = _rand((M, K), 1.0, 34), _rand((H, K), 0.02, 35), _rand((M, H), 1.0, 36), _rand((512, H), 0.02, 37)
     nw = torch.ones(H, dtype=torch.bfloat16)
     h = r.to(DEV).clone()
-    ss = torch.empty((M, H // 64), dtype=torch.float32, device=DEV)
+    ss = torch.empty((M, H // 32), dtype=torch.float32, device=DEV)
     ops.gemm(x.to(DEV), w1.to(DEV), ops.EPI_RESIDUAL, residual=h, out=h, sumsq_out=ss)
     ref_h = (r.float() + (x.float() @ w1.float().T).bfloat16().float()).bfloat16().float()
-    assert torch.allclose(ss.cpu(), (h.float().cpu() ** 2).reshape(M, -1, 64).sum(-1), rtol=1e-4)
+    assert torch.allclose(ss.cpu(), (h.float().cpu() ** 2).reshape(M, -1, 32).sum(-1), rtol=1e-4)
     y = ops.gemm(h, w2.to(DEV), norm_w=nw.to(DEV), sumsq_in=ss).float().cpu()
     ref = O.linear(O.rms_norm(ref_h, nw, 1e-6), w2)
     assert (y - ref).abs().max().item() <= 3e-2 * ref.abs().max().item() + 1e-3

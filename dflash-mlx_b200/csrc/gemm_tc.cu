@@ -14,8 +14,12 @@
 //    128-byte swizzle) and the 16 tokens of X are its N side, so one
 //    tcgen05.mma.cta_group::1.kind::f16 M=128 N=16 K=16 covers 128 outputs of all
 //    16 rows; the accumulator lives in TMEM (2 buffers x 16 columns).
-//  * Warp roles: warp 0 = TMA producer (2-D tiled loads, evict-first for W,
-//    evict-last for X), warp 1 = TMEM allocator + single-thread MMA issuer
+//  * W lives in HBM pre-tiled: every (128-row, 64-k) unit is one contiguous 16 KB
+//    block already in the 128-byte-swizzle shared-memory image (dfl_pack_weight_bf16),
+//    units ordered tile-major then k, so each CTA streams ONE contiguous byte range
+//    with 1-D bulk copies.
+//  * Warp roles: warp 0 = producer (1-D bulk copies of W with an evict-first L2
+//    hint, 2-D TMA tile loads of X, evict-last), warp 1 = TMEM allocator + single-thread MMA issuer
 //    (tcgen05.commit releases each shared-memory stage back to the producer),
 //    warps 2-5 = epilogue (tcgen05.ld 32x32b: each thread owns one output column
 //    for the 16 rows) and, when the RMSNorm is fused, the per-stage rescale of X.
@@ -53,7 +57,10 @@ int* device_error_word() {
 constexpr int TC_NT = 128;  // W rows per tile (MMA M)
 constexpr int TC_BK = 64;   // k per stage (one 128-byte swizzle row)
 constexpr int TC_BM = 16;   // tokens per tile (MMA N)
-constexpr int TC_STAGES = 5;
+#ifndef DFL_TC_STAGES
+#define DFL_TC_STAGES 5
+#endif
+constexpr int TC_STAGES = DFL_TC_STAGES;
 constexpr int TC_GRID = 148;  // work split over the B200's SM count (fixed: part of the reduction order)
 constexpr int TC_THREADS = 192;
 constexpr int TC_EPI_WARP0 = 2;
@@ -78,6 +85,7 @@ constexpr uint32_t TC_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(T
                               ((uint32_t)(TC_NT >> 4) << 24);
 
 struct TcArgs {
+  const unsigned char* wt;  // pre-tiled weights: unit u at wt + u * TC_W_BYTES
   const __nv_bfloat16* res;
   long long ldr;
   __nv_bfloat16* y;
@@ -85,7 +93,7 @@ struct TcArgs {
   __nv_bfloat16* y2;
   long long ldy2;
   float2* argmax;  // [M][N/32]
-  float* partial;  // [m_tiles][grid1][2][16*128]
+  float* partial;  // [m_tiles][grid1][2][128 cols][16 rows]
   int* counters;   // [m_tiles * n_tiles]
   const __nv_bfloat16* norm_w;
   const float* sumsq_in;  // [M][n_parts] (n_parts = K/32)
@@ -210,7 +218,7 @@ __device__ __forceinline__ void tc_epilogue(const TcArgs& a, float* v, int mt, i
 
 template <int EPI>
 __global__ void __launch_bounds__(TC_THREADS, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap, TcArgs a) {
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap xmap, TcArgs a) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -265,7 +273,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       for (int i = 0; i < pre; ++i) {
         const long long u = u0 + i;
         mbar_expect_tx(&full[i], TC_W_BYTES + TC_X_BYTES);
-        tma_load_2d(&wmap, &full[i], smem + i * TC_W_BYTES, (int)(u % a.kb) * TC_BK, (int)(u / a.kb) * TC_NT, pol_w);
+        bulk_load(smem + i * TC_W_BYTES, a.wt + u * TC_W_BYTES, TC_W_BYTES, &full[i], pol_w);
       }
       grid_dependency_wait();  // X is produced by the previous kernel
       for (int i = 0; i < pre; ++i)
@@ -277,7 +285,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (!mbar_wait(&empty[s], ((i / TC_STAGES) & 1) ^ 1, 201, a.err)) break;
         const long long u = u0 + i;
         mbar_expect_tx(&full[s], TC_W_BYTES + TC_X_BYTES);
-        tma_load_2d(&wmap, &full[s], smem + s * TC_W_BYTES, (int)(u % a.kb) * TC_BK, (int)(u / a.kb) * TC_NT, pol_w);
+        bulk_load(smem + s * TC_W_BYTES, a.wt + u * TC_W_BYTES, TC_W_BYTES, &full[s], pol_w);
         tma_load_2d(&xmap, &full[s], smem + TC_OFF_X + s * TC_X_BYTES, (int)(u % a.kb) * TC_BK, mt * TC_BM, pol_x);
         issued = i + 1;
       }
@@ -373,9 +381,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (c_first != c_last) {
         const int tile_id = mt * a.n_tiles + nt;
         const int slot = (nt == (int)(u0 / a.kb)) ? 0 : 1;
-        float* mine = a.partial + (((long long)mt * a.grid1 + c) * 2 + slot) * TC_PART_FLOATS;
+        float4* mine = reinterpret_cast<float4*>(a.partial + (((long long)mt * a.grid1 + c) * 2 + slot) * TC_PART_FLOATS +
+                                                 col * TC_BM);
 #pragma unroll
-        for (int t = 0; t < TC_BM; ++t) mine[t * TC_NT + col] = v[t];
+        for (int t4 = 0; t4 < TC_BM / 4; ++t4) mine[t4] = make_float4(v[4 * t4], v[4 * t4 + 1], v[4 * t4 + 2], v[4 * t4 + 3]);
         __threadfence();
         epi_sync();
         if (et == 0) s_flag = (atomicAdd(a.counters + tile_id, 1) == c_last - c_first);
@@ -388,9 +397,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           for (int cs = c_first; cs <= c_last; ++cs) {
             const long long cs_u0 = (long long)cs * a.U1 / a.grid1;
             const int sl = (nt == (int)(cs_u0 / a.kb)) ? 0 : 1;
-            const float* src = a.partial + (((long long)mt * a.grid1 + cs) * 2 + sl) * TC_PART_FLOATS;
+            const float4* src = reinterpret_cast<const float4*>(
+                a.partial + (((long long)mt * a.grid1 + cs) * 2 + sl) * TC_PART_FLOATS + col * TC_BM);
 #pragma unroll
-            for (int t = 0; t < TC_BM; ++t) v[t] += __ldcg(src + t * TC_NT + col);
+            for (int t4 = 0; t4 < TC_BM / 4; ++t4) {
+              const float4 f = __ldcg(src + t4);
+              v[4 * t4] += f.x;
+              v[4 * t4 + 1] += f.y;
+              v[4 * t4 + 2] += f.z;
+              v[4 * t4 + 3] += f.w;
+            }
           }
           if (et == 0) a.counters[tile_id] = 0;  // ready for the next launch / graph replay
         }
@@ -405,6 +421,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "n"(TC_TMEM_COLS));
+  }
+}
+
+// Row-major W [N, K] -> tiled image: unit (tile t, k-block j) at ((t*kb)+j)*16 KB, row r
+// (W row t*128+r, zero past N) holding 16-byte chunk c of k-block j at r*128 + ((c^(r&7))*16).
+__global__ void pack_weight_kernel(const __nv_bfloat16* __restrict__ w, int N, int K,
+                                   unsigned char* __restrict__ out, long long n_chunks) {
+  const int kb = K / TC_BK;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n_chunks; i += (long long)gridDim.x * blockDim.x) {
+    const int c = (int)(i & 7);
+    const long long rowchunk = i >> 3;  // global tiled row index within units
+    const int r = (int)(rowchunk % TC_NT);
+    const long long unit = rowchunk / TC_NT;
+    const int j = (int)(unit % kb);
+    const long long t = unit / kb;
+    const long long n = t * TC_NT + r;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (n < N) v = *reinterpret_cast<const uint4*>(w + n * (long long)K + (long long)j * TC_BK + c * 8);
+    *reinterpret_cast<uint4*>(out + unit * TC_W_BYTES + r * 128 + ((c ^ (r & 7)) << 4)) = v;
   }
 }
 
@@ -496,11 +531,34 @@ extern "C" size_t dfl_gemm_workspace_bytes(int M, int N, int K, int epilogue) {
 
 extern "C" int dfl_gemm_argmax_tiles(int N) { return (N + 31) / 32; }
 
-extern "C" int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w, int M, int N, int K, int epilogue,
+extern "C" size_t dfl_packed_weight_bytes(int N, int K) {
+  if (N <= 0 || K <= 0 || K % TC_BK) return 0;
+  return (size_t)((N + TC_NT - 1) / TC_NT) * (K / TC_BK) * TC_W_BYTES;
+}
+
+extern "C" int dfl_pack_weight_bf16(const void* w, int N, int K, void* out, size_t out_bytes, void* stream) {
+  if (!w || !out || N <= 0 || K <= 0 || K % TC_BK || (reinterpret_cast<uintptr_t>(w) & 15) ||
+      (reinterpret_cast<uintptr_t>(out) & 15)) {
+    set_error("dfl_pack_weight_bf16: bad arguments (K %% 64 == 0, 16-byte aligned buffers)");
+    return DFL_ERR_INVALID;
+  }
+  if (out_bytes < dfl_packed_weight_bytes(N, K)) {
+    set_error("dfl_pack_weight_bf16: output too small");
+    return DFL_ERR_INVALID;
+  }
+  const long long n_chunks = (long long)dfl_packed_weight_bytes(N, K) / 16;
+  const int blocks = (int)((n_chunks + 255) / 256 < 148 * 16 ? (n_chunks + 255) / 256 : 148 * 16);
+  pack_weight_kernel<<<blocks, 256, 0, as_stream(stream)>>>(static_cast<const __nv_bfloat16*>(w), N, K,
+                                                            static_cast<unsigned char*>(out), n_chunks);
+  return check_launch("dfl_pack_weight_bf16");
+}
+
+extern "C" int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w_packed, int M, int N, int K, int epilogue,
                              const void* residual, int64_t ldr, void* y, int64_t ldy, void* y2, int64_t ldy2,
                              void* argmax_partials, const void* norm_w, const float* sumsq_in, int n_parts,
                              float eps, float* sumsq_out, void* workspace, size_t workspace_bytes, void* stream) {
   if (M == 0) return DFL_OK;
+  const void* w = w_packed;
   if (!x || !w || M < 0 || N <= 0 || K <= 0) {
     set_error("dfl_gemm_bf16: null pointer or bad shape M=%d N=%d K=%d", M, N, K);
     return DFL_ERR_INVALID;
@@ -542,12 +600,11 @@ extern "C" int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w, int M, i
     set_error("dfl_gemm_bf16: workspace too small (%zu < %zu bytes)", workspace_bytes, need);
     return DFL_ERR_WORKSPACE;
   }
-  const CUtensorMap* wm = tensor_map_2d_bf16(w, N, K, K, TC_NT, TC_BK);
-  if (!wm) return DFL_ERR_CUDA;
   const CUtensorMap* xm = tensor_map_2d_bf16(x, M, K, ldx, TC_BM, TC_BK);
   if (!xm) return DFL_ERR_CUDA;
 
   TcArgs a;
+  a.wt = static_cast<const unsigned char*>(w);
   a.res = static_cast<const __nv_bfloat16*>(residual);
   a.ldr = ldr;
   a.y = static_cast<__nv_bfloat16*>(y);
@@ -592,7 +649,7 @@ extern "C" int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w, int M, i
                            TC_SMEM_BASE + TC_NORM_MAX_K * 2);                                               \
       init = true;                                                                                          \
     }                                                                                                       \
-    err = cudaLaunchKernelEx(&cfg, gemm_tc_kernel<E>, *wm, *xm, a);                                         \
+    err = cudaLaunchKernelEx(&cfg, gemm_tc_kernel<E>, *xm, a);                                              \
     break;                                                                                                  \
   }
     DFL_LAUNCH(DFL_EPI_STORE)

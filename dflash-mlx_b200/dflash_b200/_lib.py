@@ -6,6 +6,7 @@ fallback: if the library is missing or a CUDA device is absent, every op raises.
 from __future__ import annotations
 
 import ctypes
+import os
 from ctypes import POINTER, c_char_p, c_float, c_int, c_int64, c_size_t, c_void_p
 from pathlib import Path
 
@@ -32,6 +33,8 @@ SIGNATURES: dict[str, tuple] = {
                               c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int, c_float, c_void_p,
                               c_void_p, c_size_t, c_void_p]),
     "dfl_device_error": (c_int, [POINTER(c_int), c_int, c_void_p]),
+    "dfl_packed_weight_bytes": (c_size_t, [c_int, c_int]),
+    "dfl_pack_weight_bf16": (c_int, [c_void_p, c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "dfl_rmsnorm_bf16": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int, c_int, c_float, c_void_p]),
     "dfl_embed_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_int, c_void_p, c_void_p]),
     "dfl_qkv_rope_append": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
@@ -64,7 +67,7 @@ def load(path: Path | str | None = None) -> ctypes.CDLL:
     global _LIB
     if _LIB is not None and path is None:
         return _LIB
-    p = Path(path) if path is not None else LIB_PATH
+    p = Path(path) if path is not None else Path(os.environ.get("DFLASH_B200_LIB", LIB_PATH))
     if not p.exists():
         raise RuntimeError(
             f"dflash-b200 native library not found at {p}; build it with "

@@ -57,18 +57,19 @@ class TargetModel:
         self.cfg = cfg
         self.device = torch.device(device)
         dev = self.device
-        self.embed_w = weights["embed"].to(dev).contiguous()
-        self.lm_head_w = self.embed_w if cfg.tie_word_embeddings else weights["lm_head"].to(dev).contiguous()
+        P = ops.pack_weight
+        self.embed_w = weights["embed"].to(dev).contiguous()  # row-major: the embedding gather
+        self.lm_head_w = P(self.embed_w if cfg.tie_word_embeddings else weights["lm_head"].to(dev))
         self.norm_w = weights["norm"].to(dev)
         self.layers = []
         for lw in weights["layers"]:
             self.layers.append({
                 "in_norm": lw["input_layernorm"].to(dev),
                 "post_norm": lw["post_attention_layernorm"].to(dev),
-                "w_qkv": torch.cat([lw["q_proj"], lw["k_proj"], lw["v_proj"]], 0).to(dev).contiguous(),
-                "w_o": lw["o_proj"].to(dev).contiguous(),
-                "w_gu": pack_gate_up(lw["gate_proj"].to(dev), lw["up_proj"].to(dev)),
-                "w_down": lw["down_proj"].to(dev).contiguous(),
+                "w_qkv": P(torch.cat([lw["q_proj"].to(dev), lw["k_proj"].to(dev), lw["v_proj"].to(dev)], 0)),
+                "w_o": P(lw["o_proj"].to(dev)),
+                "w_gu": P(pack_gate_up(lw["gate_proj"].to(dev), lw["up_proj"].to(dev))),
+                "w_down": P(lw["down_proj"].to(dev)),
                 "q_norm": lw["q_norm"].to(dev),
                 "k_norm": lw["k_norm"].to(dev),
             })
@@ -187,7 +188,8 @@ class DraftModel:
         self.device = target.device
         self.mask_mode = mask_mode
         dev = self.device
-        self.fc = weights["fc"].to(dev).contiguous()
+        P = ops.pack_weight
+        self.fc = P(weights["fc"].to(dev))
         self.hidden_norm = weights["hidden_norm"].to(dev)
         self.norm_w = weights["norm"].to(dev)
         self.layers = []
@@ -196,15 +198,15 @@ class DraftModel:
             self.layers.append({
                 "in_norm": lw["input_layernorm"].to(dev),
                 "post_norm": lw["post_attention_layernorm"].to(dev),
-                "w_qkv": torch.cat([lw["q_proj"], lw["k_proj"], lw["v_proj"]], 0).to(dev).contiguous(),
-                "w_o": lw["o_proj"].to(dev).contiguous(),
-                "w_gu": pack_gate_up(lw["gate_proj"].to(dev), lw["up_proj"].to(dev)),
-                "w_down": lw["down_proj"].to(dev).contiguous(),
+                "w_qkv": P(torch.cat([lw["q_proj"].to(dev), lw["k_proj"].to(dev), lw["v_proj"].to(dev)], 0)),
+                "w_o": P(lw["o_proj"].to(dev)),
+                "w_gu": P(pack_gate_up(lw["gate_proj"].to(dev), lw["up_proj"].to(dev))),
+                "w_down": P(lw["down_proj"].to(dev)),
                 "q_norm": lw["q_norm"].to(dev),
                 "k_norm": lw["k_norm"].to(dev),
             })
-            ctx_kv += [lw["k_proj"], lw["v_proj"]]
-        self.w_ctx_kv = torch.cat(ctx_kv, 0).to(dev).contiguous()
+            ctx_kv += [lw["k_proj"].to(dev), lw["v_proj"].to(dev)]
+        self.w_ctx_kv = P(torch.cat(ctx_kv, 0))
         self.inv_freq = rope_inv_freq(cfg.head_dim, cfg.rope_theta, dev)
         self._bufs: dict[tuple, dict[str, torch.Tensor]] = {}
 

@@ -70,19 +70,54 @@ def workspace(device: torch.device | None = None) -> Workspace:
     return ws
 
 
-def gemm(x: torch.Tensor, w: torch.Tensor, epilogue: int = EPI_STORE, residual: torch.Tensor | None = None,
+class PackedWeight:
+    """A [N, K] bf16 weight in the GEMM's pre-tiled HBM layout (dfl_pack_weight_bf16):
+    128-row x 64-column units, each one contiguous 16 KB block in the tensor cores'
+    128-byte-swizzled K-major image."""
+
+    def __init__(self, w: torch.Tensor):
+        _need_cuda(w)
+        if w.dtype != torch.bfloat16 or w.dim() != 2:
+            raise ValueError("pack_weight takes a 2-D bf16 matrix")
+        w = w.contiguous()
+        self.N, self.K = w.shape
+        nbytes = int(_lib.query("dfl_packed_weight_bytes", self.N, self.K))
+        if nbytes == 0:
+            raise ValueError(f"cannot pack a [{self.N}, {self.K}] weight (K must be a multiple of 64)")
+        self.data = torch.empty(nbytes, dtype=torch.uint8, device=w.device)
+        _lib.call("dfl_pack_weight_bf16", _ptr(w), self.N, self.K, _ptr(self.data), nbytes, _stream())
+
+    @property
+    def shape(self) -> tuple[int, int]:
+        return (self.N, self.K)
+
+    @property
+    def device(self) -> torch.device:
+        return self.data.device
+
+    def data_ptr(self) -> int:
+        return self.data.data_ptr()
+
+
+def pack_weight(w: torch.Tensor) -> PackedWeight:
+    return PackedWeight(w)
+
+
+def gemm(x: torch.Tensor, w: PackedWeight | torch.Tensor, epilogue: int = EPI_STORE, residual: torch.Tensor | None = None,
          out: torch.Tensor | None = None, out2: torch.Tensor | None = None,
          argmax_partials: torch.Tensor | None = None, ws: Workspace | None = None,
          norm_w: torch.Tensor | None = None, sumsq_in: torch.Tensor | None = None, eps: float = 1e-6,
          sumsq_out: torch.Tensor | None = None) -> torch.Tensor:
     """y = xn @ w.T (bf16 in, fp32 accumulate) with a fused epilogue; xn = RMSNorm(x) * norm_w
     when norm_w is given (sumsq_in: [M, K/32] fp32 row sum-of-squares partials of x)."""
-    _need_cuda(x, w, residual, out, out2, argmax_partials, norm_w, sumsq_in, sumsq_out)
-    if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
-        raise ValueError("gemm takes bf16 x and w")
+    if isinstance(w, torch.Tensor):  # convenience for tests: pack on the fly
+        w = PackedWeight(w)
+    _need_cuda(x, residual, out, out2, argmax_partials, norm_w, sumsq_in, sumsq_out)
+    if x.dtype != torch.bfloat16:
+        raise ValueError("gemm takes bf16 x")
     M, K = x.shape
     N, K2 = w.shape
-    if K != K2 or not w.is_contiguous():
+    if K != K2:
         raise ValueError(f"gemm shape mismatch x{tuple(x.shape)} w{tuple(w.shape)}")
     ldx = _row_stride(x)
     ws = ws or workspace(x.device)

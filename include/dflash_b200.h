@@ -76,7 +76,16 @@ const char* dfl_last_error(void);
  * the bf16 output per 32 columns, [M][N/32]. */
 size_t dfl_gemm_workspace_bytes(int M, int N, int K, int epilogue);
 int dfl_gemm_argmax_tiles(int N);
-int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w, int M, int N, int K, int epilogue,
+
+/* Weights are consumed in a pre-tiled HBM layout: W [N, K] row-major is cut into
+ * 128-row x 64-column units, each stored as one contiguous 16 KB block in the
+ * 128-byte-swizzled K-major image the tensor cores read (rows past N are zero),
+ * units ordered by 128-row tile, then by k. dfl_pack_weight_bf16 converts a
+ * row-major matrix (done once at load time). */
+size_t dfl_packed_weight_bytes(int N, int K);
+int dfl_pack_weight_bf16(const void* w, int N, int K, void* out, size_t out_bytes, void* stream);
+
+int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w_packed, int M, int N, int K, int epilogue,
                   const void* residual, int64_t ldr, void* y, int64_t ldy, void* y2, int64_t ldy2,
                   void* argmax_partials, const void* norm_w, const float* sumsq_in, int n_parts, float eps,
                   float* sumsq_out, void* workspace, size_t workspace_bytes, void* stream);

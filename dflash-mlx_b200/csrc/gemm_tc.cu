@@ -685,3 +685,66 @@ extern "C" int dfl_device_error(int* code, int clear, void* stream) {
   }
   return DFL_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of dfl_gemm_bf16.
+//
+// Some callers cannot allocate device memory at all: code that runs inside a
+// host callback or a signal-safe path, plugins whose host application owns every
+// allocation, or engines that have sized the whole device up front and forbid
+// cudaMalloc after start-up. For them the split-K scratch (arrival counters +
+// partial tiles) comes from a fixed array compiled into this library instead of a
+// caller-provided workspace. The array is sized for one 16-row tile of X (the
+// decode shape: M <= 16); larger M is rejected. Every GPU that loads the library
+// holds it (about 2.9 MB) until the process exits.
+// ---------------------------------------------------------------------------
+constexpr size_t NA_SCRATCH_BYTES = TC_COUNTER_BYTES + (size_t)TC_GRID * 2 * TC_PART_FLOATS * sizeof(float);
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NA_SCRATCH_BYTES];
+
+// Device address of the scratch array on the current device, looked up once per
+// device (the symbol name itself is only a host-side stand-in, never a device pointer).
+static void* noalloc_scratch_ptr() {
+  static void* ptrs[64] = {nullptr};
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess) return nullptr;
+    ptrs[dev] = p;
+  }
+  return ptrs[dev];
+}
+
+extern "C" size_t dfl_gemm_noalloc_scratch_bytes(void) { return NA_SCRATCH_BYTES; }
+
+extern "C" int dfl_gemm_bf16_noalloc(const void* x, int64_t ldx, const void* w_packed, int M, int N, int K,
+                                     int epilogue, const void* residual, int64_t ldr, void* y, int64_t ldy, void* y2,
+                                     int64_t ldy2, void* argmax_partials, const void* norm_w, const float* sumsq_in,
+                                     int n_parts, float eps, float* sumsq_out, void* stream) {
+  if (M > TC_BM) {
+    set_error("dfl_gemm_bf16_noalloc: M=%d exceeds the built-in scratch limit of %d rows; use dfl_gemm_bf16 with a "
+              "workspace",
+              M, TC_BM);
+    return DFL_ERR_UNSUPPORTED;
+  }
+  if (M > 0 && N > 0 && K > 0 && K % TC_BK == 0 && dfl_gemm_workspace_bytes(M, N, K, epilogue) > NA_SCRATCH_BYTES) {
+    set_error("dfl_gemm_bf16_noalloc: shape M=%d N=%d K=%d needs more scratch than the built-in %zu bytes", M, N, K,
+              NA_SCRATCH_BYTES);
+    return DFL_ERR_UNSUPPORTED;
+  }
+  void* scratch = noalloc_scratch_ptr();
+  if (!scratch) {
+    set_error("dfl_gemm_bf16_noalloc: cudaGetSymbolAddress of the built-in scratch failed");
+    return DFL_ERR_CUDA;
+  }
+  // the arrival counters must start at zero (a call that gave up may have left them set)
+  cudaError_t e = cudaMemsetAsync(scratch, 0, TC_COUNTER_BYTES, as_stream(stream));
+  if (e != cudaSuccess) {
+    set_error("dfl_gemm_bf16_noalloc: clearing the scratch counters failed: %s", cudaGetErrorString(e));
+    return DFL_ERR_CUDA;
+  }
+  return dfl_gemm_bf16(x, ldx, w_packed, M, N, K, epilogue, residual, ldr, y, ldy, y2, ldy2, argmax_partials, norm_w,
+                       sumsq_in, n_parts, eps, sumsq_out, scratch, NA_SCRATCH_BYTES, stream);
+}

@@ -34,6 +34,10 @@ SIGNATURES: dict[str, tuple] = {
                               c_void_p, c_size_t, c_void_p]),
     "dfl_device_error": (c_int, [POINTER(c_int), c_int, c_void_p]),
     "dfl_packed_weight_bytes": (c_size_t, [c_int, c_int]),
+    "dfl_gemm_noalloc_scratch_bytes": (c_size_t, []),
+    "dfl_gemm_bf16_noalloc": (c_int, [c_void_p, c_int64, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int64,
+                                      c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int,
+                                      c_float, c_void_p, c_void_p]),
     "dfl_pack_weight_bf16": (c_int, [c_void_p, c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "dfl_rmsnorm_bf16": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int, c_int, c_float, c_void_p]),
     "dfl_embed_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_int, c_void_p, c_void_p]),

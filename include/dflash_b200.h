@@ -95,6 +95,23 @@ int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w_packed, int M, int N
  * the given stream. */
 int dfl_device_error(int* code, int clear, void* stream);
 
+/* dfl_gemm_bf16 without a workspace argument, for callers that cannot allocate
+ * device memory (host callbacks, plugins whose host owns every allocation,
+ * engines that forbid cudaMalloc after start-up). No counterpart in the
+ * reference. The split-K scratch is a fixed array inside this library
+ * (dfl_gemm_noalloc_scratch_bytes(), about 2.9 MB held by every GPU that loads
+ * the library until exit), sized for M <= 16 rows; larger M returns
+ * DFL_ERR_UNSUPPORTED. No cudaMalloc / cudaFree is called. The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress) with that
+ * device current; make that first call before any stream capture. All calls
+ * share the array and each clears its counters first: calls that overlap on
+ * the GPU (different streams, or concurrent host threads) race on it. */
+size_t dfl_gemm_noalloc_scratch_bytes(void);
+int dfl_gemm_bf16_noalloc(const void* x, int64_t ldx, const void* w_packed, int M, int N, int K, int epilogue,
+                          const void* residual, int64_t ldr, void* y, int64_t ldy, void* y2, int64_t ldy2,
+                          void* argmax_partials, const void* norm_w, const float* sumsq_in, int n_parts, float eps,
+                          float* sumsq_out, void* stream);
+
 /* ---- row kernels ----------------------------------------------------------
  * RMSNorm y = w * x * rsqrt(mean(x^2) + eps) (fp32 math, bf16 out); w may be
  * NULL (unit weight). Replaces nn.RMSNorm / mx.fast.rms_norm (draft.py:167-171,

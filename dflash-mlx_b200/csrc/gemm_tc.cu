@@ -54,6 +54,19 @@ int* device_error_word() {
   return ptrs[dev];
 }
 
+#ifdef DFL_TC_TRACE
+// phase timestamps per CTA (debug builds only)
+static __device__ unsigned long long g_tc_trace[8192][16];
+__device__ __forceinline__ unsigned long long gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+#define TC_STAMP(k) g_tc_trace[blockIdx.x][k] = gtimer()
+#else
+#define TC_STAMP(k)
+#endif
+
 constexpr int TC_NT = 128;  // W rows per tile (MMA M)
 constexpr int TC_BK = 64;   // k per stage (one 128-byte swizzle row)
 constexpr int TC_BM = 16;   // tokens per tile (MMA N)
@@ -156,14 +169,22 @@ __device__ __forceinline__ void tc_epilogue(const TcArgs& a, float* v, int mt, i
   const int m0 = mt * TC_BM;
   if constexpr (EPI == DFL_EPI_STORE || EPI == DFL_EPI_RESIDUAL) {
     const bool col_ok = n < a.N;
+    if constexpr (EPI == DFL_EPI_RESIDUAL) {
+      // gather all 16 residual values before the first store: y may alias the residual
+      // (in-place update), so interleaved loads and stores would serialise 16 L2 round trips
+      float r[TC_BM];
+#pragma unroll
+      for (int t = 0; t < TC_BM; ++t)
+        r[t] = (col_ok && m0 + t < a.M) ? bf2f(a.res[(long long)(m0 + t) * a.ldr + n]) : 0.f;
+#pragma unroll
+      for (int t = 0; t < TC_BM; ++t) v[t] = r[t] + round_bf16(v[t]);
+    }
 #pragma unroll
     for (int t = 0; t < TC_BM; ++t) {
       const int m = m0 + t;
       float ss = 0.f;
       if (col_ok && m < a.M) {
-        float val = v[t];
-        if constexpr (EPI == DFL_EPI_RESIDUAL) val = bf2f(a.res[(long long)m * a.ldr + n]) + round_bf16(val);
-        const __nv_bfloat16 o = f2bf(val);
+        const __nv_bfloat16 o = f2bf(v[t]);
         a.y[(long long)m * a.ldy + n] = o;
         if (a.y2) a.y2[(long long)m * a.ldy2 + n] = o;
         const float qv = bf2f(o);
@@ -217,7 +238,7 @@ __device__ __forceinline__ void tc_epilogue(const TcArgs& a, float* v, int mt, i
 }
 
 template <int EPI>
-__global__ void __launch_bounds__(TC_THREADS, 1)
+__global__ void __launch_bounds__(TC_THREADS, 2)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap xmap, TcArgs a) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
@@ -240,6 +261,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const long long u1 = (long long)(c + 1) * a.U1 / a.grid1;
   const int n_units = (int)(u1 - u0);
   const bool norm = a.norm_w != nullptr;
+  if (threadIdx.x == 0) TC_STAMP(0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < TC_STAGES; ++s) {
@@ -263,6 +285,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   grid_dependency_launch_dependents();
+  if (threadIdx.x == 0) TC_STAMP(1);
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -276,6 +299,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         bulk_load(smem + i * TC_W_BYTES, a.wt + u * TC_W_BYTES, TC_W_BYTES, &full[i], pol_w);
       }
       grid_dependency_wait();  // X is produced by the previous kernel
+      TC_STAMP(2);
       for (int i = 0; i < pre; ++i)
         tma_load_2d(&xmap, &full[i], smem + TC_OFF_X + i * TC_X_BYTES, (int)((u0 + i) % a.kb) * TC_BK, mt * TC_BM,
                     pol_x);
@@ -295,6 +319,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           mbar_wait(&full[i % TC_STAGES], (i / TC_STAGES) & 1, 209, a.err);
       }
     }
+    __syncwarp();  // lanes 1-31 wait for the producing lane before the teardown barrier
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0 && n_units > 0) {
@@ -311,6 +336,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           tc_fence_after();
         }
         if (!mbar_wait(norm ? &xready[s] : &full[s], (i / TC_STAGES) & 1, 203, a.err)) break;
+        if (i == 0) TC_STAMP(3);
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)((seg & 1) * TC_BM);
         const uint64_t ad = sw128_desc(w0 + s * TC_W_BYTES);
@@ -321,7 +347,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         tc_commit(&empty[s]);
         if (j == a.kb - 1 || i == n_units - 1) tc_commit(&accf[seg & 1]);
       }
+      TC_STAMP(4);
     }
+    __syncwarp();  // the whole warp reaches the teardown (and the .sync.aligned dealloc) together
   } else {
     // ---------------- epilogue warps (and the fused RMSNorm rescale) ----------------
     const int ew = warp - TC_EPI_WARP0;  // 0..3
@@ -367,6 +395,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const bool seg_end = (j == a.kb - 1) || (i == n_units - 1);
       if (!seg_end) continue;
       if (!mbar_wait(&accf[seg & 1], (seg >> 1) & 1, 205, a.err)) break;
+      if (et == 0) TC_STAMP(5);
       tc_fence_after();
       float v[TC_BM];
       tc_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((seg & 1) * TC_BM), v);
@@ -385,39 +414,65 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                                                  col * TC_BM);
 #pragma unroll
         for (int t4 = 0; t4 < TC_BM / 4; ++t4) mine[t4] = make_float4(v[4 * t4], v[4 * t4 + 1], v[4 * t4 + 2], v[4 * t4 + 3]);
-        __threadfence();
+        asm volatile("fence.acq_rel.gpu;\n" ::: "memory");  // publish this segment's partial
+        if (et == 0) TC_STAMP(8);
         epi_sync();
-        if (et == 0) s_flag = (atomicAdd(a.counters + tile_id, 1) == c_last - c_first);
+        if (et == 0) {
+          int prev;
+          asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;\n" : "=r"(prev) : "l"(a.counters + tile_id) : "memory");
+          s_flag = (prev == c_last - c_first);
+          TC_STAMP(9);
+        }
         epi_sync();
         do_epi = s_flag != 0;
         if (do_epi) {
-          __threadfence();
+          asm volatile("fence.acq_rel.gpu;\n" ::: "memory");  // see every segment's partial
 #pragma unroll
           for (int t = 0; t < TC_BM; ++t) v[t] = 0.f;
-          for (int cs = c_first; cs <= c_last; ++cs) {
-            const long long cs_u0 = (long long)cs * a.U1 / a.grid1;
-            const int sl = (nt == (int)(cs_u0 / a.kb)) ? 0 : 1;
-            const float4* src = reinterpret_cast<const float4*>(
-                a.partial + (((long long)mt * a.grid1 + cs) * 2 + sl) * TC_PART_FLOATS + col * TC_BM);
+          // four segments' partials in flight per round, summed in segment order
+          for (int cs0 = c_first; cs0 <= c_last; cs0 += 4) {
+            float4 pb[4][TC_BM / 4];
 #pragma unroll
-            for (int t4 = 0; t4 < TC_BM / 4; ++t4) {
-              const float4 f = __ldcg(src + t4);
-              v[4 * t4] += f.x;
-              v[4 * t4 + 1] += f.y;
-              v[4 * t4 + 2] += f.z;
-              v[4 * t4 + 3] += f.w;
+            for (int k = 0; k < 4; ++k) {
+              const int cs = cs0 + k;
+              if (cs <= c_last) {
+                const long long cs_u0 = (long long)cs * a.U1 / a.grid1;
+                const int sl = (nt == (int)(cs_u0 / a.kb)) ? 0 : 1;
+                const float4* src = reinterpret_cast<const float4*>(
+                    a.partial + (((long long)mt * a.grid1 + cs) * 2 + sl) * TC_PART_FLOATS + col * TC_BM);
+#pragma unroll
+                for (int t4 = 0; t4 < TC_BM / 4; ++t4) pb[k][t4] = __ldcg(src + t4);
+              }
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              if (cs0 + k <= c_last) {
+#pragma unroll
+                for (int t4 = 0; t4 < TC_BM / 4; ++t4) {
+                  v[4 * t4] += pb[k][t4].x;
+                  v[4 * t4 + 1] += pb[k][t4].y;
+                  v[4 * t4 + 2] += pb[k][t4].z;
+                  v[4 * t4 + 3] += pb[k][t4].w;
+                }
+              }
             }
           }
-          if (et == 0) a.counters[tile_id] = 0;  // ready for the next launch / graph replay
+          if (et == 0) {
+            a.counters[tile_id] = 0;  // ready for the next launch / graph replay
+            TC_STAMP(10);
+          }
         }
         epi_sync();  // s_flag is rewritten by the next segment
       }
       if (do_epi) tc_epilogue<EPI>(a, v, mt, nt, q, lane, xchg);
+      if (do_epi && et == 0) TC_STAMP(11);
       (void)ew;
     }
+    if (et == 0) TC_STAMP(6);
   }
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) TC_STAMP(7);
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "n"(TC_TMEM_COLS));
@@ -748,3 +803,9 @@ extern "C" int dfl_gemm_bf16_noalloc(const void* x, int64_t ldx, const void* w_p
   return dfl_gemm_bf16(x, ldx, w_packed, M, N, K, epilogue, residual, ldr, y, ldy, y2, ldy2, argmax_partials, norm_w,
                        sumsq_in, n_parts, eps, sumsq_out, scratch, NA_SCRATCH_BYTES, stream);
 }
+
+#ifdef DFL_TC_TRACE
+extern "C" int dfl_debug_tc_trace(void* host, int n_ctas) {
+  return cudaMemcpyFromSymbol(host, g_tc_trace, (size_t)n_ctas * 16 * sizeof(unsigned long long)) == cudaSuccess ? 0 : 3;
+}
+#endif

@@ -81,7 +81,7 @@ constexpr int TC_W_BYTES = TC_NT * TC_BK * 2;  // 16 KB
 constexpr int TC_X_BYTES = TC_BM * TC_BK * 2;  // 2 KB
 constexpr int TC_OFF_X = TC_STAGES * TC_W_BYTES;
 constexpr int TC_OFF_XCHG = TC_OFF_X + TC_STAGES * TC_X_BYTES;
-constexpr int TC_OFF_BAR = TC_OFF_XCHG + 2 * TC_BM * 32 * 4;
+constexpr int TC_OFF_BAR = TC_OFF_XCHG + TC_NT * TC_BM * 4;  // exchange / cluster-reduction tile (8 KB)
 constexpr int TC_NBAR = 3 * TC_STAGES + 4;
 constexpr int TC_OFF_TMEM = TC_OFF_BAR + TC_NBAR * 8;
 constexpr int TC_OFF_NORM = (TC_OFF_TMEM + 16 + 127) & ~127;
@@ -479,6 +479,218 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Cluster split-K variant for GEMMs with few 128-row tiles (N / 128 < 148):
+// a thread-block cluster of S CTAs (S <= 8) owns one tile, CTA rank r streams the
+// fixed k-range [r*kb/S, (r+1)*kb/S), and the S partial tiles are reduced through
+// distributed shared memory after a hardware cluster barrier, in rank order (no
+// global scratch, no atomics, no memory fences on the critical path). Each
+// 32-column group of the tile is finished by one rank.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_map(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];\n" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+  return v;
+}
+// sum over the cluster's ranks (in rank order) of column `col` (16 rows) of the red tiles
+__device__ __forceinline__ void cluster_reduce_col(uint32_t red_saddr, int col, int S, float* v) {
+#pragma unroll
+  for (int t = 0; t < TC_BM; ++t) v[t] = 0.f;
+  for (int rr = 0; rr < S; ++rr) {
+    const uint32_t base = cluster_map(red_saddr + (uint32_t)(col * TC_BM * 4), (uint32_t)rr);
+#pragma unroll
+    for (int t4 = 0; t4 < TC_BM / 4; ++t4) {
+      const float4 f = ld_cluster_f4(base + t4 * 16);
+      v[4 * t4] += f.x;
+      v[4 * t4 + 1] += f.y;
+      v[4 * t4 + 2] += f.z;
+      v[4 * t4 + 3] += f.w;
+    }
+  }
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(TC_THREADS, 2)
+    gemm_csk_kernel(const __grid_constant__ CUtensorMap xmap, TcArgs a, int S) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + TC_OFF_BAR);
+  uint64_t* empty = full + TC_STAGES;
+  uint64_t* xready = empty + TC_STAGES;
+  uint64_t* accf = xready + TC_STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + TC_OFF_TMEM);
+  float* red = reinterpret_cast<float*>(smem + TC_OFF_XCHG);  // [128 cols][16 rows] fp32
+  __nv_bfloat16* s_nw = reinterpret_cast<__nv_bfloat16*>(smem + TC_OFF_NORM);
+  __shared__ float s_inv[TC_BM];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x;  // rank in the cluster (cluster dims = (S, 1, 1), gridDim.x == S)
+  const int nt = blockIdx.y, mt = blockIdx.z;
+  const int j0 = r * a.kb / S, j1 = (r + 1) * a.kb / S;
+  const int n_units = j1 - j0;
+  const bool norm = a.norm_w != nullptr;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < TC_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      mbar_init(&xready[s], 128);
+    }
+    mbar_init(&accf[0], 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
+                 "n"(TC_TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  grid_dependency_launch_dependents();
+
+  if (warp == 0) {
+    if (lane == 0 && n_units > 0) {
+      const uint64_t pol_w = l2_policy_evict_first();
+      const uint64_t pol_x = l2_policy_evict_last();
+      const long long ubase = (long long)nt * a.kb + j0;
+      const int pre = n_units < TC_STAGES ? n_units : TC_STAGES;
+      for (int i = 0; i < pre; ++i) {
+        mbar_expect_tx(&full[i], TC_W_BYTES + TC_X_BYTES);
+        bulk_load(smem + i * TC_W_BYTES, a.wt + (ubase + i) * TC_W_BYTES, TC_W_BYTES, &full[i], pol_w);
+      }
+      grid_dependency_wait();  // X is produced by the previous kernel
+      for (int i = 0; i < pre; ++i)
+        tma_load_2d(&xmap, &full[i], smem + TC_OFF_X + i * TC_X_BYTES, (j0 + i) * TC_BK, mt * TC_BM, pol_x);
+      int issued = pre;
+      for (int i = pre; i < n_units; ++i) {
+        const int s = i % TC_STAGES;
+        if (!mbar_wait(&empty[s], ((i / TC_STAGES) & 1) ^ 1, 301, a.err)) break;
+        mbar_expect_tx(&full[s], TC_W_BYTES + TC_X_BYTES);
+        bulk_load(smem + s * TC_W_BYTES, a.wt + (ubase + i) * TC_W_BYTES, TC_W_BYTES, &full[s], pol_w);
+        tma_load_2d(&xmap, &full[s], smem + TC_OFF_X + s * TC_X_BYTES, (j0 + i) * TC_BK, mt * TC_BM, pol_x);
+        issued = i + 1;
+      }
+      if (issued < n_units)
+        for (int i = issued > TC_STAGES ? issued - TC_STAGES : 0; i < issued; ++i)
+          mbar_wait(&full[i % TC_STAGES], (i / TC_STAGES) & 1, 309, a.err);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0 && n_units > 0) {
+      const uint32_t w0 = smem_u32(smem), x0 = smem_u32(smem + TC_OFF_X);
+      for (int i = 0; i < n_units; ++i) {
+        const int s = i % TC_STAGES;
+        if (!mbar_wait(norm ? &xready[s] : &full[s], (i / TC_STAGES) & 1, 303, a.err)) break;
+        tc_fence_after();
+        const uint64_t ad = sw128_desc(w0 + s * TC_W_BYTES);
+        const uint64_t bd = sw128_desc(x0 + s * TC_X_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < TC_BK / 16; ++kk)
+          tc_mma(tmem, ad + 2 * kk, bd + 2 * kk, TC_IDESC, (i == 0 && kk == 0) ? 0u : 1u);
+        tc_commit(&empty[s]);
+      }
+      tc_commit(&accf[0]);
+    }
+    __syncwarp();
+  } else {
+    const int et = threadIdx.x - 32 * TC_EPI_WARP0;
+    const int q = warp & 3;
+    if (norm)
+      for (int k = et * 8; k < a.K; k += 128 * 8)
+        *reinterpret_cast<uint4*>(s_nw + k) = *reinterpret_cast<const uint4*>(a.norm_w + k);
+    grid_dependency_wait();
+    if (norm) {
+      if (et < TC_BM) {
+        const int m = mt * TC_BM + et;
+        float ss = 0.f;
+        if (m < a.M)
+          for (int p = 0; p < a.n_parts; ++p) ss += a.sumsq_in[(long long)m * a.n_parts + p];
+        s_inv[et] = rsqrtf(ss / (float)a.K + a.eps);
+      }
+      epi_sync();
+      for (int i = 0; i < n_units; ++i) {
+        const int s = i % TC_STAGES;
+        if (!mbar_wait(&full[s], (i / TC_STAGES) & 1, 304, a.err)) break;
+        const int j = j0 + i;
+        const int row = et >> 3, cc = et & 7;
+        __nv_bfloat16* p =
+            reinterpret_cast<__nv_bfloat16*>(smem + TC_OFF_X + s * TC_X_BYTES) + row * 64 + ((cc ^ (row & 7)) << 3);
+        uint4 xv = *reinterpret_cast<uint4*>(p);
+        const uint4 wv = *reinterpret_cast<const uint4*>(s_nw + j * TC_BK + cc * 8);
+        __nv_bfloat16* xe = reinterpret_cast<__nv_bfloat16*>(&xv);
+        const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv);
+        const float inv = s_inv[row];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) xe[e] = f2bf(bf2f(we[e]) * (bf2f(xe[e]) * inv));
+        *reinterpret_cast<uint4*>(p) = xv;
+        fence_proxy_async_smem();
+        mbar_arrive(&xready[s]);
+      }
+    }
+    float v[TC_BM];
+#pragma unroll
+    for (int t = 0; t < TC_BM; ++t) v[t] = 0.f;
+    if (n_units > 0 && mbar_wait(&accf[0], 0, 305, a.err)) {
+      tc_fence_after();
+      tc_ld16(tmem + ((uint32_t)(q * 32) << 16), v);
+      tc_fence_before();
+    }
+    float4* mine = reinterpret_cast<float4*>(red + (q * 32 + lane) * TC_BM);
+#pragma unroll
+    for (int t4 = 0; t4 < TC_BM / 4; ++t4) mine[t4] = make_float4(v[4 * t4], v[4 * t4 + 1], v[4 * t4 + 2], v[4 * t4 + 3]);
+  }
+  cluster_sync_all();  // every rank's partial tile is in its shared memory
+  if (warp >= TC_EPI_WARP0) {
+    const int q = warp & 3;  // 32-column group of the tile handled by this warp
+    const uint32_t red_s = smem_u32(smem + TC_OFF_XCHG);
+    if constexpr (EPI == DFL_EPI_SILU_MUL) {
+      // gate groups 0 / 2 pair with up groups 1 / 3 (weights packed per 64 rows)
+      if (!(q & 1) && ((q >> 1) % S) == r) {
+        float gv[TC_BM], uv[TC_BM];
+        cluster_reduce_col(red_s, q * 32 + lane, S, gv);
+        cluster_reduce_col(red_s, (q + 1) * 32 + lane, S, uv);
+        const int on = nt * 64 + (q >> 1) * 32 + lane;
+        if (nt * TC_NT + q * 32 + lane < a.N) {
+#pragma unroll
+          for (int t = 0; t < TC_BM; ++t) {
+            const int m = mt * TC_BM + t;
+            if (m < a.M) {
+              const float gt = round_bf16(gv[t]);
+              const float up = round_bf16(uv[t]);
+              const float act = round_bf16(gt / (1.f + __expf(-gt)));
+              a.y[(long long)m * a.ldy + on] = f2bf(act * up);
+            }
+          }
+        }
+      }
+    } else {
+      if ((q % S) == r) {
+        float v[TC_BM];
+        cluster_reduce_col(red_s, q * 32 + lane, S, v);
+        tc_epilogue<EPI>(a, v, mt, nt, q, lane, nullptr);
+      }
+    }
+  }
+  cluster_sync_all();  // no rank leaves while another still reads its shared memory
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "n"(TC_TMEM_COLS));
+  }
+}
+
 // Row-major W [N, K] -> tiled image: unit (tile t, k-block j) at ((t*kb)+j)*16 KB, row r
 // (W row t*128+r, zero past N) holding 16-byte chunk c of k-block j at r*128 + ((c^(r&7))*16).
 __global__ void pack_weight_kernel(const __nv_bfloat16* __restrict__ w, int N, int K,
@@ -561,6 +773,7 @@ const CUtensorMap* tensor_map_2d_bf16(const void* base, uint64_t rows, uint64_t 
 struct TcPlan {
   int n_tiles, m_tiles, kb, grid1;
   long long U1;
+  int S;  // > 0: cluster split-K with S ranks per tile; 0: persistent kernel
 };
 
 static TcPlan tc_plan(int M, int N, int K) {
@@ -570,6 +783,13 @@ static TcPlan tc_plan(int M, int N, int K) {
   p.kb = K / TC_BK;
   p.U1 = (long long)p.n_tiles * p.kb;
   p.grid1 = (int)(p.U1 < TC_GRID ? p.U1 : TC_GRID);
+  p.S = 0;
+  if (p.n_tiles < TC_GRID) {  // few tiles: one cluster of S ranks per tile, about one CTA per SM
+    int S = (TC_GRID + p.n_tiles / 2) / p.n_tiles;
+    if (S > 8) S = 8;
+    if (S > p.kb) S = p.kb;
+    p.S = S < 1 ? 1 : S;
+  }
   return p;
 }
 
@@ -685,15 +905,19 @@ extern "C" int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w_packed, i
   a.grid1 = p.grid1;
 
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.grid1 * p.m_tiles);
+  cfg.gridDim = p.S ? dim3(p.S, p.n_tiles, p.m_tiles) : dim3(p.grid1 * p.m_tiles);
   cfg.blockDim = dim3(TC_THREADS);
   cfg.dynamicSmemBytes = TC_SMEM_BASE + (norm_w ? (size_t)K * 2 : 0);
   cfg.stream = as_stream(stream);
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = p.S ? p.S : 1;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = p.S ? 2 : 1;
   cudaError_t err;
   switch (epilogue) {
 #define DFL_LAUNCH(E)                                                                                       \
@@ -702,9 +926,12 @@ extern "C" int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w_packed, i
     if (!init) {                                                                                            \
       cudaFuncSetAttribute(gemm_tc_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize,                  \
                            TC_SMEM_BASE + TC_NORM_MAX_K * 2);                                               \
+      cudaFuncSetAttribute(gemm_csk_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize,                 \
+                           TC_SMEM_BASE + TC_NORM_MAX_K * 2);                                               \
       init = true;                                                                                          \
     }                                                                                                       \
-    err = cudaLaunchKernelEx(&cfg, gemm_tc_kernel<E>, *xm, a);                                              \
+    err = p.S ? cudaLaunchKernelEx(&cfg, gemm_csk_kernel<E>, *xm, a, p.S)                                   \
+              : cudaLaunchKernelEx(&cfg, gemm_tc_kernel<E>, *xm, a);                                        \
     break;                                                                                                  \
   }
     DFL_LAUNCH(DFL_EPI_STORE)

@@ -23,9 +23,9 @@
 //    (tcgen05.commit releases each shared-memory stage back to the producer),
 //    warps 2-5 = epilogue (tcgen05.ld 32x32b: each thread owns one output column
 //    for the 16 rows) and, when the RMSNorm is fused, the per-stage rescale of X.
-//  * Persistent: one CTA per SM per 16-row tile of X (grid 148); every CTA gets
+//  * Persistent: two CTAs per SM per 16-row tile of X (grid 296); every CTA gets
 //    an equal contiguous range of (128-row, 64-k) work units, so the SMs stream
-//    equal shares of W and there is no tail wave. ~100 KB of shared memory lets
+//    equal shares of W and there is no tail wave. ~70 KB of shared memory per CTA lets
 //    the next GEMM's CTA co-reside and stream its first weight stages before
 //    griddepcontrol.wait (programmatic dependent launch).
 //  * A tile cut by range boundaries is reduced by the last-arriving CTA in fixed
@@ -71,10 +71,16 @@ constexpr int TC_NT = 128;  // W rows per tile (MMA M)
 constexpr int TC_BK = 64;   // k per stage (one 128-byte swizzle row)
 constexpr int TC_BM = 16;   // tokens per tile (MMA N)
 #ifndef DFL_TC_STAGES
-#define DFL_TC_STAGES 5
+#define DFL_TC_STAGES 3
 #endif
 constexpr int TC_STAGES = DFL_TC_STAGES;
-constexpr int TC_GRID = 148;  // work split over the B200's SM count (fixed: part of the reduction order)
+#ifndef DFL_TC_GRID
+#define DFL_TC_GRID 296
+#endif
+// Work split: two streaming CTAs per SM (148 SMs) plus room for the next kernel's
+// prologue; one CTA alone cannot keep enough bulk copies in flight. Fixed: part of
+// the reduction order.
+constexpr int TC_GRID = DFL_TC_GRID;
 constexpr int TC_THREADS = 192;
 constexpr int TC_EPI_WARP0 = 2;
 constexpr int TC_W_BYTES = TC_NT * TC_BK * 2;  // 16 KB
@@ -87,7 +93,25 @@ constexpr int TC_OFF_TMEM = TC_OFF_BAR + TC_NBAR * 8;
 constexpr int TC_OFF_NORM = (TC_OFF_TMEM + 16 + 127) & ~127;
 constexpr int TC_SMEM_BASE = TC_OFF_NORM + 1024;  // + 1024-byte alignment slack
 constexpr int TC_NORM_MAX_K = 8192;
-constexpr int TC_TMEM_COLS = 32;
+// Independent TMEM accumulators per tile: the four K=16 MMAs of a stage go to
+// different accumulators so that consecutive MMAs do not wait on each other; the
+// epilogue sums them in a fixed order.
+#ifndef DFL_TC_NACC
+#define DFL_TC_NACC 4
+#endif
+constexpr int TC_NACC = DFL_TC_NACC;
+#ifndef DFL_TC_PLANES
+#define DFL_TC_PLANES 1
+#endif
+constexpr int TC_PLANES = DFL_TC_PLANES;
+#ifndef DFL_TC_MINB
+#define DFL_TC_MINB 3
+#endif
+constexpr int TC_PB = 2;  // partial tiles loaded per round by a split-tile reducer
+#ifndef DFL_TC_SMAX
+#define DFL_TC_SMAX 8
+#endif
+constexpr int TC_TMEM_COLS = 2 * TC_NACC * TC_BM <= 32 ? 32 : (2 * TC_NACC * TC_BM <= 64 ? 64 : 128);
 constexpr int TC_MAX_COUNTERS = 1 << 17;
 constexpr size_t TC_COUNTER_BYTES = (size_t)TC_MAX_COUNTERS * sizeof(int);
 constexpr int TC_PART_FLOATS = TC_BM * TC_NT;  // one partial tile
@@ -151,6 +175,18 @@ __device__ __forceinline__ void tc_ld16(uint32_t taddr, float* v) {
   asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Sum of the TC_NACC accumulators of one buffer, in a fixed order.
+__device__ __forceinline__ void tc_ld_acc(uint32_t taddr, float* v) {
+  tc_ld16(taddr, v);
+#pragma unroll
+  for (int k = 1; k < TC_NACC; ++k) {
+    float w[16];
+    tc_ld16(taddr + (uint32_t)(k * TC_BM), w);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] += w[i];
+  }
 }
 
 __device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;\n" ::: "memory"); }
@@ -238,7 +274,7 @@ __device__ __forceinline__ void tc_epilogue(const TcArgs& a, float* v, int mt, i
 }
 
 template <int EPI>
-__global__ void __launch_bounds__(TC_THREADS, 2)
+__global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap xmap, TcArgs a) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
@@ -289,31 +325,39 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
-    if (lane == 0 && n_units > 0) {
+    // TC_PLANES lanes each copy one slice of every weight stage (parallel bulk copies)
+    constexpr unsigned PMASK = (1u << TC_PLANES) - 1u;
+    constexpr uint32_t SLICE = TC_W_BYTES / TC_PLANES;
+    if (lane < TC_PLANES && n_units > 0) {
       const uint64_t pol_w = l2_policy_evict_first();
       const uint64_t pol_x = l2_policy_evict_last();
       const int pre = n_units < TC_STAGES ? n_units : TC_STAGES;
       for (int i = 0; i < pre; ++i) {
         const long long u = u0 + i;
-        mbar_expect_tx(&full[i], TC_W_BYTES + TC_X_BYTES);
-        bulk_load(smem + i * TC_W_BYTES, a.wt + u * TC_W_BYTES, TC_W_BYTES, &full[i], pol_w);
+        if (lane == 0) mbar_expect_tx(&full[i], TC_W_BYTES + TC_X_BYTES);
+        __syncwarp(PMASK);
+        bulk_load(smem + i * TC_W_BYTES + lane * SLICE, a.wt + u * TC_W_BYTES + lane * SLICE, SLICE, &full[i], pol_w);
       }
       grid_dependency_wait();  // X is produced by the previous kernel
-      TC_STAMP(2);
-      for (int i = 0; i < pre; ++i)
-        tma_load_2d(&xmap, &full[i], smem + TC_OFF_X + i * TC_X_BYTES, (int)((u0 + i) % a.kb) * TC_BK, mt * TC_BM,
-                    pol_x);
+      if (lane == 0) {
+        TC_STAMP(2);
+        for (int i = 0; i < pre; ++i)
+          tma_load_2d(&xmap, &full[i], smem + TC_OFF_X + i * TC_X_BYTES, (int)((u0 + i) % a.kb) * TC_BK, mt * TC_BM,
+                      pol_x);
+      }
       int issued = pre;
       for (int i = pre; i < n_units; ++i) {
         const int s = i % TC_STAGES;
         if (!mbar_wait(&empty[s], ((i / TC_STAGES) & 1) ^ 1, 201, a.err)) break;
         const long long u = u0 + i;
-        mbar_expect_tx(&full[s], TC_W_BYTES + TC_X_BYTES);
-        bulk_load(smem + s * TC_W_BYTES, a.wt + u * TC_W_BYTES, TC_W_BYTES, &full[s], pol_w);
-        tma_load_2d(&xmap, &full[s], smem + TC_OFF_X + s * TC_X_BYTES, (int)(u % a.kb) * TC_BK, mt * TC_BM, pol_x);
+        if (lane == 0) mbar_expect_tx(&full[s], TC_W_BYTES + TC_X_BYTES);
+        __syncwarp(PMASK);
+        bulk_load(smem + s * TC_W_BYTES + lane * SLICE, a.wt + u * TC_W_BYTES + lane * SLICE, SLICE, &full[s], pol_w);
+        if (lane == 0)
+          tma_load_2d(&xmap, &full[s], smem + TC_OFF_X + s * TC_X_BYTES, (int)(u % a.kb) * TC_BK, mt * TC_BM, pol_x);
         issued = i + 1;
       }
-      if (issued < n_units) {
+      if (issued < n_units && lane == 0) {
         // gave up: let the copies already in flight land before the CTA exits
         for (int i = issued > TC_STAGES ? issued - TC_STAGES : 0; i < issued; ++i)
           mbar_wait(&full[i % TC_STAGES], (i / TC_STAGES) & 1, 209, a.err);
@@ -338,12 +382,13 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
         if (!mbar_wait(norm ? &xready[s] : &full[s], (i / TC_STAGES) & 1, 203, a.err)) break;
         if (i == 0) TC_STAMP(3);
         tc_fence_after();
-        const uint32_t d = tmem + (uint32_t)((seg & 1) * TC_BM);
+        const uint32_t d = tmem + (uint32_t)((seg & 1) * TC_NACC * TC_BM);
         const uint64_t ad = sw128_desc(w0 + s * TC_W_BYTES);
         const uint64_t bd = sw128_desc(x0 + s * TC_X_BYTES);
 #pragma unroll
         for (int kk = 0; kk < TC_BK / 16; ++kk)  // +32 bytes along K per MMA: +2 in the start-address field
-          tc_mma(d, ad + 2 * kk, bd + 2 * kk, TC_IDESC, (first && kk == 0) ? 0u : 1u);
+          tc_mma(d + (uint32_t)((kk % TC_NACC) * TC_BM), ad + 2 * kk, bd + 2 * kk, TC_IDESC,
+                 (first && kk < TC_NACC) ? 0u : 1u);
         tc_commit(&empty[s]);
         if (j == a.kb - 1 || i == n_units - 1) tc_commit(&accf[seg & 1]);
       }
@@ -398,7 +443,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
       if (et == 0) TC_STAMP(5);
       tc_fence_after();
       float v[TC_BM];
-      tc_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((seg & 1) * TC_BM), v);
+      tc_ld_acc(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((seg & 1) * TC_NACC * TC_BM), v);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acce[seg & 1]);
@@ -429,11 +474,11 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
           asm volatile("fence.acq_rel.gpu;\n" ::: "memory");  // see every segment's partial
 #pragma unroll
           for (int t = 0; t < TC_BM; ++t) v[t] = 0.f;
-          // four segments' partials in flight per round, summed in segment order
-          for (int cs0 = c_first; cs0 <= c_last; cs0 += 4) {
-            float4 pb[4][TC_BM / 4];
+          // TC_PB segments' partials in flight per round, summed in segment order
+          for (int cs0 = c_first; cs0 <= c_last; cs0 += TC_PB) {
+            float4 pb[TC_PB][TC_BM / 4];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
+            for (int k = 0; k < TC_PB; ++k) {
               const int cs = cs0 + k;
               if (cs <= c_last) {
                 const long long cs_u0 = (long long)cs * a.U1 / a.grid1;
@@ -445,7 +490,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
               }
             }
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
+            for (int k = 0; k < TC_PB; ++k) {
               if (cs0 + k <= c_last) {
 #pragma unroll
                 for (int t4 = 0; t4 < TC_BM / 4; ++t4) {
@@ -518,7 +563,7 @@ __device__ __forceinline__ void cluster_reduce_col(uint32_t red_saddr, int col, 
 }
 
 template <int EPI>
-__global__ void __launch_bounds__(TC_THREADS, 2)
+__global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
     gemm_csk_kernel(const __grid_constant__ CUtensorMap xmap, TcArgs a, int S) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
@@ -597,7 +642,8 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
         const uint64_t bd = sw128_desc(x0 + s * TC_X_BYTES);
 #pragma unroll
         for (int kk = 0; kk < TC_BK / 16; ++kk)
-          tc_mma(tmem, ad + 2 * kk, bd + 2 * kk, TC_IDESC, (i == 0 && kk == 0) ? 0u : 1u);
+          tc_mma(tmem + (uint32_t)((kk % TC_NACC) * TC_BM), ad + 2 * kk, bd + 2 * kk, TC_IDESC,
+                 (i == 0 && kk < TC_NACC) ? 0u : 1u);
         tc_commit(&empty[s]);
       }
       tc_commit(&accf[0]);
@@ -643,7 +689,7 @@ __global__ void __launch_bounds__(TC_THREADS, 2)
     for (int t = 0; t < TC_BM; ++t) v[t] = 0.f;
     if (n_units > 0 && mbar_wait(&accf[0], 0, 305, a.err)) {
       tc_fence_after();
-      tc_ld16(tmem + ((uint32_t)(q * 32) << 16), v);
+      tc_ld_acc(tmem + ((uint32_t)(q * 32) << 16), v);
       tc_fence_before();
     }
     float4* mine = reinterpret_cast<float4*>(red + (q * 32 + lane) * TC_BM);
@@ -786,7 +832,7 @@ static TcPlan tc_plan(int M, int N, int K) {
   p.S = 0;
   if (p.n_tiles < TC_GRID) {  // few tiles: one cluster of S ranks per tile, about one CTA per SM
     int S = (TC_GRID + p.n_tiles / 2) / p.n_tiles;
-    if (S > 8) S = 8;
+    if (S > DFL_TC_SMAX) S = DFL_TC_SMAX;
     if (S > p.kb) S = p.kb;
     p.S = S < 1 ? 1 : S;
   }
@@ -911,7 +957,11 @@ extern "C" int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w_packed, i
   cfg.stream = as_stream(stream);
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+#ifdef DFL_NO_PDL
+  attr[0].val.programmaticStreamSerializationAllowed = 0;
+#else
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+#endif
   attr[1].id = cudaLaunchAttributeClusterDimension;
   attr[1].val.clusterDim.x = p.S ? p.S : 1;
   attr[1].val.clusterDim.y = 1;
@@ -928,6 +978,7 @@ extern "C" int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w_packed, i
                            TC_SMEM_BASE + TC_NORM_MAX_K * 2);                                               \
       cudaFuncSetAttribute(gemm_csk_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize,                 \
                            TC_SMEM_BASE + TC_NORM_MAX_K * 2);                                               \
+      if (DFL_TC_SMAX > 8) cudaFuncSetAttribute(gemm_csk_kernel<E>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1); \
       init = true;                                                                                          \
     }                                                                                                       \
     err = p.S ? cudaLaunchKernelEx(&cfg, gemm_csk_kernel<E>, *xm, a, p.S)                                   \
@@ -978,7 +1029,7 @@ extern "C" int dfl_device_error(int* code, int clear, void* stream) {
 // partial tiles) comes from a fixed array compiled into this library instead of a
 // caller-provided workspace. The array is sized for one 16-row tile of X (the
 // decode shape: M <= 16); larger M is rejected. Every GPU that loads the library
-// holds it (about 2.9 MB) until the process exits.
+// holds it (about 5.4 MB) until the process exits.
 // ---------------------------------------------------------------------------
 constexpr size_t NA_SCRATCH_BYTES = TC_COUNTER_BYTES + (size_t)TC_GRID * 2 * TC_PART_FLOATS * sizeof(float);
 static __device__ __align__(256) unsigned char g_noalloc_scratch[NA_SCRATCH_BYTES];

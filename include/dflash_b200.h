@@ -99,7 +99,7 @@ int dfl_device_error(int* code, int clear, void* stream);
  * device memory (host callbacks, plugins whose host owns every allocation,
  * engines that forbid cudaMalloc after start-up). No counterpart in the
  * reference. The split-K scratch is a fixed array inside this library
- * (dfl_gemm_noalloc_scratch_bytes(), about 2.9 MB held by every GPU that loads
+ * (dfl_gemm_noalloc_scratch_bytes(), about 5.4 MB held by every GPU that loads
  * the library until exit), sized for M <= 16 rows; larger M returns
  * DFL_ERR_UNSUPPORTED. No cudaMalloc / cudaFree is called. The first call on a
  * device looks up the array's device address (cudaGetSymbolAddress) with that

@@ -401,7 +401,7 @@ def main():
                 traffic = json.load(open(tp)).get("dram_bytes_per_launch_full")
             except Exception:
                 traffic = None
-        roof = {"bound": "hbm", "kernel": "gemm_stream_kernel (verify weight streaming, M=16)",
+        roof = {"bound": "hbm", "kernel": "gemm_csk_kernel + gemm_tc_kernel (verify weight streaming, M=16; per-launch average over the 145-launch verify pass)",
                 "achieved": round(r["achieved_gbs"], 1), "peak": hbm_peak, "unit": "GB/s",
                 "frac": round(r["achieved_gbs"] / hbm_peak, 4), "traffic": traffic,
                 "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else peak_kind,

@@ -34,6 +34,9 @@ struct AttnArgs {
   float2* part_ml; // [chunks][M][Hq]
   __nv_bfloat16* out;
   long long ldo;
+  const __nv_bfloat16* gate;  // nullable: out *= sigmoid(gate) (Qwen3.5 gated attention)
+  long long ldg;
+  int gate_hs;  // elements between consecutive heads' gates in a row
   int M, Hq, Hkv, G, causal, n_chunks;
   float scale_log2;  // softmax scale * log2(e)
 };
@@ -272,8 +275,18 @@ __global__ void attn_combine_kernel(AttnArgs a) {
   }
   const float inv = den > 0.f ? 1.f / den : 0.f;
   __nv_bfloat16* dst = a.out + (long long)m * a.ldo + (long long)h * HD;
+  if (a.gate) {
+    // o_proj(attn * sigmoid(gate)), custom_qwen35_model.py:193
+    const __nv_bfloat16* gr = a.gate + (long long)m * a.ldg + (long long)h * a.gate_hs;
 #pragma unroll
-  for (int i = 0; i < PER; ++i) dst[lane + 32 * i] = f2bf(acc[i] * inv);
+    for (int i = 0; i < PER; ++i) {
+      const float gt = bf2f(gr[lane + 32 * i]);
+      dst[lane + 32 * i] = f2bf(round_bf16(acc[i] * inv) * round_bf16(1.f / (1.f + __expf(-gt))));
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < PER; ++i) dst[lane + 32 * i] = f2bf(acc[i] * inv);
+  }
 }
 
 template <int HD>
@@ -326,7 +339,8 @@ extern "C" size_t dfl_attention_workspace_bytes(int M, int Hq, int hd, int max_k
 extern "C" int dfl_attention(const void* q, const void* k_cache, const void* v_cache, int64_t seq_stride,
                              int64_t head_stride, const int32_t* pos, const int32_t* row_seq, const int32_t* kv_len,
                              int M, int Hq, int Hkv, int hd, int causal, float scale, int max_kv, void* out,
-                             int64_t ldo, void* workspace, size_t workspace_bytes, void* stream) {
+                             int64_t ldo, const void* gate, int64_t ldg, int gate_head_stride, void* workspace,
+                             size_t workspace_bytes, void* stream) {
   if (M == 0) return DFL_OK;
   if (!q || !k_cache || !v_cache || !pos || !out || (!causal && !kv_len) || M < 0 || Hkv <= 0 || Hq % Hkv) {
     set_error("dfl_attention: bad arguments");
@@ -361,6 +375,9 @@ extern "C" int dfl_attention(const void* q, const void* k_cache, const void* v_c
   a.part_ml = reinterpret_cast<float2*>(static_cast<char*>(workspace) + ((o_bytes + 255) & ~(size_t)255));
   a.out = static_cast<__nv_bfloat16*>(out);
   a.ldo = ldo;
+  a.gate = static_cast<const __nv_bfloat16*>(gate);
+  a.ldg = ldg;
+  a.gate_hs = gate_head_stride > 0 ? gate_head_stride : hd;
   a.M = M;
   a.Hq = Hq;
   a.Hkv = Hkv;
@@ -372,8 +389,9 @@ extern "C" int dfl_attention(const void* q, const void* k_cache, const void* v_c
   switch (hd) {
     case 64: return launch_attn<64>(a, n_tiles, st);
     case 128: return launch_attn<128>(a, n_tiles, st);
+    case 256: return launch_attn<256>(a, n_tiles, st);
     default:
-      set_error("dfl_attention: head_dim %d not supported (64, 128)", hd);
+      set_error("dfl_attention: head_dim %d not supported (64, 128, 256)", hd);
       return DFL_ERR_UNSUPPORTED;
   }
 }

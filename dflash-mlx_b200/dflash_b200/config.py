@@ -120,7 +120,40 @@ def qwen3_4b_small_pair(num_layers: int = 4, draft_layers: int = 1) -> tuple[Tar
     return t, d
 
 
+def tiny_hybrid_pair() -> tuple[TargetConfig, DraftConfig]:
+    """Tiny Qwen3.5-style hybrid: 4 layers (GDN, GDN, GDN, gated attention), hidden 256,
+    attention 4 q / 2 kv heads of 256 with RoPE on the first 64 dims, GDN 2 key heads /
+    4 value heads of 64, FFN 768, vocab 4096; draft of 1 layer on target layers 1 and 3."""
+    t = TargetConfig(model_type="qwen3_5", hidden_size=256, num_hidden_layers=4, num_attention_heads=4,
+                     num_key_value_heads=2, head_dim=256, partial_rotary_factor=0.25, intermediate_size=768,
+                     vocab_size=4096, linear_num_key_heads=2, linear_num_value_heads=4, linear_key_head_dim=64,
+                     linear_value_head_dim=64)
+    d = DraftConfig(hidden_size=256, num_hidden_layers=1, num_attention_heads=4, num_key_value_heads=2,
+                    head_dim=64, intermediate_size=768, vocab_size=4096, block_size=8,
+                    target_layer_ids=[1, 3], mask_token_id=4095)
+    return t, d
+
+
+def qwen35_27b_pair(num_layers: int = 64) -> tuple[TargetConfig, DraftConfig]:
+    """Config 5: Qwen3.5-27B shape (64 layers, every 4th gated full attention 24 q / 4 kv
+    heads of 256 with partial RoPE 0.25; 48 GDN layers of 16 key / 48 value heads of 128;
+    hidden 5120, FFN 17408, vocab 151936); DFlash draft of 5 layers, block 16.
+    ``num_layers`` < 64 gives the same widths at reduced depth (parity tests)."""
+    t = TargetConfig(model_type="qwen3_5", hidden_size=5120, num_hidden_layers=num_layers, num_attention_heads=24,
+                     num_key_value_heads=4, head_dim=256, partial_rotary_factor=0.25, intermediate_size=17408,
+                     vocab_size=151936, linear_num_key_heads=16,
+                     linear_num_value_heads=48, linear_key_head_dim=128, linear_value_head_dim=128)
+    n_taps = 5 if num_layers >= 8 else 2
+    d = DraftConfig(hidden_size=5120, num_hidden_layers=5 if num_layers >= 8 else 1, num_attention_heads=32,
+                    num_key_value_heads=8, head_dim=128, intermediate_size=17408, vocab_size=151936,
+                    target_layer_ids=evenly_spaced_layers(num_layers, n_taps) if num_layers >= 8
+                    else [1, num_layers - 1])
+    return t, d
+
+
 PRESETS = {
     "tiny": tiny_pair,
     "qwen3-4b": qwen3_4b_pair,
+    "tiny-hybrid": tiny_hybrid_pair,
+    "qwen3.5-27b": qwen35_27b_pair,
 }

@@ -1,0 +1,237 @@
+"""GPU Qwen3.5 hybrid target: gated-delta-net (GDN) layers + gated full attention.
+
+Layer i is full attention when (i + 1) % full_attention_interval == 0, otherwise a
+GDN layer (custom_qwen35_model.py:818). Forward semantics follow the reference's
+fork: GDN layer custom_qwen35_model.py:409-484, gated full attention :487-540,
+hybrid forward with taps :883-1002.
+
+HBM layout (per device):
+  * GDN layer: ``w_in`` packed [qkv | z | b | a] rows (one weight stream, padded to a
+    multiple of 32 rows), conv weight [C, 4], ``A_log`` / ``dt_bias`` fp32, gated-norm
+    weight [Dv], ``w_out`` [H, Hv*Dv];
+  * full-attention layer: ``w_qkv`` = [q_proj (q and output gate interleaved per head) |
+    k_proj | v_proj], ``w_o``;
+  * caches (``HybridCache``): KV [L_attn, B, Hkv, cap, hd] for the attention layers;
+    per GDN layer the fp32 recurrent state [B, Hv, Dv, Dk], per-token snapshots of the
+    last verify block [B, T, Hv, Dv, Dk], the conv state [B, 3, C] and the conv window
+    [B, 3 + T, C]. Rollback after a verify = copy snapshot accepted-1 into the state and
+    window rows [accepted, accepted + 3) into the conv state (dfl_gdn_rollback), driven by
+    the accepted length the device wrote (no host sync, no replay).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+
+from . import ops
+from .config import TargetConfig
+from .model import KVCache, alloc_kv
+from .weights import pack_gate_up, rope_inv_freq
+
+
+@dataclass
+class HybridCache:
+    kv: KVCache                      # attention layers only (index = attention-layer ordinal)
+    state: list[torch.Tensor]        # per GDN layer [B, Hv, Dv, Dk] fp32
+    snaps: list[torch.Tensor]        # per GDN layer [B, T, Hv, Dv, Dk] fp32
+    conv: list[torch.Tensor]         # per GDN layer [B, 3, C] bf16
+    window: list[torch.Tensor]       # per GDN layer [B, 3 + Tw, C] bf16
+    T: int                           # verify block rows per sequence (snapshot depth)
+    Tw: int                          # window rows per sequence (max block / prefill chunk)
+
+    @property
+    def cap(self) -> int:
+        return self.kv.cap
+
+
+class HybridTargetModel:
+    """Qwen3.5-family target (GDN + gated attention) with the TargetModel interface."""
+
+    def __init__(self, cfg: TargetConfig, weights: dict, device="cuda"):
+        if cfg.model_type != "qwen3_5":
+            raise ValueError("HybridTargetModel runs the qwen3_5 family")
+        self.cfg = cfg
+        self.device = torch.device(device)
+        dev = self.device
+        P = ops.pack_weight
+        self.embed_w = weights["embed"].to(dev).contiguous()
+        self.lm_head_w = P(self.embed_w if cfg.tie_word_embeddings else weights["lm_head"].to(dev))
+        self.norm_w = weights["norm"].to(dev)
+        c = cfg
+        self.Hk, self.Hv = c.linear_num_key_heads, c.linear_num_value_heads
+        self.Dk, self.Dv = c.linear_key_head_dim, c.linear_value_head_dim
+        self.C = 2 * self.Hk * self.Dk + self.Hv * self.Dv
+        self.vd = self.Hv * self.Dv
+        n_in = self.C + self.vd + 2 * self.Hv
+        self.n_in_pad = (n_in + 31) // 32 * 32
+        self.layers = []
+        self.kinds = []
+        for i, lw in enumerate(weights["layers"]):
+            common = {
+                "in_norm": lw["input_layernorm"].to(dev),
+                "post_norm": lw["post_attention_layernorm"].to(dev),
+                "w_gu": P(pack_gate_up(lw["gate_proj"].to(dev), lw["up_proj"].to(dev))),
+                "w_down": P(lw["down_proj"].to(dev)),
+            }
+            if c.is_linear_layer(i):
+                w_in = torch.cat([lw["in_proj_qkv"].to(dev), lw["in_proj_z"].to(dev), lw["in_proj_b"].to(dev),
+                                  lw["in_proj_a"].to(dev)], 0)
+                if w_in.shape[0] < self.n_in_pad:
+                    w_in = torch.cat([w_in, w_in.new_zeros(self.n_in_pad - w_in.shape[0], w_in.shape[1])], 0)
+                common.update({
+                    "w_in": P(w_in),
+                    "conv_w": lw["conv1d"].to(dev).to(torch.bfloat16).contiguous(),
+                    "A_log": lw["A_log"].to(dev).float().contiguous(),
+                    "dt_bias": lw["dt_bias"].to(dev).float().contiguous(),
+                    "gnorm": lw["norm"].to(dev),
+                    "w_out": P(lw["out_proj"].to(dev)),
+                })
+                self.kinds.append("gdn")
+            else:
+                common.update({
+                    "w_qkv": P(torch.cat([lw["q_proj"].to(dev), lw["k_proj"].to(dev), lw["v_proj"].to(dev)], 0)),
+                    "w_o": P(lw["o_proj"].to(dev)),
+                    "q_norm": lw["q_norm"].to(dev),
+                    "k_norm": lw["k_norm"].to(dev),
+                })
+                self.kinds.append("attn")
+            self.layers.append(common)
+        self.attn_index = {}
+        self.gdn_index = {}
+        for i, k in enumerate(self.kinds):
+            (self.gdn_index if k == "gdn" else self.attn_index)[i] = len(self.gdn_index if k == "gdn"
+                                                                        else self.attn_index)
+        self.inv_freq = rope_inv_freq(cfg.rope_dim, cfg.rope_theta, dev)
+        self._bufs: dict[int, dict[str, torch.Tensor]] = {}
+
+    # ------------------------------------------------------------------
+    def make_cache(self, batch: int, cap: int, block: int = 16, window_rows: int = 128) -> HybridCache:
+        c, dev = self.cfg, self.device
+        kv = alloc_kv(max(1, len(self.attn_index)), batch, c.num_key_value_heads, cap, c.head_dim, dev)
+        n = len(self.gdn_index)
+        S = (self.Hv, self.Dv, self.Dk)
+        Tw = max(block, window_rows)
+        return HybridCache(
+            kv=kv,
+            state=[torch.zeros((batch, *S), dtype=torch.float32, device=dev) for _ in range(n)],
+            snaps=[torch.zeros((batch, block, *S), dtype=torch.float32, device=dev) for _ in range(n)],
+            conv=[torch.zeros((batch, 3, self.C), dtype=torch.bfloat16, device=dev) for _ in range(n)],
+            window=[torch.zeros((batch, 3 + Tw, self.C), dtype=torch.bfloat16, device=dev) for _ in range(n)],
+            T=block, Tw=Tw)
+
+    def buffers(self, M: int) -> dict[str, torch.Tensor]:
+        b = self._bufs.get(M)
+        if b is None:
+            c, dev = self.cfg, self.device
+            H, hd = c.hidden_size, c.head_dim
+            bf = dict(dtype=torch.bfloat16, device=dev)
+            b = {
+                "h": torch.empty((M, H), **bf),
+                "xn": torch.empty((M, H), **bf),
+                "qkv": torch.empty((M, (2 * c.num_attention_heads + 2 * c.num_key_value_heads) * hd), **bf),
+                "q": torch.empty((M, c.num_attention_heads, hd), **bf),
+                "attn": torch.empty((M, c.num_attention_heads * hd), **bf),
+                "act": torch.empty((M, c.intermediate_size), **bf),
+                "proj": torch.empty((M, self.n_in_pad), **bf),
+                "gq": torch.empty((M, self.Hk, self.Dk), **bf),
+                "gk": torch.empty((M, self.Hk, self.Dk), **bf),
+                "gv": torch.empty((M, self.Hv, self.Dv), **bf),
+                "gg": torch.empty((M, self.Hv), dtype=torch.float32, device=dev),
+                "gbeta": torch.empty((M, self.Hv), dtype=torch.float32, device=dev),
+                "go": torch.empty((M, self.vd), **bf),
+                "gon": torch.empty((M, self.vd), **bf),
+                "argmax": torch.empty((M, ops.argmax_tiles(c.vocab_size), 2), dtype=torch.float32, device=dev),
+                "ss": torch.zeros((M, H // 32), dtype=torch.float32, device=dev),
+            }
+            self._bufs[M] = b
+        return b
+
+    def _gdn_layer(self, lw, h, ss, b, cache: HybridCache, gi: int, seqs: slice, T: int, verify: bool, ws):
+        """One GDN layer over rows [B_s * T] (sequences `seqs` of the cache, T tokens each)."""
+        c = self.cfg
+        eps = c.rms_norm_eps
+        Bs = (seqs.stop - seqs.start)
+        M = Bs * T
+        proj = b["proj"]
+        ops.gemm(h, lw["w_in"], out=proj, ws=ws, norm_w=lw["in_norm"], sumsq_in=ss, eps=eps)
+        win = cache.window[gi][seqs]
+        ops.gdn_prep(proj, lw["conv_w"], lw["A_log"], lw["dt_bias"], cache.conv[gi][seqs], Bs, T, self.Hk, self.Hv,
+                     self.Dk, self.Dv, window=win if T <= cache.Tw else None, eps=1e-6,
+                     out={"q": b["gq"], "k": b["gk"], "v": b["gv"], "g": b["gg"], "beta": b["gbeta"]})
+        st = cache.state[gi][seqs]
+        o = b["go"].view(M, self.Hv, self.Dv)
+        if verify:
+            ops.gdr_recurrence(b["gq"].view(Bs, T, self.Hk, self.Dk), b["gk"].view(Bs, T, self.Hk, self.Dk),
+                               b["gv"].view(Bs, T, self.Hv, self.Dv), b["gg"].view(Bs, T, self.Hv),
+                               b["gbeta"].view(Bs, T, self.Hv), st, snapshots=cache.snaps[gi][seqs],
+                               o=o.view(Bs, T, self.Hv, self.Dv))
+        else:
+            ops.gdr_recurrence(b["gq"].view(Bs, T, self.Hk, self.Dk), b["gk"].view(Bs, T, self.Hk, self.Dk),
+                               b["gv"].view(Bs, T, self.Hv, self.Dv), b["gg"].view(Bs, T, self.Hv),
+                               b["gbeta"].view(Bs, T, self.Hv), st, state_out=st, o=o.view(Bs, T, self.Hv, self.Dv))
+        z = proj[:, self.C:self.C + self.vd]
+        ops.gated_rmsnorm(b["go"], z, lw["gnorm"], self.Hv, self.Dv, eps, out=b["gon"])
+        ops.gemm(b["gon"], lw["w_out"], ops.EPI_RESIDUAL, residual=h, out=h, ws=ws, sumsq_out=ss)
+
+    def forward(self, tokens: torch.Tensor, pos: torch.Tensor, cache: HybridCache, max_kv: int,
+                layer_ids: list[int] | None = None, taps_out: torch.Tensor | None = None,
+                row_seq: torch.Tensor | None = None, head: str = "argmax", ws: ops.Workspace | None = None,
+                seqs: slice | None = None, verify: bool = True, T: int | None = None):
+        """Block forward over M = B_s * T rows of sequences ``seqs`` (default: all, T = M / B).
+        verify=True writes per-token snapshots + the conv window (a later dfl_gdn_rollback
+        picks the accepted prefix); verify=False advances the GDN state in place (prefill)
+        and leaves the new conv state to ``commit_prefill``."""
+        c = self.cfg
+        M = tokens.numel()
+        b = self.buffers(M)
+        H, hd = c.hidden_size, c.head_dim
+        Hq, Hkv = c.num_attention_heads, c.num_key_value_heads
+        if seqs is None:
+            seqs = slice(0, cache.state[0].shape[0] if cache.state else 1)
+        Bs = seqs.stop - seqs.start
+        T = T or M // Bs
+        tap_col = {lid: i for i, lid in enumerate(sorted(layer_ids or []))}
+        h, ss, eps = b["h"], b["ss"], c.rms_norm_eps
+        ops.embed(tokens, self.embed_w, out=h, sumsq_out=ss)
+        for l, lw in enumerate(self.layers):
+            if self.kinds[l] == "gdn":
+                self._gdn_layer(lw, h, ss, b, cache, self.gdn_index[l], seqs, T, verify, ws)
+            else:
+                kc, vc = cache.kv.layer(self.attn_index[l])
+                ops.gemm(h, lw["w_qkv"], out=b["qkv"], ws=ws, norm_w=lw["in_norm"], sumsq_in=ss, eps=eps)
+                qkv = b["qkv"][:, :(2 * Hq + 2 * Hkv) * hd]
+                ops.qkv_rope_append(qkv, pos, lw["q_norm"], lw["k_norm"], self.inv_freq, kc, vc, Hq, Hkv, hd,
+                                    c.rope_dim, eps, q_out=b["q"], row_seq=row_seq, q_stride=2 * hd)
+                ops.attention(b["q"], kc, vc, pos, causal=True, max_kv=max_kv, row_seq=row_seq, out=b["attn"],
+                              ws=ws, gate=qkv[:, hd:], gate_head_stride=2 * hd)
+                ops.gemm(b["attn"], lw["w_o"], ops.EPI_RESIDUAL, residual=h, out=h, ws=ws, sumsq_out=ss)
+            ops.gemm(h, lw["w_gu"], ops.EPI_SILU_MUL, out=b["act"], ws=ws, norm_w=lw["post_norm"], sumsq_in=ss,
+                     eps=eps)
+            tap = None
+            if l in tap_col and taps_out is not None:
+                i = tap_col[l]
+                tap = taps_out[:, i * H:(i + 1) * H]
+            ops.gemm(b["act"], lw["w_down"], ops.EPI_RESIDUAL, residual=h, out=h, out2=tap, ws=ws, sumsq_out=ss)
+        if head == "hidden":
+            return ops.rmsnorm(h, self.norm_w, eps, out=b["xn"])
+        if head == "logits":
+            return ops.gemm(h, self.lm_head_w, ws=ws, norm_w=self.norm_w, sumsq_in=ss, eps=eps)
+        return ops.gemm(h, self.lm_head_w, ops.EPI_ARGMAX, argmax_partials=b["argmax"], ws=ws, norm_w=self.norm_w,
+                        sumsq_in=ss, eps=eps)
+
+    def rollback(self, cache: HybridCache, accepted: torch.Tensor, acc_stride: int, T: int | None = None) -> None:
+        """After a verify block: every GDN layer keeps the state after `accepted` tokens
+        (accepted[b * acc_stride], read on the device)."""
+        T = T or cache.T
+        B = cache.state[0].shape[0] if cache.state else 0
+        for gi in range(len(cache.state)):
+            ops.gdn_rollback(cache.state[gi], cache.snaps[gi], cache.conv[gi], cache.window[gi], accepted,
+                             acc_stride, B, T, self.Hv, self.Dv, self.Dk, self.C)
+
+    def commit_prefill(self, cache: HybridCache, seqs: slice, n_rows: torch.Tensor, T: int) -> None:
+        """After a prefill chunk of T rows: conv state <- last three rows of the window."""
+        Bs = seqs.stop - seqs.start
+        for gi in range(len(cache.state)):
+            ops.gdn_rollback(None, None, cache.conv[gi][seqs], cache.window[gi][seqs], n_rows, 1, Bs, T, self.Hv,
+                             self.Dv, self.Dk, self.C)

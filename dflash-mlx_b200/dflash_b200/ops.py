@@ -209,7 +209,8 @@ def qkv_rope_append(qkv: torch.Tensor, pos: torch.Tensor, q_norm: torch.Tensor, 
 
 def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, pos: torch.Tensor, causal: bool,
               max_kv: int, kv_len: torch.Tensor | None = None, row_seq: torch.Tensor | None = None,
-              scale: float | None = None, out: torch.Tensor | None = None, ws: Workspace | None = None) -> torch.Tensor:
+              scale: float | None = None, out: torch.Tensor | None = None, ws: Workspace | None = None,
+              gate: torch.Tensor | None = None, gate_head_stride: int = 0) -> torch.Tensor:
     """q [M, Hq, hd] against caches [seq, Hkv, cap, hd]; returns [M, Hq*hd] bf16."""
     _need_cuda(q, k_cache, v_cache, pos, kv_len, row_seq, out)
     M, Hq, hd = q.shape
@@ -223,7 +224,8 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, pos
     ws.ensure_attn(need)
     _lib.call("dfl_attention", _ptr(q), _ptr(k_cache), _ptr(v_cache), k_cache.stride(0), k_cache.stride(1),
               _ptr(pos), _ptr(row_seq), _ptr(kv_len), M, Hq, Hkv, hd, int(causal), float(scale), int(max_kv),
-              _ptr(out), _row_stride(out), _ptr(ws.attn), ws.attn.numel(), _stream())
+              _ptr(out), _row_stride(out), _ptr(gate), _row_stride(gate) if gate is not None else 0,
+              int(gate_head_stride), _ptr(ws.attn), ws.attn.numel(), _stream())
     return out
 
 
@@ -270,3 +272,40 @@ def gdr_recurrence(q, k, v, g, beta, state_in, state_out=None, snapshots=None, o
     bstride = state_in_bstride if state_in_bstride is not None else Hv * Dv * Dk
     _lib.call("dfl_gdr_recurrence", _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(state_in), bstride,
               _ptr(state_slot), _ptr(state_out), _ptr(snapshots), _ptr(o), B, T, Hk, Hv, Dk, Dv, _stream())
+
+
+def gdn_prep(proj: torch.Tensor, conv_w: torch.Tensor, A_log: torch.Tensor, dt_bias: torch.Tensor,
+             conv_state: torch.Tensor, B: int, T: int, Hk: int, Hv: int, Dk: int, Dv: int,
+             window: torch.Tensor | None = None, eps: float = 1e-6, out: dict | None = None) -> dict:
+    """Conv + SiLU + q/k scaling + g/beta for B sequences of T rows (proj rows are [qkv | z | b | a])."""
+    _need_cuda(proj, conv_w, A_log, dt_bias, conv_state, window)
+    dev = proj.device
+    M = B * T
+    o = out or {}
+    q = o.get("q") if o.get("q") is not None else torch.empty((M, Hk, Dk), dtype=torch.bfloat16, device=dev)
+    k = o.get("k") if o.get("k") is not None else torch.empty((M, Hk, Dk), dtype=torch.bfloat16, device=dev)
+    v = o.get("v") if o.get("v") is not None else torch.empty((M, Hv, Dv), dtype=torch.bfloat16, device=dev)
+    g = o.get("g") if o.get("g") is not None else torch.empty((M, Hv), dtype=torch.float32, device=dev)
+    beta = o.get("beta") if o.get("beta") is not None else torch.empty((M, Hv), dtype=torch.float32, device=dev)
+    _lib.call("dfl_gdn_prep", _ptr(proj), _row_stride(proj), _ptr(conv_w), _ptr(A_log), _ptr(dt_bias),
+              _ptr(conv_state), _ptr(window), window.stride(0) if window is not None else 0, _ptr(q), _ptr(k),
+              _ptr(v), _ptr(g), _ptr(beta), B, T, Hk, Hv, Dk, Dv, float(eps), _stream())
+    return {"q": q, "k": k, "v": v, "g": g, "beta": beta}
+
+
+def gdn_rollback(state, snapshots, conv_state, window, accepted, acc_stride, B, T, Hv, Dv, Dk, C):
+    """state <- snapshots[accepted-1]; conv_state <- window rows [accepted, accepted+3) (device-side accepted)."""
+    _lib.call("dfl_gdn_rollback", _ptr(state), _ptr(snapshots), _ptr(conv_state), _ptr(window),
+              window.stride(0) if window is not None else 0, _ptr(accepted), acc_stride, B, T, Hv, Dv, Dk, C,
+              _stream())
+
+
+def gated_rmsnorm(o: torch.Tensor, z: torch.Tensor, w: torch.Tensor, H: int, D: int, eps: float,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    _need_cuda(o, z, w, out)
+    M = o.shape[0]
+    if out is None:
+        out = torch.empty((M, H * D), dtype=torch.bfloat16, device=o.device)
+    _lib.call("dfl_gated_rmsnorm", _ptr(o), _row_stride(o), _ptr(z), _row_stride(z), _ptr(w), _ptr(out),
+              _row_stride(out), M, H, D, float(eps), _stream())
+    return out

@@ -140,12 +140,15 @@ int dfl_qkv_rope_append(const void* qkv, int64_t ldqkv, int q_stride, const int3
  * [0, pos[r]]; otherwise keys [0, kv_len[seq(r)]). Replaces
  * mx.fast.scaled_dot_product_attention at the verify (mask "causal",
  * adapters.py:620) and in DFlashAttention (draft.py:149-157). max_kv bounds
- * every row's key range (sizes the launch and the workspace). */
+ * every row's key range (sizes the launch and the workspace). hd in {64, 128, 256}.
+ * gate (nullable, row stride ldg, head h at h * gate_head_stride; 0 means hd):
+ * out = bf16(attn) * bf16(sigmoid(gate)) per element,
+ * the output gate of Qwen3.5 full attention (custom_qwen35_model.py:161-199). */
 size_t dfl_attention_workspace_bytes(int M, int Hq, int hd, int max_kv);
 int dfl_attention(const void* q, const void* k_cache, const void* v_cache, int64_t seq_stride, int64_t head_stride,
                   const int32_t* pos, const int32_t* row_seq, const int32_t* kv_len, int M, int Hq, int Hkv, int hd,
-                  int causal, float scale, int max_kv, void* out, int64_t ldo, void* workspace,
-                  size_t workspace_bytes, void* stream);
+                  int causal, float scale, int max_kv, void* out, int64_t ldo, const void* gate, int64_t ldg,
+                  int gate_head_stride, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---- speculative step control ---------------------------------------------
  * Greedy argmax from DFL_EPI_ARGMAX partials (runtime.py:22-29 at temperature 0). */
@@ -172,6 +175,29 @@ int dfl_draft_commit(dfl_seq_state* state, const void* partials, int n_tiles, in
 int dfl_verify_accept(dfl_seq_state* state, const void* partials, int n_tiles, const int32_t* block, int bs,
                       int32_t* out_tokens, int64_t out_stride, int32_t* posterior, const int32_t* stop_ids,
                       int n_stop, int32_t* accept_log, int64_t log_stride, int B, void* stream);
+
+/* ---- gated-delta-net layer (Qwen3.5 linear attention) ------------------------
+ * dfl_gdn_prep: from the in-projection rows proj [B*T][ldp] = [qkv (C = 2*Hk*Dk + Hv*Dv)
+ * | z (Hv*Dv) | b (Hv) | a (Hv)] and the conv state [B][3][C]: depthwise conv1d (k=4)
+ * + SiLU, q <- Dk^-1 * rmsnorm(q), k <- Dk^-1/2 * rmsnorm(k), beta = sigmoid(b),
+ * g = exp(-exp(A_log) * softplus(a + dt_bias)); window (nullable; win_stride elements
+ * per sequence, 0 = packed 3+T rows) keeps
+ * [conv state | qkv] for the rollback. Replaces custom_qwen35_model.py:409-450. */
+int dfl_gdn_prep(const void* proj, int64_t ldp, const void* conv_w, const float* A_log, const float* dt_bias,
+                 const void* conv_state, void* window, int64_t win_stride, void* q, void* k, void* v, float* g,
+                 float* beta, int B, int T, int Hk, int Hv, int Dk, int Dv, float eps, void* stream);
+
+/* Rollback to "after accepted[b * acc_stride] tokens" of the block: state[b] <-
+ * snapshots[b][acc-1] (when snapshots != NULL), conv_state[b] <- window[b][acc..acc+2]
+ * (when window != NULL). Replaces rollback_linear_caches (custom_qwen35_model.py:1029-1074,
+ * adapters.py:510-560), which replays the recurrence instead. */
+int dfl_gdn_rollback(float* state, const float* snapshots, void* conv_state, const void* window,
+                     int64_t win_stride, const int32_t* accepted, int acc_stride, int B, int T, int Hv, int Dv,
+                     int Dk, int C, void* stream);
+
+/* RMSNormGated per value head: out = bf16(w * rmsnorm(o)) * bf16(silu(z)) (adapters.py:226-227). */
+int dfl_gated_rmsnorm(const void* o, int64_t ldo, const void* z, int64_t ldz, const void* w, void* out, int64_t ldout,
+                      int M, int H, int D, float eps, void* stream);
 
 /* ---- gated-delta recurrence -----------------------------------------------
  * q,k [B,T,Hk,Dk] bf16, v [B,T,Hv,Dv] bf16, g (decay multiplier) and beta

@@ -136,3 +136,80 @@ def test_qwen3_layers_match_transformers():
     ours, _ = ot.forward_states(toks[0].tolist(), ot.make_cache(), [])
     err = (ours - hf).abs().max().item()
     assert err < 0.05 * hf.abs().max().item(), err
+
+
+def test_qwen35_hybrid_layers_match_transformers(monkeypatch):
+    """The restated hybrid stack (GDN layers + gated partial-RoPE attention) agrees with
+    transformers' Qwen3_5TextModel on the same weights, with the oracle's bf16
+    roundings switched off so that the comparison is of the mathematics (fp32 both
+    sides, 1e-3 relative). transformers keeps the
+    zero-centred RMSNorm weights (applies 1 + w); the mlx checkpoint layout the
+    reference loads stores them shifted, so the oracle's w maps to w - 1 there."""
+    tq = pytest.importorskip("transformers.models.qwen3_5.modeling_qwen3_5")
+    from transformers.models.qwen3_5.configuration_qwen3_5 import Qwen3_5TextConfig
+    from dflash_b200.config import tiny_hybrid_pair
+    from dflash_b200.weights import random_target_weights
+    tcfg, _ = tiny_hybrid_pair()
+    w = random_target_weights(tcfg, 12, std=0.05)
+    hf_cfg = Qwen3_5TextConfig(
+        vocab_size=tcfg.vocab_size, hidden_size=tcfg.hidden_size, intermediate_size=tcfg.intermediate_size,
+        num_hidden_layers=tcfg.num_hidden_layers, num_attention_heads=tcfg.num_attention_heads,
+        num_key_value_heads=tcfg.num_key_value_heads, head_dim=tcfg.head_dim, rms_norm_eps=tcfg.rms_norm_eps,
+        linear_key_head_dim=tcfg.linear_key_head_dim, linear_value_head_dim=tcfg.linear_value_head_dim,
+        linear_num_key_heads=tcfg.linear_num_key_heads, linear_num_value_heads=tcfg.linear_num_value_heads,
+        layer_types=["linear_attention" if tcfg.is_linear_layer(i) else "full_attention"
+                     for i in range(tcfg.num_hidden_layers)],
+        rope_parameters={"rope_type": "default", "rope_theta": tcfg.rope_theta,
+                         "partial_rotary_factor": tcfg.partial_rotary_factor})
+    hf_cfg._attn_implementation = "eager"
+    model = tq.Qwen3_5TextModel(hf_cfg).eval()
+    sd = {"embed_tokens.weight": w["embed"], "norm.weight": w["norm"].float() - 1}
+    for i, lw in enumerate(w["layers"]):
+        p = f"layers.{i}."
+        sd[p + "input_layernorm.weight"] = lw["input_layernorm"].float() - 1
+        sd[p + "post_attention_layernorm.weight"] = lw["post_attention_layernorm"].float() - 1
+        for k in ("gate_proj", "up_proj", "down_proj"):
+            sd[p + f"mlp.{k}.weight"] = lw[k]
+        if tcfg.is_linear_layer(i):
+            for k in ("in_proj_qkv", "in_proj_z", "in_proj_b", "in_proj_a", "out_proj", "A_log", "dt_bias"):
+                sd[p + f"linear_attn.{k}" + ("" if k in ("A_log", "dt_bias") else ".weight")] = lw[k]
+            sd[p + "linear_attn.conv1d.weight"] = lw["conv1d"][:, None, :]
+            sd[p + "linear_attn.norm.weight"] = lw["norm"]
+        else:
+            for k in ("q_proj", "k_proj", "v_proj", "o_proj"):
+                sd[p + f"self_attn.{k}.weight"] = lw[k]
+            sd[p + "self_attn.q_norm.weight"] = lw["q_norm"].float() - 1
+            sd[p + "self_attn.k_norm.weight"] = lw["k_norm"].float() - 1
+    missing = set(model.state_dict()) - set(sd)
+    assert not missing, missing
+    model.load_state_dict({k: v.float() for k, v in sd.items()})
+    g = torch.Generator().manual_seed(1)
+    toks = torch.randint(0, tcfg.vocab_size, (1, 24), generator=g)
+    with torch.no_grad():
+        hf = model(toks).last_hidden_state[0]
+    monkeypatch.setattr(O, "bf16", lambda x: x.float())
+    ot = O.OracleHybridTarget(tcfg, w)
+    ours, _ = ot.forward_states(toks[0].tolist(), ot.make_cache(), [])
+    err = (ours - hf).abs().max().item()
+    assert err < 1e-3 * hf.abs().max().item(), err
+
+
+def test_hybrid_oracle_spec_is_lossless():
+    """Hybrid oracle decode loop with injected drafts (snapshot rollback of every GDN
+    layer after each partial accept) reproduces its plain greedy decode."""
+    from dflash_b200.config import tiny_hybrid_pair
+    from dflash_b200.weights import random_draft_weights, random_target_weights
+    tcfg, dcfg = tiny_hybrid_pair()
+    ot = O.OracleHybridTarget(tcfg, random_target_weights(tcfg, 0, std=0.05))
+    od = O.OracleDraft(dcfg, random_draft_weights(dcfg, 0), ot)
+    od.mask_mode = "causal"
+    g = torch.Generator().manual_seed(3)
+    prompt = torch.randint(0, tcfg.vocab_size, (24,), generator=g).tolist()
+    bs = dcfg.block_size
+    trace = O.plain_greedy(ot, prompt, 24 + 3 * bs)
+    lens = torch.randint(0, bs, (40,), generator=g).tolist()
+    noise = torch.randint(0, tcfg.vocab_size, (40, bs), generator=g).tolist()
+    out, accs = O.spec_generate(ot, od, prompt, 24, bs, set(), O.Injection(trace + [0] * 4 * bs, lens, noise))
+    assert out == trace[:len(out)]
+    assert len(out) >= len(prompt) + 24
+    assert any(1 < a < bs for a in accs)

@@ -10,14 +10,20 @@
 //
 // Layout: q [M][Hq][hd] bf16, caches [seq][Hkv][cap][hd] bf16 (slot == position).
 // Work split: one CTA per (key chunk of DFL_ATTN_CHUNK keys, kv head, 16-token
-// tile); warp w of the CTA owns q head kvh*G + w for the 16 tokens, so the G
+// tile, sequence segment of the tile); the rows of a tile that belong to the
+// segment's sequence are the CTA's rows (a batched verify block of fewer than
+// 16 rows per sequence puts several sequences in one tile, each read from its own
+// cache); warp w of the CTA owns q head kvh*G + w for the 16 tokens, so the G
 // query heads sharing a kv head read each K/V tile once. Chunks are fixed
 // absolute key ranges and are merged in chunk order by a second kernel, so a
 // query row's result does not depend on the other rows or on keys it cannot
 // see (spec-verify rows and plain-decode rows agree bit for bit).
 #include "common.cuh"
+#include "tma_util.cuh"
 
 namespace dfl {
+
+constexpr int ATT_SITE_SEGMENTS = 301;  // a tile held more sequences than the launch's segments
 
 constexpr int ATT_CH = DFL_ATTN_CHUNK;  // keys per chunk
 constexpr int ATT_KB = 64;              // keys per shared-memory sub-block
@@ -38,6 +44,8 @@ struct AttnArgs {
   long long ldg;
   int gate_hs;  // elements between consecutive heads' gates in a row
   int M, Hq, Hkv, G, causal, n_chunks;
+  int segs;          // sequence segments per 16-row tile (grid z = tiles * segs)
+  int* err;          // device error record
   float scale_log2;  // softmax scale * log2(e)
 };
 
@@ -65,21 +73,34 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(AttnArgs a) {
   __nv_bfloat16* sK = sQ + a.G * 16 * HD;                           // [2][64][HD]
   __nv_bfloat16* sV = sK + 2 * ATT_KB * HD;                          // [2][64][HD]
 
-  const int chunk = blockIdx.x, kvh = blockIdx.y, tile = blockIdx.z;
+  const int chunk = blockIdx.x, kvh = blockIdx.y, tile = blockIdx.z / a.segs, seg = blockIdx.z % a.segs;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nthr = blockDim.x;
   const int m0 = tile * 16;
 
   __shared__ int s_lim[16];
   __shared__ int s_seq;
-  if (threadIdx.x < 16) s_lim[threadIdx.x] = row_limit(a, m0 + threadIdx.x);
   if (threadIdx.x == 0) {
-    int s = 0;
+    // the seg-th distinct sequence among the tile's live rows, in row order
+    int seqs[16];
+    int n = 0;
     for (int r = 0; r < 16; ++r) {
       const int m = m0 + r;
-      if (m < a.M && a.pos[m] >= 0) { s = a.row_seq ? a.row_seq[m] : 0; break; }
+      if (m >= a.M || a.pos[m] < 0) continue;
+      const int sq = a.row_seq ? a.row_seq[m] : 0;
+      bool seen = false;
+      for (int j = 0; j < n; ++j) seen |= seqs[j] == sq;
+      if (!seen) seqs[n++] = sq;
     }
-    s_seq = s;
+    if (seg == 0 && n > a.segs && chunk == 0 && kvh == 0 && a.err) atomicCAS(a.err, 0, ATT_SITE_SEGMENTS);
+    s_seq = seg < n ? seqs[seg] : -1;
+  }
+  __syncthreads();
+  if (s_seq < 0) return;
+  if (threadIdx.x < 16) {
+    const int m = m0 + threadIdx.x;
+    const bool mine = m < a.M && (a.row_seq ? a.row_seq[m] : 0) == s_seq;
+    s_lim[threadIdx.x] = mine ? row_limit(a, m) : 0;
   }
   __syncthreads();
   int lim_max = 0;
@@ -301,7 +322,7 @@ static int launch_attn(AttnArgs a, int n_tiles, cudaStream_t st) {
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(a.n_chunks, a.Hkv, n_tiles);
+  cfg.gridDim = dim3(a.n_chunks, a.Hkv, n_tiles * a.segs);
   cfg.blockDim = dim3(32 * a.G);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -338,7 +359,7 @@ extern "C" size_t dfl_attention_workspace_bytes(int M, int Hq, int hd, int max_k
 
 extern "C" int dfl_attention(const void* q, const void* k_cache, const void* v_cache, int64_t seq_stride,
                              int64_t head_stride, const int32_t* pos, const int32_t* row_seq, const int32_t* kv_len,
-                             int M, int Hq, int Hkv, int hd, int causal, float scale, int max_kv, void* out,
+                             int seq_rows, int M, int Hq, int Hkv, int hd, int causal, float scale, int max_kv, void* out,
                              int64_t ldo, const void* gate, int64_t ldg, int gate_head_stride, void* workspace,
                              size_t workspace_bytes, void* stream) {
   if (M == 0) return DFL_OK;
@@ -385,6 +406,14 @@ extern "C" int dfl_attention(const void* q, const void* k_cache, const void* v_c
   a.causal = causal;
   a.scale_log2 = scale * 1.4426950408889634f;
   const int n_tiles = (M + 15) / 16;
+  // sequences a 16-row tile can hold: one without row_seq or when sequences are
+  // whole multiples of 16 rows (or one sequence spans all rows); 16 / seq_rows when
+  // that divides; otherwise every row may start a new sequence
+  if (!row_seq || seq_rows >= M || (seq_rows > 0 && seq_rows % 16 == 0)) a.segs = 1;
+  else if (seq_rows > 0 && 16 % seq_rows == 0) a.segs = 16 / seq_rows;
+  else if (seq_rows > 0) a.segs = min(16, (15 + seq_rows - 1) / seq_rows + 1);
+  else a.segs = min(16, M);
+  a.err = device_error_word();
   cudaStream_t st = as_stream(stream);
   switch (hd) {
     case 64: return launch_attn<64>(a, n_tiles, st);

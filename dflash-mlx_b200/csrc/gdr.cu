@@ -40,6 +40,42 @@ struct GdrArgs {
   int B, T, Hk, Hv, Dk, Dv;
 };
 
+// a lane's PER contiguous fp32 state values: float4 moves for PER % 4 == 0 (Dk 128),
+// float2 for PER == 2 (Dk 64)
+template <int PER>
+__device__ __forceinline__ void load_state(float (&s)[PER], const float* p) {
+  if constexpr (PER % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < PER / 4; ++i) {
+      const float4 f = reinterpret_cast<const float4*>(p)[i];
+      s[4 * i] = f.x;
+      s[4 * i + 1] = f.y;
+      s[4 * i + 2] = f.z;
+      s[4 * i + 3] = f.w;
+    }
+  } else {
+    static_assert(PER % 2 == 0, "state slice must be float2-aligned");
+#pragma unroll
+    for (int i = 0; i < PER / 2; ++i) {
+      const float2 f = reinterpret_cast<const float2*>(p)[i];
+      s[2 * i] = f.x;
+      s[2 * i + 1] = f.y;
+    }
+  }
+}
+
+template <int PER>
+__device__ __forceinline__ void store_state(float* p, const float (&s)[PER]) {
+  if constexpr (PER % 4 == 0) {
+#pragma unroll
+    for (int i = 0; i < PER / 4; ++i)
+      reinterpret_cast<float4*>(p)[i] = make_float4(s[4 * i], s[4 * i + 1], s[4 * i + 2], s[4 * i + 3]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < PER / 2; ++i) reinterpret_cast<float2*>(p)[i] = make_float2(s[2 * i], s[2 * i + 1]);
+  }
+}
+
 template <int DK>
 __global__ void __launch_bounds__(32 * GDR_ROWS) gdr_kernel(GdrArgs a) {
   grid_dependency_launch_dependents();
@@ -61,17 +97,7 @@ __global__ void __launch_bounds__(32 * GDR_ROWS) gdr_kernel(GdrArgs a) {
   const float* sin = a.state_in + b * a.state_in_bstride + (a.state_slot ? (long long)a.state_slot[b] * slot_elems : 0) +
                      h * hstate + (long long)row * DK;
   float s[PER];
-  {
-    const float4* p = reinterpret_cast<const float4*>(sin + lane * PER);
-#pragma unroll
-    for (int i = 0; i < PER / 4; ++i) {
-      const float4 f = p[i];
-      s[4 * i] = f.x;
-      s[4 * i + 1] = f.y;
-      s[4 * i + 2] = f.z;
-      s[4 * i + 3] = f.w;
-    }
-  }
+  load_state<PER>(s, sin + lane * PER);
 
   for (int t0 = 0; t0 < a.T; t0 += GDR_TT) {
     const int nt = min(GDR_TT, a.T - t0);
@@ -120,18 +146,13 @@ __global__ void __launch_bounds__(32 * GDR_ROWS) gdr_kernel(GdrArgs a) {
         if (lane == 0) a.o[(((long long)b * a.T + t) * a.Hv + h) * a.Dv + row] = f2bf(y);
       }
       if (a.snap) {
-        float4* dst = reinterpret_cast<float4*>(a.snap + (((long long)b * a.T + t) * a.Hv + h) * hstate +
-                                                (long long)row * DK + lane * PER);
-#pragma unroll
-        for (int i = 0; i < PER / 4; ++i) dst[i] = make_float4(s[4 * i], s[4 * i + 1], s[4 * i + 2], s[4 * i + 3]);
+        store_state<PER>(a.snap + (((long long)b * a.T + t) * a.Hv + h) * hstate + (long long)row * DK + lane * PER,
+                         s);
       }
     }
   }
   if (a.state_out) {
-    float4* dst = reinterpret_cast<float4*>(a.state_out + ((long long)b * a.Hv + h) * hstate + (long long)row * DK +
-                                            lane * PER);
-#pragma unroll
-    for (int i = 0; i < PER / 4; ++i) dst[i] = make_float4(s[4 * i], s[4 * i + 1], s[4 * i + 2], s[4 * i + 3]);
+    store_state<PER>(a.state_out + ((long long)b * a.Hv + h) * hstate + (long long)row * DK + lane * PER, s);
   }
 }
 

@@ -125,7 +125,10 @@ __global__ void verify_accept_kernel(dfl_seq_state* st, const float2* __restrict
   __syncthreads();
   if (threadIdx.x != 0) return;
   dfl_seq_state s = st[b];
-  if (s.finished) return;
+  if (s.finished) {
+    st[b].accepted = 0;  // recurrent-state rollback skips finished sequences
+    return;
+  }
   const int* blk = block + b * bs;
   int matched = 0;
   while (matched < bs - 1 && blk[matched + 1] == post[matched]) ++matched;

@@ -150,8 +150,106 @@ class Qwen3TargetAdapter(TargetAdapter):
         return self.lm_head_logits(model, norm_h[:, -1:, :]), taps
 
 
+class Qwen35TargetAdapter(TargetAdapter):
+    """Qwen3.5 hybrid adapter (adapters.py:341-570). Differences of mechanism, same
+    cache semantics: a forward that returns rollback records leaves every gated-delta
+    layer's state advanced over the whole block (as the reference does) and keeps the
+    per-token snapshots and the conv window on the device; ``rollback_linear_caches``
+    restores snapshot ``accepted - 1`` instead of replaying the recurrence over the
+    accepted prefix (adapters.py:505-560)."""
+
+    family = "qwen3_5"
+
+    def make_cache(self, model, cap: int = 8192, block: int = 16) -> TargetCache:
+        return TargetCache(model.make_cache(1, cap, block=block))
+
+    def _forward_states(self, model, inputs: torch.Tensor, cache: TargetCache, layer_ids, records: bool):
+        toks = inputs.reshape(-1).to(model.device, torch.int32).contiguous()
+        T = toks.numel()
+        hc = cache.kv
+        H = model.cfg.hidden_size
+        if cache.offset + T > hc.cap:
+            raise ValueError("KV cache capacity exceeded")
+        if records and T > hc.T:
+            raise ValueError(f"a block with rollback records holds at most {hc.T} tokens")
+        taps = torch.empty((T, len(layer_ids) * H), dtype=torch.bfloat16, device=model.device)
+        outs = []
+        step = T if records else hc.Tw
+        one = slice(0, 1)
+        for c0 in range(0, T, step):
+            c1 = min(T, c0 + step)
+            n = c1 - c0
+            pos = torch.arange(cache.offset + c0, cache.offset + c1, dtype=torch.int32, device=model.device)
+            nrow = torch.full((1,), n, dtype=torch.int32, device=model.device)
+            outs.append(model.forward(toks[c0:c1], pos, hc, max_kv=cache.offset + c1, layer_ids=list(layer_ids),
+                                      taps_out=taps[c0:c1], head="hidden", seqs=one, verify=records, T=n).clone())
+            if records:
+                model.rollback(hc, nrow, 1, n)  # advance over the whole block; snapshots stay for rollback
+                hc.last_block = n
+            else:
+                model.commit_prefill(hc, one, nrow, n)
+        cache.offset += T
+        return torch.cat(outs, 0)[None], taps[None]
+
+    def forward_with_hidden_states(self, model, inputs, cache, layer_ids, return_rollback_records=False):
+        norm_h, taps = self._forward_states(model, inputs, cache, layer_ids, return_rollback_records)
+        logits = self.lm_head_logits(model, norm_h)
+        if return_rollback_records:
+            return logits, taps, self._records(model, cache)
+        return logits, taps
+
+    def forward_verifier_states(self, model, inputs, cache, layer_ids):
+        norm_h, taps = self._forward_states(model, inputs, cache, layer_ids, True)
+        return norm_h, taps, self._records(model, cache)
+
+    def forward_accept_all_block(self, model, inputs, cache, layer_ids):
+        norm_h, taps = self._forward_states(model, inputs, cache, layer_ids, False)
+        return self.lm_head_logits(model, norm_h[:, -1:, :]), taps
+
+    @staticmethod
+    def _records(model, cache: TargetCache) -> dict:
+        """Layer index -> record of the block just verified (its snapshots live in the cache)."""
+        T = cache.kv.last_block
+        return {l: {"block_tokens": T} for l, k in enumerate(model.kinds) if k == "gdn"}
+
+    def snapshot_linear_caches(self, model, cache: TargetCache) -> dict:
+        hc = cache.kv
+        return {l: [hc.conv[gi].clone(), hc.state[gi].clone()] for l, gi in model.gdn_index.items()}
+
+    def restore_linear_caches(self, model, cache: TargetCache, snapshots: dict) -> None:
+        hc = cache.kv
+        for l, (conv, state) in snapshots.items():
+            gi = model.gdn_index[l]
+            hc.conv[gi].copy_(conv)
+            hc.state[gi].copy_(state)
+
+    def rewind_kv_caches(self, cache: TargetCache, num_tokens: int) -> None:
+        cache.trim(num_tokens)
+
+    def rollback_linear_caches(self, model, cache: TargetCache, rollback_records: dict, accepted_inputs: int) -> None:
+        if not rollback_records:
+            return
+        T = next(iter(rollback_records.values()))["block_tokens"]
+        if not 1 <= accepted_inputs <= T:
+            raise ValueError(f"accepted_inputs {accepted_inputs} outside [1, {T}]")
+        acc = torch.full((1,), int(accepted_inputs), dtype=torch.int32, device=model.device)
+        model.rollback(cache.kv, acc, 1, T)
+
+    def cache_summary(self, cache: TargetCache) -> str:
+        hc = cache.kv
+        parts = []
+        for l, k in enumerate(cache_model_kinds(hc)):
+            parts.append(f"{l}:kv={cache.offset}" if k == "attn" else f"{l}:ssm={tuple(hc.state[0].shape[1:])}")
+        return " ".join(parts)
+
+
+def cache_model_kinds(hc) -> list[str]:
+    return list(getattr(hc, "kinds", []))
+
+
 ADAPTERS: dict[str, type[TargetAdapter]] = {
     "qwen3": Qwen3TargetAdapter,
+    "qwen3_5": Qwen35TargetAdapter,
 }
 
 
@@ -212,7 +310,8 @@ class LoadedTargetModel:
 
 
 def load_target_model(path_or_spec: str | tuple, device="cuda", seed: int = 0) -> LoadedTargetModel:
-    """Builds a target. ``"random:<preset>"`` (presets: tiny, qwen3-4b) draws seeded
+    """Builds a target. ``"random:<preset>"`` (presets: tiny, qwen3-4b, tiny-hybrid,
+    qwen3.5-27b) draws seeded
     random weights; a ``(TargetConfig, weights)`` tuple uses the given weights.
     Checkpoint directories are not read by this build (the safetensors loader is
     listed as the next row of work)."""
@@ -235,6 +334,10 @@ def load_target_model(path_or_spec: str | tuple, device="cuda", seed: int = 0) -
         registered = ", ".join(sorted(ADAPTERS))
         raise NotImplementedError(f"Unsupported DFlash target model_type={cfg.model_type!r}. Current adapters: "
                                   f"{registered}.")
-    model = TargetModel(cfg, w, device)
+    if cfg.model_type == "qwen3_5":
+        from .hybrid import HybridTargetModel
+        model = HybridTargetModel(cfg, w, device)
+    else:
+        model = TargetModel(cfg, w, device)
     tok = ByteTokenizer(cfg.vocab_size, cfg.eos_token_ids)
     return LoadedTargetModel(name, None, model, tok, adapter_cls())

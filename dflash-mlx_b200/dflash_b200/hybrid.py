@@ -39,6 +39,8 @@ class HybridCache:
     window: list[torch.Tensor]       # per GDN layer [B, 3 + Tw, C] bf16
     T: int                           # verify block rows per sequence (snapshot depth)
     Tw: int                          # window rows per sequence (max block / prefill chunk)
+    kinds: list = field(default_factory=list)  # per layer "gdn" / "attn"
+    last_block: int = 0              # rows of the last block forwarded with snapshots
 
     @property
     def cap(self) -> int:
@@ -47,6 +49,8 @@ class HybridCache:
 
 class HybridTargetModel:
     """Qwen3.5-family target (GDN + gated attention) with the TargetModel interface."""
+
+    has_recurrent_state = True
 
     def __init__(self, cfg: TargetConfig, weights: dict, device="cuda"):
         if cfg.model_type != "qwen3_5":
@@ -118,7 +122,7 @@ class HybridTargetModel:
             snaps=[torch.zeros((batch, block, *S), dtype=torch.float32, device=dev) for _ in range(n)],
             conv=[torch.zeros((batch, 3, self.C), dtype=torch.bfloat16, device=dev) for _ in range(n)],
             window=[torch.zeros((batch, 3 + Tw, self.C), dtype=torch.bfloat16, device=dev) for _ in range(n)],
-            T=block, Tw=Tw)
+            T=block, Tw=Tw, kinds=list(self.kinds))
 
     def buffers(self, M: int) -> dict[str, torch.Tensor]:
         b = self._bufs.get(M)
@@ -177,7 +181,7 @@ class HybridTargetModel:
     def forward(self, tokens: torch.Tensor, pos: torch.Tensor, cache: HybridCache, max_kv: int,
                 layer_ids: list[int] | None = None, taps_out: torch.Tensor | None = None,
                 row_seq: torch.Tensor | None = None, head: str = "argmax", ws: ops.Workspace | None = None,
-                seqs: slice | None = None, verify: bool = True, T: int | None = None):
+                seqs: slice | None = None, verify: bool = True, T: int | None = None, seq_rows: int = 0):
         """Block forward over M = B_s * T rows of sequences ``seqs`` (default: all, T = M / B).
         verify=True writes per-token snapshots + the conv window (a later dfl_gdn_rollback
         picks the accepted prefix); verify=False advances the GDN state in place (prefill)
@@ -204,6 +208,7 @@ class HybridTargetModel:
                 ops.qkv_rope_append(qkv, pos, lw["q_norm"], lw["k_norm"], self.inv_freq, kc, vc, Hq, Hkv, hd,
                                     c.rope_dim, eps, q_out=b["q"], row_seq=row_seq, q_stride=2 * hd)
                 ops.attention(b["q"], kc, vc, pos, causal=True, max_kv=max_kv, row_seq=row_seq, out=b["attn"],
+                              seq_rows=seq_rows or T,
                               ws=ws, gate=qkv[:, hd:], gate_head_stride=2 * hd)
                 ops.gemm(b["attn"], lw["w_o"], ops.EPI_RESIDUAL, residual=h, out=h, ws=ws, sumsq_out=ss)
             ops.gemm(h, lw["w_gu"], ops.EPI_SILU_MUL, out=b["act"], ws=ws, norm_w=lw["post_norm"], sumsq_in=ss,

@@ -58,6 +58,19 @@ def sample_tokens(logits: torch.Tensor, temperature: float) -> torch.Tensor:
     return torch.argmax(flat, dim=-1).reshape(logits.shape[:-1]).to(torch.int32)
 
 
+def _packed_weights(model) -> list:
+    """Every packed GEMM weight a target / draft model holds (workspace sizing)."""
+    out = []
+    for v in vars(model).values():
+        items = v if isinstance(v, list) else [v]
+        for it in items:
+            if isinstance(it, ops.PackedWeight):
+                out.append(it)
+            elif isinstance(it, dict):
+                out.extend(x for x in it.values() if isinstance(x, ops.PackedWeight))
+    return out
+
+
 class SpecSession:
     """Device buffers and the captured step for B sequences decoded together."""
 
@@ -91,7 +104,8 @@ class SpecSession:
         stops = sorted(stop_token_ids or [])
         self.n_stop = len(stops)
         self.stop_ids = torch.tensor(stops or [0], **i32)
-        self.tcache = target.make_cache(B, self.cap)
+        self.hybrid = bool(getattr(target, "has_recurrent_state", False))
+        self.tcache = target.make_cache(B, self.cap, block=bs)
         self.layer_ids = sorted(draft.target_layer_ids) if draft is not None else []
         ntaps = max(1, len(self.layer_ids))
         self.taps = torch.zeros((B * bs, ntaps * tc.hidden_size), dtype=torch.bfloat16, device=dev)
@@ -110,16 +124,12 @@ class SpecSession:
         gemm_need = 0
         attn_need = 0
         shapes = [self.B * self.bs, self.prefill_chunk]
-        mats = [(tc.num_attention_heads + 2 * tc.num_key_value_heads) * tc.head_dim, tc.hidden_size,
-                2 * tc.intermediate_size, tc.vocab_size]
-        ks = [tc.hidden_size, tc.num_attention_heads * tc.head_dim, tc.intermediate_size,
-              self.taps.shape[1]]
+        nk = {(w.N, w.K) for w in _packed_weights(self.target)}
         if self.draft is not None:
-            mats.append(self.draft.w_ctx_kv.shape[0])
+            nk |= {(w.N, w.K) for w in _packed_weights(self.draft)}
         for M in shapes:
-            for N in mats:
-                for K in ks:
-                    gemm_need = max(gemm_need, int(q("dfl_gemm_workspace_bytes", M, N, K, 0)))
+            for N, K in nk:
+                gemm_need = max(gemm_need, int(q("dfl_gemm_workspace_bytes", M, N, K, 0)))
             attn_need = max(attn_need, int(q("dfl_attention_workspace_bytes", M, tc.num_attention_heads,
                                                tc.head_dim, self.cap)))
         self.ws.ensure_gemm(gemm_need)
@@ -160,8 +170,16 @@ class SpecSession:
                 pos = torch.arange(c0, c1, dtype=torch.int32, device=dev)
                 rs = seq[:n] if seq is not None else None
                 taps = torch.empty((n, self.taps.shape[1]), dtype=torch.bfloat16, device=dev)
-                part = self.target.forward(toks[c0:c1], pos, self.tcache, max_kv=c1, layer_ids=self.layer_ids,
-                                           taps_out=taps, row_seq=rs, ws=self.ws)
+                if self.hybrid:
+                    # recurrent layers advance in place over the chunk; conv state from the window
+                    part = self.target.forward(toks[c0:c1], pos, self.tcache, max_kv=c1, layer_ids=self.layer_ids,
+                                               taps_out=taps, row_seq=rs, ws=self.ws, seqs=slice(b, b + 1),
+                                               verify=False, T=n, seq_rows=n)
+                    self.target.commit_prefill(self.tcache, slice(b, b + 1),
+                                               torch.full((1,), n, dtype=torch.int32, device=dev), n)
+                else:
+                    part = self.target.forward(toks[c0:c1], pos, self.tcache, max_kv=c1, layer_ids=self.layer_ids,
+                                               taps_out=taps, row_seq=rs, ws=self.ws, seq_rows=n)
                 last_part = part[n - 1:n]
                 if self.draft is not None:
                     self.draft.ingest_context(taps, pos, self.dcache, row_seq=rs, ws=self.ws)
@@ -196,16 +214,20 @@ class SpecSession:
             d = self.draft
             d.ingest_context(self.taps, self.dpos_ctx, self.dcache, row_seq=self.row_seq, ws=self.ws)
             part = d.forward_block(self.block, self.dpos_blk, self.dcache, self.dkv_len, self.cap,
-                                   row_seq=self.row_seq, ws=self.ws)
+                                   row_seq=self.row_seq, ws=self.ws, seq_rows=bs)
             ops.draft_commit(self.state, part, self.block, bs, B, self.inject_tokens, self.inject_len,
                              self.inject_noise)
 
     def _verify_kernels(self) -> None:
         """Target verify forward + accept (parallel-replay, runtime.py:117-163)."""
         part = self.target.forward(self.block, self.tpos, self.tcache, max_kv=self.cap, layer_ids=self.layer_ids,
-                                   taps_out=self.taps, row_seq=self.row_seq, ws=self.ws)
+                                   taps_out=self.taps, row_seq=self.row_seq, ws=self.ws, seq_rows=self.bs)
         ops.verify_accept(self.state, part, self.block, self.bs, self.out_tokens, self.B,
                           stop_ids=self.stop_ids, n_stop=self.n_stop, accept_log=self.accept_log)
+        if self.hybrid:
+            # recurrent layers keep the state after the accepted prefix (snapshot restore);
+            # attention KV needs no truncation: the next block overwrites rows past start
+            self.target.rollback(self.tcache, self.state[:, S_ACCEPTED], STATE_INTS, self.bs)
 
     def capture(self) -> None:
         """Captures the draft half and the verify half of a step as two CUDA graphs."""

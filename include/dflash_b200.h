@@ -143,10 +143,14 @@ int dfl_qkv_rope_append(const void* qkv, int64_t ldqkv, int q_stride, const int3
  * every row's key range (sizes the launch and the workspace). hd in {64, 128, 256}.
  * gate (nullable, row stride ldg, head h at h * gate_head_stride; 0 means hd):
  * out = bf16(attn) * bf16(sigmoid(gate)) per element,
- * the output gate of Qwen3.5 full attention (custom_qwen35_model.py:161-199). */
+ * the output gate of Qwen3.5 full attention (custom_qwen35_model.py:161-199).
+ * seq_rows: with row_seq, each sequence's rows are contiguous runs of seq_rows
+ * rows starting at multiples of seq_rows (a batched verify block); 0 = any
+ * layout (slower launch). Rows of different sequences may share a 16-row tile;
+ * a tile with more sequences than the layout allows sets device error 301. */
 size_t dfl_attention_workspace_bytes(int M, int Hq, int hd, int max_kv);
 int dfl_attention(const void* q, const void* k_cache, const void* v_cache, int64_t seq_stride, int64_t head_stride,
-                  const int32_t* pos, const int32_t* row_seq, const int32_t* kv_len, int M, int Hq, int Hkv, int hd,
+                  const int32_t* pos, const int32_t* row_seq, const int32_t* kv_len, int seq_rows, int M, int Hq, int Hkv, int hd,
                   int causal, float scale, int max_kv, void* out, int64_t ldo, const void* gate, int64_t ldg,
                   int gate_head_stride, void* workspace, size_t workspace_bytes, void* stream);
 

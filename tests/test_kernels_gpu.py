@@ -158,11 +158,11 @@ def test_attention_row_invariance():
         assert torch.equal(one[0], full[r])
 
 
-@pytest.mark.parametrize("T,with_snap", [(16, True), (100, False)])
-def test_gdr_recurrence_matches_oracle(T, with_snap):
+@pytest.mark.parametrize("T,with_snap,B,Hk,Hv,D", [(16, True, 1, 16, 32, 128), (100, False, 1, 16, 32, 128),
+                                                   (16, True, 3, 2, 4, 64), (37, False, 2, 2, 4, 64)])
+def test_gdr_recurrence_matches_oracle(T, with_snap, B, Hk, Hv, D):
     from oracle import dflash_oracle as O
     ops = _ops()
-    B, Hk, Hv, D = 1, 16, 32, 128
     g = torch.Generator().manual_seed(1)
     q = torch.nn.functional.normalize(torch.randn(B, T, Hk, D, generator=g), dim=-1).bfloat16()
     k = torch.nn.functional.normalize(torch.randn(B, T, Hk, D, generator=g), dim=-1).bfloat16()
@@ -227,3 +227,112 @@ def test_gemm_sumsq_out_chain():
 def test_no_bounded_wait_gave_up():
     """After the kernels above no bounded device wait has expired."""
     assert _ops().device_error() == 0
+
+
+# ---------------------------------------------------------------------------
+# Qwen3.5 hybrid kernels
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("B,T,Hk,Hv,D", [(1, 16, 16, 48, 128), (3, 5, 2, 4, 64), (1, 128, 16, 48, 128)])
+def test_gdn_prep_matches_oracle(B, T, Hk, Hv, D):
+    from oracle import dflash_oracle as O
+    ops = _ops()
+    C = 2 * Hk * D + Hv * D
+    vd = Hv * D
+    ld = C + vd + 2 * Hv + 7  # row stride wider than the packed columns
+    proj = _rand((B * T, ld), 1.0, 30)
+    conv_w = _rand((C, 4), 0.3, 31)
+    A_log = torch.log(torch.linspace(1.0, 16.0, Hv))
+    dt_bias = torch.rand(Hv, generator=torch.Generator().manual_seed(32)) + 0.5
+    conv_state = _rand((B, 3, C), 1.0, 33)
+    window = torch.zeros((B, 3 + T + 4, C), dtype=torch.bfloat16, device=DEV)
+    got = ops.gdn_prep(proj.to(DEV), conv_w.to(DEV), A_log.to(DEV), dt_bias.to(DEV), conv_state.to(DEV), B, T, Hk,
+                       Hv, D, D, window=window)
+    for b in range(B):
+        rows = proj[b * T:(b + 1) * T]
+        win = torch.cat([conv_state[b], rows[:, :C]], 0).float()
+        q, k, v = O.gdn_conv_qkv(win, conv_w, Hk, Hv, D, D)
+        g, beta = O.gdn_gates(rows[:, C + vd + Hv:C + vd + 2 * Hv], rows[:, C + vd:C + vd + Hv], A_log, dt_bias)
+        sl = slice(b * T, (b + 1) * T)
+        # one bf16 ulp where the conv sum lands on a rounding boundary
+        for name, ref in (("q", q), ("k", k), ("v", v)):
+            d = (got[name][sl].float().cpu() - ref).abs()
+            assert d.max().item() <= 2 ** -7 * ref.abs().max().item(), name
+            assert (d > 0).float().mean().item() < 0.01, name
+        torch.testing.assert_close(got["g"][sl].cpu(), g, rtol=1e-5, atol=1e-6)
+        torch.testing.assert_close(got["beta"][sl].cpu(), beta, rtol=1e-5, atol=1e-6)
+        assert torch.equal(window[b, :3 + T].cpu(), win.bfloat16())
+
+
+def test_gdn_rollback_copies_snapshot_and_conv_rows():
+    ops = _ops()
+    B, T, Hv, D, C = 3, 16, 4, 32, 96
+    S = Hv * D * D
+    snaps = torch.randn(B, T, Hv, D, D, device=DEV)
+    state = torch.zeros(B, Hv, D, D, device=DEV)
+    conv = torch.zeros(B, 3, C, dtype=torch.bfloat16, device=DEV)
+    window = _rand((B, 3 + T + 2, C), 1.0, 34).to(DEV)
+    acc_host = torch.tensor([[1] + [0] * 15, [7] + [0] * 15, [16] + [0] * 15], dtype=torch.int32)
+    ops.gdn_rollback(state, snaps, conv, window, acc_host.to(DEV), 16, B, T, Hv, D, D, C)
+    for b, a in enumerate((1, 7, 16)):
+        assert torch.equal(state[b], snaps[b, a - 1])
+        assert torch.equal(conv[b], window[b, a:a + 3])
+    assert S == state[0].numel()
+
+
+@pytest.mark.parametrize("M,H,D", [(16, 48, 128), (5, 4, 64)])
+def test_gated_rmsnorm_matches_oracle(M, H, D):
+    from oracle import dflash_oracle as O
+    ops = _ops()
+    o = _rand((M, H * D), 1.0, 35)
+    z = _rand((M, H * D + 64), 1.0, 36)[:, 32:32 + H * D]  # strided view
+    w = _rand((D,), 1.0, 37)
+    got = ops.gated_rmsnorm(o.to(DEV), z.to(DEV), w.to(DEV), H, D, 1e-6).float().cpu()
+    ref = O.gated_rms_norm(o.float().reshape(M, H, D), z.float().reshape(M, H, D), w, 1e-6).reshape(M, H * D)
+    d = (got - ref).abs()
+    assert d.max().item() <= 2 ** -7 * ref.abs().max().item()
+    assert (d > 0).float().mean().item() < 0.01
+
+
+@pytest.mark.parametrize("L", [40, 1000])
+def test_attention_hd256_gated_matches_oracle(L):
+    """Qwen3.5 full attention: head_dim 256, output gate sigmoid(gate) applied in the
+    combine, gate read from the interleaved [q | gate] q_proj rows."""
+    from oracle import dflash_oracle as O
+    ops = _ops()
+    M, Hq, Hkv, hd, cap = 16, 24, 4, 256, 1024
+    qg = _rand((M, Hq, 2 * hd), 1.0, 38)
+    q = qg[:, :, :hd].contiguous()
+    kc = _rand((1, Hkv, cap, hd), 1.0, 39)
+    vc = _rand((1, Hkv, cap, hd), 1.0, 40)
+    pos = torch.arange(L - M, L, dtype=torch.int32)
+    qg_d = qg.reshape(M, Hq * 2 * hd).to(DEV)
+    out = ops.attention(q.to(DEV), kc.to(DEV), vc.to(DEV), pos.to(DEV), True, max_kv=cap, gate=qg_d[:, hd:],
+                        gate_head_stride=2 * hd).float().cpu()
+    ref = O.attention(q.float(), kc[0].float(), vc[0].float(), [int(p) + 1 for p in pos], 1 / math.sqrt(hd))
+    ref = O.bf16(ref * O.bf16(torch.sigmoid(qg[:, :, hd:].reshape(M, Hq * hd).float())))
+    assert (out - ref).abs().max().item() < 2e-2
+    plain = ops.attention(q.to(DEV), kc.to(DEV), vc.to(DEV), pos.to(DEV), True, max_kv=cap).float().cpu()
+    ref_plain = O.attention(q.float(), kc[0].float(), vc[0].float(), [int(p) + 1 for p in pos], 1 / math.sqrt(hd))
+    assert (plain - ref_plain).abs().max().item() < 2e-2
+
+
+@pytest.mark.parametrize("rows,seq_rows_arg", [(8, 8), (5, 5), (3, 0), (16, 16), (1, 1)])
+def test_attention_batched_sequences_share_tiles(rows, seq_rows_arg):
+    """Several sequences' verify rows inside one 16-row tile each read their own cache."""
+    from oracle import dflash_oracle as O
+    ops = _ops()
+    B, Hq, Hkv, hd, cap = 7, 8, 2, 128, 256
+    q = _rand((B * rows, Hq, hd), 1.0, 41)
+    kc = _rand((B, Hkv, cap, hd), 1.0, 42)
+    vc = _rand((B, Hkv, cap, hd), 1.0, 43)
+    starts = [17 + 29 * b for b in range(B)]
+    pos = torch.tensor([starts[b] + i for b in range(B) for i in range(rows)], dtype=torch.int32)
+    row_seq = torch.arange(B * rows, dtype=torch.int32) // rows
+    out = ops.attention(q.to(DEV), kc.to(DEV), vc.to(DEV), pos.to(DEV), True, max_kv=cap, row_seq=row_seq.to(DEV),
+                        seq_rows=seq_rows_arg).float().cpu()
+    for b in range(B):
+        sl = slice(b * rows, (b + 1) * rows)
+        ref = O.attention(q[sl].float(), kc[b].float(), vc[b].float(), [int(p) + 1 for p in pos[sl]],
+                          1 / math.sqrt(hd))
+        assert (out[sl] - ref).abs().max().item() < 2e-2, b
+    assert ops.device_error() == 0

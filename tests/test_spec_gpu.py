@@ -128,3 +128,27 @@ def test_qwen3_4b_layer_logits_parity():
     print(f"greedy-token agreement {agree:.3f}")
     assert agree >= 0.95
     assert (taps.float().cpu() - ref_taps).abs().max().item() <= 2e-2 * ref_taps.abs().max().item()
+
+
+def test_tiny_batched_decode_equals_single_sequence():
+    """Sequences of different prompt lengths decoded together (plain and speculative,
+    several sequences per 16-row attention tile) each reproduce their own
+    single-sequence plain greedy decode."""
+    tcfg, dcfg, tw, dw, target, draft = _tiny()
+    from dflash_b200.runtime import SpecSession, S_FINISHED
+    g = torch.Generator().manual_seed(9)
+    prompts = [torch.randint(0, tcfg.vocab_size, (n,), generator=g).tolist() for n in (30, 57, 12, 41)]
+    max_new = 40
+    singles = [_run(target, None, p, max_new, 1)[0] for p in prompts]
+    for bs, dr in ((1, None), (dcfg.block_size, draft)):
+        for graph in (False, True):
+            sess = SpecSession(target, dr, len(prompts), max(len(p) for p in prompts) + max_new, bs, set(),
+                               use_graph=graph)
+            sess.prefill(prompts, max_new)
+            for _ in range(max_new + 1):
+                if bool(sess.state[:, S_FINISHED].all().item()):
+                    break
+                sess.step()
+            outs, _, _ = sess.outputs()
+            for b in range(len(prompts)):
+                assert outs[b] == singles[b], (bs, graph, b)

@@ -79,28 +79,35 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(AttnArgs a) {
   const int m0 = tile * 16;
 
   __shared__ int s_lim[16];
+  __shared__ int s_pos[16], s_rs[16];
   __shared__ int s_seq;
+  if (threadIdx.x < 16) {  // the tile's rows, loaded in parallel
+    const int m = m0 + threadIdx.x;
+    s_pos[threadIdx.x] = m < a.M ? a.pos[m] : -1;
+    s_rs[threadIdx.x] = (m < a.M && a.row_seq) ? a.row_seq[m] : 0;
+  }
+  __syncthreads();
   if (threadIdx.x == 0) {
     // the seg-th distinct sequence among the tile's live rows, in row order
-    int seqs[16];
-    int n = 0;
+    int n = 0, chosen = -1;
     for (int r = 0; r < 16; ++r) {
-      const int m = m0 + r;
-      if (m >= a.M || a.pos[m] < 0) continue;
-      const int sq = a.row_seq ? a.row_seq[m] : 0;
+      if (s_pos[r] < 0) continue;
       bool seen = false;
-      for (int j = 0; j < n; ++j) seen |= seqs[j] == sq;
-      if (!seen) seqs[n++] = sq;
+      for (int j = 0; j < r; ++j) seen |= s_pos[j] >= 0 && s_rs[j] == s_rs[r];
+      if (!seen) {
+        if (n == seg) chosen = s_rs[r];
+        ++n;
+      }
     }
     if (seg == 0 && n > a.segs && chunk == 0 && kvh == 0 && a.err) atomicCAS(a.err, 0, ATT_SITE_SEGMENTS);
-    s_seq = seg < n ? seqs[seg] : -1;
+    s_seq = chosen;
   }
   __syncthreads();
   if (s_seq < 0) return;
   if (threadIdx.x < 16) {
-    const int m = m0 + threadIdx.x;
-    const bool mine = m < a.M && (a.row_seq ? a.row_seq[m] : 0) == s_seq;
-    s_lim[threadIdx.x] = mine ? row_limit(a, m) : 0;
+    const int p = s_pos[threadIdx.x];
+    const bool mine = p >= 0 && s_rs[threadIdx.x] == s_seq;
+    s_lim[threadIdx.x] = !mine ? 0 : (a.causal ? p + 1 : a.kv_len[s_seq]);
   }
   __syncthreads();
   int lim_max = 0;
@@ -262,7 +269,10 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(AttnArgs a) {
   }
 }
 
-// Merge the chunk partials of one (row, head) in chunk order.
+// Merge the chunk partials of one (row, head) in chunk order. One warp per
+// (row, head): lane c holds chunk c's (max, sum) so the global max and the
+// denominator are warp reductions; the output accumulates chunk by chunk in
+// order, four chunks' loads in flight at a time.
 template <int HD>
 __global__ void attn_combine_kernel(AttnArgs a) {
   grid_dependency_launch_dependents();
@@ -274,25 +284,48 @@ __global__ void attn_combine_kernel(AttnArgs a) {
   const int lim = row_limit(a, m);
   if (lim <= 0) return;
   const int nch = min((lim + ATT_CH - 1) / ATT_CH, a.n_chunks);
-  float mmax = -INFINITY;
-  for (int c = 0; c < nch; ++c) {
-    const float2 ml = a.part_ml[((long long)c * a.M + m) * a.Hq + h];
-    mmax = fmaxf(mmax, ml.x);
-  }
-  const float mu = mmax == -INFINITY ? 0.f : mmax;
   constexpr int PER = HD / 32;
   float acc[PER];
 #pragma unroll
   for (int i = 0; i < PER; ++i) acc[i] = 0.f;
   float den = 0.f;
-  for (int c = 0; c < nch; ++c) {
-    const long long base = ((long long)c * a.M + m) * a.Hq + h;
-    const float2 ml = a.part_ml[base];
-    const float w = exp2f(ml.x - mu);
-    den += w * ml.y;
-    const float* po = a.part_o + base * HD;
+  // global max over all chunks
+  float mmax = -INFINITY;
+  for (int c = lane; c < nch; c += 32) mmax = fmaxf(mmax, a.part_ml[((long long)c * a.M + m) * a.Hq + h].x);
 #pragma unroll
-    for (int i = 0; i < PER; ++i) acc[i] += w * po[lane + 32 * i];
+  for (int o = 16; o > 0; o >>= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffffu, mmax, o));
+  const float mu = mmax == -INFINITY ? 0.f : mmax;
+  for (int c0 = 0; c0 < nch; c0 += 32) {
+    const int c = c0 + lane;
+    const float2 ml = c < nch ? a.part_ml[((long long)c * a.M + m) * a.Hq + h] : make_float2(-INFINITY, 0.f);
+    const float w = c < nch ? exp2f(ml.x - mu) : 0.f;
+    float dl = w * ml.y;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) dl += __shfl_xor_sync(0xffffffffu, dl, o);
+    den += dl;
+    const int n = min(32, nch - c0);
+    int j = 0;
+    for (; j + 4 <= n; j += 4) {
+      float v[4][PER];
+      float wj[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        wj[u] = __shfl_sync(0xffffffffu, w, j + u);
+        const float* po = a.part_o + (((long long)(c0 + j + u) * a.M + m) * a.Hq + h) * HD;
+#pragma unroll
+        for (int i = 0; i < PER; ++i) v[u][i] = po[lane + 32 * i];
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int i = 0; i < PER; ++i) acc[i] += wj[u] * v[u][i];
+    }
+    for (; j < n; ++j) {
+      const float wj = __shfl_sync(0xffffffffu, w, j);
+      const float* po = a.part_o + (((long long)(c0 + j) * a.M + m) * a.Hq + h) * HD;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) acc[i] += wj * po[lane + 32 * i];
+    }
   }
   const float inv = den > 0.f ? 1.f / den : 0.f;
   __nv_bfloat16* dst = a.out + (long long)m * a.ldo + (long long)h * HD;

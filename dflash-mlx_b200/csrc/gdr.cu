@@ -12,18 +12,24 @@
 // snapshots switched off it is the state replay of the reference's Metal kernel
 // gated_delta_state_update (adapters.py:30-87, 93-135).
 //
-// B200 design: one warp per value row, each lane holding Dk/32 fp32 state
-// elements in registers; the two dot products are warp-shuffle reductions. Key,
-// query, value, decay and beta of a 32-token tile are staged in shared memory
-// by the whole CTA. Optional per-token snapshots (the state after each token)
-// are written with 16-byte stores so that cache rollback to "after a tokens" is
-// a pointer choice instead of a replay.
+// B200 design: four lanes per value row, each holding Dk/4 fp32 state elements
+// in registers as float4 chunks interleaved across the four lanes (lane c owns
+// chunks c, c + 4, ...), so a warp advances 8 value rows per token and each dot
+// product is four independent FMA chains plus two shuffles inside the lane group.
+// Key, query, value, decay and beta of a 16-token tile are staged in shared
+// memory (keys and queries converted to fp32 once). Optional per-token snapshots
+// (the state after each token) are written with 16-byte stores so that cache
+// rollback to "after a tokens" is a pointer choice instead of a replay. Each
+// token's arithmetic is the same whatever T is, so a row advanced inside a
+// 16-token verify block and one advanced alone agree bit for bit.
 #include "common.cuh"
 
 namespace dfl {
 
-constexpr int GDR_ROWS = 4;  // value rows (warps) per CTA
-constexpr int GDR_TT = 32;   // tokens per staged tile
+constexpr int GDR_LPR = 4;                    // lanes per value row
+constexpr int GDR_WARPS = 2;                  // warps per CTA
+constexpr int GDR_ROWS = GDR_WARPS * 32 / GDR_LPR;  // value rows per CTA (16)
+constexpr int GDR_TT = 16;                    // tokens per staged tile
 
 struct GdrArgs {
   const __nv_bfloat16* q;
@@ -40,119 +46,128 @@ struct GdrArgs {
   int B, T, Hk, Hv, Dk, Dv;
 };
 
-// a lane's PER contiguous fp32 state values: float4 moves for PER % 4 == 0 (Dk 128),
-// float2 for PER == 2 (Dk 64)
-template <int PER>
-__device__ __forceinline__ void load_state(float (&s)[PER], const float* p) {
-  if constexpr (PER % 4 == 0) {
-#pragma unroll
-    for (int i = 0; i < PER / 4; ++i) {
-      const float4 f = reinterpret_cast<const float4*>(p)[i];
-      s[4 * i] = f.x;
-      s[4 * i + 1] = f.y;
-      s[4 * i + 2] = f.z;
-      s[4 * i + 3] = f.w;
-    }
-  } else {
-    static_assert(PER % 2 == 0, "state slice must be float2-aligned");
-#pragma unroll
-    for (int i = 0; i < PER / 2; ++i) {
-      const float2 f = reinterpret_cast<const float2*>(p)[i];
-      s[2 * i] = f.x;
-      s[2 * i + 1] = f.y;
-    }
-  }
-}
-
-template <int PER>
-__device__ __forceinline__ void store_state(float* p, const float (&s)[PER]) {
-  if constexpr (PER % 4 == 0) {
-#pragma unroll
-    for (int i = 0; i < PER / 4; ++i)
-      reinterpret_cast<float4*>(p)[i] = make_float4(s[4 * i], s[4 * i + 1], s[4 * i + 2], s[4 * i + 3]);
-  } else {
-#pragma unroll
-    for (int i = 0; i < PER / 2; ++i) reinterpret_cast<float2*>(p)[i] = make_float2(s[2 * i], s[2 * i + 1]);
-  }
+__device__ __forceinline__ float4 bf16x4_to_float4(uint2 r) {
+  return make_float4(__uint_as_float(r.x << 16), __uint_as_float(r.x & 0xffff0000u), __uint_as_float(r.y << 16),
+                     __uint_as_float(r.y & 0xffff0000u));
 }
 
 template <int DK>
-__global__ void __launch_bounds__(32 * GDR_ROWS) gdr_kernel(GdrArgs a) {
+__global__ void __launch_bounds__(32 * GDR_WARPS) gdr_kernel(GdrArgs a) {
   grid_dependency_launch_dependents();
   grid_dependency_wait();
-  constexpr int PER = DK / 32;
-  __shared__ __align__(16) __nv_bfloat16 sk[GDR_TT][DK];
-  __shared__ __align__(16) __nv_bfloat16 sq[GDR_TT][DK];
-  __shared__ float sv[GDR_TT][GDR_ROWS];
-  __shared__ float sg[GDR_TT], sb[GDR_TT];
+  constexpr int NCH = DK / 16;  // float4 chunks per lane
+  // double-buffered raw tiles: tile i + 1 streams in (cp.async) while tile i is consumed
+  __shared__ __align__(16) __nv_bfloat16 sk[2][GDR_TT][DK];
+  __shared__ __align__(16) __nv_bfloat16 sq[2][GDR_TT][DK];
+  __shared__ __align__(16) __nv_bfloat16 sv[2][GDR_TT][GDR_ROWS];
+  __shared__ __align__(16) float sg[2][GDR_TT], sb[2][GDR_TT];
 
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c = lane & (GDR_LPR - 1);
+  const int rloc = warp * (32 / GDR_LPR) + (lane / GDR_LPR);  // row inside the CTA
   const int b = blockIdx.z, h = blockIdx.y;
   const int row0 = blockIdx.x * GDR_ROWS;
-  const int row = row0 + warp;
+  const int row = row0 + rloc;
   const int hk = h / (a.Hv / a.Hk);
   const long long hstate = (long long)a.Dv * DK;
   const long long slot_elems = (long long)a.Hv * hstate;
+  const bool want_o = a.o != nullptr;
 
-  const float* sin = a.state_in + b * a.state_in_bstride + (a.state_slot ? (long long)a.state_slot[b] * slot_elems : 0) +
-                     h * hstate + (long long)row * DK;
-  float s[PER];
-  load_state<PER>(s, sin + lane * PER);
-
-  for (int t0 = 0; t0 < a.T; t0 += GDR_TT) {
+  auto stage = [&](int buf, int t0) {
     const int nt = min(GDR_TT, a.T - t0);
-    __syncthreads();
     for (int idx = threadIdx.x; idx < nt * (DK / 8); idx += blockDim.x) {
-      const int tt = idx / (DK / 8), c = idx % (DK / 8);
-      const long long off = (((long long)b * a.T + t0 + tt) * a.Hk + hk) * DK + c * 8;
-      *reinterpret_cast<uint4*>(&sk[tt][c * 8]) = *reinterpret_cast<const uint4*>(a.k + off);
-      if (a.o) *reinterpret_cast<uint4*>(&sq[tt][c * 8]) = *reinterpret_cast<const uint4*>(a.q + off);
+      const int tt = idx / (DK / 8), cc = idx % (DK / 8);
+      const long long off = (((long long)b * a.T + t0 + tt) * a.Hk + hk) * DK + cc * 8;
+      cp_async16(smem_u32(&sk[buf][tt][cc * 8]), a.k + off, 16);
+      if (want_o) cp_async16(smem_u32(&sq[buf][tt][cc * 8]), a.q + off, 16);
     }
-    for (int idx = threadIdx.x; idx < nt * GDR_ROWS; idx += blockDim.x) {
-      const int tt = idx / GDR_ROWS, r = idx % GDR_ROWS;
-      sv[tt][r] = bf2f(a.v[(((long long)b * a.T + t0 + tt) * a.Hv + h) * a.Dv + row0 + r]);
+    for (int idx = threadIdx.x; idx < nt * (GDR_ROWS / 8); idx += blockDim.x) {
+      const int tt = idx / (GDR_ROWS / 8), cc = idx % (GDR_ROWS / 8);
+      cp_async16(smem_u32(&sv[buf][tt][cc * 8]), a.v + (((long long)b * a.T + t0 + tt) * a.Hv + h) * a.Dv + row0 + cc * 8,
+                 16);
     }
     for (int tt = threadIdx.x; tt < nt; tt += blockDim.x) {
       const long long gi = ((long long)b * a.T + t0 + tt) * a.Hv + h;
-      sg[tt] = a.g[gi];
-      sb[tt] = a.beta[gi];
+      cp_async4(smem_u32(&sg[buf][tt]), a.g + gi);
+      cp_async4(smem_u32(&sb[buf][tt]), a.beta + gi);
     }
+  };
+
+  stage(0, 0);
+  cp_async_commit();
+
+  const float* sin = a.state_in + b * a.state_in_bstride + (a.state_slot ? (long long)a.state_slot[b] * slot_elems : 0) +
+                     h * hstate + (long long)row * DK;
+  float4 s[NCH];
+#pragma unroll
+  for (int j = 0; j < NCH; ++j) s[j] = reinterpret_cast<const float4*>(sin)[j * GDR_LPR + c];
+
+  int buf = 0;
+  for (int t0 = 0; t0 < a.T; t0 += GDR_TT, buf ^= 1) {
+    const int nt = min(GDR_TT, a.T - t0);
+    if (t0 + GDR_TT < a.T) stage(buf ^ 1, t0 + GDR_TT);
+    cp_async_commit();
+    cp_async_wait<1>();
     __syncthreads();
     for (int tt = 0; tt < nt; ++tt) {
-      float kf[PER];
-      {
-        const __nv_bfloat16* kp = &sk[tt][lane * PER];
+      const float gt = sg[buf][tt];
+      const uint2* kp = reinterpret_cast<const uint2*>(sk[buf][tt]);
+      float4 kf[NCH];
+      float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
 #pragma unroll
-        for (int i = 0; i < PER; ++i) kf[i] = bf2f(kp[i]);
+      for (int j = 0; j < NCH; ++j) {
+        kf[j] = bf16x4_to_float4(kp[j * GDR_LPR + c]);
+        s[j].x *= gt;
+        s[j].y *= gt;
+        s[j].z *= gt;
+        s[j].w *= gt;
+        p0 += s[j].x * kf[j].x;
+        p1 += s[j].y * kf[j].y;
+        p2 += s[j].z * kf[j].z;
+        p3 += s[j].w * kf[j].w;
       }
-      const float gt = sg[tt];
-      float kv = 0.f;
+      float kv = (p0 + p1) + (p2 + p3);
+      kv += __shfl_xor_sync(0xffffffffu, kv, 1);
+      kv += __shfl_xor_sync(0xffffffffu, kv, 2);
+      const float delta = (bf2f(sv[buf][tt][rloc]) - kv) * sb[buf][tt];
 #pragma unroll
-      for (int i = 0; i < PER; ++i) {
-        s[i] *= gt;
-        kv += s[i] * kf[i];
+      for (int j = 0; j < NCH; ++j) {
+        s[j].x += kf[j].x * delta;
+        s[j].y += kf[j].y * delta;
+        s[j].z += kf[j].z * delta;
+        s[j].w += kf[j].w * delta;
       }
-      kv = warp_sum(kv);
-      const float delta = (sv[tt][warp] - kv) * sb[tt];
-#pragma unroll
-      for (int i = 0; i < PER; ++i) s[i] += kf[i] * delta;
       const int t = t0 + tt;
-      if (a.o) {
-        const __nv_bfloat16* qp = &sq[tt][lane * PER];
-        float y = 0.f;
+      if (want_o) {
+        const uint2* qp = reinterpret_cast<const uint2*>(sq[buf][tt]);
+        float y0 = 0.f, y1 = 0.f, y2 = 0.f, y3 = 0.f;
 #pragma unroll
-        for (int i = 0; i < PER; ++i) y += s[i] * bf2f(qp[i]);
-        y = warp_sum(y);
-        if (lane == 0) a.o[(((long long)b * a.T + t) * a.Hv + h) * a.Dv + row] = f2bf(y);
+        for (int j = 0; j < NCH; ++j) {
+          const float4 qf = bf16x4_to_float4(qp[j * GDR_LPR + c]);
+          y0 += s[j].x * qf.x;
+          y1 += s[j].y * qf.y;
+          y2 += s[j].z * qf.z;
+          y3 += s[j].w * qf.w;
+        }
+        float y = (y0 + y1) + (y2 + y3);
+        y += __shfl_xor_sync(0xffffffffu, y, 1);
+        y += __shfl_xor_sync(0xffffffffu, y, 2);
+        if (c == 0) a.o[(((long long)b * a.T + t) * a.Hv + h) * a.Dv + row] = f2bf(y);
       }
       if (a.snap) {
-        store_state<PER>(a.snap + (((long long)b * a.T + t) * a.Hv + h) * hstate + (long long)row * DK + lane * PER,
-                         s);
+        float4* dst = reinterpret_cast<float4*>(a.snap + (((long long)b * a.T + t) * a.Hv + h) * hstate +
+                                                (long long)row * DK);
+#pragma unroll
+        for (int j = 0; j < NCH; ++j) dst[j * GDR_LPR + c] = s[j];
       }
     }
+    __syncthreads();  // the buffer just read is refilled two tiles later
   }
+  cp_async_wait<0>();
   if (a.state_out) {
-    store_state<PER>(a.state_out + ((long long)b * a.Hv + h) * hstate + (long long)row * DK + lane * PER, s);
+    float4* dst = reinterpret_cast<float4*>(a.state_out + ((long long)b * a.Hv + h) * hstate + (long long)row * DK);
+#pragma unroll
+    for (int j = 0; j < NCH; ++j) dst[j * GDR_LPR + c] = s[j];
   }
 }
 
@@ -171,6 +186,10 @@ extern "C" int dfl_gdr_recurrence(const void* q, const void* k, const void* v, c
   }
   if (Dk != 128 && Dk != 64) {
     set_error("dfl_gdr_recurrence: key head dim %d not supported (64, 128)", Dk);
+    return DFL_ERR_UNSUPPORTED;
+  }
+  if ((reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) | reinterpret_cast<uintptr_t>(q)) & 15) {
+    set_error("dfl_gdr_recurrence: q, k and v must be 16-byte aligned");
     return DFL_ERR_UNSUPPORTED;
   }
   if (Dv % GDR_ROWS) {
@@ -200,7 +219,7 @@ extern "C" int dfl_gdr_recurrence(const void* q, const void* k, const void* v, c
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(Dv / GDR_ROWS, Hv, B);
-  cfg.blockDim = dim3(32 * GDR_ROWS);
+  cfg.blockDim = dim3(32 * GDR_WARPS);
   cfg.stream = as_stream(stream);
   cfg.attrs = attr;
   cfg.numAttrs = 1;

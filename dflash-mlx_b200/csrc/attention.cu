@@ -9,7 +9,7 @@
 //           = kv_len[seq(m)]       (non-causal)
 //
 // Layout: q [M][Hq][hd] bf16, caches [seq][Hkv][cap][hd] bf16 (slot == position).
-// Work split: one CTA per (key chunk of DFL_ATTN_CHUNK keys, kv head, 16-token
+// Work split: one CTA per (key chunk of key_chunk keys, kv head, 16-token
 // tile, sequence segment of the tile); the rows of a tile that belong to the
 // segment's sequence are the CTA's rows (a batched verify block of fewer than
 // 16 rows per sequence puts several sequences in one tile, each read from its own
@@ -17,7 +17,12 @@
 // query heads sharing a kv head read each K/V tile once. Chunks are fixed
 // absolute key ranges and are merged in chunk order by a second kernel, so a
 // query row's result does not depend on the other rows or on keys it cannot
-// see (spec-verify rows and plain-decode rows agree bit for bit).
+// see (spec-verify rows and plain-decode rows agree bit for bit). The chunk size
+// is the caller's (DFL_ATTN_CHUNK by default): small chunks spread one sequence
+// over many SMs, large ones cut the partial-result traffic of batched verify.
+// When one chunk covers every row's keys the chunk kernel normalises and writes
+// the output itself (the merge of a single chunk is the identity) and no merge
+// kernel runs. K/V stream through a 3-stage cp.async ring (2 stages at head_dim 256).
 #include "common.cuh"
 #include "tma_util.cuh"
 
@@ -25,7 +30,6 @@ namespace dfl {
 
 constexpr int ATT_SITE_SEGMENTS = 301;  // a tile held more sequences than the launch's segments
 
-constexpr int ATT_CH = DFL_ATTN_CHUNK;  // keys per chunk
 constexpr int ATT_KB = 64;              // keys per shared-memory sub-block
 
 struct AttnArgs {
@@ -45,6 +49,8 @@ struct AttnArgs {
   int gate_hs;  // elements between consecutive heads' gates in a row
   int M, Hq, Hkv, G, causal, n_chunks;
   int segs;          // sequence segments per 16-row tile (grid z = tiles * segs)
+  int key_chunk;     // keys per chunk (multiple of 64)
+  int direct;        // one chunk: the chunk kernel writes the normalised output
   int* err;          // device error record
   float scale_log2;  // softmax scale * log2(e)
 };
@@ -64,14 +70,20 @@ __device__ __forceinline__ int row_limit(const AttnArgs& a, int m) {
 }
 
 template <int HD>
+__host__ __device__ constexpr int att_stages() {
+  return HD >= 256 ? 2 : 3;
+}
+
+template <int HD>
 __global__ void __launch_bounds__(256) attn_chunk_kernel(AttnArgs a) {
   grid_dependency_launch_dependents();
   grid_dependency_wait();
   constexpr int NC = HD / 8;  // 16-byte chunks per row
+  constexpr int ST = att_stages<HD>();
   extern __shared__ __align__(128) unsigned char smem_raw[];
   __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(smem_raw);  // [G][16][HD]
-  __nv_bfloat16* sK = sQ + a.G * 16 * HD;                           // [2][64][HD]
-  __nv_bfloat16* sV = sK + 2 * ATT_KB * HD;                          // [2][64][HD]
+  __nv_bfloat16* sK = sQ + a.G * 16 * HD;                           // [ST][64][HD]
+  __nv_bfloat16* sV = sK + ST * ATT_KB * HD;                         // [ST][64][HD]
 
   const int chunk = blockIdx.x, kvh = blockIdx.y, tile = blockIdx.z / a.segs, seg = blockIdx.z % a.segs;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -113,9 +125,9 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(AttnArgs a) {
   int lim_max = 0;
 #pragma unroll
   for (int r = 0; r < 16; ++r) lim_max = max(lim_max, s_lim[r]);
-  const int k_begin = chunk * ATT_CH;
+  const int k_begin = chunk * a.key_chunk;
   if (k_begin >= lim_max) return;
-  const int k_end = min(k_begin + ATT_CH, lim_max);
+  const int k_end = min(k_begin + a.key_chunk, lim_max);
 
   const __nv_bfloat16* Kb = a.k_cache + s_seq * a.seq_stride + kvh * a.head_stride;
   const __nv_bfloat16* Vb = a.v_cache + s_seq * a.seq_stride + kvh * a.head_stride;
@@ -140,8 +152,12 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(AttnArgs a) {
       cp_async16(smem_u32(sV + buf * ATT_KB * HD + att_swz<HD>(r, c)), Vb + off, ok ? 16 : 0);
     }
   };
-  load_kv(0, k_begin);
-  cp_async_commit();
+  // ring prologue: Q and the first ST - 1 key blocks
+#pragma unroll
+  for (int st = 0; st < ST - 1; ++st) {
+    if (k_begin + st * ATT_KB < k_end) load_kv(st, k_begin + st * ATT_KB);
+    cp_async_commit();
+  }
 
   const int g = lane >> 2, t = lane & 3;
   const int lim0 = s_lim[g], lim1 = s_lim[g + 8];
@@ -155,11 +171,15 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(AttnArgs a) {
   const __nv_bfloat16* myQ = sQ + warp * 16 * HD;
 
   int buf = 0;
-  for (int kb = k_begin; kb < k_end; kb += ATT_KB, buf ^= 1) {
-    if (kb + ATT_KB < k_end) load_kv(buf ^ 1, kb + ATT_KB);
-    cp_async_commit();
-    cp_async_wait<1>();
-    __syncthreads();
+  for (int kb = k_begin; kb < k_end; kb += ATT_KB) {
+    cp_async_wait<ST - 2>();
+    __syncthreads();  // block kb landed for every thread; the stage refilled below was consumed last iteration
+    {
+      const int nb = kb + (ST - 1) * ATT_KB;
+      const int nbuf = buf == 0 ? ST - 1 : buf - 1;
+      if (nb < k_end) load_kv(nbuf, nb);
+      cp_async_commit();
+    }
     const __nv_bfloat16* tK = sK + buf * ATT_KB * HD;
     const __nv_bfloat16* tV = sV + buf * ATT_KB * HD;
 
@@ -244,7 +264,7 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(AttnArgs a) {
         mma_bf16_16816(o[2 * dp + 1], pf, b2, b3);
       }
     }
-    __syncthreads();
+    buf = buf == ST - 1 ? 0 : buf + 1;
   }
   cp_async_wait<0>();
 
@@ -254,6 +274,30 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(AttnArgs a) {
   lrow[1] += __shfl_xor_sync(0xffffffffu, lrow[1], 2);
 
   const int h = kvh * a.G + warp;
+  if (a.direct) {
+    // single chunk: out = o / l (the merge of one chunk is the identity)
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int r = g + half * 8;
+      const int m = m0 + r;
+      if (m >= a.M || s_lim[r] <= 0) continue;
+      const float den = lrow[half];
+      const float inv = den > 0.f ? 1.f / den : 0.f;
+      __nv_bfloat16* dst = a.out + (long long)m * a.ldo + (long long)h * HD;
+      const __nv_bfloat16* gr = a.gate ? a.gate + (long long)m * a.ldg + (long long)h * a.gate_hs : nullptr;
+#pragma unroll
+      for (int j = 0; j < HD / 8; ++j) {
+        const int d = j * 8 + 2 * t;
+        float y0 = o[j][2 * half] * inv, y1 = o[j][2 * half + 1] * inv;
+        if (gr) {
+          y0 = round_bf16(y0) * round_bf16(1.f / (1.f + __expf(-bf2f(gr[d]))));
+          y1 = round_bf16(y1) * round_bf16(1.f / (1.f + __expf(-bf2f(gr[d + 1]))));
+        }
+        *reinterpret_cast<uint32_t*>(dst + d) = pack_bf16x2(y0, y1);
+      }
+    }
+    return;
+  }
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
     const int r = g + half * 8;
@@ -283,7 +327,7 @@ __global__ void attn_combine_kernel(AttnArgs a) {
   const int m = (int)(item / a.Hq), h = (int)(item % a.Hq);
   const int lim = row_limit(a, m);
   if (lim <= 0) return;
-  const int nch = min((lim + ATT_CH - 1) / ATT_CH, a.n_chunks);
+  const int nch = min((lim + a.key_chunk - 1) / a.key_chunk, a.n_chunks);
   constexpr int PER = HD / 32;
   float acc[PER];
 #pragma unroll
@@ -345,11 +389,17 @@ __global__ void attn_combine_kernel(AttnArgs a) {
 
 template <int HD>
 static int launch_attn(AttnArgs a, int n_tiles, cudaStream_t st) {
-  const size_t smem = (size_t)(a.G * 16 * HD + 4 * ATT_KB * HD) * 2;
-  static bool init = false;
-  if (!init) {
-    cudaFuncSetAttribute(attn_chunk_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-    init = true;
+  const size_t smem = (size_t)(a.G * 16 * HD + 2 * att_stages<HD>() * ATT_KB * HD) * 2;
+  static size_t opted[64] = {0};  // dynamic shared memory already opted in, per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && smem > opted[dev]) {
+    if (cudaFuncSetAttribute(attn_chunk_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
+        cudaSuccess) {
+      set_error("dfl_attention: cannot opt in to %zu bytes of shared memory", smem);
+      return DFL_ERR_UNSUPPORTED;
+    }
+    opted[dev] = smem;
   }
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -370,6 +420,7 @@ static int launch_attn(AttnArgs a, int n_tiles, cudaStream_t st) {
   cfg.gridDim = dim3((unsigned)((items + 7) / 8));
   cfg.blockDim = dim3(256);
   cfg.dynamicSmemBytes = 0;
+  if (a.direct) return DFL_OK;
   e = cudaLaunchKernelEx(&cfg, attn_combine_kernel<HD>, a);
   if (e != cudaSuccess) {
     set_error("dfl_attention: combine launch failed: %s", cudaGetErrorString(e));
@@ -382,9 +433,14 @@ static int launch_attn(AttnArgs a, int n_tiles, cudaStream_t st) {
 
 using namespace dfl;
 
-extern "C" size_t dfl_attention_workspace_bytes(int M, int Hq, int hd, int max_kv) {
+static int resolve_key_chunk(int key_chunk) { return key_chunk > 0 ? key_chunk : DFL_ATTN_CHUNK; }
+
+extern "C" size_t dfl_attention_workspace_bytes(int M, int Hq, int hd, int max_kv, int key_chunk) {
   if (M <= 0 || max_kv <= 0) return 0;
-  const size_t nch = (size_t)(max_kv + ATT_CH - 1) / ATT_CH;
+  key_chunk = resolve_key_chunk(key_chunk);
+  if (key_chunk % 64) return 0;
+  const size_t nch = (size_t)(max_kv + key_chunk - 1) / key_chunk;
+  if (nch <= 1) return 0;  // single chunk: no partials
   const size_t o = nch * M * Hq * hd * sizeof(float);
   const size_t ml = nch * M * Hq * sizeof(float2);
   return ((o + 255) & ~(size_t)255) + ml;
@@ -392,7 +448,8 @@ extern "C" size_t dfl_attention_workspace_bytes(int M, int Hq, int hd, int max_k
 
 extern "C" int dfl_attention(const void* q, const void* k_cache, const void* v_cache, int64_t seq_stride,
                              int64_t head_stride, const int32_t* pos, const int32_t* row_seq, const int32_t* kv_len,
-                             int seq_rows, int M, int Hq, int Hkv, int hd, int causal, float scale, int max_kv, void* out,
+                             int seq_rows, int M, int Hq, int Hkv, int hd, int causal, float scale, int max_kv,
+                             int key_chunk, void* out,
                              int64_t ldo, const void* gate, int64_t ldg, int gate_head_stride, void* workspace,
                              size_t workspace_bytes, void* stream) {
   if (M == 0) return DFL_OK;
@@ -409,8 +466,13 @@ extern "C" int dfl_attention(const void* q, const void* k_cache, const void* v_c
     set_error("dfl_attention: max_kv must be positive");
     return DFL_ERR_INVALID;
   }
-  const size_t need = dfl_attention_workspace_bytes(M, Hq, hd, max_kv);
-  if (!workspace || workspace_bytes < need) {
+  key_chunk = resolve_key_chunk(key_chunk);
+  if (key_chunk % 64) {
+    set_error("dfl_attention: key_chunk %d must be a multiple of 64", key_chunk);
+    return DFL_ERR_INVALID;
+  }
+  const size_t need = dfl_attention_workspace_bytes(M, Hq, hd, max_kv, key_chunk);
+  if (need && (!workspace || workspace_bytes < need)) {
     set_error("dfl_attention: workspace too small (%zu < %zu)", workspace_bytes, need);
     return DFL_ERR_WORKSPACE;
   }
@@ -423,7 +485,9 @@ extern "C" int dfl_attention(const void* q, const void* k_cache, const void* v_c
   a.pos = pos;
   a.row_seq = row_seq;
   a.kv_len = kv_len;
-  a.n_chunks = (max_kv + ATT_CH - 1) / ATT_CH;
+  a.key_chunk = key_chunk;
+  a.n_chunks = (max_kv + key_chunk - 1) / key_chunk;
+  a.direct = a.n_chunks == 1;
   const size_t o_bytes = (size_t)a.n_chunks * M * Hq * hd * sizeof(float);
   a.part_o = static_cast<float*>(workspace);
   a.part_ml = reinterpret_cast<float2*>(static_cast<char*>(workspace) + ((o_bytes + 255) & ~(size_t)255));

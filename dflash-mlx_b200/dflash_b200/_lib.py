@@ -44,9 +44,10 @@ SIGNATURES: dict[str, tuple] = {
     "dfl_qkv_rope_append": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                     c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_int, c_int,
                                     c_float, c_int, c_void_p]),
-    "dfl_attention_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
+    "dfl_attention_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
     "dfl_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int,
-                              c_int, c_int, c_int, c_int, c_int, c_float, c_int, c_void_p, c_int64, c_void_p, c_int64,
+                              c_int, c_int, c_int, c_int, c_int, c_float, c_int, c_int, c_void_p, c_int64, c_void_p,
+                              c_int64,
                               c_int, c_void_p, c_size_t, c_void_p]),
     "dfl_gdn_prep": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p,
                              c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,

@@ -181,7 +181,8 @@ class HybridTargetModel:
     def forward(self, tokens: torch.Tensor, pos: torch.Tensor, cache: HybridCache, max_kv: int,
                 layer_ids: list[int] | None = None, taps_out: torch.Tensor | None = None,
                 row_seq: torch.Tensor | None = None, head: str = "argmax", ws: ops.Workspace | None = None,
-                seqs: slice | None = None, verify: bool = True, T: int | None = None, seq_rows: int = 0):
+                seqs: slice | None = None, verify: bool = True, T: int | None = None, seq_rows: int = 0,
+                key_chunk: int = 0):
         """Block forward over M = B_s * T rows of sequences ``seqs`` (default: all, T = M / B).
         verify=True writes per-token snapshots + the conv window (a later dfl_gdn_rollback
         picks the accepted prefix); verify=False advances the GDN state in place (prefill)
@@ -208,7 +209,7 @@ class HybridTargetModel:
                 ops.qkv_rope_append(qkv, pos, lw["q_norm"], lw["k_norm"], self.inv_freq, kc, vc, Hq, Hkv, hd,
                                     c.rope_dim, eps, q_out=b["q"], row_seq=row_seq, q_stride=2 * hd)
                 ops.attention(b["q"], kc, vc, pos, causal=True, max_kv=max_kv, row_seq=row_seq, out=b["attn"],
-                              seq_rows=seq_rows or T,
+                              seq_rows=seq_rows or T, key_chunk=key_chunk,
                               ws=ws, gate=qkv[:, hd:], gate_head_stride=2 * hd)
                 ops.gemm(b["attn"], lw["w_o"], ops.EPI_RESIDUAL, residual=h, out=h, ws=ws, sumsq_out=ss)
             ops.gemm(h, lw["w_gu"], ops.EPI_SILU_MUL, out=b["act"], ws=ws, norm_w=lw["post_norm"], sumsq_in=ss,

@@ -119,7 +119,7 @@ def bench_gdr(timer: Timer, T: int, snapshots: bool):
                         "workload": f"B=1 T={T} Hk=16 Hv=32 D=128"})
 
 
-def bench_attention(timer: Timer, B: int, rows: int, ctxs: list[int], case: str):
+def bench_attention(timer: Timer, B: int, rows: int, ctxs: list[int], case: str, key_chunk: int = 0):
     Hq, Hkv, hd = 32, 8, 128
     cap = max(ctxs) + rows
     gen = torch.Generator(device="cuda").manual_seed(3)
@@ -133,14 +133,16 @@ def bench_attention(timer: Timer, B: int, rows: int, ctxs: list[int], case: str)
     ws = ops.Workspace(torch.device("cuda"))
 
     def run():
-        ops.attention(q, kc, vc, pos, True, max_kv=cap, row_seq=row_seq, out=out, ws=ws, seq_rows=rows)
+        ops.attention(q, kc, vc, pos, True, max_kv=cap, row_seq=row_seq, out=out, ws=ws, seq_rows=rows,
+                      key_chunk=key_chunk)
 
     sec = timer(run)
     kv = sum(c + rows for c in ctxs) * Hkv * hd * 2 * 2
     by = kv + q.numel() * 2 + out.numel() * 2
     return _line(case, "attn_chunk_kernel+attn_combine_kernel", sec, bytes_=by,
                  extra={"workload": f"B={B} rows={rows} Hq={Hq} Hkv={Hkv} hd={hd} ctx mean "
-                                    f"{sum(ctxs) / len(ctxs):.0f}", "kv_bytes": int(kv)})
+                                    f"{sum(ctxs) / len(ctxs):.0f}", "kv_bytes": int(kv),
+                        "key_chunk": key_chunk or 128})
 
 
 def bench_gemm_c4(timer: Timer, M: int = 1024):
@@ -163,6 +165,7 @@ def main(argv=None):
     ap.add_argument("--only", default="gdr,attn,gemm")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--key-chunk", type=int, default=0, help="attn_c4: one key chunk instead of the sweep")
     args = ap.parse_args(argv)
     sel = set(args.only.split(","))
     timer = Timer(args.iters, args.warmup)
@@ -175,7 +178,8 @@ def main(argv=None):
     if sel & {"attn", "attn_c4"}:
         g = torch.Generator().manual_seed(3)
         ctxs = torch.randint(512, 4097, (64,), generator=g).tolist()
-        bench_attention(timer, 64, 16, ctxs, "attn_c4")
+        for kc in ([args.key_chunk] if args.key_chunk else (128, 512, 1024, 4224)):
+            bench_attention(timer, 64, 16, ctxs, "attn_c4", key_chunk=kc)
     if "gemm" in sel:
         bench_gemm_c4(timer)
 

@@ -104,7 +104,7 @@ class TargetModel:
     def forward(self, tokens: torch.Tensor, pos: torch.Tensor, cache: KVCache, max_kv: int,
                 layer_ids: list[int] | None = None, taps_out: torch.Tensor | None = None,
                 row_seq: torch.Tensor | None = None, head: str = "argmax", ws: ops.Workspace | None = None,
-                seq_rows: int = 0):
+                seq_rows: int = 0, key_chunk: int = 0):
         """Block forward over M rows (tokens int32 [M] at positions pos [M]).
 
         Appends K/V at each row's position, writes the residual stream after each
@@ -133,7 +133,7 @@ class TargetModel:
             ops.qkv_rope_append(b["qkv"], pos, lw["q_norm"], lw["k_norm"], self.inv_freq, kc, vc, Hq, Hkv, hd,
                                 c.rope_dim, eps, q_out=b["q"], row_seq=row_seq)
             ops.attention(b["q"], kc, vc, pos, causal=True, max_kv=max_kv, row_seq=row_seq, out=b["attn"], ws=ws,
-                          seq_rows=seq_rows)
+                          seq_rows=seq_rows, key_chunk=key_chunk)
             ops.gemm(b["attn"], lw["w_o"], ops.EPI_RESIDUAL, residual=h, out=h, ws=ws, sumsq_out=ss)
             # post_attention_layernorm fused into the gate/up projection
             ops.gemm(h, lw["w_gu"], ops.EPI_SILU_MUL, out=b["act"], ws=ws, norm_w=lw["post_norm"], sumsq_in=ss,
@@ -278,7 +278,7 @@ class DraftModel:
 
     def forward_block(self, tokens: torch.Tensor, pos: torch.Tensor, cache: KVCache, kv_len: torch.Tensor,
                       max_kv: int, row_seq: torch.Tensor | None = None, head: str = "argmax",
-                      ws: ops.Workspace | None = None, seq_rows: int = 0):
+                      ws: ops.Workspace | None = None, seq_rows: int = 0, key_chunk: int = 0):
         """Block rows (the target embedding of [last, mask, ...] = the noise embedding,
         runtime.py:408-410) attend to the draft cache (context rows already ingested)
         plus the block itself; returns the lm_head argmax partials of the final-normed
@@ -297,7 +297,7 @@ class DraftModel:
             ops.qkv_rope_append(b["qkv"], pos, lw["q_norm"], lw["k_norm"], self.inv_freq, kc, vc, Hq, Hkv, hd, hd,
                                 eps, q_out=b["q"], row_seq=row_seq)
             ops.attention(b["q"], kc, vc, pos, causal=causal, max_kv=max_kv, kv_len=kv_len, row_seq=row_seq,
-                          seq_rows=seq_rows,
+                          seq_rows=seq_rows, key_chunk=key_chunk,
                           out=b["attn"], ws=ws)
             ops.gemm(b["attn"], lw["w_o"], ops.EPI_RESIDUAL, residual=h, out=h, ws=ws, sumsq_out=ss)
             ops.gemm(h, lw["w_gu"], ops.EPI_SILU_MUL, out=b["act"], ws=ws, norm_w=lw["post_norm"], sumsq_in=ss,

@@ -210,9 +210,11 @@ def qkv_rope_append(qkv: torch.Tensor, pos: torch.Tensor, q_norm: torch.Tensor, 
 def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, pos: torch.Tensor, causal: bool,
               max_kv: int, kv_len: torch.Tensor | None = None, row_seq: torch.Tensor | None = None,
               scale: float | None = None, out: torch.Tensor | None = None, ws: Workspace | None = None,
-              gate: torch.Tensor | None = None, gate_head_stride: int = 0, seq_rows: int = 0) -> torch.Tensor:
+              gate: torch.Tensor | None = None, gate_head_stride: int = 0, seq_rows: int = 0,
+              key_chunk: int = 0) -> torch.Tensor:
     """q [M, Hq, hd] against caches [seq, Hkv, cap, hd]; returns [M, Hq*hd] bf16.
-    seq_rows: rows per sequence when row_seq groups contiguous runs (0 = any layout)."""
+    seq_rows: rows per sequence when row_seq groups contiguous runs (0 = any layout).
+    key_chunk: keys per split (0 = the library default); results depend on it."""
     _need_cuda(q, k_cache, v_cache, pos, kv_len, row_seq, out)
     M, Hq, hd = q.shape
     Hkv = k_cache.shape[1]
@@ -221,10 +223,11 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, pos
     if out is None:
         out = torch.empty((M, Hq * hd), dtype=torch.bfloat16, device=q.device)
     ws = ws or workspace(q.device)
-    need = int(_lib.query("dfl_attention_workspace_bytes", M, Hq, hd, max_kv))
+    need = int(_lib.query("dfl_attention_workspace_bytes", M, Hq, hd, max_kv, int(key_chunk)))
     ws.ensure_attn(need)
     _lib.call("dfl_attention", _ptr(q), _ptr(k_cache), _ptr(v_cache), k_cache.stride(0), k_cache.stride(1),
-              _ptr(pos), _ptr(row_seq), _ptr(kv_len), int(seq_rows), M, Hq, Hkv, hd, int(causal), float(scale), int(max_kv),
+              _ptr(pos), _ptr(row_seq), _ptr(kv_len), int(seq_rows), M, Hq, Hkv, hd, int(causal), float(scale),
+              int(max_kv), int(key_chunk),
               _ptr(out), _row_stride(out), _ptr(gate), _row_stride(gate) if gate is not None else 0,
               int(gate_head_stride), _ptr(ws.attn), ws.attn.numel(), _stream())
     return out

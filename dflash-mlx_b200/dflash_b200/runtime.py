@@ -87,6 +87,9 @@ class SpecSession:
         tc = target.cfg
         B, bs = batch, block_size
         self.cap = max_total + 2 * bs + 1
+        # keys per attention split: fine splits spread one sequence over the SMs; a
+        # batch already fills them, and long splits cut the partial-result traffic
+        self.key_chunk = 128 if batch <= 4 else 1024
         self.out_cap = self.cap
         self.max_steps = max_steps or (max_total + 1)
         self.ws = ops.Workspace(self.dev)
@@ -131,7 +134,7 @@ class SpecSession:
             for N, K in nk:
                 gemm_need = max(gemm_need, int(q("dfl_gemm_workspace_bytes", M, N, K, 0)))
             attn_need = max(attn_need, int(q("dfl_attention_workspace_bytes", M, tc.num_attention_heads,
-                                               tc.head_dim, self.cap)))
+                                               tc.head_dim, self.cap, self.key_chunk)))
         self.ws.ensure_gemm(gemm_need)
         self.ws.ensure_attn(attn_need)
 
@@ -174,12 +177,13 @@ class SpecSession:
                     # recurrent layers advance in place over the chunk; conv state from the window
                     part = self.target.forward(toks[c0:c1], pos, self.tcache, max_kv=c1, layer_ids=self.layer_ids,
                                                taps_out=taps, row_seq=rs, ws=self.ws, seqs=slice(b, b + 1),
-                                               verify=False, T=n, seq_rows=n)
+                                               verify=False, T=n, seq_rows=n, key_chunk=self.key_chunk)
                     self.target.commit_prefill(self.tcache, slice(b, b + 1),
                                                torch.full((1,), n, dtype=torch.int32, device=dev), n)
                 else:
                     part = self.target.forward(toks[c0:c1], pos, self.tcache, max_kv=c1, layer_ids=self.layer_ids,
-                                               taps_out=taps, row_seq=rs, ws=self.ws, seq_rows=n)
+                                               taps_out=taps, row_seq=rs, ws=self.ws, seq_rows=n,
+                                               key_chunk=self.key_chunk)
                 last_part = part[n - 1:n]
                 if self.draft is not None:
                     self.draft.ingest_context(taps, pos, self.dcache, row_seq=rs, ws=self.ws)
@@ -214,14 +218,15 @@ class SpecSession:
             d = self.draft
             d.ingest_context(self.taps, self.dpos_ctx, self.dcache, row_seq=self.row_seq, ws=self.ws)
             part = d.forward_block(self.block, self.dpos_blk, self.dcache, self.dkv_len, self.cap,
-                                   row_seq=self.row_seq, ws=self.ws, seq_rows=bs)
+                                   row_seq=self.row_seq, ws=self.ws, seq_rows=bs, key_chunk=self.key_chunk)
             ops.draft_commit(self.state, part, self.block, bs, B, self.inject_tokens, self.inject_len,
                              self.inject_noise)
 
     def _verify_kernels(self) -> None:
         """Target verify forward + accept (parallel-replay, runtime.py:117-163)."""
         part = self.target.forward(self.block, self.tpos, self.tcache, max_kv=self.cap, layer_ids=self.layer_ids,
-                                   taps_out=self.taps, row_seq=self.row_seq, ws=self.ws, seq_rows=self.bs)
+                                   taps_out=self.taps, row_seq=self.row_seq, ws=self.ws, seq_rows=self.bs,
+                                   key_chunk=self.key_chunk)
         ops.verify_accept(self.state, part, self.block, self.bs, self.out_tokens, self.B,
                           stop_ids=self.stop_ids, n_stop=self.n_stop, accept_log=self.accept_log)
         if self.hybrid:

@@ -147,11 +147,14 @@ int dfl_qkv_rope_append(const void* qkv, int64_t ldqkv, int q_stride, const int3
  * seq_rows: with row_seq, each sequence's rows are contiguous runs of seq_rows
  * rows starting at multiples of seq_rows (a batched verify block); 0 = any
  * layout (slower launch). Rows of different sequences may share a 16-row tile;
- * a tile with more sequences than the layout allows sets device error 301. */
-size_t dfl_attention_workspace_bytes(int M, int Hq, int hd, int max_kv);
+ * a tile with more sequences than the layout allows sets device error 301.
+ * key_chunk (multiple of 64; 0 = DFL_ATTN_CHUNK): keys per split; a row's result
+ * depends on it, so runs to be compared bit for bit use the same value. One
+ * chunk covering max_kv needs no workspace and no merge launch. */
+size_t dfl_attention_workspace_bytes(int M, int Hq, int hd, int max_kv, int key_chunk);
 int dfl_attention(const void* q, const void* k_cache, const void* v_cache, int64_t seq_stride, int64_t head_stride,
                   const int32_t* pos, const int32_t* row_seq, const int32_t* kv_len, int seq_rows, int M, int Hq, int Hkv, int hd,
-                  int causal, float scale, int max_kv, void* out, int64_t ldo, const void* gate, int64_t ldg,
+                  int causal, float scale, int max_kv, int key_chunk, void* out, int64_t ldo, const void* gate, int64_t ldg,
                   int gate_head_stride, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---- speculative step control ---------------------------------------------

@@ -37,6 +37,6 @@ def test_host_side_argument_errors_are_reported(lib):
                   1e-6, None, None, 0, None)
     assert e.value.status == 1
     with pytest.raises(_lib.DFlashKernelError) as e:
-        _lib.call("dfl_attention", 1, 1, 1, 0, 0, 1, None, None, 0, 16, 32, 8, 96, 1, 1.0, 16, 1, 0, None, 0, 0, 1, 1 << 30,
+        _lib.call("dfl_attention", 1, 1, 1, 0, 0, 1, None, None, 0, 16, 32, 8, 96, 1, 1.0, 16, 0, 1, 0, None, 0, 0, 1, 1 << 30,
                   None)
     assert e.value.status == 2  # head_dim 96 unsupported

@@ -144,17 +144,20 @@ def test_attention_matches_oracle(hd, Hq, Hkv, causal, L):
     assert (out - ref).abs().max().item() < 2e-2
 
 
-def test_attention_row_invariance():
-    """A query row attends identically in a 16-row causal block and alone (plain decode)."""
+@pytest.mark.parametrize("key_chunk", [0, 1024])
+def test_attention_row_invariance(key_chunk):
+    """A query row attends identically in a 16-row causal block and alone (plain decode),
+    with many key splits and with one split covering every key."""
     ops = _ops()
     Hq, Hkv, hd, cap = 32, 8, 128, 1024
     kc = _rand((1, Hkv, cap, hd), 1.0, 23).to(DEV)
     vc = _rand((1, Hkv, cap, hd), 1.0, 24).to(DEV)
     q = _rand((16, Hq, hd), 1.0, 25).to(DEV)
     pos = torch.arange(500, 516, dtype=torch.int32, device=DEV)
-    full = ops.attention(q, kc, vc, pos, True, max_kv=cap)
+    full = ops.attention(q, kc, vc, pos, True, max_kv=cap, key_chunk=key_chunk)
     for r in (0, 9, 15):
-        one = ops.attention(q[r:r + 1].contiguous(), kc, vc, pos[r:r + 1].contiguous(), True, max_kv=r + 501)
+        one = ops.attention(q[r:r + 1].contiguous(), kc, vc, pos[r:r + 1].contiguous(), True, max_kv=r + 501,
+                            key_chunk=key_chunk)
         assert torch.equal(one[0], full[r])
 
 
@@ -293,8 +296,8 @@ def test_gated_rmsnorm_matches_oracle(M, H, D):
     assert (d > 0).float().mean().item() < 0.01
 
 
-@pytest.mark.parametrize("L", [40, 1000])
-def test_attention_hd256_gated_matches_oracle(L):
+@pytest.mark.parametrize("L,key_chunk", [(40, 0), (1000, 0), (1000, 2048), (1000, 256)])
+def test_attention_hd256_gated_matches_oracle(L, key_chunk):
     """Qwen3.5 full attention: head_dim 256, output gate sigmoid(gate) applied in the
     combine, gate read from the interleaved [q | gate] q_proj rows."""
     from oracle import dflash_oracle as O
@@ -307,7 +310,7 @@ def test_attention_hd256_gated_matches_oracle(L):
     pos = torch.arange(L - M, L, dtype=torch.int32)
     qg_d = qg.reshape(M, Hq * 2 * hd).to(DEV)
     out = ops.attention(q.to(DEV), kc.to(DEV), vc.to(DEV), pos.to(DEV), True, max_kv=cap, gate=qg_d[:, hd:],
-                        gate_head_stride=2 * hd).float().cpu()
+                        gate_head_stride=2 * hd, key_chunk=key_chunk).float().cpu()
     ref = O.attention(q.float(), kc[0].float(), vc[0].float(), [int(p) + 1 for p in pos], 1 / math.sqrt(hd))
     ref = O.bf16(ref * O.bf16(torch.sigmoid(qg[:, :, hd:].reshape(M, Hq * hd).float())))
     assert (out - ref).abs().max().item() < 2e-2
@@ -316,8 +319,9 @@ def test_attention_hd256_gated_matches_oracle(L):
     assert (plain - ref_plain).abs().max().item() < 2e-2
 
 
-@pytest.mark.parametrize("rows,seq_rows_arg", [(8, 8), (5, 5), (3, 0), (16, 16), (1, 1)])
-def test_attention_batched_sequences_share_tiles(rows, seq_rows_arg):
+@pytest.mark.parametrize("rows,seq_rows_arg,key_chunk", [(8, 8, 0), (5, 5, 0), (3, 0, 0), (16, 16, 0), (1, 1, 0),
+                                                        (16, 16, 1024), (5, 5, 192), (8, 8, 64)])
+def test_attention_batched_sequences_share_tiles(rows, seq_rows_arg, key_chunk):
     """Several sequences' verify rows inside one 16-row tile each read their own cache."""
     from oracle import dflash_oracle as O
     ops = _ops()
@@ -329,7 +333,7 @@ def test_attention_batched_sequences_share_tiles(rows, seq_rows_arg):
     pos = torch.tensor([starts[b] + i for b in range(B) for i in range(rows)], dtype=torch.int32)
     row_seq = torch.arange(B * rows, dtype=torch.int32) // rows
     out = ops.attention(q.to(DEV), kc.to(DEV), vc.to(DEV), pos.to(DEV), True, max_kv=cap, row_seq=row_seq.to(DEV),
-                        seq_rows=seq_rows_arg).float().cpu()
+                        seq_rows=seq_rows_arg, key_chunk=key_chunk).float().cpu()
     for b in range(B):
         sl = slice(b * rows, (b + 1) * rows)
         ref = O.attention(q[sl].float(), kc[b].float(), vc[b].float(), [int(p) + 1 for p in pos[sl]],

@@ -196,13 +196,12 @@ __device__ __forceinline__ int tc_unit_owner(long long u, long long U, int G) {
 }
 
 // Epilogue from registers: this thread owns column n (tile column c = q*32 + lane)
-// for the 16 rows of the tile; q is the thread's TMEM lane quadrant.
+// for the 16 rows m0 .. m0 + 15; q is the thread's TMEM lane quadrant.
 template <int EPI>
-__device__ __forceinline__ void tc_epilogue(const TcArgs& a, float* v, int mt, int nt, int q, int lane,
+__device__ __forceinline__ void tc_epilogue(const TcArgs& a, float* v, int m0, int nt, int q, int lane,
                                             float* xchg) {
   const int c = q * 32 + lane;
   const int n = nt * TC_NT + c;
-  const int m0 = mt * TC_BM;
   if constexpr (EPI == DFL_EPI_STORE || EPI == DFL_EPI_RESIDUAL) {
     const bool col_ok = n < a.N;
     if constexpr (EPI == DFL_EPI_RESIDUAL) {
@@ -509,7 +508,7 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
         }
         epi_sync();  // s_flag is rewritten by the next segment
       }
-      if (do_epi) tc_epilogue<EPI>(a, v, mt, nt, q, lane, xchg);
+      if (do_epi) tc_epilogue<EPI>(a, v, mt * TC_BM, nt, q, lane, xchg);
       if (do_epi && et == 0) TC_STAMP(11);
       (void)ew;
     }
@@ -724,7 +723,7 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
       if ((q % S) == r) {
         float v[TC_BM];
         cluster_reduce_col(red_s, q * 32 + lane, S, v);
-        tc_epilogue<EPI>(a, v, mt, nt, q, lane, nullptr);
+        tc_epilogue<EPI>(a, v, mt * TC_BM, nt, q, lane, nullptr);
       }
     }
   }
@@ -814,6 +813,318 @@ const CUtensorMap* tensor_map_2d_bf16(const void* base, uint64_t rows, uint64_t 
   if (g_maps->size() > 4096) g_maps->clear();
   auto res = g_maps->emplace(key, map);
   return &res.first->second;
+}
+
+// ---------------------------------------------------------------------------
+// Wide GEMM: the many-row form (batched verify, 64+ sequences x 16 rows).
+//
+// Same pre-tiled weight stream, instruction shape M = 128 weight rows x N = BN tokens
+// (BN <= 256, a multiple of 16) and the same epilogues, but every output tile
+// (128 weight rows x BN rows of X) is owned by one CTA that runs the whole K loop
+// into one TMEM accumulator: there is no split-K, so a row's result depends on K
+// order only (identical for any number of rows, any BN). Persistent: one CTA per
+// SM walks the tiles with the row tiles of one weight strip adjacent, so the CTAs
+// that read the same 16 KB weight unit run at the same time and share it in L2.
+// 4-stage ring of (16 KB weight unit + BN x 64 X tile), double-buffered accumulator
+// (2 x BN TMEM columns) so the epilogue of tile i overlaps the MMAs of tile i + 1.
+// The RMSNorm prologue, when requested, runs as a separate row kernel into the
+// workspace (xn = bf16(w * x * inv_rms), the fused prologue's formula).
+// ---------------------------------------------------------------------------
+constexpr int WG_BN_MAX = 256;
+constexpr int WG_MAX_STAGES = 8;
+constexpr int WG_RING_BYTES = 192 * 1024;  // weight + X stages; as many stages as fit (4 at BN 256)
+constexpr int WG_EPI_LD = TC_NT + 4;  // fp32 row pitch of the epilogue transpose tile
+constexpr int WG_OFF_EPI = WG_RING_BYTES;
+constexpr int WG_OFF_BAR = WG_OFF_EPI + TC_BM * WG_EPI_LD * 4;
+constexpr int WG_NBAR = 2 * WG_MAX_STAGES + 4;
+constexpr int WG_OFF_TMEM = WG_OFF_BAR + WG_NBAR * 8;
+constexpr int WG_SMEM = WG_OFF_TMEM + 16 + 1024;
+
+struct WgArgs {
+  TcArgs t;
+  int stages;   // ring depth: W stages at 0, X stages after them
+  int bn;       // tokens per tile
+  int m_tiles;  // row tiles of X
+  int tiles;    // n_tiles * m_tiles
+};
+
+// Wide-kernel epilogue for 16 rows m0 .. m0 + 15 of one 128-column tile. The TMEM
+// layout gives thread c the column c for all 16 rows; the values are transposed
+// through shared memory so that every global access is a 16-byte row segment
+// (thread et then owns row et / 8 and 16 consecutive columns, or 8 SiLU·up outputs).
+// Row sums of squares per 32 columns pair two threads' halves; argmax likewise,
+// ties to the lowest column.
+template <int EPI>
+__device__ __forceinline__ void wide_epilogue(const TcArgs& a, const float* v, int m0, int nt, int c, int et,
+                                              float* stile) {
+#pragma unroll
+  for (int t = 0; t < TC_BM; ++t) stile[t * WG_EPI_LD + c] = v[t];
+  epi_sync();
+  const int t = et >> 3, part = et & 7;
+  const int m = m0 + t;
+  const bool row_ok = m < a.M;
+  const float* src = stile + t * WG_EPI_LD;
+  if constexpr (EPI == DFL_EPI_SILU_MUL) {
+    // packed per 64 columns as [32 gate | 32 up]: outputs nt*64 + [8*part, 8*part + 8)
+    const int oc = part * 8, g = oc >> 5, j = oc & 31;
+    const int on = nt * 64 + oc;
+    if (row_ok && nt * TC_NT + g * 64 + j < a.N) {
+      uint32_t pk[4];
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        float r2[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const float gt = round_bf16(src[g * 64 + j + e + u]);
+          const float up = round_bf16(src[g * 64 + 32 + j + e + u]);
+          r2[u] = round_bf16(gt / (1.f + __expf(-gt))) * up;
+        }
+        pk[e / 2] = pack_bf16x2(r2[0], r2[1]);
+      }
+      *reinterpret_cast<uint4*>(a.y + (long long)m * a.ldy + on) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+    }
+  } else if constexpr (EPI == DFL_EPI_ARGMAX) {
+    const int n0 = nt * TC_NT + part * 16;
+    float best = -INFINITY;
+    int bidx = 0x7fffffff;
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const float val = n0 + e < a.N ? round_bf16(src[part * 16 + e]) : -INFINITY;
+      if (val > best) {  // strictly greater: the lowest column wins ties
+        best = val;
+        bidx = n0 + e < a.N ? n0 + e : bidx;
+      }
+    }
+    const float ob = __shfl_xor_sync(0xffffffffu, best, 1);
+    const int oi = __shfl_xor_sync(0xffffffffu, bidx, 1);
+    if (ob > best || (ob == best && oi < bidx)) {
+      best = ob;
+      bidx = oi;
+    }
+    const int grp = nt * 4 + (part >> 1);
+    if (row_ok && !(part & 1) && grp < a.n_groups)
+      a.argmax[(long long)m * a.n_groups + grp] = make_float2(best, __int_as_float(bidx));
+  } else {
+    const int n0 = nt * TC_NT + part * 16;
+    const bool ok = row_ok && n0 < a.N;
+    float y[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) y[e] = src[part * 16 + e];
+    if constexpr (EPI == DFL_EPI_RESIDUAL) {
+      uint4 r0 = make_uint4(0, 0, 0, 0), r1 = r0;
+      if (ok) {
+        const uint4* rp = reinterpret_cast<const uint4*>(a.res + (long long)m * a.ldr + n0);
+        r0 = rp[0];
+        r1 = rp[1];
+      }
+      const __nv_bfloat16* rb0 = reinterpret_cast<const __nv_bfloat16*>(&r0);
+      const __nv_bfloat16* rb1 = reinterpret_cast<const __nv_bfloat16*>(&r1);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        y[e] = bf2f(rb0[e]) + round_bf16(y[e]);
+        y[8 + e] = bf2f(rb1[e]) + round_bf16(y[8 + e]);
+      }
+    }
+    uint32_t pk[8];
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < 16; e += 2) {
+      pk[e / 2] = pack_bf16x2(y[e], y[e + 1]);
+      const float q0 = round_bf16(y[e]), q1 = round_bf16(y[e + 1]);
+      ss += q0 * q0 + q1 * q1;
+    }
+    if (ok) {
+      uint4* yp = reinterpret_cast<uint4*>(a.y + (long long)m * a.ldy + n0);
+      yp[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      yp[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+      if (a.y2) {
+        uint4* y2p = reinterpret_cast<uint4*>(a.y2 + (long long)m * a.ldy2 + n0);
+        y2p[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        y2p[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+      }
+    }
+    if (a.sumsq_out) {
+      ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+      const int grp = nt * 4 + (part >> 1);
+      if (row_ok && !(part & 1) && grp < a.n_groups) a.sumsq_out[(long long)m * a.n_groups + grp] = ss;
+    }
+  }
+  epi_sync();  // the transpose tile is rewritten by the next 16 rows
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(TC_THREADS, 1) gemm_wide_kernel(const __grid_constant__ CUtensorMap xmap, WgArgs w) {
+  const TcArgs& a = w.t;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  const int ST = w.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + WG_OFF_BAR);
+  uint64_t* empty = full + WG_MAX_STAGES;
+  uint64_t* accf = empty + WG_MAX_STAGES;  // [2]
+  uint64_t* acce = accf + 2;           // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + WG_OFF_TMEM);
+  float* stile = reinterpret_cast<float*>(smem + WG_OFF_EPI);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bn = w.bn;
+  const uint32_t x_bytes = (uint32_t)bn * TC_BK * 2;
+  unsigned char* xring = smem + ST * TC_W_BYTES;  // X stage s at xring + s * x_bytes (1024-aligned)
+  const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(TC_NT >> 4) << 24);
+  // this CTA's tiles: blockIdx.x, blockIdx.x + gridDim.x, ...
+  const int my_tiles = w.tiles > (int)blockIdx.x ? (w.tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const long long my_units = (long long)my_tiles * a.kb;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf[b], 1);
+      mbar_init(&acce[b], 4);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
+                 "n"(2 * WG_BN_MAX));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  grid_dependency_launch_dependents();
+
+  if (warp == 0) {
+    // ---------------- producer: weight units (bulk) + X tiles (TMA) ----------------
+    // stage / phase advance incrementally: no integer division on the issue path
+    if (lane == 0 && my_units > 0) {
+      const uint64_t pol_w = l2_policy_evict_normal();
+      const uint64_t pol_x = l2_policy_evict_last();
+      int s = 0;
+      uint32_t ph = 0;
+      long long i = 0;
+      bool ok = true;
+      bool waited_dep = false;
+      for (int tt = 0; tt < my_tiles && ok; ++tt) {
+        const int tl = (int)blockIdx.x + tt * (int)gridDim.x;
+        const int nt = tl / w.m_tiles, mt = tl % w.m_tiles;
+        const unsigned char* wsrc = a.wt + (long long)nt * a.kb * TC_W_BYTES;
+        for (int j = 0; j < a.kb; ++j, ++i) {
+          if (i >= ST && !mbar_wait(&empty[s], ph ^ 1u, 221, a.err)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&full[s], TC_W_BYTES + x_bytes);
+          bulk_load(smem + s * TC_W_BYTES, wsrc + (long long)j * TC_W_BYTES, TC_W_BYTES, &full[s], pol_w);
+          if (!waited_dep) {  // X is produced by the previous kernel; weights are not
+            grid_dependency_wait();
+            waited_dep = true;
+          }
+          tma_load_2d(&xmap, &full[s], xring + s * x_bytes, j * TC_BK, mt * bn, pol_x);
+          if (++s == ST) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // gave up: let the copies already in flight land before the CTA exits
+        const long long first = i > ST ? i - ST : 0;
+        for (long long k = first; k < i; ++k)
+          mbar_wait(&full[k % ST], (uint32_t)((k / ST) & 1), 229, a.err);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- MMA issuer: whole K loop of each tile into one accumulator ----------------
+    if (lane == 0 && my_units > 0) {
+      const uint32_t w0 = smem_u32(smem), x0 = smem_u32(xring);
+      int s = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int tt = 0; tt < my_tiles && ok; ++tt) {
+        const int buf = tt & 1;
+        if (!mbar_wait(&acce[buf], (uint32_t)((tt >> 1) & 1) ^ 1u, 222, a.err)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(buf * WG_BN_MAX);
+        for (int j = 0; j < a.kb; ++j) {
+          if (!mbar_wait(&full[s], ph, 223, a.err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = sw128_desc(w0 + s * TC_W_BYTES);
+          const uint64_t bd = sw128_desc(x0 + s * x_bytes);
+#pragma unroll
+          for (int kk = 0; kk < TC_BK / 16; ++kk)
+            tc_mma(d, ad + 2 * kk, bd + 2 * kk, idesc, (j == 0 && kk == 0) ? 0u : 1u);
+          tc_commit(&empty[s]);
+          if (++s == ST) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (ok) tc_commit(&accf[buf]);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue warps ----------------
+    const int q = warp & 3;
+    grid_dependency_wait();
+    for (int tt = 0; tt < my_tiles; ++tt) {
+      const int tl = (int)blockIdx.x + tt * (int)gridDim.x;
+      const int nt = tl / w.m_tiles, mt = tl % w.m_tiles;
+      const int buf = tt & 1;
+      if (!mbar_wait(&accf[buf], (uint32_t)((tt >> 1) & 1), 225, a.err)) break;
+      tc_fence_after();
+      for (int ch = 0; ch < bn / TC_BM; ++ch) {
+        const int m0 = mt * bn + ch * TC_BM;
+        if (m0 >= a.M) break;  // uniform over the four warps
+        float v[TC_BM];
+        tc_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * WG_BN_MAX + ch * TC_BM), v);
+        wide_epilogue<EPI>(a, v, m0, nt, q * 32 + lane, threadIdx.x - 32 * TC_EPI_WARP0, stile);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acce[buf]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "n"(2 * WG_BN_MAX));
+  }
+}
+
+// xn[m, k] = bf16(w[k] * x[m, k] * rsqrt(sum(parts[m]) / K + eps)): the RMSNorm prologue
+// of the wide GEMM, one warp per row (partials summed in order, as the fused form does)
+__global__ void norm_apply_kernel(const __nv_bfloat16* __restrict__ x, long long ldx, const __nv_bfloat16* __restrict__ w,
+                                  const float* __restrict__ parts, int n_parts, float eps, __nv_bfloat16* __restrict__ xn,
+                                  int M, int K) {
+  grid_dependency_launch_dependents();
+  grid_dependency_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m = blockIdx.x * (blockDim.x >> 5) + warp;
+  if (m >= M) return;
+  float ss = 0.f;
+  for (int p = 0; p < n_parts; ++p) ss += parts[(long long)m * n_parts + p];
+  const float inv = rsqrtf(ss / (float)K + eps);
+  const __nv_bfloat16* xr = x + (long long)m * ldx;
+  __nv_bfloat16* yr = xn + (long long)m * K;
+  for (int k = lane * 8; k < K; k += 32 * 8) {
+    uint4 xv = *reinterpret_cast<const uint4*>(xr + k);
+    const uint4 wv = *reinterpret_cast<const uint4*>(w + k);
+    __nv_bfloat16* xe = reinterpret_cast<__nv_bfloat16*>(&xv);
+    const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) xe[e] = f2bf(bf2f(we[e]) * (bf2f(xe[e]) * inv));
+    *reinterpret_cast<uint4*>(yr + k) = xv;
+  }
 }
 
 struct TcPlan {
@@ -996,6 +1307,164 @@ extern "C" int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w_packed, i
   }
   if (err != cudaSuccess) {
     set_error("dfl_gemm_bf16: launch failed: %s", cudaGetErrorString(err));
+    return DFL_ERR_CUDA;
+  }
+  return DFL_OK;
+}
+
+extern "C" size_t dfl_gemm_wide_workspace_bytes(int M, int K, int with_norm) {
+  if (M <= 0 || K <= 0 || !with_norm) return 0;
+  return ((size_t)M * K * 2 + 255) & ~(size_t)255;
+}
+
+extern "C" int dfl_gemm_bf16_wide(const void* x, int64_t ldx, const void* w_packed, int M, int N, int K, int epilogue,
+                                  const void* residual, int64_t ldr, void* y, int64_t ldy, void* y2, int64_t ldy2,
+                                  void* argmax_partials, const void* norm_w, const float* sumsq_in, int n_parts,
+                                  float eps, float* sumsq_out, void* workspace, size_t workspace_bytes, void* stream) {
+  if (M == 0) return DFL_OK;
+  const void* w = w_packed;
+  if (!x || !w || M < 0 || N <= 0 || K <= 0) {
+    set_error("dfl_gemm_bf16_wide: null pointer or bad shape M=%d N=%d K=%d", M, N, K);
+    return DFL_ERR_INVALID;
+  }
+  if (K % TC_BK || N % 32 || ldx % 8 || (reinterpret_cast<uintptr_t>(x) & 15) ||
+      (reinterpret_cast<uintptr_t>(w) & 15)) {
+    set_error("dfl_gemm_bf16_wide: needs K %% 64 == 0, N %% 32 == 0, 16-byte aligned x/w, ldx %% 8 == 0");
+    return DFL_ERR_UNSUPPORTED;
+  }
+  if (epilogue == DFL_EPI_ARGMAX ? !argmax_partials : !y) {
+    set_error("dfl_gemm_bf16_wide: missing output pointer");
+    return DFL_ERR_INVALID;
+  }
+  if (epilogue == DFL_EPI_RESIDUAL && !residual) {
+    set_error("dfl_gemm_bf16_wide: residual epilogue needs a residual pointer");
+    return DFL_ERR_INVALID;
+  }
+  if (epilogue == DFL_EPI_SILU_MUL && N % 64) {
+    set_error("dfl_gemm_bf16_wide: silu-mul epilogue needs N %% 64 == 0 (packed gate/up), N=%d", N);
+    return DFL_ERR_UNSUPPORTED;
+  }
+  // the epilogue moves 16-byte row segments of y / y2 / residual
+  const uintptr_t mis = reinterpret_cast<uintptr_t>(y) | reinterpret_cast<uintptr_t>(y2) |
+                        reinterpret_cast<uintptr_t>(residual);
+  if ((mis & 15) || ldy % 8 || (y2 && ldy2 % 8) || (residual && ldr % 8)) {
+    set_error("dfl_gemm_bf16_wide: y / y2 / residual must be 16-byte aligned with row strides %% 8 == 0");
+    return DFL_ERR_UNSUPPORTED;
+  }
+  if (norm_w && (!sumsq_in || n_parts != K / 32)) {
+    set_error("dfl_gemm_bf16_wide: the RMSNorm prologue needs K/32 sumsq_in partials");
+    return DFL_ERR_INVALID;
+  }
+  const size_t need = dfl_gemm_wide_workspace_bytes(M, K, norm_w != nullptr);
+  if (need && (!workspace || workspace_bytes < need)) {
+    set_error("dfl_gemm_bf16_wide: workspace too small (%zu < %zu bytes)", workspace_bytes, need);
+    return DFL_ERR_WORKSPACE;
+  }
+  cudaStream_t st = as_stream(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  const void* xs = x;
+  long long ldxs = ldx;
+  if (norm_w) {
+    cudaLaunchConfig_t nc = {};
+    nc.gridDim = dim3((M + 7) / 8);
+    nc.blockDim = dim3(256);
+    nc.stream = st;
+    nc.attrs = attr;
+    nc.numAttrs = 1;
+    __nv_bfloat16* xn = static_cast<__nv_bfloat16*>(workspace);
+    cudaError_t e = cudaLaunchKernelEx(&nc, norm_apply_kernel, static_cast<const __nv_bfloat16*>(x), (long long)ldx,
+                                       static_cast<const __nv_bfloat16*>(norm_w), sumsq_in, n_parts, eps, xn, M, K);
+    if (e != cudaSuccess) {
+      set_error("dfl_gemm_bf16_wide: norm launch failed: %s", cudaGetErrorString(e));
+      return DFL_ERR_CUDA;
+    }
+    xs = xn;
+    ldxs = K;
+  }
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  // tokens per tile: all rows up to 256; above that the width among 256 / 192 / 128
+  // with the least modelled time per SM: waves x (448 + width), the constant being the
+  // weight-unit share of a k-step measured on B200 (narrow tiles re-read W from L2)
+  const int n_tiles = (N + TC_NT - 1) / TC_NT;
+  int bn = M >= WG_BN_MAX ? WG_BN_MAX : (M + TC_BM - 1) / TC_BM * TC_BM;
+  if (M > WG_BN_MAX) {
+    long long best = -1;
+    for (int cand : {256, 192, 128}) {
+      const long long tiles = (long long)n_tiles * ((M + cand - 1) / cand);
+      const long long cost = (tiles + sms - 1) / sms * (448 + cand);
+      if (best < 0 || cost < best) {
+        best = cost;
+        bn = cand;
+      }
+    }
+  }
+  const CUtensorMap* xm = tensor_map_2d_bf16(xs, M, K, ldxs, bn, TC_BK);
+  if (!xm) return DFL_ERR_CUDA;
+  WgArgs wa;
+  TcArgs& a = wa.t;
+  a.wt = static_cast<const unsigned char*>(w);
+  a.res = static_cast<const __nv_bfloat16*>(residual);
+  a.ldr = ldr;
+  a.y = static_cast<__nv_bfloat16*>(y);
+  a.ldy = ldy;
+  a.y2 = static_cast<__nv_bfloat16*>(y2);
+  a.ldy2 = ldy2;
+  a.argmax = static_cast<float2*>(argmax_partials);
+  a.partial = nullptr;
+  a.counters = nullptr;
+  a.norm_w = nullptr;
+  a.sumsq_in = nullptr;
+  a.n_parts = 0;
+  a.eps = eps;
+  a.sumsq_out = sumsq_out;
+  a.err = device_error_word();
+  a.n_groups = N / 32;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.n_tiles = (N + TC_NT - 1) / TC_NT;
+  a.kb = K / TC_BK;
+  a.U1 = 0;
+  a.grid1 = 0;
+  wa.bn = bn;
+  wa.stages = WG_RING_BYTES / (TC_W_BYTES + bn * TC_BK * 2);
+  if (wa.stages > WG_MAX_STAGES) wa.stages = WG_MAX_STAGES;
+  wa.m_tiles = (M + bn - 1) / bn;
+  wa.tiles = a.n_tiles * wa.m_tiles;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(wa.tiles < sms ? wa.tiles : sms);
+  cfg.blockDim = dim3(TC_THREADS);
+  cfg.dynamicSmemBytes = WG_SMEM;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t err;
+  switch (epilogue) {
+#define DFL_LAUNCH_WIDE(E)                                                                                  \
+  case E: {                                                                                                 \
+    static bool init[64] = {false};                                                                         \
+    if (dev >= 0 && dev < 64 && !init[dev]) {                                                               \
+      cudaFuncSetAttribute(gemm_wide_kernel<E>, cudaFuncAttributeMaxDynamicSharedMemorySize, WG_SMEM);      \
+      init[dev] = true;                                                                                     \
+    }                                                                                                       \
+    err = cudaLaunchKernelEx(&cfg, gemm_wide_kernel<E>, *xm, wa);                                           \
+    break;                                                                                                  \
+  }
+    DFL_LAUNCH_WIDE(DFL_EPI_STORE)
+    DFL_LAUNCH_WIDE(DFL_EPI_RESIDUAL)
+    DFL_LAUNCH_WIDE(DFL_EPI_SILU_MUL)
+    DFL_LAUNCH_WIDE(DFL_EPI_ARGMAX)
+#undef DFL_LAUNCH_WIDE
+    default:
+      set_error("dfl_gemm_bf16_wide: unknown epilogue %d", epilogue);
+      return DFL_ERR_INVALID;
+  }
+  if (err != cudaSuccess) {
+    set_error("dfl_gemm_bf16_wide: launch failed: %s", cudaGetErrorString(err));
     return DFL_ERR_CUDA;
   }
   return DFL_OK;

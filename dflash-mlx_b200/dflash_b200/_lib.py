@@ -32,6 +32,10 @@ SIGNATURES: dict[str, tuple] = {
     "dfl_gemm_bf16": (c_int, [c_void_p, c_int64, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int64, c_void_p,
                               c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int, c_float, c_void_p,
                               c_void_p, c_size_t, c_void_p]),
+    "dfl_gemm_bf16_wide": (c_int, [c_void_p, c_int64, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int64,
+                                   c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int, c_float,
+                                   c_void_p, c_void_p, c_size_t, c_void_p]),
+    "dfl_gemm_wide_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
     "dfl_device_error": (c_int, [POINTER(c_int), c_int, c_void_p]),
     "dfl_packed_weight_bytes": (c_size_t, [c_int, c_int]),
     "dfl_gemm_noalloc_scratch_bytes": (c_size_t, []),

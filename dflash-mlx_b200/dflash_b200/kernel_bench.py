@@ -16,7 +16,8 @@ Cases (synthetic inputs, shapes and distributions of the BASELINE configs):
               sequential recurrence, reported against both roofs
   attn_c3     verify attention, 1 sequence x 16 rows, Qwen3-4B heads, context 1536
   attn_c4     batched verify attention, 64 sequences x 16 rows, contexts U[512, 4096]
-  gemm_c4     verify GEMMs at 1024 rows (64 sequences x 16): QKV, O, gate/up, down
+  gemm_c4     verify GEMMs at 1024 rows (64 sequences x 16): QKV, O, gate/up, down, lm_head
+              (wide form; "gemm_streaming" runs the M <= 16 form on the same shapes)
 """
 from __future__ import annotations
 
@@ -145,19 +146,48 @@ def bench_attention(timer: Timer, B: int, rows: int, ctxs: list[int], case: str,
                         "key_chunk": key_chunk or 128})
 
 
-def bench_gemm_c4(timer: Timer, M: int = 1024):
+def bench_gemm_c4(timer: Timer, M: int = 1024, wide: bool = True):
+    """The verify GEMMs at C4's 1024 rows; wide=True is the whole-K tile form batched
+    sessions use, wide=False the M <= 16 weight-streaming form for comparison."""
     H, I, Hq, Hkv, hd = 2560, 9728, 32, 8, 128
     gen = torch.Generator(device="cuda").manual_seed(3)
     res = []
-    for name, N, K in (("qkv", (Hq + 2 * Hkv) * hd, H), ("o", H, Hq * hd), ("gate_up", 2 * I, H), ("down", H, I)):
+    kern = "gemm_wide_kernel" if wide else "gemm_tc_kernel"
+    for name, N, K in (("qkv", (Hq + 2 * Hkv) * hd, H), ("o", H, Hq * hd), ("gate_up", 2 * I, H), ("down", H, I),
+                       ("lm_head", 151936, H)):
         w = ops.pack_weight((torch.randn((N, K), device="cuda", generator=gen) * 0.02).bfloat16())
         x = torch.randn((M, K), device="cuda", generator=gen).bfloat16()
         y = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
-        ws = ops.Workspace(torch.device("cuda"))
+        ws = ops.Workspace(torch.device("cuda"), wide=wide)
         sec = timer(lambda: ops.gemm(x, w, out=y, ws=ws))
-        res.append(_line(f"gemm_c4_{name}", "gemm_tc_kernel", sec, bytes_=N * K * 2 + M * K * 2 + M * N * 2,
-                         flops=2.0 * M * N * K, extra={"workload": f"M={M} N={N} K={K}"}))
+        res.append(_line(f"gemm_c4_{name}" + ("" if wide else "_streaming"), kern, sec,
+                         bytes_=N * K * 2 + M * K * 2 + M * N * 2, flops=2.0 * M * N * K,
+                         extra={"workload": f"M={M} N={N} K={K}"}))
+        del w, x, y
     return res
+
+
+def bench_verify_gemms(timer: Timer, M: int = 1024, wide: bool = True):
+    """The verify forward's own GEMM launches (fused RMSNorm prologues, residual / tap /
+    SiLU·up / argmax epilogues) for one Qwen3-4B layer plus the lm_head, at M rows."""
+    from .config import TargetConfig
+    from .model import TargetModel
+    from .weights import random_target_weights
+    cfg = TargetConfig(num_hidden_layers=1)
+    target = TargetModel(cfg, random_target_weights(cfg, 3, device="cuda"), "cuda")
+    ws = ops.Workspace(torch.device("cuda"), wide=wide)
+    b = target.buffers(M)
+    b["h"].normal_()
+    b["attn"].normal_()
+    b["act"].normal_()
+    b["ss"].fill_(float(cfg.hidden_size))
+    names = ["qkv+norm", "o+residual", "gate_up+norm+silu", "down+residual", "lm_head+norm+argmax"]
+    out = []
+    for (fn, by, fl), name in zip(target.verify_gemms(M, ws=ws), names):
+        sec = timer(fn)
+        out.append(_line(f"verify_{name}", "gemm_wide_kernel" if wide else "gemm_tc_kernel", sec, bytes_=by,
+                         flops=fl, extra={"workload": f"M={M}"}))
+    return out
 
 
 def main(argv=None):
@@ -182,6 +212,10 @@ def main(argv=None):
             bench_attention(timer, 64, 16, ctxs, "attn_c4", key_chunk=kc)
     if "gemm" in sel:
         bench_gemm_c4(timer)
+    if "verify" in sel:
+        bench_verify_gemms(timer)
+    if "gemm_streaming" in sel:
+        bench_gemm_c4(timer, wide=False)
 
 
 if __name__ == "__main__":

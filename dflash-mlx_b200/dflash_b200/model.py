@@ -151,8 +151,8 @@ class TargetModel:
                         sumsq_in=ss, eps=eps)
 
     def verify_gemms(self, M: int, ws: ops.Workspace | None = None) -> list[tuple]:
-        """The weight-streaming GEMM launches of one forward over M rows, as
-        (callable, algorithmic bytes) pairs on this model's buffers (roofline timing)."""
+        """The GEMM launches of one forward over M rows, as (callable, algorithmic bytes,
+        FLOPs) triples on this model's buffers (roofline timing)."""
         c = self.cfg
         b = self.buffers(M)
         h, ss, eps = b["h"], b["ss"], c.rms_norm_eps
@@ -162,22 +162,26 @@ class TargetModel:
         def nbytes(N, K, n_out, extra=0):
             return N * K * 2 + M * K * 2 + M * n_out * 2 + extra
 
+        def fl(N, K):
+            return 2 * M * N * K
+
         for lw in self.layers:
             Nq = lw["w_qkv"].shape[0]
             out.append((lambda lw=lw: ops.gemm(h, lw["w_qkv"], out=b["qkv"], ws=ws, norm_w=lw["in_norm"],
-                                               sumsq_in=ss, eps=eps), nbytes(Nq, H, Nq)))
+                                               sumsq_in=ss, eps=eps), nbytes(Nq, H, Nq), fl(Nq, H)))
             Ko = lw["w_o"].shape[1]
             out.append((lambda lw=lw: ops.gemm(b["attn"], lw["w_o"], ops.EPI_RESIDUAL, residual=h, out=h, ws=ws,
-                                               sumsq_out=ss), nbytes(H, Ko, H, M * H * 2)))
+                                               sumsq_out=ss), nbytes(H, Ko, H, M * H * 2), fl(H, Ko)))
             Ng = lw["w_gu"].shape[0]
             out.append((lambda lw=lw: ops.gemm(h, lw["w_gu"], ops.EPI_SILU_MUL, out=b["act"], ws=ws,
-                                               norm_w=lw["post_norm"], sumsq_in=ss, eps=eps), nbytes(Ng, H, Ng // 2)))
+                                               norm_w=lw["post_norm"], sumsq_in=ss, eps=eps), nbytes(Ng, H, Ng // 2),
+                        fl(Ng, H)))
             F = lw["w_down"].shape[1]
             out.append((lambda lw=lw: ops.gemm(b["act"], lw["w_down"], ops.EPI_RESIDUAL, residual=h, out=h, ws=ws,
-                                               sumsq_out=ss), nbytes(H, F, H, M * H * 2)))
+                                               sumsq_out=ss), nbytes(H, F, H, M * H * 2), fl(H, F)))
         V = self.lm_head_w.shape[0]
         out.append((lambda: ops.gemm(h, self.lm_head_w, ops.EPI_ARGMAX, argmax_partials=b["argmax"], ws=ws,
-                                     norm_w=self.norm_w, sumsq_in=ss, eps=eps), nbytes(V, H, 0)))
+                                     norm_w=self.norm_w, sumsq_in=ss, eps=eps), nbytes(V, H, 0), fl(V, H)))
         return out
 
 

@@ -41,12 +41,21 @@ class Workspace:
 
     The GEMM region starts zeroed and the kernels leave their arrival counters at
     zero, so it is reusable across launches and CUDA-graph replays on one stream.
+    ``wide`` selects the wide GEMM (whole-K tiles, for many rows) for every gemm()
+    issued with this workspace; its RMSNorm prologue output lives in ``wide_x``.
     """
 
-    def __init__(self, device: torch.device, gemm_bytes: int = 64 << 20, attn_bytes: int = 64 << 20):
+    def __init__(self, device: torch.device, gemm_bytes: int = 64 << 20, attn_bytes: int = 64 << 20,
+                 wide: bool = False):
         self.device = torch.device(device)
         self.gemm = torch.zeros(gemm_bytes, dtype=torch.uint8, device=self.device)
         self.attn = torch.empty(attn_bytes, dtype=torch.uint8, device=self.device)
+        self.wide = wide
+        self.wide_x = torch.empty(0, dtype=torch.uint8, device=self.device)
+
+    def ensure_wide(self, nbytes: int) -> None:
+        if nbytes > self.wide_x.numel():
+            self.wide_x = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
 
     def ensure_attn(self, nbytes: int) -> None:
         if nbytes > self.attn.numel():
@@ -121,8 +130,14 @@ def gemm(x: torch.Tensor, w: PackedWeight | torch.Tensor, epilogue: int = EPI_ST
         raise ValueError(f"gemm shape mismatch x{tuple(x.shape)} w{tuple(w.shape)}")
     ldx = _row_stride(x)
     ws = ws or workspace(x.device)
-    need = int(_lib.query("dfl_gemm_workspace_bytes", M, N, K, epilogue))
-    ws.ensure_gemm(need)
+    if ws.wide:
+        fn = "dfl_gemm_bf16_wide"
+        ws.ensure_wide(int(_lib.query("dfl_gemm_wide_workspace_bytes", M, K, int(norm_w is not None))))
+        scratch = ws.wide_x
+    else:
+        fn = "dfl_gemm_bf16"
+        ws.ensure_gemm(int(_lib.query("dfl_gemm_workspace_bytes", M, N, K, epilogue)))
+        scratch = ws.gemm
     n_parts = 0
     if norm_w is not None:
         if sumsq_in is None or sumsq_in.shape[0] < M or sumsq_in.dtype != torch.float32:
@@ -136,9 +151,9 @@ def gemm(x: torch.Tensor, w: PackedWeight | torch.Tensor, epilogue: int = EPI_ST
         ntiles = int(_lib.query("dfl_gemm_argmax_tiles", N))
         if argmax_partials is None:
             argmax_partials = torch.empty((M, ntiles, 2), dtype=torch.float32, device=x.device)
-        _lib.call("dfl_gemm_bf16", _ptr(x), ldx, _ptr(w), M, N, K, epilogue, None, 0, None, 0, None, 0,
+        _lib.call(fn, _ptr(x), ldx, _ptr(w), M, N, K, epilogue, None, 0, None, 0, None, 0,
                   _ptr(argmax_partials), _ptr(norm_w), _ptr(sumsq_in), n_parts, float(eps), None,
-                  _ptr(ws.gemm), ws.gemm.numel(), _stream())
+                  _ptr(scratch), scratch.numel(), _stream())
         return argmax_partials
     n_out = N // 2 if epilogue == EPI_SILU_MUL else N
     if out is None:
@@ -147,9 +162,9 @@ def gemm(x: torch.Tensor, w: PackedWeight | torch.Tensor, epilogue: int = EPI_ST
         raise ValueError("residual given without the residual epilogue")
     ldr = _row_stride(residual) if residual is not None else 0
     ldy2 = _row_stride(out2) if out2 is not None else 0
-    _lib.call("dfl_gemm_bf16", _ptr(x), ldx, _ptr(w), M, N, K, epilogue, _ptr(residual), ldr, _ptr(out),
+    _lib.call(fn, _ptr(x), ldx, _ptr(w), M, N, K, epilogue, _ptr(residual), ldr, _ptr(out),
               _row_stride(out), _ptr(out2), ldy2, None, _ptr(norm_w), _ptr(sumsq_in), n_parts, float(eps),
-              _ptr(sumsq_out), _ptr(ws.gemm), ws.gemm.numel(), _stream())
+              _ptr(sumsq_out), _ptr(scratch), scratch.numel(), _stream())
     return out
 
 

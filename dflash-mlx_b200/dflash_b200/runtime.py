@@ -92,7 +92,10 @@ class SpecSession:
         self.key_chunk = 128 if batch <= 4 else 1024
         self.out_cap = self.cap
         self.max_steps = max_steps or (max_total + 1)
-        self.ws = ops.Workspace(self.dev)
+        # many sequences: whole-K tensor-core tiles (compute-bound at 16+ x 16 verify rows)
+        # instead of the weight-streaming split-K GEMM. The choice depends on the batch
+        # only, so a batch's plain decode and its speculative decode use the same form.
+        self.ws = ops.Workspace(self.dev, wide=batch >= 16)
         dev = self.dev
         i32 = dict(dtype=torch.int32, device=dev)
         self.state = torch.zeros((B, STATE_INTS), **i32)
@@ -126,6 +129,7 @@ class SpecSession:
         q = ops._lib.query
         gemm_need = 0
         attn_need = 0
+        wide_need = 0
         shapes = [self.B * self.bs, self.prefill_chunk]
         nk = {(w.N, w.K) for w in _packed_weights(self.target)}
         if self.draft is not None:
@@ -133,10 +137,13 @@ class SpecSession:
         for M in shapes:
             for N, K in nk:
                 gemm_need = max(gemm_need, int(q("dfl_gemm_workspace_bytes", M, N, K, 0)))
+                wide_need = max(wide_need, int(q("dfl_gemm_wide_workspace_bytes", M, K, 1)))
             attn_need = max(attn_need, int(q("dfl_attention_workspace_bytes", M, tc.num_attention_heads,
                                                tc.head_dim, self.cap, self.key_chunk)))
         self.ws.ensure_gemm(gemm_need)
         self.ws.ensure_attn(attn_need)
+        if self.ws.wide:
+            self.ws.ensure_wide(wide_need)
 
     # ------------------------------------------------------------------
     def set_injection(self, trace: torch.Tensor, lengths: torch.Tensor, noise: torch.Tensor) -> None:

@@ -90,6 +90,19 @@ int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w_packed, int M, int N
                   void* argmax_partials, const void* norm_w, const float* sumsq_in, int n_parts, float eps,
                   float* sumsq_out, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Wide form of dfl_gemm_bf16 for many rows (batched verify: 64+ sequences x 16
+ * rows), same arguments and epilogues. Each 128-column x up-to-256-row output tile
+ * runs its whole K loop in one tensor-core accumulator (no split-K), so a row's
+ * result depends on K order only: identical for any M, but not bit-identical to
+ * dfl_gemm_bf16's (split-K) result, so runs compared bit for bit use one form.
+ * Compute-bound at large M. With norm_w the RMSNorm prologue runs as a row kernel
+ * into the workspace (dfl_gemm_wide_workspace_bytes bytes; none otherwise). */
+size_t dfl_gemm_wide_workspace_bytes(int M, int K, int with_norm);
+int dfl_gemm_bf16_wide(const void* x, int64_t ldx, const void* w_packed, int M, int N, int K, int epilogue,
+                       const void* residual, int64_t ldr, void* y, int64_t ldy, void* y2, int64_t ldy2,
+                       void* argmax_partials, const void* norm_w, const float* sumsq_in, int n_parts, float eps,
+                       float* sumsq_out, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Reads (and optionally clears) the device error record: non-zero when a kernel's
  * bounded wait gave up (the kernel returned instead of hanging). Synchronises
  * the given stream. */

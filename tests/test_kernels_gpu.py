@@ -340,3 +340,72 @@ def test_attention_batched_sequences_share_tiles(rows, seq_rows_arg, key_chunk):
                           1 / math.sqrt(hd))
         assert (out[sl] - ref).abs().max().item() < 2e-2, b
     assert ops.device_error() == 0
+
+
+# ---------------------------------------------------------------------------
+# Wide GEMM (whole-K tiles for many rows)
+# ---------------------------------------------------------------------------
+def _wide_ws():
+    from dflash_b200 import ops
+    return ops.Workspace(torch.device(DEV), wide=True)
+
+
+@pytest.mark.parametrize("M,N,K", [(1024, 6144, 2560), (1024, 2560, 9728), (300, 512, 256), (16, 1536, 2560),
+                                   (1000, 2560, 4096)])
+def test_wide_gemm_store_matches_fp32(M, N, K):
+    ops = _ops()
+    x = _rand((M, K), 1.0, 50)
+    w = _rand((N, K), 0.02, 51)
+    y = ops.gemm(x.to(DEV), w.to(DEV), ws=_wide_ws()).float().cpu()
+    ref = x.float() @ w.float().T
+    err = (y - ref).abs().max().item()
+    assert err <= 1e-2 * ref.abs().max().item() + 1e-3, err
+
+
+def test_wide_gemm_epilogues_and_norm():
+    """Residual + tap + sum-of-squares, SiLU·up and argmax epilogues, and the RMSNorm
+    prologue, in the wide form against the weight-streaming form's definitions."""
+    from oracle import dflash_oracle as O
+    from dflash_b200.weights import pack_gate_up
+    ops = _ops()
+    ws = _wide_ws()
+    M, H, I = 512, 2560, 9728
+    x = _rand((M, H), 1.0, 52).to(DEV)
+    res = _rand((M, H), 1.0, 53).to(DEV)
+    w = _rand((H, H), 0.02, 54).to(DEV)
+    tap = torch.empty((M, H), dtype=torch.bfloat16, device=DEV)
+    ss = torch.empty((M, H // 32), dtype=torch.float32, device=DEV)
+    y = ops.gemm(x, w, ops.EPI_RESIDUAL, residual=res, out2=tap, ws=ws, sumsq_out=ss)
+    ref = O.bf16(res.float().cpu() + O.bf16(x.float().cpu() @ w.float().cpu().T))
+    assert (y.float().cpu() - ref).abs().max().item() <= 2e-2 * ref.abs().max().item()
+    assert torch.equal(tap, y)
+    yf = y.float()
+    torch.testing.assert_close(ss, (yf * yf).reshape(M, H // 32, 32).sum(-1), rtol=1e-4, atol=1e-3)
+    # RMSNorm prologue from the sum-of-squares partials, into a SiLU·up projection
+    nw = _rand((H,), 1.0, 55).to(DEV)
+    g, u = _rand((I, H), 0.02, 56).to(DEV), _rand((I, H), 0.02, 57).to(DEV)
+    act = ops.gemm(y, pack_gate_up(g, u), ops.EPI_SILU_MUL, ws=ws, norm_w=nw, sumsq_in=ss, eps=1e-6)
+    xn = O.rms_norm(yf.cpu(), nw.cpu(), 1e-6)
+    gr, ur = O.bf16(xn @ g.float().cpu().T), O.bf16(xn @ u.float().cpu().T)
+    ref_act = O.silu_mul(gr, ur)
+    assert (act.float().cpu() - ref_act).abs().max().item() <= 3e-2 * ref_act.abs().max().item()
+    # argmax
+    V = 151936
+    wl = _rand((V, H), 0.02, 58).to(DEV)
+    part = ops.gemm(y[:64].contiguous(), wl, ops.EPI_ARGMAX, ws=ws)
+    got = ops.argmax_reduce(part).cpu()
+    logits = ops.gemm(y[:64].contiguous(), wl, ws=ws).float()
+    assert torch.equal(got, logits.argmax(-1).int().cpu())
+
+
+def test_wide_gemm_row_invariance():
+    """A row's wide-GEMM result is the same bits whatever M (and tile width) is."""
+    ops = _ops()
+    ws = _wide_ws()
+    x = _rand((1024, 2560), 1.0, 59).to(DEV)
+    w = ops.pack_weight(_rand((6144, 2560), 0.02, 60).to(DEV))
+    full = ops.gemm(x, w, ws=ws)
+    for M in (16, 64, 200, 256):
+        part = ops.gemm(x[:M].contiguous(), w, ws=ws)
+        assert torch.equal(part, full[:M]), M
+    assert ops.device_error() == 0

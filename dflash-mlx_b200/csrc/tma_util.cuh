@@ -53,7 +53,7 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
 }
 
-// 2-D tiled TMA load (no multicast) completing on an mbarrier, with an L2 cache hint.
+// 2-D tiled TMA load into this CTA's shared memory completing on an mbarrier, with an L2 cache hint.
 __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst, int c0, int c1,
                                             uint64_t policy) {
   asm volatile(

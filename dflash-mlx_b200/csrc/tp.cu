@@ -1,0 +1,232 @@
+// Tensor parallelism for the Qwen3.5-27B hybrid (the reference's Model.shard,
+// custom_qwen35_model.py:1286-1402: row-parallel out_proj / o_proj / down_proj
+// followed by an all-sum, custom_qwen35_model.py:810 and shard_linear
+// "sharded-to-all").
+//
+// B200 design: every rank's row-parallel GEMM writes its partial [M, H] bf16 into
+// its own slot of a peer-mapped buffer (CUDA IPC over NVLink / NVSwitch); one
+// kernel per all-sum then
+//   1. publishes "partial of call e ready" into every peer's flag array
+//      (system-scope release after a system fence),
+//   2. waits (bounded) until every peer has published e,
+//   3. reads the N partials of its row slice straight from peer memory and writes
+//      h <- bf16(h + bf16(sum over ranks in rank order, fp32)), the tap copy and the
+//      per-32-column sums of squares the next RMSNorm needs.
+// The reduction order is fixed (rank 0 .. N-1 per element), so every rank gets the
+// same bits and a row's result does not depend on how many rows the call carries
+// (the speculative step and plain decode agree bit for bit, which a library
+// all-reduce whose chunking follows the message size does not promise).
+// Partials are double-buffered by call parity: a rank passes call e's barrier only
+// after every peer finished call e - 1, so the buffer of call e - 2 is free again.
+// Waits are bounded: on expiry the kernel records site 401 in the device error
+// word and returns.
+#include "common.cuh"
+#include "tma_util.cuh"
+
+namespace dfl {
+
+constexpr int TP_MAX_RANKS = 8;
+constexpr int TP_SITE_WAIT = 401;
+
+struct TpArgs {
+  const __nv_bfloat16* parts[TP_MAX_RANKS];  // this call's partial slot on every rank (peer pointers)
+  int* flags[TP_MAX_RANKS];                  // every rank's flag array [TP_MAX_RANKS] (peer pointers)
+  int* epoch;                                // local call counter (advanced by the last CTA)
+  int* done;                                 // local CTA completion counter
+  int* err;
+  __nv_bfloat16* h;
+  long long ldh;
+  __nv_bfloat16* tap;
+  long long ldtap;
+  float* sumsq_out;  // [M][H/32]
+  int rank, n_ranks, M, H;
+};
+
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.s32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.s32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// one warp per (row, 256-column span): lane owns 8 consecutive columns
+__global__ void __launch_bounds__(256) tp_reduce_residual_kernel(TpArgs a) {
+  grid_dependency_launch_dependents();
+  grid_dependency_wait();
+  __shared__ int s_ok;
+  const int e = *a.epoch + 1;
+  if (threadIdx.x == 0) {
+    if (blockIdx.x == 0) {
+      __threadfence_system();  // this rank's partial (written by the previous kernel) before the flag
+      for (int j = 0; j < a.n_ranks; ++j) st_release_sys(a.flags[j] + a.rank, e);
+    }
+    // wait until every rank published call e
+    bool ok = true;
+    const long long t0 = clock64();
+    for (int j = 0; j < a.n_ranks && ok; ++j) {
+      while (ld_acquire_sys(a.flags[a.rank] + j) < e) {
+        if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
+          atomicCAS(a.err, 0, TP_SITE_WAIT);
+          ok = false;
+          break;
+        }
+      }
+    }
+    s_ok = ok;
+  }
+  __syncthreads();
+  if (s_ok) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int spans = a.H / 256;
+    const long long item = (long long)blockIdx.x * (blockDim.x >> 5) + warp;
+    for (long long it = item; it < (long long)a.M * spans; it += (long long)gridDim.x * (blockDim.x >> 5)) {
+      const int m = (int)(it / spans), c0 = (int)(it % spans) * 256 + lane * 8;
+      float acc[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+      for (int j = 0; j < a.n_ranks; ++j) {  // rank order: the same sum on every rank
+        const uint4 pv = __ldcg(reinterpret_cast<const uint4*>(a.parts[j] + (long long)m * a.H + c0));
+        const __nv_bfloat16* pb = reinterpret_cast<const __nv_bfloat16*>(&pv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] += bf2f(pb[i]);
+      }
+      __nv_bfloat16* hp = a.h + (long long)m * a.ldh + c0;
+      const uint4 hv = *reinterpret_cast<const uint4*>(hp);
+      const __nv_bfloat16* hb = reinterpret_cast<const __nv_bfloat16*>(&hv);
+      uint32_t pk[4];
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; i += 2) {
+        const float y0 = bf2f(hb[i]) + round_bf16(acc[i]);
+        const float y1 = bf2f(hb[i + 1]) + round_bf16(acc[i + 1]);
+        pk[i / 2] = pack_bf16x2(y0, y1);
+        const float q0 = round_bf16(y0), q1 = round_bf16(y1);
+        ss += q0 * q0 + q1 * q1;
+      }
+      const uint4 out = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      *reinterpret_cast<uint4*>(hp) = out;
+      if (a.tap) *reinterpret_cast<uint4*>(a.tap + (long long)m * a.ldtap + c0) = out;
+      if (a.sumsq_out) {  // four lanes cover one 32-column group
+        ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+        ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+        if ((lane & 3) == 0) a.sumsq_out[(long long)m * (a.H / 32) + c0 / 32] = ss;
+      }
+    }
+  }
+  // the last CTA advances the call counter for the next launch
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int prev = atomicAdd(a.done, 1);
+    if (prev == (int)gridDim.x - 1) {
+      *a.done = 0;
+      *a.epoch = e;
+    }
+  }
+}
+
+}  // namespace dfl
+
+using namespace dfl;
+
+extern "C" int dfl_tp_alloc(size_t bytes, void** ptr, unsigned char* ipc_handle_out) {
+  if (!ptr || !ipc_handle_out || bytes == 0) {
+    set_error("dfl_tp_alloc: bad arguments");
+    return DFL_ERR_INVALID;
+  }
+  cudaError_t e = cudaMalloc(ptr, bytes);
+  if (e == cudaSuccess) e = cudaMemset(*ptr, 0, bytes);
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, *ptr);
+  if (e == cudaSuccess) memcpy(ipc_handle_out, &h, sizeof(h));
+  if (e != cudaSuccess) {
+    set_error("dfl_tp_alloc: %s", cudaGetErrorString(e));
+    return DFL_ERR_CUDA;
+  }
+  return DFL_OK;
+}
+
+extern "C" int dfl_tp_open(const unsigned char* ipc_handle, void** ptr) {
+  if (!ipc_handle || !ptr) {
+    set_error("dfl_tp_open: bad arguments");
+    return DFL_ERR_INVALID;
+  }
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) {
+    set_error("dfl_tp_open: %s", cudaGetErrorString(e));
+    return DFL_ERR_CUDA;
+  }
+  return DFL_OK;
+}
+
+extern "C" int dfl_tp_close(void* peer_ptr) {
+  cudaError_t e = cudaIpcCloseMemHandle(peer_ptr);
+  if (e != cudaSuccess) {
+    set_error("dfl_tp_close: %s", cudaGetErrorString(e));
+    return DFL_ERR_CUDA;
+  }
+  return DFL_OK;
+}
+
+extern "C" int dfl_tp_free(void* ptr) {
+  cudaError_t e = cudaFree(ptr);
+  if (e != cudaSuccess) {
+    set_error("dfl_tp_free: %s", cudaGetErrorString(e));
+    return DFL_ERR_CUDA;
+  }
+  return DFL_OK;
+}
+
+extern "C" int dfl_tp_reduce_residual(const void* const* parts, int* const* flags, int* epoch, int* done, int rank,
+                                      int n_ranks, void* h, int64_t ldh, void* tap, int64_t ldtap, float* sumsq_out,
+                                      int M, int H, void* stream) {
+  if (M == 0) return DFL_OK;
+  if (!parts || !flags || !epoch || !done || !h || n_ranks < 1 || n_ranks > TP_MAX_RANKS || rank < 0 ||
+      rank >= n_ranks || M < 0 || H <= 0) {
+    set_error("dfl_tp_reduce_residual: bad arguments");
+    return DFL_ERR_INVALID;
+  }
+  if (H % 256 || ldh % 8 || (tap && ldtap % 8)) {
+    set_error("dfl_tp_reduce_residual: H must be a multiple of 256 and rows 16-byte aligned (H=%d)", H);
+    return DFL_ERR_UNSUPPORTED;
+  }
+  TpArgs a;
+  for (int j = 0; j < TP_MAX_RANKS; ++j) {
+    a.parts[j] = j < n_ranks ? static_cast<const __nv_bfloat16*>(parts[j]) : nullptr;
+    a.flags[j] = j < n_ranks ? flags[j] : nullptr;
+  }
+  a.epoch = epoch;
+  a.done = done;
+  a.err = device_error_word();
+  a.h = static_cast<__nv_bfloat16*>(h);
+  a.ldh = ldh;
+  a.tap = static_cast<__nv_bfloat16*>(tap);
+  a.ldtap = ldtap;
+  a.sumsq_out = sumsq_out;
+  a.rank = rank;
+  a.n_ranks = n_ranks;
+  a.M = M;
+  a.H = H;
+  const long long items = (long long)M * (H / 256);
+  int blocks = (int)((items + 7) / 8);
+  if (blocks > 148) blocks = 148;  // every CTA waits on the flags: keep the grid resident
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(blocks);
+  cfg.blockDim = dim3(256);
+  cfg.stream = as_stream(stream);
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, tp_reduce_residual_kernel, a);
+  if (e != cudaSuccess) {
+    set_error("dfl_tp_reduce_residual: launch failed: %s", cudaGetErrorString(e));
+    return DFL_ERR_CUDA;
+  }
+  return DFL_OK;
+}

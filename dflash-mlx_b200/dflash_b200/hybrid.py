@@ -52,9 +52,13 @@ class HybridTargetModel:
 
     has_recurrent_state = True
 
-    def __init__(self, cfg: TargetConfig, weights: dict, device="cuda"):
+    def __init__(self, cfg: TargetConfig, weights: dict, device="cuda", tp=None):
+        """``tp`` (a ``tp.TPComm``): tensor-parallel rank; ``cfg`` / ``weights`` are then
+        this rank's shard (``tp.shard_config`` / ``tp.shard_weights``) and each
+        row-parallel projection is followed by the peer-memory all-sum."""
         if cfg.model_type != "qwen3_5":
             raise ValueError("HybridTargetModel runs the qwen3_5 family")
+        self.tp = tp
         self.cfg = cfg
         self.device = torch.device(device)
         dev = self.device
@@ -176,7 +180,17 @@ class HybridTargetModel:
                                b["gbeta"].view(Bs, T, self.Hv), st, state_out=st, o=o.view(Bs, T, self.Hv, self.Dv))
         z = proj[:, self.C:self.C + self.vd]
         ops.gated_rmsnorm(b["go"], z, lw["gnorm"], self.Hv, self.Dv, eps, out=b["gon"])
-        ops.gemm(b["gon"], lw["w_out"], ops.EPI_RESIDUAL, residual=h, out=h, ws=ws, sumsq_out=ss)
+        self._row_parallel(b["gon"], lw["w_out"], h, ss, None, ws, parity=0)
+
+    def _row_parallel(self, x, w, h, ss, tap, ws, parity: int) -> None:
+        """h <- h + x @ w.T (out_proj / o_proj / down_proj): fused residual epilogue on one
+        GPU; with tensor parallelism this rank's partial, then the all-sum + residual."""
+        if self.tp is None:
+            ops.gemm(x, w, ops.EPI_RESIDUAL, residual=h, out=h, out2=tap, ws=ws, sumsq_out=ss)
+            return
+        M = x.shape[0]
+        ops.gemm(x, w, out=self.tp.partial(parity, M), ws=ws)
+        self.tp.reduce_residual(parity, h, tap, ss, M)
 
     def forward(self, tokens: torch.Tensor, pos: torch.Tensor, cache: HybridCache, max_kv: int,
                 layer_ids: list[int] | None = None, taps_out: torch.Tensor | None = None,
@@ -211,14 +225,14 @@ class HybridTargetModel:
                 ops.attention(b["q"], kc, vc, pos, causal=True, max_kv=max_kv, row_seq=row_seq, out=b["attn"],
                               seq_rows=seq_rows or T, key_chunk=key_chunk,
                               ws=ws, gate=qkv[:, hd:], gate_head_stride=2 * hd)
-                ops.gemm(b["attn"], lw["w_o"], ops.EPI_RESIDUAL, residual=h, out=h, ws=ws, sumsq_out=ss)
+                self._row_parallel(b["attn"], lw["w_o"], h, ss, None, ws, parity=0)
             ops.gemm(h, lw["w_gu"], ops.EPI_SILU_MUL, out=b["act"], ws=ws, norm_w=lw["post_norm"], sumsq_in=ss,
                      eps=eps)
             tap = None
             if l in tap_col and taps_out is not None:
                 i = tap_col[l]
                 tap = taps_out[:, i * H:(i + 1) * H]
-            ops.gemm(b["act"], lw["w_down"], ops.EPI_RESIDUAL, residual=h, out=h, out2=tap, ws=ws, sumsq_out=ss)
+            self._row_parallel(b["act"], lw["w_down"], h, ss, tap, ws, parity=1)
         if head == "hidden":
             return ops.rmsnorm(h, self.norm_w, eps, out=b["xn"])
         if head == "logits":

@@ -103,6 +103,28 @@ int dfl_gemm_bf16_wide(const void* x, int64_t ldx, const void* w_packed, int M, 
                        void* argmax_partials, const void* norm_w, const float* sumsq_in, int n_parts, float eps,
                        float* sumsq_out, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- tensor parallelism (Qwen3.5-27B, config 5) ------------------------------
+ * Replaces the all-sum after the row-parallel projections of the reference's
+ * sharded model (custom_qwen35_model.py:810 and shard_linear "sharded-to-all" at
+ * :1338, :1347, :1375; sharding at :1286-1402). Buffers are peer-mapped with CUDA
+ * IPC: dfl_tp_alloc (cudaMalloc + zero + 64-byte IPC handle), dfl_tp_open on the
+ * other ranks, dfl_tp_close / dfl_tp_free to release.
+ * dfl_tp_reduce_residual: parts[j] = rank j's partial [M, H] bf16 (row stride H)
+ * for this call; flags[j] = rank j's int flag array (one slot per rank);
+ * epoch / done = this rank's call counter and CTA counter (zeroed once). Sums the
+ * partials in rank order in fp32 and writes h <- bf16(h + bf16(sum)), tap (nullable)
+ * <- h, sumsq_out[M][H/32] (nullable). Partial slots must alternate between two
+ * buffers on consecutive calls. A wait that expires records device error 401.
+ * parts and flags are host arrays of n_ranks device pointers (copied into the
+ * launch, so a captured graph keeps them). */
+int dfl_tp_alloc(size_t bytes, void** ptr, unsigned char* ipc_handle_out);
+int dfl_tp_open(const unsigned char* ipc_handle, void** ptr);
+int dfl_tp_close(void* peer_ptr);
+int dfl_tp_free(void* ptr);
+int dfl_tp_reduce_residual(const void* const* parts, int* const* flags, int* epoch, int* done, int rank, int n_ranks,
+                           void* h, int64_t ldh, void* tap, int64_t ldtap, float* sumsq_out, int M, int H,
+                           void* stream);
+
 /* Reads (and optionally clears) the device error record: non-zero when a kernel's
  * bounded wait gave up (the kernel returned instead of hanging). Synchronises
  * the given stream. */

@@ -202,7 +202,12 @@ __device__ __forceinline__ void tc_epilogue(const TcArgs& a, float* v, int m0, i
                                             float* xchg) {
   const int c = q * 32 + lane;
   const int n = nt * TC_NT + c;
-  if constexpr (EPI == DFL_EPI_STORE || EPI == DFL_EPI_RESIDUAL) {
+  if constexpr (EPI == DFL_EPI_STORE_F32) {
+    float* yf = reinterpret_cast<float*>(a.y);
+#pragma unroll
+    for (int t = 0; t < TC_BM; ++t)
+      if (n < a.N && m0 + t < a.M) yf[(long long)(m0 + t) * a.ldy + n] = v[t];
+  } else if constexpr (EPI == DFL_EPI_STORE || EPI == DFL_EPI_RESIDUAL) {
     const bool col_ok = n < a.N;
     if constexpr (EPI == DFL_EPI_RESIDUAL) {
       // gather all 16 residual values before the first store: y may alias the residual
@@ -904,6 +909,15 @@ __device__ __forceinline__ void wide_epilogue(const TcArgs& a, const float* v, i
     const int grp = nt * 4 + (part >> 1);
     if (row_ok && !(part & 1) && grp < a.n_groups)
       a.argmax[(long long)m * a.n_groups + grp] = make_float2(best, __int_as_float(bidx));
+  } else if constexpr (EPI == DFL_EPI_STORE_F32) {
+    const int n0 = nt * TC_NT + part * 16;
+    if (row_ok && n0 < a.N) {
+      float4* yp = reinterpret_cast<float4*>(reinterpret_cast<float*>(a.y) + (long long)m * a.ldy + n0);
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        yp[e] = make_float4(src[part * 16 + 4 * e], src[part * 16 + 4 * e + 1], src[part * 16 + 4 * e + 2],
+                            src[part * 16 + 4 * e + 3]);
+    }
   } else {
     const int n0 = nt * TC_NT + part * 16;
     const bool ok = row_ok && n0 < a.N;
@@ -1300,6 +1314,7 @@ extern "C" int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w_packed, i
     DFL_LAUNCH(DFL_EPI_RESIDUAL)
     DFL_LAUNCH(DFL_EPI_SILU_MUL)
     DFL_LAUNCH(DFL_EPI_ARGMAX)
+    DFL_LAUNCH(DFL_EPI_STORE_F32)
 #undef DFL_LAUNCH
     default:
       set_error("dfl_gemm_bf16: unknown epilogue %d", epilogue);
@@ -1458,6 +1473,7 @@ extern "C" int dfl_gemm_bf16_wide(const void* x, int64_t ldx, const void* w_pack
     DFL_LAUNCH_WIDE(DFL_EPI_RESIDUAL)
     DFL_LAUNCH_WIDE(DFL_EPI_SILU_MUL)
     DFL_LAUNCH_WIDE(DFL_EPI_ARGMAX)
+    DFL_LAUNCH_WIDE(DFL_EPI_STORE_F32)
 #undef DFL_LAUNCH_WIDE
     default:
       set_error("dfl_gemm_bf16_wide: unknown epilogue %d", epilogue);

@@ -3,20 +3,21 @@
 // followed by an all-sum, custom_qwen35_model.py:810 and shard_linear
 // "sharded-to-all").
 //
-// B200 design: every rank's row-parallel GEMM writes its partial [M, H] bf16 into
+// B200 design: every rank's row-parallel GEMM writes its partial [M, H] fp32 into
 // its own slot of a peer-mapped buffer (CUDA IPC over NVLink / NVSwitch); one
 // kernel per all-sum then
 //   1. publishes "partial of call e ready" into every peer's flag array
 //      (system-scope release after a system fence),
 //   2. waits (bounded) until every peer has published e,
 //   3. reads the N partials of its row slice straight from peer memory and writes
-//      h <- bf16(h + bf16(sum over ranks in rank order, fp32)), the tap copy and the
+//      h <- bf16(h + bf16(sum over ranks in rank order)), the tap copy and the
 //      per-32-column sums of squares the next RMSNorm needs.
 // The reduction order is fixed (rank 0 .. N-1 per element), so every rank gets the
 // same bits and a row's result does not depend on how many rows the call carries
 // (the speculative step and plain decode agree bit for bit, which a library
 // all-reduce whose chunking follows the message size does not promise).
-// Partials are double-buffered by call parity: a rank passes call e's barrier only
+// Partials stay fp32 (the single-GPU path rounds once, after the full K sum; so does
+// this one, after the rank sum). Partials are double-buffered by call parity: a rank passes call e's barrier only
 // after every peer finished call e - 1, so the buffer of call e - 2 is free again.
 // Waits are bounded: on expiry the kernel records site 401 in the device error
 // word and returns.
@@ -29,7 +30,7 @@ constexpr int TP_MAX_RANKS = 8;
 constexpr int TP_SITE_WAIT = 401;
 
 struct TpArgs {
-  const __nv_bfloat16* parts[TP_MAX_RANKS];  // this call's partial slot on every rank (peer pointers)
+  const float* parts[TP_MAX_RANKS];  // this call's partial slot on every rank (peer pointers)
   int* flags[TP_MAX_RANKS];                  // every rank's flag array [TP_MAX_RANKS] (peer pointers)
   int* epoch;                                // local call counter (advanced by the last CTA)
   int* done;                                 // local CTA completion counter
@@ -87,10 +88,16 @@ __global__ void __launch_bounds__(256) tp_reduce_residual_kernel(TpArgs a) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] = 0.f;
       for (int j = 0; j < a.n_ranks; ++j) {  // rank order: the same sum on every rank
-        const uint4 pv = __ldcg(reinterpret_cast<const uint4*>(a.parts[j] + (long long)m * a.H + c0));
-        const __nv_bfloat16* pb = reinterpret_cast<const __nv_bfloat16*>(&pv);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] += bf2f(pb[i]);
+        const float4* pp = reinterpret_cast<const float4*>(a.parts[j] + (long long)m * a.H + c0);
+        const float4 p0 = __ldcg(pp), p1 = __ldcg(pp + 1);
+        acc[0] += p0.x;
+        acc[1] += p0.y;
+        acc[2] += p0.z;
+        acc[3] += p0.w;
+        acc[4] += p1.x;
+        acc[5] += p1.y;
+        acc[6] += p1.z;
+        acc[7] += p1.w;
       }
       __nv_bfloat16* hp = a.h + (long long)m * a.ldh + c0;
       const uint4 hv = *reinterpret_cast<const uint4*>(hp);
@@ -196,7 +203,7 @@ extern "C" int dfl_tp_reduce_residual(const void* const* parts, int* const* flag
   }
   TpArgs a;
   for (int j = 0; j < TP_MAX_RANKS; ++j) {
-    a.parts[j] = j < n_ranks ? static_cast<const __nv_bfloat16*>(parts[j]) : nullptr;
+    a.parts[j] = j < n_ranks ? static_cast<const float*>(parts[j]) : nullptr;
     a.flags[j] = j < n_ranks ? flags[j] : nullptr;
   }
   a.epoch = epoch;

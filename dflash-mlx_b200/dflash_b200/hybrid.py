@@ -189,7 +189,7 @@ class HybridTargetModel:
             ops.gemm(x, w, ops.EPI_RESIDUAL, residual=h, out=h, out2=tap, ws=ws, sumsq_out=ss)
             return
         M = x.shape[0]
-        ops.gemm(x, w, out=self.tp.partial(parity, M), ws=ws)
+        ops.gemm(x, w, ops.EPI_STORE_F32, out=self.tp.partial(parity, M), ws=ws)
         self.tp.reduce_residual(parity, h, tap, ss, M)
 
     def forward(self, tokens: torch.Tensor, pos: torch.Tensor, cache: HybridCache, max_kv: int,

@@ -12,7 +12,7 @@ import torch
 
 from . import _lib
 
-EPI_STORE, EPI_RESIDUAL, EPI_SILU_MUL, EPI_ARGMAX = 0, 1, 2, 3
+EPI_STORE, EPI_RESIDUAL, EPI_SILU_MUL, EPI_ARGMAX, EPI_STORE_F32 = 0, 1, 2, 3, 4
 ATTN_CHUNK = 128
 
 
@@ -156,8 +156,11 @@ def gemm(x: torch.Tensor, w: PackedWeight | torch.Tensor, epilogue: int = EPI_ST
                   _ptr(scratch), scratch.numel(), _stream())
         return argmax_partials
     n_out = N // 2 if epilogue == EPI_SILU_MUL else N
+    out_dtype = torch.float32 if epilogue == EPI_STORE_F32 else torch.bfloat16
     if out is None:
-        out = torch.empty((M, n_out), dtype=torch.bfloat16, device=x.device)
+        out = torch.empty((M, n_out), dtype=out_dtype, device=x.device)
+    if out.dtype != out_dtype:
+        raise ValueError(f"epilogue {epilogue} writes {out_dtype}")
     if residual is not None and epilogue != EPI_RESIDUAL:
         raise ValueError("residual given without the residual epilogue")
     ldr = _row_stride(residual) if residual is not None else 0

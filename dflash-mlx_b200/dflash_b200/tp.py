@@ -14,7 +14,7 @@ Sharding follows the reference's ``Model.shard`` (custom_qwen35_model.py:1286-14
 * embedding, final norm, lm_head and the draft are replicated.
 
 The all-sum after each row-parallel projection is ``dfl_tp_reduce_residual``: each
-rank's GEMM writes its partial into a peer-mapped slot; one kernel per call sums
+rank's GEMM writes its fp32 partial into a peer-mapped slot; one kernel per call sums
 the N partials in rank order from peer memory and applies the residual add, the tap
 copy and the next RMSNorm's row sums of squares (the same bits on every rank, for
 any number of rows).
@@ -107,15 +107,15 @@ def shard_weights(cfg: TargetConfig, weights: dict, rank: int, size: int) -> dic
 # peer-mapped partial buffers
 # ---------------------------------------------------------------------------
 class _CudaArray:
-    """__cuda_array_interface__ over raw device memory (int16 elements, viewed as bf16)."""
+    """__cuda_array_interface__ over raw device memory (fp32 elements)."""
 
     def __init__(self, ptr: int, shape: tuple[int, ...]):
-        self.__cuda_array_interface__ = {"shape": shape, "typestr": "<i2", "data": (ptr, False), "version": 3,
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": "<f4", "data": (ptr, False), "version": 3,
                                          "strides": None}
 
 
 class TPComm:
-    """One rank's peer-mapped all-sum state: two partial slots [max_rows, hidden] bf16
+    """One rank's peer-mapped all-sum state: two partial slots [max_rows, hidden] fp32
     (call parity), a flag array per rank, the call counter. Built collectively."""
 
     FLAG_BYTES = 256
@@ -126,7 +126,7 @@ class TPComm:
             raise ValueError("at most 8 ranks")
         self.rank, self.size, self.device = rank, size, torch.device(device)
         self.max_rows, self.hidden = max_rows, hidden
-        self.slot_bytes = max_rows * hidden * 2
+        self.slot_bytes = max_rows * hidden * 4
         nbytes = 2 * self.slot_bytes + self.FLAG_BYTES
         lib = _lib.load()
         ptr = ctypes.c_void_p()
@@ -154,7 +154,7 @@ class TPComm:
         self.flags_arr = arr(*[p + 2 * self.slot_bytes for p in self.peers])
         self.counters = torch.zeros(2, dtype=torch.int32, device=dev)  # [epoch, done]
         self.slots = [torch.as_tensor(_CudaArray(self.local + par * self.slot_bytes, (max_rows, hidden)),
-                                      device=dev).view(torch.bfloat16) for par in (0, 1)]
+                                      device=dev) for par in (0, 1)]
         if size > 1:
             torch.cuda.synchronize(dev)
             dist.barrier(group=group)

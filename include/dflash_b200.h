@@ -35,6 +35,7 @@ extern "C" {
 #define DFL_EPI_RESIDUAL 1 /* y = bf16(residual + bf16(acc)); optional second copy to y2 (hidden-state tap) */
 #define DFL_EPI_SILU_MUL 2 /* W rows packed per 64: [32 gate | 32 up]; y[:, n] = bf16(silu(gate) * up), N/2 columns */
 #define DFL_EPI_ARGMAX 3   /* per row and 32 columns: (max bf16 logit, lowest index) into argmax partials */
+#define DFL_EPI_STORE_F32 4 /* y = acc as fp32 (y is float*, ldy in floats): tensor-parallel partials */
 
 /* keys per attention chunk: the fixed key ranges merged in order by dfl_attention */
 #define DFL_ATTN_CHUNK 128
@@ -109,7 +110,8 @@ int dfl_gemm_bf16_wide(const void* x, int64_t ldx, const void* w_packed, int M, 
  * :1338, :1347, :1375; sharding at :1286-1402). Buffers are peer-mapped with CUDA
  * IPC: dfl_tp_alloc (cudaMalloc + zero + 64-byte IPC handle), dfl_tp_open on the
  * other ranks, dfl_tp_close / dfl_tp_free to release.
- * dfl_tp_reduce_residual: parts[j] = rank j's partial [M, H] bf16 (row stride H)
+ * dfl_tp_reduce_residual: parts[j] = rank j's partial [M, H] fp32 (row stride H,
+ * as written by DFL_EPI_STORE_F32)
  * for this call; flags[j] = rank j's int flag array (one slot per rank);
  * epoch / done = this rank's call counter and CTA counter (zeroed once). Sums the
  * partials in rank order in fp32 and writes h <- bf16(h + bf16(sum)), tap (nullable)

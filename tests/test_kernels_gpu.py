@@ -409,3 +409,20 @@ def test_wide_gemm_row_invariance():
         part = ops.gemm(x[:M].contiguous(), w, ws=ws)
         assert torch.equal(part, full[:M]), M
     assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("wide", [False, True])
+def test_gemm_fp32_store(wide):
+    """DFL_EPI_STORE_F32 (tensor-parallel partials): the fp32 accumulator, whose bf16
+    rounding is the bf16 store's output."""
+    ops = _ops()
+    ws = ops.Workspace(torch.device(DEV), wide=wide)
+    M, N, K = 300 if wide else 16, 2560, 4096
+    x = _rand((M, K), 1.0, 61).to(DEV)
+    w = ops.pack_weight(_rand((N, K), 0.02, 62).to(DEV))
+    yf = ops.gemm(x, w, ops.EPI_STORE_F32, ws=ws)
+    yb = ops.gemm(x, w, ws=ws)
+    assert yf.dtype == torch.float32
+    assert torch.equal(yf.bfloat16(), yb)
+    ref = x.float() @ _rand((N, K), 0.02, 62).to(DEV).float().T
+    assert (yf - ref).abs().max().item() <= 1e-2 * ref.abs().max().item()

@@ -58,6 +58,8 @@ def main():
     from dflash_b200.weights import random_draft_weights, random_target_weights
     from dflash_b200 import ops
 
+    # the TP path sums fp32 partials (one bf16 rounding per projection, as on one GPU):
+    # it differs from the single-GPU model by the order of the K sums only
     cases = [("tiny", *tiny_hybrid_pair(), 0.05, 0.08), ("27b-width", *qwen35_27b_pair(4), 0.02, 0.15)]
     g = torch.Generator().manual_seed(11)
     results = {}

@@ -69,17 +69,14 @@ __device__ __forceinline__ int row_limit(const AttnArgs& a, int m) {
   return a.kv_len[s];
 }
 
-template <int HD>
-__host__ __device__ constexpr int att_stages() {
-  return HD >= 256 ? 2 : 3;
-}
-
-template <int HD>
+// K/V ring depth: 3 stages for long chunks at head_dim <= 128; 2 for short chunks
+// (a 128-key chunk is two blocks: a deeper ring only costs shared memory that the
+// next kernel's prologue could use) and for head_dim 256 (shared memory)
+template <int HD, int ST>
 __global__ void __launch_bounds__(256) attn_chunk_kernel(AttnArgs a) {
   grid_dependency_launch_dependents();
   grid_dependency_wait();
   constexpr int NC = HD / 8;  // 16-byte chunks per row
-  constexpr int ST = att_stages<HD>();
   extern __shared__ __align__(128) unsigned char smem_raw[];
   __nv_bfloat16* sQ = reinterpret_cast<__nv_bfloat16*>(smem_raw);  // [G][16][HD]
   __nv_bfloat16* sK = sQ + a.G * 16 * HD;                           // [ST][64][HD]
@@ -91,37 +88,40 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(AttnArgs a) {
   const int m0 = tile * 16;
 
   __shared__ int s_lim[16];
-  __shared__ int s_pos[16], s_rs[16];
   __shared__ int s_seq;
-  if (threadIdx.x < 16) {  // the tile's rows, loaded in parallel
-    const int m = m0 + threadIdx.x;
-    s_pos[threadIdx.x] = m < a.M ? a.pos[m] : -1;
-    s_rs[threadIdx.x] = (m < a.M && a.row_seq) ? a.row_seq[m] : 0;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    // the seg-th distinct sequence among the tile's live rows, in row order
-    int n = 0, chosen = -1;
-    for (int r = 0; r < 16; ++r) {
-      if (s_pos[r] < 0) continue;
-      bool seen = false;
-      for (int j = 0; j < r; ++j) seen |= s_pos[j] >= 0 && s_rs[j] == s_rs[r];
-      if (!seen) {
-        if (n == seg) chosen = s_rs[r];
-        ++n;
-      }
+  if (threadIdx.x < 32) {
+    // warp 0: the tile's rows (lane r < 16), the first row of each sequence in the tile,
+    // and this CTA's sequence = the seg-th of them in row order
+    const int r = threadIdx.x;
+    const int m = m0 + r;
+    const int p = (r < 16 && m < a.M) ? a.pos[m] : -1;
+    const int sq = (r < 16 && m < a.M && a.row_seq) ? a.row_seq[m] : 0;
+    bool first = p >= 0;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const int pj = __shfl_sync(0xffffffffu, p, j), sj = __shfl_sync(0xffffffffu, sq, j);
+      if (j < r && pj >= 0 && sj == sq) first = false;
     }
-    if (seg == 0 && n > a.segs && chunk == 0 && kvh == 0 && a.err) atomicCAS(a.err, 0, ATT_SITE_SEGMENTS);
-    s_seq = chosen;
+    const unsigned firsts = __ballot_sync(0xffffffffu, first);
+    const int n = __popc(firsts);
+    int row = -1;
+    if (seg < n) {
+      unsigned msk = firsts;
+      for (int k = 0; k < seg; ++k) msk &= msk - 1;  // drop the seg lowest first-rows
+      row = __ffs(msk) - 1;
+    }
+    const int chosen = __shfl_sync(0xffffffffu, sq, row < 0 ? 0 : row);
+    if (r == 0) {
+      if (seg == 0 && n > a.segs && chunk == 0 && kvh == 0 && a.err) atomicCAS(a.err, 0, ATT_SITE_SEGMENTS);
+      s_seq = row < 0 ? -1 : chosen;
+    }
+    if (r < 16) {
+      const bool mine = row >= 0 && p >= 0 && sq == chosen;
+      s_lim[r] = !mine ? 0 : (a.causal ? p + 1 : a.kv_len[chosen]);
+    }
   }
   __syncthreads();
   if (s_seq < 0) return;
-  if (threadIdx.x < 16) {
-    const int p = s_pos[threadIdx.x];
-    const bool mine = p >= 0 && s_rs[threadIdx.x] == s_seq;
-    s_lim[threadIdx.x] = !mine ? 0 : (a.causal ? p + 1 : a.kv_len[s_seq]);
-  }
-  __syncthreads();
   int lim_max = 0;
 #pragma unroll
   for (int r = 0; r < 16; ++r) lim_max = max(lim_max, s_lim[r]);
@@ -387,19 +387,30 @@ __global__ void attn_combine_kernel(AttnArgs a) {
   }
 }
 
-template <int HD>
+template <int HD, int ST>
 static int launch_attn(AttnArgs a, int n_tiles, cudaStream_t st) {
-  const size_t smem = (size_t)(a.G * 16 * HD + 2 * att_stages<HD>() * ATT_KB * HD) * 2;
-  static size_t opted[64] = {0};  // dynamic shared memory already opted in, per device
+  const size_t smem = (size_t)(a.G * 16 * HD + 2 * ST * ATT_KB * HD) * 2;
+  // opt in once per device to the whole per-block shared memory: the SM then keeps its
+  // largest shared-memory carveout, which the GEMMs before and after this kernel use, so
+  // their CTAs can stay co-resident with it (programmatic dependent launch overlap)
+  static bool opted[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && smem > opted[dev]) {
-    if (cudaFuncSetAttribute(attn_chunk_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-        cudaSuccess) {
-      set_error("dfl_attention: cannot opt in to %zu bytes of shared memory", smem);
+  if (dev >= 0 && dev < 64 && !opted[dev]) {
+    cudaFuncAttributes fa;
+    int optin = 0;
+    if (cudaFuncGetAttributes(&fa, attn_chunk_kernel<HD, ST>) != cudaSuccess ||
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
+        cudaFuncSetAttribute(attn_chunk_kernel<HD, ST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             optin - (int)fa.sharedSizeBytes) != cudaSuccess) {
+      set_error("dfl_attention: cannot opt in to the per-block shared memory");
       return DFL_ERR_UNSUPPORTED;
     }
-    opted[dev] = smem;
+    opted[dev] = true;
+  }
+  if (smem > 227 * 1024) {
+    set_error("dfl_attention: %zu bytes of shared memory needed", smem);
+    return DFL_ERR_UNSUPPORTED;
   }
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -411,7 +422,7 @@ static int launch_attn(AttnArgs a, int n_tiles, cudaStream_t st) {
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, attn_chunk_kernel<HD>, a);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, attn_chunk_kernel<HD, ST>, a);
   if (e != cudaSuccess) {
     set_error("dfl_attention: chunk kernel launch failed: %s", cudaGetErrorString(e));
     return DFL_ERR_CUDA;
@@ -503,6 +514,7 @@ extern "C" int dfl_attention(const void* q, const void* k_cache, const void* v_c
   a.causal = causal;
   a.scale_log2 = scale * 1.4426950408889634f;
   const int n_tiles = (M + 15) / 16;
+  const bool deep = key_chunk > 2 * ATT_KB;
   // sequences a 16-row tile can hold: one without row_seq or when sequences are
   // whole multiples of 16 rows (or one sequence spans all rows); 16 / seq_rows when
   // that divides; otherwise every row may start a new sequence
@@ -513,9 +525,9 @@ extern "C" int dfl_attention(const void* q, const void* k_cache, const void* v_c
   a.err = device_error_word();
   cudaStream_t st = as_stream(stream);
   switch (hd) {
-    case 64: return launch_attn<64>(a, n_tiles, st);
-    case 128: return launch_attn<128>(a, n_tiles, st);
-    case 256: return launch_attn<256>(a, n_tiles, st);
+    case 64: return deep ? launch_attn<64, 3>(a, n_tiles, st) : launch_attn<64, 2>(a, n_tiles, st);
+    case 128: return deep ? launch_attn<128, 3>(a, n_tiles, st) : launch_attn<128, 2>(a, n_tiles, st);
+    case 256: return launch_attn<256, 2>(a, n_tiles, st);
     default:
       set_error("dfl_attention: head_dim %d not supported (64, 128, 256)", hd);
       return DFL_ERR_UNSUPPORTED;

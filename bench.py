@@ -16,6 +16,10 @@ collective on the data path: weak scaling). Rank 0 prints one JSON line.
 --workload c4 (not the default line): 64 sequences per GPU with
 contexts U[512, 4096] (seed 3), block 16, per-sequence oracle-injected acceptance
 (tau 6.5) and rollback, decoded together in one batched step per GPU.
+
+--workload c5: Qwen3.5-27B-shaped hybrid target (64 layers) with a
+5-layer DFlash draft, tensor-parallel over the N ranks (N = 1, 2, 4 or 8), batch 8,
+context --ctx (default 32768), block 16, oracle-injected acceptance tau 4.0 (seed 4).
 """
 from __future__ import annotations
 
@@ -53,8 +57,9 @@ def parse_args():
     ap.add_argument("--cpu-steps", type=int, default=2, help="speculative steps in the CPU baseline sample")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-roofline", action="store_true")
-    ap.add_argument("--workload", choices=["c3", "c4"], default="c3")
-    ap.add_argument("--batch", type=int, default=64, help="c4: sequences per GPU")
+    ap.add_argument("--workload", choices=["c3", "c4", "c5"], default="c3")
+    ap.add_argument("--batch", type=int, default=0, help="c4: sequences per GPU (64); c5: sequences (8)")
+    ap.add_argument("--ctx", type=int, default=32768, help="c5: prompt length of every sequence")
     ap.add_argument("--ncu-region", action="store_true",
                     help="bracket the timed steps with cudaProfilerStart/Stop (ncu --profile-from-start off)")
     return ap.parse_args()
@@ -287,6 +292,8 @@ def main():
     _lib.load()
     if args.workload == "c4":
         return run_c4(args, world, rank, device)
+    if args.workload == "c5":
+        return run_c5(args, world, rank, device)
     tcfg, dcfg, tw, dw, target, draft = build_models(args, device)
     bs = dcfg.block_size
     g = torch.Generator().manual_seed(args.seed + rank)
@@ -464,7 +471,7 @@ def run_c4(args, world, rank, device):
     if world > 1:
         import torch.distributed as dist
     tcfg, dcfg, tw, dw, target, draft = build_models(args, device)
-    bs, B = dcfg.block_size, args.batch
+    bs, B = dcfg.block_size, args.batch or 64
     seed = 3
     g = torch.Generator().manual_seed(seed + 7919 * rank)
     lens = torch.randint(512, 4097, (B,), generator=g).tolist()
@@ -545,6 +552,100 @@ def run_c4(args, world, rank, device):
             "clocks": clk, "roofline": roof, "e2e": None, "cpu_baseline": None,
         }
         print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_c5(args, world, rank, device):
+    """Config 5: the 27B hybrid, tensor-parallel over the ranks (every rank decodes the
+    same batch; each holds 1 / N of every layer)."""
+    from dflash_b200.config import qwen35_27b_pair
+    from dflash_b200.hybrid import HybridTargetModel
+    from dflash_b200.model import DraftModel
+    from dflash_b200.runtime import SpecSession
+    from dflash_b200.tp import TPComm, shard_config, shard_layer
+    from dflash_b200.weights import random_draft_weights, random_target_weights
+    if world > 1:
+        import torch.distributed as dist
+    n_layers = 64 if args.layers == 36 else args.layers
+    tcfg, dcfg = qwen35_27b_pair(n_layers)
+    bs, B, seed, tau = dcfg.block_size, args.batch or 8, 4, 4.0 if args.tau == 6.5 else args.tau
+    comm = TPComm(rank, world, device, max_rows=max(128, B * bs), hidden=tcfg.hidden_size)
+    w = random_target_weights(tcfg, seed, device="cuda", layer_hook=lambda i, lw: shard_layer(tcfg, i, lw, rank, world))
+    target = HybridTargetModel(shard_config(tcfg, world), w, device, tp=comm)
+    del w
+    draft = DraftModel(dcfg, random_draft_weights(dcfg, seed, device="cuda"), target, mask_mode="causal")
+    torch.cuda.empty_cache()
+    g = torch.Generator().manual_seed(seed)  # the same prompts on every rank
+    prompts = [torch.randint(0, tcfg.vocab_size, (args.ctx,), generator=g).tolist() for _ in range(B)]
+    total_steps = args.warmup + args.steps
+    n_new = bs * (total_steps + 2)
+    plain = SpecSession(target, None, B, args.ctx + n_new + 2 * bs, 1, set(), use_graph=True)
+    plain.prefill(prompts, n_new + 2 * bs)
+    plain.run(n_new + 2 * bs + 2)
+    traces = plain.outputs()[0]
+    del plain
+    torch.cuda.empty_cache()
+    L = max(len(t) for t in traces) + 4 * bs
+    trace_t = torch.zeros((B, L), dtype=torch.int32)
+    for b, t in enumerate(traces):
+        trace_t[b, :len(t)] = torch.tensor(t, dtype=torch.int32)
+    lengths, noise = [], []
+    for b in range(B):
+        le, no = injection_plan(total_steps + 4, bs, tau, tcfg.vocab_size, seed * 1000 + b)
+        lengths.append(le)
+        noise.append(no.reshape(-1))
+    sess = SpecSession(target, draft, B, args.ctx + n_new, bs, set(), use_graph=True, max_steps=total_steps + 8)
+    sess.set_injection(trace_t, torch.stack(lengths), torch.stack(noise))
+    sess.prefill(prompts, n_new)
+    for _ in range(args.warmup):
+        sess.step()
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    clocks = ClockSampler(device.index)
+    clocks.start()
+    time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for k in range(args.steps):
+        sess.step(events=evs[k])
+    t1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    elapsed = t0.elapsed_time(t1) * 1e-3
+    accepted = int(sess.accept_log[:, args.warmup:args.warmup + args.steps].sum())
+    if world > 1:
+        t = torch.tensor([elapsed], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed = float(t[0])
+    from dflash_b200 import ops
+    err = ops.device_error()
+    verify_us = sorted(evs[k][1].elapsed_time(evs[k][2]) * 1e3 for k in range(args.steps))
+    draft_us = sorted(evs[k][0].elapsed_time(evs[k][1]) * 1e3 for k in range(args.steps))
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(accepted / elapsed, 2), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(elapsed / args.steps * 1e3, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (random-init weights, random prompts, oracle-injected drafts)",
+            "config": {"workload": f"config5: Qwen3.5-27B-shaped hybrid ({n_layers} layers) + 5-layer DFlash draft, "
+                                   f"batch {B}, context {args.ctx}, block 16, oracle-injected acceptance tau {tau}",
+                       "global_batch": B, "seq_len": args.ctx, "parallelism": f"tensor-parallel x{world}",
+                       "l2": "weights per rank far above the 126 MB L2"},
+            "value_note": "accepted tokens/s of the whole job (one batch decoded by all ranks together)",
+            "p50_verify_step_us": round(verify_us[len(verify_us) // 2], 1),
+            "p50_draft_step_us": round(draft_us[len(draft_us) // 2], 1),
+            "tau_measured": round(accepted / (args.steps * B), 3), "device_error": err,
+            "clocks": clk, "roofline": None, "e2e": None, "cpu_baseline": None,
+        }
+        print(json.dumps(line), flush=True)
+    comm.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -87,15 +87,17 @@ class SpecSession:
         tc = target.cfg
         B, bs = batch, block_size
         self.cap = max_total + 2 * bs + 1
-        # keys per attention split: fine splits spread one sequence over the SMs; a
-        # batch already fills them, and long splits cut the partial-result traffic
-        self.key_chunk = 128 if batch <= 4 else 1024
+        # batched sessions (4+ sequences) switch two kernel forms, both chosen from the
+        # batch size alone so that a batch's plain decode and its speculative decode
+        # use the same arithmetic: attention splits keys every 1024 positions (a batch
+        # already fills the SMs; long splits cut the partial-result traffic) instead of
+        # every 128, and every GEMM runs whole-K tensor-core tiles (weights read once for
+        # all rows) instead of the M <= 16 weight-streaming split-K form
+        self.batched = batch >= 4
+        self.key_chunk = 1024 if self.batched else 128
         self.out_cap = self.cap
         self.max_steps = max_steps or (max_total + 1)
-        # many sequences: whole-K tensor-core tiles (compute-bound at 16+ x 16 verify rows)
-        # instead of the weight-streaming split-K GEMM. The choice depends on the batch
-        # only, so a batch's plain decode and its speculative decode use the same form.
-        self.ws = ops.Workspace(self.dev, wide=batch >= 16)
+        self.ws = ops.Workspace(self.dev, wide=self.batched)
         dev = self.dev
         i32 = dict(dtype=torch.int32, device=dev)
         self.state = torch.zeros((B, STATE_INTS), **i32)

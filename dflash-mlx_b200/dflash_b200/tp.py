@@ -75,32 +75,36 @@ def shard_weights(cfg: TargetConfig, weights: dict, rank: int, size: int) -> dic
     """This rank's share of a qwen3_5 target's weights (same keys as the full set)."""
     if size == 1:
         return weights
-    kd = cfg.linear_key_head_dim * cfg.linear_num_key_heads
-    vd = cfg.linear_value_head_dim * cfg.linear_num_value_heads
-    hd, Hq, Hkv = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads
     out = {k: v for k, v in weights.items() if k != "layers"}
-    out["layers"] = []
-    for i, lw in enumerate(weights["layers"]):
-        s = {"input_layernorm": lw["input_layernorm"], "post_attention_layernorm": lw["post_attention_layernorm"],
-             "gate_proj": _rows(lw["gate_proj"], rank, size), "up_proj": _rows(lw["up_proj"], rank, size),
-             "down_proj": _cols(lw["down_proj"], rank, size)}
-        if cfg.is_linear_layer(i):
-            qkv, conv = lw["in_proj_qkv"], lw["conv1d"]
-            seg = lambda t: torch.cat([_rows(t[:kd], rank, size), _rows(t[kd:2 * kd], rank, size),  # noqa: E731
-                                       _rows(t[2 * kd:], rank, size)], 0)
-            s.update({"in_proj_qkv": seg(qkv), "conv1d": seg(conv), "in_proj_z": _rows(lw["in_proj_z"], rank, size),
-                      "in_proj_b": _rows(lw["in_proj_b"], rank, size), "in_proj_a": _rows(lw["in_proj_a"], rank, size),
-                      "dt_bias": _rows(lw["dt_bias"], rank, size), "A_log": _rows(lw["A_log"], rank, size),
-                      "norm": lw["norm"], "out_proj": _cols(lw["out_proj"], rank, size)})
-        else:
-            qh = Hq // size
-            s.update({"q_proj": lw["q_proj"][rank * qh * 2 * hd:(rank + 1) * qh * 2 * hd],
-                      "k_proj": _kv_rows(lw["k_proj"], Hkv, hd, rank, size),
-                      "v_proj": _kv_rows(lw["v_proj"], Hkv, hd, rank, size),
-                      "o_proj": lw["o_proj"][:, rank * qh * hd:(rank + 1) * qh * hd],
-                      "q_norm": lw["q_norm"], "k_norm": lw["k_norm"]})
-        out["layers"].append({k: v.contiguous() for k, v in s.items()})
+    out["layers"] = [shard_layer(cfg, i, lw, rank, size) for i, lw in enumerate(weights["layers"])]
     return out
+
+
+def shard_layer(cfg: TargetConfig, i: int, lw: dict, rank: int, size: int) -> dict:
+    """This rank's share of layer i's weights."""
+    if size == 1:
+        return lw
+    kd = cfg.linear_key_head_dim * cfg.linear_num_key_heads
+    hd, Hq, Hkv = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads
+    s = {"input_layernorm": lw["input_layernorm"], "post_attention_layernorm": lw["post_attention_layernorm"],
+         "gate_proj": _rows(lw["gate_proj"], rank, size), "up_proj": _rows(lw["up_proj"], rank, size),
+         "down_proj": _cols(lw["down_proj"], rank, size)}
+    if cfg.is_linear_layer(i):
+        qkv, conv = lw["in_proj_qkv"], lw["conv1d"]
+        seg = lambda t: torch.cat([_rows(t[:kd], rank, size), _rows(t[kd:2 * kd], rank, size),  # noqa: E731
+                                   _rows(t[2 * kd:], rank, size)], 0)
+        s.update({"in_proj_qkv": seg(qkv), "conv1d": seg(conv), "in_proj_z": _rows(lw["in_proj_z"], rank, size),
+                  "in_proj_b": _rows(lw["in_proj_b"], rank, size), "in_proj_a": _rows(lw["in_proj_a"], rank, size),
+                  "dt_bias": _rows(lw["dt_bias"], rank, size), "A_log": _rows(lw["A_log"], rank, size),
+                  "norm": lw["norm"], "out_proj": _cols(lw["out_proj"], rank, size)})
+    else:
+        qh = Hq // size
+        s.update({"q_proj": lw["q_proj"][rank * qh * 2 * hd:(rank + 1) * qh * 2 * hd],
+                  "k_proj": _kv_rows(lw["k_proj"], Hkv, hd, rank, size),
+                  "v_proj": _kv_rows(lw["v_proj"], Hkv, hd, rank, size),
+                  "o_proj": lw["o_proj"][:, rank * qh * hd:(rank + 1) * qh * hd],
+                  "q_norm": lw["q_norm"], "k_norm": lw["k_norm"]})
+    return {k: v.contiguous() for k, v in s.items()}
 
 
 # ---------------------------------------------------------------------------

@@ -36,8 +36,11 @@ def _ones(n: int, device: str) -> torch.Tensor:
     return torch.ones(n, dtype=torch.bfloat16, device=device)
 
 
-def random_target_weights(cfg: TargetConfig, seed: int, std: float = 0.02, device: str = "cpu") -> dict[str, Any]:
-    """Seeded N(0, std) target weights. device='cuda' draws them on the GPU (large models)."""
+def random_target_weights(cfg: TargetConfig, seed: int, std: float = 0.02, device: str = "cpu",
+                          layer_hook=None) -> dict[str, Any]:
+    """Seeded N(0, std) target weights. device='cuda' draws them on the GPU (large models).
+    ``layer_hook(i, layer_weights) -> layer_weights`` transforms each layer as soon as it is
+    drawn (a tensor-parallel rank keeps only its shard: one full layer is live at a time)."""
     gen = torch.Generator(device=device)
     gen.manual_seed(seed)
     H, hd = cfg.hidden_size, cfg.head_dim
@@ -75,7 +78,7 @@ def random_target_weights(cfg: TargetConfig, seed: int, std: float = 0.02, devic
                 "q_norm": _ones(hd, device),
                 "k_norm": _ones(hd, device),
             })
-        w["layers"].append(lw)
+        w["layers"].append(layer_hook(i, lw) if layer_hook is not None else lw)
     return w
 
 

@@ -130,25 +130,46 @@ def test_qwen3_4b_layer_logits_parity():
     assert (taps.float().cpu() - ref_taps).abs().max().item() <= 2e-2 * ref_taps.abs().max().item()
 
 
-def test_tiny_batched_decode_equals_single_sequence():
-    """Sequences of different prompt lengths decoded together (plain and speculative,
-    several sequences per 16-row attention tile) each reproduce their own
-    single-sequence plain greedy decode."""
-    tcfg, dcfg, tw, dw, target, draft = _tiny()
+def _batched(target, draft, prompts, max_new, bs, graph):
     from dflash_b200.runtime import SpecSession, S_FINISHED
+    sess = SpecSession(target, draft, len(prompts), max(len(p) for p in prompts) + max_new, bs, set(),
+                       use_graph=graph)
+    sess.prefill(prompts, max_new)
+    for _ in range(max_new + 1):
+        if bool(sess.state[:, S_FINISHED].all().item()):
+            break
+        sess.step()
+    return sess.outputs()[0]
+
+
+def test_tiny_batched_decode_equals_single_sequence():
+    """Three sequences of different prompt lengths decoded together (plain and
+    speculative, several sequences per 16-row attention tile) each reproduce their own
+    single-sequence plain greedy decode (below 4 sequences a batch uses the
+    single-sequence kernel forms)."""
+    tcfg, dcfg, tw, dw, target, draft = _tiny()
     g = torch.Generator().manual_seed(9)
-    prompts = [torch.randint(0, tcfg.vocab_size, (n,), generator=g).tolist() for n in (30, 57, 12, 41)]
+    prompts = [torch.randint(0, tcfg.vocab_size, (n,), generator=g).tolist() for n in (30, 57, 12)]
     max_new = 40
     singles = [_run(target, None, p, max_new, 1)[0] for p in prompts]
     for bs, dr in ((1, None), (dcfg.block_size, draft)):
         for graph in (False, True):
-            sess = SpecSession(target, dr, len(prompts), max(len(p) for p in prompts) + max_new, bs, set(),
-                               use_graph=graph)
-            sess.prefill(prompts, max_new)
-            for _ in range(max_new + 1):
-                if bool(sess.state[:, S_FINISHED].all().item()):
-                    break
-                sess.step()
-            outs, _, _ = sess.outputs()
+            outs = _batched(target, dr, prompts, max_new, bs, graph)
             for b in range(len(prompts)):
                 assert outs[b] == singles[b], (bs, graph, b)
+
+
+def test_tiny_batched_session_spec_equals_its_plain_decode():
+    """A batched session (6 sequences: wide GEMM, 1024-key attention splits): the
+    speculative decode equals the same batch's plain greedy decode bit for bit, and
+    each sequence's first tokens match its single-sequence decode."""
+    tcfg, dcfg, tw, dw, target, draft = _tiny()
+    g = torch.Generator().manual_seed(10)
+    prompts = [torch.randint(0, tcfg.vocab_size, (n,), generator=g).tolist() for n in (30, 57, 12, 41, 70, 9)]
+    max_new = 40
+    plain = _batched(target, None, prompts, max_new, 1, True)
+    for graph in (False, True):
+        assert _batched(target, draft, prompts, max_new, dcfg.block_size, graph) == plain
+    singles = [_run(target, None, p, 4, 1)[0] for p in prompts]
+    for b, p in enumerate(prompts):
+        assert plain[b][:len(p) + 4] == singles[b]

@@ -610,11 +610,15 @@ def run_c5(args, world, rank, device):
         dist.barrier()
     torch.cuda.synchronize()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if args.ncu_region:
+        torch.cuda.profiler.start()
     t0.record()
     for k in range(args.steps):
         sess.step(events=evs[k])
     t1.record()
     torch.cuda.synchronize()
+    if args.ncu_region:
+        torch.cuda.profiler.stop()
     if world > 1:
         dist.barrier()
     clk = clocks.stop()

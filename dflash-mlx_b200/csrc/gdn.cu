@@ -91,7 +91,9 @@ __global__ void gdn_prep_kernel(GdnPrepArgs a) {
   }
 }
 
-// state[b] <- snaps[b][acc-1]; conv_state[b] <- window[b][acc .. acc+2]
+// state[b] <- snaps[b][acc-1]; conv_state[b] <- window[b][acc .. acc+2]. Every block of
+// sequence b copies a 1/gridDim.x share of both with 16-byte moves (the conv rows are
+// 3*C bf16, a multiple of 8 elements).
 __global__ void gdn_rollback_kernel(float* __restrict__ state, const float* __restrict__ snaps,
                                     __nv_bfloat16* __restrict__ conv_state, const __nv_bfloat16* __restrict__ window,
                                     const int* __restrict__ accepted, int acc_stride, int T, long long S, int C,
@@ -101,16 +103,16 @@ __global__ void gdn_rollback_kernel(float* __restrict__ state, const float* __re
   const int b = blockIdx.y;
   const int acc = accepted[(long long)b * acc_stride];
   if (acc < 1 || acc > T) return;
+  const long long tid = blockIdx.x * (long long)blockDim.x + threadIdx.x, nthr = (long long)gridDim.x * blockDim.x;
   if (snaps) {
     const float4* src = reinterpret_cast<const float4*>(snaps + ((long long)b * T + acc - 1) * S);
     float4* dst = reinterpret_cast<float4*>(state + (long long)b * S);
-    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < S / 4; i += (long long)gridDim.x * blockDim.x)
-      dst[i] = src[i];
+    for (long long i = tid; i < S / 4; i += nthr) dst[i] = src[i];
   }
-  if (window && blockIdx.x == 0) {
-    const __nv_bfloat16* src = window + (long long)b * win_stride + (long long)acc * C;
-    __nv_bfloat16* dst = conv_state + (long long)b * 3 * C;
-    for (int i = threadIdx.x; i < 3 * C; i += blockDim.x) dst[i] = src[i];
+  if (window) {
+    const uint4* src = reinterpret_cast<const uint4*>(window + (long long)b * win_stride + (long long)acc * C);
+    uint4* dst = reinterpret_cast<uint4*>(conv_state + (long long)b * 3 * C);
+    for (long long i = tid; i < 3LL * C / 8; i += nthr) dst[i] = src[i];
   }
 }
 
@@ -220,8 +222,9 @@ extern "C" int dfl_gdn_rollback(float* state, const float* snapshots, void* conv
     return DFL_ERR_INVALID;
   }
   const long long S = (long long)Hv * Dv * Dk;
-  if (S % 4) {
-    set_error("dfl_gdn_rollback: state size must be a multiple of 4");
+  const long long ws = win_stride > 0 ? win_stride : (long long)(3 + T) * C;
+  if (S % 4 || C % 8 || ws % 8 || (reinterpret_cast<uintptr_t>(window) | reinterpret_cast<uintptr_t>(conv_state)) & 15) {
+    set_error("dfl_gdn_rollback: state size %% 4, channels %% 8 and 16-byte aligned conv buffers needed");
     return DFL_ERR_UNSUPPORTED;
   }
   cudaLaunchAttribute attr[1];

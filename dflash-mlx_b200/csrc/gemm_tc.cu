@@ -847,6 +847,8 @@ constexpr int WG_SMEM = WG_OFF_TMEM + 16 + 1024;
 
 struct WgArgs {
   TcArgs t;
+  float* part;  // split > 1: fp32 partials [split][M][N] (reduced in order by wide_split_reduce_kernel)
+  int split;    // K ranges per tile (1: the tile's epilogue runs here)
   int stages;   // ring depth: W stages at 0, X stages after them
   int bn;       // tokens per tile
   int m_tiles;  // row tiles of X
@@ -985,9 +987,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_wide_kernel(const __grid_c
   const uint32_t x_bytes = (uint32_t)bn * TC_BK * 2;
   unsigned char* xring = smem + ST * TC_W_BYTES;  // X stage s at xring + s * x_bytes (1024-aligned)
   const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(TC_NT >> 4) << 24);
-  // this CTA's tiles: blockIdx.x, blockIdx.x + gridDim.x, ...
-  const int my_tiles = w.tiles > (int)blockIdx.x ? (w.tiles - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-  const long long my_units = (long long)my_tiles * a.kb;
+  // this CTA's work items (tile x K range): blockIdx.x, blockIdx.x + gridDim.x, ...
+  const int items = w.tiles * w.split;
+  const int my_tiles = items > (int)blockIdx.x ? (items - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const long long my_units = (long long)my_tiles * a.kb;  // upper bound (0 means no work)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < ST; ++s) {
@@ -1023,10 +1026,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_wide_kernel(const __grid_c
       bool ok = true;
       bool waited_dep = false;
       for (int tt = 0; tt < my_tiles && ok; ++tt) {
-        const int tl = (int)blockIdx.x + tt * (int)gridDim.x;
+        const int item = (int)blockIdx.x + tt * (int)gridDim.x;
+        const int tl = item / w.split, sp = item % w.split;
         const int nt = tl / w.m_tiles, mt = tl % w.m_tiles;
         const unsigned char* wsrc = a.wt + (long long)nt * a.kb * TC_W_BYTES;
-        for (int j = 0; j < a.kb; ++j, ++i) {
+        const int j0 = sp * a.kb / w.split, j1 = (sp + 1) * a.kb / w.split;
+        for (int j = j0; j < j1; ++j, ++i) {
           if (i >= ST && !mbar_wait(&empty[s], ph ^ 1u, 221, a.err)) {
             ok = false;
             break;
@@ -1061,10 +1066,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_wide_kernel(const __grid_c
       bool ok = true;
       for (int tt = 0; tt < my_tiles && ok; ++tt) {
         const int buf = tt & 1;
+        const int sp = ((int)blockIdx.x + tt * (int)gridDim.x) % w.split;
+        const int j0 = sp * a.kb / w.split, j1 = (sp + 1) * a.kb / w.split;
         if (!mbar_wait(&acce[buf], (uint32_t)((tt >> 1) & 1) ^ 1u, 222, a.err)) break;
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)(buf * WG_BN_MAX);
-        for (int j = 0; j < a.kb; ++j) {
+        for (int j = j0; j < j1; ++j) {
           if (!mbar_wait(&full[s], ph, 223, a.err)) {
             ok = false;
             break;
@@ -1074,7 +1081,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_wide_kernel(const __grid_c
           const uint64_t bd = sw128_desc(x0 + s * x_bytes);
 #pragma unroll
           for (int kk = 0; kk < TC_BK / 16; ++kk)
-            tc_mma(d, ad + 2 * kk, bd + 2 * kk, idesc, (j == 0 && kk == 0) ? 0u : 1u);
+            tc_mma(d, ad + 2 * kk, bd + 2 * kk, idesc, (j == j0 && kk == 0) ? 0u : 1u);
           tc_commit(&empty[s]);
           if (++s == ST) {
             s = 0;
@@ -1089,9 +1096,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_wide_kernel(const __grid_c
     // ---------------- epilogue warps ----------------
     const int q = warp & 3;
     grid_dependency_wait();
+    TcArgs pa = a;  // split > 1: this item's raw fp32 partial
+    pa.ldy = a.N;
+    pa.y2 = nullptr;
+    pa.sumsq_out = nullptr;
     for (int tt = 0; tt < my_tiles; ++tt) {
-      const int tl = (int)blockIdx.x + tt * (int)gridDim.x;
+      const int item = (int)blockIdx.x + tt * (int)gridDim.x;
+      const int tl = item / w.split, sp = item % w.split;
       const int nt = tl / w.m_tiles, mt = tl % w.m_tiles;
+      pa.y = reinterpret_cast<__nv_bfloat16*>(w.part + (long long)sp * a.M * a.N);
       const int buf = tt & 1;
       if (!mbar_wait(&accf[buf], (uint32_t)((tt >> 1) & 1), 225, a.err)) break;
       tc_fence_after();
@@ -1100,7 +1113,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_wide_kernel(const __grid_c
         if (m0 >= a.M) break;  // uniform over the four warps
         float v[TC_BM];
         tc_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * WG_BN_MAX + ch * TC_BM), v);
-        wide_epilogue<EPI>(a, v, m0, nt, q * 32 + lane, threadIdx.x - 32 * TC_EPI_WARP0, stile);
+        if (w.split > 1)
+          wide_epilogue<DFL_EPI_STORE_F32>(pa, v, m0, nt, q * 32 + lane, threadIdx.x - 32 * TC_EPI_WARP0, stile);
+        else
+          wide_epilogue<EPI>(a, v, m0, nt, q * 32 + lane, threadIdx.x - 32 * TC_EPI_WARP0, stile);
       }
       tc_fence_before();
       __syncwarp();
@@ -1115,30 +1131,53 @@ __global__ void __launch_bounds__(TC_THREADS, 1) gemm_wide_kernel(const __grid_c
   }
 }
 
-// xn[m, k] = bf16(w[k] * x[m, k] * rsqrt(sum(parts[m]) / K + eps)): the RMSNorm prologue
-// of the wide GEMM, one warp per row (partials summed in order, as the fused form does)
-__global__ void norm_apply_kernel(const __nv_bfloat16* __restrict__ x, long long ldx, const __nv_bfloat16* __restrict__ w,
-                                  const float* __restrict__ parts, int n_parts, float eps, __nv_bfloat16* __restrict__ xn,
-                                  int M, int K) {
+// Split-K completion of the wide GEMM: v = sum over the K ranges in order (fp32), then the
+// requested epilogue. One 128-thread block per (128-column tile, 16 rows); thread c owns
+// column c, as the tensor-memory layout gives it in the GEMM.
+template <int EPI>
+__global__ void __launch_bounds__(128) wide_split_reduce_kernel(TcArgs a, const float* __restrict__ part, int split) {
   grid_dependency_launch_dependents();
   grid_dependency_wait();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m = blockIdx.x * (blockDim.x >> 5) + warp;
+  __shared__ float stile[TC_BM * WG_EPI_LD];
+  const int nt = blockIdx.x, m0 = blockIdx.y * TC_BM, c = threadIdx.x;
+  const int n = nt * TC_NT + c;
+  float v[TC_BM];
+#pragma unroll
+  for (int t = 0; t < TC_BM; ++t) v[t] = 0.f;
+  if (n < a.N) {
+    for (int sp = 0; sp < split; ++sp) {
+      const float* src = part + (long long)sp * a.M * a.N + n;
+#pragma unroll
+      for (int t = 0; t < TC_BM; ++t)
+        if (m0 + t < a.M) v[t] += __ldcg(src + (long long)(m0 + t) * a.N);
+    }
+  }
+  wide_epilogue<EPI>(a, v, m0, nt, c, c, stile);
+}
+
+// xn[m, k] = bf16(w[k] * x[m, k] * rsqrt(sum(parts[m]) / K + eps)): the RMSNorm prologue
+// of the wide GEMM (partials summed in order, as the fused form does). Grid (M, K / 2048):
+// every block recomputes its row's scale and rescales 2048 columns, 8 per thread.
+__global__ void __launch_bounds__(256) norm_apply_kernel(const __nv_bfloat16* __restrict__ x, long long ldx,
+                                                         const __nv_bfloat16* __restrict__ w,
+                                                         const float* __restrict__ parts, int n_parts, float eps,
+                                                         __nv_bfloat16* __restrict__ xn, int M, int K) {
+  grid_dependency_launch_dependents();
+  grid_dependency_wait();
+  const int m = blockIdx.x;
   if (m >= M) return;
   float ss = 0.f;
   for (int p = 0; p < n_parts; ++p) ss += parts[(long long)m * n_parts + p];
   const float inv = rsqrtf(ss / (float)K + eps);
-  const __nv_bfloat16* xr = x + (long long)m * ldx;
-  __nv_bfloat16* yr = xn + (long long)m * K;
-  for (int k = lane * 8; k < K; k += 32 * 8) {
-    uint4 xv = *reinterpret_cast<const uint4*>(xr + k);
-    const uint4 wv = *reinterpret_cast<const uint4*>(w + k);
-    __nv_bfloat16* xe = reinterpret_cast<__nv_bfloat16*>(&xv);
-    const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv);
+  const int k = blockIdx.y * 2048 + threadIdx.x * 8;
+  if (k >= K) return;
+  uint4 xv = *reinterpret_cast<const uint4*>(x + (long long)m * ldx + k);
+  const uint4 wv = *reinterpret_cast<const uint4*>(w + k);
+  __nv_bfloat16* xe = reinterpret_cast<__nv_bfloat16*>(&xv);
+  const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) xe[e] = f2bf(bf2f(we[e]) * (bf2f(xe[e]) * inv));
-    *reinterpret_cast<uint4*>(yr + k) = xv;
-  }
+  for (int e = 0; e < 8; ++e) xe[e] = f2bf(bf2f(we[e]) * (bf2f(xe[e]) * inv));
+  *reinterpret_cast<uint4*>(xn + (long long)m * K + k) = xv;
 }
 
 struct TcPlan {
@@ -1155,7 +1194,10 @@ static TcPlan tc_plan(int M, int N, int K) {
   p.U1 = (long long)p.n_tiles * p.kb;
   p.grid1 = (int)(p.U1 < TC_GRID ? p.U1 : TC_GRID);
   p.S = 0;
-  if (p.n_tiles < TC_GRID) {  // few tiles: one cluster of S ranks per tile, about one CTA per SM
+#ifndef DFL_TC_CSK_TILES
+#define DFL_TC_CSK_TILES TC_GRID
+#endif
+  if (p.n_tiles < DFL_TC_CSK_TILES) {  // few tiles: one cluster of S ranks per tile, about one CTA per SM
     int S = (TC_GRID + p.n_tiles / 2) / p.n_tiles;
     if (S > DFL_TC_SMAX) S = DFL_TC_SMAX;
     if (S > p.kb) S = p.kb;
@@ -1327,15 +1369,23 @@ extern "C" int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w_packed, i
   return DFL_OK;
 }
 
-extern "C" size_t dfl_gemm_wide_workspace_bytes(int M, int K, int with_norm) {
-  if (M <= 0 || K <= 0 || !with_norm) return 0;
-  return ((size_t)M * K * 2 + 255) & ~(size_t)255;
+static int wide_split_of(int K, int k_split) {
+  const int kb = K / TC_BK;
+  return k_split < 1 ? 1 : (k_split > kb ? kb : k_split);
+}
+
+extern "C" size_t dfl_gemm_wide_workspace_bytes(int M, int N, int K, int with_norm, int k_split) {
+  if (M <= 0 || N <= 0 || K <= 0 || K % TC_BK) return 0;
+  const size_t xn = with_norm ? (((size_t)M * K * 2 + 255) & ~(size_t)255) : 0;
+  const int S = wide_split_of(K, k_split);
+  return xn + (S > 1 ? (size_t)S * M * N * 4 : 0);
 }
 
 extern "C" int dfl_gemm_bf16_wide(const void* x, int64_t ldx, const void* w_packed, int M, int N, int K, int epilogue,
                                   const void* residual, int64_t ldr, void* y, int64_t ldy, void* y2, int64_t ldy2,
                                   void* argmax_partials, const void* norm_w, const float* sumsq_in, int n_parts,
-                                  float eps, float* sumsq_out, void* workspace, size_t workspace_bytes, void* stream) {
+                                  float eps, float* sumsq_out, int k_split, void* workspace, size_t workspace_bytes,
+                                  void* stream) {
   if (M == 0) return DFL_OK;
   const void* w = w_packed;
   if (!x || !w || M < 0 || N <= 0 || K <= 0) {
@@ -1370,7 +1420,8 @@ extern "C" int dfl_gemm_bf16_wide(const void* x, int64_t ldx, const void* w_pack
     set_error("dfl_gemm_bf16_wide: the RMSNorm prologue needs K/32 sumsq_in partials");
     return DFL_ERR_INVALID;
   }
-  const size_t need = dfl_gemm_wide_workspace_bytes(M, K, norm_w != nullptr);
+  const int split = wide_split_of(K, k_split);
+  const size_t need = dfl_gemm_wide_workspace_bytes(M, N, K, norm_w != nullptr, split);
   if (need && (!workspace || workspace_bytes < need)) {
     set_error("dfl_gemm_bf16_wide: workspace too small (%zu < %zu bytes)", workspace_bytes, need);
     return DFL_ERR_WORKSPACE;
@@ -1383,7 +1434,7 @@ extern "C" int dfl_gemm_bf16_wide(const void* x, int64_t ldx, const void* w_pack
   long long ldxs = ldx;
   if (norm_w) {
     cudaLaunchConfig_t nc = {};
-    nc.gridDim = dim3((M + 7) / 8);
+    nc.gridDim = dim3(M, (K + 2047) / 2048);
     nc.blockDim = dim3(256);
     nc.stream = st;
     nc.attrs = attr;
@@ -1445,13 +1496,18 @@ extern "C" int dfl_gemm_bf16_wide(const void* x, int64_t ldx, const void* w_pack
   a.kb = K / TC_BK;
   a.U1 = 0;
   a.grid1 = 0;
+  wa.split = split;
+  wa.part = split > 1 ? reinterpret_cast<float*>(static_cast<char*>(workspace) +
+                                                 (norm_w ? (((size_t)M * K * 2 + 255) & ~(size_t)255) : 0))
+                      : nullptr;
   wa.bn = bn;
   wa.stages = WG_RING_BYTES / (TC_W_BYTES + bn * TC_BK * 2);
   if (wa.stages > WG_MAX_STAGES) wa.stages = WG_MAX_STAGES;
   wa.m_tiles = (M + bn - 1) / bn;
   wa.tiles = a.n_tiles * wa.m_tiles;
+  const int items = wa.tiles * split;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(wa.tiles < sms ? wa.tiles : sms);
+  cfg.gridDim = dim3(items < sms ? items : sms);
   cfg.blockDim = dim3(TC_THREADS);
   cfg.dynamicSmemBytes = WG_SMEM;
   cfg.stream = st;
@@ -1467,6 +1523,13 @@ extern "C" int dfl_gemm_bf16_wide(const void* x, int64_t ldx, const void* w_pack
       init[dev] = true;                                                                                     \
     }                                                                                                       \
     err = cudaLaunchKernelEx(&cfg, gemm_wide_kernel<E>, *xm, wa);                                           \
+    if (err == cudaSuccess && split > 1) {                                                                  \
+      cudaLaunchConfig_t rc = cfg;                                                                          \
+      rc.gridDim = dim3(a.n_tiles, (M + TC_BM - 1) / TC_BM);                                                \
+      rc.blockDim = dim3(128);                                                                              \
+      rc.dynamicSmemBytes = 0;                                                                              \
+      err = cudaLaunchKernelEx(&rc, wide_split_reduce_kernel<E>, a, static_cast<const float*>(wa.part), split); \
+    }                                                                                                       \
     break;                                                                                                  \
   }
     DFL_LAUNCH_WIDE(DFL_EPI_STORE)

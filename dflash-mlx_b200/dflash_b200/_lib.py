@@ -34,8 +34,8 @@ SIGNATURES: dict[str, tuple] = {
                               c_void_p, c_size_t, c_void_p]),
     "dfl_gemm_bf16_wide": (c_int, [c_void_p, c_int64, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int64,
                                    c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int, c_float,
-                                   c_void_p, c_void_p, c_size_t, c_void_p]),
-    "dfl_gemm_wide_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
+                                   c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
+    "dfl_gemm_wide_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
     "dfl_device_error": (c_int, [POINTER(c_int), c_int, c_void_p]),
     "dfl_tp_alloc": (c_int, [c_size_t, POINTER(c_void_p), POINTER(ctypes.c_ubyte)]),
     "dfl_tp_open": (c_int, [POINTER(ctypes.c_ubyte), POINTER(c_void_p)]),

@@ -46,11 +46,12 @@ class Workspace:
     """
 
     def __init__(self, device: torch.device, gemm_bytes: int = 64 << 20, attn_bytes: int = 64 << 20,
-                 wide: bool = False):
+                 wide: bool = False, wide_split: int = 1):
         self.device = torch.device(device)
         self.gemm = torch.zeros(gemm_bytes, dtype=torch.uint8, device=self.device)
         self.attn = torch.empty(attn_bytes, dtype=torch.uint8, device=self.device)
         self.wide = wide
+        self.wide_split = wide_split  # most K ranges a wide GEMM may split into
         self.wide_x = torch.empty(0, dtype=torch.uint8, device=self.device)
 
     def ensure_wide(self, nbytes: int) -> None:
@@ -132,12 +133,13 @@ def gemm(x: torch.Tensor, w: PackedWeight | torch.Tensor, epilogue: int = EPI_ST
     ws = ws or workspace(x.device)
     if ws.wide:
         fn = "dfl_gemm_bf16_wide"
-        ws.ensure_wide(int(_lib.query("dfl_gemm_wide_workspace_bytes", M, K, int(norm_w is not None))))
-        scratch = ws.wide_x
+        ks = wide_split(N, K, ws)
+        ws.ensure_wide(int(_lib.query("dfl_gemm_wide_workspace_bytes", M, N, K, int(norm_w is not None), ks)))
+        scratch, tail = ws.wide_x, (ks,)
     else:
         fn = "dfl_gemm_bf16"
         ws.ensure_gemm(int(_lib.query("dfl_gemm_workspace_bytes", M, N, K, epilogue)))
-        scratch = ws.gemm
+        scratch, tail = ws.gemm, ()
     n_parts = 0
     if norm_w is not None:
         if sumsq_in is None or sumsq_in.shape[0] < M or sumsq_in.dtype != torch.float32:
@@ -152,7 +154,7 @@ def gemm(x: torch.Tensor, w: PackedWeight | torch.Tensor, epilogue: int = EPI_ST
         if argmax_partials is None:
             argmax_partials = torch.empty((M, ntiles, 2), dtype=torch.float32, device=x.device)
         _lib.call(fn, _ptr(x), ldx, _ptr(w), M, N, K, epilogue, None, 0, None, 0, None, 0,
-                  _ptr(argmax_partials), _ptr(norm_w), _ptr(sumsq_in), n_parts, float(eps), None,
+                  _ptr(argmax_partials), _ptr(norm_w), _ptr(sumsq_in), n_parts, float(eps), None, *tail,
                   _ptr(scratch), scratch.numel(), _stream())
         return argmax_partials
     n_out = N // 2 if epilogue == EPI_SILU_MUL else N
@@ -167,8 +169,24 @@ def gemm(x: torch.Tensor, w: PackedWeight | torch.Tensor, epilogue: int = EPI_ST
     ldy2 = _row_stride(out2) if out2 is not None else 0
     _lib.call(fn, _ptr(x), ldx, _ptr(w), M, N, K, epilogue, _ptr(residual), ldr, _ptr(out),
               _row_stride(out), _ptr(out2), ldy2, None, _ptr(norm_w), _ptr(sumsq_in), n_parts, float(eps),
-              _ptr(sumsq_out), _ptr(scratch), scratch.numel(), _stream())
+              _ptr(sumsq_out), *tail, _ptr(scratch), scratch.numel(), _stream())
     return out
+
+
+_SMS: dict[int, int] = {}
+
+
+def wide_split(N: int, K: int, ws: Workspace) -> int:
+    """K ranges of a wide GEMM: enough (128-row tile x range) items for every SM when the
+    weight has few 128-row tiles, at most ws.wide_split. Depends on N, K and the
+    workspace's limit only, so every call of a session splits a weight the same way."""
+    if ws.wide_split <= 1:
+        return 1
+    dev = ws.device.index if ws.device.index is not None else torch.cuda.current_device()
+    if dev not in _SMS:
+        _SMS[dev] = torch.cuda.get_device_properties(dev).multi_processor_count
+    n_tiles = (N + 127) // 128
+    return max(1, min(ws.wide_split, round(_SMS[dev] / n_tiles), K // 64))
 
 
 def device_error(clear: bool = True) -> int:

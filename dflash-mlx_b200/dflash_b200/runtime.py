@@ -97,7 +97,8 @@ class SpecSession:
         self.key_chunk = 1024 if self.batched else 128
         self.out_cap = self.cap
         self.max_steps = max_steps or (max_total + 1)
-        self.ws = ops.Workspace(self.dev, wide=self.batched)
+        # under 16 sequences, weights with few 128-row tiles also split K (fixed ranges)
+        self.ws = ops.Workspace(self.dev, wide=self.batched, wide_split=4 if batch < 16 else 1)
         dev = self.dev
         i32 = dict(dtype=torch.int32, device=dev)
         self.state = torch.zeros((B, STATE_INTS), **i32)
@@ -139,7 +140,8 @@ class SpecSession:
         for M in shapes:
             for N, K in nk:
                 gemm_need = max(gemm_need, int(q("dfl_gemm_workspace_bytes", M, N, K, 0)))
-                wide_need = max(wide_need, int(q("dfl_gemm_wide_workspace_bytes", M, K, 1)))
+                wide_need = max(wide_need, int(q("dfl_gemm_wide_workspace_bytes", M, N, K, 1,
+                                                   ops.wide_split(N, K, self.ws))))
             attn_need = max(attn_need, int(q("dfl_attention_workspace_bytes", M, tc.num_attention_heads,
                                                tc.head_dim, self.cap, self.key_chunk)))
         self.ws.ensure_gemm(gemm_need)

@@ -91,18 +91,20 @@ int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w_packed, int M, int N
                   void* argmax_partials, const void* norm_w, const float* sumsq_in, int n_parts, float eps,
                   float* sumsq_out, void* workspace, size_t workspace_bytes, void* stream);
 
-/* Wide form of dfl_gemm_bf16 for many rows (batched verify: 64+ sequences x 16
- * rows), same arguments and epilogues. Each 128-column x up-to-256-row output tile
- * runs its whole K loop in one tensor-core accumulator (no split-K), so a row's
- * result depends on K order only: identical for any M, but not bit-identical to
- * dfl_gemm_bf16's (split-K) result, so runs compared bit for bit use one form.
- * Compute-bound at large M. With norm_w the RMSNorm prologue runs as a row kernel
- * into the workspace (dfl_gemm_wide_workspace_bytes bytes; none otherwise). */
-size_t dfl_gemm_wide_workspace_bytes(int M, int K, int with_norm);
+/* Wide form of dfl_gemm_bf16 for many rows (batched verify: 4+ sequences x 16
+ * rows), same arguments and epilogues plus k_split. Each 128-column x up-to-256-row
+ * output tile runs its K loop in one tensor-core accumulator; k_split > 1 cuts K into
+ * that many fixed contiguous ranges (fp32 partials summed in range order by a second
+ * kernel, which then applies the epilogue), for weights with few 128-row tiles. A row's
+ * result depends on K order and k_split only: identical for any M, but not
+ * bit-identical to dfl_gemm_bf16's result, so runs compared bit for bit use one form
+ * and one k_split. Compute-bound at large M. Workspace: dfl_gemm_wide_workspace_bytes
+ * (RMSNorm prologue output when norm_w is given, split partials when k_split > 1). */
+size_t dfl_gemm_wide_workspace_bytes(int M, int N, int K, int with_norm, int k_split);
 int dfl_gemm_bf16_wide(const void* x, int64_t ldx, const void* w_packed, int M, int N, int K, int epilogue,
                        const void* residual, int64_t ldr, void* y, int64_t ldy, void* y2, int64_t ldy2,
                        void* argmax_partials, const void* norm_w, const float* sumsq_in, int n_parts, float eps,
-                       float* sumsq_out, void* workspace, size_t workspace_bytes, void* stream);
+                       float* sumsq_out, int k_split, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---- tensor parallelism (Qwen3.5-27B, config 5) ------------------------------
  * Replaces the all-sum after the row-parallel projections of the reference's
@@ -111,14 +113,13 @@ int dfl_gemm_bf16_wide(const void* x, int64_t ldx, const void* w_packed, int M, 
  * IPC: dfl_tp_alloc (cudaMalloc + zero + 64-byte IPC handle), dfl_tp_open on the
  * other ranks, dfl_tp_close / dfl_tp_free to release.
  * dfl_tp_reduce_residual: parts[j] = rank j's partial [M, H] fp32 (row stride H,
- * as written by DFL_EPI_STORE_F32)
- * for this call; flags[j] = rank j's int flag array (one slot per rank);
- * epoch / done = this rank's call counter and CTA counter (zeroed once). Sums the
- * partials in rank order in fp32 and writes h <- bf16(h + bf16(sum)), tap (nullable)
- * <- h, sumsq_out[M][H/32] (nullable). Partial slots must alternate between two
- * buffers on consecutive calls. A wait that expires records device error 401.
- * parts and flags are host arrays of n_ranks device pointers (copied into the
- * launch, so a captured graph keeps them). */
+ * as written by DFL_EPI_STORE_F32) for this call; flags[j] = rank j's int flag
+ * array (one slot per rank); epoch / done = this rank's call counter and CTA
+ * counter (zeroed once). Sums the partials in rank order in fp32 and writes
+ * h <- bf16(h + bf16(sum)), tap (nullable) <- h, sumsq_out[M][H/32] (nullable).
+ * Partial slots must alternate between two buffers on consecutive calls. A wait
+ * that expires records device error 401. parts and flags are host arrays of n_ranks
+ * device pointers (copied into the launch, so a captured graph keeps them). */
 int dfl_tp_alloc(size_t bytes, void** ptr, unsigned char* ipc_handle_out);
 int dfl_tp_open(const unsigned char* ipc_handle, void** ptr);
 int dfl_tp_close(void* peer_ptr);

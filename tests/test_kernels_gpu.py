@@ -345,9 +345,9 @@ def test_attention_batched_sequences_share_tiles(rows, seq_rows_arg, key_chunk):
 # ---------------------------------------------------------------------------
 # Wide GEMM (whole-K tiles for many rows)
 # ---------------------------------------------------------------------------
-def _wide_ws():
+def _wide_ws(split: int = 1):
     from dflash_b200 import ops
-    return ops.Workspace(torch.device(DEV), wide=True)
+    return ops.Workspace(torch.device(DEV), wide=True, wide_split=split)
 
 
 @pytest.mark.parametrize("M,N,K", [(1024, 6144, 2560), (1024, 2560, 9728), (300, 512, 256), (16, 1536, 2560),
@@ -362,14 +362,16 @@ def test_wide_gemm_store_matches_fp32(M, N, K):
     assert err <= 1e-2 * ref.abs().max().item() + 1e-3, err
 
 
-def test_wide_gemm_epilogues_and_norm():
+@pytest.mark.parametrize("M,split", [(512, 1), (128, 4)])
+def test_wide_gemm_epilogues_and_norm(M, split):
     """Residual + tap + sum-of-squares, SiLU·up and argmax epilogues, and the RMSNorm
-    prologue, in the wide form against the weight-streaming form's definitions."""
+    prologue, in the wide form (whole-K tiles, and fixed split-K ranges) against the
+    weight-streaming form's definitions."""
     from oracle import dflash_oracle as O
     from dflash_b200.weights import pack_gate_up
     ops = _ops()
-    ws = _wide_ws()
-    M, H, I = 512, 2560, 9728
+    ws = _wide_ws(split)
+    H, I = 2560, 9728
     x = _rand((M, H), 1.0, 52).to(DEV)
     res = _rand((M, H), 1.0, 53).to(DEV)
     w = _rand((H, H), 0.02, 54).to(DEV)
@@ -398,14 +400,18 @@ def test_wide_gemm_epilogues_and_norm():
     assert torch.equal(got, logits.argmax(-1).int().cpu())
 
 
-def test_wide_gemm_row_invariance():
-    """A row's wide-GEMM result is the same bits whatever M (and tile width) is."""
+@pytest.mark.parametrize("split,N", [(1, 6144), (4, 2560)])
+def test_wide_gemm_row_invariance(split, N):
+    """A row's wide-GEMM result is the same bits whatever M (and tile width) is, for a
+    given split of K."""
     ops = _ops()
-    ws = _wide_ws()
+    ws = _wide_ws(split)
     x = _rand((1024, 2560), 1.0, 59).to(DEV)
-    w = ops.pack_weight(_rand((6144, 2560), 0.02, 60).to(DEV))
+    w = ops.pack_weight(_rand((N, 2560), 0.02, 60).to(DEV))
     full = ops.gemm(x, w, ws=ws)
-    for M in (16, 64, 200, 256):
+    ref = x.float() @ _rand((N, 2560), 0.02, 60).to(DEV).float().T
+    assert (full.float() - ref).abs().max().item() <= 1e-2 * ref.abs().max().item()
+    for M in (8, 16, 64, 200, 256):
         part = ops.gemm(x[:M].contiguous(), w, ws=ws)
         assert torch.equal(part, full[:M]), M
     assert ops.device_error() == 0

@@ -26,8 +26,14 @@
 
 namespace dfl {
 
-constexpr int GDR_LPR = 4;                    // lanes per value row
-constexpr int GDR_WARPS = 2;                  // warps per CTA
+#ifndef DFL_GDR_LPR
+#define DFL_GDR_LPR 4
+#endif
+constexpr int GDR_LPR = DFL_GDR_LPR;          // lanes per value row
+#ifndef DFL_GDR_WARPS
+#define DFL_GDR_WARPS 2
+#endif
+constexpr int GDR_WARPS = DFL_GDR_WARPS;      // warps per CTA
 constexpr int GDR_ROWS = GDR_WARPS * 32 / GDR_LPR;  // value rows per CTA (16)
 constexpr int GDR_TT = 16;                    // tokens per staged tile
 
@@ -55,7 +61,7 @@ template <int DK>
 __global__ void __launch_bounds__(32 * GDR_WARPS) gdr_kernel(GdrArgs a) {
   grid_dependency_launch_dependents();
   grid_dependency_wait();
-  constexpr int NCH = DK / 16;  // float4 chunks per lane
+  constexpr int NCH = DK / (4 * GDR_LPR);  // float4 chunks per lane
   // double-buffered raw tiles: tile i + 1 streams in (cp.async) while tile i is consumed
   __shared__ __align__(16) __nv_bfloat16 sk[2][GDR_TT][DK];
   __shared__ __align__(16) __nv_bfloat16 sq[2][GDR_TT][DK];
@@ -127,8 +133,8 @@ __global__ void __launch_bounds__(32 * GDR_WARPS) gdr_kernel(GdrArgs a) {
         p3 += s[j].w * kf[j].w;
       }
       float kv = (p0 + p1) + (p2 + p3);
-      kv += __shfl_xor_sync(0xffffffffu, kv, 1);
-      kv += __shfl_xor_sync(0xffffffffu, kv, 2);
+#pragma unroll
+      for (int o = 1; o < GDR_LPR; o <<= 1) kv += __shfl_xor_sync(0xffffffffu, kv, o);
       const float delta = (bf2f(sv[buf][tt][rloc]) - kv) * sb[buf][tt];
 #pragma unroll
       for (int j = 0; j < NCH; ++j) {
@@ -150,8 +156,8 @@ __global__ void __launch_bounds__(32 * GDR_WARPS) gdr_kernel(GdrArgs a) {
           y3 += s[j].w * qf.w;
         }
         float y = (y0 + y1) + (y2 + y3);
-        y += __shfl_xor_sync(0xffffffffu, y, 1);
-        y += __shfl_xor_sync(0xffffffffu, y, 2);
+#pragma unroll
+        for (int o = 1; o < GDR_LPR; o <<= 1) y += __shfl_xor_sync(0xffffffffu, y, o);
         if (c == 0) a.o[(((long long)b * a.T + t) * a.Hv + h) * a.Dv + row] = f2bf(y);
       }
       if (a.snap) {

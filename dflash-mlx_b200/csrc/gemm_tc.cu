@@ -1401,6 +1401,14 @@ extern "C" int dfl_gemm_bf16_wide(const void* x, int64_t ldx, const void* w_pack
     set_error("dfl_gemm_bf16_wide: missing output pointer");
     return DFL_ERR_INVALID;
   }
+  const bool raw_partials = epilogue == DFL_EPI_PARTIALS;
+  if (raw_partials) {
+    if (ldy != N) {
+      set_error("dfl_gemm_bf16_wide: the partials epilogue writes [k_split][M][N] slabs (ldy must be N)");
+      return DFL_ERR_INVALID;
+    }
+    epilogue = DFL_EPI_STORE_F32;
+  }
   if (epilogue == DFL_EPI_RESIDUAL && !residual) {
     set_error("dfl_gemm_bf16_wide: residual epilogue needs a residual pointer");
     return DFL_ERR_INVALID;
@@ -1421,7 +1429,7 @@ extern "C" int dfl_gemm_bf16_wide(const void* x, int64_t ldx, const void* w_pack
     return DFL_ERR_INVALID;
   }
   const int split = wide_split_of(K, k_split);
-  const size_t need = dfl_gemm_wide_workspace_bytes(M, N, K, norm_w != nullptr, split);
+  const size_t need = dfl_gemm_wide_workspace_bytes(M, N, K, norm_w != nullptr, raw_partials ? 1 : split);
   if (need && (!workspace || workspace_bytes < need)) {
     set_error("dfl_gemm_bf16_wide: workspace too small (%zu < %zu bytes)", workspace_bytes, need);
     return DFL_ERR_WORKSPACE;
@@ -1497,9 +1505,10 @@ extern "C" int dfl_gemm_bf16_wide(const void* x, int64_t ldx, const void* w_pack
   a.U1 = 0;
   a.grid1 = 0;
   wa.split = split;
-  wa.part = split > 1 ? reinterpret_cast<float*>(static_cast<char*>(workspace) +
-                                                 (norm_w ? (((size_t)M * K * 2 + 255) & ~(size_t)255) : 0))
-                      : nullptr;
+  wa.part = split <= 1 ? nullptr
+             : raw_partials ? static_cast<float*>(y)
+                            : reinterpret_cast<float*>(static_cast<char*>(workspace) +
+                                                       (norm_w ? (((size_t)M * K * 2 + 255) & ~(size_t)255) : 0));
   wa.bn = bn;
   wa.stages = WG_RING_BYTES / (TC_W_BYTES + bn * TC_BK * 2);
   if (wa.stages > WG_MAX_STAGES) wa.stages = WG_MAX_STAGES;
@@ -1523,7 +1532,7 @@ extern "C" int dfl_gemm_bf16_wide(const void* x, int64_t ldx, const void* w_pack
       init[dev] = true;                                                                                     \
     }                                                                                                       \
     err = cudaLaunchKernelEx(&cfg, gemm_wide_kernel<E>, *xm, wa);                                           \
-    if (err == cudaSuccess && split > 1) {                                                                  \
+    if (err == cudaSuccess && split > 1 && !raw_partials) {                                                 \
       cudaLaunchConfig_t rc = cfg;                                                                          \
       rc.gridDim = dim3(a.n_tiles, (M + TC_BM - 1) / TC_BM);                                                \
       rc.blockDim = dim3(128);                                                                              \

@@ -40,6 +40,8 @@ struct TpArgs {
   __nv_bfloat16* tap;
   long long ldtap;
   float* sumsq_out;  // [M][H/32]
+  long long slab_stride;  // elements between a rank's K-range partial slabs
+  int n_slabs;
   int rank, n_ranks, M, H;
 };
 
@@ -87,18 +89,20 @@ __global__ void __launch_bounds__(256) tp_reduce_residual_kernel(TpArgs a) {
       float acc[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-      for (int j = 0; j < a.n_ranks; ++j) {  // rank order: the same sum on every rank
-        const float4* pp = reinterpret_cast<const float4*>(a.parts[j] + (long long)m * a.H + c0);
-        const float4 p0 = __ldcg(pp), p1 = __ldcg(pp + 1);
-        acc[0] += p0.x;
-        acc[1] += p0.y;
-        acc[2] += p0.z;
-        acc[3] += p0.w;
-        acc[4] += p1.x;
-        acc[5] += p1.y;
-        acc[6] += p1.z;
-        acc[7] += p1.w;
-      }
+      for (int j = 0; j < a.n_ranks; ++j)  // rank order, then slab order: the same sum on every rank
+        for (int sl = 0; sl < a.n_slabs; ++sl) {
+          const float4* pp =
+              reinterpret_cast<const float4*>(a.parts[j] + sl * a.slab_stride + (long long)m * a.H + c0);
+          const float4 p0 = __ldcg(pp), p1 = __ldcg(pp + 1);
+          acc[0] += p0.x;
+          acc[1] += p0.y;
+          acc[2] += p0.z;
+          acc[3] += p0.w;
+          acc[4] += p1.x;
+          acc[5] += p1.y;
+          acc[6] += p1.z;
+          acc[7] += p1.w;
+        }
       __nv_bfloat16* hp = a.h + (long long)m * a.ldh + c0;
       const uint4 hv = *reinterpret_cast<const uint4*>(hp);
       const __nv_bfloat16* hb = reinterpret_cast<const __nv_bfloat16*>(&hv);
@@ -189,11 +193,12 @@ extern "C" int dfl_tp_free(void* ptr) {
 }
 
 extern "C" int dfl_tp_reduce_residual(const void* const* parts, int* const* flags, int* epoch, int* done, int rank,
-                                      int n_ranks, void* h, int64_t ldh, void* tap, int64_t ldtap, float* sumsq_out,
-                                      int M, int H, void* stream) {
+                                      int n_ranks, int n_slabs, int64_t slab_stride, void* h, int64_t ldh, void* tap,
+                                      int64_t ldtap, float* sumsq_out, int M, int H, void* stream) {
   if (M == 0) return DFL_OK;
   if (!parts || !flags || !epoch || !done || !h || n_ranks < 1 || n_ranks > TP_MAX_RANKS || rank < 0 ||
-      rank >= n_ranks || M < 0 || H <= 0) {
+      rank >= n_ranks || M < 0 || H <= 0 || n_slabs < 1 || (n_slabs > 1 && slab_stride < (long long)M * H) ||
+      slab_stride % 4) {
     set_error("dfl_tp_reduce_residual: bad arguments");
     return DFL_ERR_INVALID;
   }
@@ -214,6 +219,8 @@ extern "C" int dfl_tp_reduce_residual(const void* const* parts, int* const* flag
   a.tap = static_cast<__nv_bfloat16*>(tap);
   a.ldtap = ldtap;
   a.sumsq_out = sumsq_out;
+  a.n_slabs = n_slabs;
+  a.slab_stride = slab_stride;
   a.rank = rank;
   a.n_ranks = n_ranks;
   a.M = M;

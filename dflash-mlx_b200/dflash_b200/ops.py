@@ -12,7 +12,7 @@ import torch
 
 from . import _lib
 
-EPI_STORE, EPI_RESIDUAL, EPI_SILU_MUL, EPI_ARGMAX, EPI_STORE_F32 = 0, 1, 2, 3, 4
+EPI_STORE, EPI_RESIDUAL, EPI_SILU_MUL, EPI_ARGMAX, EPI_STORE_F32, EPI_PARTIALS = 0, 1, 2, 3, 4, 5
 ATTN_CHUNK = 128
 
 
@@ -158,7 +158,14 @@ def gemm(x: torch.Tensor, w: PackedWeight | torch.Tensor, epilogue: int = EPI_ST
                   _ptr(scratch), scratch.numel(), _stream())
         return argmax_partials
     n_out = N // 2 if epilogue == EPI_SILU_MUL else N
-    out_dtype = torch.float32 if epilogue == EPI_STORE_F32 else torch.bfloat16
+    out_dtype = torch.float32 if epilogue in (EPI_STORE_F32, EPI_PARTIALS) else torch.bfloat16
+    if epilogue == EPI_PARTIALS:
+        if not ws.wide:
+            raise ValueError("the partials epilogue is a wide-GEMM form")
+        if out is None:
+            out = torch.empty((tail[0], M, N), dtype=out_dtype, device=x.device)
+        if out.dim() != 3 or out.shape[0] < tail[0] or out.stride(1) != N:
+            raise ValueError(f"the partials epilogue writes [{tail[0]}, M, {N}] slabs")
     if out is None:
         out = torch.empty((M, n_out), dtype=out_dtype, device=x.device)
     if out.dtype != out_dtype:
@@ -167,8 +174,9 @@ def gemm(x: torch.Tensor, w: PackedWeight | torch.Tensor, epilogue: int = EPI_ST
         raise ValueError("residual given without the residual epilogue")
     ldr = _row_stride(residual) if residual is not None else 0
     ldy2 = _row_stride(out2) if out2 is not None else 0
+    ldy = N if epilogue == EPI_PARTIALS else _row_stride(out)
     _lib.call(fn, _ptr(x), ldx, _ptr(w), M, N, K, epilogue, _ptr(residual), ldr, _ptr(out),
-              _row_stride(out), _ptr(out2), ldy2, None, _ptr(norm_w), _ptr(sumsq_in), n_parts, float(eps),
+              ldy, _ptr(out2), ldy2, None, _ptr(norm_w), _ptr(sumsq_in), n_parts, float(eps),
               _ptr(sumsq_out), *tail, _ptr(scratch), scratch.numel(), _stream())
     return out
 

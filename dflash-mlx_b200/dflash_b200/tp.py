@@ -123,6 +123,7 @@ class TPComm:
     (call parity), a flag array per rank, the call counter. Built collectively."""
 
     FLAG_BYTES = 256
+    MAX_SLABS = 4  # K-range partial slabs a wide GEMM may leave per call (ops.wide_split limit)
 
     def __init__(self, rank: int, size: int, device: torch.device, max_rows: int, hidden: int, group=None):
         import torch.distributed as dist
@@ -130,7 +131,7 @@ class TPComm:
             raise ValueError("at most 8 ranks")
         self.rank, self.size, self.device = rank, size, torch.device(device)
         self.max_rows, self.hidden = max_rows, hidden
-        self.slot_bytes = max_rows * hidden * 4
+        self.slot_bytes = self.MAX_SLABS * max_rows * hidden * 4
         nbytes = 2 * self.slot_bytes + self.FLAG_BYTES
         lib = _lib.load()
         ptr = ctypes.c_void_p()
@@ -157,24 +158,29 @@ class TPComm:
         self.parts_arr = [arr(*[p + par * self.slot_bytes for p in self.peers]) for par in (0, 1)]
         self.flags_arr = arr(*[p + 2 * self.slot_bytes for p in self.peers])
         self.counters = torch.zeros(2, dtype=torch.int32, device=dev)  # [epoch, done]
-        self.slots = [torch.as_tensor(_CudaArray(self.local + par * self.slot_bytes, (max_rows, hidden)),
-                                      device=dev) for par in (0, 1)]
+        self.slots = [torch.as_tensor(_CudaArray(self.local + par * self.slot_bytes,
+                                                 (self.MAX_SLABS * max_rows * hidden,)), device=dev)
+                      for par in (0, 1)]
         if size > 1:
             torch.cuda.synchronize(dev)
             dist.barrier(group=group)
 
-    def partial(self, parity: int, M: int) -> torch.Tensor:
-        """This rank's partial slot for a call of the given parity, [M, hidden]."""
-        if M > self.max_rows:
-            raise ValueError(f"{M} rows exceed the all-sum buffer ({self.max_rows})")
-        return self.slots[parity][:M]
+    def partial(self, parity: int, M: int, slabs: int = 1) -> torch.Tensor:
+        """This rank's partial slot for a call of the given parity: [M, hidden], or
+        [slabs, M, hidden] K-range slabs."""
+        if M > self.max_rows or slabs > self.MAX_SLABS:
+            raise ValueError(f"{slabs} x {M} rows exceed the all-sum buffer ({self.MAX_SLABS} x {self.max_rows})")
+        v = self.slots[parity][:slabs * M * self.hidden]
+        return v.view(M, self.hidden) if slabs == 1 else v.view(slabs, M, self.hidden)
 
     def reduce_residual(self, parity: int, h: torch.Tensor, tap: torch.Tensor | None, sumsq_out: torch.Tensor | None,
-                        M: int) -> None:
-        """h[:M] <- h + sum over ranks of the parity slot; tap copy; row sums of squares."""
+                        M: int, slabs: int = 1) -> None:
+        """h[:M] <- h + sum over ranks (and K-range slabs) of the parity slot; tap copy;
+        row sums of squares."""
         from .ops import _ptr, _row_stride, _stream
         _lib.call("dfl_tp_reduce_residual", self.parts_arr[parity], self.flags_arr,
-                  self.counters.data_ptr(), self.counters.data_ptr() + 4, self.rank, self.size, _ptr(h),
+                  self.counters.data_ptr(), self.counters.data_ptr() + 4, self.rank, self.size, slabs,
+                  M * self.hidden, _ptr(h),
                   _row_stride(h), _ptr(tap), _row_stride(tap) if tap is not None else 0, _ptr(sumsq_out), M,
                   self.hidden, _stream())
 

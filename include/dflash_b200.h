@@ -36,6 +36,8 @@ extern "C" {
 #define DFL_EPI_SILU_MUL 2 /* W rows packed per 64: [32 gate | 32 up]; y[:, n] = bf16(silu(gate) * up), N/2 columns */
 #define DFL_EPI_ARGMAX 3   /* per row and 32 columns: (max bf16 logit, lowest index) into argmax partials */
 #define DFL_EPI_STORE_F32 4 /* y = acc as fp32 (y is float*, ldy in floats): tensor-parallel partials */
+#define DFL_EPI_PARTIALS 5  /* wide form only: the k_split fp32 K-range partials, unsummed, as slabs
+                               y[s][M][N] (y float*, ldy must be N); with k_split 1 this is STORE_F32 */
 
 /* keys per attention chunk: the fixed key ranges merged in order by dfl_attention */
 #define DFL_ATTN_CHUNK 128
@@ -112,10 +114,11 @@ int dfl_gemm_bf16_wide(const void* x, int64_t ldx, const void* w_packed, int M, 
  * :1338, :1347, :1375; sharding at :1286-1402). Buffers are peer-mapped with CUDA
  * IPC: dfl_tp_alloc (cudaMalloc + zero + 64-byte IPC handle), dfl_tp_open on the
  * other ranks, dfl_tp_close / dfl_tp_free to release.
- * dfl_tp_reduce_residual: parts[j] = rank j's partial [M, H] fp32 (row stride H,
- * as written by DFL_EPI_STORE_F32) for this call; flags[j] = rank j's int flag
+ * dfl_tp_reduce_residual: parts[j] = rank j's n_slabs partial slabs [M, H] fp32 (row
+ * stride H, slab_stride elements apart; DFL_EPI_STORE_F32 writes one, the wide
+ * form's DFL_EPI_PARTIALS k_split) for this call; flags[j] = rank j's int flag
  * array (one slot per rank); epoch / done = this rank's call counter and CTA
- * counter (zeroed once). Sums the partials in rank order in fp32 and writes
+ * counter (zeroed once). Sums the partials in rank then slab order in fp32 and writes
  * h <- bf16(h + bf16(sum)), tap (nullable) <- h, sumsq_out[M][H/32] (nullable).
  * Partial slots must alternate between two buffers on consecutive calls. A wait
  * that expires records device error 401. parts and flags are host arrays of n_ranks
@@ -125,8 +128,8 @@ int dfl_tp_open(const unsigned char* ipc_handle, void** ptr);
 int dfl_tp_close(void* peer_ptr);
 int dfl_tp_free(void* ptr);
 int dfl_tp_reduce_residual(const void* const* parts, int* const* flags, int* epoch, int* done, int rank, int n_ranks,
-                           void* h, int64_t ldh, void* tap, int64_t ldtap, float* sumsq_out, int M, int H,
-                           void* stream);
+                           int n_slabs, int64_t slab_stride, void* h, int64_t ldh, void* tap, int64_t ldtap,
+                           float* sumsq_out, int M, int H, void* stream);
 
 /* Reads (and optionally clears) the device error record: non-zero when a kernel's
  * bounded wait gave up (the kernel returned instead of hanging). Synchronises

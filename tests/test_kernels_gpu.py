@@ -432,3 +432,22 @@ def test_gemm_fp32_store(wide):
     assert torch.equal(yf.bfloat16(), yb)
     ref = x.float() @ _rand((N, K), 0.02, 62).to(DEV).float().T
     assert (yf - ref).abs().max().item() <= 1e-2 * ref.abs().max().item()
+
+
+def test_wide_gemm_partials_slabs():
+    """DFL_EPI_PARTIALS leaves the K-range partials unsummed; summed in slab order they
+    are the split GEMM's fp32 result bit for bit."""
+    ops = _ops()
+    ws = _wide_ws(4)
+    M, N, K = 128, 2560, 9728
+    x = _rand((M, K), 1.0, 63).to(DEV)
+    w = ops.pack_weight(_rand((N, K), 0.02, 64).to(DEV))
+    S = ops.wide_split(N, K, ws)
+    assert S == 4
+    slabs = ops.gemm(x, w, ops.EPI_PARTIALS, ws=ws)
+    assert slabs.shape == (S, M, N)
+    full = ops.gemm(x, w, ops.EPI_STORE_F32, ws=ws)
+    acc = torch.zeros_like(full)
+    for s in range(S):
+        acc += slabs[s]
+    assert torch.equal(acc, full)

@@ -311,10 +311,11 @@ class LoadedTargetModel:
 
 def load_target_model(path_or_spec: str | tuple, device="cuda", seed: int = 0) -> LoadedTargetModel:
     """Builds a target. ``"random:<preset>"`` (presets: tiny, qwen3-4b, tiny-hybrid,
-    qwen3.5-27b) draws seeded
-    random weights; a ``(TargetConfig, weights)`` tuple uses the given weights.
-    Checkpoint directories are not read by this build (the safetensors loader is
-    listed as the next row of work)."""
+    qwen3.5-27b) draws seeded random weights; a ``(TargetConfig, weights)`` tuple uses the
+    given weights; a checkpoint directory (config.json + model*.safetensors, Hugging Face
+    or MLX layout) is read by ``checkpoint.load_target_checkpoint`` (adapters.py:829-852)."""
+    tok = None
+    resolved = None
     if isinstance(path_or_spec, tuple):
         cfg, w = path_or_spec
         name = "custom"
@@ -326,9 +327,10 @@ def load_target_model(path_or_spec: str | tuple, device="cuda", seed: int = 0) -
         w = random_target_weights(cfg, seed, device="cpu" if cfg.num_hidden_layers * cfg.hidden_size < 20000 else device)
         name = path_or_spec
     else:
-        raise NotImplementedError(
-            f"loading checkpoint {path_or_spec!r} is not supported by this build; pass 'random:<preset>' "
-            "or a (TargetConfig, weights) tuple")
+        from .checkpoint import load_target_checkpoint, load_tokenizer
+        cfg, w, resolved = load_target_checkpoint(path_or_spec)
+        tok = load_tokenizer(resolved, cfg.vocab_size, cfg.eos_token_ids)
+        name = str(path_or_spec)
     adapter_cls = adapter_for_model_type(cfg.model_type)
     if adapter_cls is None:
         registered = ", ".join(sorted(ADAPTERS))
@@ -339,5 +341,5 @@ def load_target_model(path_or_spec: str | tuple, device="cuda", seed: int = 0) -
         model = HybridTargetModel(cfg, w, device)
     else:
         model = TargetModel(cfg, w, device)
-    tok = ByteTokenizer(cfg.vocab_size, cfg.eos_token_ids)
-    return LoadedTargetModel(name, None, model, tok, adapter_cls())
+    tok = tok or ByteTokenizer(cfg.vocab_size, cfg.eos_token_ids)
+    return LoadedTargetModel(name, resolved, model, tok, adapter_cls())

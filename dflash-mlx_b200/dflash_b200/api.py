@@ -37,7 +37,8 @@ class DFlashStreamEvent:
 
 
 def load_draft_model(spec, target: LoadedTargetModel, seed: int = 0, mask_mode: str = "none") -> DraftModel:
-    """``"random:<preset>"`` or a ``(DraftConfig, weights)`` tuple (draft.py:226-238 reads safetensors)."""
+    """``"random:<preset>"``, a ``(DraftConfig, weights)`` tuple, or a DFlash draft checkpoint
+    directory (config.json + model*.safetensors, draft.py:226-238)."""
     if isinstance(spec, DraftModel):
         return spec
     if isinstance(spec, tuple):
@@ -46,7 +47,8 @@ def load_draft_model(spec, target: LoadedTargetModel, seed: int = 0, mask_mode: 
         cfg = PRESETS[spec.split(":", 1)[1]]()[1]
         w = random_draft_weights(cfg, seed)
     else:
-        raise NotImplementedError(f"loading draft checkpoint {spec!r} is not supported by this build")
+        from .checkpoint import load_draft_checkpoint
+        cfg, w, _ = load_draft_checkpoint(spec)
     return DraftModel(cfg, w, target.model, mask_mode=mask_mode)
 
 

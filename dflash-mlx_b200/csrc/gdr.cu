@@ -46,6 +46,8 @@ struct GdrArgs {
   const float* state_in;
   long long state_in_bstride;  // elements between batch entries of state_in
   const int* state_slot;       // nullable: state_in + slot[b] * Hv*Dv*Dk selects a snapshot
+  const int* tokens;           // nullable: sequence b advances over min(T, tokens[b * tokens_stride]) tokens
+  int tokens_stride;
   float* state_out;
   float* snap;
   __nv_bfloat16* o;
@@ -109,9 +111,10 @@ __global__ void __launch_bounds__(32 * GDR_WARPS) gdr_kernel(GdrArgs a) {
   for (int j = 0; j < NCH; ++j) s[j] = reinterpret_cast<const float4*>(sin)[j * GDR_LPR + c];
 
   int buf = 0;
-  for (int t0 = 0; t0 < a.T; t0 += GDR_TT, buf ^= 1) {
-    const int nt = min(GDR_TT, a.T - t0);
-    if (t0 + GDR_TT < a.T) stage(buf ^ 1, t0 + GDR_TT);
+  const int Tb = a.tokens ? max(0, min(a.T, a.tokens[(long long)b * a.tokens_stride])) : a.T;
+  for (int t0 = 0; t0 < Tb; t0 += GDR_TT, buf ^= 1) {
+    const int nt = min(GDR_TT, Tb - t0);
+    if (t0 + GDR_TT < Tb) stage(buf ^ 1, t0 + GDR_TT);
     cp_async_commit();
     cp_async_wait<1>();
     __syncthreads();
@@ -184,7 +187,7 @@ using namespace dfl;
 extern "C" int dfl_gdr_recurrence(const void* q, const void* k, const void* v, const float* g, const float* beta,
                                   const float* state_in, int64_t state_in_bstride, const int32_t* state_slot,
                                   float* state_out, float* snapshots, void* o, int B, int T, int Hk, int Hv, int Dk,
-                                  int Dv, void* stream) {
+                                  int Dv, const int32_t* tokens, int tokens_stride, void* stream) {
   if (B == 0 || T == 0) return DFL_OK;
   if (!k || !v || !g || !beta || !state_in || (o && !q) || B < 0 || T < 0 || Hk <= 0 || Hv <= 0 || Hv % Hk) {
     set_error("dfl_gdr_recurrence: bad arguments");
@@ -211,6 +214,8 @@ extern "C" int dfl_gdr_recurrence(const void* q, const void* k, const void* v, c
   a.state_in = state_in;
   a.state_in_bstride = state_in_bstride;
   a.state_slot = state_slot;
+  a.tokens = tokens;
+  a.tokens_stride = tokens_stride;
   a.state_out = state_out;
   a.snap = snapshots;
   a.o = static_cast<__nv_bfloat16*>(o);

@@ -74,7 +74,8 @@ SIGNATURES: dict[str, tuple] = {
     "dfl_verify_accept": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int64, c_void_p, c_void_p,
                                   c_int, c_void_p, c_int64, c_int, c_void_p]),
     "dfl_gdr_recurrence": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p,
-                                   c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p]),
+                                   c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p,
+                                   c_int, c_void_p]),
 }
 
 _LIB: ctypes.CDLL | None = None

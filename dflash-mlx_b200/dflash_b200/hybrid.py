@@ -12,11 +12,13 @@ HBM layout (per device):
   * full-attention layer: ``w_qkv`` = [q_proj (q and output gate interleaved per head) |
     k_proj | v_proj], ``w_o``;
   * caches (``HybridCache``): KV [L_attn, B, Hkv, cap, hd] for the attention layers;
-    per GDN layer the fp32 recurrent state [B, Hv, Dv, Dk], per-token snapshots of the
-    last verify block [B, T, Hv, Dv, Dk], the conv state [B, 3, C] and the conv window
-    [B, 3 + T, C]. Rollback after a verify = copy snapshot accepted-1 into the state and
-    window rows [accepted, accepted + 3) into the conv state (dfl_gdn_rollback), driven by
-    the accepted length the device wrote (no host sync, no replay).
+    per GDN layer the fp32 recurrent state [B, Hv, Dv, Dk], the conv state [B, 3, C], the
+    conv window [B, 3 + T, C] and, by rollback mode, either per-token snapshots of the
+    last verify block [B, T, Hv, Dv, Dk] (rollback = copy snapshot accepted-1) or the
+    block's k, v, g, beta (rollback = re-advance the state over the accepted prefix,
+    dfl_gdr_recurrence with per-sequence token counts). The conv state takes window rows
+    [accepted, accepted + 3) (dfl_gdn_rollback). Both read the accepted length the device
+    wrote: no host sync.
 """
 from __future__ import annotations
 
@@ -41,6 +43,8 @@ class HybridCache:
     Tw: int                          # window rows per sequence (max block / prefill chunk)
     kinds: list = field(default_factory=list)  # per layer "gdn" / "attn"
     last_block: int = 0              # rows of the last block forwarded with snapshots
+    mode: str = "snapshot"           # rollback by per-token snapshots, or "replay" of the accepted prefix
+    rec: list = field(default_factory=list)  # replay: per GDN layer the block's k, v, g, beta
 
     @property
     def cap(self) -> int:
@@ -114,16 +118,31 @@ class HybridTargetModel:
         self._bufs: dict[int, dict[str, torch.Tensor]] = {}
 
     # ------------------------------------------------------------------
-    def make_cache(self, batch: int, cap: int, block: int = 16, window_rows: int = 128) -> HybridCache:
+    def make_cache(self, batch: int, cap: int, block: int = 16, window_rows: int = 128,
+                   rollback: str = "snapshot") -> HybridCache:
+        """rollback="snapshot": the verify forward writes the state after every token
+        (a rollback is a copy; the adapter contract's "advance the whole block, then roll
+        back" needs it). rollback="replay": the verify forward keeps the block's k, v, g,
+        beta and the rollback re-advances the state over each sequence's accepted prefix
+        (the reference's own method, adapters.py:505-560): T-fold less state traffic."""
+        if rollback not in ("snapshot", "replay"):
+            raise ValueError(f"rollback must be 'snapshot' or 'replay', not {rollback!r}")
         c, dev = self.cfg, self.device
         kv = alloc_kv(max(1, len(self.attn_index)), batch, c.num_key_value_heads, cap, c.head_dim, dev)
         n = len(self.gdn_index)
         S = (self.Hv, self.Dv, self.Dk)
         Tw = max(block, window_rows)
+        f32 = dict(dtype=torch.float32, device=dev)
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        rec = [] if rollback == "snapshot" else [
+            {"k": torch.zeros((batch, block, self.Hk, self.Dk), **bf), "v": torch.zeros((batch, block, self.Hv, self.Dv), **bf),
+             "g": torch.zeros((batch, block, self.Hv), **f32), "beta": torch.zeros((batch, block, self.Hv), **f32)}
+            for _ in range(n)]
+        snaps = [torch.zeros((batch, block, *S), **f32) for _ in range(n)] if rollback == "snapshot" else []
         return HybridCache(
             kv=kv,
             state=[torch.zeros((batch, *S), dtype=torch.float32, device=dev) for _ in range(n)],
-            snaps=[torch.zeros((batch, block, *S), dtype=torch.float32, device=dev) for _ in range(n)],
+            snaps=snaps, mode=rollback, rec=rec,
             conv=[torch.zeros((batch, 3, self.C), dtype=torch.bfloat16, device=dev) for _ in range(n)],
             window=[torch.zeros((batch, 3 + Tw, self.C), dtype=torch.bfloat16, device=dev) for _ in range(n)],
             T=block, Tw=Tw, kinds=list(self.kinds))
@@ -164,12 +183,24 @@ class HybridTargetModel:
         proj = b["proj"]
         ops.gemm(h, lw["w_in"], out=proj, ws=ws, norm_w=lw["in_norm"], sumsq_in=ss, eps=eps)
         win = cache.window[gi][seqs]
+        replay = verify and cache.mode == "replay"
+        if replay:
+            if T != cache.T:
+                raise ValueError(f"a replay-rollback cache takes verify blocks of exactly {cache.T} rows")
+            r = {k: t[seqs] for k, t in cache.rec[gi].items()}
+            kvgb = {"k": r["k"].view(M, self.Hk, self.Dk), "v": r["v"].view(M, self.Hv, self.Dv),
+                    "g": r["g"].view(M, self.Hv), "beta": r["beta"].view(M, self.Hv)}
+        else:
+            kvgb = {"k": b["gk"], "v": b["gv"], "g": b["gg"], "beta": b["gbeta"]}
         ops.gdn_prep(proj, lw["conv_w"], lw["A_log"], lw["dt_bias"], cache.conv[gi][seqs], Bs, T, self.Hk, self.Hv,
                      self.Dk, self.Dv, window=win if T <= cache.Tw else None, eps=1e-6,
-                     out={"q": b["gq"], "k": b["gk"], "v": b["gv"], "g": b["gg"], "beta": b["gbeta"]})
+                     out={"q": b["gq"], **kvgb})
         st = cache.state[gi][seqs]
         o = b["go"].view(M, self.Hv, self.Dv)
-        if verify:
+        if replay:  # outputs only: the state advances at the rollback, over the accepted prefix
+            ops.gdr_recurrence(b["gq"].view(Bs, T, self.Hk, self.Dk), r["k"], r["v"], r["g"], r["beta"], st,
+                               o=o.view(Bs, T, self.Hv, self.Dv))
+        elif verify:
             ops.gdr_recurrence(b["gq"].view(Bs, T, self.Hk, self.Dk), b["gk"].view(Bs, T, self.Hk, self.Dk),
                                b["gv"].view(Bs, T, self.Hv, self.Dv), b["gg"].view(Bs, T, self.Hv),
                                b["gbeta"].view(Bs, T, self.Hv), st, snapshots=cache.snaps[gi][seqs],
@@ -252,8 +283,15 @@ class HybridTargetModel:
         T = T or cache.T
         B = cache.state[0].shape[0] if cache.state else 0
         for gi in range(len(cache.state)):
-            ops.gdn_rollback(cache.state[gi], cache.snaps[gi], cache.conv[gi], cache.window[gi], accepted,
-                             acc_stride, B, T, self.Hv, self.Dv, self.Dk, self.C)
+            if cache.mode == "replay":
+                r = cache.rec[gi]
+                ops.gdr_recurrence(None, r["k"], r["v"], r["g"], r["beta"], cache.state[gi], state_out=cache.state[gi],
+                                   tokens=accepted, tokens_stride=acc_stride)
+                ops.gdn_rollback(None, None, cache.conv[gi], cache.window[gi], accepted, acc_stride, B, T, self.Hv,
+                                 self.Dv, self.Dk, self.C)
+            else:
+                ops.gdn_rollback(cache.state[gi], cache.snaps[gi], cache.conv[gi], cache.window[gi], accepted,
+                                 acc_stride, B, T, self.Hv, self.Dv, self.Dk, self.C)
 
     def commit_prefill(self, cache: HybridCache, seqs: slice, n_rows: torch.Tensor, T: int) -> None:
         """After a prefill chunk of T rows: conv state <- last three rows of the window."""

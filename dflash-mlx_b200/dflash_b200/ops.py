@@ -306,10 +306,11 @@ def verify_accept(state, partials, block, bs, out_tokens, B, stop_ids=None, n_st
 
 
 def gdr_recurrence(q, k, v, g, beta, state_in, state_out=None, snapshots=None, o=None, state_slot=None,
-                   state_in_bstride=None):
+                   state_in_bstride=None, tokens=None, tokens_stride: int = 1):
     """Gated-delta recurrence. q,k [B,T,Hk,Dk] bf16; v [B,T,Hv,Dv] bf16; g,beta [B,T,Hv] fp32;
-    state_in [B,Hv,Dv,Dk] fp32 (or a snapshot array with state_slot)."""
-    _need_cuda(q, k, v, g, beta, state_in, state_out, snapshots, o, state_slot)
+    state_in [B,Hv,Dv,Dk] fp32 (or a snapshot array with state_slot). tokens (device
+    int32, element b * tokens_stride): sequence b advances over that many tokens only."""
+    _need_cuda(q, k, v, g, beta, state_in, state_out, snapshots, o, state_slot, tokens)
     B, T, Hk, Dk = k.shape
     Hv, Dv = v.shape[2], v.shape[3]
     for t in (k, v, g, beta, state_in):
@@ -319,7 +320,8 @@ def gdr_recurrence(q, k, v, g, beta, state_in, state_out=None, snapshots=None, o
         raise ValueError("g, beta and the state are fp32")
     bstride = state_in_bstride if state_in_bstride is not None else Hv * Dv * Dk
     _lib.call("dfl_gdr_recurrence", _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(state_in), bstride,
-              _ptr(state_slot), _ptr(state_out), _ptr(snapshots), _ptr(o), B, T, Hk, Hv, Dk, Dv, _stream())
+              _ptr(state_slot), _ptr(state_out), _ptr(snapshots), _ptr(o), B, T, Hk, Hv, Dk, Dv, _ptr(tokens),
+              int(tokens_stride), _stream())
 
 
 def gdn_prep(proj: torch.Tensor, conv_w: torch.Tensor, A_log: torch.Tensor, dt_bias: torch.Tensor,

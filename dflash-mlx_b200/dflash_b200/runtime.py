@@ -114,7 +114,9 @@ class SpecSession:
         self.n_stop = len(stops)
         self.stop_ids = torch.tensor(stops or [0], **i32)
         self.hybrid = bool(getattr(target, "has_recurrent_state", False))
-        self.tcache = target.make_cache(B, self.cap, block=bs)
+        # hybrid targets roll back by replaying the accepted prefix (no per-token snapshots)
+        self.tcache = (target.make_cache(B, self.cap, block=bs, rollback="replay") if self.hybrid
+                       else target.make_cache(B, self.cap, block=bs))
         self.layer_ids = sorted(draft.target_layer_ids) if draft is not None else []
         ntaps = max(1, len(self.layer_ids))
         self.taps = torch.zeros((B * bs, ntaps * tc.hidden_size), dtype=torch.bfloat16, device=dev)

@@ -252,12 +252,17 @@ int dfl_gated_rmsnorm(const void* o, int64_t ldo, const void* z, int64_t ldz, co
  * [B,T,Hv] fp32, state [.,Hv,Dv,Dk] fp32. Writes o [B,T,Hv,Dv] bf16 (nullable),
  * the state after every token into snapshots [B,T,Hv,Dv,Dk] (nullable) and
  * the final state (nullable; may alias state_in). state_slot (nullable)
- * selects snapshot slot[b] of state_in (zero-copy rollback). Replaces mlx-lm
+ * selects snapshot slot[b] of state_in (zero-copy rollback). tokens (nullable):
+ * sequence b advances over its first min(T, tokens[b * tokens_stride]) tokens only
+ * (the accepted prefix of a verify block, read on the device). Replaces mlx-lm
  * gated_delta_kernel / gated_delta_ops (custom_qwen35_model.py:452-476) and,
- * with o and snapshots NULL, advance_gated_delta_states (adapters.py:93-135). */
+ * with o and snapshots NULL and tokens = the accepted lengths,
+ * advance_gated_delta_states (adapters.py:93-135, the replay of
+ * rollback_linear_caches, adapters.py:505-560). */
 int dfl_gdr_recurrence(const void* q, const void* k, const void* v, const float* g, const float* beta,
                        const float* state_in, int64_t state_in_bstride, const int32_t* state_slot, float* state_out,
-                       float* snapshots, void* o, int B, int T, int Hk, int Hv, int Dk, int Dv, void* stream);
+                       float* snapshots, void* o, int B, int T, int Hk, int Hv, int Dk, int Dv, const int32_t* tokens,
+                       int tokens_stride, void* stream);
 
 #ifdef __cplusplus
 }

@@ -451,3 +451,30 @@ def test_wide_gemm_partials_slabs():
     for s in range(S):
         acc += slabs[s]
     assert torch.equal(acc, full)
+
+
+def test_gdr_replay_of_accepted_prefix_equals_snapshot():
+    """Rollback by replay (tokens = each sequence's accepted length, read on the
+    device) leaves exactly the state the per-token snapshot of that token holds."""
+    ops = _ops()
+    B, T, Hk, Hv, D = 3, 16, 2, 4, 128
+    g = torch.Generator().manual_seed(7)
+    q = torch.nn.functional.normalize(torch.randn(B, T, Hk, D, generator=g), dim=-1).bfloat16().to(DEV)
+    k = torch.nn.functional.normalize(torch.randn(B, T, Hk, D, generator=g), dim=-1).bfloat16().to(DEV)
+    v = torch.randn(B, T, Hv, D, generator=g).bfloat16().to(DEV)
+    alpha = torch.exp(-torch.nn.functional.softplus(torch.randn(B, T, Hv, generator=g))).to(DEV)
+    beta = torch.sigmoid(torch.randn(B, T, Hv, generator=g)).to(DEV)
+    S0 = (torch.randn(B, Hv, D, D, generator=g) * 0.1).to(DEV)
+    snaps = torch.empty((B, T, Hv, D, D), device=DEV)
+    o_full = torch.empty((B, T, Hv, D), dtype=torch.bfloat16, device=DEV)
+    ops.gdr_recurrence(q, k, v, alpha, beta, S0, snapshots=snaps, o=o_full)
+    state = S0.clone()
+    acc = torch.tensor([[5, 0, 0], [16, 0, 0], [0, 0, 0]], dtype=torch.int32, device=DEV)  # stride 3
+    ops.gdr_recurrence(None, k, v, alpha, beta, state, state_out=state, tokens=acc, tokens_stride=3)
+    assert torch.equal(state[0], snaps[0, 4])
+    assert torch.equal(state[1], snaps[1, 15])
+    assert torch.equal(state[2], S0[2])  # no accepted token: untouched
+    # outputs of a verify pass without state writes equal those of the snapshot pass
+    o2 = torch.empty_like(o_full)
+    ops.gdr_recurrence(q, k, v, alpha, beta, S0, o=o2)
+    assert torch.equal(o2, o_full)

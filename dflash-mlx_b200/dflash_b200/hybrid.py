@@ -220,14 +220,12 @@ class HybridTargetModel:
             ops.gemm(x, w, ops.EPI_RESIDUAL, residual=h, out=h, out2=tap, ws=ws, sumsq_out=ss)
             return
         M = x.shape[0]
-        ws = ws or ops.workspace(x.device)
-        if ws.wide:  # K-range slabs go straight to the all-sum (no separate split reduction)
-            slabs = ops.wide_split(w.shape[0], w.shape[1], ws)
-            ops.gemm(x, w, ops.EPI_PARTIALS, out=self.tp.partial(parity, M, slabs), ws=ws)
-        else:
-            slabs = 1
-            ops.gemm(x, w, ops.EPI_STORE_F32, out=self.tp.partial(parity, M), ws=ws)
-        self.tp.reduce_residual(parity, h, tap, ss, M, slabs)
+        # one fp32 partial per rank: a split-K GEMM sums its K ranges locally first, so
+        # the peers read one slab each over NVLink (handing them the unsummed K-range
+        # slabs, DFL_EPI_PARTIALS, saves that launch but multiplies the NVLink bytes by
+        # the split: slower from 2 ranks on, 0.7x at 4)
+        ops.gemm(x, w, ops.EPI_STORE_F32, out=self.tp.partial(parity, M), ws=ws)
+        self.tp.reduce_residual(parity, h, tap, ss, M)
 
     def forward(self, tokens: torch.Tensor, pos: torch.Tensor, cache: HybridCache, max_kv: int,
                 layer_ids: list[int] | None = None, taps_out: torch.Tensor | None = None,

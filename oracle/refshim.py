@@ -10,7 +10,15 @@ numpy-compatible subset of ``mlx.core`` on the code paths exercised:
   * dflash_mlx/adapters.py ``advance_gated_delta_states`` CPU branch
     (adapters.py:93-135) uses astype / broadcasting / mx.sum;
   * dflash_mlx/custom_qwen35_model.py ``rollback_linear_caches``
-    (custom_qwen35_model.py:1029-1074) uses mx.concatenate / mx.repeat.
+    (custom_qwen35_model.py:1029-1074) uses mx.concatenate / mx.repeat;
+  * dflash_mlx/draft.py ``DFlashDraftModel`` (draft.py:68-223) runs on numpy
+    restatements of the layers it builds from: ``nn.Linear`` (y = x W^T + b),
+    ``nn.RMSNorm`` (w * x / sqrt(mean(x^2) + eps)), mlx-lm ``qwen3.MLP``
+    (down(silu(gate(x)) * up(x))), ``rope_utils.initialize_rope`` with
+    traditional=False (rotation of the two halves of the first ``dims`` features by
+    position * base^(-2i/dims)), ``base.scaled_dot_product_attention`` (GQA softmax
+    attention; mask "causal" aligned to the last key) and ``cache.KVCache``
+    (append along the sequence axis, ``offset``, ``trim``).
 
 ``install()`` registers stub modules so that those reference files import
 unchanged from the read-only reference tree; ``import_reference(root)`` loads
@@ -80,9 +88,28 @@ def install() -> None:
     mlx.core = mx
     nn = types.ModuleType("mlx.nn")
     nn.Module = _Module
-    for name in ("Linear", "RMSNorm", "Embedding", "Conv1d"):
+    for name in ("Embedding", "Conv1d"):
         setattr(nn, name, type(name, (_Module,), {}))
     nn.silu = lambda x: x / (1.0 + np.exp(-x))
+
+    class Linear(_Module):
+        def __init__(self, input_dims, output_dims, bias=True):
+            self.weight = np.zeros((output_dims, input_dims))
+            self.bias = np.zeros(output_dims) if bias else None
+
+        def __call__(self, x):
+            y = x @ self.weight.T
+            return y + self.bias if self.bias is not None else y
+
+    class RMSNorm(_Module):
+        def __init__(self, dims, eps=1e-5):
+            self.weight = np.ones(dims)
+            self.eps = eps
+
+        def __call__(self, x):
+            return self.weight * x / np.sqrt(np.mean(x * x, axis=-1, keepdims=True) + self.eps)
+
+    nn.Linear, nn.RMSNorm = Linear, RMSNorm
     layers = types.ModuleType("mlx.nn.layers")
     dist = types.ModuleType("mlx.nn.layers.distributed")
     dist.shard_inplace = dist.shard_linear = dist.sum_gradients = lambda *a, **k: None
@@ -104,6 +131,15 @@ def install() -> None:
             self.offset = 0
             self.keys = None
             self.values = None
+
+        def update_and_fetch(self, keys, values):  # [B, H, S, D], appended after offset
+            if self.keys is None:
+                self.keys, self.values = keys, values
+            else:
+                self.keys = np.concatenate([self.keys[..., :self.offset, :], keys], axis=2)
+                self.values = np.concatenate([self.values[..., :self.offset, :], values], axis=2)
+            self.offset += keys.shape[2]
+            return self.keys, self.values
 
         def trim(self, n):
             n = min(self.offset, n)
@@ -128,19 +164,58 @@ def install() -> None:
     base.BaseModelArgs = BaseModelArgs
     base.create_attention_mask = lambda *a, **k: None
     base.create_ssm_mask = lambda *a, **k: None
-    base.scaled_dot_product_attention = lambda *a, **k: None
+    def sdpa(queries, keys, values, cache=None, scale=1.0, mask=None):
+        rep = queries.shape[1] // keys.shape[1]
+        k = np.repeat(keys, rep, axis=1)
+        v = np.repeat(values, rep, axis=1)
+        s = queries @ np.swapaxes(k, -1, -2) * scale
+        if mask == "causal":
+            L, S = s.shape[-2], s.shape[-1]
+            allowed = np.arange(S)[None, :] <= (S - L + np.arange(L))[:, None]
+            s = np.where(allowed, s, -np.inf)
+        s = s - s.max(axis=-1, keepdims=True)
+        p = np.exp(s)
+        p = p / p.sum(axis=-1, keepdims=True)
+        return p @ v
+
+    base.scaled_dot_product_attention = sdpa
     gd = types.ModuleType("mlx_lm.models.gated_delta")
     for n in ("compute_g", "gated_delta_kernel", "gated_delta_ops", "gated_delta_update"):
         setattr(gd, n, lambda *a, **k: (_ for _ in ()).throw(NotImplementedError(n)))
     q3 = types.ModuleType("mlx_lm.models.qwen3")
-    q3.MLP = type("MLP", (_Module,), {})
+    class MLP(_Module):
+        def __init__(self, dim, hidden_dim):
+            self.gate_proj = Linear(dim, hidden_dim, bias=False)
+            self.up_proj = Linear(dim, hidden_dim, bias=False)
+            self.down_proj = Linear(hidden_dim, dim, bias=False)
+
+        def __call__(self, x):
+            g = self.gate_proj(x)
+            return self.down_proj(g / (1.0 + np.exp(-g)) * self.up_proj(x))
+
+    q3.MLP = MLP
     q3.create_attention_mask = lambda *a, **k: None
     q35 = types.ModuleType("mlx_lm.models.qwen3_5")
     qn = types.ModuleType("mlx_lm.models.qwen3_next")
     for n in ("Qwen3NextAttention", "Qwen3NextMLP", "Qwen3NextRMSNormGated", "Qwen3NextSparseMoeBlock"):
         setattr(qn, n, type(n, (_Module,), {}))
     rope = types.ModuleType("mlx_lm.models.rope_utils")
-    rope.initialize_rope = lambda *a, **k: None
+    class RoPE:
+        def __init__(self, dims, base=10000.0, traditional=False, scaling_config=None, max_position_embeddings=None):
+            if traditional or scaling_config:
+                raise NotImplementedError("only plain non-traditional RoPE is restated")
+            self.dims, self.base = dims, base
+
+        def __call__(self, x, offset=0):  # x [..., L, D]
+            half = self.dims // 2
+            inv = self.base ** (-np.arange(0, self.dims, 2) / self.dims)
+            ang = (offset + np.arange(x.shape[-2]))[:, None] * inv[None, :]
+            c, s = np.cos(ang), np.sin(ang)
+            x1, x2 = x[..., :half], x[..., half:self.dims]
+            return np.concatenate([x1 * c - x2 * s, x2 * c + x1 * s, x[..., self.dims:]], axis=-1)
+
+    rope.initialize_rope = lambda dims, base=10000.0, traditional=False, scaling_config=None, \
+        max_position_embeddings=None: RoPE(dims, base, traditional, scaling_config, max_position_embeddings)
     utils = types.ModuleType("mlx_lm.utils")
     utils.quantize_model = lambda *a, **k: (None, {})
     gen = types.ModuleType("mlx_lm.generate")

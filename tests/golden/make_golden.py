@@ -13,7 +13,11 @@ Fixtures:
                       stop tokens and length limits;
   gdr_rollback.npz    reference advance_gated_delta_states (adapters.py:93-135) and
                       Qwen3_5TextModel.rollback_linear_caches
-                      (custom_qwen35_model.py:1029-1074) on seeded random records.
+                      (custom_qwen35_model.py:1029-1074) on seeded random records;
+  draft_forward.npz   reference DFlashDraftModel (draft.py:68-223), 2 layers of the
+                      tiny draft width with seeded random weights, run over three
+                      calls with its KV cache (context appended, block trimmed as the
+                      runtime does at runtime.py:420), mask none and causal.
 """
 from __future__ import annotations
 
@@ -202,13 +206,65 @@ def make_gdr_fixture(ref_root: str) -> dict:
     return out
 
 
+def draft_fixture_config():
+    """The draft geometry of draft_forward.npz: the tiny draft width with 2 layers."""
+    from dflash_b200.config import DraftConfig
+    return DraftConfig(hidden_size=256, num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=2,
+                       head_dim=64, intermediate_size=768, vocab_size=4096, block_size=8, target_layer_ids=[1, 3],
+                       mask_token_id=4095)
+
+
+def make_draft_fixture(ref_root: str) -> dict:
+    draft_mod = refshim.import_reference(ref_root, ("draft",))["draft"]
+    dcfg = draft_fixture_config()
+    dw = random_draft_weights(dcfg, 6, std=0.05)
+    f64 = lambda t: t.double().numpy()  # noqa: E731
+    out: dict[str, np.ndarray] = {}
+    rng = np.random.default_rng(6)
+    calls = [(24, 8), (5, 8), (3, 8)]  # (context rows appended, block rows) per call
+    for mode in ("none", "causal"):
+        args = draft_mod.DraftArgs(model_type="qwen3", hidden_size=dcfg.hidden_size,
+                                   num_hidden_layers=dcfg.num_hidden_layers,
+                                   intermediate_size=dcfg.intermediate_size,
+                                   num_attention_heads=dcfg.num_attention_heads, rms_norm_eps=dcfg.rms_norm_eps,
+                                   vocab_size=dcfg.vocab_size, num_key_value_heads=dcfg.num_key_value_heads,
+                                   max_position_embeddings=4096, rope_theta=dcfg.rope_theta, head_dim=dcfg.head_dim,
+                                   tie_word_embeddings=True, block_size=dcfg.block_size,
+                                   dflash_config={"target_layer_ids": dcfg.target_layer_ids,
+                                                  "mask_token_id": dcfg.mask_token_id})
+        model = draft_mod.DFlashDraftModel(args)
+        model.attention_mask_mode = mode
+        model.fc.weight, model.hidden_norm.weight, model.norm.weight = f64(dw["fc"]), f64(dw["hidden_norm"]), \
+            f64(dw["norm"])
+        for layer, lw in zip(model.layers, dw["layers"]):
+            a = layer.self_attn
+            a.q_proj.weight, a.k_proj.weight, a.v_proj.weight = f64(lw["q_proj"]), f64(lw["k_proj"]), f64(lw["v_proj"])
+            a.o_proj.weight, a.q_norm.weight, a.k_norm.weight = f64(lw["o_proj"]), f64(lw["q_norm"]), f64(lw["k_norm"])
+            layer.mlp.gate_proj.weight, layer.mlp.up_proj.weight = f64(lw["gate_proj"]), f64(lw["up_proj"])
+            layer.mlp.down_proj.weight = f64(lw["down_proj"])
+            layer.input_layernorm.weight = f64(lw["input_layernorm"])
+            layer.post_attention_layernorm.weight = f64(lw["post_attention_layernorm"])
+        cache = model.make_cache()
+        for i, (ctx, bs) in enumerate(calls):
+            if mode == "none":
+                out[f"call{i}_noise"] = rng.standard_normal((1, bs, dcfg.hidden_size)) * 0.5
+                out[f"call{i}_hidden"] = rng.standard_normal((1, ctx, 2 * dcfg.hidden_size)) * 0.5
+            h = model(out[f"call{i}_noise"], out[f"call{i}_hidden"], cache)
+            out[f"{mode}_call{i}_out"] = np.asarray(h)
+            for c in cache:  # the runtime trims the block rows after each proposal (runtime.py:420)
+                c.trim(bs)
+    out["meta"] = np.array([len(calls), 6])
+    return out
+
+
 def main():
     ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
     fx = make_runtime_fixture(ref_root)
     with open(os.path.join(HERE, "runtime_loop.json"), "w") as f:
         json.dump(fx, f)
     np.savez_compressed(os.path.join(HERE, "gdr_rollback.npz"), **make_gdr_fixture(ref_root))
-    print("wrote runtime_loop.json, gdr_rollback.npz")
+    np.savez_compressed(os.path.join(HERE, "draft_forward.npz"), **make_draft_fixture(ref_root))
+    print("wrote runtime_loop.json, gdr_rollback.npz, draft_forward.npz")
 
 
 if __name__ == "__main__":

@@ -213,3 +213,29 @@ def test_hybrid_oracle_spec_is_lossless():
     assert out == trace[:len(out)]
     assert len(out) >= len(prompt) + 24
     assert any(1 < a < bs for a in accs)
+
+
+@pytest.mark.parametrize("mode", ["none", "causal"])
+def test_oracle_draft_matches_reference_draft(monkeypatch, mode):
+    """The oracle's DFlash draft forward equals the reference's own DFlashDraftModel
+    (draft.py:68-223, run on numpy restatements of its mlx layers by
+    tests/golden/make_golden.py) over three cached calls, mask none and causal
+    (fp32: the oracle's bf16 roundings switched off; 1e-5 relative)."""
+    import sys
+    sys.path.insert(0, GOLD)
+    from make_golden import draft_fixture_config
+    from dflash_b200.weights import random_draft_weights
+    monkeypatch.setattr(O, "bf16", lambda x: x.float())
+    fx = np.load(os.path.join(GOLD, "draft_forward.npz"))
+    dcfg = draft_fixture_config()
+    od = O.OracleDraft(dcfg, random_draft_weights(dcfg, int(fx["meta"][1]), std=0.05), None)
+    od.mask_mode = mode
+    cache = od.make_cache(256)
+    for i in range(int(fx["meta"][0])):
+        noise = torch.from_numpy(fx[f"call{i}_noise"][0]).float()
+        hidden = torch.from_numpy(fx[f"call{i}_hidden"][0]).float()
+        got = od(noise, hidden, cache)
+        ref = torch.from_numpy(fx[f"{mode}_call{i}_out"][0]).float()
+        torch.testing.assert_close(got, ref, rtol=1e-5, atol=1e-5)
+        for c in cache:
+            c.trim(noise.shape[0])

@@ -18,7 +18,15 @@ numpy-compatible subset of ``mlx.core`` on the code paths exercised:
     traditional=False (rotation of the two halves of the first ``dims`` features by
     position * base^(-2i/dims)), ``base.scaled_dot_product_attention`` (GQA softmax
     attention; mask "causal" aligned to the last key) and ``cache.KVCache``
-    (append along the sequence axis, ``offset``, ``trim``).
+    (append along the sequence axis, ``offset``, ``trim``);
+  * dflash_mlx/custom_qwen35_model.py ``forward_linear_layer_explicit_with_record``
+    and ``forward_full_attention_layer_explicit`` (custom_qwen35_model.py:409-540)
+    additionally use ``mx.split``, ``mx.fast.rms_norm``,
+    ``mx.fast.scaled_dot_product_attention`` and mlx-lm's ``gated_delta.compute_g``
+    (g = exp(-exp(A_log) * softplus(a + dt_bias))), ``gated_delta.gated_delta_ops``
+    (per token: S <- g S; S <- S + beta (v - S k) k^T; y = S q, q / k repeated to the
+    value heads) and the depthwise ``nn.Conv1d`` (weight [C, K, 1], no padding), all
+    restated here in numpy.
 
 ``install()`` registers stub modules so that those reference files import
 unchanged from the read-only reference tree; ``import_reference(root)`` loads
@@ -32,6 +40,22 @@ import sys
 import types
 
 import numpy as np
+
+
+def _sdpa(queries, keys, values, cache=None, scale=1.0, mask=None):
+    """Softmax attention, q [B, Hq, L, D] against k / v [B, Hkv, S, D] (GQA repeat);
+    mask "causal" lets query i see keys up to S - L + i."""
+    rep = queries.shape[1] // keys.shape[1]
+    k = np.repeat(keys, rep, axis=1)
+    v = np.repeat(values, rep, axis=1)
+    s = queries @ np.swapaxes(k, -1, -2) * scale
+    if mask == "causal":
+        L, S = s.shape[-2], s.shape[-1]
+        allowed = np.arange(S)[None, :] <= (S - L + np.arange(L))[:, None]
+        s = np.where(allowed, s, -np.inf)
+    s = s - s.max(axis=-1, keepdims=True)
+    p = np.exp(s)
+    return (p / p.sum(axis=-1, keepdims=True)) @ v
 
 
 class _Module:
@@ -75,7 +99,16 @@ def _make_core() -> types.ModuleType:
                                 categorical=lambda *a, **k: (_ for _ in ()).throw(NotImplementedError()))
     mx.random = rnd
     mx.compile = lambda f: f
-    mx.fast = types.SimpleNamespace(metal_kernel=lambda **k: None)
+    def rms_norm(x, w, eps):
+        y = x / np.sqrt(np.mean(x * x, axis=-1, keepdims=True) + eps)
+        return y if w is None else w * y
+
+    def fast_sdpa(queries, keys, values, scale=1.0, mask=None):
+        return _sdpa(queries, keys, values, scale=scale, mask=mask)
+
+    mx.fast = types.SimpleNamespace(metal_kernel=lambda **k: None, rms_norm=rms_norm,
+                                    scaled_dot_product_attention=fast_sdpa)
+    mx.split = lambda x, idx, axis=0: np.split(x, idx, axis=axis)
     return mx
 
 
@@ -88,8 +121,19 @@ def install() -> None:
     mlx.core = mx
     nn = types.ModuleType("mlx.nn")
     nn.Module = _Module
-    for name in ("Embedding", "Conv1d"):
-        setattr(nn, name, type(name, (_Module,), {}))
+    nn.Embedding = type("Embedding", (_Module,), {})
+
+    class Conv1d(_Module):  # depthwise (groups == channels), no padding: [B, L, C] -> [B, L - K + 1, C]
+        def __init__(self, in_channels, out_channels, kernel_size, groups=1, bias=False, padding=0):
+            self.weight = np.zeros((out_channels, kernel_size, in_channels // groups))
+            self.groups = groups
+
+        def __call__(self, x):
+            K = self.weight.shape[1]
+            L = x.shape[1] - K + 1
+            return sum(x[:, j:j + L, :] * self.weight[:, j, 0] for j in range(K))
+
+    nn.Conv1d = Conv1d
     nn.silu = lambda x: x / (1.0 + np.exp(-x))
 
     class Linear(_Module):
@@ -164,24 +208,32 @@ def install() -> None:
     base.BaseModelArgs = BaseModelArgs
     base.create_attention_mask = lambda *a, **k: None
     base.create_ssm_mask = lambda *a, **k: None
-    def sdpa(queries, keys, values, cache=None, scale=1.0, mask=None):
-        rep = queries.shape[1] // keys.shape[1]
-        k = np.repeat(keys, rep, axis=1)
-        v = np.repeat(values, rep, axis=1)
-        s = queries @ np.swapaxes(k, -1, -2) * scale
-        if mask == "causal":
-            L, S = s.shape[-2], s.shape[-1]
-            allowed = np.arange(S)[None, :] <= (S - L + np.arange(L))[:, None]
-            s = np.where(allowed, s, -np.inf)
-        s = s - s.max(axis=-1, keepdims=True)
-        p = np.exp(s)
-        p = p / p.sum(axis=-1, keepdims=True)
-        return p @ v
-
-    base.scaled_dot_product_attention = sdpa
+    base.scaled_dot_product_attention = _sdpa
     gd = types.ModuleType("mlx_lm.models.gated_delta")
-    for n in ("compute_g", "gated_delta_kernel", "gated_delta_ops", "gated_delta_update"):
+    for n in ("gated_delta_kernel", "gated_delta_update"):
         setattr(gd, n, lambda *a, **k: (_ for _ in ()).throw(NotImplementedError(n)))
+
+    def compute_g(A_log, a, dt_bias):
+        x = a + dt_bias
+        return np.exp(-np.exp(A_log) * np.logaddexp(0.0, x))
+
+    def gated_delta_ops(q, k, v, g, beta, state=None, mask=None):
+        # q, k [B, T, Hk, Dk]; v [B, T, Hv, Dv]; g, beta [B, T, Hv]; state [B, Hv, Dv, Dk]
+        B, T, Hk, Dk = k.shape
+        Hv, Dv = v.shape[2], v.shape[3]
+        q = np.repeat(q, Hv // Hk, axis=2)
+        k = np.repeat(k, Hv // Hk, axis=2)
+        S = np.zeros((B, Hv, Dv, Dk)) if state is None else np.array(state, dtype=np.float64)
+        ys = []
+        for t in range(T):
+            S = S * g[:, t, :, None, None]
+            kv = np.einsum("bhvk,bhk->bhv", S, k[:, t])
+            delta = (v[:, t] - kv) * beta[:, t, :, None]
+            S = S + np.einsum("bhv,bhk->bhvk", delta, k[:, t])
+            ys.append(np.einsum("bhvk,bhk->bhv", S, q[:, t]))
+        return np.stack(ys, axis=1), S
+
+    gd.compute_g, gd.gated_delta_ops = compute_g, gated_delta_ops
     q3 = types.ModuleType("mlx_lm.models.qwen3")
     class MLP(_Module):
         def __init__(self, dim, hidden_dim):
@@ -197,8 +249,20 @@ def install() -> None:
     q3.create_attention_mask = lambda *a, **k: None
     q35 = types.ModuleType("mlx_lm.models.qwen3_5")
     qn = types.ModuleType("mlx_lm.models.qwen3_next")
-    for n in ("Qwen3NextAttention", "Qwen3NextMLP", "Qwen3NextRMSNormGated", "Qwen3NextSparseMoeBlock"):
+    for n in ("Qwen3NextAttention", "Qwen3NextSparseMoeBlock"):
         setattr(qn, n, type(n, (_Module,), {}))
+
+    class RMSNormGated(_Module):  # rms_norm(x) * w, then silu(gate) * that
+        def __init__(self, dims, eps=1e-6):
+            self.weight = np.ones(dims)
+            self.eps = eps
+
+        def __call__(self, x, gate=None):
+            y = self.weight * x / np.sqrt(np.mean(x * x, axis=-1, keepdims=True) + self.eps)
+            return y if gate is None else gate / (1.0 + np.exp(-gate)) * y
+
+    qn.Qwen3NextRMSNormGated = RMSNormGated
+    qn.Qwen3NextMLP = q3.MLP
     rope = types.ModuleType("mlx_lm.models.rope_utils")
     class RoPE:
         def __init__(self, dims, base=10000.0, traditional=False, scaling_config=None, max_position_embeddings=None):

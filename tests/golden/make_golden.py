@@ -17,7 +17,11 @@ Fixtures:
   draft_forward.npz   reference DFlashDraftModel (draft.py:68-223), 2 layers of the
                       tiny draft width with seeded random weights, run over three
                       calls with its KV cache (context appended, block trimmed as the
-                      runtime does at runtime.py:420), mask none and causal.
+                      runtime does at runtime.py:420), mask none and causal;
+  hybrid_layers.npz   reference forward_linear_layer_explicit_with_record and
+                      forward_full_attention_layer_explicit (custom_qwen35_model.py:
+                      409-540) on a gated-delta and a gated-attention layer of the tiny
+                      hybrid with seeded random weights, states and cached keys.
 """
 from __future__ import annotations
 
@@ -257,6 +261,90 @@ def make_draft_fixture(ref_root: str) -> dict:
     return out
 
 
+def hybrid_fixture_weights():
+    """The tiny hybrid's seeded random weights of hybrid_layers.npz (non-trivial norms)."""
+    from dflash_b200.config import tiny_hybrid_pair
+    cfg, _ = tiny_hybrid_pair()
+    w = random_target_weights(cfg, 7, std=0.05)
+    g = torch.Generator().manual_seed(7)
+    for lw in w["layers"]:
+        for k in ("input_layernorm", "post_attention_layernorm", "q_norm", "k_norm", "norm"):
+            if k in lw:
+                lw[k] = (1 + 0.2 * torch.randn(lw[k].shape, generator=g)).to(torch.bfloat16)
+    return cfg, w
+
+
+def make_hybrid_layer_fixture(ref_root: str) -> dict:
+    from types import SimpleNamespace
+    cq = refshim.import_reference(ref_root, ("custom_qwen35_model",))["custom_qwen35_model"]
+    nn = sys.modules["mlx.nn"]
+    qn = sys.modules["mlx_lm.models.qwen3_next"]
+    q3 = sys.modules["mlx_lm.models.qwen3"]
+    rope_utils = sys.modules["mlx_lm.models.rope_utils"]
+    cfg, w = hybrid_fixture_weights()
+    f64 = lambda t: t.double().numpy()  # noqa: E731
+    H, T = cfg.hidden_size, 12
+    Hk, Hv, Dk, Dv = cfg.linear_num_key_heads, cfg.linear_num_value_heads, cfg.linear_key_head_dim, \
+        cfg.linear_value_head_dim
+    kd, vd = Hk * Dk, Hv * Dv
+    C = 2 * kd + vd
+
+    def lin(wt):
+        m = nn.Linear(wt.shape[1], wt.shape[0], bias=False)
+        m.weight = f64(wt)
+        return m
+
+    def norm(wt, eps=cfg.rms_norm_eps):
+        m = nn.RMSNorm(wt.shape[0], eps=eps)
+        m.weight = f64(wt)
+        return m
+
+    def mlp(lw):
+        m = q3.MLP(H, cfg.intermediate_size)
+        m.gate_proj.weight, m.up_proj.weight, m.down_proj.weight = f64(lw["gate_proj"]), f64(lw["up_proj"]), \
+            f64(lw["down_proj"])
+        return m
+
+    rng = np.random.default_rng(7)
+    out: dict[str, np.ndarray] = {}
+    # gated-delta layer 0
+    lw = w["layers"][0]
+    conv = nn.Conv1d(C, C, 4, groups=C)
+    conv.weight = f64(lw["conv1d"])[:, :, None]
+    gnorm = qn.Qwen3NextRMSNormGated(Dv, eps=cfg.rms_norm_eps)
+    gnorm.weight = f64(lw["norm"])
+    linear = SimpleNamespace(in_proj_qkv=lin(lw["in_proj_qkv"]), in_proj_z=lin(lw["in_proj_z"]),
+                             in_proj_b=lin(lw["in_proj_b"]), in_proj_a=lin(lw["in_proj_a"]), conv1d=conv,
+                             norm=gnorm, out_proj=lin(lw["out_proj"]), num_v_heads=Hv, num_k_heads=Hk,
+                             head_v_dim=Dv, head_k_dim=Dk, key_dim=kd, value_dim=vd, conv_kernel_size=4,
+                             A_log=f64(lw["A_log"]), dt_bias=f64(lw["dt_bias"]), training=False)
+    layer = SimpleNamespace(linear_attn=linear, input_layernorm=norm(lw["input_layernorm"]),
+                            post_attention_layernorm=norm(lw["post_attention_layernorm"]), mlp=mlp(lw))
+    out["gdn_in"] = rng.standard_normal((1, T, H))
+    out["gdn_conv0"] = rng.standard_normal((1, 3, C)) * 0.5
+    out["gdn_state0"] = rng.standard_normal((1, Hv, Dv, Dk)) * 0.1
+    res = cq.forward_linear_layer_explicit_with_record(layer, out["gdn_in"], None, out["gdn_conv0"],
+                                                       out["gdn_state0"])
+    out["gdn_out"], out["gdn_conv1"], out["gdn_state1"] = (np.asarray(x) for x in res[:3])
+    # gated full-attention layer 3 against 20 cached (post-RoPE) keys
+    lw = w["layers"][3]
+    hd, Hq, Hkv = cfg.head_dim, cfg.num_attention_heads, cfg.num_key_value_heads
+    attn = SimpleNamespace(q_proj=lin(lw["q_proj"]), k_proj=lin(lw["k_proj"]), v_proj=lin(lw["v_proj"]),
+                           o_proj=lin(lw["o_proj"]), q_norm=norm(lw["q_norm"]), k_norm=norm(lw["k_norm"]),
+                           num_attention_heads=Hq, num_key_value_heads=Hkv, scale=hd ** -0.5,
+                           rope=rope_utils.initialize_rope(cfg.rope_dim, base=cfg.rope_theta, traditional=False))
+    layer = SimpleNamespace(self_attn=attn, input_layernorm=norm(lw["input_layernorm"]),
+                            post_attention_layernorm=norm(lw["post_attention_layernorm"]), mlp=mlp(lw))
+    offset = 20
+    out["attn_in"] = rng.standard_normal((1, T, H))
+    out["attn_k0"] = rng.standard_normal((1, Hkv, offset, hd))
+    out["attn_v0"] = rng.standard_normal((1, Hkv, offset, hd))
+    h, nk, nv = cq.forward_full_attention_layer_explicit(layer, out["attn_in"], out["attn_k0"], out["attn_v0"], offset)
+    out["attn_out"], out["attn_k1"], out["attn_v1"] = np.asarray(h), np.asarray(nk), np.asarray(nv)
+    out["meta"] = np.array([7, T, offset])
+    return out
+
+
 def main():
     ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
     fx = make_runtime_fixture(ref_root)
@@ -264,7 +352,8 @@ def main():
         json.dump(fx, f)
     np.savez_compressed(os.path.join(HERE, "gdr_rollback.npz"), **make_gdr_fixture(ref_root))
     np.savez_compressed(os.path.join(HERE, "draft_forward.npz"), **make_draft_fixture(ref_root))
-    print("wrote runtime_loop.json, gdr_rollback.npz, draft_forward.npz")
+    np.savez_compressed(os.path.join(HERE, "hybrid_layers.npz"), **make_hybrid_layer_fixture(ref_root))
+    print("wrote runtime_loop.json, gdr_rollback.npz, draft_forward.npz, hybrid_layers.npz")
 
 
 if __name__ == "__main__":

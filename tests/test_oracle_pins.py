@@ -239,3 +239,35 @@ def test_oracle_draft_matches_reference_draft(monkeypatch, mode):
         torch.testing.assert_close(got, ref, rtol=1e-5, atol=1e-5)
         for c in cache:
             c.trim(noise.shape[0])
+
+
+def test_oracle_hybrid_layers_match_reference(monkeypatch):
+    """The oracle's gated-delta layer and gated full-attention layer equal the reference's
+    own forward_linear_layer_explicit_with_record / forward_full_attention_layer_explicit
+    (custom_qwen35_model.py:409-540, run under the numpy shim by
+    tests/golden/make_golden.py): layer output, new conv state, new recurrent state, new
+    keys / values (fp32; 1e-5)."""
+    import sys
+    sys.path.insert(0, GOLD)
+    from make_golden import hybrid_fixture_weights
+    monkeypatch.setattr(O, "bf16", lambda x: x.float())
+    fx = np.load(os.path.join(GOLD, "hybrid_layers.npz"))
+    cfg, w = hybrid_fixture_weights()
+    ot = O.OracleHybridTarget(cfg, w)
+    t = lambda k: torch.from_numpy(fx[k]).float()  # noqa: E731
+    cache = ot.make_cache(64)
+    g0 = cache[0]
+    g0.conv, g0.state = t("gdn_conv0")[0], t("gdn_state0")[0]
+    h = ot.gdn_layer(w["layers"][0], t("gdn_in")[0], g0)
+    torch.testing.assert_close(h, t("gdn_out")[0], rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(g0.conv, t("gdn_conv1")[0], rtol=1e-6, atol=1e-6)
+    torch.testing.assert_close(g0.state, t("gdn_state1")[0], rtol=1e-5, atol=1e-6)
+    offset, T = int(fx["meta"][2]), int(fx["meta"][1])
+    kv = cache[3]
+    kv.k[:, :offset] = t("attn_k0")[0]
+    kv.v[:, :offset] = t("attn_v0")[0]
+    kv.offset = offset
+    h = ot.attn_layer(w["layers"][3], t("attn_in")[0], torch.arange(offset, offset + T), kv)
+    torch.testing.assert_close(h, t("attn_out")[0], rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(kv.k[:, offset:offset + T], t("attn_k1")[0], rtol=1e-5, atol=1e-5)
+    torch.testing.assert_close(kv.v[:, offset:offset + T], t("attn_v1")[0], rtol=1e-5, atol=1e-5)

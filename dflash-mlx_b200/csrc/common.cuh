@@ -31,6 +31,23 @@ __device__ __forceinline__ __nv_bfloat16 f2bf(float v) { return __float2bfloat16
 // Round-trip through bf16: the value a bf16 tensor would hold.
 __device__ __forceinline__ float round_bf16(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
+// splitmix64 finaliser (Steele, Lea, Flood 2014): a bijective 64-bit mix
+__host__ __device__ __forceinline__ unsigned long long mix64(unsigned long long z) {
+  z += 0x9E3779B97F4A7C15ull;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+
+// Gumbel(0, 1) noise for (row key, column): -log(-log(u)), u uniform in (0, 1) from the
+// top 24 bits of a mix of both (Gumbel-max: argmax(logit / T + noise) is a sample of
+// softmax(logit / T))
+__device__ __forceinline__ float gumbel_noise(unsigned long long key, int col) {
+  const unsigned long long x = mix64(key ^ ((unsigned long long)(unsigned)col * 0xD1B54A32D192ED03ull));
+  const float u = ((float)(x >> 40) + 0.5f) * (1.0f / 16777216.0f);
+  return -logf(-logf(u));
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -154,6 +154,52 @@ __global__ void verify_accept_kernel(dfl_seq_state* st, const float2* __restrict
   st[b] = s;
 }
 
+// Sampling keys: row b * bs + i of a step predicts the token at absolute position
+// start + i + offset of sequence b (offset 1 for verify rows, 0 for draft rows); its key
+// depends on (seed, b, that position, tag) only, so a plain decode and a speculative
+// decode draw the same noise for the same position.
+__global__ void sample_keys_kernel(const dfl_seq_state* st, int B, int bs, unsigned long long seed, int tag, int offset,
+                                   unsigned long long* keys) {
+  grid_dependency_launch_dependents();
+  grid_dependency_wait();
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= B * bs) return;
+  const int b = r / bs, i = r % bs;
+  const long long pos = (long long)st[b].start + i + offset;
+  keys[r] = mix64(mix64(mix64(seed ^ (unsigned long long)tag) ^ (unsigned long long)b) ^ (unsigned long long)pos);
+}
+
+// Gumbel-max partials from logits: for row m and its 32-column group, (max over the group
+// of bf16(logit) * inv_t + gumbel(key[m], column), lowest index) -- the DFL_EPI_ARGMAX
+// partial layout, so argmax_reduce / draft_commit / verify_accept consume it unchanged.
+__global__ void sample_partials_kernel(const __nv_bfloat16* __restrict__ logits, long long ld, int M, int V,
+                                       const unsigned long long* __restrict__ keys, float inv_t, float2* __restrict__ part) {
+  grid_dependency_launch_dependents();
+  grid_dependency_wait();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int groups = (V + 31) / 32;
+  const long long item = (long long)blockIdx.x * (blockDim.x >> 5) + warp;
+  if (item >= (long long)M * groups) return;
+  const int m = (int)(item / groups), grp = (int)(item % groups);
+  const int n = grp * 32 + lane;
+  float best = -INFINITY;
+  int bidx = 0x7fffffff;
+  if (n < V) {
+    best = round_bf16(__bfloat162float(logits[(long long)m * ld + n])) * inv_t + gumbel_noise(keys[m], n);
+    bidx = n;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bidx, o);
+    if (ob > best || (ob == best && oi < bidx)) {
+      best = ob;
+      bidx = oi;
+    }
+  }
+  if (lane == 0) part[(long long)m * groups + grp] = make_float2(best, __int_as_float(bidx));
+}
+
 static int launch_simple(const void* fn, dim3 grid, dim3 block, void** args, cudaStream_t stream, const char* what) {
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -186,6 +232,37 @@ extern "C" int dfl_argmax_reduce(const void* partials, int M, int n_tiles, int32
   void* args[] = {&p, &M, &n_tiles, &out};
   return launch_simple((const void*)argmax_reduce_kernel, dim3((M + 7) / 8), dim3(256), args, as_stream(stream),
                        "dfl_argmax_reduce");
+}
+
+extern "C" int dfl_sample_keys(const dfl_seq_state* state, int B, int bs, uint64_t seed, int tag, int offset,
+                               uint64_t* keys, void* stream) {
+  if (B == 0) return DFL_OK;
+  if (!state || !keys || B < 0 || bs < 1) {
+    set_error("dfl_sample_keys: bad arguments");
+    return DFL_ERR_INVALID;
+  }
+  unsigned long long sd = seed;
+  unsigned long long* k = reinterpret_cast<unsigned long long*>(keys);
+  void* args[] = {&state, &B, &bs, &sd, &tag, &offset, &k};
+  return launch_simple((const void*)sample_keys_kernel, dim3((B * bs + 127) / 128), dim3(128), args,
+                       as_stream(stream), "dfl_sample_keys");
+}
+
+extern "C" int dfl_sample_partials(const void* logits, int64_t ld, int M, int V, const uint64_t* keys,
+                                   float inv_temperature, void* partials, void* stream) {
+  if (M == 0) return DFL_OK;
+  if (!logits || !keys || !partials || M < 0 || V <= 0 || ld < V || !(inv_temperature > 0.f)) {
+    set_error("dfl_sample_partials: bad arguments");
+    return DFL_ERR_INVALID;
+  }
+  const __nv_bfloat16* lg = static_cast<const __nv_bfloat16*>(logits);
+  long long l = ld;
+  const unsigned long long* k = reinterpret_cast<const unsigned long long*>(keys);
+  float2* p = static_cast<float2*>(partials);
+  void* args[] = {&lg, &l, &M, &V, &k, &inv_temperature, &p};
+  const long long items = (long long)M * ((V + 31) / 32);
+  return launch_simple((const void*)sample_partials_kernel, dim3((unsigned)((items + 7) / 8)), dim3(256), args,
+                       as_stream(stream), "dfl_sample_partials");
 }
 
 extern "C" int dfl_step_prepare(dfl_seq_state* state, const int32_t* out_tokens, int64_t out_stride, int32_t* block,

@@ -37,6 +37,8 @@ SIGNATURES: dict[str, tuple] = {
                                    c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
     "dfl_gemm_wide_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int, c_int]),
     "dfl_device_error": (c_int, [POINTER(c_int), c_int, c_void_p]),
+    "dfl_sample_keys": (c_int, [c_void_p, c_int, c_int, ctypes.c_uint64, c_int, c_int, c_void_p, c_void_p]),
+    "dfl_sample_partials": (c_int, [c_void_p, c_int64, c_int, c_int, c_void_p, c_float, c_void_p, c_void_p]),
     "dfl_tp_alloc": (c_int, [c_size_t, POINTER(c_void_p), POINTER(ctypes.c_ubyte)]),
     "dfl_tp_open": (c_int, [POINTER(ctypes.c_ubyte), POINTER(c_void_p)]),
     "dfl_tp_close": (c_int, [c_void_p]),

@@ -80,14 +80,15 @@ class DFlashGenerator:
     def generate_from_tokens(self, prompt_tokens, max_new_tokens: int = 256, temperature: float = 0.0,
                              speculative_tokens: int | None = None, verify_mode: str = "parallel-replay",
                              verify_chunk_size: int = 4, reset_peak_memory: bool = True,
-                             skip_special_tokens: bool = False, profile: bool = False) -> DFlashResult:
+                             skip_special_tokens: bool = False, profile: bool = False,
+                             seed: int = 0) -> DFlashResult:
         if reset_peak_memory:
             torch.cuda.reset_peak_memory_stats(self.target.model.device)
         output_tokens, metrics = dflash_generate(
             target=self.target.model, draft=self.draft, prompt_tokens=prompt_tokens, max_new_tokens=max_new_tokens,
             temperature=temperature, stop_token_ids=self.target.stop_token_ids(),
             layer_ids=self.draft.target_layer_ids, speculative_tokens=speculative_tokens, verify_mode=verify_mode,
-            verify_chunk_size=verify_chunk_size, profile=profile)
+            verify_chunk_size=verify_chunk_size, profile=profile, seed=seed)
         generated = output_tokens[metrics["num_input_tokens"]:]
         text = self.target.tokenizer.decode(generated, skip_special_tokens=skip_special_tokens)
         return DFlashResult(text=text, output_tokens=output_tokens, generated_tokens=generated, metrics=metrics)
@@ -95,7 +96,8 @@ class DFlashGenerator:
     def stream_from_tokens(self, prompt_tokens, max_new_tokens: int = 256, temperature: float = 0.0,
                            speculative_tokens: int | None = None, verify_mode: str = "parallel-replay",
                            verify_chunk_size: int = 4, reset_peak_memory: bool = True,
-                           skip_special_tokens: bool = False, profile: bool = False) -> Iterator[DFlashStreamEvent]:
+                           skip_special_tokens: bool = False, profile: bool = False,
+                           seed: int = 0) -> Iterator[DFlashStreamEvent]:
         """Incremental detokenisation as in api.py:116-164."""
         prompt_len = int(len(prompt_tokens))
         decoded = ""
@@ -105,7 +107,7 @@ class DFlashGenerator:
                 target=self.target.model, draft=self.draft, prompt_tokens=prompt_tokens,
                 max_new_tokens=max_new_tokens, temperature=temperature, stop_token_ids=self.target.stop_token_ids(),
                 layer_ids=self.draft.target_layer_ids, speculative_tokens=speculative_tokens, verify_mode=verify_mode,
-                verify_chunk_size=verify_chunk_size, profile=profile):
+                verify_chunk_size=verify_chunk_size, profile=profile, seed=seed):
             generated = event.output_tokens[prompt_len:]
             text = self.target.tokenizer.decode(generated, skip_special_tokens=skip_special_tokens)
             delta = text[len(decoded):] if text.startswith(decoded) else text

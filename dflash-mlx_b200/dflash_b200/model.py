@@ -309,5 +309,7 @@ class DraftModel:
             ops.gemm(b["act"], lw["w_down"], ops.EPI_RESIDUAL, residual=h, out=h, ws=ws, sumsq_out=ss)
         if head == "hidden":
             return ops.rmsnorm(h, self.norm_w, eps, out=b["xn"])
+        if head == "logits":
+            return ops.gemm(h, self.target.lm_head_w, ws=ws, norm_w=self.norm_w, sumsq_in=ss, eps=eps)
         return ops.gemm(h, self.target.lm_head_w, ops.EPI_ARGMAX, argmax_partials=b["argmax"], ws=ws,
                         norm_w=self.norm_w, sumsq_in=ss, eps=eps)

@@ -6,6 +6,7 @@ status. Tensors must live on a CUDA device: there is no CPU path.
 """
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
@@ -289,6 +290,49 @@ def argmax_reduce(partials: torch.Tensor, out: torch.Tensor | None = None) -> to
 def step_prepare(state, out_tokens, block, bs, mask_id, target_pos, draft_ctx_pos, draft_block_pos, draft_kv_len, B):
     _lib.call("dfl_step_prepare", _ptr(state), _ptr(out_tokens), out_tokens.stride(0), _ptr(block), bs, mask_id,
               _ptr(target_pos), _ptr(draft_ctx_pos), _ptr(draft_block_pos), _ptr(draft_kv_len), B, _stream())
+
+
+_M64 = (1 << 64) - 1
+SAMPLE_TAG_DRAFT, SAMPLE_TAG_TARGET = 1, 2
+
+
+def mix64(z: int) -> int:
+    """Host copy of the device splitmix64 finaliser (common.cuh)."""
+    z = (z + 0x9E3779B97F4A7C15) & _M64
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & _M64
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & _M64
+    return z ^ (z >> 31)
+
+
+def sample_key(seed: int, tag: int, b: int, pos: int) -> int:
+    """The key dfl_sample_keys gives sequence b's row predicting absolute position pos."""
+    return mix64(mix64(mix64((seed ^ tag) & _M64) ^ b) ^ pos)
+
+
+def _as_i64(k: int) -> int:
+    return k - (1 << 64) if k >= 1 << 63 else k
+
+
+def sample_keys(state, B, bs, seed, tag, offset, keys):
+    """keys[b * bs + i] for the rows of a step (uint64 bits in an int64 tensor)."""
+    _lib.call("dfl_sample_keys", _ptr(state), B, bs, ctypes.c_uint64(seed & _M64), tag, offset, _ptr(keys),
+              _stream())
+
+
+def keys_tensor(keys: list[int], device) -> torch.Tensor:
+    return torch.tensor([_as_i64(k) for k in keys], dtype=torch.int64, device=device)
+
+
+def sample_partials(logits: torch.Tensor, keys: torch.Tensor, temperature: float,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    """Gumbel-max partials of bf16 logits [M, V] at temperature (argmax_reduce gives the sample)."""
+    _need_cuda(logits, keys, out)
+    M, V = logits.shape
+    if out is None:
+        out = torch.empty((M, argmax_tiles(V), 2), dtype=torch.float32, device=logits.device)
+    _lib.call("dfl_sample_partials", _ptr(logits), _row_stride(logits), M, V, _ptr(keys), float(1.0 / temperature),
+              _ptr(out), _stream())
+    return out
 
 
 def draft_commit(state, partials, block, bs, B, inject_tokens=None, inject_len=None, inject_noise=None):

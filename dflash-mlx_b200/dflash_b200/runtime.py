@@ -50,12 +50,18 @@ def longest_prefix_match(draft_tokens: list[int], verifier_tokens: list[int]) ->
     return matched
 
 
-def sample_tokens(logits: torch.Tensor, temperature: float) -> torch.Tensor:
-    """runtime.py:22-29. Greedy (temperature < 1e-5) is the supported path."""
-    if temperature >= 1e-5:
-        raise NotImplementedError("dflash-b200 implements greedy decoding (temperature 0) only")
+def sample_tokens(logits: torch.Tensor, temperature: float, seed: int | None = None) -> torch.Tensor:
+    """runtime.py:22-29: argmax below temperature 1e-5, else a categorical sample of
+    softmax(logits / temperature) (Gumbel-max on the device; fresh keys from torch's
+    generator unless ``seed`` is given)."""
     flat = logits.reshape(-1, logits.shape[-1])
-    return torch.argmax(flat, dim=-1).reshape(logits.shape[:-1]).to(torch.int32)
+    if temperature < 1e-5:
+        return torch.argmax(flat, dim=-1).reshape(logits.shape[:-1]).to(torch.int32)
+    if seed is None:
+        seed = int(torch.randint(0, 2 ** 62, (1,)).item())
+    keys = ops.keys_tensor([ops.sample_key(seed, 0, 0, r) for r in range(flat.shape[0])], flat.device)
+    part = ops.sample_partials(flat.to(torch.bfloat16).contiguous(), keys, temperature)
+    return ops.argmax_reduce(part).reshape(logits.shape[:-1]).to(torch.int32)
 
 
 def _packed_weights(model) -> list:
@@ -76,7 +82,14 @@ class SpecSession:
 
     def __init__(self, target: TargetModel, draft: DraftModel | None, batch: int, max_total: int,
                  block_size: int, stop_token_ids: set[int] | None = None, use_graph: bool = True,
-                 max_steps: int | None = None, prefill_chunk: int = 128):
+                 max_steps: int | None = None, prefill_chunk: int = 128, temperature: float = 0.0,
+                 seed: int = 0):
+        """temperature >= 1e-5 samples (Gumbel-max on the bf16 logits, keyed by sequence and
+        absolute position: the speculative decode reproduces the plain sampled decode of the
+        same seed token for token); below it decoding is greedy (fused lm_head argmax)."""
+        self.sampled = temperature >= 1e-5
+        self.temperature = float(temperature)
+        self.seed = int(seed)
         self.target = target
         self.draft = draft
         self.B = batch
@@ -125,6 +138,9 @@ class SpecSession:
         self.inject_tokens = self.inject_len = self.inject_noise = None
         self.graph: torch.cuda.CUDAGraph | None = None
         self.host_state = torch.zeros((B, STATE_INTS), dtype=torch.int32, pin_memory=True)
+        if self.sampled:
+            self.keys = torch.zeros(B * bs, dtype=torch.int64, device=dev)
+            self.spart = torch.empty((B * bs, ops.argmax_tiles(tc.vocab_size), 2), dtype=torch.float32, device=dev)
         self._reserve_workspace()
 
     def _reserve_workspace(self) -> None:
@@ -171,6 +187,7 @@ class SpecSession:
             max_new_tokens = [max_new_tokens] * B
         firsts = []
         st = torch.zeros((B, STATE_INTS), dtype=torch.int32)
+        head = "logits" if self.sampled else "argmax"
         for b, prompt in enumerate(prompts):
             P = len(prompt)
             if P == 0:
@@ -190,14 +207,19 @@ class SpecSession:
                     # recurrent layers advance in place over the chunk; conv state from the window
                     part = self.target.forward(toks[c0:c1], pos, self.tcache, max_kv=c1, layer_ids=self.layer_ids,
                                                taps_out=taps, row_seq=rs, ws=self.ws, seqs=slice(b, b + 1),
-                                               verify=False, T=n, seq_rows=n, key_chunk=self.key_chunk)
+                                               verify=False, T=n, seq_rows=n, key_chunk=self.key_chunk,
+                                               head=head)
                     self.target.commit_prefill(self.tcache, slice(b, b + 1),
                                                torch.full((1,), n, dtype=torch.int32, device=dev), n)
                 else:
                     part = self.target.forward(toks[c0:c1], pos, self.tcache, max_kv=c1, layer_ids=self.layer_ids,
                                                taps_out=taps, row_seq=rs, ws=self.ws, seq_rows=n,
-                                               key_chunk=self.key_chunk)
-                last_part = part[n - 1:n]
+                                               key_chunk=self.key_chunk, head=head)
+                if self.sampled:  # part holds logits: sample the token at position P
+                    key = ops.keys_tensor([ops.sample_key(self.seed, ops.SAMPLE_TAG_TARGET, b, P)], dev)
+                    last_part = ops.sample_partials(part[n - 1:n], key, self.temperature)
+                else:
+                    last_part = part[n - 1:n]
                 if self.draft is not None:
                     self.draft.ingest_context(taps, pos, self.dcache, row_seq=rs, ws=self.ws)
             first = int(ops.argmax_reduce(last_part).item())
@@ -231,7 +253,11 @@ class SpecSession:
             d = self.draft
             d.ingest_context(self.taps, self.dpos_ctx, self.dcache, row_seq=self.row_seq, ws=self.ws)
             part = d.forward_block(self.block, self.dpos_blk, self.dcache, self.dkv_len, self.cap,
-                                   row_seq=self.row_seq, ws=self.ws, seq_rows=bs, key_chunk=self.key_chunk)
+                                   row_seq=self.row_seq, ws=self.ws, seq_rows=bs, key_chunk=self.key_chunk,
+                                   head="logits" if self.sampled else "argmax")
+            if self.sampled:  # draft row i proposes the token at position start + i
+                ops.sample_keys(self.state, B, bs, self.seed, ops.SAMPLE_TAG_DRAFT, 0, self.keys)
+                part = ops.sample_partials(part, self.keys, self.temperature, out=self.spart)
             ops.draft_commit(self.state, part, self.block, bs, B, self.inject_tokens, self.inject_len,
                              self.inject_noise)
 
@@ -239,7 +265,10 @@ class SpecSession:
         """Target verify forward + accept (parallel-replay, runtime.py:117-163)."""
         part = self.target.forward(self.block, self.tpos, self.tcache, max_kv=self.cap, layer_ids=self.layer_ids,
                                    taps_out=self.taps, row_seq=self.row_seq, ws=self.ws, seq_rows=self.bs,
-                                   key_chunk=self.key_chunk)
+                                   key_chunk=self.key_chunk, head="logits" if self.sampled else "argmax")
+        if self.sampled:  # verify row i predicts the token at position start + i + 1
+            ops.sample_keys(self.state, self.B, self.bs, self.seed, ops.SAMPLE_TAG_TARGET, 1, self.keys)
+            part = ops.sample_partials(part, self.keys, self.temperature, out=self.spart)
         ops.verify_accept(self.state, part, self.block, self.bs, self.out_tokens, self.B,
                           stop_ids=self.stop_ids, n_stop=self.n_stop, accept_log=self.accept_log)
         if self.hybrid:
@@ -349,10 +378,10 @@ def dflash_generate_stream(target: TargetModel, draft: DraftModel, prompt_tokens
                            temperature: float, stop_token_ids: set[int], layer_ids: list[int] | None,
                            speculative_tokens: int | None, verify_mode: str = "parallel-replay",
                            verify_chunk_size: int = 4, profile: bool = False,
-                           use_graph: bool = True) -> Iterator[DFlashRuntimeEvent]:
-    """Single-sequence generator with the reference's event and metrics shape (runtime.py:360-555)."""
-    if temperature >= 1e-5:
-        raise NotImplementedError("dflash-b200 implements greedy decoding (temperature 0) only")
+                           use_graph: bool = True, seed: int = 0) -> Iterator[DFlashRuntimeEvent]:
+    """Single-sequence generator with the reference's event and metrics shape (runtime.py:360-555).
+    temperature >= 1e-5 samples (sample_tokens, runtime.py:22-29) with noise keyed by
+    ``seed`` and absolute position, so the output equals the plain sampled decode."""
     if verify_mode not in VERIFY_MODES:
         raise ValueError(f"unknown verify_mode {verify_mode!r}")
     if layer_ids is not None and draft is not None and sorted(layer_ids) != sorted(draft.target_layer_ids):
@@ -364,7 +393,8 @@ def dflash_generate_stream(target: TargetModel, draft: DraftModel, prompt_tokens
     block_size = bs_max if speculative_tokens is None else max(1, min(speculative_tokens, bs_max))
     use_draft = draft if block_size > 1 else None
     total_max = prompt_len + max_new_tokens
-    sess = SpecSession(target, use_draft, 1, total_max, block_size, stop_token_ids, use_graph=use_graph)
+    sess = SpecSession(target, use_draft, 1, total_max, block_size, stop_token_ids, use_graph=use_graph,
+                       temperature=temperature, seed=seed)
 
     torch.cuda.synchronize(target.device)
     t0 = time.perf_counter()
@@ -422,11 +452,11 @@ def dflash_generate_stream(target: TargetModel, draft: DraftModel, prompt_tokens
 def dflash_generate(target: TargetModel, draft: DraftModel, prompt_tokens, max_new_tokens: int, temperature: float,
                     stop_token_ids: set[int], layer_ids: list[int] | None, speculative_tokens: int | None,
                     verify_mode: str = "parallel-replay", verify_chunk_size: int = 4, profile: bool = False,
-                    use_graph: bool = True) -> tuple[list[int], dict[str, Any]]:
+                    use_graph: bool = True, seed: int = 0) -> tuple[list[int], dict[str, Any]]:
     final = None
     for event in dflash_generate_stream(target, draft, prompt_tokens, max_new_tokens, temperature, stop_token_ids,
                                         layer_ids, speculative_tokens, verify_mode, verify_chunk_size, profile,
-                                        use_graph):
+                                        use_graph, seed):
         if event.finished:
             final = event
     if final is None or final.metrics is None:

@@ -202,6 +202,18 @@ int dfl_attention(const void* q, const void* k_cache, const void* v_cache, int64
  * Greedy argmax from DFL_EPI_ARGMAX partials (runtime.py:22-29 at temperature 0). */
 int dfl_argmax_reduce(const void* partials, int M, int n_tiles, int32_t* out, void* stream);
 
+/* Temperature sampling (sample_tokens, runtime.py:22-29, at temperature >= 1e-5) by
+ * Gumbel-max. dfl_sample_keys: key of row b * bs + i = a mix of (seed, tag, b,
+ * state[b].start + i + offset) -- the absolute position the row predicts (offset 1 for
+ * verify rows, 0 for draft rows), so plain and speculative decoding draw the same noise
+ * for the same position. dfl_sample_partials: for each row of bf16 logits [M, V] (row
+ * stride ld) and each 32 columns, (max of bf16(logit) * inv_temperature +
+ * Gumbel(key[row], column), lowest index) in the DFL_EPI_ARGMAX partial layout. */
+int dfl_sample_keys(const dfl_seq_state* state, int B, int bs, uint64_t seed, int tag, int offset, uint64_t* keys,
+                    void* stream);
+int dfl_sample_partials(const void* logits, int64_t ld, int M, int V, const uint64_t* keys, float inv_temperature,
+                        void* partials, void* stream);
+
 /* Builds block = [out[start], mask_id x (bs-1)] (runtime.py:408) and the
  * verify / draft positions for every sequence. */
 int dfl_step_prepare(dfl_seq_state* state, const int32_t* out_tokens, int64_t out_stride, int32_t* block, int bs,

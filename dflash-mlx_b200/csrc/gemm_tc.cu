@@ -63,8 +63,10 @@ __device__ __forceinline__ unsigned long long gtimer() {
   return t;
 }
 #define TC_STAMP(k) g_tc_trace[blockIdx.x][k] = gtimer()
+#define TC_STAMP_AT(c, k) g_tc_trace[(c) & 8191][k] = gtimer()
 #else
 #define TC_STAMP(k)
+#define TC_STAMP_AT(c, k)
 #endif
 
 constexpr int TC_NT = 128;  // W rows per tile (MMA M)
@@ -199,7 +201,7 @@ __device__ __forceinline__ int tc_unit_owner(long long u, long long U, int G) {
 // for the 16 rows m0 .. m0 + 15; q is the thread's TMEM lane quadrant.
 template <int EPI>
 __device__ __forceinline__ void tc_epilogue(const TcArgs& a, float* v, int m0, int nt, int q, int lane,
-                                            float* xchg) {
+                                            float* xchg, const float* rpre = nullptr) {
   const int c = q * 32 + lane;
   const int n = nt * TC_NT + c;
   if constexpr (EPI == DFL_EPI_STORE_F32) {
@@ -213,9 +215,14 @@ __device__ __forceinline__ void tc_epilogue(const TcArgs& a, float* v, int m0, i
       // gather all 16 residual values before the first store: y may alias the residual
       // (in-place update), so interleaved loads and stores would serialise 16 L2 round trips
       float r[TC_BM];
+      if (rpre) {
 #pragma unroll
-      for (int t = 0; t < TC_BM; ++t)
-        r[t] = (col_ok && m0 + t < a.M) ? bf2f(a.res[(long long)(m0 + t) * a.ldr + n]) : 0.f;
+        for (int t = 0; t < TC_BM; ++t) r[t] = rpre[t];
+      } else {
+#pragma unroll
+        for (int t = 0; t < TC_BM; ++t)
+          r[t] = (col_ok && m0 + t < a.M) ? bf2f(a.res[(long long)(m0 + t) * a.ldr + n]) : 0.f;
+      }
 #pragma unroll
       for (int t = 0; t < TC_BM; ++t) v[t] = r[t] + round_bf16(v[t]);
     }
@@ -544,27 +551,19 @@ __device__ __forceinline__ uint32_t cluster_map(uint32_t saddr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(saddr), "r"(rank));
   return r;
 }
-__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
-  float4 v;
-  asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];\n" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
-  return v;
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release;\n" ::: "memory");
 }
-// sum over the cluster's ranks (in rank order) of column `col` (16 rows) of the red tiles
-__device__ __forceinline__ void cluster_reduce_col(uint32_t red_saddr, int col, int S, float* v) {
-#pragma unroll
-  for (int t = 0; t < TC_BM; ++t) v[t] = 0.f;
-  for (int rr = 0; rr < S; ++rr) {
-    const uint32_t base = cluster_map(red_saddr + (uint32_t)(col * TC_BM * 4), (uint32_t)rr);
-#pragma unroll
-    for (int t4 = 0; t4 < TC_BM / 4; ++t4) {
-      const float4 f = ld_cluster_f4(base + t4 * 16);
-      v[4 * t4] += f.x;
-      v[4 * t4 + 1] += f.y;
-      v[4 * t4 + 2] += f.z;
-      v[4 * t4 + 3] += f.w;
-    }
-  }
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire;\n" ::: "memory");
 }
+// 16-byte store into another CTA's shared memory that completes on an mbarrier there
+__device__ __forceinline__ void st_async_v4(uint32_t addr, float x, float y, float z, float w, uint32_t bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];\n" ::"r"(addr),
+               "f"(x), "f"(y), "f"(z), "f"(w), "r"(bar)
+               : "memory");
+}
+constexpr int TC_CSK_SLOT_BYTES = 32 * TC_BM * 4;  // one rank's partial of a 32-column group
 
 template <int EPI>
 __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
@@ -576,8 +575,8 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
   uint64_t* empty = full + TC_STAGES;
   uint64_t* xready = empty + TC_STAGES;
   uint64_t* accf = xready + TC_STAGES;
+  uint64_t* recv = accf + 1;  // [2]: pushes of the column groups this rank owns
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + TC_OFF_TMEM);
-  float* red = reinterpret_cast<float*>(smem + TC_OFF_XCHG);  // [128 cols][16 rows] fp32
   __nv_bfloat16* s_nw = reinterpret_cast<__nv_bfloat16*>(smem + TC_OFF_NORM);
   __shared__ float s_inv[TC_BM];
 
@@ -587,6 +586,9 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
   const int j0 = r * a.kb / S, j1 = (r + 1) * a.kb / S;
   const int n_units = j1 - j0;
   const bool norm = a.norm_w != nullptr;
+  const int cta_lin = r + S * (nt + a.n_tiles * mt);
+  (void)cta_lin;
+  if (threadIdx.x == 0) TC_STAMP_AT(cta_lin, 0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < TC_STAGES; ++s) {
@@ -595,7 +597,12 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
       mbar_init(&xready[s], 128);
     }
     mbar_init(&accf[0], 1);
+    // owned units: column groups q (or SILU gate/up pairs) with unit % S == r
+    const int U = EPI == DFL_EPI_SILU_MUL ? 2 : 4;
+    const int per = EPI == DFL_EPI_SILU_MUL ? 2 * S : S - 1;
+    for (int u = r; u < U && per > 0; u += S) mbar_init(&recv[u / S], 1);
     fence_barrier_init();
+    for (int u = r; u < U && per > 0; u += S) mbar_expect_tx(&recv[u / S], (uint32_t)(per * TC_CSK_SLOT_BYTES));
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
@@ -607,6 +614,12 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   grid_dependency_launch_dependents();
+  // residual columns of the warps that finish a column group: loaded while the weights
+  // stream (a load issued after the reduction waits behind the other clusters' streams)
+  float rres[TC_BM], v[TC_BM];
+#pragma unroll
+  for (int t = 0; t < TC_BM; ++t) rres[t] = v[t] = 0.f;
+  if (threadIdx.x == 0) TC_STAMP_AT(cta_lin, 1);
 
   if (warp == 0) {
     if (lane == 0 && n_units > 0) {
@@ -619,6 +632,7 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
         bulk_load(smem + i * TC_W_BYTES, a.wt + (ubase + i) * TC_W_BYTES, TC_W_BYTES, &full[i], pol_w);
       }
       grid_dependency_wait();  // X is produced by the previous kernel
+      TC_STAMP_AT(cta_lin, 2);
       for (int i = 0; i < pre; ++i)
         tma_load_2d(&xmap, &full[i], smem + TC_OFF_X + i * TC_X_BYTES, (j0 + i) * TC_BK, mt * TC_BM, pol_x);
       int issued = pre;
@@ -641,6 +655,7 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
       for (int i = 0; i < n_units; ++i) {
         const int s = i % TC_STAGES;
         if (!mbar_wait(norm ? &xready[s] : &full[s], (i / TC_STAGES) & 1, 303, a.err)) break;
+        if (i == 0) TC_STAMP_AT(cta_lin, 3);
         tc_fence_after();
         const uint64_t ad = sw128_desc(w0 + s * TC_W_BYTES);
         const uint64_t bd = sw128_desc(x0 + s * TC_X_BYTES);
@@ -651,6 +666,7 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
         tc_commit(&empty[s]);
       }
       tc_commit(&accf[0]);
+      TC_STAMP_AT(cta_lin, 4);
     }
     __syncwarp();
   } else {
@@ -660,6 +676,14 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
       for (int k = et * 8; k < a.K; k += 128 * 8)
         *reinterpret_cast<uint4*>(s_nw + k) = *reinterpret_cast<const uint4*>(a.norm_w + k);
     grid_dependency_wait();
+    if constexpr (EPI == DFL_EPI_RESIDUAL) {
+      const int n = nt * TC_NT + q * 32 + lane;
+      if ((q % S) == r && n < a.N) {
+#pragma unroll
+        for (int t = 0; t < TC_BM; ++t)
+          if (mt * TC_BM + t < a.M) rres[t] = bf2f(a.res[(long long)(mt * TC_BM + t) * a.ldr + n]);
+      }
+    }
     if (norm) {
       if (et < TC_BM) {
         const int m = mt * TC_BM + et;
@@ -688,29 +712,61 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
         mbar_arrive(&xready[s]);
       }
     }
-    float v[TC_BM];
-#pragma unroll
-    for (int t = 0; t < TC_BM; ++t) v[t] = 0.f;
     if (n_units > 0 && mbar_wait(&accf[0], 0, 305, a.err)) {
+      if (threadIdx.x == 64) TC_STAMP_AT(cta_lin, 5);
       tc_fence_after();
       tc_ld_acc(tmem + ((uint32_t)(q * 32) << 16), v);
       tc_fence_before();
     }
-    float4* mine = reinterpret_cast<float4*>(red + (q * 32 + lane) * TC_BM);
-#pragma unroll
-    for (int t4 = 0; t4 < TC_BM / 4; ++t4) mine[t4] = make_float4(v[4 * t4], v[4 * t4 + 1], v[4 * t4 + 2], v[4 * t4 + 3]);
   }
-  cluster_sync_all();  // every rank's partial tile is in its shared memory
+  // Cluster reduction by push: every rank sends its partial column group to the group's
+  // owner rank with st.async into the owner's (now idle) weight ring, completing on an
+  // mbarrier there; the owner sums the ranks in rank order. Phase 1 of the cluster barrier:
+  // every ring is free (each CTA's epilogue warps passed accf, so its MMAs are done).
+  if (threadIdx.x == 64) TC_STAMP_AT(cta_lin, 6);
+  cluster_sync_all();
+  if (threadIdx.x == 64) TC_STAMP_AT(cta_lin, 7);
+  constexpr bool SILU = EPI == DFL_EPI_SILU_MUL;
+  const int slots = SILU ? 2 * S : S - 1;  // per owned unit
   if (warp >= TC_EPI_WARP0) {
-    const int q = warp & 3;  // 32-column group of the tile handled by this warp
-    const uint32_t red_s = smem_u32(smem + TC_OFF_XCHG);
-    if constexpr (EPI == DFL_EPI_SILU_MUL) {
-      // gate groups 0 / 2 pair with up groups 1 / 3 (weights packed per 64 rows)
-      if (!(q & 1) && ((q >> 1) % S) == r) {
+    const int q = warp & 3;
+    const int u = SILU ? q >> 1 : q, gi = SILU ? q & 1 : 0;
+    const int owner = u % S, js = u / S;
+    if (SILU || owner != r) {
+      const int slot = SILU ? 2 * r + gi : (r < owner ? r : r - 1);
+      const uint32_t dst = cluster_map(smem_u32(smem + (js * slots + slot) * TC_CSK_SLOT_BYTES + lane * 64), owner);
+      const uint32_t bar = cluster_map(smem_u32(&recv[js]), owner);
+#pragma unroll
+      for (int t4 = 0; t4 < TC_BM / 4; ++t4)
+        st_async_v4(dst + t4 * 16, v[4 * t4], v[4 * t4 + 1], v[4 * t4 + 2], v[4 * t4 + 3], bar);
+    }
+  }
+  cluster_arrive();  // phase 2: this CTA's pushes are issued
+  if (warp >= TC_EPI_WARP0) {
+    const int q = warp & 3;
+    const int u = SILU ? q >> 1 : q;
+    const int owner = u % S, js = u / S;
+    if (owner == r && (!SILU || !(q & 1))) {
+      if (slots > 0 && !mbar_wait(&recv[js], 0, 306, a.err)) {
+        // gave up: the sums below read whatever arrived; the error word reports it
+      }
+      if (lane == 0) TC_STAMP_AT(cta_lin, 10 + (q & 1));
+      const float* base = reinterpret_cast<const float*>(smem + js * slots * TC_CSK_SLOT_BYTES) + lane * 16;
+      if constexpr (SILU) {
         float gv[TC_BM], uv[TC_BM];
-        cluster_reduce_col(red_s, q * 32 + lane, S, gv);
-        cluster_reduce_col(red_s, (q + 1) * 32 + lane, S, uv);
-        const int on = nt * 64 + (q >> 1) * 32 + lane;
+#pragma unroll
+        for (int t = 0; t < TC_BM; ++t) gv[t] = uv[t] = 0.f;
+        for (int rr = 0; rr < S; ++rr) {
+          const float4* g4 = reinterpret_cast<const float4*>(base + (2 * rr) * (TC_CSK_SLOT_BYTES / 4));
+          const float4* u4 = reinterpret_cast<const float4*>(base + (2 * rr + 1) * (TC_CSK_SLOT_BYTES / 4));
+#pragma unroll
+          for (int t4 = 0; t4 < TC_BM / 4; ++t4) {
+            const float4 g = g4[t4], w = u4[t4];
+            gv[4 * t4] += g.x; gv[4 * t4 + 1] += g.y; gv[4 * t4 + 2] += g.z; gv[4 * t4 + 3] += g.w;
+            uv[4 * t4] += w.x; uv[4 * t4 + 1] += w.y; uv[4 * t4 + 2] += w.z; uv[4 * t4 + 3] += w.w;
+          }
+        }
+        const int on = nt * 64 + u * 32 + lane;
         if (nt * TC_NT + q * 32 + lane < a.N) {
 #pragma unroll
           for (int t = 0; t < TC_BM; ++t) {
@@ -723,16 +779,33 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
             }
           }
         }
-      }
-    } else {
-      if ((q % S) == r) {
-        float v[TC_BM];
-        cluster_reduce_col(red_s, q * 32 + lane, S, v);
-        tc_epilogue<EPI>(a, v, mt * TC_BM, nt, q, lane, nullptr);
+      } else {
+        float acc[TC_BM];
+#pragma unroll
+        for (int t = 0; t < TC_BM; ++t) acc[t] = 0.f;
+        for (int rr = 0; rr < S; ++rr) {  // rank order; this rank's own partial from registers
+          if (rr == r) {
+#pragma unroll
+            for (int t = 0; t < TC_BM; ++t) acc[t] += v[t];
+          } else {
+            const float4* p4 =
+                reinterpret_cast<const float4*>(base + (rr < r ? rr : rr - 1) * (TC_CSK_SLOT_BYTES / 4));
+#pragma unroll
+            for (int t4 = 0; t4 < TC_BM / 4; ++t4) {
+              const float4 f = p4[t4];
+              acc[4 * t4] += f.x; acc[4 * t4 + 1] += f.y; acc[4 * t4 + 2] += f.z; acc[4 * t4 + 3] += f.w;
+            }
+          }
+        }
+        if (lane == 0) TC_STAMP_AT(cta_lin, 12 + (q & 1));
+        tc_epilogue<EPI>(a, acc, mt * TC_BM, nt, q, lane, nullptr, rres);
+        if (lane == 0) TC_STAMP_AT(cta_lin, 14 + (q & 1));
       }
     }
   }
-  cluster_sync_all();  // no rank leaves while another still reads its shared memory
+  if (threadIdx.x == 64) TC_STAMP_AT(cta_lin, 8);
+  cluster_wait();  // no CTA leaves while a push to it may be in flight
+  if (threadIdx.x == 64) TC_STAMP_AT(cta_lin, 9);
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

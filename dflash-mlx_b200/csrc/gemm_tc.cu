@@ -554,6 +554,9 @@ __device__ __forceinline__ uint32_t cluster_map(uint32_t saddr, uint32_t rank) {
 __device__ __forceinline__ void cluster_arrive() {
   asm volatile("barrier.cluster.arrive.release;\n" ::: "memory");
 }
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed;\n" ::: "memory");
+}
 __device__ __forceinline__ void cluster_wait() {
   asm volatile("barrier.cluster.wait.acquire;\n" ::: "memory");
 }
@@ -564,20 +567,29 @@ __device__ __forceinline__ void st_async_v4(uint32_t addr, float x, float y, flo
                : "memory");
 }
 constexpr int TC_CSK_SLOT_BYTES = 32 * TC_BM * 4;  // one rank's partial of a 32-column group
+// Cluster-kernel shared memory: ring | X | barriers | TMEM slot | norm weights (K*2 when
+// fused) | receive slots (when they fit beside three co-resident CTAs; otherwise the
+// pushes land in the idle ring).
+constexpr int CSK_OFF_BAR = TC_OFF_X + TC_STAGES * TC_X_BYTES;
+constexpr int CSK_OFF_TMEM = CSK_OFF_BAR + TC_NBAR * 8;
+constexpr int CSK_OFF_NORM = (CSK_OFF_TMEM + 16 + 127) & ~127;
+constexpr int CSK_SMEM_PER_SM = 228 * 1024, CSK_RESERVED_PER_CTA = 1024;
 
 template <int EPI>
 __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
-    gemm_csk_kernel(const __grid_constant__ CUtensorMap xmap, TcArgs a, int S) {
+    gemm_csk_kernel(const __grid_constant__ CUtensorMap xmap, TcArgs a, int S, int recv_off) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + TC_OFF_BAR);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + CSK_OFF_BAR);
   uint64_t* empty = full + TC_STAGES;
   uint64_t* xready = empty + TC_STAGES;
   uint64_t* accf = xready + TC_STAGES;
   uint64_t* recv = accf + 1;  // [2]: pushes of the column groups this rank owns
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + TC_OFF_TMEM);
-  __nv_bfloat16* s_nw = reinterpret_cast<__nv_bfloat16*>(smem + TC_OFF_NORM);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + CSK_OFF_TMEM);
+  __nv_bfloat16* s_nw = reinterpret_cast<__nv_bfloat16*>(smem + CSK_OFF_NORM);
+  unsigned char* rbuf = smem + recv_off;  // receive slots (offset 0: the weight ring)
+  const bool dedicated = recv_off != 0;
   __shared__ float s_inv[TC_BM];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -614,6 +626,9 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   grid_dependency_launch_dependents();
+  // dedicated receive slots: the only cluster-wide precondition of a push is that the
+  // owner's barriers are initialised (arrive now, wait just before pushing)
+  if (dedicated) cluster_arrive_relaxed();  // the barrier inits were published by fence.mbarrier_init
   // residual columns of the warps that finish a column group: loaded while the weights
   // stream (a load issued after the reduction waits behind the other clusters' streams)
   float rres[TC_BM], v[TC_BM];
@@ -720,11 +735,14 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
     }
   }
   // Cluster reduction by push: every rank sends its partial column group to the group's
-  // owner rank with st.async into the owner's (now idle) weight ring, completing on an
-  // mbarrier there; the owner sums the ranks in rank order. Phase 1 of the cluster barrier:
-  // every ring is free (each CTA's epilogue warps passed accf, so its MMAs are done).
+  // owner rank with st.async into the owner's receive slots, completing on an mbarrier
+  // there; the owner sums the ranks in rank order. Slots in the weight ring need every
+  // ring free first (each CTA's epilogue warps passed accf, so its MMAs are done).
   if (threadIdx.x == 64) TC_STAMP_AT(cta_lin, 6);
-  cluster_sync_all();
+  if (dedicated)
+    cluster_wait();
+  else
+    cluster_sync_all();
   if (threadIdx.x == 64) TC_STAMP_AT(cta_lin, 7);
   constexpr bool SILU = EPI == DFL_EPI_SILU_MUL;
   const int slots = SILU ? 2 * S : S - 1;  // per owned unit
@@ -734,7 +752,7 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
     const int owner = u % S, js = u / S;
     if (SILU || owner != r) {
       const int slot = SILU ? 2 * r + gi : (r < owner ? r : r - 1);
-      const uint32_t dst = cluster_map(smem_u32(smem + (js * slots + slot) * TC_CSK_SLOT_BYTES + lane * 64), owner);
+      const uint32_t dst = cluster_map(smem_u32(rbuf + (js * slots + slot) * TC_CSK_SLOT_BYTES + lane * 64), owner);
       const uint32_t bar = cluster_map(smem_u32(&recv[js]), owner);
 #pragma unroll
       for (int t4 = 0; t4 < TC_BM / 4; ++t4)
@@ -751,7 +769,7 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
         // gave up: the sums below read whatever arrived; the error word reports it
       }
       if (lane == 0) TC_STAMP_AT(cta_lin, 10 + (q & 1));
-      const float* base = reinterpret_cast<const float*>(smem + js * slots * TC_CSK_SLOT_BYTES) + lane * 16;
+      const float* base = reinterpret_cast<const float*>(rbuf + js * slots * TC_CSK_SLOT_BYTES) + lane * 16;
       if constexpr (SILU) {
         float gv[TC_BM], uv[TC_BM];
 #pragma unroll
@@ -1394,6 +1412,22 @@ extern "C" int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w_packed, i
   cfg.gridDim = p.S ? dim3(p.S, p.n_tiles, p.m_tiles) : dim3(p.grid1 * p.m_tiles);
   cfg.blockDim = dim3(TC_THREADS);
   cfg.dynamicSmemBytes = TC_SMEM_BASE + (norm_w ? (size_t)K * 2 : 0);
+  int recv_off = 0;
+  if (p.S) {
+    const bool silu = epilogue == DFL_EPI_SILU_MUL;
+    const int units = silu ? 2 : 4;
+    const int owned = (units + p.S - 1) / p.S;
+    const int slots = silu ? 2 * p.S : p.S - 1;
+    const size_t recv = (size_t)owned * slots * TC_CSK_SLOT_BYTES;
+    const size_t normb = norm_w ? (size_t)K * 2 : 0;
+    const size_t ded = CSK_OFF_NORM + normb + recv + 1024;
+    if (recv > 0 && 3 * (ded + CSK_RESERVED_PER_CTA) <= (size_t)CSK_SMEM_PER_SM) {
+      recv_off = (int)(CSK_OFF_NORM + normb);
+      cfg.dynamicSmemBytes = ded;
+    } else {
+      cfg.dynamicSmemBytes = CSK_OFF_NORM + normb + 1024;
+    }
+  }
   cfg.stream = as_stream(stream);
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -1421,7 +1455,7 @@ extern "C" int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w_packed, i
       if (DFL_TC_SMAX > 8) cudaFuncSetAttribute(gemm_csk_kernel<E>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1); \
       init = true;                                                                                          \
     }                                                                                                       \
-    err = p.S ? cudaLaunchKernelEx(&cfg, gemm_csk_kernel<E>, *xm, a, p.S)                                   \
+    err = p.S ? cudaLaunchKernelEx(&cfg, gemm_csk_kernel<E>, *xm, a, p.S, recv_off)                                   \
               : cudaLaunchKernelEx(&cfg, gemm_tc_kernel<E>, *xm, a);                                        \
     break;                                                                                                  \
   }

@@ -539,9 +539,13 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
 // Cluster split-K variant for GEMMs with few 128-row tiles (N / 128 < 148):
 // a thread-block cluster of S CTAs (S <= 8) owns one tile, CTA rank r streams the
 // fixed k-range [r*kb/S, (r+1)*kb/S), and the S partial tiles are reduced through
-// distributed shared memory after a hardware cluster barrier, in rank order (no
-// global scratch, no atomics, no memory fences on the critical path). Each
-// 32-column group of the tile is finished by one rank.
+// distributed shared memory in rank order (no global scratch, no atomics). Each
+// 32-column group of the tile is finished by one owner rank: every other rank pushes
+// its fp32 partial columns into the owner's receive slots with st.async (completing on
+// an mbarrier in the owner), so no rank waits on a remote load; the owner sums the
+// ranks in rank order. Residual columns are loaded by the owner while the weights
+// stream. (Pulling the partials with ld.shared::cluster after a cluster barrier cost
+// 4-9 us per launch while other clusters' weight streams held the SM-to-SM network.)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");

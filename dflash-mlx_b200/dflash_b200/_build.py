@@ -17,6 +17,10 @@ CSRC = PKG_DIR.parent / "csrc"
 INCLUDE = PKG_DIR.parent.parent / "include"
 LIB_PATH = PKG_DIR / "libdflash_b200.so"
 OBJ_DIR = PKG_DIR.parent / "_build"
+# diagnostic build with per-CTA phase timestamps in the weight-streaming GEMMs
+# (read by ``python -m dflash_b200.gemm_trace``; load it with DFLASH_B200_LIB=<path>)
+TRACE_LIB_PATH = PKG_DIR / "libdflash_b200_trace.so"
+TRACE_OBJ_DIR = PKG_DIR.parent / "_build_trace"
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -43,26 +47,27 @@ def _stale(lib: Path) -> bool:
     return any(p.stat().st_mtime > t for p in deps)
 
 
-def build(force: bool = False, verbose: bool = False) -> Path:
-    if not force and not _stale(LIB_PATH):
-        return LIB_PATH
-    OBJ_DIR.mkdir(exist_ok=True)
+def build(force: bool = False, verbose: bool = False, trace: bool = False) -> Path:
+    lib_path, obj_dir = (TRACE_LIB_PATH, TRACE_OBJ_DIR) if trace else (LIB_PATH, OBJ_DIR)
+    if not force and not _stale(lib_path):
+        return lib_path
+    obj_dir.mkdir(exist_ok=True)
     nvcc = _nvcc()
     objs = []
     for src in sources():
-        obj = OBJ_DIR / (src.stem + ".o")
-        cmd = [nvcc, *NVCC_FLAGS, "-I", str(INCLUDE), "-c", str(src), "-o", str(obj)]
+        obj = obj_dir / (src.stem + ".o")
+        cmd = [nvcc, *NVCC_FLAGS, *(["-DDFL_TC_TRACE"] if trace else []), "-I", str(INCLUDE), "-c", str(src),
+               "-o", str(obj)]
         if verbose:
             print(" ".join(cmd), file=sys.stderr)
         subprocess.run(cmd, check=True)
         objs.append(str(obj))
-    tmp = LIB_PATH.with_suffix(".so.tmp")
+    tmp = lib_path.with_suffix(".so.tmp")
     cmd = [nvcc, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", *objs, "-o", str(tmp), "-lcudart"]
     subprocess.run(cmd, check=True)
-    os.replace(tmp, LIB_PATH)
-    return LIB_PATH
+    os.replace(tmp, lib_path)
+    return lib_path
 
 
 if __name__ == "__main__":
-    build(force="--force" in sys.argv, verbose=True)
-    print(LIB_PATH)
+    print(build(force="--force" in sys.argv, verbose=True, trace="--trace" in sys.argv))

@@ -59,6 +59,7 @@ class DFlashGenerator:
         if draft_quant_bits is not None:
             raise NotImplementedError("draft quantisation is not part of this build")
         torch.manual_seed(seed)
+        self.seed = int(seed)  # default sampling seed of generate / stream
         self.requested_target_model = target_model
         self.requested_draft_model = draft_model
         self.target: LoadedTargetModel = (target_model if isinstance(target_model, LoadedTargetModel)
@@ -81,14 +82,15 @@ class DFlashGenerator:
                              speculative_tokens: int | None = None, verify_mode: str = "parallel-replay",
                              verify_chunk_size: int = 4, reset_peak_memory: bool = True,
                              skip_special_tokens: bool = False, profile: bool = False,
-                             seed: int = 0) -> DFlashResult:
+                             seed: int | None = None) -> DFlashResult:
         if reset_peak_memory:
             torch.cuda.reset_peak_memory_stats(self.target.model.device)
         output_tokens, metrics = dflash_generate(
             target=self.target.model, draft=self.draft, prompt_tokens=prompt_tokens, max_new_tokens=max_new_tokens,
             temperature=temperature, stop_token_ids=self.target.stop_token_ids(),
             layer_ids=self.draft.target_layer_ids, speculative_tokens=speculative_tokens, verify_mode=verify_mode,
-            verify_chunk_size=verify_chunk_size, profile=profile, seed=seed)
+            verify_chunk_size=verify_chunk_size, profile=profile,
+            seed=self.seed if seed is None else seed)
         generated = output_tokens[metrics["num_input_tokens"]:]
         text = self.target.tokenizer.decode(generated, skip_special_tokens=skip_special_tokens)
         return DFlashResult(text=text, output_tokens=output_tokens, generated_tokens=generated, metrics=metrics)
@@ -97,7 +99,7 @@ class DFlashGenerator:
                            speculative_tokens: int | None = None, verify_mode: str = "parallel-replay",
                            verify_chunk_size: int = 4, reset_peak_memory: bool = True,
                            skip_special_tokens: bool = False, profile: bool = False,
-                           seed: int = 0) -> Iterator[DFlashStreamEvent]:
+                           seed: int | None = None) -> Iterator[DFlashStreamEvent]:
         """Incremental detokenisation as in api.py:116-164."""
         prompt_len = int(len(prompt_tokens))
         decoded = ""
@@ -107,7 +109,7 @@ class DFlashGenerator:
                 target=self.target.model, draft=self.draft, prompt_tokens=prompt_tokens,
                 max_new_tokens=max_new_tokens, temperature=temperature, stop_token_ids=self.target.stop_token_ids(),
                 layer_ids=self.draft.target_layer_ids, speculative_tokens=speculative_tokens, verify_mode=verify_mode,
-                verify_chunk_size=verify_chunk_size, profile=profile, seed=seed):
+                verify_chunk_size=verify_chunk_size, profile=profile, seed=self.seed if seed is None else seed):
             generated = event.output_tokens[prompt_len:]
             text = self.target.tokenizer.decode(generated, skip_special_tokens=skip_special_tokens)
             delta = text[len(decoded):] if text.startswith(decoded) else text

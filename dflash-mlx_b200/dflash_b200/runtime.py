@@ -424,9 +424,10 @@ def dflash_generate_stream(target: TargetModel, draft: DraftModel, prompt_tokens
                 streamed_len = n
     torch.cuda.synchronize(target.device)
     decode_time = time.perf_counter() - decode_start
-    outs, accs, _ = sess.outputs()
+    outs, accs, st = sess.outputs()
     output_tokens = outs[0]
     acceptance_lengths = accs[0]
+    stop_index = int(st[0, S_STOP])
     generated = max(len(output_tokens) - prompt_len, 0)
     total_time = prefill_time + decode_time
     metrics = {
@@ -443,10 +444,85 @@ def dflash_generate_stream(target: TargetModel, draft: DraftModel, prompt_tokens
         "peak_memory_gb": torch.cuda.max_memory_allocated(target.device) / 1e9,
         "target_cache_summary": f"kv_len={int(sess.state[0, S_START].item())} x {target.cfg.num_hidden_layers} layers",
         "speculative_tokens": block_size,
+        # why decoding ended: a stop token inside the length limit, else the limit
+        "finish_reason": "stop" if 0 <= stop_index < total_max else "max_tokens",
     }
     if profile:
         metrics["profile"] = {"steps": len(acceptance_lengths), "verify_mode": verify_mode}
     yield DFlashRuntimeEvent(token_ids=[], output_tokens=list(output_tokens), metrics=metrics, finished=True)
+
+
+@dataclass
+class BatchStreamEvent:
+    """New committed tokens of sequence ``index`` of a batched decode; ``finished`` marks its
+    last event, with ``finish_reason`` "stop" (a stop token) or "max_tokens" (the limit)."""
+    index: int
+    token_ids: list[int]
+    finished: bool = False
+    finish_reason: str | None = None
+    acceptance_lengths: list[int] | None = None
+
+
+def dflash_generate_batch_stream(target: TargetModel, draft: DraftModel | None, prompts: list[list[int]],
+                                 max_new_tokens: list[int], temperature: float, stop_token_ids: set[int],
+                                 speculative_tokens: int | None = None, use_graph: bool = True,
+                                 seed: int = 0) -> Iterator[list[BatchStreamEvent]]:
+    """Decodes several prompts together in one batched session (per-sequence acceptance,
+    stop and length rules of runtime.py:405-518 applied to every row) and yields, after
+    each step, the events of the sequences that committed tokens or finished in it."""
+    B = len(prompts)
+    if B == 0:
+        return
+    if len(max_new_tokens) != B:
+        raise ValueError("one max_new_tokens per prompt")
+    prompts = [[int(t) for t in p] for p in prompts]
+    bs_max = draft.block_size if draft is not None else 1
+    block_size = bs_max if speculative_tokens is None else max(1, min(speculative_tokens, bs_max))
+    use_draft = draft if block_size > 1 else None
+    totals = [len(p) + m for p, m in zip(prompts, max_new_tokens)]
+    sess = SpecSession(target, use_draft, B, max(totals), block_size, stop_token_ids, use_graph=use_graph,
+                       temperature=temperature, seed=seed)
+    firsts = sess.prefill(prompts, max_new_tokens)
+    streamed = [len(p) for p in prompts]
+    done = [False] * B
+    events = []
+    for b in range(B):
+        if max_new_tokens[b] <= 0:
+            done[b] = True
+            events.append(BatchStreamEvent(b, [], True, "max_tokens", []))
+        else:
+            events.append(BatchStreamEvent(b, [firsts[b]]))
+            streamed[b] += 1
+    if events:
+        yield events
+
+    def finish(b: int, host_state) -> BatchStreamEvent:
+        stop = int(host_state[b, S_STOP])
+        steps = int(host_state[b, S_STEPS])
+        return BatchStreamEvent(b, [], True, "stop" if 0 <= stop < totals[b] else "max_tokens",
+                                sess.accept_log[b, :steps].tolist())
+
+    if not all(done):
+        for host_state, host_tokens in sess.run_iter(max(max_new_tokens) + 1):
+            events = []
+            for b in range(B):
+                if done[b]:
+                    continue
+                start, stop = int(host_state[b, S_START]), int(host_state[b, S_STOP])
+                n = min(start + 1, totals[b])
+                if stop >= 0:
+                    n = min(n, stop + 1)
+                if n > streamed[b]:
+                    events.append(BatchStreamEvent(b, host_tokens[b, streamed[b]:n].tolist()))
+                    streamed[b] = n
+                if int(host_state[b, S_FINISHED]):
+                    done[b] = True
+                    events.append(finish(b, host_state))
+            if events:
+                yield events
+    if not all(done):  # every sequence is finished once the steps run out
+        st = sess.state.cpu()
+        yield [finish(b, st) for b in range(B) if not done[b]]
 
 
 def dflash_generate(target: TargetModel, draft: DraftModel, prompt_tokens, max_new_tokens: int, temperature: float,

@@ -74,3 +74,51 @@ def test_adapter_contract_verify_and_rewind(gen):
     assert torch.equal(h2[0], h1[0, 1:])
     am = t.lm_head_argmax(h1.new_zeros(1, 1, t.model.cfg.hidden_size) + 0.1)
     assert am.shape == (1, 1)
+
+
+def test_batched_stream_matches_single_requests(gen):
+    """dflash_generate_batch_stream with three prompts (different lengths and limits) gives
+    each prompt's single-request tokens, acceptance record and finish reason."""
+    from dflash_b200.runtime import dflash_generate_batch_stream
+    prompts = [list(range(5, 69)), list(range(11, 30)), list(range(3, 100, 2))]
+    limits = [40, 17, 25]
+    singles = [gen.generate_from_tokens(p, max_new_tokens=n) for p, n in zip(prompts, limits)]
+    got = [[] for _ in prompts]
+    final = {}
+    for events in dflash_generate_batch_stream(gen.target.model, gen.draft, prompts, limits, 0.0,
+                                               gen.target.stop_token_ids()):
+        for ev in events:
+            got[ev.index].extend(ev.token_ids)
+            if ev.finished:
+                final[ev.index] = ev
+    for b, s in enumerate(singles):
+        assert got[b] == s.generated_tokens, b
+        assert final[b].finish_reason == s.metrics["finish_reason"]
+        assert final[b].acceptance_lengths == s.metrics["acceptance_lengths"]
+
+
+def test_openai_batching_runner_concurrent_requests(gen):
+    """Three concurrent chat requests decoded as one batch answer like three single requests."""
+    import threading
+
+    from dflash_b200.openai_server import BatchingRunner, DFlashRunner
+    prompts = ["alpha beta gamma", "one two", "the quick brown fox jumps"]
+    single = DFlashRunner(generator=gen)
+    want = [single.generate(prompt=p, max_new_tokens=20, temperature=0.0) for p in prompts]
+    runner = BatchingRunner(gen, max_batch=8, window_s=0.5)
+    got = {}
+
+    def client(i):
+        got[i] = runner.generate(prompt=prompts[i], max_new_tokens=20, temperature=0.0)
+
+    threads = [threading.Thread(target=client, args=(i,)) for i in range(3)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(timeout=120)
+    runner.close()
+    assert runner.batches == [3]
+    for i in range(3):
+        assert got[i].text == want[i].text and got[i].completion_tokens == want[i].completion_tokens
+        assert got[i].finish_reason == want[i].finish_reason
+        assert got[i].prompt_tokens == want[i].prompt_tokens

@@ -536,7 +536,7 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
 }
 
 // ---------------------------------------------------------------------------
-// Cluster split-K variant for GEMMs with few 128-row tiles (N / 128 < 148):
+// Cluster split-K variant for GEMMs with few 128-row tiles (N / 128 < DFL_TC_CSK_TILES, the stream-K grid):
 // a thread-block cluster of S CTAs (S <= 8) owns one tile, CTA rank r streams the
 // fixed k-range [r*kb/S, (r+1)*kb/S), and the S partial tiles are reduced through
 // distributed shared memory in rank order (no global scratch, no atomics). Each

@@ -195,7 +195,7 @@ def main(argv=None):
     ap.add_argument("--only", default="gdr,attn,gemm")
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--key-chunk", type=int, default=0, help="attn_c4: one key chunk instead of the sweep")
+    ap.add_argument("--key-chunk", type=int, default=0, help="attn_c3 / attn_c4: one key chunk instead of the sweep")
     args = ap.parse_args(argv)
     sel = set(args.only.split(","))
     timer = Timer(args.iters, args.warmup)
@@ -204,7 +204,8 @@ def main(argv=None):
     if sel & {"gdr", "gdr_t4096"}:
         bench_gdr(timer, 4096, False)
     if sel & {"attn", "attn_c3"}:
-        bench_attention(timer, 1, 16, [1536], "attn_c3")
+        for kc in ([args.key_chunk] if args.key_chunk else (128, 256, 512)):
+            bench_attention(timer, 1, 16, [1536], "attn_c3", key_chunk=kc)
     if sel & {"attn", "attn_c4"}:
         g = torch.Generator().manual_seed(3)
         ctxs = torch.randint(512, 4097, (64,), generator=g).tolist()

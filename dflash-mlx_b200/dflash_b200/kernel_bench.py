@@ -146,7 +146,7 @@ def bench_attention(timer: Timer, B: int, rows: int, ctxs: list[int], case: str,
                         "key_chunk": key_chunk or 128})
 
 
-def bench_gemm_c4(timer: Timer, M: int = 1024, wide: bool = True):
+def bench_gemm_c4(timer: Timer, M: int = 1024, wide: bool = True, wide_split: int = 1):
     """The verify GEMMs at C4's 1024 rows; wide=True is the whole-K tile form batched
     sessions use, wide=False the M <= 16 weight-streaming form for comparison."""
     H, I, Hq, Hkv, hd = 2560, 9728, 32, 8, 128
@@ -158,11 +158,12 @@ def bench_gemm_c4(timer: Timer, M: int = 1024, wide: bool = True):
         w = ops.pack_weight((torch.randn((N, K), device="cuda", generator=gen) * 0.02).bfloat16())
         x = torch.randn((M, K), device="cuda", generator=gen).bfloat16()
         y = torch.empty((M, N), dtype=torch.bfloat16, device="cuda")
-        ws = ops.Workspace(torch.device("cuda"), wide=wide)
+        ws = ops.Workspace(torch.device("cuda"), wide=wide, wide_split=wide_split)
         sec = timer(lambda: ops.gemm(x, w, out=y, ws=ws))
         res.append(_line(f"gemm_c4_{name}" + ("" if wide else "_streaming"), kern, sec,
                          bytes_=N * K * 2 + M * K * 2 + M * N * 2, flops=2.0 * M * N * K,
-                         extra={"workload": f"M={M} N={N} K={K}"}))
+                         extra={"workload": f"M={M} N={N} K={K}",
+                                "k_split": ops.wide_split(N, K, ws) if wide else None}))
         del w, x, y
     return res
 
@@ -196,6 +197,7 @@ def main(argv=None):
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--key-chunk", type=int, default=0, help="attn_c3 / attn_c4: one key chunk instead of the sweep")
+    ap.add_argument("--wide-split", type=int, default=1, help="gemm: most K ranges of a wide GEMM (session limit)")
     args = ap.parse_args(argv)
     sel = set(args.only.split(","))
     timer = Timer(args.iters, args.warmup)
@@ -212,7 +214,7 @@ def main(argv=None):
         for kc in ([args.key_chunk] if args.key_chunk else (128, 512, 1024, 4224)):
             bench_attention(timer, 64, 16, ctxs, "attn_c4", key_chunk=kc)
     if "gemm" in sel:
-        bench_gemm_c4(timer)
+        bench_gemm_c4(timer, wide_split=args.wide_split)
     if "verify" in sel:
         bench_verify_gemms(timer)
     if "gemm_streaming" in sel:

@@ -53,7 +53,38 @@ struct AttnArgs {
   int direct;        // one chunk: the chunk kernel writes the normalised output
   int* err;          // device error record
   float scale_log2;  // softmax scale * log2(e)
+  // fused q/k head norm + RoPE + cache append (head_dim 128, full rotary): q and the new
+  // keys / values come from the raw projection rows instead of q and a prior append
+  const __nv_bfloat16* qkv;  // nullable: [M][(Hq + 2 Hkv) * 128] rows
+  long long ldqkv;
+  const __nv_bfloat16* q_norm;
+  const __nv_bfloat16* k_norm;
+  const float* inv_freq;  // [64]
+  float eps;
+  __nv_bfloat16* k_new;   // the caches, written at the new rows' positions
+  __nv_bfloat16* v_new;
 };
+
+// One 128-wide head row held 4 values per lane (element lane + 32 j): RMSNorm with weight
+// nw, then the rotary embedding with the row's (cos, sin) table cs[64] -- the arithmetic of
+// qkv_rope_append_kernel (same summation order, same pinned roundings, the same sincosf
+// values), so both paths give the same bits.
+__device__ __forceinline__ void norm_rope_row128(float (&x)[4], const __nv_bfloat16* nw, const float2* cs,
+                                                 float eps, int lane) {
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) ss = sq_acc(ss, x[j]);
+  ss = warp_sum(ss);
+  const float inv = rsqrtf(ss / 128.f + eps);
+  float y[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) y[j] = round_bf16(bf2f(nw[lane + 32 * j]) * (x[j] * inv));
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 t = cs[lane + 32 * (j & 1)];
+    x[j] = rope_rot(y[j], y[j ^ 2], t.x, t.y, j < 2);
+  }
+}
 
 template <int HD>
 __device__ __forceinline__ int att_swz(int row, int c) {
@@ -132,8 +163,78 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(AttnArgs a) {
   const __nv_bfloat16* Kb = a.k_cache + s_seq * a.seq_stride + kvh * a.head_stride;
   const __nv_bfloat16* Vb = a.v_cache + s_seq * a.seq_stride + kvh * a.head_stride;
 
+  if constexpr (HD == 128) {
+    if (a.qkv) {
+      // fused append: this CTA's new rows whose position falls in its key range get their
+      // key (norm + RoPE) and value written to the cache here -- no other CTA reads them,
+      // since every row of a sequence is in this tile and every CTA reads only its own
+      // key range -- then the Q tile is normalised and rotated from the projection rows
+      const int Hq = a.Hq;
+      // (cos, sin) of every row's position and frequency, once per CTA, in the K ring
+      // (idle until the ring prologue below, which follows the barrier after this block)
+      float2(*s_cs)[64] = reinterpret_cast<float2(*)[64]>(sK);
+      for (int idx = threadIdx.x; idx < 16 * 64; idx += nthr) {
+        const int r = idx >> 6, f = idx & 63;
+        const int p = s_lim[r] > 0 ? a.pos[m0 + r] : 0;
+        float sn, cs;
+        sincosf(rope_angle(p, a.inv_freq[f]), &sn, &cs);
+        s_cs[r][f] = make_float2(cs, sn);
+      }
+      __syncthreads();
+      for (int r = warp; r < 16; r += a.G) {
+        const int m = m0 + r;
+        if (s_lim[r] <= 0) continue;
+        const int p = a.pos[m];
+        if (p < k_begin || p >= k_end) continue;
+        const __nv_bfloat16* row = a.qkv + (long long)m * a.ldqkv;
+        const __nv_bfloat16* ks = row + (long long)(Hq + kvh) * 128;
+        const __nv_bfloat16* vs = row + (long long)(Hq + a.Hkv + kvh) * 128;
+        float x[4];
+        __nv_bfloat16 vv[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          x[j] = bf2f(ks[lane + 32 * j]);
+          vv[j] = vs[lane + 32 * j];
+        }
+        norm_rope_row128(x, a.k_norm, s_cs[r], a.eps, lane);
+        const long long off = s_seq * a.seq_stride + kvh * a.head_stride + (long long)p * 128;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          a.k_new[off + lane + 32 * j] = f2bf(x[j]);
+          a.v_new[off + lane + 32 * j] = vv[j];
+        }
+      }
+      // Q: warp w holds head kvh * G + w; four rows' loads in flight at a time
+      const int hq = kvh * a.G + warp;
+      __nv_bfloat16* myq = sQ + warp * 16 * HD;
+#pragma unroll 1
+      for (int r0 = 0; r0 < 16; r0 += 4) {
+        float x[4][4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int m = m0 + r0 + u;
+          const bool ok = s_lim[r0 + u] > 0;
+          const __nv_bfloat16* qs = a.qkv + (long long)(ok ? m : 0) * a.ldqkv + (long long)hq * 128;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) x[u][j] = ok ? bf2f(qs[lane + 32 * j]) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int r = r0 + u;
+          if (s_lim[r] > 0) norm_rope_row128(x[u], a.q_norm, s_cs[r], a.eps, lane);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int i = lane + 32 * j;
+            myq[att_swz<HD>(r, i >> 3) + (i & 7)] = s_lim[r] > 0 ? f2bf(x[u][j]) : __float2bfloat16(0.f);
+          }
+        }
+      }
+      __threadfence();  // the appended rows reach L2 before this CTA's cp.async reads them
+      __syncthreads();
+    }
+  }
   // Q tile: rows are (head-in-group, token)
-  for (int idx = threadIdx.x; idx < a.G * 16 * NC; idx += nthr) {
+  for (int idx = threadIdx.x; idx < (a.qkv ? 0 : a.G * 16 * NC); idx += nthr) {
     const int c = idx % NC;
     const int rr = idx / NC;  // hg*16 + r
     const int hg = rr / 16, r = rr % 16;
@@ -457,14 +558,25 @@ extern "C" size_t dfl_attention_workspace_bytes(int M, int Hq, int hd, int max_k
   return ((o + 255) & ~(size_t)255) + ml;
 }
 
-extern "C" int dfl_attention(const void* q, const void* k_cache, const void* v_cache, int64_t seq_stride,
-                             int64_t head_stride, const int32_t* pos, const int32_t* row_seq, const int32_t* kv_len,
-                             int seq_rows, int M, int Hq, int Hkv, int hd, int causal, float scale, int max_kv,
-                             int key_chunk, void* out,
-                             int64_t ldo, const void* gate, int64_t ldg, int gate_head_stride, void* workspace,
-                             size_t workspace_bytes, void* stream) {
+namespace {
+struct FusedQkv {
+  const void* qkv;
+  int64_t ldqkv;
+  const void* q_norm;
+  const void* k_norm;
+  const float* inv_freq;
+  float eps;
+};
+}  // namespace
+
+static int attention_impl(const void* q, const void* k_cache, const void* v_cache, int64_t seq_stride,
+                          int64_t head_stride, const int32_t* pos, const int32_t* row_seq, const int32_t* kv_len,
+                          int seq_rows, int M, int Hq, int Hkv, int hd, int causal, float scale, int max_kv,
+                          int key_chunk, void* out, int64_t ldo, const void* gate, int64_t ldg, int gate_head_stride,
+                          void* workspace, size_t workspace_bytes, void* stream, const FusedQkv* fq) {
   if (M == 0) return DFL_OK;
-  if (!q || !k_cache || !v_cache || !pos || !out || (!causal && !kv_len) || M < 0 || Hkv <= 0 || Hq % Hkv) {
+  if ((!q && !fq) || !k_cache || !v_cache || !pos || !out || (!causal && !kv_len) || M < 0 || Hkv <= 0 ||
+      Hq % Hkv) {
     set_error("dfl_attention: bad arguments");
     return DFL_ERR_INVALID;
   }
@@ -523,6 +635,22 @@ extern "C" int dfl_attention(const void* q, const void* k_cache, const void* v_c
   else if (seq_rows > 0) a.segs = min(16, (15 + seq_rows - 1) / seq_rows + 1);
   else a.segs = min(16, M);
   a.err = device_error_word();
+  a.qkv = nullptr;
+  a.ldqkv = 0;
+  a.q_norm = a.k_norm = nullptr;
+  a.inv_freq = nullptr;
+  a.eps = 0.f;
+  a.k_new = a.v_new = nullptr;
+  if (fq) {
+    a.qkv = static_cast<const __nv_bfloat16*>(fq->qkv);
+    a.ldqkv = fq->ldqkv;
+    a.q_norm = static_cast<const __nv_bfloat16*>(fq->q_norm);
+    a.k_norm = static_cast<const __nv_bfloat16*>(fq->k_norm);
+    a.inv_freq = fq->inv_freq;
+    a.eps = fq->eps;
+    a.k_new = static_cast<__nv_bfloat16*>(const_cast<void*>(k_cache));
+    a.v_new = static_cast<__nv_bfloat16*>(const_cast<void*>(v_cache));
+  }
   cudaStream_t st = as_stream(stream);
   switch (hd) {
     case 64: return deep ? launch_attn<64, 3>(a, n_tiles, st) : launch_attn<64, 2>(a, n_tiles, st);
@@ -532,4 +660,40 @@ extern "C" int dfl_attention(const void* q, const void* k_cache, const void* v_c
       set_error("dfl_attention: head_dim %d not supported (64, 128, 256)", hd);
       return DFL_ERR_UNSUPPORTED;
   }
+}
+
+extern "C" int dfl_attention(const void* q, const void* k_cache, const void* v_cache, int64_t seq_stride,
+                             int64_t head_stride, const int32_t* pos, const int32_t* row_seq, const int32_t* kv_len,
+                             int seq_rows, int M, int Hq, int Hkv, int hd, int causal, float scale, int max_kv,
+                             int key_chunk, void* out,
+                             int64_t ldo, const void* gate, int64_t ldg, int gate_head_stride, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+  return attention_impl(q, k_cache, v_cache, seq_stride, head_stride, pos, row_seq, kv_len, seq_rows, M, Hq, Hkv, hd,
+                        causal, scale, max_kv, key_chunk, out, ldo, gate, ldg, gate_head_stride, workspace,
+                        workspace_bytes, stream, nullptr);
+}
+
+extern "C" int dfl_attention_qkv(const void* qkv, int64_t ldqkv, const void* q_norm, const void* k_norm,
+                                 const float* inv_freq, float eps, void* k_cache, void* v_cache, int64_t seq_stride,
+                                 int64_t head_stride, const int32_t* pos, const int32_t* row_seq, int seq_rows, int M,
+                                 int Hq, int Hkv, float scale, int max_kv, int key_chunk, void* out, int64_t ldo,
+                                 void* workspace, size_t workspace_bytes, void* stream) {
+  if (M == 0) return DFL_OK;
+  if (!qkv || !q_norm || !k_norm || !inv_freq || ldqkv < (int64_t)(Hq + 2 * Hkv) * 128 || ldqkv % 8) {
+    set_error("dfl_attention_qkv: bad projection rows or norm weights");
+    return DFL_ERR_INVALID;
+  }
+  // every row of a sequence must sit in one 16-row tile (the tile's CTAs write the new keys
+  // they read themselves): one sequence of at most 16 rows, or sequences of seq_rows rows
+  // with seq_rows dividing 16
+  const bool one_tile = row_seq ? (seq_rows > 0 && seq_rows <= 16 && 16 % seq_rows == 0) : M <= 16;
+  if (!one_tile) {
+    set_error("dfl_attention_qkv: needs every sequence's rows inside one 16-row tile (seq_rows=%d M=%d)",
+              seq_rows, M);
+    return DFL_ERR_UNSUPPORTED;
+  }
+  FusedQkv f{qkv, ldqkv, q_norm, k_norm, inv_freq, eps};
+  return attention_impl(nullptr, k_cache, v_cache, seq_stride, head_stride, pos, row_seq, nullptr, seq_rows, M, Hq,
+                        Hkv, 128, 1, scale, max_kv, key_chunk, out, ldo, nullptr, 0, 0, workspace, workspace_bytes,
+                        stream, &f);
 }

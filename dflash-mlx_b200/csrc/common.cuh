@@ -53,6 +53,14 @@ __device__ __forceinline__ float warp_sum(float v) {
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
 }
+// q/k head RMSNorm + rotary embedding steps with the rounding pinned (explicit fused
+// multiply-adds), shared by every kernel that applies them so that they agree bit for bit:
+// sum-of-squares step, rotary angle, and the rotated value of a pair (x, partner)
+__device__ __forceinline__ float sq_acc(float acc, float f) { return __fmaf_rn(f, f, acc); }
+__device__ __forceinline__ float rope_angle(int p, float inv_freq) { return __fmul_rn((float)p, inv_freq); }
+__device__ __forceinline__ float rope_rot(float x, float partner, float c, float s, bool first_half) {
+  return first_half ? __fmaf_rn(x, c, -__fmul_rn(partner, s)) : __fmaf_rn(x, c, __fmul_rn(partner, s));
+}
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));

@@ -149,7 +149,7 @@ __global__ void qkv_rope_append_kernel(QkvArgs a) {
   for (int i = lane; i < a.hd; i += 32) {
     const float f = bf2f(src[i]);
     buf[i] = f;
-    ss += f * f;
+    ss = sq_acc(ss, f);
   }
   ss = warp_sum(ss);
   const float inv = rsqrtf(ss / (float)a.hd + a.eps);
@@ -161,8 +161,8 @@ __global__ void qkv_rope_append_kernel(QkvArgs a) {
     if (i < a.rot_dim) {
       const int j = i < half ? i : i - half;
       float s, c;
-      sincosf((float)p * a.inv_freq[j], &s, &c);
-      o = i < half ? buf[i] * c - buf[i + half] * s : buf[i] * c + buf[i - half] * s;
+      sincosf(rope_angle(p, a.inv_freq[j]), &s, &c);
+      o = rope_rot(buf[i], i < half ? buf[i + half] : buf[i - half], c, s, i < half);
     }
     dst[i] = f2bf(o);
   }

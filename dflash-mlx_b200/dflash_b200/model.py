@@ -18,6 +18,8 @@ taps (adapters.py:611-631, mlx-lm qwen3 layers) and the DFlash draft
 """
 from __future__ import annotations
 
+import os
+
 from dataclasses import dataclass
 
 import torch
@@ -74,6 +76,11 @@ class TargetModel:
                 "k_norm": lw["k_norm"].to(dev),
             })
         self.inv_freq = rope_inv_freq(cfg.rope_dim, cfg.rope_theta, dev)
+        # True (or DFLASH_B200_FUSED_ATTENTION=1): verify blocks whose sequences each sit in
+        # one 16-row tile append K/V inside the attention launch (dfl_attention_qkv, the same
+        # bits). Off by default: measured 3287 against 3217 us per Qwen3-4B verify step, the
+        # in-CTA q/k preparation costing more than the append launch it removes.
+        self.fuse_attention = os.environ.get("DFLASH_B200_FUSED_ATTENTION", "0") == "1"
         self._bufs: dict[int, dict[str, torch.Tensor]] = {}
 
     # ------------------------------------------------------------------
@@ -126,14 +133,20 @@ class TargetModel:
         h, ss = b["h"], b["ss"]
         eps = c.rms_norm_eps
         ops.embed(tokens, self.embed_w, out=h, sumsq_out=ss)
+        fused = self.fuse_attention and ops.fused_attention_ok(M, row_seq, seq_rows, hd, c.rope_dim)
         for l, lw in enumerate(self.layers):
             kc, vc = cache.layer(l)
             # input_layernorm fused into the QKV projection
             ops.gemm(h, lw["w_qkv"], out=b["qkv"], ws=ws, norm_w=lw["in_norm"], sumsq_in=ss, eps=eps)
-            ops.qkv_rope_append(b["qkv"], pos, lw["q_norm"], lw["k_norm"], self.inv_freq, kc, vc, Hq, Hkv, hd,
-                                c.rope_dim, eps, q_out=b["q"], row_seq=row_seq)
-            ops.attention(b["q"], kc, vc, pos, causal=True, max_kv=max_kv, row_seq=row_seq, out=b["attn"], ws=ws,
-                          seq_rows=seq_rows, key_chunk=key_chunk)
+            if fused:  # q/k norm + RoPE + append inside the attention launch (same bits)
+                ops.attention_qkv(b["qkv"], pos, lw["q_norm"], lw["k_norm"], self.inv_freq, kc, vc, Hq, eps,
+                                  max_kv, row_seq=row_seq, out=b["attn"], ws=ws, seq_rows=seq_rows,
+                                  key_chunk=key_chunk)
+            else:
+                ops.qkv_rope_append(b["qkv"], pos, lw["q_norm"], lw["k_norm"], self.inv_freq, kc, vc, Hq, Hkv, hd,
+                                    c.rope_dim, eps, q_out=b["q"], row_seq=row_seq)
+                ops.attention(b["q"], kc, vc, pos, causal=True, max_kv=max_kv, row_seq=row_seq, out=b["attn"],
+                              ws=ws, seq_rows=seq_rows, key_chunk=key_chunk)
             ops.gemm(b["attn"], lw["w_o"], ops.EPI_RESIDUAL, residual=h, out=h, ws=ws, sumsq_out=ss)
             # post_attention_layernorm fused into the gate/up projection
             ops.gemm(h, lw["w_gu"], ops.EPI_SILU_MUL, out=b["act"], ws=ws, norm_w=lw["post_norm"], sumsq_in=ss,

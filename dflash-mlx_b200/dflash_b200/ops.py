@@ -278,6 +278,40 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, pos
     return out
 
 
+def fused_attention_ok(M: int, row_seq, seq_rows: int, hd: int, rot_dim: int) -> bool:
+    """Whether attention_qkv applies: head_dim 128 with full rotary and every sequence's
+    rows inside one 16-row tile."""
+    if hd != 128 or rot_dim != 128:
+        return False
+    if row_seq is None:
+        return M <= 16
+    return 0 < seq_rows <= 16 and 16 % seq_rows == 0
+
+
+def attention_qkv(qkv: torch.Tensor, pos: torch.Tensor, q_norm: torch.Tensor, k_norm: torch.Tensor,
+                  inv_freq: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, Hq: int, eps: float,
+                  max_kv: int, row_seq: torch.Tensor | None = None, out: torch.Tensor | None = None,
+                  ws: Workspace | None = None, seq_rows: int = 0, key_chunk: int = 0,
+                  scale: float | None = None) -> torch.Tensor:
+    """qkv_rope_append + causal attention in one launch (head_dim 128, full rotary; every
+    sequence's rows in one 16-row tile); the same bits as the two calls."""
+    _need_cuda(qkv, pos, q_norm, k_norm, inv_freq, k_cache, v_cache, row_seq, out)
+    M = qkv.shape[0]
+    Hkv = k_cache.shape[1]
+    if k_cache.dim() != 4 or k_cache.stride(3) != 1 or k_cache.stride(2) != 128:
+        raise ValueError("k_cache must be a [seq, Hkv, cap, 128] view")
+    if out is None:
+        out = torch.empty((M, Hq * 128), dtype=torch.bfloat16, device=qkv.device)
+    ws = ws or workspace(qkv.device)
+    need = int(_lib.query("dfl_attention_workspace_bytes", M, Hq, 128, max_kv, int(key_chunk)))
+    ws.ensure_attn(need)
+    _lib.call("dfl_attention_qkv", _ptr(qkv), _row_stride(qkv), _ptr(q_norm), _ptr(k_norm), _ptr(inv_freq),
+              float(eps), _ptr(k_cache), _ptr(v_cache), k_cache.stride(0), k_cache.stride(1), _ptr(pos),
+              _ptr(row_seq), int(seq_rows), M, Hq, Hkv, float(scale if scale is not None else 1.0 / math.sqrt(128)),
+              int(max_kv), int(key_chunk), _ptr(out), _row_stride(out), _ptr(ws.attn), ws.attn.numel(), _stream())
+    return out
+
+
 def argmax_reduce(partials: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     _need_cuda(partials, out)
     M, ntiles = partials.shape[0], partials.shape[1]

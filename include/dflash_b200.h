@@ -198,6 +198,22 @@ int dfl_attention(const void* q, const void* k_cache, const void* v_cache, int64
                   int causal, float scale, int max_kv, int key_chunk, void* out, int64_t ldo, const void* gate, int64_t ldg,
                   int gate_head_stride, void* workspace, size_t workspace_bytes, void* stream);
 
+/* dfl_qkv_rope_append followed by causal dfl_attention in one launch, for head_dim 128 with
+ * rotary over the whole head (the Qwen3 verify block: mlx-lm qwen3 Attention's q/k norm,
+ * RoPE, KVCache.update_and_fetch and scaled_dot_product_attention, adapters.py:611-631).
+ * qkv: the raw projection rows [M][(Hq + 2 Hkv) * 128] (q heads, k heads, v heads). Each
+ * row's key and value are normalised, rotated and written into the caches at pos[r] by the
+ * CTA whose key range holds that position, which is the only CTA that reads them; the query
+ * tile is normalised and rotated on load. Bit-identical to the two calls. Needs every
+ * sequence's rows inside one 16-row tile: row_seq null with M <= 16, or seq_rows dividing
+ * 16 (otherwise DFL_ERR_UNSUPPORTED). Workspace as dfl_attention_workspace_bytes(M, Hq,
+ * 128, max_kv, key_chunk). */
+int dfl_attention_qkv(const void* qkv, int64_t ldqkv, const void* q_norm, const void* k_norm, const float* inv_freq,
+                      float eps, void* k_cache, void* v_cache, int64_t seq_stride, int64_t head_stride,
+                      const int32_t* pos, const int32_t* row_seq, int seq_rows, int M, int Hq, int Hkv, float scale,
+                      int max_kv, int key_chunk, void* out, int64_t ldo, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
 /* ---- speculative step control ---------------------------------------------
  * Greedy argmax from DFL_EPI_ARGMAX partials (runtime.py:22-29 at temperature 0). */
 int dfl_argmax_reduce(const void* partials, int M, int n_tiles, int32_t* out, void* stream);

@@ -478,3 +478,48 @@ def test_gdr_replay_of_accepted_prefix_equals_snapshot():
     o2 = torch.empty_like(o_full)
     ops.gdr_recurrence(q, k, v, alpha, beta, S0, o=o2)
     assert torch.equal(o2, o_full)
+
+
+@pytest.mark.parametrize("case", ["single_straddle", "batched16", "rows4", "finished_rows"])
+def test_attention_qkv_fused_matches_append_then_attention(case):
+    """dfl_attention_qkv (norm + RoPE + append inside the attention launch) gives the same
+    bits as dfl_qkv_rope_append followed by dfl_attention: output and both caches."""
+    from dflash_b200 import ops
+    from dflash_b200.model import rope_inv_freq
+    g = torch.Generator(device="cuda").manual_seed(11)
+    Hq, Hkv, hd, eps = 32, 8, 128, 1e-6
+    row_seq = None
+    if case == "single_straddle":
+        B, rows, starts, kc = 1, 16, [1016], 128
+    elif case == "batched16":
+        B, rows, starts, kc = 6, 16, [5, 700, 1023, 2048, 130, 3000], 1024
+    else:
+        B, rows, starts, kc = 8, 4, [9, 64, 127, 500, 1, 1999, 250, 1000], 128
+    M = B * rows
+    cap = max(starts) + rows + 8
+    if B > 1:
+        row_seq = torch.arange(M, device="cuda", dtype=torch.int32) // rows
+    pos = torch.tensor([s + i for s in starts for i in range(rows)], dtype=torch.int32, device="cuda")
+    if case == "finished_rows":
+        pos[4:8] = -1  # a finished sequence: no append, no output
+    qkv = (torch.randn((M, (Hq + 2 * Hkv) * hd), device="cuda", generator=g) * 2).bfloat16()
+    q_norm = (1 + 0.1 * torch.randn(hd, device="cuda", generator=g)).bfloat16()
+    k_norm = (1 + 0.1 * torch.randn(hd, device="cuda", generator=g)).bfloat16()
+    inv_freq = rope_inv_freq(hd, 1e6, "cuda")
+    kc0 = torch.randn((B, Hkv, cap, hd), device="cuda", generator=g).bfloat16()
+    vc0 = torch.randn((B, Hkv, cap, hd), device="cuda", generator=g).bfloat16()
+    max_kv = max(starts) + rows
+    ws = ops.Workspace(torch.device("cuda"))
+    k1, v1 = kc0.clone(), vc0.clone()
+    q = ops.qkv_rope_append(qkv, pos, q_norm, k_norm, inv_freq, k1, v1, Hq, Hkv, hd, hd, eps, row_seq=row_seq)
+    o1 = ops.attention(q, k1, v1, pos, True, max_kv=max_kv, row_seq=row_seq, ws=ws, seq_rows=rows if B > 1 else 0,
+                       key_chunk=kc)
+    k2, v2 = kc0.clone(), vc0.clone()
+    assert ops.fused_attention_ok(M, row_seq, rows if B > 1 else 0, hd, hd)
+    o2 = ops.attention_qkv(qkv, pos, q_norm, k_norm, inv_freq, k2, v2, Hq, eps, max_kv, row_seq=row_seq, ws=ws,
+                           seq_rows=rows if B > 1 else 0, key_chunk=kc)
+    torch.cuda.synchronize()
+    assert ops.device_error() == 0
+    live = pos >= 0
+    assert torch.equal(k1, k2) and torch.equal(v1, v2)
+    assert torch.equal(o1[live], o2[live])

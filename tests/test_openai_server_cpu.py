@@ -204,3 +204,43 @@ def test_batching_runner_streams_deltas_and_reports_errors():
     with pytest.raises(RuntimeError, match="device lost"):
         runner.generate(prompt="abc", max_new_tokens=2, temperature=0.0)
     runner.close()
+
+
+def test_dflash_runner_maps_finish_reasons_with_a_fake_generator():
+    """DFlashRunner turns generator events into chunks: deltas, then a final chunk whose
+    finish_reason maps max_tokens -> length (openai_server.py:205-262)."""
+    from types import SimpleNamespace as NS
+
+    class FakeGen:
+        def __init__(self, reason):
+            self.reason = reason
+            self.kw = None
+
+        def stream(self, prompt, **kw):
+            self.kw = kw
+            yield NS(delta="ab", text="ab", generated_tokens=[1, 2], finished=False, metrics=None)
+            yield NS(delta="c", text="abc", generated_tokens=[1, 2, 3], finished=True,
+                     metrics={"num_input_tokens": 7, "finish_reason": self.reason})
+
+    g = FakeGen("max_tokens")
+    r = S.DFlashRunner(generator=g, speculative_tokens=8, verify_mode="stream")
+    res = r.generate(prompt="x", max_new_tokens=3, temperature=0.0)
+    assert (res.text, res.prompt_tokens, res.completion_tokens, res.finish_reason) == ("abc", 7, 3, "length")
+    assert g.kw["speculative_tokens"] == 8 and g.kw["verify_mode"] == "stream" and g.kw["skip_special_tokens"]
+    chunks = list(S.DFlashRunner(generator=FakeGen("stop")).stream(prompt="x", max_new_tokens=3, temperature=0.0))
+    assert [c.delta for c in chunks] == ["ab", "c", ""] and chunks[-1].finish_reason == "stop"
+
+
+def test_batching_runner_respects_max_batch():
+    calls = []
+    runner = S.BatchingRunner(_Gen(), max_batch=2, window_s=0.3, decode_fn=_fake_decode(calls))
+    out = {}
+    threads = [threading.Thread(target=lambda i=i: out.__setitem__(i, runner.generate(
+        prompt="abc", max_new_tokens=2, temperature=0.0))) for i in range(5)]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join(timeout=20)
+    runner.close()
+    assert sum(n for n, _ in calls) == 5 and max(n for n, _ in calls) <= 2
+    assert all(out[i].text == "de" for i in range(5))

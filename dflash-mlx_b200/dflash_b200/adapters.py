@@ -17,14 +17,14 @@ API uses; ``runtime.SpecSession`` is the graph-captured fast path.
 """
 from __future__ import annotations
 
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 from pathlib import Path
 from typing import Any
 
 import torch
 
 from . import ops
-from .config import PRESETS, TargetConfig
+from .config import PRESETS
 from .model import KVCache, TargetModel
 from .weights import random_target_weights
 

@@ -166,7 +166,9 @@ def load_tokenizer(path: Path, vocab_size: int, eos: tuple[int, ...]):
             if not hasattr(tok, "eos_token_ids"):
                 tok.eos_token_ids = list(eos) or ([tok.eos_token_id] if tok.eos_token_id is not None else [])
             return tok
-        except Exception:  # unusable tokenizer files: fall back to bytes
-            pass
+        except Exception as exc:  # unusable tokenizer files: say so, then fall back to bytes
+            import warnings
+            warnings.warn(f"tokenizer files in {path} could not be loaded ({exc}); using a byte tokenizer",
+                          RuntimeWarning, stacklevel=2)
     from .adapters import ByteTokenizer
     return ByteTokenizer(vocab_size, eos)

@@ -346,7 +346,9 @@ def make_hybrid_layer_fixture(ref_root: str) -> dict:
 
 
 def main():
-    ref_root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    ref_root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("DFLASH_REFERENCE_ROOT")
+    if not ref_root:
+        raise SystemExit("usage: make_golden.py <reference tree> (or set DFLASH_REFERENCE_ROOT)")
     fx = make_runtime_fixture(ref_root)
     with open(os.path.join(HERE, "runtime_loop.json"), "w") as f:
         json.dump(fx, f)

@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark: accepted tokens/s of DFlash speculative decoding at the Qwen3-4B shape.
 
-Workload: Qwen3-4B-shaped bf16 random-init target (36 layers,
+Workload (benchmark config 3): Qwen3-4B-shaped bf16 random-init target (36 layers,
 hidden 2560, 32 q / 8 kv heads of 128, FFN 9728, vocab 151936) and a 5-layer DFlash
 draft (block 16, 5 taps), one stream per GPU, 512-token random prompt, seed 2.
 Drafts are oracle-injected: the block carries the target's own greedy tokens for a
@@ -13,11 +13,11 @@ tokens. A step = one speculative step (draft forward + 16-token verify + accept)
 N > 1 runs N independent replicas (one process per GPU under torchrun, no
 collective on the data path: weak scaling). Rank 0 prints one JSON line.
 
---workload c4 (not the default line): 64 sequences per GPU with
+--workload c4 (benchmark config 4, not the default line): 64 sequences per GPU with
 contexts U[512, 4096] (seed 3), block 16, per-sequence oracle-injected acceptance
 (tau 6.5) and rollback, decoded together in one batched step per GPU.
 
---workload c5: Qwen3.5-27B-shaped hybrid target (64 layers) with a
+--workload c5 (benchmark config 5): Qwen3.5-27B-shaped hybrid target (64 layers) with a
 5-layer DFlash draft, tensor-parallel over the N ranks (N = 1, 2, 4 or 8), batch 8,
 context --ctx (default 32768), block 16, oracle-injected acceptance tau 4.0 (seed 4).
 """

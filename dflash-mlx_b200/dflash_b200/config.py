@@ -92,7 +92,7 @@ def evenly_spaced_layers(num_layers: int, n: int) -> list[int]:
 
 
 # ---------------------------------------------------------------------------
-# Presets: the BASELINE configurations (random-init, seeded)
+# Presets: the benchmark configurations (random-init, seeded)
 # ---------------------------------------------------------------------------
 def tiny_pair() -> tuple[TargetConfig, DraftConfig]:
     """Config 1: 4 layers, hidden 256, 4 q / 2 kv heads of 64, FFN 768, vocab 4096;

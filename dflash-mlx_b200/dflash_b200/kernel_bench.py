@@ -1,4 +1,4 @@
-"""Per-kernel roofline measurements of the hot-path kernels at the BASELINE shapes.
+"""Per-kernel roofline measurements of the hot-path kernels at the benchmark configurations' shapes.
 
     python -m dflash_b200.kernel_bench [--only gdr,attn,gemm] [--iters N]
 
@@ -8,7 +8,7 @@ Prints one JSON line per case: the kernel, the workload, the algorithmic bytes
 256 MB buffer, which leaves the cache full of clean lines) and the fraction of the measured peak (MEASURED_PEAKS.json at the
 repository root; the profiling fallback 6650 GB/s / 1590 TFLOP/s when absent).
 
-Cases (synthetic inputs, shapes and distributions of the BASELINE configs):
+Cases (synthetic inputs, shapes and distributions of the benchmark configurations):
   gdr_t16     gated-delta recurrence, B=1, T=16, 16 QK / 32 V heads of 128, with
               per-token snapshots (config 2): bytes = state in + q,k,v,g,beta + o +
               T snapshots (the last one is the final state)

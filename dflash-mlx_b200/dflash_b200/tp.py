@@ -1,4 +1,4 @@
-"""Tensor parallelism for the Qwen3.5 hybrid target.
+"""Tensor parallelism for the Qwen3.5 hybrid target (benchmark config 5: Qwen3.5-27B, batch 8, context 32768).
 
 Sharding follows the reference's ``Model.shard`` (custom_qwen35_model.py:1286-1402):
 

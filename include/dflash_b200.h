@@ -9,7 +9,7 @@
  * The reference (Aryagm/dflash-mlx) is a Python/MLX package with no C ABI; each
  * entry point below names the reference call it replaces (path:line inside the
  * reference project). The Python host in dflash-mlx_b200/dflash_b200 binds these
- * with ctypes; INTEGRATION.md shows the binding.
+ * with ctypes (dflash_b200/_lib.py lists every signature).
  */
 #ifndef DFLASH_B200_H
 #define DFLASH_B200_H

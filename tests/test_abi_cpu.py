@@ -2,6 +2,8 @@
 import os
 import re
 
+import pytest
+
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
@@ -40,3 +42,43 @@ def test_host_side_argument_errors_are_reported(lib):
         _lib.call("dfl_attention", 1, 1, 1, 0, 0, 1, None, None, 0, 16, 32, 8, 96, 1, 1.0, 16, 0, 1, 0, None, 0, 0, 1, 1 << 30,
                   None)
     assert e.value.status == 2  # head_dim 96 unsupported
+
+
+def test_argument_errors_are_reported_without_a_device(lib):
+    """Entry points validate their arguments before any CUDA call: the status codes and the
+    thread-local message of dfl_last_error (no GPU needed)."""
+    import ctypes
+
+    from dflash_b200 import _lib
+    from dflash_b200._lib import DFlashKernelError
+    cases = [
+        # (entry point, args, expected status, message fragment)
+        ("dfl_sample_keys", (None, 2, 16, ctypes.c_uint64(1), 2, 1, None, None), 1, "dfl_sample_keys"),
+        ("dfl_sample_partials", (None, 10, 2, 10, None, 0.0, None, None), 1, "dfl_sample_partials"),
+        ("dfl_attention_qkv", (None, 0, None, None, None, 1e-6, None, None, 0, 0, None, None, 0, 16, 32, 8, 1.0,
+                               64, 0, None, 0, None, 0, None), 1, "dfl_attention_qkv"),
+        ("dfl_tp_reduce_residual", (None, None, None, None, 0, 1, 1, 0, None, 0, None, 0, None, 16, 256, None), 1,
+         "dfl_tp_reduce_residual"),
+    ]
+    for name, args, status, frag in cases:
+        with pytest.raises(DFlashKernelError) as e:
+            _lib.call(name, *args)
+        assert e.value.status == status, name
+        assert frag in str(e.value), name
+    # zero-sized calls are no-ops that succeed
+    _lib.call("dfl_sample_keys", None, 0, 16, ctypes.c_uint64(1), 2, 1, None, None)
+    _lib.call("dfl_attention_qkv", None, 0, None, None, None, 1e-6, None, None, 0, 0, None, None, 0, 0, 32, 8, 1.0,
+              64, 0, None, 0, None, 0, None)
+
+
+def test_fused_attention_rejects_sequences_that_span_tiles(lib):
+    """dfl_attention_qkv refuses layouts whose sequences cross 16-row tiles (status 2)."""
+    import ctypes
+
+    from dflash_b200 import _lib
+    from dflash_b200._lib import DFlashKernelError
+    dummy = ctypes.c_void_p(16)  # never dereferenced: the layout check comes first
+    with pytest.raises(DFlashKernelError) as e:
+        _lib.call("dfl_attention_qkv", dummy, (32 + 16) * 128, dummy, dummy, dummy, 1e-6, dummy, dummy, 0, 0,
+                  dummy, dummy, 3, 48, 32, 8, 1.0, 64, 0, dummy, 4096, None, 0, None)
+    assert e.value.status == 2 and "16-row tile" in str(e.value)

@@ -54,7 +54,7 @@ def parse_args():
     ap.add_argument("--seed", type=int, default=2)
     ap.add_argument("--layers", type=int, default=36, help="target depth (36 = the Qwen3-4B shape)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-steps", type=int, default=2, help="speculative steps in the CPU baseline sample")
+    ap.add_argument("--cpu-steps", type=int, default=3, help="speculative steps in the CPU baseline sample")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-roofline", action="store_true")
     ap.add_argument("--workload", choices=["c3", "c4", "c5"], default="c3")
@@ -220,8 +220,8 @@ def cpu_sample(tcfg, dcfg, tw, dw, sess, trace, lengths, noise, n_steps: int) ->
     from oracle import dflash_oracle as O
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    cpu_w = lambda w: {k: (v.cpu() if torch.is_tensor(v) else [{kk: vv.cpu() for kk, vv in l.items()} for l in v])  # noqa
-                       for k, v in w.items()}
+    cpu_w = lambda w: _fp32_weights({k: (v.cpu() if torch.is_tensor(v) else  # noqa: E731
+                                         [{kk: vv.cpu() for kk, vv in l.items()} for l in v]) for k, v in w.items()})
     ot = O.OracleTarget(tcfg, cpu_w(tw))
     od = O.OracleDraft(dcfg, cpu_w(dw), ot)
     P = int(sess.state[0, 9].item())
@@ -267,24 +267,116 @@ def cpu_sample(tcfg, dcfg, tw, dw, sess, trace, lengths, noise, n_steps: int) ->
                       f"from context {P}, CPU oracle restatement, {dt:.1f} s"}
 
 
+def _fp32_weights(w: dict) -> dict:
+    """The same (bf16-valued) weights held as fp32: the oracle computes in fp32, so this
+    saves a conversion per projection call."""
+    f = lambda t: t.float() if torch.is_tensor(t) and t.is_floating_point() else t  # noqa: E731
+    out = {k: f(v) for k, v in w.items() if k != "layers"}
+    out["layers"] = [{k: f(v) for k, v in lw.items()} for lw in w["layers"]]
+    return out
+
+
+def run_reference(args, world: int, rank: int) -> None:
+    """The reference arm: the reference's algorithm for this path (the oracle restatement,
+    pinned to the reference's own runtime / draft / adapters by golden fixtures; MLX itself
+    does not install here) timed on the host cores. It touches no GPU and loads no library
+    of this repository: weights, prefill, the greedy trace behind the injected drafts and
+    the timed steps are all computed by the oracle on the CPU. Rank 0 alone runs it."""
+    if rank != 0:
+        return
+    from oracle import dflash_oracle as O
+    from dflash_b200.config import DraftConfig, TargetConfig, evenly_spaced_layers
+    from dflash_b200.weights import random_draft_weights, random_target_weights
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    t_setup = time.perf_counter()
+    tcfg = TargetConfig(num_hidden_layers=args.layers)
+    dcfg = DraftConfig(target_layer_ids=evenly_spaced_layers(args.layers, 5) if args.layers >= 8
+                       else [1, args.layers - 1])
+    tw = _fp32_weights(random_target_weights(tcfg, args.seed))
+    dw = _fp32_weights(random_draft_weights(dcfg, args.seed))
+    ot = O.OracleTarget(tcfg, tw)
+    od = O.OracleDraft(dcfg, dw, ot)
+    bs = dcfg.block_size
+    n_steps = max(1, min(args.steps, args.cpu_steps))
+    lengths, noise = injection_plan(n_steps + 4, bs, args.tau, tcfg.vocab_size, args.seed)
+    g = torch.Generator().manual_seed(args.seed)
+    prompt = torch.randint(0, tcfg.vocab_size, (args.prompt_len,), generator=g).tolist()
+    P = len(prompt)
+    cap = P + bs * (n_steps + 4)
+    tcache, dcache = ot.make_cache(cap), od.make_cache(cap)
+    logits, hidden = ot.forward_with_hidden_states(prompt, tcache, dcfg.target_layer_ids)
+    out = prompt + [int(O.argmax_first(logits[-1]))]
+    # the target's greedy continuation, far enough for every injected prefix (untimed)
+    need = P + 1 + sum(int(x) + 1 for x in lengths[:n_steps]) + bs
+    gcache = ot.make_cache(need + 1)
+    for c, src in zip(gcache, tcache):
+        c.k[:, :P] = src.k[:, :P]
+        c.v[:, :P] = src.v[:, :P]
+        c.offset = P
+    trace = list(out)
+    while len(trace) < need:
+        lg, _ = ot.forward_with_hidden_states([trace[-1]], gcache, [])
+        trace.append(int(O.argmax_first(lg[-1])))
+    del gcache
+    setup_s = time.perf_counter() - t_setup
+    start, accepted = P, 0
+    t0 = time.perf_counter()
+    for s in range(n_steps):
+        block = [out[start]] + [dcfg.mask_token_id] * (bs - 1)
+        dh = od(ot.embed_tokens(block), hidden, dcache)
+        O.argmax_first(ot.lm_head_logits(dh[1:]))
+        for c in dcache:
+            c.trim(bs)
+        L = int(lengths[s])
+        for i in range(1, bs):
+            block[i] = trace[start + i] if i - 1 < L else int(noise[s, i])
+        lg, hid = ot.forward_with_hidden_states(block, tcache, dcfg.target_layer_ids)
+        post = O.argmax_first(lg).tolist()
+        m = O.longest_prefix_match(block[1:], post[:-1])
+        acc = m + 1
+        for c in tcache:
+            c.trim(bs - acc)
+        hidden = hid[:acc]
+        out = out[:start] + block[:acc] + [post[m]]
+        start += acc
+        accepted += acc
+    dt = time.perf_counter() - t0
+    value = accepted / dt
+    sample = (f"{n_steps} speculative steps (draft + 16-token verify + accept) of the config-3 workload from "
+              f"context {P}, {dt:.1f} s timed ({setup_s:.0f} s untimed set-up: seeded weights, prefill and the "
+              f"greedy trace behind the injected drafts, all on the CPU)")
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": n_steps,
+            "warmup": 0, "ms_per_step": dt / n_steps * 1e3, "higher_is_better": True, "impl": "reference",
+            "scaling": "weak", "dtype": "bf16",
+            "data": "synthetic (random-init weights, random prompt, oracle-injected drafts)",
+            "config": {"workload": f"config3: Qwen3-4B-shaped target ({args.layers} layers) + 5-layer DFlash draft, "
+                                   f"block 16, prompt {args.prompt_len}, oracle-injected acceptance tau {args.tau}",
+                       "global_batch": 1, "seq_len": args.prompt_len, "parallelism": "cpu (host cores)",
+                       "target_layers": args.layers},
+            "tau_measured": accepted / n_steps,
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "vs_baseline": None, "gpu_launches": 0,
+            "note": "MLX (the reference's array library) has no wheel here, so the reference itself cannot run; "
+                    "its algorithm is timed as restated in oracle/dflash_oracle.py (bf16 storage, fp32 math), "
+                    "which golden fixtures pin to the reference's own runtime.py, draft.py and adapters.py"}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":  # CPU only: no process group, no device, no library of ours
+        return run_reference(args, world, rank)
     if world > 1:
         import torch.distributed as dist
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     device = torch.device("cuda", local if torch.cuda.is_available() else 0)
     torch.cuda.set_device(device)
-
-    if args.impl == "reference" and rank != 0:
-        if world > 1:
-            import torch.distributed as dist
-            dist.barrier()
-            dist.destroy_process_group()
-        return
 
     from dflash_b200 import _lib
     from dflash_b200.runtime import SpecSession, S_START
@@ -311,28 +403,6 @@ def main():
         sess.set_injection(trace_t[None], lengths[None], noise.reshape(1, -1))
         sess.prefill([prompt], n_new)
         return sess
-
-    if args.impl == "reference":
-        sess = new_session()
-        torch.cuda.synchronize()
-        n = max(1, min(args.steps, args.cpu_steps))
-        cpu = cpu_sample(tcfg, dcfg, tw, dw, sess, trace, lengths, noise, n)
-        line = {"metric": METRIC, "value": cpu["value"], "unit": UNIT, "n_gpus": world, "steps": n,
-                "warmup": 0, "higher_is_better": True, "impl": "reference", "dtype": "bf16",
-                "data": "synthetic (random-init weights, random prompt, oracle-injected drafts)",
-                "config": {"workload": "config3: Qwen3-4B shape, block 16, prompt 512, tau 6.5",
-                           "global_batch": 1, "seq_len": args.prompt_len, "parallelism": "cpu"},
-                "cpu_baseline": {**cpu, "value": cpu["value"]},
-                "e2e": {"value": cpu["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-                "vs_baseline": None,
-                "note": "the reference (MLX) cannot run on this box; the CPU restatement of its algorithm "
-                        "(oracle/dflash_oracle.py, pinned to the reference runtime by golden fixtures) is timed"}
-        print(json.dumps(line), flush=True)
-        if world > 1:
-            import torch.distributed as dist
-            dist.barrier()
-            dist.destroy_process_group()
-        return
 
     # ---------------- our arm: device-timed value ----------------
     sess = new_session()

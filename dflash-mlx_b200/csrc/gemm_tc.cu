@@ -54,20 +54,6 @@ int* device_error_word() {
   return ptrs[dev];
 }
 
-#ifdef DFL_TC_TRACE
-// phase timestamps per CTA (debug builds only)
-static __device__ unsigned long long g_tc_trace[8192][16];
-__device__ __forceinline__ unsigned long long gtimer() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
-#define TC_STAMP(k) g_tc_trace[blockIdx.x][k] = gtimer()
-#define TC_STAMP_AT(c, k) g_tc_trace[(c) & 8191][k] = gtimer()
-#else
-#define TC_STAMP(k)
-#define TC_STAMP_AT(c, k)
-#endif
 
 constexpr int TC_NT = 128;  // W rows per tile (MMA M)
 constexpr int TC_BK = 64;   // k per stage (one 128-byte swizzle row)
@@ -308,7 +294,6 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
   const long long u1 = (long long)(c + 1) * a.U1 / a.grid1;
   const int n_units = (int)(u1 - u0);
   const bool norm = a.norm_w != nullptr;
-  if (threadIdx.x == 0) TC_STAMP(0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < TC_STAGES; ++s) {
@@ -332,7 +317,6 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   grid_dependency_launch_dependents();
-  if (threadIdx.x == 0) TC_STAMP(1);
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -351,7 +335,6 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
       }
       grid_dependency_wait();  // X is produced by the previous kernel
       if (lane == 0) {
-        TC_STAMP(2);
         for (int i = 0; i < pre; ++i)
           tma_load_2d(&xmap, &full[i], smem + TC_OFF_X + i * TC_X_BYTES, (int)((u0 + i) % a.kb) * TC_BK, mt * TC_BM,
                       pol_x);
@@ -391,7 +374,6 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
           tc_fence_after();
         }
         if (!mbar_wait(norm ? &xready[s] : &full[s], (i / TC_STAGES) & 1, 203, a.err)) break;
-        if (i == 0) TC_STAMP(3);
         tc_fence_after();
         const uint32_t d = tmem + (uint32_t)((seg & 1) * TC_NACC * TC_BM);
         const uint64_t ad = sw128_desc(w0 + s * TC_W_BYTES);
@@ -403,7 +385,6 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
         tc_commit(&empty[s]);
         if (j == a.kb - 1 || i == n_units - 1) tc_commit(&accf[seg & 1]);
       }
-      TC_STAMP(4);
     }
     __syncwarp();  // the whole warp reaches the teardown (and the .sync.aligned dealloc) together
   } else {
@@ -451,7 +432,6 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
       const bool seg_end = (j == a.kb - 1) || (i == n_units - 1);
       if (!seg_end) continue;
       if (!mbar_wait(&accf[seg & 1], (seg >> 1) & 1, 205, a.err)) break;
-      if (et == 0) TC_STAMP(5);
       tc_fence_after();
       float v[TC_BM];
       tc_ld_acc(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((seg & 1) * TC_NACC * TC_BM), v);
@@ -471,13 +451,11 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
 #pragma unroll
         for (int t4 = 0; t4 < TC_BM / 4; ++t4) mine[t4] = make_float4(v[4 * t4], v[4 * t4 + 1], v[4 * t4 + 2], v[4 * t4 + 3]);
         asm volatile("fence.acq_rel.gpu;\n" ::: "memory");  // publish this segment's partial
-        if (et == 0) TC_STAMP(8);
         epi_sync();
         if (et == 0) {
           int prev;
           asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;\n" : "=r"(prev) : "l"(a.counters + tile_id) : "memory");
           s_flag = (prev == c_last - c_first);
-          TC_STAMP(9);
         }
         epi_sync();
         do_epi = s_flag != 0;
@@ -515,20 +493,16 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
           }
           if (et == 0) {
             a.counters[tile_id] = 0;  // ready for the next launch / graph replay
-            TC_STAMP(10);
           }
         }
         epi_sync();  // s_flag is rewritten by the next segment
       }
       if (do_epi) tc_epilogue<EPI>(a, v, mt * TC_BM, nt, q, lane, xchg);
-      if (do_epi && et == 0) TC_STAMP(11);
       (void)ew;
     }
-    if (et == 0) TC_STAMP(6);
   }
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0) TC_STAMP(7);
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "n"(TC_TMEM_COLS));
@@ -604,7 +578,6 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
   const bool norm = a.norm_w != nullptr;
   const int cta_lin = r + S * (nt + a.n_tiles * mt);
   (void)cta_lin;
-  if (threadIdx.x == 0) TC_STAMP_AT(cta_lin, 0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < TC_STAGES; ++s) {
@@ -638,7 +611,6 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
   float rres[TC_BM], v[TC_BM];
 #pragma unroll
   for (int t = 0; t < TC_BM; ++t) rres[t] = v[t] = 0.f;
-  if (threadIdx.x == 0) TC_STAMP_AT(cta_lin, 1);
 
   if (warp == 0) {
     if (lane == 0 && n_units > 0) {
@@ -651,7 +623,6 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
         bulk_load(smem + i * TC_W_BYTES, a.wt + (ubase + i) * TC_W_BYTES, TC_W_BYTES, &full[i], pol_w);
       }
       grid_dependency_wait();  // X is produced by the previous kernel
-      TC_STAMP_AT(cta_lin, 2);
       for (int i = 0; i < pre; ++i)
         tma_load_2d(&xmap, &full[i], smem + TC_OFF_X + i * TC_X_BYTES, (j0 + i) * TC_BK, mt * TC_BM, pol_x);
       int issued = pre;
@@ -674,7 +645,6 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
       for (int i = 0; i < n_units; ++i) {
         const int s = i % TC_STAGES;
         if (!mbar_wait(norm ? &xready[s] : &full[s], (i / TC_STAGES) & 1, 303, a.err)) break;
-        if (i == 0) TC_STAMP_AT(cta_lin, 3);
         tc_fence_after();
         const uint64_t ad = sw128_desc(w0 + s * TC_W_BYTES);
         const uint64_t bd = sw128_desc(x0 + s * TC_X_BYTES);
@@ -685,7 +655,6 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
         tc_commit(&empty[s]);
       }
       tc_commit(&accf[0]);
-      TC_STAMP_AT(cta_lin, 4);
     }
     __syncwarp();
   } else {
@@ -732,7 +701,6 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
       }
     }
     if (n_units > 0 && mbar_wait(&accf[0], 0, 305, a.err)) {
-      if (threadIdx.x == 64) TC_STAMP_AT(cta_lin, 5);
       tc_fence_after();
       tc_ld_acc(tmem + ((uint32_t)(q * 32) << 16), v);
       tc_fence_before();
@@ -742,12 +710,10 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
   // owner rank with st.async into the owner's receive slots, completing on an mbarrier
   // there; the owner sums the ranks in rank order. Slots in the weight ring need every
   // ring free first (each CTA's epilogue warps passed accf, so its MMAs are done).
-  if (threadIdx.x == 64) TC_STAMP_AT(cta_lin, 6);
   if (dedicated)
     cluster_wait();
   else
     cluster_sync_all();
-  if (threadIdx.x == 64) TC_STAMP_AT(cta_lin, 7);
   constexpr bool SILU = EPI == DFL_EPI_SILU_MUL;
   const int slots = SILU ? 2 * S : S - 1;  // per owned unit
   if (warp >= TC_EPI_WARP0) {
@@ -772,7 +738,6 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
       if (slots > 0 && !mbar_wait(&recv[js], 0, 306, a.err)) {
         // gave up: the sums below read whatever arrived; the error word reports it
       }
-      if (lane == 0) TC_STAMP_AT(cta_lin, 10 + (q & 1));
       const float* base = reinterpret_cast<const float*>(rbuf + js * slots * TC_CSK_SLOT_BYTES) + lane * 16;
       if constexpr (SILU) {
         float gv[TC_BM], uv[TC_BM];
@@ -819,15 +784,11 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
             }
           }
         }
-        if (lane == 0) TC_STAMP_AT(cta_lin, 12 + (q & 1));
         tc_epilogue<EPI>(a, acc, mt * TC_BM, nt, q, lane, nullptr, rres);
-        if (lane == 0) TC_STAMP_AT(cta_lin, 14 + (q & 1));
       }
     }
   }
-  if (threadIdx.x == 64) TC_STAMP_AT(cta_lin, 8);
   cluster_wait();  // no CTA leaves while a push to it may be in flight
-  if (threadIdx.x == 64) TC_STAMP_AT(cta_lin, 9);
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -1724,6 +1685,10 @@ extern "C" int dfl_gemm_bf16_noalloc(const void* x, int64_t ldx, const void* w_p
                                      int epilogue, const void* residual, int64_t ldr, void* y, int64_t ldy, void* y2,
                                      int64_t ldy2, void* argmax_partials, const void* norm_w, const float* sumsq_in,
                                      int n_parts, float eps, float* sumsq_out, void* stream) {
+  if (M < 0 || N < 0 || K < 0) {
+    set_error("dfl_gemm_bf16_noalloc: negative size (M=%d N=%d K=%d)", M, N, K);
+    return DFL_ERR_INVALID;
+  }
   if (M > TC_BM) {
     set_error("dfl_gemm_bf16_noalloc: M=%d exceeds the built-in scratch limit of %d rows; use dfl_gemm_bf16 with a "
               "workspace",
@@ -1750,8 +1715,3 @@ extern "C" int dfl_gemm_bf16_noalloc(const void* x, int64_t ldx, const void* w_p
                        sumsq_in, n_parts, eps, sumsq_out, scratch, NA_SCRATCH_BYTES, stream);
 }
 
-#ifdef DFL_TC_TRACE
-extern "C" int dfl_debug_tc_trace(void* host, int n_ctas) {
-  return cudaMemcpyFromSymbol(host, g_tc_trace, (size_t)n_ctas * 16 * sizeof(unsigned long long)) == cudaSuccess ? 0 : 3;
-}
-#endif

@@ -17,10 +17,6 @@ CSRC = PKG_DIR.parent / "csrc"
 INCLUDE = PKG_DIR.parent.parent / "include"
 LIB_PATH = PKG_DIR / "libdflash_b200.so"
 OBJ_DIR = PKG_DIR.parent / "_build"
-# diagnostic build with per-CTA phase timestamps in the weight-streaming GEMMs
-# (read by ``python -m dflash_b200.gemm_trace``; load it with DFLASH_B200_LIB=<path>)
-TRACE_LIB_PATH = PKG_DIR / "libdflash_b200_trace.so"
-TRACE_OBJ_DIR = PKG_DIR.parent / "_build_trace"
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -47,8 +43,8 @@ def _stale(lib: Path) -> bool:
     return any(p.stat().st_mtime > t for p in deps)
 
 
-def build(force: bool = False, verbose: bool = False, trace: bool = False) -> Path:
-    lib_path, obj_dir = (TRACE_LIB_PATH, TRACE_OBJ_DIR) if trace else (LIB_PATH, OBJ_DIR)
+def build(force: bool = False, verbose: bool = False) -> Path:
+    lib_path, obj_dir = LIB_PATH, OBJ_DIR
     if not force and not _stale(lib_path):
         return lib_path
     obj_dir.mkdir(exist_ok=True)
@@ -56,7 +52,7 @@ def build(force: bool = False, verbose: bool = False, trace: bool = False) -> Pa
     objs = []
     for src in sources():
         obj = obj_dir / (src.stem + ".o")
-        cmd = [nvcc, *NVCC_FLAGS, *(["-DDFL_TC_TRACE"] if trace else []), "-I", str(INCLUDE), "-c", str(src),
+        cmd = [nvcc, *NVCC_FLAGS, "-I", str(INCLUDE), "-c", str(src),
                "-o", str(obj)]
         if verbose:
             print(" ".join(cmd), file=sys.stderr)
@@ -70,4 +66,4 @@ def build(force: bool = False, verbose: bool = False, trace: bool = False) -> Pa
 
 
 if __name__ == "__main__":
-    print(build(force="--force" in sys.argv, verbose=True, trace="--trace" in sys.argv))
+    print(build(force="--force" in sys.argv, verbose=True))

@@ -50,16 +50,43 @@ def test_tiny_spec_equals_plain_greedy():
 
 
 def test_tiny_greedy_agrees_with_oracle():
+    """Config 1's whole 128-token greedy run. Free running, the two decodes agree up to
+    the first bf16 near-tie (after it the contexts differ), reported. Teacher forced over
+    the oracle's own 192-token sequence, the GPU's greedy token equals the oracle's on
+    every row except near-ties (top-two oracle logits within 2e-2), asserted."""
     from oracle import dflash_oracle as O
     tcfg, dcfg, tw, dw, target, draft = _tiny()
     g = torch.Generator().manual_seed(0)
     prompt = torch.randint(0, tcfg.vocab_size, (64,), generator=g).tolist()
-    plain, _ = _run(target, None, prompt, 32, 1)
-    ref = O.plain_greedy(O.OracleTarget(tcfg, tw), prompt, 32)
-    agree = sum(int(a == b) for a, b in zip(plain[64:], ref[64:])) / 32
-    print(f"greedy-token agreement with the oracle: {agree:.3f}")
-    # first divergence only comes from bf16 near-ties; the prefix must agree
+    n = 128
+    plain, _ = _run(target, None, prompt, n, 1)
+    ot = O.OracleTarget(tcfg, tw)
+    ref = O.plain_greedy(ot, prompt, n)
+    agree = sum(int(a == b) for a, b in zip(plain[64:], ref[64:])) / n
+    first = next((i for i, (a, b) in enumerate(zip(plain[64:], ref[64:])) if a != b), n)
+    print(f"free-running greedy-token agreement with the oracle over {n} tokens: {agree:.3f} "
+          f"(first divergence at token {first})")
     assert plain[64:68] == ref[64:68]
+    # teacher forced: both models read the oracle's sequence
+    seq = ref[:64 + n]
+    cache = target.make_cache(1, len(seq))
+    parts = []
+    for c0 in range(0, len(seq), 96):
+        c1 = min(len(seq), c0 + 96)
+        parts.append(target.forward(torch.tensor(seq[c0:c1], dtype=torch.int32, device="cuda"),
+                                    torch.arange(c0, c1, dtype=torch.int32, device="cuda"), cache, max_kv=c1,
+                                    head="logits").float().cpu())
+    got = torch.cat(parts, 0)[63:]
+    ref_lg, _ = ot.forward_with_hidden_states(seq, ot.make_cache(len(seq) + 8), [])
+    ref_lg = ref_lg[63:]
+    mism = got.argmax(-1) != ref_lg.argmax(-1)
+    top2 = ref_lg.topk(2, dim=-1).values
+    gap = top2[:, 0] - top2[:, 1]
+    tf_agree = 1.0 - mism.float().mean().item()
+    print(f"teacher-forced greedy-token agreement over {len(got)} rows: {tf_agree:.3f}; "
+          f"logits max err {(got - ref_lg).abs().max().item():.4f}")
+    assert bool((gap[mism] <= 2e-2).all()), gap[mism]
+    assert tf_agree >= 0.97
 
 
 def test_tiny_injected_acceptance_matches_oracle():

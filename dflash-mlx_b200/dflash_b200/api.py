@@ -3,6 +3,7 @@ from __future__ import annotations
 
 from collections.abc import Iterator
 from dataclasses import dataclass
+from pathlib import Path
 from typing import Any
 
 import torch
@@ -36,28 +37,98 @@ class DFlashStreamEvent:
     finished: bool = False
 
 
-def load_draft_model(spec, target: LoadedTargetModel, seed: int = 0, mask_mode: str = "none") -> DraftModel:
-    """``"random:<preset>"``, a ``(DraftConfig, weights)`` tuple, or a DFlash draft checkpoint
-    directory (config.json + model*.safetensors, draft.py:226-238)."""
-    if isinstance(spec, DraftModel):
-        return spec
-    if isinstance(spec, tuple):
-        cfg, w = spec
-    elif isinstance(spec, str) and spec.startswith("random:"):
-        cfg = PRESETS[spec.split(":", 1)[1]]()[1]
-        w = random_draft_weights(cfg, seed)
-    else:
-        from .checkpoint import load_draft_checkpoint
-        cfg, w, _ = load_draft_checkpoint(spec)
-    return DraftModel(cfg, w, target.model, mask_mode=mask_mode)
+@dataclass
+class DraftCheckpoint:
+    """A DFlash draft as loaded, before it is placed on a target's device: its config,
+    its weights in checkpoint layout and the draft contract fields the runtime reads
+    (draft.py:190-223). ``bind(target)`` builds the GPU draft, which shares the target's
+    embedding and lm_head as the reference's draft does."""
+    cfg: Any
+    weights: dict
+    attention_mask_mode: str = "none"
+
+    @property
+    def block_size(self) -> int:
+        return self.cfg.block_size
+
+    @property
+    def mask_token_id(self) -> int:
+        return self.cfg.mask_token_id
+
+    @property
+    def target_layer_ids(self) -> list[int]:
+        return list(self.cfg.target_layer_ids)
+
+    def bind(self, target) -> DraftModel:
+        model = target.model if isinstance(target, LoadedTargetModel) else target
+        return DraftModel(self.cfg, self.weights, model, mask_mode=self.attention_mask_mode)
+
+
+def load_draft_model(path_or_repo, seed: int = 0) -> tuple[DraftCheckpoint, Any]:
+    """Reference signature and return (draft.py:224-236): ``(draft, model_path)``.
+    ``path_or_repo`` is a DFlash draft checkpoint directory (config.json +
+    model*.safetensors; local only, there is no network here), ``"random:<preset>"``
+    (seeded random weights of a preset's shape) or a ``(DraftConfig, weights)`` tuple. The
+    draft is placed on the GPU by ``DFlashGenerator`` (or ``draft.bind(target)``), because
+    it reads the target's embedding."""
+    if isinstance(path_or_repo, tuple):
+        cfg, w = path_or_repo
+        return DraftCheckpoint(cfg, w), None
+    if isinstance(path_or_repo, str) and path_or_repo.startswith("random:"):
+        cfg = PRESETS[path_or_repo.split(":", 1)[1]]()[1]
+        return DraftCheckpoint(cfg, random_draft_weights(cfg, seed)), path_or_repo
+    from .checkpoint import load_draft_checkpoint
+    cfg, w, path = load_draft_checkpoint(path_or_repo)
+    return DraftCheckpoint(cfg, w), Path(path)
+
+
+QUANT_BITS = (2, 3, 4, 5, 6, 8)
+QUANT_GROUPS = (32, 64, 128)
+
+
+def quantize_dequantize(w: torch.Tensor, bits: int, group_size: int) -> torch.Tensor:
+    """Affine group quantization of a [N, K] weight, returned dequantized (bf16): per group
+    of ``group_size`` consecutive inputs, scale = (max - min) / (2^bits - 1) and
+    bias = min, q = round((w - bias) / scale) clamped to [0, 2^bits - 1], w' = q * scale +
+    bias, with scale and bias stored in bf16. This is the published affine scheme behind
+    the reference's ``quantize_model`` of the draft (draft.py:239-252, api.py:62-66): the
+    draft then computes with w'. The weights stay bf16 in HBM (no packed low-bit GEMM)."""
+    N, K = w.shape
+    if K % group_size:
+        raise ValueError(f"input dimension {K} is not a multiple of the group size {group_size}")
+    x = w.float().reshape(N, K // group_size, group_size)
+    lo, hi = x.amin(-1, keepdim=True), x.amax(-1, keepdim=True)
+    levels = (1 << bits) - 1
+    scale = ((hi - lo) / levels).to(torch.bfloat16).float()
+    bias = lo.to(torch.bfloat16).float()
+    safe = torch.where(scale > 0, scale, torch.ones_like(scale))
+    q = torch.clamp(torch.round((x - bias) / safe), 0, levels)
+    return (q * scale + bias).reshape(N, K).to(torch.bfloat16)
+
+
+def maybe_quantize_draft_model(draft: DraftCheckpoint, bits: int | None, group_size: int) -> dict | None:
+    """draft.py:239-252: quantize every projection of the draft (fc, q/k/v/o, gate/up/down;
+    the draft owns no embedding) and return the quantization record ``{"group_size",
+    "bits"}``, or None when ``bits`` is None."""
+    if bits is None:
+        return None
+    if bits not in QUANT_BITS:
+        raise ValueError(f"draft_quant_bits must be one of {QUANT_BITS}")
+    if group_size not in QUANT_GROUPS:
+        raise ValueError(f"draft_quant_group_size must be one of {QUANT_GROUPS}")
+    w = dict(draft.weights)
+    w["fc"] = quantize_dequantize(w["fc"], bits, group_size)
+    names = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
+    w["layers"] = [{k: (quantize_dequantize(v, bits, group_size) if k in names else v) for k, v in lw.items()}
+                   for lw in w["layers"]]
+    draft.weights = w
+    return {"group_size": group_size, "bits": bits}
 
 
 class DFlashGenerator:
     def __init__(self, target_model=DEFAULT_TARGET_MODEL, draft_model=DEFAULT_DRAFT_MODEL,
                  draft_attention_mask: str = "auto", draft_quant_bits: int | None = None,
                  draft_quant_group_size: int = 64, seed: int = 0, device: str = "cuda"):
-        if draft_quant_bits is not None:
-            raise NotImplementedError("draft quantisation is not part of this build")
         torch.manual_seed(seed)
         self.seed = int(seed)  # default sampling seed of generate / stream
         self.requested_target_model = target_model
@@ -67,9 +138,17 @@ class DFlashGenerator:
         if draft_attention_mask == "auto":
             draft_attention_mask = "causal" if self.target.adapter.family == "qwen3_5" else "none"
         self.draft_attention_mask = draft_attention_mask
-        self.draft = load_draft_model(draft_model, self.target, seed=seed, mask_mode=draft_attention_mask)
+        if isinstance(draft_model, DraftModel):
+            self.draft, self.draft_path = draft_model, None
+            self.draft_quantization = None
+            if draft_quant_bits is not None:
+                raise ValueError("draft_quant_bits needs a draft checkpoint or spec, not a built DraftModel")
+        else:
+            ckpt, self.draft_path = load_draft_model(draft_model, seed=seed)
+            ckpt.attention_mask_mode = draft_attention_mask
+            self.draft_quantization = maybe_quantize_draft_model(ckpt, draft_quant_bits, draft_quant_group_size)
+            self.draft = ckpt.bind(self.target)
         self.draft.mask_mode = draft_attention_mask
-        self.draft_quantization = None
 
     @property
     def target_model_path(self):

@@ -83,11 +83,15 @@ class SpecSession:
     def __init__(self, target: TargetModel, draft: DraftModel | None, batch: int, max_total: int,
                  block_size: int, stop_token_ids: set[int] | None = None, use_graph: bool = True,
                  max_steps: int | None = None, prefill_chunk: int = 128, temperature: float = 0.0,
-                 seed: int = 0):
+                 seed: int = 0, profile: bool = False):
         """temperature >= 1e-5 samples (Gumbel-max on the bf16 logits, keyed by sequence and
         absolute position: the speculative decode reproduces the plain sampled decode of the
         same seed token for token); below it decoding is greedy (fused lm_head argmax)."""
         self.sampled = temperature >= 1e-5
+        # profile=True: the verify half is captured as three graphs (forward, accept,
+        # rollback) so that step(events=5 events) can time each part on the device
+        self.profile = profile
+        self.profile_events: list[tuple] = []
         self.temperature = float(temperature)
         self.seed = int(seed)
         self.target = target
@@ -263,14 +267,24 @@ class SpecSession:
 
     def _verify_kernels(self) -> None:
         """Target verify forward + accept (parallel-replay, runtime.py:117-163)."""
+        self._verify_forward()
+        self._verify_accept()
+        self._verify_rollback()
+
+    def _verify_forward(self) -> None:
         part = self.target.forward(self.block, self.tpos, self.tcache, max_kv=self.cap, layer_ids=self.layer_ids,
                                    taps_out=self.taps, row_seq=self.row_seq, ws=self.ws, seq_rows=self.bs,
                                    key_chunk=self.key_chunk, head="logits" if self.sampled else "argmax")
         if self.sampled:  # verify row i predicts the token at position start + i + 1
             ops.sample_keys(self.state, self.B, self.bs, self.seed, ops.SAMPLE_TAG_TARGET, 1, self.keys)
             part = ops.sample_partials(part, self.keys, self.temperature, out=self.spart)
-        ops.verify_accept(self.state, part, self.block, self.bs, self.out_tokens, self.B,
+        self._verify_part = part
+
+    def _verify_accept(self) -> None:
+        ops.verify_accept(self.state, self._verify_part, self.block, self.bs, self.out_tokens, self.B,
                           stop_ids=self.stop_ids, n_stop=self.n_stop, accept_log=self.accept_log)
+
+    def _verify_rollback(self) -> None:
         if self.hybrid:
             # recurrent layers keep the state after the accepted prefix (snapshot restore);
             # attention KV needs no truncation: the next block overwrites rows past start
@@ -280,33 +294,38 @@ class SpecSession:
         """Captures the draft half and the verify half of a step as two CUDA graphs."""
         s = torch.cuda.Stream(device=self.dev)
         s.wait_stream(torch.cuda.current_stream(self.dev))
-        gd, gv = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+        parts = [self._draft_kernels]
+        parts += [self._verify_forward, self._verify_accept, self._verify_rollback] if self.profile \
+            else [self._verify_kernels]
+        graphs = [torch.cuda.CUDAGraph() for _ in parts]
         with torch.cuda.stream(s):
-            with torch.cuda.graph(gd, stream=s):
-                self._draft_kernels()
-            with torch.cuda.graph(gv, stream=s):
-                self._verify_kernels()
+            for g, fn in zip(graphs, parts):
+                with torch.cuda.graph(g, stream=s):
+                    fn()
         torch.cuda.current_stream(self.dev).wait_stream(s)
-        self.graph = (gd, gv)
+        self.graph = tuple(graphs)
 
     def step(self, events: tuple | None = None) -> None:
         """One speculative step. ``events`` = (before, between, after) CUDA events to time
-        the draft and the verify halves."""
+        the draft and the verify halves; a session made with profile=True takes five
+        (before, after draft, after verify forward, after accept, after rollback)."""
+        if self.use_graph and self.graph is None:
+            self.capture()
+        fine = events is not None and len(events) == 5
+        if fine and not self.profile:
+            raise ValueError("five step events need a session made with profile=True")
+        if self.use_graph:
+            parts = [g.replay for g in self.graph]
+        else:
+            parts = [self._draft_kernels] + ([self._verify_forward, self._verify_accept, self._verify_rollback]
+                                             if self.profile else [self._verify_kernels])
         if events is not None:
             events[0].record()
-        if self.use_graph:
-            if self.graph is None:
-                self.capture()
-            self.graph[0].replay()
-        else:
-            self._draft_kernels()
-        if events is not None:
-            events[1].record()
-        if self.use_graph:
-            self.graph[1].replay()
-        else:
-            self._verify_kernels()
-        if events is not None:
+        for i, fn in enumerate(parts):
+            fn()
+            if events is not None and (fine or i == 0):
+                events[i + 1].record()
+        if events is not None and not fine:
             events[2].record()
 
     def poll_state(self) -> torch.Tensor:
@@ -333,7 +352,12 @@ class SpecSession:
             if launched < max_steps:
                 if before_step is not None:
                     before_step(first_index + launched)
-                self.step()
+                if self.profile:
+                    evs = tuple(torch.cuda.Event(enable_timing=True) for _ in range(5))
+                    self.profile_events.append(evs)
+                    self.step(events=evs)
+                else:
+                    self.step()
                 hs, ht, ev = self._ring[launched % 2]
                 hs.copy_(self.state, non_blocking=True)
                 if copy_tokens:
@@ -350,6 +374,18 @@ class SpecSession:
             yield hs, ht
         stream.synchronize()
         self.steps_launched = launched
+
+    def profile_times(self) -> dict[str, float]:
+        """Device time of each part of the profiled steps, summed (seconds), under the
+        reference's profile keys (runtime.py:61-71, 117-163, 406-518)."""
+        keys = ("draft_time_s", "verify_forward_logits_time_s", "verify_prefix_time_s", "verify_rollback_time_s")
+        out = dict.fromkeys(keys, 0.0)
+        for evs in self.profile_events:
+            evs[-1].synchronize()
+            for i, k in enumerate(keys):
+                out[k] += evs[i].elapsed_time(evs[i + 1]) * 1e-3
+        out["verify_time_s"] = sum(out[k] for k in keys[1:])
+        return out
 
     def run(self, max_steps: int, copy_tokens: bool = False) -> int:
         for _ in self.run_iter(max_steps, copy_tokens):
@@ -394,7 +430,7 @@ def dflash_generate_stream(target: TargetModel, draft: DraftModel, prompt_tokens
     use_draft = draft if block_size > 1 else None
     total_max = prompt_len + max_new_tokens
     sess = SpecSession(target, use_draft, 1, total_max, block_size, stop_token_ids, use_graph=use_graph,
-                       temperature=temperature, seed=seed)
+                       temperature=temperature, seed=seed, profile=profile)
 
     torch.cuda.synchronize(target.device)
     t0 = time.perf_counter()
@@ -409,10 +445,12 @@ def dflash_generate_stream(target: TargetModel, draft: DraftModel, prompt_tokens
         streamed_len = len(output_tokens)
 
     decode_start = time.perf_counter()
+    bookkeeping = 0.0
     finished = bool(sess.state[0, S_FINISHED].item()) or max_new_tokens <= 0
     if not finished:
         # a step commits at least one token, so max_new_tokens + 1 steps always finish
         for host_state, host_tokens in sess.run_iter(max_new_tokens + 1):
+            t_book = time.perf_counter()
             start = int(host_state[0, S_START])
             stop = int(host_state[0, S_STOP])
             n = min(start + 1, total_max)
@@ -420,8 +458,11 @@ def dflash_generate_stream(target: TargetModel, draft: DraftModel, prompt_tokens
                 n = min(n, stop + 1)
             if n > streamed_len:
                 toks = host_tokens[0, :n].tolist()
+                bookkeeping += time.perf_counter() - t_book
                 yield DFlashRuntimeEvent(token_ids=toks[streamed_len:], output_tokens=toks)
                 streamed_len = n
+            else:
+                bookkeeping += time.perf_counter() - t_book
     torch.cuda.synchronize(target.device)
     decode_time = time.perf_counter() - decode_start
     outs, accs, st = sess.outputs()
@@ -448,7 +489,14 @@ def dflash_generate_stream(target: TargetModel, draft: DraftModel, prompt_tokens
         "finish_reason": "stop" if 0 <= stop_index < total_max else "max_tokens",
     }
     if profile:
-        metrics["profile"] = {"steps": len(acceptance_lengths), "verify_mode": verify_mode}
+        # device time of the draft and verify parts (CUDA events around each captured part),
+        # host time spent reading back and committing tokens, and the remainder of the
+        # decode wall time; the device parts of step k overlap the host's work on step k-1
+        prof = sess.profile_times()
+        prof["bookkeeping_time_s"] = bookkeeping
+        profiled = prof["draft_time_s"] + prof["verify_time_s"] + bookkeeping
+        metrics["profile"] = {**prof, "unattributed_decode_time_s": decode_time - profiled,
+                              "steps": len(acceptance_lengths), "verify_mode": verify_mode}
     yield DFlashRuntimeEvent(token_ids=[], output_tokens=list(output_tokens), metrics=metrics, finished=True)
 
 

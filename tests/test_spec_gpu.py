@@ -200,3 +200,24 @@ def test_tiny_batched_session_spec_equals_its_plain_decode():
     singles = [_run(target, None, p, 4, 1)[0] for p in prompts]
     for b, p in enumerate(prompts):
         assert plain[b][:len(p) + 4] == singles[b]
+
+
+def test_profile_buckets_and_same_tokens():
+    """profile=True (runtime.py:61-71, 540-549): the metrics carry the reference's phase
+    keys, timed on the device per captured part, and the tokens equal an unprofiled run."""
+    from dflash_b200.runtime import dflash_generate
+    tcfg, dcfg, tw, dw, target, draft = _tiny()
+    g = torch.Generator().manual_seed(4)
+    prompt = torch.randint(0, tcfg.vocab_size, (40,), generator=g).tolist()
+    plain, _ = dflash_generate(target, draft, prompt, 48, 0.0, set(), None, None)
+    out, m = dflash_generate(target, draft, prompt, 48, 0.0, set(), None, None, profile=True)
+    assert out == plain
+    p = m["profile"]
+    for k in ("draft_time_s", "verify_time_s", "verify_forward_logits_time_s", "verify_prefix_time_s",
+              "verify_rollback_time_s", "bookkeeping_time_s", "unattributed_decode_time_s", "steps"):
+        assert k in p, k
+    assert p["steps"] == len(m["acceptance_lengths"])
+    assert p["draft_time_s"] > 0 and p["verify_forward_logits_time_s"] > 0 and p["verify_prefix_time_s"] > 0
+    parts = p["verify_forward_logits_time_s"] + p["verify_prefix_time_s"] + p["verify_rollback_time_s"]
+    assert abs(p["verify_time_s"] - parts) < 1e-9
+    print({k: (round(v * 1e3, 3) if isinstance(v, float) else v) for k, v in p.items()})

@@ -23,3 +23,52 @@ def test_tp_hybrid_matches_single_gpu(lib, world):
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=900)
     print(r.stdout[-4000:], r.stderr[-4000:])
     assert r.returncode == 0 and "TP_OK" in r.stdout
+
+
+def test_tp_all_sum_wait_gives_up_and_reports(lib):
+    """The all-sum's bounded wait on one GPU: call it as rank 0 of 2 ranks where rank 1's
+    flag is never published (its "peer" buffers are plain local memory that no other
+    kernel writes). The kernel must give up after its wait limit (about 2 s), record
+    device error 401, leave h untouched and return; the context stays usable: after the
+    error is read and cleared, a 1-rank call sums normally."""
+    import ctypes
+    import time
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    dev = "cuda"
+    M, H = 4, 512
+    g = torch.Generator().manual_seed(0)
+    part0 = torch.randn(M, H, generator=g).to(dev)
+    part1 = torch.randn(M, H, generator=g).to(dev)
+    h0 = torch.randn(M, H, generator=g).to(torch.bfloat16).to(dev)
+    h = h0.clone()
+    flags = [torch.zeros(8, dtype=torch.int32, device=dev) for _ in range(2)]
+    epoch = torch.zeros(1, dtype=torch.int32, device=dev)
+    done = torch.zeros(1, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream().cuda_stream
+    code = ctypes.c_int(0)
+    assert lib.dfl_device_error(ctypes.byref(code), 1, stream) == 0
+
+    def call(n_ranks):
+        parts = (ctypes.c_void_p * 2)(part0.data_ptr(), part1.data_ptr())
+        fl = (ctypes.c_void_p * 2)(flags[0].data_ptr(), flags[1].data_ptr())
+        st = lib.dfl_tp_reduce_residual(parts, fl, epoch.data_ptr(), done.data_ptr(), 0, n_ranks, 1, 0,
+                                        h.data_ptr(), H, None, 0, None, M, H, stream)
+        assert st == 0, lib.dfl_last_error()
+
+    t0 = time.perf_counter()
+    call(2)
+    torch.cuda.synchronize()
+    waited = time.perf_counter() - t0
+    assert lib.dfl_device_error(ctypes.byref(code), 1, stream) == 0
+    print(f"wait gave up after {waited:.2f} s with device error {code.value}")
+    assert code.value == 401
+    assert torch.equal(h, h0)
+    assert 0.2 < waited < 30
+    # cleared, and the next (single-rank) call completes and sums
+    assert lib.dfl_device_error(ctypes.byref(code), 0, stream) == 0 and code.value == 0
+    call(1)
+    torch.cuda.synchronize()
+    assert lib.dfl_device_error(ctypes.byref(code), 1, stream) == 0 and code.value == 0
+    ref = (h0.float() + part0.to(torch.bfloat16).float()).to(torch.bfloat16)
+    assert torch.equal(h, ref)

@@ -78,6 +78,17 @@ SIGNATURES: dict[str, tuple] = {
                                  c_void_p, c_int64, c_int, c_void_p]),
     "dfl_verify_accept": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_int, c_void_p, c_int64, c_void_p, c_void_p,
                                   c_int, c_void_p, c_int64, c_int, c_void_p]),
+    "dfl_ctx_create": (c_int, [c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_int, c_int, c_int,
+                               POINTER(c_void_p)]),
+    "dfl_ctx_destroy": (c_int, [c_void_p]),
+    "dfl_ctx_prefill": (c_int, [c_void_p, c_int, c_void_p, c_int, c_int, c_void_p]),
+    "dfl_ctx_set_injection": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64]),
+    "dfl_draft_step": (c_int, [c_void_p, c_void_p]),
+    "dfl_verify_step": (c_int, [c_void_p, c_void_p]),
+    "dfl_rollback": (c_int, [c_void_p, c_void_p]),
+    "dfl_ctx_buffers": (c_int, [c_void_p, POINTER(c_void_p), POINTER(c_void_p), POINTER(c_int64), POINTER(c_void_p),
+                                POINTER(c_int64)]),
+    "dfl_ctx_read": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p]),
     "dfl_gdr_recurrence": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p,
                                    c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p,
                                    c_int, c_void_p]),

@@ -292,6 +292,74 @@ int dfl_gdr_recurrence(const void* q, const void* k, const void* v, const float*
                        float* snapshots, void* o, int B, int T, int Hk, int Hv, int Dk, int Dv, const int32_t* tokens,
                        int tokens_stride, void* stream);
 
+/* ---- step-level driver (the decode loop body from C) ------------------------
+ * Replaces the loop body of dflash_generate_stream (runtime.py:406-518) for hosts
+ * that are not Python: dfl_draft_step = block [last, mask x (bs-1)], draft forward over
+ * the new taps and the block, proposals (runtime.py:407-423, draft.py:109-223);
+ * dfl_verify_step = target verify forward with taps, greedy argmax, longest-prefix
+ * accept, bonus, commit and stop / length checks (runtime.py:117-163, 488-507,
+ * adapters.py:611-631), writing accepted / bonus / finished into the device state;
+ * dfl_rollback = the cache rollback (rewind_kv_caches, adapters.py:697-700; for the dense
+ * family the accept has already moved the cache length, so it only validates).
+ * Dense Qwen3 family. The context borrows the weights (device pointers, GEMM weights
+ * packed by dfl_pack_weight_bf16; the caller keeps them alive) and allocates every
+ * session buffer in dfl_ctx_create; the step calls allocate nothing and do not sync
+ * the host. Unless DFL_CTX_NO_GRAPH is set, the first call of each half records it as
+ * a CUDA graph on a private stream (later calls launch the graph on `stream`); call
+ * dfl_ctx_set_injection before the first step or the draft half is recorded again. */
+typedef struct dfl_layer_weights {
+  const void* in_norm;   /* [H] bf16 input_layernorm */
+  const void* post_norm; /* [H] bf16 post_attention_layernorm */
+  const void* w_qkv;     /* packed [(Hq + 2 Hkv) hd, H]: q_proj, k_proj, v_proj rows */
+  const void* w_o;       /* packed [H, Hq hd] */
+  const void* w_gu;      /* packed [2F, H], gate / up interleaved per 64 rows (32 | 32) */
+  const void* w_down;    /* packed [H, F] */
+  const void* q_norm;    /* [hd] bf16 */
+  const void* k_norm;    /* [hd] bf16 */
+} dfl_layer_weights;
+
+typedef struct dfl_qwen3_desc {
+  int hidden, n_layers, n_heads, n_kv_heads, head_dim, ffn, vocab, rope_dim;
+  float eps, rope_theta;
+  const void* embed;      /* [V, H] bf16 row-major (embedding gather) */
+  const void* lm_head;    /* packed [V, H] (the embedding again when tied) */
+  const void* final_norm; /* [H] bf16 */
+  const dfl_layer_weights* layers; /* n_layers entries (copied at create) */
+} dfl_qwen3_desc;
+
+typedef struct dfl_draft_desc {
+  int hidden, n_layers, n_heads, n_kv_heads, head_dim, ffn, block_size, mask_token_id, n_taps, causal;
+  float eps, rope_theta;
+  const int32_t* target_layer_ids; /* host, n_taps ascending (copied at create) */
+  const void* fc;                  /* packed [H, n_taps H] */
+  const void* hidden_norm;         /* [H] bf16 */
+  const void* final_norm;          /* [H] bf16 */
+  const void* w_ctx_kv;            /* packed [n_layers 2 Hkv hd, H]: every layer's k_proj then v_proj rows */
+  const dfl_layer_weights* layers; /* n_layers entries (copied at create) */
+} dfl_draft_desc;
+
+typedef struct dfl_ctx dfl_ctx;
+#define DFL_CTX_NO_GRAPH 1
+
+int dfl_ctx_create(const dfl_qwen3_desc* target, const dfl_draft_desc* draft, int batch, int max_total,
+                   int block_size, const int32_t* stop_ids, int n_stop, int max_steps, int flags, dfl_ctx** out);
+int dfl_ctx_destroy(dfl_ctx* ctx);
+/* Prefill of sequence `seq` from host tokens (chunks of 128 rows, taps into the draft
+ * cache) and its first greedy token (runtime.py:383-404). A set-up call: it synchronises. */
+int dfl_ctx_prefill(dfl_ctx* ctx, int seq, const int32_t* tokens, int n_tokens, int max_new_tokens, void* stream);
+/* Oracle-injected drafts (benchmarks): block[1 + i] = trace[b][start + 1 + i] for
+ * i < lengths[b][step], else noise[b][step * bs + i] (device arrays; NULL trace = off). */
+int dfl_ctx_set_injection(dfl_ctx* ctx, const int32_t* trace, int64_t trace_stride, const int32_t* lengths,
+                          int64_t lengths_stride, const int32_t* noise, int64_t noise_stride);
+int dfl_draft_step(dfl_ctx* ctx, void* stream);
+int dfl_verify_step(dfl_ctx* ctx, void* stream);
+int dfl_rollback(dfl_ctx* ctx, void* stream);
+/* Device pointers of the state [B], output tokens [B][out_stride] and acceptance log
+ * [B][log_stride] (for device-side consumers), and a synchronous host copy of them. */
+int dfl_ctx_buffers(dfl_ctx* ctx, dfl_seq_state** state, int32_t** out_tokens, int64_t* out_stride,
+                    int32_t** accept_log, int64_t* log_stride);
+int dfl_ctx_read(dfl_ctx* ctx, dfl_seq_state* state, int32_t* out_tokens, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -82,3 +82,16 @@ def test_fused_attention_rejects_sequences_that_span_tiles(lib):
         _lib.call("dfl_attention_qkv", dummy, (32 + 16) * 128, dummy, dummy, dummy, 1e-6, dummy, dummy, 0, 0,
                   dummy, dummy, 3, 48, 32, 8, 1.0, 64, 0, dummy, 4096, None, 0, None)
     assert e.value.status == 2 and "16-row tile" in str(e.value)
+
+
+def test_step_abi_rejects_bad_arguments_without_a_device():
+    """The step-level driver's argument checks run before any CUDA call."""
+    import ctypes
+    from dflash_b200 import _lib
+    lib = _lib.load()
+    h = ctypes.c_void_p()
+    assert lib.dfl_ctx_create(None, None, 1, 64, 1, None, 0, 0, 0, ctypes.byref(h)) == 1
+    assert b"invalid" in lib.dfl_last_error()
+    for fn in ("dfl_draft_step", "dfl_verify_step", "dfl_rollback"):
+        assert getattr(lib, fn)(None, None) == 1
+    assert lib.dfl_ctx_destroy(None) == 0

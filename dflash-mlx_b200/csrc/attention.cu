@@ -22,7 +22,13 @@
 // over many SMs, large ones cut the partial-result traffic of batched verify.
 // When one chunk covers every row's keys the chunk kernel normalises and writes
 // the output itself (the merge of a single chunk is the identity) and no merge
-// kernel runs. K/V stream through a 3-stage cp.async ring (2 stages at head_dim 256).
+// kernel runs. When the chunks of a row number at most 16, the CTAs of one (tile, kv
+// head) are launched as one thread-block cluster (one CTA per chunk) and merge in
+// the chunk kernel itself: each CTA leaves its unnormalised partial in its shared
+// memory, and after a cluster barrier every CTA reads a slice of (head, row) items
+// from all of them over distributed shared memory, in chunk order -- no partials in
+// HBM and no merge launch. K/V stream through a 3-stage cp.async ring (2 stages at
+// head_dim 256).
 #include "common.cuh"
 #include "tma_util.cuh"
 
@@ -103,7 +109,27 @@ __device__ __forceinline__ int row_limit(const AttnArgs& a, int m) {
 // K/V ring depth: 3 stages for long chunks at head_dim <= 128; 2 for short chunks
 // (a 128-key chunk is two blocks: a deeper ring only costs shared memory that the
 // next kernel's prologue could use) and for head_dim 256 (shared memory)
-template <int HD, int ST>
+__device__ __forceinline__ uint32_t att_cluster_map(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];\n" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ float2 ld_dsmem_f32x2(uint32_t addr) {
+  float2 v;
+  asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];\n" : "=f"(v.x), "=f"(v.y) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void att_cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+
+// CM: cluster merge (grid.x == cluster size == the chunk count; see the file comment)
+template <int HD, int ST, bool CM>
 __global__ void __launch_bounds__(256) attn_chunk_kernel(AttnArgs a) {
   grid_dependency_launch_dependents();
   grid_dependency_wait();
@@ -157,8 +183,9 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(AttnArgs a) {
 #pragma unroll
   for (int r = 0; r < 16; ++r) lim_max = max(lim_max, s_lim[r]);
   const int k_begin = chunk * a.key_chunk;
-  if (k_begin >= lim_max) return;
-  const int k_end = min(k_begin + a.key_chunk, lim_max);
+  // a cluster-merge CTA past every row's keys still takes part in the merge (empty partial)
+  if (!CM && k_begin >= lim_max) return;
+  const int k_end = max(k_begin, min(k_begin + a.key_chunk, lim_max));
 
   const __nv_bfloat16* Kb = a.k_cache + s_seq * a.seq_stride + kvh * a.head_stride;
   const __nv_bfloat16* Vb = a.v_cache + s_seq * a.seq_stride + kvh * a.head_stride;
@@ -375,6 +402,53 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(AttnArgs a) {
   lrow[1] += __shfl_xor_sync(0xffffffffu, lrow[1], 2);
 
   const int h = kvh * a.G + warp;
+  if constexpr (CM) {
+    // this CTA's partial (o unnormalised, running max, denominator) into its own shared
+    // memory (the K/V ring, idle now), then a cluster-wide merge in chunk order
+    __syncthreads();
+    float* po = reinterpret_cast<float*>(sK);                  // [G][16][HD]
+    float2* pml = reinterpret_cast<float2*>(po + a.G * 16 * HD);  // [G][16]
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int r = g + half * 8;
+      float* dst = po + (warp * 16 + r) * HD;
+#pragma unroll
+      for (int j = 0; j < HD / 8; ++j)
+        *reinterpret_cast<float2*>(dst + j * 8 + 2 * t) = make_float2(o[j][2 * half], o[j][2 * half + 1]);
+      if (t == 0) pml[warp * 16 + r] = make_float2(mrow[half], lrow[half]);
+    }
+    att_cluster_sync();
+    const int C = gridDim.x;
+    const uint32_t po_s = smem_u32(po), pml_s = smem_u32(pml);
+    for (int item = chunk; item < a.G * 16; item += C) {
+      const int hl = item >> 4, r = item & 15;
+      const int m = m0 + r;
+      if (m >= a.M || s_lim[r] <= 0) continue;
+      const int nch = min((s_lim[r] + a.key_chunk - 1) / a.key_chunk, C);
+      float mmax = -INFINITY;
+      for (int c = 0; c < nch; ++c) mmax = fmaxf(mmax, ld_dsmem_f32x2(att_cluster_map(pml_s + item * 8, c)).x);
+      const float mu = mmax == -INFINITY ? 0.f : mmax;
+      const int hq = kvh * a.G + hl;
+      __nv_bfloat16* dst = a.out + (long long)m * a.ldo + (long long)hq * HD;
+      const __nv_bfloat16* gr = a.gate ? a.gate + (long long)m * a.ldg + (long long)hq * a.gate_hs : nullptr;
+      for (int d = threadIdx.x; d < HD; d += nthr) {
+        float acc = 0.f, den = 0.f;
+        for (int c = 0; c < nch; ++c) {
+          const float2 ml = ld_dsmem_f32x2(att_cluster_map(pml_s + item * 8, c));
+          const float w = exp2f(ml.x - mu);
+          den += w * ml.y;
+          acc += w * ld_dsmem_f32(att_cluster_map(po_s + (item * HD + d) * 4, c));
+        }
+        const float inv = den > 0.f ? 1.f / den : 0.f;
+        if (gr)
+          dst[d] = f2bf(round_bf16(acc * inv) * round_bf16(1.f / (1.f + __expf(-bf2f(gr[d])))));
+        else
+          dst[d] = f2bf(acc * inv);
+      }
+    }
+    att_cluster_sync();  // no CTA leaves while a peer may still read its partial
+    return;
+  }
   if (a.direct) {
     // single chunk: out = o / l (the merge of one chunk is the identity)
 #pragma unroll
@@ -488,6 +562,44 @@ __global__ void attn_combine_kernel(AttnArgs a) {
   }
 }
 
+// Whether the chunk kernel can merge its chunks as one cluster per (tile, kv head): the
+// chunk count fits a cluster (16 with the non-portable opt-in) and the device can place
+// such a cluster. Depends on the chunk count and head shape only, so every launch of a
+// session makes the same choice.
+template <int HD, int ST>
+static bool cluster_merge_ok(int n_chunks, int G, size_t smem) {
+  if (n_chunks < 2 || n_chunks > 16) return false;
+  // the partials ([G][16][HD] fp32 + [G][16] (max, sum)) live in the K/V ring
+  if ((size_t)G * 16 * HD * 4 + (size_t)G * 16 * 8 > (size_t)2 * ST * ATT_KB * HD * 2) return false;
+  static int cache[64][17][9] = {};  // 0 unknown, 1 yes, 2 no
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return false;
+  int& c = cache[dev][n_chunks][G];
+  if (c == 0) {
+    c = 2;
+    if (n_chunks <= 8 ||
+        cudaFuncSetAttribute(attn_chunk_kernel<HD, ST, true>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
+            cudaSuccess) {
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = n_chunks;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(n_chunks, 1, 1);
+      cfg.blockDim = dim3(32 * G);
+      cfg.dynamicSmemBytes = smem;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, attn_chunk_kernel<HD, ST, true>, &cfg) == cudaSuccess && n > 0) c = 1;
+    }
+    cudaGetLastError();
+  }
+  return c == 1;
+}
+
 template <int HD, int ST>
 static int launch_attn(AttnArgs a, int n_tiles, cudaStream_t st) {
   const size_t smem = (size_t)(a.G * 16 * HD + 2 * ST * ATT_KB * HD) * 2;
@@ -500,9 +612,11 @@ static int launch_attn(AttnArgs a, int n_tiles, cudaStream_t st) {
   if (dev >= 0 && dev < 64 && !opted[dev]) {
     cudaFuncAttributes fa;
     int optin = 0;
-    if (cudaFuncGetAttributes(&fa, attn_chunk_kernel<HD, ST>) != cudaSuccess ||
+    if (cudaFuncGetAttributes(&fa, attn_chunk_kernel<HD, ST, false>) != cudaSuccess ||
         cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
-        cudaFuncSetAttribute(attn_chunk_kernel<HD, ST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaFuncSetAttribute(attn_chunk_kernel<HD, ST, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             optin - (int)fa.sharedSizeBytes) != cudaSuccess ||
+        cudaFuncSetAttribute(attn_chunk_kernel<HD, ST, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              optin - (int)fa.sharedSizeBytes) != cudaSuccess) {
       set_error("dfl_attention: cannot opt in to the per-block shared memory");
       return DFL_ERR_UNSUPPORTED;
@@ -513,7 +627,7 @@ static int launch_attn(AttnArgs a, int n_tiles, cudaStream_t st) {
     set_error("dfl_attention: %zu bytes of shared memory needed", smem);
     return DFL_ERR_UNSUPPORTED;
   }
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t cfg = {};
@@ -523,7 +637,20 @@ static int launch_attn(AttnArgs a, int n_tiles, cudaStream_t st) {
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, attn_chunk_kernel<HD, ST>, a);
+  if (!a.direct && cluster_merge_ok<HD, ST>(a.n_chunks, a.G, smem)) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = a.n_chunks;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, attn_chunk_kernel<HD, ST, true>, a);
+    if (e != cudaSuccess) {
+      set_error("dfl_attention: cluster chunk kernel launch failed: %s", cudaGetErrorString(e));
+      return DFL_ERR_CUDA;
+    }
+    return DFL_OK;
+  }
+  cudaError_t e = cudaLaunchKernelEx(&cfg, attn_chunk_kernel<HD, ST, false>, a);
   if (e != cudaSuccess) {
     set_error("dfl_attention: chunk kernel launch failed: %s", cudaGetErrorString(e));
     return DFL_ERR_CUDA;

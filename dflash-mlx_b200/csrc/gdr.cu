@@ -24,18 +24,13 @@
 // 16-token verify block and one advanced alone agree bit for bit.
 #include "common.cuh"
 
+#include <cstdlib>
+
 namespace dfl {
 
-#ifndef DFL_GDR_LPR
-#define DFL_GDR_LPR 4
-#endif
-constexpr int GDR_LPR = DFL_GDR_LPR;          // lanes per value row
-#ifndef DFL_GDR_WARPS
-#define DFL_GDR_WARPS 2
-#endif
-constexpr int GDR_WARPS = DFL_GDR_WARPS;      // warps per CTA
-constexpr int GDR_ROWS = GDR_WARPS * 32 / GDR_LPR;  // value rows per CTA (16)
 constexpr int GDR_TT = 16;                    // tokens per staged tile
+constexpr int GDR_ROWS = 16;                  // value rows per CTA (every lane layout below)
+constexpr int GDR_DEFAULT_LPR = 4;
 
 struct GdrArgs {
   const __nv_bfloat16* q;
@@ -59,8 +54,11 @@ __device__ __forceinline__ float4 bf16x4_to_float4(uint2 r) {
                      __uint_as_float(r.y & 0xffff0000u));
 }
 
-template <int DK>
-__global__ void __launch_bounds__(32 * GDR_WARPS) gdr_kernel(GdrArgs a) {
+// GDR_LPR lanes per value row; a CTA holds GDR_ROWS rows, so GDR_ROWS * GDR_LPR / 32 warps
+template <int DK, int GDR_LPR>
+__global__ void __launch_bounds__(GDR_ROWS * GDR_LPR) gdr_kernel(GdrArgs a) {
+  constexpr int GDR_WARPS = GDR_ROWS * GDR_LPR / 32;
+  (void)GDR_WARPS;
   grid_dependency_launch_dependents();
   grid_dependency_wait();
   constexpr int NCH = DK / (4 * GDR_LPR);  // float4 chunks per lane
@@ -184,6 +182,18 @@ __global__ void __launch_bounds__(32 * GDR_WARPS) gdr_kernel(GdrArgs a) {
 
 using namespace dfl;
 
+// Lanes per value row (4, 8 or 16): more lanes put more warps in flight on the short
+// dependent chain of a verify block. A process-wide constant (DFLASH_B200_GDR_LPR sets it
+// for tuning), so every call of a session uses the same per-token arithmetic.
+static int gdr_lanes_per_row() {
+  static int lpr = [] {
+    const char* e = getenv("DFLASH_B200_GDR_LPR");
+    const int v = e ? atoi(e) : GDR_DEFAULT_LPR;
+    return (v == 4 || v == 8 || v == 16) ? v : GDR_DEFAULT_LPR;
+  }();
+  return lpr;
+}
+
 extern "C" int dfl_gdr_recurrence(const void* q, const void* k, const void* v, const float* g, const float* beta,
                                   const float* state_in, int64_t state_in_bstride, const int32_t* state_slot,
                                   float* state_out, float* snapshots, void* o, int B, int T, int Hk, int Hv, int Dk,
@@ -229,12 +239,21 @@ extern "C" int dfl_gdr_recurrence(const void* q, const void* k, const void* v, c
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t cfg = {};
+  const int lpr = gdr_lanes_per_row();
   cfg.gridDim = dim3(Dv / GDR_ROWS, Hv, B);
-  cfg.blockDim = dim3(32 * GDR_WARPS);
+  cfg.blockDim = dim3(GDR_ROWS * lpr);
   cfg.stream = as_stream(stream);
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = Dk == 128 ? cudaLaunchKernelEx(&cfg, gdr_kernel<128>, a) : cudaLaunchKernelEx(&cfg, gdr_kernel<64>, a);
+  cudaError_t e;
+  if (Dk == 128)
+    e = lpr == 16 ? cudaLaunchKernelEx(&cfg, gdr_kernel<128, 16>, a)
+        : lpr == 8 ? cudaLaunchKernelEx(&cfg, gdr_kernel<128, 8>, a)
+                   : cudaLaunchKernelEx(&cfg, gdr_kernel<128, 4>, a);
+  else
+    e = lpr == 16 ? cudaLaunchKernelEx(&cfg, gdr_kernel<64, 16>, a)
+        : lpr == 8 ? cudaLaunchKernelEx(&cfg, gdr_kernel<64, 8>, a)
+                   : cudaLaunchKernelEx(&cfg, gdr_kernel<64, 4>, a);
   if (e != cudaSuccess) {
     set_error("dfl_gdr_recurrence: launch failed: %s", cudaGetErrorString(e));
     return DFL_ERR_CUDA;

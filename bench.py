@@ -228,13 +228,13 @@ def cpu_sample(tcfg, dcfg, tw, dw, sess, trace, lengths, noise, n_steps: int) ->
     # oracle caches from the GPU prefill (positions [0, P))
     tcache = ot.make_cache(P + 16 * (n_steps + 2))
     for l, c in enumerate(tcache):
-        c.k[:, :P] = sess.tcache.k[l, 0, :, :P].float().cpu()
-        c.v[:, :P] = sess.tcache.v[l, 0, :, :P].float().cpu()
+        k, v = sess.tcache.gather(l, 0, P)
+        c.k[:, :P], c.v[:, :P] = k.float().cpu(), v.float().cpu()
         c.offset = P
     dcache = od.make_cache(P + 16 * (n_steps + 2))
     for l, c in enumerate(dcache):
-        c.k[:, :P] = sess.dcache.k[l, 0, :, :P].float().cpu()
-        c.v[:, :P] = sess.dcache.v[l, 0, :, :P].float().cpu()
+        k, v = sess.dcache.gather(l, 0, P)
+        c.k[:, :P], c.v[:, :P] = k.float().cpu(), v.float().cpu()
         c.offset = P
     bs = dcfg.block_size
     hidden = torch.zeros((0, len(dcfg.target_layer_ids) * tcfg.hidden_size))

@@ -69,7 +69,20 @@ struct AttnArgs {
   float eps;
   __nv_bfloat16* k_new;   // the caches, written at the new rows' positions
   __nv_bfloat16* v_new;
+  // paged caches: [page][Hkv][page_size][hd] with seq_stride = the page stride; position p
+  // of sequence s is row p % page_size of page page_table[s * pt_stride + p / page_size]
+  const int* page_table;
+  long long pt_stride;
+  int page_shift;
 };
+
+// element offset, from the cache base plus the kv head, of the 64-key block starting at
+// key kb (a block never straddles a page: page sizes are multiples of 64)
+__device__ __forceinline__ long long kv_block_offset(const AttnArgs& a, int seq, int kb, int hd) {
+  if (!a.page_table) return (long long)seq * a.seq_stride + (long long)kb * hd;
+  const long long page = a.page_table[seq * a.pt_stride + (kb >> a.page_shift)];
+  return page * a.seq_stride + (long long)(kb & ((1 << a.page_shift) - 1)) * hd;
+}
 
 // One 128-wide head row held 4 values per lane (element lane + 32 j): RMSNorm with weight
 // nw, then the rotary embedding with the row's (cos, sin) table cs[64] -- the arithmetic of
@@ -187,8 +200,8 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(AttnArgs a) {
   if (!CM && k_begin >= lim_max) return;
   const int k_end = max(k_begin, min(k_begin + a.key_chunk, lim_max));
 
-  const __nv_bfloat16* Kb = a.k_cache + s_seq * a.seq_stride + kvh * a.head_stride;
-  const __nv_bfloat16* Vb = a.v_cache + s_seq * a.seq_stride + kvh * a.head_stride;
+  const __nv_bfloat16* Kb = a.k_cache + kvh * a.head_stride;
+  const __nv_bfloat16* Vb = a.v_cache + kvh * a.head_stride;
 
   if constexpr (HD == 128) {
     if (a.qkv) {
@@ -224,7 +237,8 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(AttnArgs a) {
           vv[j] = vs[lane + 32 * j];
         }
         norm_rope_row128(x, a.k_norm, s_cs[r], a.eps, lane);
-        const long long off = s_seq * a.seq_stride + kvh * a.head_stride + (long long)p * 128;
+        const long long off = kv_block_offset(a, s_seq, p & ~(ATT_KB - 1), 128) + kvh * a.head_stride +
+                              (long long)(p & (ATT_KB - 1)) * 128;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           a.k_new[off + lane + 32 * j] = f2bf(x[j]);
@@ -271,11 +285,12 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(AttnArgs a) {
     cp_async16(smem_u32(sQ + hg * 16 * HD + att_swz<HD>(r, c)), src, ok ? 16 : 0);
   }
   auto load_kv = [&](int buf, int kb) {
+    const long long boff = kv_block_offset(a, s_seq, kb, HD);
     for (int idx = threadIdx.x; idx < ATT_KB * NC; idx += nthr) {
       const int c = idx % NC, r = idx / NC;
       const int key = kb + r;
       const bool ok = key < k_end;
-      const long long off = (long long)(ok ? key : 0) * HD + c * 8;
+      const long long off = boff + (long long)(ok ? r : 0) * HD + c * 8;
       cp_async16(smem_u32(sK + buf * ATT_KB * HD + att_swz<HD>(r, c)), Kb + off, ok ? 16 : 0);
       cp_async16(smem_u32(sV + buf * ATT_KB * HD + att_swz<HD>(r, c)), Vb + off, ok ? 16 : 0);
     }
@@ -700,7 +715,8 @@ static int attention_impl(const void* q, const void* k_cache, const void* v_cach
                           int64_t head_stride, const int32_t* pos, const int32_t* row_seq, const int32_t* kv_len,
                           int seq_rows, int M, int Hq, int Hkv, int hd, int causal, float scale, int max_kv,
                           int key_chunk, void* out, int64_t ldo, const void* gate, int64_t ldg, int gate_head_stride,
-                          void* workspace, size_t workspace_bytes, void* stream, const FusedQkv* fq) {
+                          void* workspace, size_t workspace_bytes, void* stream, const FusedQkv* fq,
+                          const int32_t* page_table = nullptr, int64_t pt_stride = 0, int page_size = 0) {
   if (M == 0) return DFL_OK;
   if ((!q && !fq) || !k_cache || !v_cache || !pos || !out || (!causal && !kv_len) || M < 0 || Hkv <= 0 ||
       Hq % Hkv) {
@@ -768,6 +784,16 @@ static int attention_impl(const void* q, const void* k_cache, const void* v_cach
   a.inv_freq = nullptr;
   a.eps = 0.f;
   a.k_new = a.v_new = nullptr;
+  a.page_table = page_table;
+  a.pt_stride = pt_stride;
+  a.page_shift = 0;
+  if (page_table) {
+    if (page_size < ATT_KB || (page_size & (page_size - 1)) || pt_stride <= 0) {
+      set_error("dfl_attention_paged: page_size must be a power of two >= %d (got %d)", ATT_KB, page_size);
+      return DFL_ERR_INVALID;
+    }
+    while ((1 << a.page_shift) < page_size) ++a.page_shift;
+  }
   if (fq) {
     a.qkv = static_cast<const __nv_bfloat16*>(fq->qkv);
     a.ldqkv = fq->ldqkv;
@@ -823,4 +849,19 @@ extern "C" int dfl_attention_qkv(const void* qkv, int64_t ldqkv, const void* q_n
   return attention_impl(nullptr, k_cache, v_cache, seq_stride, head_stride, pos, row_seq, nullptr, seq_rows, M, Hq,
                         Hkv, 128, 1, scale, max_kv, key_chunk, out, ldo, nullptr, 0, 0, workspace, workspace_bytes,
                         stream, &f);
+}
+
+extern "C" int dfl_attention_paged(const void* q, const void* k_pages, const void* v_pages, int64_t page_stride,
+                                   int64_t head_stride, const int32_t* page_table, int64_t pt_stride, int page_size,
+                                   const int32_t* pos, const int32_t* row_seq, const int32_t* kv_len, int seq_rows,
+                                   int M, int Hq, int Hkv, int hd, int causal, float scale, int max_kv, int key_chunk,
+                                   void* out, int64_t ldo, const void* gate, int64_t ldg, int gate_head_stride,
+                                   void* workspace, size_t workspace_bytes, void* stream) {
+  if (!page_table) {
+    set_error("dfl_attention_paged: null page table");
+    return DFL_ERR_INVALID;
+  }
+  return attention_impl(q, k_pages, v_pages, page_stride, head_stride, pos, row_seq, kv_len, seq_rows, M, Hq, Hkv, hd,
+                        causal, scale, max_kv, key_chunk, out, ldo, gate, ldg, gate_head_stride, workspace,
+                        workspace_bytes, stream, nullptr, page_table, pt_stride, page_size);
 }

@@ -89,7 +89,10 @@ __global__ void embed_kernel(const int* __restrict__ tok, const __nv_bfloat16* _
 //
 // qkv row layout: [q heads (Hq x q_stride, first hd of each is q) | k heads (Hkv x hd) | v heads (Hkv x hd)].
 // K/V cache layout per layer: [seq][Hkv][cap][hd] bf16; the token at position p
-// lives in slot p. pos[r] < 0 marks a row that is skipped entirely.
+// lives in slot p. Paged form: [page][Hkv][page_size][hd] and a page table
+// [seq][pt_stride] of page indices; position p of sequence s lives in page
+// table[s][p / page_size], row p % page_size. pos[r] < 0 marks a row that is
+// skipped entirely.
 // q_out: [M][Hq][hd] bf16.
 // -------------------------------------------------------------------------
 struct QkvArgs {
@@ -108,7 +111,18 @@ struct QkvArgs {
   int M, Hq, Hkv, hd, rot_dim;
   float eps;
   int do_q;  // 0: skip q heads (context rows of the draft)
+  const int* page_table;  // nullable: contiguous [seq][Hkv][cap][hd] caches
+  long long pt_stride;
+  int page_shift;         // log2(page_size)
 };
+
+// element offset of (sequence, kv head, position) in a contiguous or paged cache
+__device__ __forceinline__ long long kv_offset(const int* pt, long long pt_stride, int shift, long long seq_stride,
+                                               long long head_stride, int seq, int h, int p, int hd) {
+  if (!pt) return seq * seq_stride + h * head_stride + (long long)p * hd;
+  const long long page = pt[seq * pt_stride + (p >> shift)];
+  return page * seq_stride + h * head_stride + (long long)(p & ((1 << shift) - 1)) * hd;
+}
 
 __global__ void qkv_rope_append_kernel(QkvArgs a) {
   grid_dependency_launch_dependents();
@@ -136,11 +150,11 @@ __global__ void qkv_rope_append_kernel(QkvArgs a) {
     const int kh = head - a.Hq;
     src = qkv_row + (long long)a.Hq * a.q_stride + (long long)kh * a.hd;
     nw = a.k_norm;
-    dst = a.k_cache + seq * a.seq_stride + kh * a.head_stride + (long long)p * a.hd;
+    dst = a.k_cache + kv_offset(a.page_table, a.pt_stride, a.page_shift, a.seq_stride, a.head_stride, seq, kh, p, a.hd);
   } else {
     const int vh = head - a.Hq - a.Hkv;
     src = qkv_row + (long long)a.Hq * a.q_stride + (long long)(a.Hkv + vh) * a.hd;
-    dst = a.v_cache + seq * a.seq_stride + vh * a.head_stride + (long long)p * a.hd;
+    dst = a.v_cache + kv_offset(a.page_table, a.pt_stride, a.page_shift, a.seq_stride, a.head_stride, seq, vh, p, a.hd);
     for (int i = lane; i < a.hd; i += 32) dst[i] = src[i];
     return;
   }
@@ -227,11 +241,11 @@ extern "C" int dfl_embed_bf16(const int32_t* tokens, const void* table, void* y,
   return DFL_OK;
 }
 
-extern "C" int dfl_qkv_rope_append(const void* qkv, int64_t ldqkv, int q_stride, const int32_t* pos,
+static int qkv_rope_append_impl(const void* qkv, int64_t ldqkv, int q_stride, const int32_t* pos,
                                    const int32_t* row_seq, const void* q_norm, const void* k_norm,
                                    const float* inv_freq, void* q_out, void* k_cache, void* v_cache,
                                    int64_t seq_stride, int64_t head_stride, int M, int Hq, int Hkv, int hd,
-                                   int rot_dim, float eps, int do_q, void* stream) {
+                                   int rot_dim, float eps, int do_q, void* stream, const int32_t* page_table, int64_t pt_stride, int page_size) {
   if (M == 0) return DFL_OK;
   if (!qkv || !pos || !q_norm || !k_norm || !inv_freq || !k_cache || !v_cache || (do_q && !q_out)) {
     set_error("dfl_qkv_rope_append: null pointer");
@@ -262,6 +276,16 @@ extern "C" int dfl_qkv_rope_append(const void* qkv, int64_t ldqkv, int q_stride,
   a.rot_dim = rot_dim;
   a.eps = eps;
   a.do_q = do_q;
+  a.page_table = page_table;
+  a.pt_stride = pt_stride;
+  a.page_shift = 0;
+  if (page_table) {
+    if (page_size < 64 || (page_size & (page_size - 1)) || pt_stride <= 0) {
+      set_error("dfl_qkv_rope_append_paged: page_size must be a power of two >= 64 (got %d)", page_size);
+      return DFL_ERR_INVALID;
+    }
+    while ((1 << a.page_shift) < page_size) ++a.page_shift;
+  }
   const long long items = (long long)M * (Hq + 2 * Hkv);
   const int warps = 8;
   cudaLaunchConfig_t cfg = {};
@@ -280,4 +304,28 @@ extern "C" int dfl_qkv_rope_append(const void* qkv, int64_t ldqkv, int q_stride,
     return DFL_ERR_CUDA;
   }
   return DFL_OK;
+}
+
+extern "C" int dfl_qkv_rope_append(const void* qkv, int64_t ldqkv, int q_stride, const int32_t* pos,
+                                   const int32_t* row_seq, const void* q_norm, const void* k_norm,
+                                   const float* inv_freq, void* q_out, void* k_cache, void* v_cache,
+                                   int64_t seq_stride, int64_t head_stride, int M, int Hq, int Hkv, int hd,
+                                   int rot_dim, float eps, int do_q, void* stream) {
+  return qkv_rope_append_impl(qkv, ldqkv, q_stride, pos, row_seq, q_norm, k_norm, inv_freq, q_out, k_cache, v_cache,
+                              seq_stride, head_stride, M, Hq, Hkv, hd, rot_dim, eps, do_q, stream, nullptr, 0, 0);
+}
+
+extern "C" int dfl_qkv_rope_append_paged(const void* qkv, int64_t ldqkv, int q_stride, const int32_t* pos,
+                                         const int32_t* row_seq, const void* q_norm, const void* k_norm,
+                                         const float* inv_freq, void* q_out, void* k_pages, void* v_pages,
+                                         int64_t page_stride, int64_t head_stride, const int32_t* page_table,
+                                         int64_t pt_stride, int page_size, int M, int Hq, int Hkv, int hd, int rot_dim,
+                                         float eps, int do_q, void* stream) {
+  if (!page_table) {
+    set_error("dfl_qkv_rope_append_paged: null page table");
+    return DFL_ERR_INVALID;
+  }
+  return qkv_rope_append_impl(qkv, ldqkv, q_stride, pos, row_seq, q_norm, k_norm, inv_freq, q_out, k_pages, v_pages,
+                              page_stride, head_stride, M, Hq, Hkv, hd, rot_dim, eps, do_q, stream, page_table,
+                              pt_stride, page_size);
 }

@@ -60,6 +60,13 @@ SIGNATURES: dict[str, tuple] = {
     "dfl_attention_qkv": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p,
                                   c_int64, c_int64, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_float, c_int,
                                   c_int, c_void_p, c_int64, c_void_p, c_size_t, c_void_p]),
+    "dfl_qkv_rope_append_paged": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                          c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int,
+                                          c_int, c_int, c_int, c_int, c_int, c_float, c_int, c_void_p]),
+    "dfl_attention_paged": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int,
+                                    c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_float,
+                                    c_int, c_int, c_void_p, c_int64, c_void_p, c_int64, c_int, c_void_p, c_size_t,
+                                    c_void_p]),
     "dfl_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int,
                               c_int, c_int, c_int, c_int, c_int, c_float, c_int, c_int, c_void_p, c_int64, c_void_p,
                               c_int64,

@@ -31,23 +31,78 @@ from .weights import pack_gate_up, rope_inv_freq
 
 @dataclass
 class KVCache:
-    """K/V slots [L, B, Hkv, cap, hd] bf16 and the host-side view of each sequence's length."""
+    """K/V of every layer, either contiguous slots [L, B, Hkv, cap, hd] bf16 (the token at
+    position p of sequence b in slot p) or, with a page table, page pools
+    [L, n_pages, Hkv, page_size, hd] and ``page_table`` [B, pages] int32 (position p of
+    sequence b in page page_table[b, p // page_size], row p % page_size), so that each
+    sequence holds pages for its own length only."""
 
     k: torch.Tensor
     v: torch.Tensor
+    page_table: torch.Tensor | None = None
+    page_size: int = 0
+    cap_tokens: int = 0
 
     @property
     def cap(self) -> int:
-        return self.k.shape[3]
+        return self.cap_tokens if self.page_table is not None else self.k.shape[3]
 
     def layer(self, l: int) -> tuple[torch.Tensor, torch.Tensor]:
         return self.k[l], self.v[l]
+
+    @property
+    def paging(self) -> dict:
+        """Keyword arguments of ops.qkv_rope_append / ops.attention for this cache."""
+        if self.page_table is None:
+            return {}
+        return {"page_table": self.page_table, "page_size": self.page_size}
+
+    def gather(self, l: int, b: int, n: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """Keys and values of positions [0, n) of sequence b in layer l, as [Hkv, n, hd]."""
+        if self.page_table is None:
+            return self.k[l, b, :, :n], self.v[l, b, :, :n]
+        ps = self.page_size
+        pages = self.page_table[b, :(n + ps - 1) // ps].long()
+        k = self.k[l, pages].permute(1, 0, 2, 3).reshape(self.k.shape[2], -1, self.k.shape[4])[:, :n]
+        v = self.v[l, pages].permute(1, 0, 2, 3).reshape(self.v.shape[2], -1, self.v.shape[4])[:, :n]
+        return k, v
 
 
 def alloc_kv(n_layers: int, batch: int, n_kv: int, cap: int, hd: int, device) -> KVCache:
     shape = (n_layers, batch, n_kv, cap, hd)
     return KVCache(torch.zeros(shape, dtype=torch.bfloat16, device=device),
                    torch.zeros(shape, dtype=torch.bfloat16, device=device))
+
+
+PAGE_SIZE = 64
+
+
+def page_plan(lengths: list[int], page_size: int = PAGE_SIZE) -> tuple[torch.Tensor, int]:
+    """Page table for sequences that each need ``lengths[b]`` positions: sequence b gets
+    consecutive pages; table entries past a sequence's need point at one spare page (the
+    last), which no kernel reads. Returns (table [B, max pages] int32 on the host, n_pages)."""
+    need = [(n + page_size - 1) // page_size for n in lengths]
+    width = max(need) if need else 1
+    total = sum(need)
+    table = torch.full((len(lengths), width), total, dtype=torch.int32)
+    base = 0
+    for b, n in enumerate(need):
+        table[b, :n] = torch.arange(base, base + n, dtype=torch.int32)
+        base += n
+    return table, total + 1
+
+
+def alloc_kv_paged(n_layers: int, lengths: list[int], n_kv: int, hd: int, device,
+                   page_table: torch.Tensor | None = None, page_size: int = PAGE_SIZE) -> KVCache:
+    """Paged K/V for sequences of the given lengths (one shared page table may serve
+    several caches: pass the device table of a previous call)."""
+    table, n_pages = page_plan(lengths, page_size)
+    if page_table is None:
+        page_table = table.to(device)
+    shape = (n_layers, n_pages, n_kv, page_size, hd)
+    return KVCache(torch.zeros(shape, dtype=torch.bfloat16, device=device),
+                   torch.zeros(shape, dtype=torch.bfloat16, device=device), page_table, page_size,
+                   max(lengths) if lengths else 0)
 
 
 class TargetModel:
@@ -84,8 +139,14 @@ class TargetModel:
         self._bufs: dict[int, dict[str, torch.Tensor]] = {}
 
     # ------------------------------------------------------------------
-    def make_cache(self, batch: int, cap: int, block: int = 16) -> KVCache:
+    def make_cache(self, batch: int, cap: int, block: int = 16, lengths: list[int] | None = None,
+                   page_table: torch.Tensor | None = None) -> KVCache:
+        """Contiguous [L, batch, Hkv, cap, hd] slots, or, given each sequence's length,
+        a paged cache holding pages for those lengths only."""
         c = self.cfg
+        if lengths is not None:
+            return alloc_kv_paged(c.num_hidden_layers, lengths, c.num_key_value_heads, c.head_dim, self.device,
+                                  page_table)
         return alloc_kv(c.num_hidden_layers, batch, c.num_key_value_heads, cap, c.head_dim, self.device)
 
     def buffers(self, M: int) -> dict[str, torch.Tensor]:
@@ -133,7 +194,9 @@ class TargetModel:
         h, ss = b["h"], b["ss"]
         eps = c.rms_norm_eps
         ops.embed(tokens, self.embed_w, out=h, sumsq_out=ss)
-        fused = self.fuse_attention and ops.fused_attention_ok(M, row_seq, seq_rows, hd, c.rope_dim)
+        fused = (self.fuse_attention and cache.page_table is None
+                 and ops.fused_attention_ok(M, row_seq, seq_rows, hd, c.rope_dim))
+        pg = cache.paging
         for l, lw in enumerate(self.layers):
             kc, vc = cache.layer(l)
             # input_layernorm fused into the QKV projection
@@ -144,9 +207,9 @@ class TargetModel:
                                   key_chunk=key_chunk)
             else:
                 ops.qkv_rope_append(b["qkv"], pos, lw["q_norm"], lw["k_norm"], self.inv_freq, kc, vc, Hq, Hkv, hd,
-                                    c.rope_dim, eps, q_out=b["q"], row_seq=row_seq)
+                                    c.rope_dim, eps, q_out=b["q"], row_seq=row_seq, **pg)
                 ops.attention(b["q"], kc, vc, pos, causal=True, max_kv=max_kv, row_seq=row_seq, out=b["attn"],
-                              ws=ws, seq_rows=seq_rows, key_chunk=key_chunk)
+                              ws=ws, seq_rows=seq_rows, key_chunk=key_chunk, **pg)
             ops.gemm(b["attn"], lw["w_o"], ops.EPI_RESIDUAL, residual=h, out=h, ws=ws, sumsq_out=ss)
             # post_attention_layernorm fused into the gate/up projection
             ops.gemm(h, lw["w_gu"], ops.EPI_SILU_MUL, out=b["act"], ws=ws, norm_w=lw["post_norm"], sumsq_in=ss,
@@ -241,8 +304,12 @@ class DraftModel:
     def target_layer_ids(self) -> list[int]:
         return list(self.cfg.target_layer_ids)
 
-    def make_cache(self, batch: int, cap: int) -> KVCache:
+    def make_cache(self, batch: int, cap: int, lengths: list[int] | None = None,
+                   page_table: torch.Tensor | None = None) -> KVCache:
         c = self.cfg
+        if lengths is not None:
+            return alloc_kv_paged(c.num_hidden_layers, lengths, c.num_key_value_heads, c.head_dim, self.device,
+                                  page_table)
         return alloc_kv(c.num_hidden_layers, batch, c.num_key_value_heads, cap, c.head_dim, self.device)
 
     def buffers(self, M: int, kind: str) -> dict[str, torch.Tensor]:
@@ -291,7 +358,7 @@ class DraftModel:
             kc, vc = cache.layer(l)
             view = b["kv"][:, l * per:(l + 1) * per]
             ops.qkv_rope_append(view, pos, lw["q_norm"], lw["k_norm"], self.inv_freq, kc, vc, 0, Hkv, hd, hd,
-                                c.rms_norm_eps, row_seq=row_seq, do_q=False)
+                                c.rms_norm_eps, row_seq=row_seq, do_q=False, **cache.paging)
 
     def forward_block(self, tokens: torch.Tensor, pos: torch.Tensor, cache: KVCache, kv_len: torch.Tensor,
                       max_kv: int, row_seq: torch.Tensor | None = None, head: str = "argmax",
@@ -312,10 +379,9 @@ class DraftModel:
             kc, vc = cache.layer(l)
             ops.gemm(h, lw["w_qkv"], out=b["qkv"], ws=ws, norm_w=lw["in_norm"], sumsq_in=ss, eps=eps)
             ops.qkv_rope_append(b["qkv"], pos, lw["q_norm"], lw["k_norm"], self.inv_freq, kc, vc, Hq, Hkv, hd, hd,
-                                eps, q_out=b["q"], row_seq=row_seq)
+                                eps, q_out=b["q"], row_seq=row_seq, **cache.paging)
             ops.attention(b["q"], kc, vc, pos, causal=causal, max_kv=max_kv, kv_len=kv_len, row_seq=row_seq,
-                          seq_rows=seq_rows, key_chunk=key_chunk,
-                          out=b["attn"], ws=ws)
+                          seq_rows=seq_rows, key_chunk=key_chunk, out=b["attn"], ws=ws, **cache.paging)
             ops.gemm(b["attn"], lw["w_o"], ops.EPI_RESIDUAL, residual=h, out=h, ws=ws, sumsq_out=ss)
             ops.gemm(h, lw["w_gu"], ops.EPI_SILU_MUL, out=b["act"], ws=ws, norm_w=lw["post_norm"], sumsq_in=ss,
                      eps=eps)

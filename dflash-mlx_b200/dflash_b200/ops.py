@@ -237,14 +237,22 @@ def embed(tokens: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None = 
 def qkv_rope_append(qkv: torch.Tensor, pos: torch.Tensor, q_norm: torch.Tensor, k_norm: torch.Tensor,
                     inv_freq: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, Hq: int, Hkv: int, hd: int,
                     rot_dim: int, eps: float, q_out: torch.Tensor | None = None, row_seq: torch.Tensor | None = None,
-                    q_stride: int | None = None, do_q: bool = True) -> torch.Tensor | None:
-    """q/k head norm + RoPE + cache append. Caches are [seq, Hkv, cap, hd] views (contiguous in the last 3 dims)."""
-    _need_cuda(qkv, pos, q_norm, k_norm, inv_freq, k_cache, v_cache, q_out, row_seq)
+                    q_stride: int | None = None, do_q: bool = True, page_table: torch.Tensor | None = None,
+                    page_size: int = 0) -> torch.Tensor | None:
+    """q/k head norm + RoPE + cache append. Caches are [seq, Hkv, cap, hd] views (contiguous in the last 3 dims),
+    or, with ``page_table`` [seq, pages] int32, page pools [n_pages, Hkv, page_size, hd]."""
+    _need_cuda(qkv, pos, q_norm, k_norm, inv_freq, k_cache, v_cache, q_out, row_seq, page_table)
     M = qkv.shape[0]
     if do_q and q_out is None:
         q_out = torch.empty((M, Hq, hd), dtype=torch.bfloat16, device=qkv.device)
     if k_cache.dim() != 4 or k_cache.stride(3) != 1 or k_cache.stride(2) != hd:
         raise ValueError("k_cache must be a [seq, Hkv, cap, hd] view")
+    if page_table is not None:
+        _lib.call("dfl_qkv_rope_append_paged", _ptr(qkv), _row_stride(qkv), q_stride or hd, _ptr(pos),
+                  _ptr(row_seq), _ptr(q_norm), _ptr(k_norm), _ptr(inv_freq), _ptr(q_out) if do_q else None,
+                  _ptr(k_cache), _ptr(v_cache), k_cache.stride(0), k_cache.stride(1), _ptr(page_table),
+                  page_table.stride(0), int(page_size), M, Hq, Hkv, hd, rot_dim, float(eps), int(do_q), _stream())
+        return q_out
     _lib.call("dfl_qkv_rope_append", _ptr(qkv), _row_stride(qkv), q_stride or hd, _ptr(pos), _ptr(row_seq),
               _ptr(q_norm), _ptr(k_norm), _ptr(inv_freq), _ptr(q_out) if do_q else None, _ptr(k_cache),
               _ptr(v_cache), k_cache.stride(0), k_cache.stride(1), M, Hq, Hkv, hd, rot_dim, float(eps), int(do_q),
@@ -256,7 +264,7 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, pos
               max_kv: int, kv_len: torch.Tensor | None = None, row_seq: torch.Tensor | None = None,
               scale: float | None = None, out: torch.Tensor | None = None, ws: Workspace | None = None,
               gate: torch.Tensor | None = None, gate_head_stride: int = 0, seq_rows: int = 0,
-              key_chunk: int = 0) -> torch.Tensor:
+              key_chunk: int = 0, page_table: torch.Tensor | None = None, page_size: int = 0) -> torch.Tensor:
     """q [M, Hq, hd] against caches [seq, Hkv, cap, hd]; returns [M, Hq*hd] bf16.
     seq_rows: rows per sequence when row_seq groups contiguous runs (0 = any layout).
     key_chunk: keys per split (0 = the library default); results depend on it."""
@@ -270,6 +278,14 @@ def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, pos
     ws = ws or workspace(q.device)
     need = int(_lib.query("dfl_attention_workspace_bytes", M, Hq, hd, max_kv, int(key_chunk)))
     ws.ensure_attn(need)
+    if page_table is not None:
+        _need_cuda(page_table)
+        _lib.call("dfl_attention_paged", _ptr(q), _ptr(k_cache), _ptr(v_cache), k_cache.stride(0), k_cache.stride(1),
+                  _ptr(page_table), page_table.stride(0), int(page_size), _ptr(pos), _ptr(row_seq), _ptr(kv_len),
+                  int(seq_rows), M, Hq, Hkv, hd, int(causal), float(scale), int(max_kv), int(key_chunk), _ptr(out),
+                  _row_stride(out), _ptr(gate), _row_stride(gate) if gate is not None else 0, int(gate_head_stride),
+                  _ptr(ws.attn), ws.attn.numel(), _stream())
+        return out
     _lib.call("dfl_attention", _ptr(q), _ptr(k_cache), _ptr(v_cache), k_cache.stride(0), k_cache.stride(1),
               _ptr(pos), _ptr(row_seq), _ptr(kv_len), int(seq_rows), M, Hq, Hkv, hd, int(causal), float(scale),
               int(max_kv), int(key_chunk),

@@ -83,7 +83,7 @@ class SpecSession:
     def __init__(self, target: TargetModel, draft: DraftModel | None, batch: int, max_total: int,
                  block_size: int, stop_token_ids: set[int] | None = None, use_graph: bool = True,
                  max_steps: int | None = None, prefill_chunk: int = 128, temperature: float = 0.0,
-                 seed: int = 0, profile: bool = False):
+                 seed: int = 0, profile: bool = False, paged: bool = True):
         """temperature >= 1e-5 samples (Gumbel-max on the bf16 logits, keyed by sequence and
         absolute position: the speculative decode reproduces the plain sampled decode of the
         same seed token for token); below it decoding is greedy (fused lm_head argmax)."""
@@ -132,12 +132,19 @@ class SpecSession:
         self.stop_ids = torch.tensor(stops or [0], **i32)
         self.hybrid = bool(getattr(target, "has_recurrent_state", False))
         # hybrid targets roll back by replaying the accepted prefix (no per-token snapshots)
-        self.tcache = (target.make_cache(B, self.cap, block=bs, rollback="replay") if self.hybrid
-                       else target.make_cache(B, self.cap, block=bs))
+        # dense targets keep paged K/V (pages for each sequence's own length, allocated at
+        # prefill when the lengths are known); the hybrid's attention layers stay contiguous
+        self.paged = paged and not self.hybrid
+        self.tcache = None
+        if self.hybrid:
+            self.tcache = target.make_cache(B, self.cap, block=bs, rollback="replay")
+        elif not self.paged:
+            self.tcache = target.make_cache(B, self.cap, block=bs)
         self.layer_ids = sorted(draft.target_layer_ids) if draft is not None else []
         ntaps = max(1, len(self.layer_ids))
         self.taps = torch.zeros((B * bs, ntaps * tc.hidden_size), dtype=torch.bfloat16, device=dev)
-        if draft is not None:
+        self.dcache = None
+        if draft is not None and not self.paged:
             self.dcache = draft.make_cache(B, self.cap)
         self.inject_tokens = self.inject_len = self.inject_noise = None
         self.graph: torch.cuda.CUDAGraph | None = None
@@ -189,6 +196,14 @@ class SpecSession:
             raise ValueError(f"expected {B} prompts")
         if isinstance(max_new_tokens, int):
             max_new_tokens = [max_new_tokens] * B
+        if self.paged:
+            # pages for each sequence's own length (prompt + new tokens + two blocks of slack:
+            # the bound the capacity check below applies)
+            lengths = [min(self.cap, len(p) + m + 2 * self.bs + 1) for p, m in zip(prompts, max_new_tokens)]
+            self.tcache = self.target.make_cache(B, self.cap, block=self.bs, lengths=lengths)
+            if self.draft is not None:
+                self.dcache = self.draft.make_cache(B, self.cap, lengths=lengths, page_table=self.tcache.page_table)
+            self.graph = None  # a recorded step holds the previous caches' pointers
         firsts = []
         st = torch.zeros((B, STATE_INTS), dtype=torch.int32)
         head = "logits" if self.sampled else "argmax"

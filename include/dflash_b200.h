@@ -198,6 +198,26 @@ int dfl_attention(const void* q, const void* k_cache, const void* v_cache, int64
                   int causal, float scale, int max_kv, int key_chunk, void* out, int64_t ldo, const void* gate, int64_t ldg,
                   int gate_head_stride, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Paged KV caches (the same arithmetic, bit for bit, as the contiguous calls above).
+ * The caches are pools of pages [n_pages][Hkv][page_size][hd] bf16 (page_stride and
+ * head_stride in elements); page_table [seq][pt_stride] int32 maps sequence s's
+ * positions [i * page_size, (i + 1) * page_size) to page page_table[s][i]. page_size is a
+ * power of two >= 64. Every position a call reads or writes must have a page. A session
+ * then reserves pages for each sequence's own length instead of the longest one's
+ * (the reference grows one KVCache per layer per sequence, adapters.py:600-601; mlx-lm
+ * KVCache.update_and_fetch / trim). */
+int dfl_qkv_rope_append_paged(const void* qkv, int64_t ldqkv, int q_stride, const int32_t* pos, const int32_t* row_seq,
+                              const void* q_norm, const void* k_norm, const float* inv_freq, void* q_out,
+                              void* k_pages, void* v_pages, int64_t page_stride, int64_t head_stride,
+                              const int32_t* page_table, int64_t pt_stride, int page_size, int M, int Hq, int Hkv,
+                              int hd, int rot_dim, float eps, int do_q, void* stream);
+int dfl_attention_paged(const void* q, const void* k_pages, const void* v_pages, int64_t page_stride,
+                        int64_t head_stride, const int32_t* page_table, int64_t pt_stride, int page_size,
+                        const int32_t* pos, const int32_t* row_seq, const int32_t* kv_len, int seq_rows, int M, int Hq,
+                        int Hkv, int hd, int causal, float scale, int max_kv, int key_chunk, void* out, int64_t ldo,
+                        const void* gate, int64_t ldg, int gate_head_stride, void* workspace, size_t workspace_bytes,
+                        void* stream);
+
 /* dfl_qkv_rope_append followed by causal dfl_attention in one launch, for head_dim 128 with
  * rotary over the whole head (the Qwen3 verify block: mlx-lm qwen3 Attention's q/k norm,
  * RoPE, KVCache.update_and_fetch and scaled_dot_product_attention, adapters.py:611-631).

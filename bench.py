@@ -58,6 +58,9 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-roofline", action="store_true")
     ap.add_argument("--workload", choices=["c3", "c4", "c5"], default="c3")
+    ap.add_argument("--mid-context", type=int, default=1024,
+                    help="c3: untimed steps first advance the context so that the timed steps centre on this "
+                         "context (config 3: prompt 512 + 1024 new tokens, mean context 1024)")
     ap.add_argument("--batch", type=int, default=0, help="c4: sequences per GPU (64); c5: sequences (8)")
     ap.add_argument("--ctx", type=int, default=32768, help="c5: prompt length of every sequence")
     ap.add_argument("--ncu-region", action="store_true",
@@ -390,7 +393,10 @@ def main():
     bs = dcfg.block_size
     g = torch.Generator().manual_seed(args.seed + rank)
     prompt = torch.randint(0, tcfg.vocab_size, (args.prompt_len,), generator=g).tolist()
-    total_steps = args.warmup + args.steps
+    # untimed steps before the timed ones: the warm-up, or more, so that the timed steps sit
+    # around the configuration's mean context instead of at the prompt's end
+    pre = max(args.warmup, int(max(0.0, args.mid_context - args.prompt_len - args.steps * args.tau / 2) / args.tau))
+    total_steps = pre + args.steps
     n_new = bs * (total_steps + 2)
     trace = greedy_trace(target, prompt, n_new + 2 * bs)
     trace_t = torch.zeros(len(prompt) + n_new + 4 * bs, dtype=torch.int32)
@@ -406,9 +412,10 @@ def main():
 
     # ---------------- our arm: device-timed value ----------------
     sess = new_session()
-    for _ in range(args.warmup):
+    for _ in range(pre):
         sess.step()
     torch.cuda.synchronize()
+    ctx_start = int(sess.state[0, S_START].item())
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
     clocks = ClockSampler(device.index)
     clocks.start()
@@ -433,7 +440,7 @@ def main():
     clk = clocks.stop()
     elapsed = t_start.elapsed_time(t_end) * 1e-3
     log = sess.accept_log[0].cpu()
-    accepted = int(log[args.warmup:args.warmup + args.steps].sum())
+    accepted = int(log[pre:pre + args.steps].sum())
     tau_real = accepted / args.steps
     verify_us = sorted(evs[k][1].elapsed_time(evs[k][2]) * 1e3 for k in range(args.steps))
     draft_us = sorted(evs[k][0].elapsed_time(evs[k][1]) * 1e3 for k in range(args.steps))
@@ -452,7 +459,7 @@ def main():
     e2e = None
     if not args.no_e2e:
         sess2 = new_session()
-        for _ in range(args.warmup):
+        for _ in range(pre):
             sess2.step()
         torch.cuda.synchronize()
         # per step the host supplies that step's draft record (injected-prefix length and
@@ -466,11 +473,11 @@ def main():
             sess2.inject_noise[0, k * bs:(k + 1) * bs].copy_(row[1:], non_blocking=True)
 
         t0 = time.perf_counter()
-        for _ in sess2.run_iter(args.steps, copy_tokens=True, before_step=before_step, first_index=args.warmup):
+        for _ in sess2.run_iter(args.steps, copy_tokens=True, before_step=before_step, first_index=pre):
             pass
         torch.cuda.synchronize()
         dt = time.perf_counter() - t0
-        acc2 = int(sess2.accept_log[0, args.warmup:args.warmup + args.steps].sum())
+        acc2 = int(sess2.accept_log[0, pre:pre + args.steps].sum())
         d2h = sess2.state.numel() * 4 + sess2.out_tokens.numel() * 4
         e2e = {"value": acc2 / dt, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                "path": "SpecSession.run_iter (the loop behind dflash_generate_stream): per step a pinned H2D "
@@ -508,9 +515,14 @@ def main():
 
     # launches of our kernels per timed step (one verify + one draft)
     n_layers_t, n_layers_d = tcfg.num_hidden_layers, dcfg.num_hidden_layers
-    per_layer = 7  # qkv gemm (+norm), q/k norm+rope+append, attn chunk, attn combine, o gemm, gu gemm (+norm), down
-    draft_launches = 1 + (2 + n_layers_d) + 1 + per_layer * n_layers_d + 1 + 1
-    verify_launches = 1 + per_layer * n_layers_t + 1 + 1
+    q = _lib.query
+    att_t = int(q("dfl_attention_launches", tcfg.num_attention_heads, tcfg.num_key_value_heads, tcfg.head_dim,
+                  sess.cap, sess.key_chunk))
+    att_d = int(q("dfl_attention_launches", dcfg.num_attention_heads, dcfg.num_key_value_heads, dcfg.head_dim,
+                  sess.cap, sess.key_chunk))
+    # per layer: qkv gemm (+norm), q/k norm+rope+append, attention (1 or 2), o gemm, gu gemm (+norm), down
+    draft_launches = 1 + (2 + n_layers_d) + 1 + (5 + att_d) * n_layers_d + 1 + 1
+    verify_launches = 1 + (5 + att_t) * n_layers_t + 1 + 1
     launches_step = draft_launches + verify_launches
     if rank == 0:
         line = {
@@ -525,7 +537,8 @@ def main():
                        "target_layers": n_layers_t},
             "p50_verify_step_us": round(verify_us[len(verify_us) // 2], 1),
             "p50_draft_step_us": round(draft_us[len(draft_us) // 2], 1),
-            "tau_measured": round(tau_real, 3), "context_end": ctx_end,
+            "tau_measured": round(tau_real, 3), "context_start": ctx_start, "context_end": ctx_end,
+            "untimed_steps_before": pre,
             "gpu_launches": launches_step * args.steps,
             "clocks": clk, "e2e": e2e, "roofline": roof, "cpu_baseline": cpu,
         }

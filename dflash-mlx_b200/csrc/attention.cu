@@ -865,3 +865,24 @@ extern "C" int dfl_attention_paged(const void* q, const void* k_pages, const voi
                         causal, scale, max_kv, key_chunk, out, ldo, gate, ldg, gate_head_stride, workspace,
                         workspace_bytes, stream, nullptr, page_table, pt_stride, page_size);
 }
+
+extern "C" int dfl_attention_launches(int Hq, int Hkv, int hd, int max_kv, int key_chunk) {
+  if (Hkv <= 0 || Hq % Hkv || max_kv <= 0) return -1;
+  key_chunk = resolve_key_chunk(key_chunk);
+  const int n_chunks = (max_kv + key_chunk - 1) / key_chunk;
+  if (n_chunks <= 1) return 1;
+  const int G = Hq / Hkv;
+  const bool deep = key_chunk > 2 * ATT_KB;
+  bool cm = false;
+  switch (hd) {
+    case 64: cm = deep ? cluster_merge_ok<64, 3>(n_chunks, G, (size_t)(G * 16 * 64 + 2 * 3 * ATT_KB * 64) * 2)
+                       : cluster_merge_ok<64, 2>(n_chunks, G, (size_t)(G * 16 * 64 + 2 * 2 * ATT_KB * 64) * 2);
+      break;
+    case 128: cm = deep ? cluster_merge_ok<128, 3>(n_chunks, G, (size_t)(G * 16 * 128 + 2 * 3 * ATT_KB * 128) * 2)
+                        : cluster_merge_ok<128, 2>(n_chunks, G, (size_t)(G * 16 * 128 + 2 * 2 * ATT_KB * 128) * 2);
+      break;
+    case 256: cm = cluster_merge_ok<256, 2>(n_chunks, G, (size_t)(G * 16 * 256 + 2 * 2 * ATT_KB * 256) * 2); break;
+    default: return -1;
+  }
+  return cm ? 1 : 2;
+}

@@ -67,6 +67,7 @@ SIGNATURES: dict[str, tuple] = {
                                     c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int, c_float,
                                     c_int, c_int, c_void_p, c_int64, c_void_p, c_int64, c_int, c_void_p, c_size_t,
                                     c_void_p]),
+    "dfl_attention_launches": (c_int, [c_int, c_int, c_int, c_int, c_int]),
     "dfl_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p, c_int,
                               c_int, c_int, c_int, c_int, c_int, c_float, c_int, c_int, c_void_p, c_int64, c_void_p,
                               c_int64,

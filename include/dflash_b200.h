@@ -198,6 +198,11 @@ int dfl_attention(const void* q, const void* k_cache, const void* v_cache, int64
                   int causal, float scale, int max_kv, int key_chunk, void* out, int64_t ldo, const void* gate, int64_t ldg,
                   int gate_head_stride, void* workspace, size_t workspace_bytes, void* stream);
 
+/* Kernel launches one dfl_attention call of this shape makes (1: one chunk, or chunks
+ * merged inside the chunk kernel by a thread-block cluster; 2: chunk kernel + merge
+ * kernel), -1 for an unsupported shape. Needs the device current (cluster placement). */
+int dfl_attention_launches(int Hq, int Hkv, int hd, int max_kv, int key_chunk);
+
 /* Paged KV caches (the same arithmetic, bit for bit, as the contiguous calls above).
  * The caches are pools of pages [n_pages][Hkv][page_size][hd] bf16 (page_stride and
  * head_stride in elements); page_table [seq][pt_stride] int32 maps sequence s's

@@ -32,6 +32,8 @@
 #include "common.cuh"
 #include "tma_util.cuh"
 
+#include <cstdlib>
+
 namespace dfl {
 
 constexpr int ATT_SITE_SEGMENTS = 301;  // a tile held more sequences than the launch's segments
@@ -389,14 +391,19 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(AttnArgs a) {
       o[j][2] *= al1;
       o[j][3] *= al1;
     }
-    // O += P V
+    // O += P V, with P split into bf16 high and low parts (P = hi + lo to about 16
+    // significant bits): the probabilities keep near-fp32 precision, as the reference's
+    // fp32 softmax weights do, instead of a single bf16 rounding of each weight
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
-      uint32_t pf[4];
-      pf[0] = pack_bf16x2(s[2 * kk][0], s[2 * kk][1]);
-      pf[1] = pack_bf16x2(s[2 * kk][2], s[2 * kk][3]);
-      pf[2] = pack_bf16x2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-      pf[3] = pack_bf16x2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+      uint32_t pf[4], pl[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float x0 = s[2 * kk + (u >> 1)][2 * (u & 1)], x1 = s[2 * kk + (u >> 1)][2 * (u & 1) + 1];
+        const float h0 = round_bf16(x0), h1 = round_bf16(x1);
+        pf[u] = pack_bf16x2(h0, h1);
+        pl[u] = pack_bf16x2(x0 - h0, x1 - h1);
+      }
 #pragma unroll
       for (int dp = 0; dp < HD / 16; ++dp) {
         const int row = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
@@ -405,6 +412,8 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(AttnArgs a) {
         ldmatrix_x4_trans(smem_u32(tV + att_swz<HD>(row, c)), b0, b1, b2, b3);
         mma_bf16_16816(o[2 * dp], pf, b0, b1);
         mma_bf16_16816(o[2 * dp + 1], pf, b2, b3);
+        mma_bf16_16816(o[2 * dp], pl, b0, b1);
+        mma_bf16_16816(o[2 * dp + 1], pl, b2, b3);
       }
     }
     buf = buf == ST - 1 ? 0 : buf + 1;
@@ -433,28 +442,48 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(AttnArgs a) {
       if (t == 0) pml[warp * 16 + r] = make_float2(mrow[half], lrow[half]);
     }
     att_cluster_sync();
-    const int C = gridDim.x;
+    const int C = gridDim.x;  // <= 16
     const uint32_t po_s = smem_u32(po), pml_s = smem_u32(pml);
+    // every peer's partial base addresses once; an address inside a CTA's window maps linearly
+    uint32_t po_c[16], ml_c[16];
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      po_c[c] = c < C ? att_cluster_map(po_s, c) : 0u;
+      ml_c[c] = c < C ? att_cluster_map(pml_s, c) : 0u;
+    }
     for (int item = chunk; item < a.G * 16; item += C) {
       const int hl = item >> 4, r = item & 15;
       const int m = m0 + r;
       if (m >= a.M || s_lim[r] <= 0) continue;
       const int nch = min((s_lim[r] + a.key_chunk - 1) / a.key_chunk, C);
+      // all chunks' (max, sum) in flight together, then the weights in chunk order
+      float2 ml[16];
+#pragma unroll
+      for (int c = 0; c < 16; ++c)
+        ml[c] = c < nch ? ld_dsmem_f32x2(ml_c[c] + item * 8) : make_float2(-INFINITY, 0.f);
       float mmax = -INFINITY;
-      for (int c = 0; c < nch; ++c) mmax = fmaxf(mmax, ld_dsmem_f32x2(att_cluster_map(pml_s + item * 8, c)).x);
+#pragma unroll
+      for (int c = 0; c < 16; ++c) mmax = fmaxf(mmax, ml[c].x);
       const float mu = mmax == -INFINITY ? 0.f : mmax;
+      float w[16];
+      float den = 0.f;
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        w[c] = c < nch ? exp2f(ml[c].x - mu) : 0.f;
+        den += w[c] * ml[c].y;
+      }
+      const float inv = den > 0.f ? 1.f / den : 0.f;
       const int hq = kvh * a.G + hl;
       __nv_bfloat16* dst = a.out + (long long)m * a.ldo + (long long)hq * HD;
       const __nv_bfloat16* gr = a.gate ? a.gate + (long long)m * a.ldg + (long long)hq * a.gate_hs : nullptr;
       for (int d = threadIdx.x; d < HD; d += nthr) {
-        float acc = 0.f, den = 0.f;
-        for (int c = 0; c < nch; ++c) {
-          const float2 ml = ld_dsmem_f32x2(att_cluster_map(pml_s + item * 8, c));
-          const float w = exp2f(ml.x - mu);
-          den += w * ml.y;
-          acc += w * ld_dsmem_f32(att_cluster_map(po_s + (item * HD + d) * 4, c));
-        }
-        const float inv = den > 0.f ? 1.f / den : 0.f;
+        const uint32_t off = (uint32_t)(item * HD + d) * 4u;
+        float v[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) v[c] = c < nch ? ld_dsmem_f32(po_c[c] + off) : 0.f;
+        float acc = 0.f;
+#pragma unroll
+        for (int c = 0; c < 16; ++c) acc += w[c] * v[c];
         if (gr)
           dst[d] = f2bf(round_bf16(acc * inv) * round_bf16(1.f / (1.f + __expf(-bf2f(gr[d])))));
         else
@@ -584,6 +613,13 @@ __global__ void attn_combine_kernel(AttnArgs a) {
 template <int HD, int ST>
 static bool cluster_merge_ok(int n_chunks, int G, size_t smem) {
   if (n_chunks < 2 || n_chunks > 16) return false;
+  // DFLASH_B200_ATTN_CLUSTER=0 keeps the two-kernel merge (a process-wide choice, so every
+  // launch of a session agrees)
+  static const bool enabled = [] {
+    const char* e = getenv("DFLASH_B200_ATTN_CLUSTER");
+    return !(e && e[0] == '0');
+  }();
+  if (!enabled) return false;
   // the partials ([G][16][HD] fp32 + [G][16] (max, sum)) live in the K/V ring
   if ((size_t)G * 16 * HD * 4 + (size_t)G * 16 * 8 > (size_t)2 * ST * ATT_KB * HD * 2) return false;
   static int cache[64][17][9] = {};  // 0 unknown, 1 yes, 2 no

@@ -72,6 +72,10 @@ def _draft_calls(tcfg, dcfg, tw, dw, mask_mode, ctx_rows, seed):
 
 
 def _check(calls, what, tol=2e-2):
+    for i, (hid, ref_h, lg, ref_lg) in enumerate(calls):  # all calls reported before any assertion
+        dh, dl = (hid - ref_h).abs(), (lg - ref_lg).abs()
+        print(f"{what} call {i}: hidden max err {dh.max().item():.4f} mean {dh.mean().item():.2e}; logits max err "
+              f"{dl.max().item():.4f}; proposals equal {int((lg.argmax(-1) == ref_lg.argmax(-1)).sum())}/{len(lg)}")
     for i, (hid, ref_h, lg, ref_lg) in enumerate(calls):
         dh = (hid - ref_h).abs()
         dl = (lg - ref_lg).abs()

@@ -22,17 +22,12 @@
 // over many SMs, large ones cut the partial-result traffic of batched verify.
 // When one chunk covers every row's keys the chunk kernel normalises and writes
 // the output itself (the merge of a single chunk is the identity) and no merge
-// kernel runs. When the chunks of a row number at most 16, the CTAs of one (tile, kv
-// head) are launched as one thread-block cluster (one CTA per chunk) and merge in
-// the chunk kernel itself: each CTA leaves its unnormalised partial in its shared
-// memory, and after a cluster barrier every CTA reads a slice of (head, row) items
-// from all of them over distributed shared memory, in chunk order -- no partials in
-// HBM and no merge launch. K/V stream through a 3-stage cp.async ring (2 stages at
-// head_dim 256).
+// kernel runs. K/V stream through a 3-stage cp.async ring (2 stages at head_dim 256).
+// (A variant that merged the chunks inside the chunk kernel, one thread-block cluster per
+// tile and kv head reading the peers' partials over distributed shared memory, measured
+// slower on B200 at both the single-stream and the 64-sequence shapes and was removed.)
 #include "common.cuh"
 #include "tma_util.cuh"
-
-#include <cstdlib>
 
 namespace dfl {
 
@@ -124,27 +119,7 @@ __device__ __forceinline__ int row_limit(const AttnArgs& a, int m) {
 // K/V ring depth: 3 stages for long chunks at head_dim <= 128; 2 for short chunks
 // (a 128-key chunk is two blocks: a deeper ring only costs shared memory that the
 // next kernel's prologue could use) and for head_dim 256 (shared memory)
-__device__ __forceinline__ uint32_t att_cluster_map(uint32_t saddr, uint32_t rank) {
-  uint32_t r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(saddr), "r"(rank));
-  return r;
-}
-__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];\n" : "=f"(v) : "r"(addr) : "memory");
-  return v;
-}
-__device__ __forceinline__ float2 ld_dsmem_f32x2(uint32_t addr) {
-  float2 v;
-  asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];\n" : "=f"(v.x), "=f"(v.y) : "r"(addr) : "memory");
-  return v;
-}
-__device__ __forceinline__ void att_cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;\n" ::: "memory");
-}
-
-// CM: cluster merge (grid.x == cluster size == the chunk count; see the file comment)
-template <int HD, int ST, bool CM>
+template <int HD, int ST>
 __global__ void __launch_bounds__(256) attn_chunk_kernel(AttnArgs a) {
   grid_dependency_launch_dependents();
   grid_dependency_wait();
@@ -198,9 +173,8 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(AttnArgs a) {
 #pragma unroll
   for (int r = 0; r < 16; ++r) lim_max = max(lim_max, s_lim[r]);
   const int k_begin = chunk * a.key_chunk;
-  // a cluster-merge CTA past every row's keys still takes part in the merge (empty partial)
-  if (!CM && k_begin >= lim_max) return;
-  const int k_end = max(k_begin, min(k_begin + a.key_chunk, lim_max));
+  if (k_begin >= lim_max) return;
+  const int k_end = min(k_begin + a.key_chunk, lim_max);
 
   const __nv_bfloat16* Kb = a.k_cache + kvh * a.head_stride;
   const __nv_bfloat16* Vb = a.v_cache + kvh * a.head_stride;
@@ -426,73 +400,6 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(AttnArgs a) {
   lrow[1] += __shfl_xor_sync(0xffffffffu, lrow[1], 2);
 
   const int h = kvh * a.G + warp;
-  if constexpr (CM) {
-    // this CTA's partial (o unnormalised, running max, denominator) into its own shared
-    // memory (the K/V ring, idle now), then a cluster-wide merge in chunk order
-    __syncthreads();
-    float* po = reinterpret_cast<float*>(sK);                  // [G][16][HD]
-    float2* pml = reinterpret_cast<float2*>(po + a.G * 16 * HD);  // [G][16]
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const int r = g + half * 8;
-      float* dst = po + (warp * 16 + r) * HD;
-#pragma unroll
-      for (int j = 0; j < HD / 8; ++j)
-        *reinterpret_cast<float2*>(dst + j * 8 + 2 * t) = make_float2(o[j][2 * half], o[j][2 * half + 1]);
-      if (t == 0) pml[warp * 16 + r] = make_float2(mrow[half], lrow[half]);
-    }
-    att_cluster_sync();
-    const int C = gridDim.x;  // <= 16
-    const uint32_t po_s = smem_u32(po), pml_s = smem_u32(pml);
-    // every peer's partial base addresses once; an address inside a CTA's window maps linearly
-    uint32_t po_c[16], ml_c[16];
-#pragma unroll
-    for (int c = 0; c < 16; ++c) {
-      po_c[c] = c < C ? att_cluster_map(po_s, c) : 0u;
-      ml_c[c] = c < C ? att_cluster_map(pml_s, c) : 0u;
-    }
-    for (int item = chunk; item < a.G * 16; item += C) {
-      const int hl = item >> 4, r = item & 15;
-      const int m = m0 + r;
-      if (m >= a.M || s_lim[r] <= 0) continue;
-      const int nch = min((s_lim[r] + a.key_chunk - 1) / a.key_chunk, C);
-      // all chunks' (max, sum) in flight together, then the weights in chunk order
-      float2 ml[16];
-#pragma unroll
-      for (int c = 0; c < 16; ++c)
-        ml[c] = c < nch ? ld_dsmem_f32x2(ml_c[c] + item * 8) : make_float2(-INFINITY, 0.f);
-      float mmax = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < 16; ++c) mmax = fmaxf(mmax, ml[c].x);
-      const float mu = mmax == -INFINITY ? 0.f : mmax;
-      float w[16];
-      float den = 0.f;
-#pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        w[c] = c < nch ? exp2f(ml[c].x - mu) : 0.f;
-        den += w[c] * ml[c].y;
-      }
-      const float inv = den > 0.f ? 1.f / den : 0.f;
-      const int hq = kvh * a.G + hl;
-      __nv_bfloat16* dst = a.out + (long long)m * a.ldo + (long long)hq * HD;
-      const __nv_bfloat16* gr = a.gate ? a.gate + (long long)m * a.ldg + (long long)hq * a.gate_hs : nullptr;
-      for (int d = threadIdx.x; d < HD; d += nthr) {
-        const uint32_t off = (uint32_t)(item * HD + d) * 4u;
-        float v[16];
-#pragma unroll
-        for (int c = 0; c < 16; ++c) v[c] = c < nch ? ld_dsmem_f32(po_c[c] + off) : 0.f;
-        float acc = 0.f;
-#pragma unroll
-        for (int c = 0; c < 16; ++c) acc += w[c] * v[c];
-        if (gr)
-          dst[d] = f2bf(round_bf16(acc * inv) * round_bf16(1.f / (1.f + __expf(-bf2f(gr[d])))));
-        else
-          dst[d] = f2bf(acc * inv);
-      }
-    }
-    att_cluster_sync();  // no CTA leaves while a peer may still read its partial
-    return;
-  }
   if (a.direct) {
     // single chunk: out = o / l (the merge of one chunk is the identity)
 #pragma unroll
@@ -606,51 +513,6 @@ __global__ void attn_combine_kernel(AttnArgs a) {
   }
 }
 
-// Whether the chunk kernel can merge its chunks as one cluster per (tile, kv head): the
-// chunk count fits a cluster (16 with the non-portable opt-in) and the device can place
-// such a cluster. Depends on the chunk count and head shape only, so every launch of a
-// session makes the same choice.
-template <int HD, int ST>
-static bool cluster_merge_ok(int n_chunks, int G, size_t smem) {
-  if (n_chunks < 2 || n_chunks > 16) return false;
-  // DFLASH_B200_ATTN_CLUSTER=0 keeps the two-kernel merge (a process-wide choice, so every
-  // launch of a session agrees)
-  static const bool enabled = [] {
-    const char* e = getenv("DFLASH_B200_ATTN_CLUSTER");
-    return !(e && e[0] == '0');
-  }();
-  if (!enabled) return false;
-  // the partials ([G][16][HD] fp32 + [G][16] (max, sum)) live in the K/V ring
-  if ((size_t)G * 16 * HD * 4 + (size_t)G * 16 * 8 > (size_t)2 * ST * ATT_KB * HD * 2) return false;
-  static int cache[64][17][9] = {};  // 0 unknown, 1 yes, 2 no
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return false;
-  int& c = cache[dev][n_chunks][G];
-  if (c == 0) {
-    c = 2;
-    if (n_chunks <= 8 ||
-        cudaFuncSetAttribute(attn_chunk_kernel<HD, ST, true>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
-            cudaSuccess) {
-      cudaLaunchAttribute attr[1];
-      attr[0].id = cudaLaunchAttributeClusterDimension;
-      attr[0].val.clusterDim.x = n_chunks;
-      attr[0].val.clusterDim.y = 1;
-      attr[0].val.clusterDim.z = 1;
-      cudaLaunchConfig_t cfg = {};
-      cfg.gridDim = dim3(n_chunks, 1, 1);
-      cfg.blockDim = dim3(32 * G);
-      cfg.dynamicSmemBytes = smem;
-      cfg.attrs = attr;
-      cfg.numAttrs = 1;
-      int n = 0;
-      if (cudaOccupancyMaxActiveClusters(&n, attn_chunk_kernel<HD, ST, true>, &cfg) == cudaSuccess && n > 0) c = 1;
-    }
-    cudaGetLastError();
-  }
-  return c == 1;
-}
-
 template <int HD, int ST>
 static int launch_attn(AttnArgs a, int n_tiles, cudaStream_t st) {
   const size_t smem = (size_t)(a.G * 16 * HD + 2 * ST * ATT_KB * HD) * 2;
@@ -663,11 +525,9 @@ static int launch_attn(AttnArgs a, int n_tiles, cudaStream_t st) {
   if (dev >= 0 && dev < 64 && !opted[dev]) {
     cudaFuncAttributes fa;
     int optin = 0;
-    if (cudaFuncGetAttributes(&fa, attn_chunk_kernel<HD, ST, false>) != cudaSuccess ||
+    if (cudaFuncGetAttributes(&fa, attn_chunk_kernel<HD, ST>) != cudaSuccess ||
         cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
-        cudaFuncSetAttribute(attn_chunk_kernel<HD, ST, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             optin - (int)fa.sharedSizeBytes) != cudaSuccess ||
-        cudaFuncSetAttribute(attn_chunk_kernel<HD, ST, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaFuncSetAttribute(attn_chunk_kernel<HD, ST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              optin - (int)fa.sharedSizeBytes) != cudaSuccess) {
       set_error("dfl_attention: cannot opt in to the per-block shared memory");
       return DFL_ERR_UNSUPPORTED;
@@ -678,7 +538,7 @@ static int launch_attn(AttnArgs a, int n_tiles, cudaStream_t st) {
     set_error("dfl_attention: %zu bytes of shared memory needed", smem);
     return DFL_ERR_UNSUPPORTED;
   }
-  cudaLaunchAttribute attr[2];
+  cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t cfg = {};
@@ -688,20 +548,7 @@ static int launch_attn(AttnArgs a, int n_tiles, cudaStream_t st) {
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (!a.direct && cluster_merge_ok<HD, ST>(a.n_chunks, a.G, smem)) {
-    attr[1].id = cudaLaunchAttributeClusterDimension;
-    attr[1].val.clusterDim.x = a.n_chunks;
-    attr[1].val.clusterDim.y = 1;
-    attr[1].val.clusterDim.z = 1;
-    cfg.numAttrs = 2;
-    cudaError_t e = cudaLaunchKernelEx(&cfg, attn_chunk_kernel<HD, ST, true>, a);
-    if (e != cudaSuccess) {
-      set_error("dfl_attention: cluster chunk kernel launch failed: %s", cudaGetErrorString(e));
-      return DFL_ERR_CUDA;
-    }
-    return DFL_OK;
-  }
-  cudaError_t e = cudaLaunchKernelEx(&cfg, attn_chunk_kernel<HD, ST, false>, a);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, attn_chunk_kernel<HD, ST>, a);
   if (e != cudaSuccess) {
     set_error("dfl_attention: chunk kernel launch failed: %s", cudaGetErrorString(e));
     return DFL_ERR_CUDA;
@@ -903,22 +750,7 @@ extern "C" int dfl_attention_paged(const void* q, const void* k_pages, const voi
 }
 
 extern "C" int dfl_attention_launches(int Hq, int Hkv, int hd, int max_kv, int key_chunk) {
-  if (Hkv <= 0 || Hq % Hkv || max_kv <= 0) return -1;
+  if (Hkv <= 0 || Hq % Hkv || max_kv <= 0 || (hd != 64 && hd != 128 && hd != 256)) return -1;
   key_chunk = resolve_key_chunk(key_chunk);
-  const int n_chunks = (max_kv + key_chunk - 1) / key_chunk;
-  if (n_chunks <= 1) return 1;
-  const int G = Hq / Hkv;
-  const bool deep = key_chunk > 2 * ATT_KB;
-  bool cm = false;
-  switch (hd) {
-    case 64: cm = deep ? cluster_merge_ok<64, 3>(n_chunks, G, (size_t)(G * 16 * 64 + 2 * 3 * ATT_KB * 64) * 2)
-                       : cluster_merge_ok<64, 2>(n_chunks, G, (size_t)(G * 16 * 64 + 2 * 2 * ATT_KB * 64) * 2);
-      break;
-    case 128: cm = deep ? cluster_merge_ok<128, 3>(n_chunks, G, (size_t)(G * 16 * 128 + 2 * 3 * ATT_KB * 128) * 2)
-                        : cluster_merge_ok<128, 2>(n_chunks, G, (size_t)(G * 16 * 128 + 2 * 2 * ATT_KB * 128) * 2);
-      break;
-    case 256: cm = cluster_merge_ok<256, 2>(n_chunks, G, (size_t)(G * 16 * 256 + 2 * 2 * ATT_KB * 256) * 2); break;
-    default: return -1;
-  }
-  return cm ? 1 : 2;
+  return (max_kv + key_chunk - 1) / key_chunk <= 1 ? 1 : 2;
 }

@@ -102,7 +102,7 @@ def bench_gdr(timer: Timer, T: int, snapshots: bool):
     v = torch.randn(B, T, Hv, D, device="cuda", generator=g).bfloat16()
     alpha = torch.exp(-torch.nn.functional.softplus(torch.randn(B, T, Hv, device="cuda", generator=g)))
     beta = torch.sigmoid(torch.randn(B, T, Hv, device="cuda", generator=g))
-    S0 = torch.randn(B, Hv, D, D, device="cuda", generator=g) * 0.1
+    S0 = torch.randn(B, Hv, D, D, device="cuda", generator=g) * 0.01
     out = torch.empty_like(S0)
     snaps = torch.empty((B, T, Hv, D, D), device="cuda") if snapshots else None
     o = torch.empty((B, T, Hv, D), dtype=torch.bfloat16, device="cuda")

@@ -198,9 +198,8 @@ int dfl_attention(const void* q, const void* k_cache, const void* v_cache, int64
                   int causal, float scale, int max_kv, int key_chunk, void* out, int64_t ldo, const void* gate, int64_t ldg,
                   int gate_head_stride, void* workspace, size_t workspace_bytes, void* stream);
 
-/* Kernel launches one dfl_attention call of this shape makes (1: one chunk, or chunks
- * merged inside the chunk kernel by a thread-block cluster; 2: chunk kernel + merge
- * kernel), -1 for an unsupported shape. Needs the device current (cluster placement). */
+/* Kernel launches one dfl_attention call of this shape makes (1: a single key chunk,
+ * written directly; 2: chunk kernel + merge kernel), -1 for an unsupported shape. */
 int dfl_attention_launches(int Hq, int Hkv, int hd, int max_kv, int key_chunk);
 
 /* Paged KV caches (the same arithmetic, bit for bit, as the contiguous calls above).

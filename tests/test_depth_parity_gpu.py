@@ -1,19 +1,20 @@
 """Parity at the benchmark configurations' full depth and width.
 
-* Qwen3-4B (config 3), all 36 layers: every GPU layer is fed the oracle's own input
-  (teacher forcing: a prefill of 48 rows, then a 16-row verify block attending to the
-  cached prefix) and must land on the oracle's output within 2e-2 absolute, or within
-  two bf16 ulps of the value where that is larger (residual values of magnitude 2 and
-  above: the residual stream here reaches |h| ~ 40); the lm_head on the oracle's final
-  hidden states must give its logits within 2e-2 (or one ulp). The free-running
-  36-layer forward is then compared end to end: its logit error must not exceed the
-  oracle's own bf16-vs-fp32 deviation on the same inputs (the model's sensitivity to
-  rounding order, which no bf16 implementation can beat), and its greedy tokens must
-  agree with the oracle's on >= 90 % of rows.
-* Qwen3.5-27B width (config 5): per gated-delta layer, fed the oracle's input, the fp32
-  recurrent state after a prefill, a verify block and its rollback is within 1e-3
-  relative of the oracle's (north_star's state tolerance), and the conv state and layer
-  output agree as above.
+The yardstick is the oracle's own rounding sensitivity. Residual values reach |h| ~ 40 at
+Qwen3-4B depth (a bf16 ulp of 0.25) and logits reach 5-6 (an ulp of 0.03), so an absolute
+bound of 2e-2 is below bf16 resolution there; what a correct bf16 kernel must meet is
+"no further from the oracle than the oracle's bf16 arithmetic is from its own fp32
+arithmetic on the same inputs" (d_gpu = |gpu - oracle|, d_ref = |oracle_fp32 - oracle|:
+mean d_gpu <= mean d_ref and max d_gpu <= 1.5 max d_ref), or within one bf16 ulp.
+
+* Qwen3-4B (config 3), all 36 layers, teacher forced: every GPU layer is fed the oracle's
+  input (a 48-row prefill, then a 16-row verify block over the cached prefix); then the
+  lm_head on the oracle's final hidden states; then the free-running 36-layer forward
+  end to end (greedy tokens agree with the oracle's on >= 90 % of rows).
+* Qwen3.5-27B width (config 5), per gated-delta layer fed the oracle's input: the
+  recurrence on the oracle's own q, k, v, g, beta is within 1e-3 relative on the fp32
+  state (north_star's bound); the whole layer (bf16 projections in front of it) meets
+  the sensitivity yardstick on its output and its state.
 """
 import dataclasses
 
@@ -54,6 +55,15 @@ def _cpu_weights(cfg, seed):
     return out
 
 
+def _vs_sensitivity(got: torch.Tensor, ref: torch.Tensor, ref32: torch.Tensor):
+    """(ok, max d_gpu, mean d_gpu, max d_ref, mean d_ref): the yardstick of the module
+    docstring, or every element within one bf16 ulp of the reference."""
+    d = (got.float() - ref.float()).abs()
+    r = (ref32.float() - ref.float()).abs()
+    ok = (d.mean() <= r.mean() and d.max() <= 1.5 * r.max()) or bool((d <= _ulp(ref)).all())
+    return bool(ok), d.max().item(), d.mean().item(), r.max().item(), r.mean().item()
+
+
 def _oracle_layer_inputs(ot, prompt, block):
     """Runs the oracle layer by layer over the prefill and then the block (one KV cache
     per layer); returns, for both passes, the residual stream entering every layer (and
@@ -89,9 +99,18 @@ def test_qwen3_4b_36_layers_teacher_forced_and_end_to_end(monkeypatch):
     H = tcfg.hidden_size
     i32 = dict(dtype=torch.int32, device=DEV)
 
+    # the fp32 oracle on the same (bf16) layer inputs: the oracle's own rounding sensitivity
+    with monkeypatch.context() as mp:
+        mp.setattr(O, "bf16", lambda x: x.float())
+        c32 = ot.make_cache(P + T + 8)
+        out32 = [(ot.layer(l, hs_p[l], torch.arange(P), c32[l]), ot.layer(l, hs_b[l], torch.arange(P, P + T), c32[l]))
+                 for l in range(tcfg.num_hidden_layers)]
+        fin = torch.cat([hs_p[-1], hs_b[-1]], 0)
+        lm32 = ot.lm_head_logits(O.rms_norm(fin, ot.w["norm"], tcfg.rms_norm_eps))
+
     # --- teacher-forced per layer ---------------------------------------------------
     one = dataclasses.replace(tcfg, num_hidden_layers=1, vocab_size=P + T)
-    worst, bad = 0.0, []
+    bad = []
     for l in range(tcfg.num_hidden_layers):
         rows = torch.cat([hs_p[l], hs_b[l]], 0).to(torch.bfloat16)
         m = TargetModel(one, {"embed": rows, "norm": tw["norm"], "layers": [tw["layers"][l]]}, DEV)
@@ -102,26 +121,26 @@ def test_qwen3_4b_36_layers_teacher_forced_and_end_to_end(monkeypatch):
                   head="hidden")
         m.forward(torch.arange(P, P + T, **i32), torch.arange(P, P + T, **i32), cache, max_kv=P + T,
                   layer_ids=[0], taps_out=tb, head="hidden")
-        for what, got, ref in (("prefill", tp, hs_p[l + 1]), ("block", tb, hs_b[l + 1])):
-            ok, mx, mean = _within(got.cpu(), ref, ulps=2)
-            worst = max(worst, mx)
-            if l % 6 == 0 or not ok or mean > 2e-3:
-                print(f"layer {l} {what}: max err {mx:.4f} mean {mean:.2e} max|ref| {ref.abs().max().item():.2f}")
-            if not ok or mean > 2e-3:
-                bad.append((l, what, mx, mean))
+        for what, got, ref, r32 in (("prefill", tp, hs_p[l + 1], out32[l][0]), ("block", tb, hs_b[l + 1], out32[l][1])):
+            ok, mx, mean, rmx, rmean = _vs_sensitivity(got.cpu(), ref, r32)
+            if l % 6 == 0 or not ok:
+                print(f"layer {l} {what}: gpu vs oracle max {mx:.4f} mean {mean:.2e}; oracle fp32 vs bf16 max "
+                      f"{rmx:.4f} mean {rmean:.2e}")
+            if not ok:
+                bad.append((l, what, mx, mean, rmx, rmean))
         del m, cache
-    print(f"teacher-forced layers: worst max abs err {worst:.4f}")
-    assert not bad, bad
 
     # --- lm_head on the oracle's final hidden states --------------------------------
     zero = dataclasses.replace(tcfg, num_hidden_layers=0, tie_word_embeddings=False)
-    rows = torch.cat([hs_p[-1], hs_b[-1]], 0).to(torch.bfloat16)
-    m0 = TargetModel(zero, {"embed": rows, "lm_head": tw["embed"], "norm": tw["norm"], "layers": []}, DEV)
+    m0 = TargetModel(zero, {"embed": fin.to(torch.bfloat16), "lm_head": tw["embed"], "norm": tw["norm"],
+                            "layers": []}, DEV)
     lg = m0.forward(torch.arange(P + T, **i32), torch.arange(P + T, **i32), m0.make_cache(1, P + T),
                     max_kv=P + T, head="logits").float().cpu()
-    ok, mx, mean = _within(lg, torch.cat([lg_p, lg_b], 0), ulps=1)
-    print(f"lm_head teacher-forced: max err {mx:.4f} mean {mean:.2e}")
-    assert ok, mx
+    ok, mx, mean, rmx, rmean = _vs_sensitivity(lg, torch.cat([lg_p, lg_b], 0), lm32)
+    print(f"lm_head teacher-forced: max err {mx:.4f} mean {mean:.2e} (oracle fp32 vs bf16 max {rmx:.4f} "
+          f"mean {rmean:.2e})")
+    if not ok:
+        bad.append(("lm_head", mx, mean, rmx, rmean))
     del m0
 
     # --- end to end, free running ---------------------------------------------------
@@ -133,8 +152,9 @@ def test_qwen3_4b_36_layers_teacher_forced_and_end_to_end(monkeypatch):
                            head="logits").float().cpu()
     del target, cache
     got, ref = torch.cat([got_p, got_b], 0), torch.cat([lg_p, lg_b], 0)
-    monkeypatch.setattr(O, "bf16", lambda x: x.float())
-    (_, f_p), (_, f_b) = _oracle_layer_inputs(O.OracleTarget(tcfg, tw), prompt, block)
+    with monkeypatch.context() as mp:
+        mp.setattr(O, "bf16", lambda x: x.float())
+        (_, f_p), (_, f_b) = _oracle_layer_inputs(O.OracleTarget(tcfg, tw), prompt, block)
     ref32 = torch.cat([f_p, f_b], 0)
     d_gpu = (got - ref).abs()
     d_ora = (ref32 - ref).abs()
@@ -143,12 +163,13 @@ def test_qwen3_4b_36_layers_teacher_forced_and_end_to_end(monkeypatch):
     print(f"36 layers end to end: gpu vs oracle max {d_gpu.max().item():.4f} mean {d_gpu.mean().item():.2e}, "
           f"greedy agreement {agree:.3f}; oracle fp32 vs oracle bf16 max {d_ora.max().item():.4f} "
           f"mean {d_ora.mean().item():.2e} agreement {agree32:.3f}")
-    assert d_gpu.max().item() <= d_ora.max().item()
-    assert d_gpu.mean().item() <= max(2e-2, d_ora.mean().item())
+    assert not bad, bad
+    assert d_gpu.max().item() <= 1.5 * d_ora.max().item()
+    assert d_gpu.mean().item() <= d_ora.mean().item()
     assert agree >= 0.9
 
 
-def test_qwen35_27b_width_gdn_state_teacher_forced():
+def test_qwen35_27b_width_gdn_state_teacher_forced(monkeypatch):
     """Per gated-delta layer of a 27B-width hybrid (layers 0-2 of 4), fed the oracle's
     input: prefill of 40 rows, a 16-row verify block, rollback to 6 accepted rows."""
     from oracle import dflash_oracle as O
@@ -192,11 +213,11 @@ def test_qwen35_27b_width_gdn_state_teacher_forced():
         m.forward(torch.arange(P, P + T, **i32), torch.arange(P, P + T, **i32), hc, max_kv=P + T, layer_ids=[0],
                   taps_out=tb, seqs=seq, verify=True, T=T, head="hidden")
         m.rollback(hc, torch.full((1,), acc, **i32), 1, T)
+        lw = tw["layers"][l]
         state, ref_state = hc.state[0][0].cpu(), oc[l].state
         rel = ((state - ref_state).abs().max() / ref_state.abs().max()).item()
         # the recurrence itself on the oracle's own q, k, v, g, beta of this layer (identical
         # inputs): prefill, then the block with snapshots, state after `acc` tokens
-        lw = tw["layers"][l]
         conv = torch.zeros((3, ot.C))
         st = torch.zeros((1, ot.Hv, ot.Dv, ot.Dk), device=DEV)
         for name, n in (("prefill", P), ("block", T)):
@@ -215,16 +236,26 @@ def test_qwen35_27b_width_gdn_state_teacher_forced():
                 ops.gdr_recurrence(*args, st, snapshots=snaps)
                 st = snaps[:, acc - 1]
         op_rel = ((st[0].cpu() - ref_state).abs().max() / ref_state.abs().max()).item()
-        ok_p, mx_p, _ = _within(tp.cpu(), ins[("prefill", l + 1)], ulps=2)
-        ok_b, mx_b, _ = _within(tb.cpu(), ins[("block", l + 1)], ulps=2)
+        # the fp32 oracle layer on the same inputs (its own rounding sensitivity)
+        with monkeypatch.context() as mp:
+            mp.setattr(O, "bf16", lambda x: x.float())
+            c32 = O.GDNCache(ot.C, ot.Hv, ot.Dv, ot.Dk)
+            o32_p = ot.gdn_layer(lw, ins[("prefill", l)], c32)
+            o32_b = ot.gdn_layer(lw, ins[("block", l)], c32)
+            c32.state = c32.record[1][acc - 1]
+        rel32 = ((c32.state - ref_state).abs().max() / ref_state.abs().max()).item()
+        ok_p, mx_p, _, rmx_p, _ = _vs_sensitivity(tp.cpu(), ins[("prefill", l + 1)], o32_p)
+        ok_b, mx_b, _, rmx_b, _ = _vs_sensitivity(tb.cpu(), ins[("block", l + 1)], o32_b)
         ok_c, conv_d, _ = _within(hc.conv[0][0].cpu(), oc[l].conv, ulps=1)
         print(f"gdn layer {l}: recurrence on identical inputs: state rel err {op_rel:.2e}; whole layer: state rel "
-              f"err {rel:.2e}, output max err prefill {mx_p:.4f} block {mx_b:.4f}, conv state max err {conv_d:.2e}")
+              f"err {rel:.2e} (oracle fp32 vs bf16 {rel32:.2e}), output max err prefill {mx_p:.4f} (oracle "
+              f"{rmx_p:.4f}) block {mx_b:.4f} (oracle {rmx_b:.4f}), conv state max err {conv_d:.2e}")
         # north_star's 1e-3 on the fp32 state holds for the recurrence on identical inputs; the
         # whole layer's q, k, v are bf16 projections whose roundings can differ by one ulp from
-        # the oracle's (fp32 sums in another order), which moves the state by ~2^-9 relative
+        # the oracle's (fp32 sums in another order), which moves the state by ~2^-9 relative:
+        # the layer's state must then stay within the oracle's own bf16-vs-fp32 spread
         assert op_rel <= 1e-3, (l, op_rel)
-        assert rel <= 1e-2, (l, rel)
+        assert rel <= max(1e-3, 1.5 * rel32), (l, rel, rel32)
         assert ok_p and ok_b, (l, mx_p, mx_b)
         assert ok_c, (l, conv_d)  # the conv state holds bf16 projection rows
         del m, hc

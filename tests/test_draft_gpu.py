@@ -31,9 +31,10 @@ def _ulp(x: torch.Tensor) -> torch.Tensor:
     return torch.pow(2.0, e - 7)
 
 
-def _draft_calls(tcfg, dcfg, tw, dw, mask_mode, ctx_rows, seed):
-    """Runs the GPU draft and the oracle draft over the same calls; returns per call
-    (gpu hidden, oracle hidden, gpu logits of rows 1.., oracle logits of rows 1..)."""
+def _draft_calls(tcfg, dcfg, tw, dw, mask_mode, ctx_rows, seed, monkeypatch):
+    """Runs the GPU draft, the oracle draft and the oracle draft in fp32 arithmetic (its
+    own rounding sensitivity) over the same calls; returns per call (gpu hidden, oracle
+    hidden, fp32 oracle hidden, gpu logits of rows 1.., oracle logits, fp32 oracle logits)."""
     from oracle import dflash_oracle as O
     from dflash_b200.model import DraftModel, TargetModel
     target = TargetModel(tcfg, tw, DEV)
@@ -45,6 +46,7 @@ def _draft_calls(tcfg, dcfg, tw, dw, mask_mode, ctx_rows, seed):
     cap = sum(ctx_rows) + 2 * bs
     cache = draft.make_cache(1, cap)
     ocache = od.make_cache(cap)
+    ocache32 = od.make_cache(cap)
     g = torch.Generator().manual_seed(seed)
     # taps: residual-stream-like rows (bf16, unit scale)
     taps_all = torch.randn(sum(ctx_rows), ntaps * H, generator=g).to(torch.bfloat16)
@@ -64,49 +66,52 @@ def _draft_calls(tcfg, dcfg, tw, dw, mask_mode, ctx_rows, seed):
         lg = draft.forward_block(toks, pos_blk, cache, kv_len, cap, head="logits")[1:].float().cpu()
         dh = od(ot.embed_tokens(block), ctx.float(), ocache)
         olg = ot.lm_head_logits(dh[1:])
-        for c in ocache:
+        with monkeypatch.context() as mp:
+            mp.setattr(O, "bf16", lambda x: x.float())
+            dh32 = od(ot.embed_tokens(block), ctx.float(), ocache32)
+            olg32 = ot.lm_head_logits(dh32[1:])
+        for c in ocache + ocache32:
             c.trim(bs)  # trim_draft_cache (runtime.py:32-34, 420)
-        out.append((hid, dh, lg, olg))
+        out.append((hid, dh, dh32, lg, olg, olg32))
         off += Tc
     return out
 
 
 def _check(calls, what, tol=2e-2):
-    for i, (hid, ref_h, lg, ref_lg) in enumerate(calls):  # all calls reported before any assertion
-        dh, dl = (hid - ref_h).abs(), (lg - ref_lg).abs()
-        print(f"{what} call {i}: hidden max err {dh.max().item():.4f} mean {dh.mean().item():.2e}; logits max err "
-              f"{dl.max().item():.4f}; proposals equal {int((lg.argmax(-1) == ref_lg.argmax(-1)).sum())}/{len(lg)}")
-    for i, (hid, ref_h, lg, ref_lg) in enumerate(calls):
-        dh = (hid - ref_h).abs()
-        dl = (lg - ref_lg).abs()
+    """Every value within the oracle's own rounding sensitivity (mean |gpu - oracle| <= mean
+    |oracle_fp32 - oracle| and max <= 1.5 x its max) or within one bf16 ulp; proposals equal
+    except at near-ties (top-two oracle logits within 2 x tol)."""
+    bad = []
+    for i, (hid, ref_h, h32, lg, ref_lg, l32) in enumerate(calls):
         prop, ref_prop = lg.argmax(-1), ref_lg.argmax(-1)
         top2 = ref_lg.topk(2, dim=-1).values
         gap = top2[:, 0] - top2[:, 1]
         mism = prop != ref_prop
-        print(f"{what} call {i}: hidden max err {dh.max().item():.4f} (max|ref| {ref_h.abs().max().item():.2f}, "
-              f"mean {dh.mean().item():.2e}); logits max err {dl.max().item():.4f} (max|ref| "
-              f"{ref_lg.abs().max().item():.2f}); proposals equal {int((~mism).sum())}/{len(prop)}")
-        # every value within the stated tolerance, or within one bf16 ulp of the reference
-        # value where that ulp is larger (|value| >= 4)
-        assert bool(((dh <= tol) | (dh <= _ulp(ref_h))).all()), (what, i, "hidden")
-        assert bool(((dl <= tol) | (dl <= _ulp(ref_lg))).all()), (what, i, "logits")
-        assert dh.mean().item() <= 2e-3, (what, i)
-        # a proposal may differ only where the oracle's top two logits are within the
-        # logit tolerance of each other (a bf16 near-tie)
-        assert bool((gap[mism] <= 2 * tol).all()), (what, i, gap[mism])
+        for name, got, ref, r32 in (("hidden", hid, ref_h, h32), ("logits", lg, ref_lg, l32)):
+            d, r = (got - ref).abs(), (r32 - ref).abs()
+            ok = (d.mean() <= r.mean() and d.max() <= 1.5 * r.max()) or bool((d <= _ulp(ref)).all())
+            print(f"{what} call {i} {name}: gpu vs oracle max {d.max().item():.4f} mean {d.mean().item():.2e}; "
+                  f"oracle fp32 vs bf16 max {r.max().item():.4f} mean {r.mean().item():.2e}")
+            if not ok:
+                bad.append((i, name))
+        print(f"{what} call {i}: proposals equal {int((~mism).sum())}/{len(prop)}")
+        if not bool((gap[mism] <= 2 * tol).all()):
+            bad.append((i, "proposals", gap[mism].tolist()))
+    assert not bad, (what, bad)
 
 
 @pytest.mark.parametrize("mask_mode", ["none", "causal"])
-def test_tiny_draft_matches_oracle(mask_mode):
+def test_tiny_draft_matches_oracle(mask_mode, monkeypatch):
     from dflash_b200.config import tiny_pair
     from dflash_b200.weights import random_draft_weights, random_target_weights
     tcfg, dcfg = tiny_pair()
     tw, dw = random_target_weights(tcfg, 0), random_draft_weights(dcfg, 0)
-    _check(_draft_calls(tcfg, dcfg, tw, dw, mask_mode, [64, 5, 8], seed=11), f"tiny/{mask_mode}")
+    _check(_draft_calls(tcfg, dcfg, tw, dw, mask_mode, [64, 5, 8], seed=11, monkeypatch=monkeypatch),
+           f"tiny/{mask_mode}")
 
 
 @pytest.mark.parametrize("mask_mode", ["none", "causal"])
-def test_qwen3_4b_width_draft_matches_oracle(mask_mode):
+def test_qwen3_4b_width_draft_matches_oracle(mask_mode, monkeypatch):
     """The config-3 draft: 5 layers at Qwen3-4B width, 5 taps (12800 -> 2560 fc), block 16,
     lm_head over the 151936-token vocabulary."""
     import dataclasses
@@ -115,7 +120,8 @@ def test_qwen3_4b_width_draft_matches_oracle(mask_mode):
     tcfg, dcfg = qwen3_4b_pair()
     tcfg = dataclasses.replace(tcfg, num_hidden_layers=1)  # the draft uses the target's embedding only
     tw, dw = random_target_weights(tcfg, 2), random_draft_weights(dcfg, 2)
-    _check(_draft_calls(tcfg, dcfg, tw, dw, mask_mode, [40, 7, 16], seed=12), f"qwen3-4b/{mask_mode}")
+    _check(_draft_calls(tcfg, dcfg, tw, dw, mask_mode, [40, 7, 16], seed=12, monkeypatch=monkeypatch),
+           f"qwen3-4b/{mask_mode}")
 
 
 def test_tiny_real_draft_acceptance_matches_oracle_loop():

@@ -5,7 +5,8 @@ Qwen3-4B depth (a bf16 ulp of 0.25) and logits reach 5-6 (an ulp of 0.03), so an
 bound of 2e-2 is below bf16 resolution there; what a correct bf16 kernel must meet is
 "no further from the oracle than the oracle's bf16 arithmetic is from its own fp32
 arithmetic on the same inputs" (d_gpu = |gpu - oracle|, d_ref = |oracle_fp32 - oracle|:
-mean d_gpu <= mean d_ref and max d_gpu <= 1.5 max d_ref), or within one bf16 ulp.
+mean d_gpu <= mean d_ref, and every element's d_gpu <= 1.5 max d_ref or within one bf16
+ulp of the oracle's value).
 
 * Qwen3-4B (config 3), all 36 layers, teacher forced: every GPU layer is fed the oracle's
   input (a 48-row prefill, then a 16-row verify block over the cached prefix); then the
@@ -57,10 +58,10 @@ def _cpu_weights(cfg, seed):
 
 def _vs_sensitivity(got: torch.Tensor, ref: torch.Tensor, ref32: torch.Tensor):
     """(ok, max d_gpu, mean d_gpu, max d_ref, mean d_ref): the yardstick of the module
-    docstring, or every element within one bf16 ulp of the reference."""
+    docstring."""
     d = (got.float() - ref.float()).abs()
     r = (ref32.float() - ref.float()).abs()
-    ok = (d.mean() <= r.mean() and d.max() <= 1.5 * r.max()) or bool((d <= _ulp(ref)).all())
+    ok = bool(d.mean() <= r.mean()) and bool((d <= torch.clamp(_ulp(ref), min=1.5 * r.max())).all())
     return bool(ok), d.max().item(), d.mean().item(), r.max().item(), r.mean().item()
 
 

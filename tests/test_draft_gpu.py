@@ -78,9 +78,10 @@ def _draft_calls(tcfg, dcfg, tw, dw, mask_mode, ctx_rows, seed, monkeypatch):
 
 
 def _check(calls, what, tol=2e-2):
-    """Every value within the oracle's own rounding sensitivity (mean |gpu - oracle| <= mean
-    |oracle_fp32 - oracle| and max <= 1.5 x its max) or within one bf16 ulp; proposals equal
-    except at near-ties (top-two oracle logits within 2 x tol)."""
+    """Within the oracle's own rounding sensitivity: mean |gpu - oracle| <= mean
+    |oracle_fp32 - oracle|, and every element within 1.5 x the latter's max or within one
+    bf16 ulp of the oracle's value; proposals equal except at near-ties (top-two oracle
+    logits within 2 x tol)."""
     bad = []
     for i, (hid, ref_h, h32, lg, ref_lg, l32) in enumerate(calls):
         prop, ref_prop = lg.argmax(-1), ref_lg.argmax(-1)
@@ -89,7 +90,7 @@ def _check(calls, what, tol=2e-2):
         mism = prop != ref_prop
         for name, got, ref, r32 in (("hidden", hid, ref_h, h32), ("logits", lg, ref_lg, l32)):
             d, r = (got - ref).abs(), (r32 - ref).abs()
-            ok = (d.mean() <= r.mean() and d.max() <= 1.5 * r.max()) or bool((d <= _ulp(ref)).all())
+            ok = bool(d.mean() <= r.mean()) and bool((d <= torch.clamp(_ulp(ref), min=1.5 * r.max())).all())
             print(f"{what} call {i} {name}: gpu vs oracle max {d.max().item():.4f} mean {d.mean().item():.2e}; "
                   f"oracle fp32 vs bf16 max {r.max().item():.4f} mean {r.mean().item():.2e}")
             if not ok:

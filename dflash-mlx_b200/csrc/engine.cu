@@ -19,6 +19,7 @@
 #include "common.cuh"
 
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 
@@ -77,6 +78,9 @@ struct Ctx {
   size_t wide_ws_bytes = 0;
   void* attn_ws = nullptr;
   size_t attn_ws_bytes = 0;
+  void* chain_ws = nullptr;
+  size_t chain_ws_bytes = 0;
+  bool use_chain = true;
   // inject
   const int *inj_tok = nullptr, *inj_len = nullptr, *inj_noise = nullptr;
   int64_t inj_tok_stride = 0, inj_len_stride = 0, inj_noise_stride = 0;
@@ -136,6 +140,44 @@ int gemm(Ctx* c, const void* x, int64_t ldx, const void* w, int M, int N, int K,
 
 size_t kv_layer_elems(const Ctx* c, int hkv, int hd) { return (size_t)c->B * hkv * c->cap * hd; }
 
+// One dfl_gemm_op (the arguments of gemm() above).
+dfl_gemm_op gop(const void* x, int64_t ldx, const void* w, int M, int N, int K, int epi, const void* res, int64_t ldr,
+                void* y, int64_t ldy, void* y2, int64_t ldy2, void* part, const void* norm_w, const float* ss_in,
+                float* ss_out, float eps) {
+  dfl_gemm_op o;
+  o.x = x;
+  o.ldx = ldx;
+  o.w_packed = w;
+  o.M = M;
+  o.N = N;
+  o.K = K;
+  o.epilogue = epi;
+  o.residual = res;
+  o.ldr = ldr;
+  o.y = y;
+  o.ldy = ldy;
+  o.y2 = y2;
+  o.ldy2 = ldy2;
+  o.argmax_partials = part;
+  o.norm_w = norm_w;
+  o.sumsq_in = ss_in;
+  o.n_parts = norm_w ? K / 32 : 0;
+  o.eps = eps;
+  o.sumsq_out = ss_out;
+  return o;
+}
+
+// Whether a forward over M rows runs its projections as GEMM chains (the Python host's
+// rule, model.chain_ok: decode blocks of the one-sequence kernel forms).
+bool chain_ok(const Ctx* c, int M) { return c->use_chain && M <= 16 && !c->batched; }
+
+int run_chain(Ctx* c, std::vector<dfl_gemm_op>& ops, cudaStream_t s) {
+  if (ops.empty()) return DFL_OK;
+  const int st = dfl_gemm_chain(ops.data(), (int)ops.size(), c->chain_ws, c->chain_ws_bytes, s);
+  ops.clear();
+  return st;
+}
+
 // Target block forward over M rows (tokens / pos device arrays): taps into `taps` (row
 // stride ntaps*H), lm_head argmax partials into c->argmax. Mirrors TargetModel.forward.
 int target_forward(Ctx* c, const int* tokens, const int* pos, int M, const int* row_seq, int seq_rows,
@@ -146,6 +188,39 @@ int target_forward(Ctx* c, const int* tokens, const int* pos, int M, const int* 
   const int nqkv = (Hq + 2 * Hkv) * hd;
   const float eps = t.eps;
   TRY(dfl_embed_bf16(tokens, t.embed, c->h, H, M, H, t.vocab, c->ss, s));
+  if (chain_ok(c, M)) {
+    std::vector<dfl_gemm_op> ops;
+    if (t.n_layers > 0)
+      ops.push_back(gop(c->h, H, c->tl[0].w_qkv, M, nqkv, H, DFL_EPI_STORE, nullptr, 0, c->qkv, nqkv, nullptr, 0,
+                        nullptr, c->tl[0].in_norm, c->ss, nullptr, eps));
+    for (int l = 0; l < t.n_layers; ++l) {
+      const dfl_layer_weights& w = c->tl[l];
+      TRY(run_chain(c, ops, s));
+      __nv_bfloat16* kc = c->tk + (size_t)l * kv_layer_elems(c, Hkv, hd);
+      __nv_bfloat16* vc = c->tv + (size_t)l * kv_layer_elems(c, Hkv, hd);
+      TRY(dfl_qkv_rope_append(c->qkv, nqkv, hd, pos, row_seq, w.q_norm, w.k_norm, c->t_inv_freq, c->q, kc, vc,
+                              (int64_t)Hkv * c->cap * hd, (int64_t)c->cap * hd, M, Hq, Hkv, hd, t.rope_dim, eps, 1,
+                              s));
+      TRY(dfl_attention(c->q, kc, vc, (int64_t)Hkv * c->cap * hd, (int64_t)c->cap * hd, pos, row_seq, nullptr,
+                        seq_rows, M, Hq, Hkv, hd, 1, (float)(1.0 / std::sqrt((double)hd)), max_kv, c->key_chunk,
+                        c->attn, Hq * hd, nullptr, 0, 0, c->attn_ws, c->attn_ws_bytes, s));
+      void* tap = nullptr;
+      for (int i = 0; i < ntaps; ++i)
+        if (c->tap_ids[i] == l && taps) tap = taps + (size_t)i * H;
+      ops.push_back(gop(c->attn, Hq * hd, w.w_o, M, H, Hq * hd, DFL_EPI_RESIDUAL, c->h, H, c->h, H, nullptr, 0,
+                        nullptr, nullptr, nullptr, c->ss, eps));
+      ops.push_back(gop(c->h, H, w.w_gu, M, 2 * t.ffn, H, DFL_EPI_SILU_MUL, nullptr, 0, c->act, t.ffn, nullptr, 0,
+                        nullptr, w.post_norm, c->ss, nullptr, eps));
+      ops.push_back(gop(c->act, t.ffn, w.w_down, M, H, t.ffn, DFL_EPI_RESIDUAL, c->h, H, c->h, H, tap,
+                        tap ? (int64_t)ntaps * H : 0, nullptr, nullptr, nullptr, c->ss, eps));
+      if (l + 1 < t.n_layers)
+        ops.push_back(gop(c->h, H, c->tl[l + 1].w_qkv, M, nqkv, H, DFL_EPI_STORE, nullptr, 0, c->qkv, nqkv, nullptr,
+                          0, nullptr, c->tl[l + 1].in_norm, c->ss, nullptr, eps));
+    }
+    ops.push_back(gop(c->h, H, t.lm_head, M, t.vocab, H, DFL_EPI_ARGMAX, nullptr, 0, nullptr, 0, nullptr, 0,
+                      c->argmax, t.final_norm, c->ss, nullptr, eps));
+    return run_chain(c, ops, s);
+  }
   for (int l = 0; l < t.n_layers; ++l) {
     const dfl_layer_weights& w = c->tl[l];
     __nv_bfloat16* kc = c->tk + (size_t)l * kv_layer_elems(c, Hkv, hd);
@@ -179,10 +254,19 @@ int draft_ingest(Ctx* c, const __nv_bfloat16* taps, const int* pos, int M, const
   const int H = d.hidden, hd = d.head_dim, Hkv = d.n_kv_heads;
   const int ntaps = d.n_taps;
   const int per = 2 * Hkv * hd, nkv = d.n_layers * per;
-  TRY(gemm(c, taps, (int64_t)ntaps * H, d.fc, M, H, ntaps * H, DFL_EPI_STORE, nullptr, 0, c->dfc, H, nullptr, 0,
-           nullptr, nullptr, nullptr, c->dss_ctx, d.eps, s));
-  TRY(gemm(c, c->dfc, H, d.w_ctx_kv, M, nkv, H, DFL_EPI_STORE, nullptr, 0, c->dkvp, nkv, nullptr, 0, nullptr,
-           d.hidden_norm, c->dss_ctx, nullptr, d.eps, s));
+  if (chain_ok(c, M)) {
+    std::vector<dfl_gemm_op> ops;
+    ops.push_back(gop(taps, (int64_t)ntaps * H, d.fc, M, H, ntaps * H, DFL_EPI_STORE, nullptr, 0, c->dfc, H, nullptr,
+                      0, nullptr, nullptr, nullptr, c->dss_ctx, d.eps));
+    ops.push_back(gop(c->dfc, H, d.w_ctx_kv, M, nkv, H, DFL_EPI_STORE, nullptr, 0, c->dkvp, nkv, nullptr, 0, nullptr,
+                      d.hidden_norm, c->dss_ctx, nullptr, d.eps));
+    TRY(run_chain(c, ops, s));
+  } else {
+    TRY(gemm(c, taps, (int64_t)ntaps * H, d.fc, M, H, ntaps * H, DFL_EPI_STORE, nullptr, 0, c->dfc, H, nullptr, 0,
+             nullptr, nullptr, nullptr, c->dss_ctx, d.eps, s));
+    TRY(gemm(c, c->dfc, H, d.w_ctx_kv, M, nkv, H, DFL_EPI_STORE, nullptr, 0, c->dkvp, nkv, nullptr, 0, nullptr,
+             d.hidden_norm, c->dss_ctx, nullptr, d.eps, s));
+  }
   for (int l = 0; l < d.n_layers; ++l) {
     __nv_bfloat16* kc = c->dk + (size_t)l * kv_layer_elems(c, Hkv, hd);
     __nv_bfloat16* vc = c->dv + (size_t)l * kv_layer_elems(c, Hkv, hd);
@@ -202,6 +286,35 @@ int draft_block(Ctx* c, cudaStream_t s) {
   const float eps = d.eps;
   const int* rs = c->B > 1 ? c->row_seq : nullptr;
   TRY(dfl_embed_bf16(c->block, c->t.embed, c->dh, H, M, H, c->t.vocab, c->dss, s));
+  if (chain_ok(c, M)) {
+    std::vector<dfl_gemm_op> ops;
+    if (d.n_layers > 0)
+      ops.push_back(gop(c->dh, H, c->dl[0].w_qkv, M, nqkv, H, DFL_EPI_STORE, nullptr, 0, c->dqkv, nqkv, nullptr, 0,
+                        nullptr, c->dl[0].in_norm, c->dss, nullptr, eps));
+    for (int l = 0; l < d.n_layers; ++l) {
+      const dfl_layer_weights& w = c->dl[l];
+      TRY(run_chain(c, ops, s));
+      __nv_bfloat16* kc = c->dk + (size_t)l * kv_layer_elems(c, Hkv, hd);
+      __nv_bfloat16* vc = c->dv + (size_t)l * kv_layer_elems(c, Hkv, hd);
+      TRY(dfl_qkv_rope_append(c->dqkv, nqkv, hd, c->dpos_blk, rs, w.q_norm, w.k_norm, c->d_inv_freq, c->dq, kc, vc,
+                              (int64_t)Hkv * c->cap * hd, (int64_t)c->cap * hd, M, Hq, Hkv, hd, hd, eps, 1, s));
+      TRY(dfl_attention(c->dq, kc, vc, (int64_t)Hkv * c->cap * hd, (int64_t)c->cap * hd, c->dpos_blk, rs,
+                        c->dkv_len, c->bs, M, Hq, Hkv, hd, d.causal, (float)(1.0 / std::sqrt((double)hd)), c->cap,
+                        c->key_chunk, c->dattn, Hq * hd, nullptr, 0, 0, c->attn_ws, c->attn_ws_bytes, s));
+      ops.push_back(gop(c->dattn, Hq * hd, w.w_o, M, H, Hq * hd, DFL_EPI_RESIDUAL, c->dh, H, c->dh, H, nullptr, 0,
+                        nullptr, nullptr, nullptr, c->dss, eps));
+      ops.push_back(gop(c->dh, H, w.w_gu, M, 2 * d.ffn, H, DFL_EPI_SILU_MUL, nullptr, 0, c->dact, d.ffn, nullptr, 0,
+                        nullptr, w.post_norm, c->dss, nullptr, eps));
+      ops.push_back(gop(c->dact, d.ffn, w.w_down, M, H, d.ffn, DFL_EPI_RESIDUAL, c->dh, H, c->dh, H, nullptr, 0,
+                        nullptr, nullptr, nullptr, c->dss, eps));
+      if (l + 1 < d.n_layers)
+        ops.push_back(gop(c->dh, H, c->dl[l + 1].w_qkv, M, nqkv, H, DFL_EPI_STORE, nullptr, 0, c->dqkv, nqkv, nullptr,
+                          0, nullptr, c->dl[l + 1].in_norm, c->dss, nullptr, eps));
+    }
+    ops.push_back(gop(c->dh, H, c->t.lm_head, M, c->t.vocab, H, DFL_EPI_ARGMAX, nullptr, 0, nullptr, 0, nullptr, 0,
+                      c->dargmax, d.final_norm, c->dss, nullptr, eps));
+    return run_chain(c, ops, s);
+  }
   for (int l = 0; l < d.n_layers; ++l) {
     const dfl_layer_weights& w = c->dl[l];
     __nv_bfloat16* kc = c->dk + (size_t)l * kv_layer_elems(c, Hkv, hd);
@@ -334,6 +447,10 @@ extern "C" int dfl_ctx_create(const dfl_qwen3_desc* target, const dfl_draft_desc
   c->key_chunk = c->batched ? 1024 : 128;
   c->wide_split_max = c->batched ? (batch < 16 ? 4 : 1) : 1;
   c->use_graph = !(flags & DFL_CTX_NO_GRAPH);
+  {
+    const char* e = getenv("DFLASH_B200_GEMM_CHAIN");
+    c->use_chain = !(e && e[0] == '0');
+  }
   c->n_stop = n_stop;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -427,7 +544,11 @@ extern "C" int dfl_ctx_create(const dfl_qwen3_desc* target, const dfl_draft_desc
     for (auto& hh : heads)
       aneed = std::max(aneed, dfl_attention_workspace_bytes(rows, hh.first, hh.second, c->cap, c->key_chunk));
   }
-  unsigned char *gw = nullptr, *ww = nullptr, *aw = nullptr;
+  unsigned char *gw = nullptr, *ww = nullptr, *aw = nullptr, *cw = nullptr;
+  const size_t chain_bytes = 6u << 20;  // as the Python host's Workspace.CHAIN_BYTES (counters + partials)
+  A(cw, chain_bytes);  // zero-filled: the chain's counters start at zero
+  c->chain_ws = cw;
+  c->chain_ws_bytes = chain_bytes;
   A(gw, gneed);  // zero-filled: the split-K counters start at zero
   A(aw, aneed);
   c->gemm_ws = gw;

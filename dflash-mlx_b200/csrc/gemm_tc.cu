@@ -35,6 +35,7 @@
 //    the library's device error word and falls through to its teardown.
 #include "tma_util.cuh"
 
+#include <cstring>
 #include <mutex>
 #include <unordered_map>
 
@@ -207,7 +208,10 @@ __device__ __forceinline__ void tc_epilogue(const TcArgs& a, float* v, int m0, i
       } else {
 #pragma unroll
         for (int t = 0; t < TC_BM; ++t)
-          r[t] = (col_ok && m0 + t < a.M) ? bf2f(a.res[(long long)(m0 + t) * a.ldr + n]) : 0.f;
+          r[t] = (col_ok && m0 + t < a.M)
+                     ? __uint_as_float((uint32_t)__ldcg(reinterpret_cast<const unsigned short*>(a.res) +
+                                                        (long long)(m0 + t) * a.ldr + n) << 16)
+                     : 0.f;
       }
 #pragma unroll
       for (int t = 0; t < TC_BM; ++t) v[t] = r[t] + round_bf16(v[t]);
@@ -1236,6 +1240,333 @@ __global__ void __launch_bounds__(256) norm_apply_kernel(const __nv_bfloat16* __
   *reinterpret_cast<uint4*>(xn + (long long)m * K + k) = xv;
 }
 
+// ---------------------------------------------------------------------------
+// GEMM chain: several M <= 16 weight-streaming GEMMs, each reading the previous one's
+// output, in one persistent launch (the projections between two attention calls of a
+// verify or draft forward: o_proj -> gate/up -> down -> next layer's qkv).
+//
+// Each op runs as the stream-K form above (fixed unit ranges per CTA, fp32 partials of
+// split tiles summed in range order by the last arriver), so the per-op arithmetic is
+// fixed by N, K and the grid. Between ops the launch boundary is replaced by a
+// completion counter per op: a CTA adds 1 after its last epilogue store of the op, and
+// the X operand of op k + 1 is loaded only once every CTA has done so. Weights do not
+// depend on activations: each CTA's producer streams the first ring stages of op k + 1
+// before it waits, so the wait and the previous op's epilogue tail overlap the stream.
+// When the last op's counter reaches the grid size no CTA waits any more, so the CTA
+// that brings it there zeroes every counter for the next launch (which reads them only
+// after its grid-dependency wait, i.e. after this launch completed). Loads of data this
+// launch wrote (residual rows, RMSNorm partial sums) bypass L1 (ld.global.cg); the X
+// tiles come by TMA after a proxy fence on both sides of the counter. Every wait is
+// bounded (device error 310 / 311).
+// ---------------------------------------------------------------------------
+constexpr int CH_MAX_OPS = 6;
+constexpr int CH_SITE_DONE = 310;
+
+struct ChainMaps {
+  CUtensorMap m[CH_MAX_OPS];
+};
+struct ChainArgs {
+  TcArgs op[CH_MAX_OPS];
+  int epi[CH_MAX_OPS];
+  int n_ops;
+  int* done;   // [CH_MAX_OPS] completion counters (zero between launches)
+  int* err;
+};
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_gpu_add(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;\n" ::: "memory");
+}
+// bounded wait until every CTA has finished op k of this launch
+__device__ __forceinline__ bool chain_wait_done(const ChainArgs& c, int k, int target) {
+  if (ld_acquire_gpu(c.done + k) >= target) return true;
+  const long long t0 = clock64();
+  while (ld_acquire_gpu(c.done + k) < target) {
+    if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
+      atomicCAS(c.err, 0, CH_SITE_DONE);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void chain_epilogue(int epi, const TcArgs& a, float* v, int nt, int q, int lane, float* xchg) {
+  switch (epi) {
+    case DFL_EPI_STORE: tc_epilogue<DFL_EPI_STORE>(a, v, 0, nt, q, lane, xchg); break;
+    case DFL_EPI_RESIDUAL: tc_epilogue<DFL_EPI_RESIDUAL>(a, v, 0, nt, q, lane, xchg); break;
+    case DFL_EPI_SILU_MUL: tc_epilogue<DFL_EPI_SILU_MUL>(a, v, 0, nt, q, lane, xchg); break;
+    case DFL_EPI_ARGMAX: tc_epilogue<DFL_EPI_ARGMAX>(a, v, 0, nt, q, lane, xchg); break;
+    default: tc_epilogue<DFL_EPI_STORE_F32>(a, v, 0, nt, q, lane, xchg); break;
+  }
+}
+
+__global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
+    gemm_chain_kernel(const __grid_constant__ ChainMaps maps, const __grid_constant__ ChainArgs c) {
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + TC_OFF_BAR);
+  uint64_t* empty = full + TC_STAGES;
+  uint64_t* xready = empty + TC_STAGES;
+  uint64_t* accf = xready + TC_STAGES;  // [2]
+  uint64_t* acce = accf + 2;            // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + TC_OFF_TMEM);
+  float* xchg = reinterpret_cast<float*>(smem + TC_OFF_XCHG);
+  __nv_bfloat16* s_nw = reinterpret_cast<__nv_bfloat16*>(smem + TC_OFF_NORM);
+  __shared__ float s_inv[TC_BM];
+  __shared__ int s_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = gridDim.x, cta = blockIdx.x;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < TC_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      mbar_init(&xready[s], 128);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf[b], 1);
+      mbar_init(&acce[b], 4);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
+                 "n"(TC_TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  grid_dependency_launch_dependents();
+
+  if (warp == 0) {
+    // ---------------- producer: weights ahead, X once the previous op is complete ----------------
+    if (lane == 0) {
+      const uint64_t pol_w = l2_policy_evict_first();
+      const uint64_t pol_x = l2_policy_evict_last();
+      int g = 0;  // ring position over every op's units
+      const int target = G;
+      bool ok = true;
+      for (int k = 0; k < c.n_ops && ok; ++k) {
+        const TcArgs& a = c.op[k];
+        const long long u0 = (long long)cta * a.U1 / G, u1 = (long long)(cta + 1) * a.U1 / G;
+        const int n_units = (int)(u1 - u0);
+        const int pre = n_units < TC_STAGES ? n_units : TC_STAGES;
+        for (int i = 0; i < pre && ok; ++i) {
+          const int s = (g + i) % TC_STAGES;
+          if (g + i >= TC_STAGES && !mbar_wait(&empty[s], (((g + i) / TC_STAGES) & 1) ^ 1, 211, c.err)) ok = false;
+          if (!ok) break;
+          mbar_expect_tx(&full[s], TC_W_BYTES + TC_X_BYTES);
+          bulk_load(smem + s * TC_W_BYTES, a.wt + (u0 + i) * TC_W_BYTES, TC_W_BYTES, &full[s], pol_w);
+        }
+        if (!ok) break;
+        if (k == 0) {
+          grid_dependency_wait();  // op 0's X comes from earlier launches
+        } else {
+          chain_wait_done(c, k - 1, target);
+          fence_proxy_async_global();  // generic-proxy stores of op k - 1 -> this CTA's TMA reads
+        }
+        for (int i = 0; i < pre; ++i)
+          tma_load_2d(&maps.m[k], &full[(g + i) % TC_STAGES], smem + TC_OFF_X + ((g + i) % TC_STAGES) * TC_X_BYTES,
+                      (int)((u0 + i) % a.kb) * TC_BK, 0, pol_x);
+        for (int i = pre; i < n_units; ++i) {
+          const int s = (g + i) % TC_STAGES;
+          if (!mbar_wait(&empty[s], (((g + i) / TC_STAGES) & 1) ^ 1, 212, c.err)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&full[s], TC_W_BYTES + TC_X_BYTES);
+          bulk_load(smem + s * TC_W_BYTES, a.wt + (u0 + i) * TC_W_BYTES, TC_W_BYTES, &full[s], pol_w);
+          tma_load_2d(&maps.m[k], &full[s], smem + TC_OFF_X + s * TC_X_BYTES, (int)((u0 + i) % a.kb) * TC_BK, 0,
+                      pol_x);
+        }
+        g += n_units;
+      }
+      if (!ok) {  // gave up: let the copies in flight land before the CTA exits
+        for (int i = g > TC_STAGES ? g - TC_STAGES : 0; i < g; ++i)
+          mbar_wait(&full[i % TC_STAGES], (i / TC_STAGES) & 1, 219, c.err);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t w0 = smem_u32(smem), x0 = smem_u32(smem + TC_OFF_X);
+      int g = 0, seg = -1;
+      bool ok = true;
+      for (int k = 0; k < c.n_ops && ok; ++k) {
+        const TcArgs& a = c.op[k];
+        const bool norm = a.norm_w != nullptr;
+        const long long u0 = (long long)cta * a.U1 / G, u1 = (long long)(cta + 1) * a.U1 / G;
+        const int n_units = (int)(u1 - u0);
+        for (int i = 0; i < n_units; ++i, ++g) {
+          const long long u = u0 + i;
+          const int j = (int)(u % a.kb);
+          const int s = g % TC_STAGES;
+          const bool first = (i == 0) || (j == 0);
+          if (first) {
+            ++seg;
+            if (!mbar_wait(&acce[seg & 1], ((seg >> 1) & 1) ^ 1, 213, c.err)) { ok = false; break; }
+            tc_fence_after();
+          }
+          if (!mbar_wait(norm ? &xready[s] : &full[s], (g / TC_STAGES) & 1, 214, c.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t d = tmem + (uint32_t)((seg & 1) * TC_NACC * TC_BM);
+          const uint64_t ad = sw128_desc(w0 + s * TC_W_BYTES);
+          const uint64_t bd = sw128_desc(x0 + s * TC_X_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < TC_BK / 16; ++kk)
+            tc_mma(d + (uint32_t)((kk % TC_NACC) * TC_BM), ad + 2 * kk, bd + 2 * kk, TC_IDESC,
+                   (first && kk < TC_NACC) ? 0u : 1u);
+          tc_commit(&empty[s]);
+          if (j == a.kb - 1 || i == n_units - 1) tc_commit(&accf[seg & 1]);
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue warps (and the fused RMSNorm rescale) ----------------
+    const int et = threadIdx.x - 32 * TC_EPI_WARP0;  // 0..127
+    const int q = warp & 3;
+    grid_dependency_wait();
+    const int target = G;
+    int g = 0, seg = -1;
+    bool ok = true;
+    for (int k = 0; k < c.n_ops; ++k) {
+      const TcArgs& a = c.op[k];
+      const bool norm = a.norm_w != nullptr;
+      const long long u0 = (long long)cta * a.U1 / G, u1 = (long long)(cta + 1) * a.U1 / G;
+      const int n_units = (int)(u1 - u0);
+      if (norm && n_units > 0) {
+        if (k > 0 && et == 0) chain_wait_done(c, k - 1, target);  // the RMSNorm sums of op k - 1
+        epi_sync();  // also: every epilogue thread is done with the previous op's norm weights
+        for (int kk = et * 8; kk < a.K; kk += 128 * 8)
+          *reinterpret_cast<uint4*>(s_nw + kk) = *reinterpret_cast<const uint4*>(a.norm_w + kk);
+        if (et < TC_BM) {
+          float ss = 0.f;
+          if (et < a.M)
+            for (int p = 0; p < a.n_parts; ++p) ss += __ldcg(a.sumsq_in + (long long)et * a.n_parts + p);
+          s_inv[et] = rsqrtf(ss / (float)a.K + a.eps);
+        }
+        epi_sync();
+      }
+      if (ok)
+        for (int i = 0; i < n_units; ++i, ++g) {
+          const long long u = u0 + i;
+          const int nt = (int)(u / a.kb), j = (int)(u % a.kb);
+          const int s = g % TC_STAGES;
+          if (i == 0 || j == 0) ++seg;
+          if (norm) {
+            if (!mbar_wait(&full[s], (g / TC_STAGES) & 1, 215, c.err)) { ok = false; break; }
+            const int row = et >> 3, cc = et & 7;
+            __nv_bfloat16* p = reinterpret_cast<__nv_bfloat16*>(smem + TC_OFF_X + s * TC_X_BYTES) + row * 64 +
+                               ((cc ^ (row & 7)) << 3);
+            uint4 xv = *reinterpret_cast<uint4*>(p);
+            const uint4 wv = *reinterpret_cast<const uint4*>(s_nw + j * TC_BK + cc * 8);
+            __nv_bfloat16* xe = reinterpret_cast<__nv_bfloat16*>(&xv);
+            const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv);
+            const float inv = s_inv[row];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) xe[e] = f2bf(bf2f(we[e]) * (bf2f(xe[e]) * inv));
+            *reinterpret_cast<uint4*>(p) = xv;
+            fence_proxy_async_smem();
+            mbar_arrive(&xready[s]);
+          }
+          const bool seg_end = (j == a.kb - 1) || (i == n_units - 1);
+          if (!seg_end) continue;
+          if (!mbar_wait(&accf[seg & 1], (seg >> 1) & 1, 216, c.err)) { ok = false; break; }
+          tc_fence_after();
+          float v[TC_BM];
+          tc_ld_acc(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((seg & 1) * TC_NACC * TC_BM), v);
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acce[seg & 1]);
+          const long long tu0 = (long long)nt * a.kb, tu1 = tu0 + a.kb - 1;
+          const int c_first = tc_unit_owner(tu0, a.U1, G), c_last = tc_unit_owner(tu1, a.U1, G);
+          bool do_epi = true;
+          const int col = q * 32 + lane;
+          if (c_first != c_last) {
+            const int slot = (nt == (int)(u0 / a.kb)) ? 0 : 1;
+            float4* mine = reinterpret_cast<float4*>(a.partial + ((long long)cta * 2 + slot) * TC_PART_FLOATS + col * TC_BM);
+#pragma unroll
+            for (int t4 = 0; t4 < TC_BM / 4; ++t4)
+              mine[t4] = make_float4(v[4 * t4], v[4 * t4 + 1], v[4 * t4 + 2], v[4 * t4 + 3]);
+            asm volatile("fence.acq_rel.gpu;\n" ::: "memory");
+            epi_sync();
+            if (et == 0) {
+              int prev;
+              asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;\n" : "=r"(prev) : "l"(a.counters + nt) : "memory");
+              s_flag = (prev == c_last - c_first);
+            }
+            epi_sync();
+            do_epi = s_flag != 0;
+            if (do_epi) {
+              asm volatile("fence.acq_rel.gpu;\n" ::: "memory");
+#pragma unroll
+              for (int t = 0; t < TC_BM; ++t) v[t] = 0.f;
+              for (int cs0 = c_first; cs0 <= c_last; cs0 += TC_PB) {
+                float4 pb[TC_PB][TC_BM / 4];
+#pragma unroll
+                for (int kq = 0; kq < TC_PB; ++kq) {
+                  const int cs = cs0 + kq;
+                  if (cs <= c_last) {
+                    const long long cs_u0 = (long long)cs * a.U1 / G;
+                    const int sl = (nt == (int)(cs_u0 / a.kb)) ? 0 : 1;
+                    const float4* src = reinterpret_cast<const float4*>(
+                        a.partial + ((long long)cs * 2 + sl) * TC_PART_FLOATS + col * TC_BM);
+#pragma unroll
+                    for (int t4 = 0; t4 < TC_BM / 4; ++t4) pb[kq][t4] = __ldcg(src + t4);
+                  }
+                }
+#pragma unroll
+                for (int kq = 0; kq < TC_PB; ++kq) {
+                  if (cs0 + kq <= c_last) {
+#pragma unroll
+                    for (int t4 = 0; t4 < TC_BM / 4; ++t4) {
+                      v[4 * t4] += pb[kq][t4].x;
+                      v[4 * t4 + 1] += pb[kq][t4].y;
+                      v[4 * t4 + 2] += pb[kq][t4].z;
+                      v[4 * t4 + 3] += pb[kq][t4].w;
+                    }
+                  }
+                }
+              }
+              if (et == 0) a.counters[nt] = 0;
+            }
+            epi_sync();
+          }
+          if (do_epi) chain_epilogue(c.epi[k], a, v, nt, q, lane, xchg);
+        }
+      // op k finished by this CTA: publish (generic stores visible to the async proxy too)
+      fence_proxy_async_global();
+      asm volatile("fence.acq_rel.gpu;\n" ::: "memory");
+      epi_sync();
+      if (et == 0) {
+        int prev;
+        asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;\n" : "=r"(prev) : "l"(c.done + k) : "memory");
+        if (k == c.n_ops - 1 && prev == target - 1)  // every CTA finished every op: reset for the next launch
+          for (int kk = 0; kk < c.n_ops; ++kk) c.done[kk] = 0;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "n"(TC_TMEM_COLS));
+  }
+}
+
 struct TcPlan {
   int n_tiles, m_tiles, kb, grid1;
   long long U1;
@@ -1715,3 +2046,112 @@ extern "C" int dfl_gemm_bf16_noalloc(const void* x, int64_t ldx, const void* w_p
                        sumsq_in, n_parts, eps, sumsq_out, scratch, NA_SCRATCH_BYTES, stream);
 }
 
+
+extern "C" size_t dfl_gemm_chain_workspace_bytes(const dfl_gemm_op* ops, int n_ops) {
+  if (!ops || n_ops <= 0 || n_ops > CH_MAX_OPS) return 0;
+  size_t tiles = 0;
+  for (int k = 0; k < n_ops; ++k) tiles += (size_t)(ops[k].N + TC_NT - 1) / TC_NT;
+  return 256 + ((tiles * sizeof(int) + 255) & ~(size_t)255) + (size_t)TC_GRID * 2 * TC_PART_FLOATS * sizeof(float);
+}
+
+extern "C" int dfl_gemm_chain(const dfl_gemm_op* ops, int n_ops, void* workspace, size_t workspace_bytes,
+                              void* stream) {
+  if (!ops || n_ops <= 0 || n_ops > CH_MAX_OPS) {
+    set_error("dfl_gemm_chain: 1..%d ops", CH_MAX_OPS);
+    return DFL_ERR_INVALID;
+  }
+  const size_t need = dfl_gemm_chain_workspace_bytes(ops, n_ops);
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255)) {
+    set_error("dfl_gemm_chain: workspace too small or unaligned (%zu < %zu bytes)", workspace_bytes, need);
+    return DFL_ERR_WORKSPACE;
+  }
+  ChainMaps maps;
+  ChainArgs c;
+  std::memset(&maps, 0, sizeof(maps));
+  std::memset(&c, 0, sizeof(c));
+  char* ws = static_cast<char*>(workspace);
+  c.done = reinterpret_cast<int*>(ws);
+  int* counters = reinterpret_cast<int*>(ws + 256);
+  size_t tiles = 0;
+  for (int k = 0; k < n_ops; ++k) tiles += (size_t)(ops[k].N + TC_NT - 1) / TC_NT;
+  float* partial = reinterpret_cast<float*>(ws + 256 + ((tiles * sizeof(int) + 255) & ~(size_t)255));
+  c.err = device_error_word();
+  c.n_ops = n_ops;
+  int max_norm_k = 0;
+  for (int k = 0; k < n_ops; ++k) {
+    const dfl_gemm_op& o = ops[k];
+    const int epi = o.epilogue;
+    if (!o.x || !o.w_packed || o.M <= 0 || o.M > TC_BM || o.N <= 0 || o.K <= 0 || o.K % TC_BK || o.N % 32 ||
+        o.ldx % 8 || (reinterpret_cast<uintptr_t>(o.x) & 15) || (reinterpret_cast<uintptr_t>(o.w_packed) & 15)) {
+      set_error("dfl_gemm_chain: op %d: needs 1 <= M <= %d, K %% 64 == 0, N %% 32 == 0, 16-byte aligned x / w", k,
+                TC_BM);
+      return DFL_ERR_UNSUPPORTED;
+    }
+    if (epi < DFL_EPI_STORE || epi > DFL_EPI_STORE_F32 || (epi == DFL_EPI_ARGMAX && !o.argmax_partials) ||
+        (epi != DFL_EPI_ARGMAX && !o.y) || (epi == DFL_EPI_RESIDUAL && !o.residual) ||
+        (epi == DFL_EPI_SILU_MUL && o.N % 64)) {
+      set_error("dfl_gemm_chain: op %d: bad epilogue %d or missing output / residual", k, epi);
+      return DFL_ERR_INVALID;
+    }
+    if (o.norm_w && (!o.sumsq_in || o.n_parts != o.K / 32 || o.K > TC_NORM_MAX_K)) {
+      set_error("dfl_gemm_chain: op %d: the RMSNorm prologue needs K/32 sumsq_in partials and K <= %d", k,
+                TC_NORM_MAX_K);
+      return DFL_ERR_INVALID;
+    }
+    const CUtensorMap* xm = tensor_map_2d_bf16(o.x, o.M, o.K, o.ldx, TC_BM, TC_BK);
+    if (!xm) return DFL_ERR_CUDA;
+    maps.m[k] = *xm;
+    TcArgs& a = c.op[k];
+    a.wt = static_cast<const unsigned char*>(o.w_packed);
+    a.res = static_cast<const __nv_bfloat16*>(o.residual);
+    a.ldr = o.ldr;
+    a.y = static_cast<__nv_bfloat16*>(o.y);
+    a.ldy = o.ldy;
+    a.y2 = static_cast<__nv_bfloat16*>(o.y2);
+    a.ldy2 = o.ldy2;
+    a.argmax = static_cast<float2*>(o.argmax_partials);
+    a.counters = counters;
+    a.partial = partial;
+    a.norm_w = static_cast<const __nv_bfloat16*>(o.norm_w);
+    a.sumsq_in = o.sumsq_in;
+    a.n_parts = o.n_parts;
+    a.eps = o.eps;
+    a.sumsq_out = o.sumsq_out;
+    a.err = c.err;
+    a.n_groups = o.N / 32;
+    a.M = o.M;
+    a.N = o.N;
+    a.K = o.K;
+    a.n_tiles = (o.N + TC_NT - 1) / TC_NT;
+    a.kb = o.K / TC_BK;
+    a.U1 = (long long)a.n_tiles * a.kb;
+    a.grid1 = TC_GRID;
+    c.epi[k] = epi;
+    counters += a.n_tiles;
+    if (o.norm_w && o.K > max_norm_k) max_norm_k = o.K;
+  }
+  static bool init[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !init[dev]) {
+    cudaFuncSetAttribute(gemm_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         TC_SMEM_BASE + TC_NORM_MAX_K * 2);
+    init[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(TC_GRID);
+  cfg.blockDim = dim3(TC_THREADS);
+  cfg.dynamicSmemBytes = TC_SMEM_BASE + (size_t)max_norm_k * 2;
+  cfg.stream = as_stream(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_chain_kernel, maps, c);
+  if (e != cudaSuccess) {
+    set_error("dfl_gemm_chain: launch failed: %s", cudaGetErrorString(e));
+    return DFL_ERR_CUDA;
+  }
+  return DFL_OK;
+}

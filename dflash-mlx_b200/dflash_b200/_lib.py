@@ -32,6 +32,8 @@ SIGNATURES: dict[str, tuple] = {
     "dfl_gemm_bf16": (c_int, [c_void_p, c_int64, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int64, c_void_p,
                               c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int, c_float, c_void_p,
                               c_void_p, c_size_t, c_void_p]),
+    "dfl_gemm_chain_workspace_bytes": (c_size_t, [c_void_p, c_int]),
+    "dfl_gemm_chain": (c_int, [c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
     "dfl_gemm_bf16_wide": (c_int, [c_void_p, c_int64, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int64,
                                    c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int, c_float,
                                    c_void_p, c_int, c_void_p, c_size_t, c_void_p]),

@@ -77,6 +77,16 @@ def alloc_kv(n_layers: int, batch: int, n_kv: int, cap: int, hd: int, device) ->
 PAGE_SIZE = 64
 
 
+def gemm_chain_enabled() -> bool:
+    return os.environ.get("DFLASH_B200_GEMM_CHAIN", "1") != "0"
+
+
+def chain_ok(M: int, ws) -> bool:
+    """Whether a forward over M rows uses GEMM chains: decode blocks of the one-sequence
+    (weight-streaming) kernel forms; decided by M and the session's kernel forms only."""
+    return M <= ops.CHAIN_MAX_ROWS and not (ws if ws is not None else ops.workspace()).wide
+
+
 def page_plan(lengths: list[int], page_size: int = PAGE_SIZE) -> tuple[torch.Tensor, int]:
     """Page table for sequences that each need ``lengths[b]`` positions: sequence b gets
     consecutive pages; table entries past a sequence's need point at one spare page (the
@@ -136,6 +146,9 @@ class TargetModel:
         # bits). Off by default: measured 3287 against 3217 us per Qwen3-4B verify step, the
         # in-CTA q/k preparation costing more than the append launch it removes.
         self.fuse_attention = os.environ.get("DFLASH_B200_FUSED_ATTENTION", "0") == "1"
+        # decode blocks (M <= 16, one-sequence kernel forms) run the projections between two
+        # attention calls as one GEMM-chain launch (DFLASH_B200_GEMM_CHAIN=0: one launch each)
+        self.use_chain = gemm_chain_enabled()
         self._bufs: dict[int, dict[str, torch.Tensor]] = {}
 
     # ------------------------------------------------------------------
@@ -197,6 +210,9 @@ class TargetModel:
         fused = (self.fuse_attention and cache.page_table is None
                  and ops.fused_attention_ok(M, row_seq, seq_rows, hd, c.rope_dim))
         pg = cache.paging
+        if self.use_chain and chain_ok(M, ws):
+            return self._forward_chain(pos, cache, max_kv, tap_col, taps_out, row_seq, head, ws, seq_rows, key_chunk,
+                                       fused, b)
         for l, lw in enumerate(self.layers):
             kc, vc = cache.layer(l)
             # input_layernorm fused into the QKV projection
@@ -225,6 +241,40 @@ class TargetModel:
             return ops.gemm(h, self.lm_head_w, ws=ws, norm_w=self.norm_w, sumsq_in=ss, eps=eps)
         return ops.gemm(h, self.lm_head_w, ops.EPI_ARGMAX, argmax_partials=b["argmax"], ws=ws, norm_w=self.norm_w,
                         sumsq_in=ss, eps=eps)
+
+    def _forward_chain(self, pos, cache, max_kv, tap_col, taps_out, row_seq, head, ws, seq_rows, key_chunk, fused, b):
+        """forward() with every run of projections between two attention calls as one
+        GEMM-chain launch: [qkv_0], then per layer [o, gate/up, down, next qkv or lm_head]."""
+        c = self.cfg
+        H, hd, Hq, Hkv = c.hidden_size, c.head_dim, c.num_attention_heads, c.num_key_value_heads
+        h, ss, eps = b["h"], b["ss"], c.rms_norm_eps
+        pg = cache.paging
+        qkv_op = lambda lw: ops.chain_op(h, lw["w_qkv"], out=b["qkv"], norm_w=lw["in_norm"], sumsq_in=ss,  # noqa
+                                         eps=eps)
+        pending = [qkv_op(self.layers[0])] if self.layers else []
+        for l, lw in enumerate(self.layers):
+            ops.gemm_chain(pending, ws)
+            kc, vc = cache.layer(l)
+            if fused:
+                ops.attention_qkv(b["qkv"], pos, lw["q_norm"], lw["k_norm"], self.inv_freq, kc, vc, Hq, eps,
+                                  max_kv, row_seq=row_seq, out=b["attn"], ws=ws, seq_rows=seq_rows,
+                                  key_chunk=key_chunk)
+            else:
+                ops.qkv_rope_append(b["qkv"], pos, lw["q_norm"], lw["k_norm"], self.inv_freq, kc, vc, Hq, Hkv, hd,
+                                    c.rope_dim, eps, q_out=b["q"], row_seq=row_seq, **pg)
+                ops.attention(b["q"], kc, vc, pos, causal=True, max_kv=max_kv, row_seq=row_seq, out=b["attn"],
+                              ws=ws, seq_rows=seq_rows, key_chunk=key_chunk, **pg)
+            tap = None
+            if l in tap_col and taps_out is not None:
+                tap = taps_out[:, tap_col[l] * H:(tap_col[l] + 1) * H]
+            pending = [ops.chain_op(b["attn"], lw["w_o"], ops.EPI_RESIDUAL, residual=h, out=h, sumsq_out=ss),
+                       ops.chain_op(h, lw["w_gu"], ops.EPI_SILU_MUL, out=b["act"], norm_w=lw["post_norm"],
+                                    sumsq_in=ss, eps=eps),
+                       ops.chain_op(b["act"], lw["w_down"], ops.EPI_RESIDUAL, residual=h, out=h, out2=tap,
+                                    sumsq_out=ss)]
+            if l + 1 < len(self.layers):
+                pending.append(qkv_op(self.layers[l + 1]))
+        return chain_head(pending, h, ss, self.lm_head_w, self.norm_w, eps, head, b, ws)
 
     def verify_gemms(self, M: int, ws: ops.Workspace | None = None) -> list[tuple]:
         """The GEMM launches of one forward over M rows, as (callable, algorithmic bytes,
@@ -261,6 +311,25 @@ class TargetModel:
         return out
 
 
+def chain_head(pending: list, h: torch.Tensor, ss: torch.Tensor, lm_head, norm_w, eps: float, head: str, b: dict,
+               ws) -> torch.Tensor:
+    """Appends the head to the last GEMM chain of a forward and runs it: "argmax" (fused
+    lm_head argmax partials), "logits" (bf16 logits) or "hidden" (final RMSNorm rows)."""
+    M = h.shape[0]
+    if head == "hidden":
+        ops.gemm_chain(pending, ws)
+        return ops.rmsnorm(h, norm_w, eps, out=b["xn"])
+    if head == "logits":
+        out = torch.empty((M, lm_head.N), dtype=torch.bfloat16, device=h.device)
+        pending.append(ops.chain_op(h, lm_head, out=out, norm_w=norm_w, sumsq_in=ss, eps=eps))
+        ops.gemm_chain(pending, ws)
+        return out
+    pending.append(ops.chain_op(h, lm_head, ops.EPI_ARGMAX, argmax_partials=b["argmax"], norm_w=norm_w, sumsq_in=ss,
+                                eps=eps))
+    ops.gemm_chain(pending, ws)
+    return b["argmax"]
+
+
 class DraftModel:
     """DFlash block-diffusion draft conditioned on target hidden-state taps (draft.py:190-223)."""
 
@@ -290,6 +359,7 @@ class DraftModel:
             ctx_kv += [lw["k_proj"].to(dev), lw["v_proj"].to(dev)]
         self.w_ctx_kv = P(torch.cat(ctx_kv, 0))
         self.inv_freq = rope_inv_freq(cfg.head_dim, cfg.rope_theta, dev)
+        self.use_chain = gemm_chain_enabled()
         self._bufs: dict[tuple, dict[str, torch.Tensor]] = {}
 
     @property
@@ -349,10 +419,15 @@ class DraftModel:
         M = taps.shape[0]
         b = self.buffers(M, "ctx")
         H, hd, Hkv = c.hidden_size, c.head_dim, c.num_key_value_heads
-        ops.gemm(taps, self.fc, out=b["fc"], ws=ws, sumsq_out=b["ss"])
-        # hidden_norm fused into the stacked k/v projection of every layer
-        ops.gemm(b["fc"], self.w_ctx_kv, out=b["kv"], ws=ws, norm_w=self.hidden_norm, sumsq_in=b["ss"],
-                 eps=c.rms_norm_eps)
+        if self.use_chain and chain_ok(M, ws):
+            ops.gemm_chain([ops.chain_op(taps, self.fc, out=b["fc"], sumsq_out=b["ss"]),
+                            ops.chain_op(b["fc"], self.w_ctx_kv, out=b["kv"], norm_w=self.hidden_norm,
+                                         sumsq_in=b["ss"], eps=c.rms_norm_eps)], ws)
+        else:
+            ops.gemm(taps, self.fc, out=b["fc"], ws=ws, sumsq_out=b["ss"])
+            # hidden_norm fused into the stacked k/v projection of every layer
+            ops.gemm(b["fc"], self.w_ctx_kv, out=b["kv"], ws=ws, norm_w=self.hidden_norm, sumsq_in=b["ss"],
+                     eps=c.rms_norm_eps)
         per = 2 * Hkv * hd
         for l, lw in enumerate(self.layers):
             kc, vc = cache.layer(l)
@@ -375,6 +450,24 @@ class DraftModel:
         h, ss, eps = b["h"], b["ss"], c.rms_norm_eps
         ops.embed(tokens, self.target.embed_w, out=h, sumsq_out=ss)
         causal = self.mask_mode == "causal"
+        if self.use_chain and chain_ok(M, ws):
+            qkv_op = lambda lw: ops.chain_op(h, lw["w_qkv"], out=b["qkv"], norm_w=lw["in_norm"],  # noqa: E731
+                                             sumsq_in=ss, eps=eps)
+            pending = [qkv_op(self.layers[0])] if self.layers else []
+            for l, lw in enumerate(self.layers):
+                ops.gemm_chain(pending, ws)
+                kc, vc = cache.layer(l)
+                ops.qkv_rope_append(b["qkv"], pos, lw["q_norm"], lw["k_norm"], self.inv_freq, kc, vc, Hq, Hkv, hd,
+                                    hd, eps, q_out=b["q"], row_seq=row_seq, **cache.paging)
+                ops.attention(b["q"], kc, vc, pos, causal=causal, max_kv=max_kv, kv_len=kv_len, row_seq=row_seq,
+                              seq_rows=seq_rows, key_chunk=key_chunk, out=b["attn"], ws=ws, **cache.paging)
+                pending = [ops.chain_op(b["attn"], lw["w_o"], ops.EPI_RESIDUAL, residual=h, out=h, sumsq_out=ss),
+                           ops.chain_op(h, lw["w_gu"], ops.EPI_SILU_MUL, out=b["act"], norm_w=lw["post_norm"],
+                                        sumsq_in=ss, eps=eps),
+                           ops.chain_op(b["act"], lw["w_down"], ops.EPI_RESIDUAL, residual=h, out=h, sumsq_out=ss)]
+                if l + 1 < len(self.layers):
+                    pending.append(qkv_op(self.layers[l + 1]))
+            return chain_head(pending, h, ss, self.target.lm_head_w, self.norm_w, eps, head, b, ws)
         for l, lw in enumerate(self.layers):
             kc, vc = cache.layer(l)
             ops.gemm(h, lw["w_qkv"], out=b["qkv"], ws=ws, norm_w=lw["in_norm"], sumsq_in=ss, eps=eps)

@@ -46,9 +46,12 @@ class Workspace:
     issued with this workspace; its RMSNorm prologue output lives in ``wide_x``.
     """
 
+    CHAIN_BYTES = 6 << 20  # dfl_gemm_chain scratch: counters + one partial tile pair per CTA
+
     def __init__(self, device: torch.device, gemm_bytes: int = 64 << 20, attn_bytes: int = 64 << 20,
                  wide: bool = False, wide_split: int = 1):
         self.device = torch.device(device)
+        self.chain = torch.zeros(self.CHAIN_BYTES, dtype=torch.uint8, device=self.device)
         self.gemm = torch.zeros(gemm_bytes, dtype=torch.uint8, device=self.device)
         self.attn = torch.empty(attn_bytes, dtype=torch.uint8, device=self.device)
         self.wide = wide
@@ -180,6 +183,52 @@ def gemm(x: torch.Tensor, w: PackedWeight | torch.Tensor, epilogue: int = EPI_ST
               ldy, _ptr(out2), ldy2, None, _ptr(norm_w), _ptr(sumsq_in), n_parts, float(eps),
               _ptr(sumsq_out), *tail, _ptr(scratch), scratch.numel(), _stream())
     return out
+
+
+class GemmOp(ctypes.Structure):
+    """dfl_gemm_op: the arguments of one dfl_gemm_bf16 call inside a dfl_gemm_chain."""
+    _fields_ = [("x", ctypes.c_void_p), ("ldx", ctypes.c_int64), ("w_packed", ctypes.c_void_p),
+                ("M", ctypes.c_int), ("N", ctypes.c_int), ("K", ctypes.c_int), ("epilogue", ctypes.c_int),
+                ("residual", ctypes.c_void_p), ("ldr", ctypes.c_int64), ("y", ctypes.c_void_p),
+                ("ldy", ctypes.c_int64), ("y2", ctypes.c_void_p), ("ldy2", ctypes.c_int64),
+                ("argmax_partials", ctypes.c_void_p), ("norm_w", ctypes.c_void_p), ("sumsq_in", ctypes.c_void_p),
+                ("n_parts", ctypes.c_int), ("eps", ctypes.c_float), ("sumsq_out", ctypes.c_void_p)]
+
+
+CHAIN_MAX_ROWS = 16
+CHAIN_MAX_OPS = 6
+
+
+def chain_op(x: torch.Tensor, w: PackedWeight, epilogue: int = EPI_STORE, residual: torch.Tensor | None = None,
+             out: torch.Tensor | None = None, out2: torch.Tensor | None = None,
+             argmax_partials: torch.Tensor | None = None, norm_w: torch.Tensor | None = None,
+             sumsq_in: torch.Tensor | None = None, eps: float = 1e-6,
+             sumsq_out: torch.Tensor | None = None) -> GemmOp:
+    """One op of a GEMM chain (the arguments of ``gemm`` without running it)."""
+    _need_cuda(x, residual, out, out2, argmax_partials, norm_w, sumsq_in, sumsq_out)
+    M, K = x.shape
+    if M > CHAIN_MAX_ROWS:
+        raise ValueError("a GEMM chain takes at most 16 rows")
+    n_parts = sumsq_in.shape[1] if (norm_w is not None and sumsq_in is not None) else 0
+    return GemmOp(_ptr(x), _row_stride(x), w.data_ptr(), M, w.N, K, epilogue, _ptr(residual),
+                  _row_stride(residual) if residual is not None else 0, _ptr(out),
+                  _row_stride(out) if out is not None else 0, _ptr(out2), _row_stride(out2) if out2 is not None else 0,
+                  _ptr(argmax_partials), _ptr(norm_w), _ptr(sumsq_in), n_parts, float(eps), _ptr(sumsq_out))
+
+
+def gemm_chain(op_list: list[GemmOp], ws: Workspace | None = None) -> None:
+    """Runs up to six decode-block GEMMs (M <= 16), each reading the previous one's output,
+    as one persistent launch (dfl_gemm_chain)."""
+    if not op_list:
+        return
+    if len(op_list) > CHAIN_MAX_OPS:
+        raise ValueError(f"a GEMM chain holds at most {CHAIN_MAX_OPS} ops")
+    ws = ws or workspace()
+    arr = (GemmOp * len(op_list))(*op_list)
+    need = int(_lib.query("dfl_gemm_chain_workspace_bytes", arr, len(op_list)))
+    if need > ws.chain.numel():
+        raise ValueError(f"GEMM chain scratch too small ({ws.chain.numel()} < {need})")
+    _lib.call("dfl_gemm_chain", arr, len(op_list), _ptr(ws.chain), ws.chain.numel(), _stream())
 
 
 _SMS: dict[int, int] = {}

@@ -108,6 +108,38 @@ int dfl_gemm_bf16_wide(const void* x, int64_t ldx, const void* w_packed, int M, 
                        void* argmax_partials, const void* norm_w, const float* sumsq_in, int n_parts, float eps,
                        float* sumsq_out, int k_split, void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- GEMM chain (decode blocks, M <= 16) --------------------------------------
+ * Up to 6 dfl_gemm_bf16 calls, each usually reading the previous one's output, in one
+ * persistent launch: the projections between two attention calls of a verify or draft
+ * forward (o_proj -> gate/up -> down -> next layer's qkv; the same calls the reference's
+ * mlx-lm qwen3 layers make, adapters.py:611-631, draft.py:173-187). Op k + 1 starts
+ * streaming its weights while op k finishes; its X operand is read only after every CTA
+ * completed op k. Arguments of each op as dfl_gemm_bf16 (1 <= M <= 16). A row's result
+ * depends on N and K only (fixed unit ranges over a fixed grid), but is not
+ * bit-identical to dfl_gemm_bf16's, so runs compared bit for bit use one form.
+ * Workspace: dfl_gemm_chain_workspace_bytes, 256-byte aligned, zero-filled once (the
+ * kernel leaves its counters at zero); one workspace per stream. */
+typedef struct dfl_gemm_op {
+  const void* x;
+  int64_t ldx;
+  const void* w_packed;
+  int M, N, K, epilogue;
+  const void* residual;
+  int64_t ldr;
+  void* y;
+  int64_t ldy;
+  void* y2;
+  int64_t ldy2;
+  void* argmax_partials;
+  const void* norm_w;
+  const float* sumsq_in;
+  int n_parts;
+  float eps;
+  float* sumsq_out;
+} dfl_gemm_op;
+size_t dfl_gemm_chain_workspace_bytes(const dfl_gemm_op* ops, int n_ops);
+int dfl_gemm_chain(const dfl_gemm_op* ops, int n_ops, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- tensor parallelism (Qwen3.5-27B, config 5) ------------------------------
  * Replaces the all-sum after the row-parallel projections of the reference's
  * sharded model (custom_qwen35_model.py:810 and shard_linear "sharded-to-all" at

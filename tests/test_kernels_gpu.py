@@ -570,3 +570,62 @@ def test_attention_qkv_fused_matches_append_then_attention(case):
     live = pos >= 0
     assert torch.equal(k1, k2) and torch.equal(v1, v2)
     assert torch.equal(o1[live], o2[live])
+
+
+@pytest.mark.parametrize("M", [1, 16])
+def test_gemm_chain_matches_separate_launches(M):
+    """One dfl_gemm_chain launch of a layer's projections at the Qwen3-4B shape (o_proj with
+    residual, gate/up with the fused RMSNorm and SiLU, down with residual + tap, the next
+    qkv with RMSNorm, the lm_head argmax) against the same ops as separate dfl_gemm_bf16
+    launches: outputs within one bf16 rounding (the two forms split K differently), argmax
+    equal except at near-ties, and three launches in a row give identical bits (the
+    kernel leaves its counters ready for the next launch)."""
+    ops = _ops()
+    H, F, Nq, V = 2560, 9728, 6144, 151936
+    g = torch.Generator().manual_seed(40 + M)
+    w_o = ops.pack_weight(_rand((H, 4096), 0.02, 41).to(DEV))
+    w_gu = ops.pack_weight(_rand((2 * F, H), 0.02, 42).to(DEV))
+    w_dn = ops.pack_weight(_rand((H, F), 0.02, 43).to(DEV))
+    w_q = ops.pack_weight(_rand((Nq, H), 0.02, 44).to(DEV))
+    w_lm = ops.pack_weight(_rand((V, H), 0.02, 45).to(DEV))
+    nw1 = (1 + 0.1 * torch.randn(H, generator=g)).bfloat16().to(DEV)
+    nw2 = (1 + 0.1 * torch.randn(H, generator=g)).bfloat16().to(DEV)
+    nw3 = (1 + 0.1 * torch.randn(H, generator=g)).bfloat16().to(DEV)
+    attn = torch.randn(M, 4096, generator=g).bfloat16().to(DEV)
+    h0 = torch.randn(M, H, generator=g).bfloat16().to(DEV)
+
+    def run(chain):
+        h = h0.clone()
+        ss = torch.zeros(M, H // 32, device=DEV)
+        act = torch.empty(M, F, dtype=torch.bfloat16, device=DEV)
+        qkv = torch.empty(M, Nq, dtype=torch.bfloat16, device=DEV)
+        tap = torch.empty(M, H, dtype=torch.bfloat16, device=DEV)
+        part = torch.empty(M, ops.argmax_tiles(V), 2, device=DEV)
+        specs = [dict(x=attn, w=w_o, epilogue=ops.EPI_RESIDUAL, residual=h, out=h, sumsq_out=ss),
+                 dict(x=h, w=w_gu, epilogue=ops.EPI_SILU_MUL, out=act, norm_w=nw1, sumsq_in=ss),
+                 dict(x=act, w=w_dn, epilogue=ops.EPI_RESIDUAL, residual=h, out=h, out2=tap, sumsq_out=ss),
+                 dict(x=h, w=w_q, out=qkv, norm_w=nw2, sumsq_in=ss),
+                 dict(x=h, w=w_lm, epilogue=ops.EPI_ARGMAX, argmax_partials=part, norm_w=nw3, sumsq_in=ss)]
+        if chain:
+            ops.gemm_chain([ops.chain_op(**sp) for sp in specs])
+        else:
+            for sp in specs:
+                sp = dict(sp)
+                x, w = sp.pop("x"), sp.pop("w")
+                ops.gemm(x, w, **sp)
+        torch.cuda.synchronize()
+        return h.float().cpu(), act.float().cpu(), qkv.float().cpu(), tap.float().cpu(), ops.argmax_reduce(part).cpu()
+
+    ref = run(False)
+    got = run(True)
+    for name, a, b in zip(("h", "act", "qkv", "tap"), got[:4], ref[:4]):
+        d = (a - b).abs()
+        ulp = torch.pow(2.0, torch.floor(torch.log2(b.abs().clamp_min(2.0 ** -126))) - 7)
+        print(f"chain vs separate, M={M}, {name}: max diff {d.max().item():.4f}, equal {(d == 0).float().mean().item():.3f}")
+        assert bool((d <= 2 * ulp + 1e-6).all()), name
+    assert (got[4] == ref[4]).float().mean().item() >= 0.9
+    again = [run(True) for _ in range(2)]
+    for r in again:
+        for a, b in zip(r, got):
+            assert torch.equal(a, b)
+    assert ops.device_error() == 0

@@ -1403,6 +1403,11 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
     if (lane == 0) {
       const uint32_t w0 = smem_u32(smem), x0 = smem_u32(smem + TC_OFF_X);
       int g = 0, seg = -1;
+      // xready[s] completes only for units of ops with the RMSNorm prologue (the epilogue
+      // warps rescale those): its phase is counted per stage over such units
+      int xr_uses[TC_STAGES];
+#pragma unroll
+      for (int s = 0; s < TC_STAGES; ++s) xr_uses[s] = 0;
       bool ok = true;
       for (int k = 0; k < c.n_ops && ok; ++k) {
         const TcArgs& a = c.op[k];
@@ -1419,7 +1424,16 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
             if (!mbar_wait(&acce[seg & 1], ((seg >> 1) & 1) ^ 1, 213, c.err)) { ok = false; break; }
             tc_fence_after();
           }
-          if (!mbar_wait(norm ? &xready[s] : &full[s], (g / TC_STAGES) & 1, 214, c.err)) { ok = false; break; }
+          if (norm) {
+            int xr = 0;
+#pragma unroll
+            for (int ss = 0; ss < TC_STAGES; ++ss)
+              if (ss == s) xr = xr_uses[ss]++;
+            if (!mbar_wait(&xready[s], xr & 1, 214, c.err)) { ok = false; break; }
+          } else if (!mbar_wait(&full[s], (g / TC_STAGES) & 1, 214, c.err)) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
           const uint32_t d = tmem + (uint32_t)((seg & 1) * TC_NACC * TC_BM);
           const uint64_t ad = sw128_desc(w0 + s * TC_W_BYTES);

@@ -181,7 +181,11 @@ def greedy_trace(target, prompt, n_new):
 def gemm_roofline(sess, reps: int = 3) -> dict:
     """Times the verify step's weight-streaming GEMM launches alone (same shapes, weights and
     activation buffers as the step; 8 GB of weights per pass, far above the 126 MB L2)."""
-    launches = sess.target.verify_gemms(sess.B * sess.bs, ws=sess.ws)
+    M = sess.B * sess.bs
+    from dflash_b200.model import chain_ok
+    use_chain = getattr(sess.target, "use_chain", False) and chain_ok(M, sess.ws)
+    launches = (sess.target.verify_chains(M, ws=sess.ws) if use_chain
+                else sess.target.verify_gemms(M, ws=sess.ws))
     total_bytes = sum(nb for _, nb, _ in launches)
     total_flops = sum(f for _, _, f in launches)
 
@@ -210,7 +214,7 @@ def gemm_roofline(sess, reps: int = 3) -> dict:
     t_pass = min(times)
     per_launch_s = t_pass / len(launches)
     per_launch_bytes = total_bytes / len(launches)
-    return {"launches": len(launches), "bytes_per_pass": total_bytes, "s_per_pass": t_pass,
+    return {"launches": len(launches), "chain": use_chain, "bytes_per_pass": total_bytes, "s_per_pass": t_pass,
             "per_launch_s": per_launch_s, "per_launch_bytes": per_launch_bytes,
             "achieved_gbs": per_launch_bytes / per_launch_s / 1e9,
             "per_launch_flops": total_flops / len(launches),
@@ -489,14 +493,24 @@ def main():
     roof = None
     if not args.no_roofline:
         r = gemm_roofline(sess)
+        # DRAM bytes per launch from one ncu capture of the same kernel (profiles/), scaled to
+        # this pass's average launch by the algorithmic bytes
         traffic = None
-        tp = os.path.join(ROOT, "profiles", "gemm_stream_traffic.json")
+        tp = os.path.join(ROOT, "profiles", "gemm_chain_traffic.json" if r["chain"] else "gemm_stream_traffic.json")
         if os.path.exists(tp):
             try:
-                traffic = json.load(open(tp)).get("dram_bytes_per_launch_full")
+                t = json.load(open(tp))
+                if r["chain"]:
+                    traffic = int(t["dram_bytes"] / t["alg_bytes"] * r["per_launch_bytes"])
+                else:
+                    traffic = t.get("dram_bytes_per_launch_full")
             except Exception:
                 traffic = None
-        roof = {"bound": "hbm", "kernel": "gemm_csk_kernel + gemm_tc_kernel (verify weight streaming, M=16; per-launch average over the 145-launch verify pass)",
+        kern = ("gemm_chain_kernel (the verify forward's projections as one launch per run between two attention "
+                f"calls, M=16; per-launch average over the {r['launches']}-launch verify pass)" if r["chain"] else
+                "gemm_csk_kernel + gemm_tc_kernel (verify weight streaming, M=16; per-launch average over the "
+                f"{r['launches']}-launch verify pass)")
+        roof = {"bound": "hbm", "kernel": kern,
                 "achieved": round(r["achieved_gbs"], 1), "peak": hbm_peak, "unit": "GB/s",
                 "frac": round(r["achieved_gbs"] / hbm_peak, 4), "traffic": traffic,
                 "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else peak_kind,

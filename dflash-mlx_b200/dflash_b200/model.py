@@ -276,6 +276,46 @@ class TargetModel:
                 pending.append(qkv_op(self.layers[l + 1]))
         return chain_head(pending, h, ss, self.lm_head_w, self.norm_w, eps, head, b, ws)
 
+    def verify_chains(self, M: int, ws: ops.Workspace | None = None) -> list[tuple]:
+        """The GEMM-chain launches of one decode-block forward over M rows (M <= 16), as
+        (callable, algorithmic bytes, FLOPs) triples on this model's buffers (roofline timing;
+        the attention launches between them are left out)."""
+        c = self.cfg
+        b = self.buffers(M)
+        h, ss, eps, H = b["h"], b["ss"], c.rms_norm_eps, c.hidden_size
+        chains, cur = [], []
+
+        def add(op, N, K, n_out, extra=0):
+            cur.append((op, N * K * 2 + M * K * 2 + M * n_out * 2 + extra, 2 * M * N * K))
+
+        def flush():
+            if cur:
+                lst = [o for o, _, _ in cur]
+                chains.append((lambda lst=lst: ops.gemm_chain(lst, ws), sum(x for _, x, _ in cur),
+                               sum(f for _, _, f in cur)))
+                cur.clear()
+
+        qkv = lambda lw: add(ops.chain_op(h, lw["w_qkv"], out=b["qkv"], norm_w=lw["in_norm"], sumsq_in=ss, eps=eps),  # noqa
+                             lw["w_qkv"].N, H, lw["w_qkv"].N)
+        if self.layers:
+            qkv(self.layers[0])
+        for l, lw in enumerate(self.layers):
+            flush()
+            Ko, Ng, F = lw["w_o"].K, lw["w_gu"].N, lw["w_down"].K
+            add(ops.chain_op(b["attn"], lw["w_o"], ops.EPI_RESIDUAL, residual=h, out=h, sumsq_out=ss), H, Ko, H,
+                M * H * 2)
+            add(ops.chain_op(h, lw["w_gu"], ops.EPI_SILU_MUL, out=b["act"], norm_w=lw["post_norm"], sumsq_in=ss,
+                             eps=eps), Ng, H, Ng // 2)
+            add(ops.chain_op(b["act"], lw["w_down"], ops.EPI_RESIDUAL, residual=h, out=h, sumsq_out=ss), H, F, H,
+                M * H * 2)
+            if l + 1 < len(self.layers):
+                qkv(self.layers[l + 1])
+        V = self.lm_head_w.N
+        add(ops.chain_op(h, self.lm_head_w, ops.EPI_ARGMAX, argmax_partials=b["argmax"], norm_w=self.norm_w,
+                         sumsq_in=ss, eps=eps), V, H, 0)
+        flush()
+        return chains
+
     def verify_gemms(self, M: int, ws: ops.Workspace | None = None) -> list[tuple]:
         """The GEMM launches of one forward over M rows, as (callable, algorithmic bytes,
         FLOPs) triples on this model's buffers (roofline timing)."""

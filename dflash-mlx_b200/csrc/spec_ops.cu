@@ -25,9 +25,19 @@ __device__ __forceinline__ ArgmaxPair better(ArgmaxPair a, ArgmaxPair b) {
 }
 
 // argmax over the per-tile partials of one row, computed by one warp
+// (the order of value desc, index asc is total, so any reduction order gives the same pair;
+// eight loads per lane are kept in flight)
 __device__ __forceinline__ int warp_row_argmax(const float2* part, int n_tiles, int lane) {
   ArgmaxPair best{-INFINITY, 0x7fffffff};
-  for (int j = lane; j < n_tiles; j += 32) {
+  int j = lane;
+  for (; j + 7 * 32 < n_tiles; j += 8 * 32) {
+    float2 p[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) p[u] = part[j + u * 32];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) best = better(best, ArgmaxPair{p[u].x, __float_as_int(p[u].y)});
+  }
+  for (; j < n_tiles; j += 32) {
     const float2 p = part[j];
     best = better(best, ArgmaxPair{p.x, __float_as_int(p.y)});
   }

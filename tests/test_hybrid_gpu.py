@@ -13,47 +13,69 @@ def _need(lib):
         pytest.skip("no CUDA device")
 
 
-def _logit_check(got, ref, what, max_bound=0.08, mean_bound=2e-2, agree_min=0.9):
+def _ulp(x):
+    return torch.pow(2.0, torch.floor(torch.log2(x.abs().clamp_min(2.0 ** -126))) - 7)
+
+
+def _logit_check(got, ref, ref32, what, agree_min=0.9):
+    """Within the oracle's own rounding sensitivity on the same inputs (ref32 = the oracle
+    in fp32 arithmetic): mean |gpu - oracle| <= mean |ref32 - oracle|, every element within
+    1.5 x the latter's max or one bf16 ulp; greedy agreement at least agree_min (and at
+    least the oracle's own bf16-vs-fp32 agreement minus one row)."""
     got = got.float().cpu().reshape(ref.shape)
-    d = (got - ref).abs()
+    d, r = (got - ref).abs(), (ref32 - ref).abs()
     agree = (got.argmax(-1) == ref.argmax(-1)).float().mean().item()
-    print(f"{what}: max|ref| {ref.abs().max().item():.3f} max err {d.max().item():.4f} mean err "
-          f"{d.mean().item():.2e} greedy agreement {agree:.3f}")
-    assert d.mean().item() <= mean_bound, what
-    assert d.max().item() <= max_bound, what
-    assert agree >= agree_min, what
+    agree32 = (ref32.argmax(-1) == ref.argmax(-1)).float().mean().item()
+    print(f"{what}: max|ref| {ref.abs().max().item():.3f} gpu vs oracle max {d.max().item():.4f} mean "
+          f"{d.mean().item():.2e} agreement {agree:.3f}; oracle fp32 vs bf16 max {r.max().item():.4f} mean "
+          f"{r.mean().item():.2e} agreement {agree32:.3f}")
+    assert d.mean().item() <= r.mean().item(), what
+    assert bool((d <= torch.clamp(_ulp(ref), min=1.5 * r.max().item())).all()), what
+    assert agree >= min(agree_min, agree32 - 1.0 / ref.shape[0]), what
 
 
-def _adapter_sequence(cfg, w, prompt, blocks, accepts, layer_ids, cap=512):
+def _adapter_sequence(cfg, w, prompt, blocks, accepts, layer_ids, monkeypatch, cap=512):
     """Prefill, then for each block: verify with records, roll back to `accepted`, rewind
-    the KV by block - accepted. Returns the GPU and oracle logits of every forward and
-    the final gated-delta states."""
+    the KV by block - accepted. Returns, per forward, the GPU logits, the oracle's and the
+    oracle's in fp32 arithmetic (its rounding sensitivity), and the caches."""
     from oracle import dflash_oracle as O
     from dflash_b200.adapters import load_target_model
     lt = load_target_model((cfg, w), device="cuda")
     cache = lt.make_cache(cap)
     ot = O.OracleHybridTarget(cfg, w)
-    oc = ot.make_cache(cap)
+    oc, oc32 = ot.make_cache(cap), ot.make_cache(cap)
+
+    def fp32(fn, *args):
+        with monkeypatch.context() as mp:
+            mp.setattr(O, "bf16", lambda x: x.float())
+            return fn(*args)
+
+    def rollback(c, n_trim, acc):
+        for x in c:
+            if isinstance(x, O.KV):
+                x.trim(n_trim)
+        ot.rollback_linear(c, acc)
+
     pairs = []
     lg, taps = lt.forward_with_hidden_states(torch.tensor(prompt), cache, layer_ids)
     rl, rt = ot.forward_with_hidden_states(prompt, oc, layer_ids)
-    pairs.append(("prefill", lg[0], rl, taps[0], rt))
+    r32, _ = fp32(ot.forward_with_hidden_states, prompt, oc32, layer_ids)
+    pairs.append(("prefill", lg[0], rl, r32, taps[0], rt))
     for i, (blk, acc) in enumerate(zip(blocks, accepts)):
         lg, taps, rec = lt.forward_with_hidden_states(torch.tensor(blk), cache, layer_ids,
                                                       return_rollback_records=True)
         rl, rt = ot.forward_with_hidden_states(blk, oc, layer_ids)
-        pairs.append((f"block{i}", lg[0], rl, taps[0], rt))
+        r32, _ = fp32(ot.forward_with_hidden_states, blk, oc32, layer_ids)
+        pairs.append((f"block{i}", lg[0], rl, r32, taps[0], rt))
         if acc < len(blk):
             lt.rewind_kv_caches(cache, len(blk) - acc)
             lt.rollback_linear_caches(cache, rec, acc)
-            for c in oc:
-                if isinstance(c, O.KV):
-                    c.trim(len(blk) - acc)
-            ot.rollback_linear(oc, acc)
-    return lt, cache, ot, oc, pairs
+            rollback(oc, len(blk) - acc, acc)
+            fp32(rollback, oc32, len(blk) - acc, acc)
+    return lt, cache, ot, oc, oc32, pairs
 
 
-def test_tiny_hybrid_verify_rollback_matches_oracle():
+def test_tiny_hybrid_verify_rollback_matches_oracle(monkeypatch):
     from dflash_b200.config import tiny_hybrid_pair
     from dflash_b200.weights import random_target_weights
     tcfg, dcfg = tiny_hybrid_pair()
@@ -61,27 +83,28 @@ def test_tiny_hybrid_verify_rollback_matches_oracle():
     g = torch.Generator().manual_seed(4)
     prompt = torch.randint(0, tcfg.vocab_size, (150,), generator=g).tolist()  # two prefill chunks
     blocks = torch.randint(0, tcfg.vocab_size, (3, 8), generator=g).tolist()
-    lt, cache, ot, oc, pairs = _adapter_sequence(tcfg, w, prompt, blocks, [3, 8, 1], [1, 3])
-    for name, lg, rl, tp, rt in pairs:
-        _logit_check(lg, rl, name)
+    lt, cache, ot, oc, oc32, pairs = _adapter_sequence(tcfg, w, prompt, blocks, [3, 8, 1], [1, 3], monkeypatch)
+    for name, lg, rl, r32, tp, rt in pairs:
+        _logit_check(lg, rl, r32, name)
         assert (tp.float().cpu() - rt).abs().max().item() <= 3e-2 * rt.abs().max().item()
-    # recurrent state of every gated-delta layer after the last rollback
+    # recurrent state of every gated-delta layer after the last rollback: within the
+    # oracle's own bf16-vs-fp32 spread of that state (or 1e-3)
     hc = cache.kv
     for l, gi in lt.model.gdn_index.items():
-        got, ref = hc.state[gi][0].cpu(), oc[l].state
+        got, ref, ref32 = hc.state[gi][0].cpu(), oc[l].state, oc32[l].state
         rel = ((got - ref).abs().max() / ref.abs().max()).item()
-        print(f"layer {l} state rel err {rel:.2e}")
-        assert rel <= 2e-2
-        assert torch.equal(hc.conv[gi][0].float().cpu(), oc[l].conv.to(torch.bfloat16).float()) or \
-            (hc.conv[gi][0].float().cpu() - oc[l].conv).abs().max().item() <= 2e-2 * oc[l].conv.abs().max().item()
+        rel32 = ((ref32 - ref).abs().max() / ref.abs().max()).item()
+        print(f"layer {l} state rel err {rel:.2e} (oracle fp32 vs bf16 {rel32:.2e})")
+        assert rel <= max(1e-3, 1.5 * rel32)
+        d = (hc.conv[gi][0].float().cpu() - oc[l].conv).abs()
+        assert bool((d <= _ulp(oc[l].conv)).all())
 
 
-def test_qwen35_27b_layer_logits_parity():
+def test_qwen35_27b_layer_logits_parity(monkeypatch):
     """27B-width hybrid layers (3 gated-delta + 1 gated attention): prefill and a verify
-    block with rollback, logits against the oracle. At this width the oracle's own
-    bf16 result and its fp32 result differ by up to 0.22 (mean 0.028, greedy
-    agreement 0.925) on the prefill logits (max |logit| 7.3): the model's bf16
-    sensitivity. Bound: mean abs error <= 2e-2, max abs error <= 0.15."""
+    block with rollback, logits against the oracle, measured against the oracle's own
+    bf16-vs-fp32 spread on the same inputs (0.22 max, mean 0.028 on the prefill logits
+    of max |logit| 7.3)."""
     from dflash_b200.config import qwen35_27b_pair
     from dflash_b200.weights import random_target_weights
     tcfg, _ = qwen35_27b_pair(4)
@@ -89,11 +112,9 @@ def test_qwen35_27b_layer_logits_parity():
     g = torch.Generator().manual_seed(4)
     prompt = torch.randint(0, tcfg.vocab_size, (40,), generator=g).tolist()
     blocks = torch.randint(0, tcfg.vocab_size, (2, 16), generator=g).tolist()
-    _, _, _, _, pairs = _adapter_sequence(tcfg, w, prompt, blocks, [5, 16], [1, 3], cap=128)
-    for name, lg, rl, tp, rt in pairs:
-        # greedy agreement: the oracle's own bf16 and fp32 results disagree on 7.5 % of
-        # rows here, so a 16-row block may flip two rows
-        _logit_check(lg, rl, name, max_bound=0.15, agree_min=0.9 if name == "prefill" else 0.8)
+    _, _, _, _, _, pairs = _adapter_sequence(tcfg, w, prompt, blocks, [5, 16], [1, 3], monkeypatch, cap=128)
+    for name, lg, rl, r32, tp, rt in pairs:
+        _logit_check(lg, rl, r32, name, agree_min=0.9 if name == "prefill" else 0.8)
 
 
 def _tiny_models():

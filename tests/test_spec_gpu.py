@@ -123,8 +123,10 @@ def test_tiny_injected_acceptance_matches_oracle():
     assert accs == exp[:len(accs)]
 
 
-def test_qwen3_4b_layer_logits_parity():
-    """Full-width Qwen3-4B layers (reduced depth): logits within 2e-2 of the oracle."""
+def test_qwen3_4b_layer_logits_parity(monkeypatch):
+    """Full-width Qwen3-4B layers (reduced depth): logits against the oracle, within the
+    oracle's own bf16-vs-fp32 spread on the same inputs (mean and per element, or one bf16
+    ulp), greedy agreement >= 0.95, taps within 2e-2 of their scale."""
     from oracle import dflash_oracle as O
     from dflash_b200.config import qwen3_4b_small_pair
     from dflash_b200.model import TargetModel
@@ -141,16 +143,17 @@ def test_qwen3_4b_layer_logits_parity():
     logits = target.forward(toks, pos, cache, max_kv=48, layer_ids=[0, 1], taps_out=taps, head="logits")
     ot = O.OracleTarget(tcfg, tw)
     ref_logits, ref_taps = ot.forward_with_hidden_states(prompt, ot.make_cache(128), [0, 1])
+    with monkeypatch.context() as mp:
+        mp.setattr(O, "bf16", lambda x: x.float())
+        ref32, _ = ot.forward_with_hidden_states(prompt, ot.make_cache(128), [0, 1])
     got = logits.float().cpu()
-    diff = (got - ref_logits).abs()
-    # The oracle computed in bf16 and the same oracle computed in fp32 differ by up to
-    # 0.062 (mean 0.009) on these logits: that is the model's own bf16 sensitivity, and
-    # no bf16 implementation (the reference's MLX path included) can beat it per logit.
-    # Bound: mean abs error <= 2e-2, max abs error <= 0.08.
+    diff, spread = (got - ref_logits).abs(), (ref32 - ref_logits).abs()
+    ulp = torch.pow(2.0, torch.floor(torch.log2(ref_logits.abs().clamp_min(2.0 ** -126))) - 7)
     print(f"logits: max|ref| {ref_logits.abs().max().item():.3f} max abs err {diff.max().item():.4f} "
-          f"mean abs err {diff.mean().item():.2e} exact {(diff == 0).float().mean().item():.3f}")
-    assert diff.mean().item() <= 2e-2
-    assert diff.max().item() <= 0.08
+          f"mean abs err {diff.mean().item():.2e} exact {(diff == 0).float().mean().item():.3f}; oracle fp32 vs "
+          f"bf16 max {spread.max().item():.4f} mean {spread.mean().item():.2e}")
+    assert diff.mean().item() <= spread.mean().item()
+    assert bool((diff <= torch.clamp(ulp, min=1.5 * spread.max().item())).all())
     agree = (got.argmax(-1) == ref_logits.argmax(-1)).float().mean().item()
     print(f"greedy-token agreement {agree:.3f}")
     assert agree >= 0.95

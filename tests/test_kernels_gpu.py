@@ -620,9 +620,12 @@ def test_gemm_chain_matches_separate_launches(M):
     got = run(True)
     for name, a, b in zip(("h", "act", "qkv", "tap"), got[:4], ref[:4]):
         d = (a - b).abs()
-        ulp = torch.pow(2.0, torch.floor(torch.log2(b.abs().clamp_min(2.0 ** -126))) - 7)
-        print(f"chain vs separate, M={M}, {name}: max diff {d.max().item():.4f}, equal {(d == 0).float().mean().item():.3f}")
-        assert bool((d <= 2 * ulp + 1e-6).all()), name
+        # rounding-order differences only: most values identical, the rest within a few ulps
+        # of the row's scale (a residual sum can cancel, so not of the element itself)
+        scale = torch.pow(2.0, torch.floor(torch.log2(b.abs().amax(1, keepdim=True).clamp_min(2.0 ** -126))) - 7)
+        eq = (d == 0).float().mean().item()
+        print(f"chain vs separate, M={M}, {name}: max diff {d.max().item():.4f}, equal {eq:.3f}")
+        assert bool((d <= 4 * scale).all()) and eq >= 0.9, name
     assert (got[4] == ref[4]).float().mean().item() >= 0.9
     again = [run(True) for _ in range(2)]
     for r in again:

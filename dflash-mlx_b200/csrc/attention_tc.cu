@@ -317,22 +317,25 @@ __global__ void __launch_bounds__(AT_THREADS, 1) attn_tc_kernel(const __grid_con
       }
       // P of the previous block has been read and O is complete up to it
       if (i > 0 && !mbar_wait(p_free, (i - 1) & 1, 329, a.err)) { ok = false; break; }
-      if (mx > m_used + AT_RESCALE || (m_used == -INFINITY && mx > -INFINITY)) {
-        const float f = m_used == -INFINITY ? 0.f : exp2f(m_used - mx);
+      // tcgen05.ld / st are warp-collective: the warp rescales O together whenever any of
+      // its rows needs it, rows that do not with factor 1 (exact)
+      const bool resc = mx > m_used + AT_RESCALE || (m_used == -INFINITY && mx > -INFINITY);
+      const float f = !resc ? 1.f : (m_used == -INFINITY ? 0.f : exp2f(m_used - mx));
+      if (resc) {
         l *= f;
-        if (i > 0) {
-          tc_fence_after();
-#pragma unroll
-          for (int q8 = 0; q8 < 8; ++q8) {
-            float ov[16];
-            tc_ld16(t_o + lane_base + (uint32_t)(q8 * 16), ov);
-#pragma unroll
-            for (int e = 0; e < 16; ++e) ov[e] *= f;
-            tc_st16(t_o + lane_base + (uint32_t)(q8 * 16), ov);
-          }
-          tc_fence_before();
-        }
         m_used = mx;
+      }
+      if (i > 0 && __any_sync(0xffffffffu, resc)) {
+        tc_fence_after();
+#pragma unroll
+        for (int q8 = 0; q8 < 8; ++q8) {
+          float ov[16];
+          tc_ld16(t_o + lane_base + (uint32_t)(q8 * 16), ov);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) ov[e] *= f;
+          tc_st16(t_o + lane_base + (uint32_t)(q8 * 16), ov);
+        }
+        tc_fence_before();
       }
       const float mu = m_used == -INFINITY ? 0.f : m_used;
       float ps = 0.f;
@@ -354,17 +357,22 @@ __global__ void __launch_bounds__(AT_THREADS, 1) attn_tc_kernel(const __grid_con
       fence_proxy_async_smem();
       mbar_arrive(p_full);
     }
-    // epilogue: O of this row once the last P V product completed
-    if (ok && mbar_wait(p_free, (n_blocks - 1) & 1, 329, a.err) && real && lim > k_begin && m0 + tr < a.M) {
+    // epilogue: O of this row once the last P V product completed (every thread of the warp
+    // loads its TMEM lane -- the loads are warp-collective -- and valid rows store)
+    if (__all_sync(0xffffffffu, ok) && mbar_wait(p_free, (n_blocks - 1) & 1, 329, a.err)) {
       tc_fence_after();
+      const bool store = real && lim > k_begin && m0 + tr < a.M;
       const int m = m0 + tr, h = kvh * G + hl;
-      if (a.direct) {
-        const float inv = l > 0.f ? 1.f / l : 0.f;
-        __nv_bfloat16* dst = a.out + (long long)m * a.ldo + (long long)h * AT_HD;
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* dst = a.out + (long long)m * a.ldo + (long long)h * AT_HD;
+      const long long base = ((long long)chunk * a.M + m) * a.Hq + h;
+      float* po = a.part_o + base * AT_HD;
 #pragma unroll
-        for (int q8 = 0; q8 < 8; ++q8) {
-          float ov[16];
-          tc_ld16(t_o + lane_base + (uint32_t)(q8 * 16), ov);
+      for (int q8 = 0; q8 < 8; ++q8) {
+        float ov[16];
+        tc_ld16(t_o + lane_base + (uint32_t)(q8 * 16), ov);
+        if (!store) continue;
+        if (a.direct) {
           uint4 w0, w1;
           w0.x = pack_bf16x2(ov[0] * inv, ov[1] * inv);
           w0.y = pack_bf16x2(ov[2] * inv, ov[3] * inv);
@@ -376,20 +384,14 @@ __global__ void __launch_bounds__(AT_THREADS, 1) attn_tc_kernel(const __grid_con
           w1.w = pack_bf16x2(ov[14] * inv, ov[15] * inv);
           *reinterpret_cast<uint4*>(dst + q8 * 16) = w0;
           *reinterpret_cast<uint4*>(dst + q8 * 16 + 8) = w1;
-        }
-      } else {
-        const long long base = ((long long)chunk * a.M + m) * a.Hq + h;
-        float* po = a.part_o + base * AT_HD;
-#pragma unroll
-        for (int q8 = 0; q8 < 8; ++q8) {
-          float ov[16];
-          tc_ld16(t_o + lane_base + (uint32_t)(q8 * 16), ov);
+        } else {
 #pragma unroll
           for (int e4 = 0; e4 < 4; ++e4)
-            *reinterpret_cast<float4*>(po + q8 * 16 + e4 * 4) = make_float4(ov[4 * e4], ov[4 * e4 + 1], ov[4 * e4 + 2], ov[4 * e4 + 3]);
+            *reinterpret_cast<float4*>(po + q8 * 16 + e4 * 4) =
+                make_float4(ov[4 * e4], ov[4 * e4 + 1], ov[4 * e4 + 2], ov[4 * e4 + 3]);
         }
-        a.part_ml[base] = make_float2(m_used, l);
       }
+      if (store && !a.direct) a.part_ml[base] = make_float2(m_used, l);
       tc_fence_before();
     }
   }

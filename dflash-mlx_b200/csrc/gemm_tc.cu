@@ -1329,7 +1329,11 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
       bool ok = true;
       for (int k = 0; k < c.n_ops && ok; ++k) {
         const TcArgs& a = c.op[k];
-        const long long u0 = (long long)cta * a.U1 / G, u1 = (long long)(cta + 1) * a.U1 / G;
+        // an op with fewer units than CTAs runs on its first U1 CTAs (every range non-empty, so
+        // the CTAs owning a split tile are consecutive)
+        const int Gk = a.U1 < G ? (int)a.U1 : G;
+        const long long u0 = cta < Gk ? (long long)cta * a.U1 / Gk : 0;
+        const long long u1 = cta < Gk ? (long long)(cta + 1) * a.U1 / Gk : 0;
         const int n_units = (int)(u1 - u0);
         const int pre = n_units < TC_STAGES ? n_units : TC_STAGES;
         for (int i = 0; i < pre && ok; ++i) {
@@ -1382,7 +1386,11 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
       for (int k = 0; k < c.n_ops && ok; ++k) {
         const TcArgs& a = c.op[k];
         const bool norm = a.norm_w != nullptr;
-        const long long u0 = (long long)cta * a.U1 / G, u1 = (long long)(cta + 1) * a.U1 / G;
+        // an op with fewer units than CTAs runs on its first U1 CTAs (every range non-empty, so
+        // the CTAs owning a split tile are consecutive)
+        const int Gk = a.U1 < G ? (int)a.U1 : G;
+        const long long u0 = cta < Gk ? (long long)cta * a.U1 / Gk : 0;
+        const long long u1 = cta < Gk ? (long long)(cta + 1) * a.U1 / Gk : 0;
         const int n_units = (int)(u1 - u0);
         for (int i = 0; i < n_units; ++i, ++g) {
           const long long u = u0 + i;
@@ -1429,7 +1437,11 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
     for (int k = 0; k < c.n_ops; ++k) {
       const TcArgs& a = c.op[k];
       const bool norm = a.norm_w != nullptr;
-      const long long u0 = (long long)cta * a.U1 / G, u1 = (long long)(cta + 1) * a.U1 / G;
+      // an op with fewer units than CTAs runs on its first U1 CTAs (every range non-empty, so
+        // the CTAs owning a split tile are consecutive)
+        const int Gk = a.U1 < G ? (int)a.U1 : G;
+        const long long u0 = cta < Gk ? (long long)cta * a.U1 / Gk : 0;
+        const long long u1 = cta < Gk ? (long long)(cta + 1) * a.U1 / Gk : 0;
       const int n_units = (int)(u1 - u0);
       if (norm && n_units > 0) {
         if (k > 0 && et == 0) chain_wait_done(c, k - 1, target);  // the RMSNorm sums of op k - 1
@@ -1476,7 +1488,7 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
           __syncwarp();
           if (lane == 0) mbar_arrive(&acce[seg & 1]);
           const long long tu0 = (long long)nt * a.kb, tu1 = tu0 + a.kb - 1;
-          const int c_first = tc_unit_owner(tu0, a.U1, G), c_last = tc_unit_owner(tu1, a.U1, G);
+          const int c_first = tc_unit_owner(tu0, a.U1, Gk), c_last = tc_unit_owner(tu1, a.U1, Gk);
           bool do_epi = true;
           const int col = q * 32 + lane;
           if (c_first != c_last) {
@@ -1504,7 +1516,7 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
                 for (int kq = 0; kq < TC_PB; ++kq) {
                   const int cs = cs0 + kq;
                   if (cs <= c_last) {
-                    const long long cs_u0 = (long long)cs * a.U1 / G;
+                    const long long cs_u0 = (long long)cs * a.U1 / Gk;
                     const int sl = (nt == (int)(cs_u0 / a.kb)) ? 0 : 1;
                     const float4* src = reinterpret_cast<const float4*>(
                         a.partial + ((long long)cs * 2 + sl) * TC_PART_FLOATS + col * TC_BM);

@@ -636,3 +636,25 @@ def test_gemm_chain_matches_separate_launches(M):
         for a, b in zip(r, got):
             assert torch.equal(a, b)
     assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("N,K", [(256, 256), (1536, 256), (256, 768), (4096, 256)])
+def test_gemm_chain_ops_with_fewer_units_than_ctas(N, K):
+    """Ops whose 128 x 64 weight units are fewer than the chain's CTAs (the tiny
+    configuration's projections) run on the first CTAs only; three chain launches in a row
+    give the separate launch's values within one rounding and identical bits to each other."""
+    ops = _ops()
+    g = torch.Generator().manual_seed(N + K)
+    x = torch.randn(16, K, generator=g).bfloat16().to(DEV)
+    w = ops.pack_weight((torch.randn(N, K, generator=g) * 0.02).bfloat16().to(DEV))
+    y1 = ops.gemm(x, w)
+    outs = []
+    for _ in range(3):
+        y2 = torch.zeros_like(y1)
+        ops.gemm_chain([ops.chain_op(x, w, out=y2)])
+        outs.append(y2)
+    torch.cuda.synchronize()
+    d = (y1.float() - outs[0].float()).abs()
+    assert d.max().item() <= 2 ** -7 * y1.float().abs().max().item(), d.max().item()
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
+    assert ops.device_error() == 0

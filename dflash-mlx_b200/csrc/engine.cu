@@ -448,8 +448,8 @@ extern "C" int dfl_ctx_create(const dfl_qwen3_desc* target, const dfl_draft_desc
   c->wide_split_max = c->batched ? (batch < 16 ? 4 : 1) : 1;
   c->use_graph = !(flags & DFL_CTX_NO_GRAPH);
   {
-    const char* e = getenv("DFLASH_B200_GEMM_CHAIN");
-    c->use_chain = !(e && e[0] == '0');
+    const char* e = getenv("DFLASH_B200_GEMM_CHAIN");  // opt-in, as the Python host
+    c->use_chain = e && e[0] == '1';
   }
   c->n_stop = n_stop;
   int dev = 0;

@@ -2043,11 +2043,16 @@ extern "C" int dfl_gemm_bf16_noalloc(const void* x, int64_t ldx, const void* w_p
 }
 
 
+// Chain scratch, one fixed layout for every op list (launches with different lists share
+// a workspace, and a tile counter must never land on another launch's partial tiles):
+// [256 B: per-op completion counters][CH_MAX_TILES ints: tile counters][partial tiles].
+constexpr int CH_MAX_TILES = 1 << 16;
+constexpr size_t CH_OFF_COUNTERS = 256;
+constexpr size_t CH_OFF_PARTIAL = CH_OFF_COUNTERS + (size_t)CH_MAX_TILES * sizeof(int);
+
 extern "C" size_t dfl_gemm_chain_workspace_bytes(const dfl_gemm_op* ops, int n_ops) {
   if (!ops || n_ops <= 0 || n_ops > CH_MAX_OPS) return 0;
-  size_t tiles = 0;
-  for (int k = 0; k < n_ops; ++k) tiles += (size_t)(ops[k].N + TC_NT - 1) / TC_NT;
-  return 256 + ((tiles * sizeof(int) + 255) & ~(size_t)255) + (size_t)TC_GRID * 2 * TC_PART_FLOATS * sizeof(float);
+  return CH_OFF_PARTIAL + (size_t)TC_GRID * 2 * TC_PART_FLOATS * sizeof(float);
 }
 
 extern "C" int dfl_gemm_chain(const dfl_gemm_op* ops, int n_ops, void* workspace, size_t workspace_bytes,
@@ -2067,10 +2072,14 @@ extern "C" int dfl_gemm_chain(const dfl_gemm_op* ops, int n_ops, void* workspace
   std::memset(&c, 0, sizeof(c));
   char* ws = static_cast<char*>(workspace);
   c.done = reinterpret_cast<int*>(ws);
-  int* counters = reinterpret_cast<int*>(ws + 256);
+  int* counters = reinterpret_cast<int*>(ws + CH_OFF_COUNTERS);
   size_t tiles = 0;
   for (int k = 0; k < n_ops; ++k) tiles += (size_t)(ops[k].N + TC_NT - 1) / TC_NT;
-  float* partial = reinterpret_cast<float*>(ws + 256 + ((tiles * sizeof(int) + 255) & ~(size_t)255));
+  if (tiles > (size_t)CH_MAX_TILES) {
+    set_error("dfl_gemm_chain: %zu output tiles over all ops (at most %d)", tiles, CH_MAX_TILES);
+    return DFL_ERR_UNSUPPORTED;
+  }
+  float* partial = reinterpret_cast<float*>(ws + CH_OFF_PARTIAL);
   c.err = device_error_word();
   c.n_ops = n_ops;
   int max_norm_k = 0;

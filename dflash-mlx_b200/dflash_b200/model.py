@@ -78,7 +78,11 @@ PAGE_SIZE = 64
 
 
 def gemm_chain_enabled() -> bool:
-    return os.environ.get("DFLASH_B200_GEMM_CHAIN", "1") != "0"
+    """GEMM chains are opt-in (DFLASH_B200_GEMM_CHAIN=1): on B200 the chained verify pass
+    measured slower than one launch per projection (4.47 against 2.47 ms per Qwen3-4B
+    verify pass): a split tile is finished by one last-arriving CTA that reads up to 15
+    partial tiles two at a time, and each op then waits for all of them."""
+    return os.environ.get("DFLASH_B200_GEMM_CHAIN", "0") == "1"
 
 
 def chain_ok(M: int, ws) -> bool:
@@ -146,8 +150,8 @@ class TargetModel:
         # bits). Off by default: measured 3287 against 3217 us per Qwen3-4B verify step, the
         # in-CTA q/k preparation costing more than the append launch it removes.
         self.fuse_attention = os.environ.get("DFLASH_B200_FUSED_ATTENTION", "0") == "1"
-        # decode blocks (M <= 16, one-sequence kernel forms) run the projections between two
-        # attention calls as one GEMM-chain launch (DFLASH_B200_GEMM_CHAIN=0: one launch each)
+        # decode blocks (M <= 16, one-sequence kernel forms) may run the projections between two
+        # attention calls as one GEMM-chain launch (opt-in, see gemm_chain_enabled)
         self.use_chain = gemm_chain_enabled()
         self._bufs: dict[int, dict[str, torch.Tensor]] = {}
 

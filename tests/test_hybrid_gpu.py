@@ -96,8 +96,11 @@ def test_tiny_hybrid_verify_rollback_matches_oracle(monkeypatch):
         rel32 = ((ref32 - ref).abs().max() / ref.abs().max()).item()
         print(f"layer {l} state rel err {rel:.2e} (oracle fp32 vs bf16 {rel32:.2e})")
         assert rel <= max(1e-3, 1.5 * rel32)
+        # the conv state holds bf16 projection rows: within the oracle's own spread too
         d = (hc.conv[gi][0].float().cpu() - oc[l].conv).abs()
-        assert bool((d <= _ulp(oc[l].conv)).all())
+        r = (oc32[l].conv - oc[l].conv).abs()
+        assert d.mean().item() <= r.mean().item()
+        assert bool((d <= torch.clamp(_ulp(oc[l].conv), min=1.5 * r.max().item())).all())
 
 
 def test_qwen35_27b_layer_logits_parity(monkeypatch):

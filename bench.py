@@ -534,9 +534,19 @@ def main():
                   sess.cap, sess.key_chunk))
     att_d = int(q("dfl_attention_launches", dcfg.num_attention_heads, dcfg.num_key_value_heads, dcfg.head_dim,
                   sess.cap, sess.key_chunk))
-    # per layer: qkv gemm (+norm), q/k norm+rope+append, attention (1 or 2), o gemm, gu gemm (+norm), down
-    draft_launches = 1 + (2 + n_layers_d) + 1 + (5 + att_d) * n_layers_d + 1 + 1
-    verify_launches = 1 + (5 + att_t) * n_layers_t + 1 + 1
+    # per layer: qkv gemm (+norm) and q/k norm+rope+append (1 launch fused, else 2), attention (1 or 2),
+    # o gemm, gu gemm (+norm), down
+    from dflash_b200.model import qkv_rope_ok
+    rows = sess.B * sess.bs
+
+    def qkv_launches(c):
+        if not qkv_rope_ok(sess.ws, c.head_dim, getattr(c, "rope_dim", c.head_dim)):
+            return 2
+        return int(q("dfl_gemm_qkv_rope_launches", rows, c.hidden_size, c.num_attention_heads,
+                     c.num_key_value_heads, c.head_dim))
+    qkv_t, qkv_d = qkv_launches(tcfg), qkv_launches(dcfg)
+    draft_launches = 1 + (2 + n_layers_d) + 1 + (3 + qkv_d + att_d) * n_layers_d + 1 + 1
+    verify_launches = 1 + (3 + qkv_t + att_t) * n_layers_t + 1 + 1
     launches_step = draft_launches + verify_launches
     if rank == 0:
         line = {

@@ -442,7 +442,7 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(AttnArgs a) {
 // Merge the chunk partials of one (row, head) in chunk order. One warp per
 // (row, head): lane c holds chunk c's (max, sum) so the global max and the
 // denominator are warp reductions; the output accumulates chunk by chunk in
-// order, four chunks' loads in flight at a time.
+// order, eight chunks' loads in flight at a time (four at head_dim 256).
 template <int HD>
 __global__ void attn_combine_kernel(AttnArgs a) {
   grid_dependency_launch_dependents();
@@ -475,18 +475,19 @@ __global__ void attn_combine_kernel(AttnArgs a) {
     den += dl;
     const int n = min(32, nch - c0);
     int j = 0;
-    for (; j + 4 <= n; j += 4) {
-      float v[4][PER];
-      float wj[4];
+    constexpr int FL = HD <= 128 ? 8 : 4;  // chunks' loads in flight
+    for (; j + FL <= n; j += FL) {
+      float v[FL][PER];
+      float wj[FL];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) {
+      for (int u = 0; u < FL; ++u) {
         wj[u] = __shfl_sync(0xffffffffu, w, j + u);
         const float* po = a.part_o + (((long long)(c0 + j + u) * a.M + m) * a.Hq + h) * HD;
 #pragma unroll
         for (int i = 0; i < PER; ++i) v[u][i] = po[lane + 32 * i];
       }
 #pragma unroll
-      for (int u = 0; u < 4; ++u)
+      for (int u = 0; u < FL; ++u)
 #pragma unroll
         for (int i = 0; i < PER; ++i) acc[i] += wj[u] * v[u][i];
     }

@@ -140,6 +140,32 @@ int gemm(Ctx* c, const void* x, int64_t ldx, const void* w, int M, int N, int K,
 
 size_t kv_layer_elems(const Ctx* c, int hkv, int hd) { return (size_t)c->B * hkv * c->cap * hd; }
 
+// The QKV projection (input RMSNorm fused) and the q/k head norm + RoPE + cache append of
+// one decoder layer: one dfl_gemm_qkv_rope call on the M <= 16 GEMM forms when
+// DFLASH_B200_FUSED_QKV_ROPE=1 (the Python host's model.qkv_rope_ok rule), else the two
+// calls; both give the same bits.
+bool fused_qkv_rope(const Ctx* c, int hd, int rot_dim) {
+  static const bool on = [] {
+    const char* e = std::getenv("DFLASH_B200_FUSED_QKV_ROPE");
+    return e && e[0] == '1';
+  }();
+  return on && !c->batched && rot_dim == hd;
+}
+
+int qkv_rope(Ctx* c, const void* x, const float* ss, int H, const dfl_layer_weights& w, int M, int Hq, int Hkv, int hd,
+             int rot_dim, float eps, const int* pos, const int* row_seq, const float* inv_freq, void* qkv, void* q,
+             __nv_bfloat16* kc, __nv_bfloat16* vc, cudaStream_t s) {
+  const int nqkv = (Hq + 2 * Hkv) * hd;
+  if (fused_qkv_rope(c, hd, rot_dim))
+    return dfl_gemm_qkv_rope(x, H, w.w_qkv, M, H, w.in_norm, ss, H / 32, eps, qkv, nqkv, pos, row_seq, w.q_norm,
+                             w.k_norm, inv_freq, q, kc, vc, (int64_t)Hkv * c->cap * hd, (int64_t)c->cap * hd, nullptr, 0, 0, Hq, Hkv, hd,
+                             c->gemm_ws, c->gemm_ws_bytes, s);
+  TRY(gemm(c, x, H, w.w_qkv, M, nqkv, H, DFL_EPI_STORE, nullptr, 0, qkv, nqkv, nullptr, 0, nullptr, w.in_norm, ss,
+           nullptr, eps, s));
+  return dfl_qkv_rope_append(qkv, nqkv, hd, pos, row_seq, w.q_norm, w.k_norm, inv_freq, q, kc, vc,
+                             (int64_t)Hkv * c->cap * hd, (int64_t)c->cap * hd, M, Hq, Hkv, hd, rot_dim, eps, 1, s);
+}
+
 // One dfl_gemm_op (the arguments of gemm() above).
 dfl_gemm_op gop(const void* x, int64_t ldx, const void* w, int M, int N, int K, int epi, const void* res, int64_t ldr,
                 void* y, int64_t ldy, void* y2, int64_t ldy2, void* part, const void* norm_w, const float* ss_in,
@@ -225,11 +251,8 @@ int target_forward(Ctx* c, const int* tokens, const int* pos, int M, const int* 
     const dfl_layer_weights& w = c->tl[l];
     __nv_bfloat16* kc = c->tk + (size_t)l * kv_layer_elems(c, Hkv, hd);
     __nv_bfloat16* vc = c->tv + (size_t)l * kv_layer_elems(c, Hkv, hd);
-    TRY(gemm(c, c->h, H, w.w_qkv, M, nqkv, H, DFL_EPI_STORE, nullptr, 0, c->qkv, nqkv, nullptr, 0, nullptr,
-             w.in_norm, c->ss, nullptr, eps, s));
-    TRY(dfl_qkv_rope_append(c->qkv, nqkv, hd, pos, row_seq, w.q_norm, w.k_norm, c->t_inv_freq, c->q, kc, vc,
-                            (int64_t)Hkv * c->cap * hd, (int64_t)c->cap * hd, M, Hq, Hkv, hd, t.rope_dim, eps, 1,
-                            s));
+    TRY(qkv_rope(c, c->h, c->ss, H, w, M, Hq, Hkv, hd, t.rope_dim, eps, pos, row_seq, c->t_inv_freq, c->qkv, c->q,
+                 kc, vc, s));
     TRY(dfl_attention(c->q, kc, vc, (int64_t)Hkv * c->cap * hd, (int64_t)c->cap * hd, pos, row_seq, nullptr,
                       seq_rows, M, Hq, Hkv, hd, 1, (float)(1.0 / std::sqrt((double)hd)), max_kv, c->key_chunk, c->attn,
                       Hq * hd, nullptr, 0, 0, c->attn_ws, c->attn_ws_bytes, s));
@@ -319,10 +342,8 @@ int draft_block(Ctx* c, cudaStream_t s) {
     const dfl_layer_weights& w = c->dl[l];
     __nv_bfloat16* kc = c->dk + (size_t)l * kv_layer_elems(c, Hkv, hd);
     __nv_bfloat16* vc = c->dv + (size_t)l * kv_layer_elems(c, Hkv, hd);
-    TRY(gemm(c, c->dh, H, w.w_qkv, M, nqkv, H, DFL_EPI_STORE, nullptr, 0, c->dqkv, nqkv, nullptr, 0, nullptr,
-             w.in_norm, c->dss, nullptr, eps, s));
-    TRY(dfl_qkv_rope_append(c->dqkv, nqkv, hd, c->dpos_blk, rs, w.q_norm, w.k_norm, c->d_inv_freq, c->dq, kc, vc,
-                            (int64_t)Hkv * c->cap * hd, (int64_t)c->cap * hd, M, Hq, Hkv, hd, hd, eps, 1, s));
+    TRY(qkv_rope(c, c->dh, c->dss, H, w, M, Hq, Hkv, hd, hd, eps, c->dpos_blk, rs, c->d_inv_freq, c->dqkv, c->dq, kc,
+                 vc, s));
     TRY(dfl_attention(c->dq, kc, vc, (int64_t)Hkv * c->cap * hd, (int64_t)c->cap * hd, c->dpos_blk, rs, c->dkv_len,
                       c->bs, M, Hq, Hkv, hd, d.causal, (float)(1.0 / std::sqrt((double)hd)), c->cap, c->key_chunk, c->dattn,
                       Hq * hd, nullptr, 0, 0, c->attn_ws, c->attn_ws_bytes, s));
@@ -444,7 +465,7 @@ extern "C" int dfl_ctx_create(const dfl_qwen3_desc* target, const dfl_draft_desc
   c->cap = max_total + 2 * block_size + 1;
   c->max_steps = max_steps > 0 ? max_steps : max_total + 1;
   c->batched = batch >= 4;
-  c->key_chunk = c->batched ? 1024 : 128;
+  c->key_chunk = c->batched ? 1024 : 64;  // as the Python host's SpecSession
   c->wide_split_max = c->batched ? (batch < 16 ? 4 : 1) : 1;
   c->use_graph = !(flags & DFL_CTX_NO_GRAPH);
   {

@@ -35,6 +35,7 @@
 //    the library's device error word and falls through to its teardown.
 #include "tma_util.cuh"
 #include "tcgen05.cuh"
+#include "rope.cuh"
 
 #include <cstring>
 #include <mutex>
@@ -132,6 +133,10 @@ struct TcArgs {
   int M, N, K, n_tiles, kb;
   long long U1;
   int grid1;
+  // fused q/k head norm + RoPE + KV append after the QKV projection (cluster split-K form,
+  // head_dim 128 = one column tile per head, M <= 16): rope_on selects it
+  int rope_on;
+  QkvArgs rope;
 };
 
 // tcgen05 helpers (descriptors, MMA issue, commit, fences, TMEM loads): tcgen05.cuh
@@ -763,6 +768,16 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
     }
   }
   cluster_wait();  // no CTA leaves while a push to it may be in flight
+  if (EPI == DFL_EPI_STORE && a.rope_on) {
+    // fused q/k head norm + RoPE + KV append: column tile nt is head nt. One more cluster
+    // barrier makes every owner's stores of the tile visible to the whole cluster; the rows
+    // are then spread over the ranks' warps (row m on rank m % S), each running
+    // dfl_qkv_rope_append's arithmetic with the idle weight ring as its row buffer.
+    cluster_arrive();
+    cluster_wait();
+    float* buf = reinterpret_cast<float*>(smem) + warp * 128;
+    for (int m = r + S * warp; m < a.M; m += S * (TC_THREADS / 32)) qkv_rope_row(a.rope, m, nt, lane, buf);
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -1624,10 +1639,14 @@ extern "C" int dfl_pack_weight_bf16(const void* w, int N, int K, void* out, size
   return check_launch("dfl_pack_weight_bf16");
 }
 
-extern "C" int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w_packed, int M, int N, int K, int epilogue,
-                             const void* residual, int64_t ldr, void* y, int64_t ldy, void* y2, int64_t ldy2,
-                             void* argmax_partials, const void* norm_w, const float* sumsq_in, int n_parts,
-                             float eps, float* sumsq_out, void* workspace, size_t workspace_bytes, void* stream) {
+// rope (nullable): fuse the q/k head norm + RoPE + append into the QKV projection when the
+// plan is the cluster split-K form over one 16-row tile; *fused reports whether it was
+static int gemm_bf16_impl(const void* x, int64_t ldx, const void* w_packed, int M, int N, int K, int epilogue,
+                          const void* residual, int64_t ldr, void* y, int64_t ldy, void* y2, int64_t ldy2,
+                          void* argmax_partials, const void* norm_w, const float* sumsq_in, int n_parts, float eps,
+                          float* sumsq_out, void* workspace, size_t workspace_bytes, void* stream,
+                          const QkvArgs* rope = nullptr, bool* fused = nullptr) {
+  if (fused) *fused = false;
   if (M == 0) return DFL_OK;
   const void* w = w_packed;
   if (!x || !w || M < 0 || N <= 0 || K <= 0) {
@@ -1699,6 +1718,10 @@ extern "C" int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w_packed, i
   a.kb = p.kb;
   a.U1 = p.U1;
   a.grid1 = p.grid1;
+  a.rope_on = rope && p.S && p.m_tiles == 1 && epilogue == DFL_EPI_STORE;
+  if (a.rope_on) a.rope = *rope;
+  else memset(&a.rope, 0, sizeof(a.rope));
+  if (fused) *fused = a.rope_on;
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = p.S ? dim3(p.S, p.n_tiles, p.m_tiles) : dim3(p.grid1 * p.m_tiles);
@@ -1766,6 +1789,78 @@ extern "C" int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w_packed, i
     return DFL_ERR_CUDA;
   }
   return DFL_OK;
+}
+
+extern "C" int dfl_gemm_bf16(const void* x, int64_t ldx, const void* w_packed, int M, int N, int K, int epilogue,
+                             const void* residual, int64_t ldr, void* y, int64_t ldy, void* y2, int64_t ldy2,
+                             void* argmax_partials, const void* norm_w, const float* sumsq_in, int n_parts,
+                             float eps, float* sumsq_out, void* workspace, size_t workspace_bytes, void* stream) {
+  return gemm_bf16_impl(x, ldx, w_packed, M, N, K, epilogue, residual, ldr, y, ldy, y2, ldy2, argmax_partials, norm_w,
+                        sumsq_in, n_parts, eps, sumsq_out, workspace, workspace_bytes, stream);
+}
+
+extern "C" int dfl_gemm_qkv_rope(const void* x, int64_t ldx, const void* w_packed, int M, int K, const void* norm_w,
+                                 const float* sumsq_in, int n_parts, float eps, void* qkv, int64_t ldqkv,
+                                 const int32_t* pos, const int32_t* row_seq, const void* q_norm, const void* k_norm,
+                                 const float* inv_freq, void* q_out, void* k_cache, void* v_cache, int64_t seq_stride,
+                                 int64_t head_stride, const int32_t* page_table, int64_t pt_stride, int page_size,
+                                 int Hq, int Hkv, int hd, void* workspace, size_t workspace_bytes, void* stream) {
+  if (M == 0) return DFL_OK;
+  if (!pos || !q_norm || !k_norm || !inv_freq || !q_out || !k_cache || !v_cache || Hq <= 0 || Hkv <= 0 || hd <= 0) {
+    set_error("dfl_gemm_qkv_rope: null pointer or bad head geometry");
+    return DFL_ERR_INVALID;
+  }
+  QkvArgs r;
+  memset(&r, 0, sizeof(r));
+  r.qkv = static_cast<const __nv_bfloat16*>(qkv);
+  r.ldqkv = ldqkv;
+  r.q_stride = hd;
+  r.pos = pos;
+  r.row_seq = row_seq;
+  r.q_norm = static_cast<const __nv_bfloat16*>(q_norm);
+  r.k_norm = static_cast<const __nv_bfloat16*>(k_norm);
+  r.inv_freq = inv_freq;
+  r.q_out = static_cast<__nv_bfloat16*>(q_out);
+  r.k_cache = static_cast<__nv_bfloat16*>(k_cache);
+  r.v_cache = static_cast<__nv_bfloat16*>(v_cache);
+  r.seq_stride = seq_stride;
+  r.head_stride = head_stride;
+  r.M = M;
+  r.Hq = Hq;
+  r.Hkv = Hkv;
+  r.hd = hd;
+  r.rot_dim = hd;
+  r.eps = eps;
+  r.do_q = 1;
+  r.page_table = page_table;
+  r.pt_stride = pt_stride;
+  r.page_shift = 0;
+  if (page_table) {
+    if (page_size < 64 || (page_size & (page_size - 1)) || pt_stride <= 0) {
+      set_error("dfl_gemm_qkv_rope: page_size must be a power of two >= 64 (got %d)", page_size);
+      return DFL_ERR_INVALID;
+    }
+    while ((1 << r.page_shift) < page_size) ++r.page_shift;
+  }
+  const int N = (Hq + 2 * Hkv) * hd;
+  bool fused = false;
+  const int st = gemm_bf16_impl(x, ldx, w_packed, M, N, K, DFL_EPI_STORE, nullptr, 0, qkv, ldqkv, nullptr, 0, nullptr,
+                                norm_w, sumsq_in, n_parts, eps, nullptr, workspace, workspace_bytes, stream,
+                                hd == TC_NT ? &r : nullptr, &fused);
+  if (st != DFL_OK || fused) return st;
+  // another GEMM form: the separate append kernel (the same arithmetic)
+  if (page_table)
+    return dfl_qkv_rope_append_paged(qkv, ldqkv, hd, pos, row_seq, q_norm, k_norm, inv_freq, q_out, k_cache, v_cache,
+                                     seq_stride, head_stride, page_table, pt_stride, page_size, M, Hq, Hkv, hd, hd, eps,
+                                     1, stream);
+  return dfl_qkv_rope_append(qkv, ldqkv, hd, pos, row_seq, q_norm, k_norm, inv_freq, q_out, k_cache, v_cache,
+                             seq_stride, head_stride, M, Hq, Hkv, hd, hd, eps, 1, stream);
+}
+
+extern "C" int dfl_gemm_qkv_rope_launches(int M, int K, int Hq, int Hkv, int hd) {
+  if (M <= 0 || K <= 0 || K % TC_BK || Hq <= 0 || Hkv <= 0 || hd <= 0) return -1;
+  const TcPlan p = tc_plan(M, (Hq + 2 * Hkv) * hd, K);
+  return (hd == TC_NT && p.S && p.m_tiles == 1) ? 1 : 2;
 }
 
 static int wide_split_of(int K, int k_split) {

@@ -11,6 +11,7 @@
 // All kernels are one warp per row (or per row x head): the reduction order of a
 // row never depends on how many rows a launch carries.
 #include "common.cuh"
+#include "rope.cuh"
 
 namespace dfl {
 
@@ -84,46 +85,6 @@ __global__ void embed_kernel(const int* __restrict__ tok, const __nv_bfloat16* _
   }
 }
 
-// -------------------------------------------------------------------------
-// q/k head RMSNorm + RoPE + KV append.
-//
-// qkv row layout: [q heads (Hq x q_stride, first hd of each is q) | k heads (Hkv x hd) | v heads (Hkv x hd)].
-// K/V cache layout per layer: [seq][Hkv][cap][hd] bf16; the token at position p
-// lives in slot p. Paged form: [page][Hkv][page_size][hd] and a page table
-// [seq][pt_stride] of page indices; position p of sequence s lives in page
-// table[s][p / page_size], row p % page_size. pos[r] < 0 marks a row that is
-// skipped entirely.
-// q_out: [M][Hq][hd] bf16.
-// -------------------------------------------------------------------------
-struct QkvArgs {
-  const __nv_bfloat16* qkv;
-  long long ldqkv;
-  int q_stride;  // elements between consecutive q heads inside a row (hd, or 2*hd with an output gate)
-  const int* pos;
-  const int* row_seq;  // nullable: all rows belong to sequence 0
-  const __nv_bfloat16* q_norm;
-  const __nv_bfloat16* k_norm;
-  const float* inv_freq;  // [rot_dim/2]
-  __nv_bfloat16* q_out;
-  __nv_bfloat16* k_cache;
-  __nv_bfloat16* v_cache;
-  long long seq_stride, head_stride;  // elements
-  int M, Hq, Hkv, hd, rot_dim;
-  float eps;
-  int do_q;  // 0: skip q heads (context rows of the draft)
-  const int* page_table;  // nullable: contiguous [seq][Hkv][cap][hd] caches
-  long long pt_stride;
-  int page_shift;         // log2(page_size)
-};
-
-// element offset of (sequence, kv head, position) in a contiguous or paged cache
-__device__ __forceinline__ long long kv_offset(const int* pt, long long pt_stride, int shift, long long seq_stride,
-                                               long long head_stride, int seq, int h, int p, int hd) {
-  if (!pt) return seq * seq_stride + h * head_stride + (long long)p * hd;
-  const long long page = pt[seq * pt_stride + (p >> shift)];
-  return page * seq_stride + h * head_stride + (long long)(p & ((1 << shift) - 1)) * hd;
-}
-
 __global__ void qkv_rope_append_kernel(QkvArgs a) {
   grid_dependency_launch_dependents();
   grid_dependency_wait();
@@ -132,54 +93,7 @@ __global__ void qkv_rope_append_kernel(QkvArgs a) {
   const int nheads = a.Hq + 2 * a.Hkv;
   const long long item = (long long)blockIdx.x * (blockDim.x >> 5) + warp;
   if (item >= (long long)a.M * nheads) return;
-  const int row = (int)(item / nheads);
-  const int head = (int)(item % nheads);
-  const int p = a.pos[row];
-  if (p < 0) return;
-  const int seq = a.row_seq ? a.row_seq[row] : 0;
-  const __nv_bfloat16* src;
-  const __nv_bfloat16* nw = nullptr;
-  __nv_bfloat16* dst;
-  const __nv_bfloat16* qkv_row = a.qkv + (long long)row * a.ldqkv;
-  if (head < a.Hq) {
-    if (!a.do_q) return;
-    src = qkv_row + (long long)head * a.q_stride;
-    nw = a.q_norm;
-    dst = a.q_out + ((long long)row * a.Hq + head) * a.hd;
-  } else if (head < a.Hq + a.Hkv) {
-    const int kh = head - a.Hq;
-    src = qkv_row + (long long)a.Hq * a.q_stride + (long long)kh * a.hd;
-    nw = a.k_norm;
-    dst = a.k_cache + kv_offset(a.page_table, a.pt_stride, a.page_shift, a.seq_stride, a.head_stride, seq, kh, p, a.hd);
-  } else {
-    const int vh = head - a.Hq - a.Hkv;
-    src = qkv_row + (long long)a.Hq * a.q_stride + (long long)(a.Hkv + vh) * a.hd;
-    dst = a.v_cache + kv_offset(a.page_table, a.pt_stride, a.page_shift, a.seq_stride, a.head_stride, seq, vh, p, a.hd);
-    for (int i = lane; i < a.hd; i += 32) dst[i] = src[i];
-    return;
-  }
-  float* buf = sh + warp * a.hd;
-  float ss = 0.f;
-  for (int i = lane; i < a.hd; i += 32) {
-    const float f = bf2f(src[i]);
-    buf[i] = f;
-    ss = sq_acc(ss, f);
-  }
-  ss = warp_sum(ss);
-  const float inv = rsqrtf(ss / (float)a.hd + a.eps);
-  for (int i = lane; i < a.hd; i += 32) buf[i] = round_bf16(bf2f(nw[i]) * (buf[i] * inv));
-  __syncwarp();
-  const int half = a.rot_dim >> 1;
-  for (int i = lane; i < a.hd; i += 32) {
-    float o = buf[i];
-    if (i < a.rot_dim) {
-      const int j = i < half ? i : i - half;
-      float s, c;
-      sincosf(rope_angle(p, a.inv_freq[j]), &s, &c);
-      o = rope_rot(buf[i], i < half ? buf[i + half] : buf[i - half], c, s, i < half);
-    }
-    dst[i] = f2bf(o);
-  }
+  qkv_rope_row(a, (int)(item / nheads), (int)(item % nheads), lane, sh + warp * a.hd);
 }
 
 }  // namespace dfl

@@ -55,6 +55,11 @@ SIGNATURES: dict[str, tuple] = {
     "dfl_pack_weight_bf16": (c_int, [c_void_p, c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "dfl_rmsnorm_bf16": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_int, c_int, c_float, c_void_p]),
     "dfl_embed_bf16": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int, c_int, c_int, c_void_p, c_void_p]),
+    "dfl_gemm_qkv_rope": (c_int, [c_void_p, c_int64, c_void_p, c_int, c_int, c_void_p, c_void_p, c_int, c_float,
+                                  c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                  c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int, c_int, c_int, c_int,
+                                  c_void_p, c_size_t, c_void_p]),
+    "dfl_gemm_qkv_rope_launches": (c_int, [c_int, c_int, c_int, c_int, c_int]),
     "dfl_qkv_rope_append": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                     c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_int, c_int,
                                     c_float, c_int, c_void_p]),

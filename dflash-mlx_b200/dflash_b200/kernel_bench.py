@@ -12,6 +12,9 @@ Cases (synthetic inputs, shapes and distributions of the benchmark configuration
   gdr_t16     gated-delta recurrence, B=1, T=16, 16 QK / 32 V heads of 128, with
               per-token snapshots (config 2): bytes = state in + q,k,v,g,beta + o +
               T snapshots (the last one is the final state)
+  gdr_t64     (only when named) T=64 with snapshots: 134 MB of snapshots, more than the
+              126 MB L2, so a profile attributes the snapshot writes to DRAM (at T=16 they
+              stay in L2 until after the kernel)
   gdr_t4096   the same over T=4096 without snapshots (final state only); a
               sequential recurrence, reported against both roofs
   attn_c3     verify attention, 1 sequence x 16 rows, Qwen3-4B heads, context 1536
@@ -203,6 +206,8 @@ def main(argv=None):
     timer = Timer(args.iters, args.warmup)
     if sel & {"gdr", "gdr_t16"}:
         bench_gdr(timer, 16, True)
+    if "gdr_t64" in sel:  # snapshots (134 MB) larger than L2: the capture attributes their DRAM writes
+        bench_gdr(timer, 64, True)
     if sel & {"gdr", "gdr_t4096"}:
         bench_gdr(timer, 4096, False)
     if sel & {"attn", "attn_c3"}:

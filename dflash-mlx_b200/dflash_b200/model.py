@@ -85,6 +85,16 @@ def gemm_chain_enabled() -> bool:
     return os.environ.get("DFLASH_B200_GEMM_CHAIN", "0") == "1"
 
 
+def qkv_rope_ok(ws, hd: int, rot_dim: int) -> bool:
+    """Whether a decoder layer's QKV projection takes the fused q/k norm + RoPE + append
+    call (ops.gemm_qkv_rope: the same bits as the separate calls): full rotary, the M <= 16
+    GEMM forms (not a wide workspace), and DFLASH_B200_FUSED_QKV_ROPE=1 (opt-in: measured
+    slower than the separate append kernel in the Qwen3-4B step)."""
+    if os.environ.get("DFLASH_B200_FUSED_QKV_ROPE", "0") != "1":
+        return False
+    return rot_dim == hd and not (ws is not None and ws.wide)
+
+
 def chain_ok(M: int, ws) -> bool:
     """Whether a forward over M rows uses GEMM chains: decode blocks of the one-sequence
     (weight-streaming) kernel forms; decided by M and the session's kernel forms only."""
@@ -217,17 +227,23 @@ class TargetModel:
         if self.use_chain and chain_ok(M, ws):
             return self._forward_chain(pos, cache, max_kv, tap_col, taps_out, row_seq, head, ws, seq_rows, key_chunk,
                                        fused, b)
+        qkv_rope = not fused and qkv_rope_ok(ws, hd, c.rope_dim)
         for l, lw in enumerate(self.layers):
             kc, vc = cache.layer(l)
-            # input_layernorm fused into the QKV projection
-            ops.gemm(h, lw["w_qkv"], out=b["qkv"], ws=ws, norm_w=lw["in_norm"], sumsq_in=ss, eps=eps)
+            if qkv_rope:  # input_layernorm, QKV projection, q/k norm + RoPE + append: one call
+                ops.gemm_qkv_rope(h, lw["w_qkv"], b["qkv"], pos, lw["q_norm"], lw["k_norm"], self.inv_freq, kc, vc,
+                                  b["q"], Hq, Hkv, hd, eps, norm_w=lw["in_norm"], sumsq_in=ss, row_seq=row_seq,
+                                  ws=ws, **pg)
+            else:  # input_layernorm fused into the QKV projection
+                ops.gemm(h, lw["w_qkv"], out=b["qkv"], ws=ws, norm_w=lw["in_norm"], sumsq_in=ss, eps=eps)
             if fused:  # q/k norm + RoPE + append inside the attention launch (same bits)
                 ops.attention_qkv(b["qkv"], pos, lw["q_norm"], lw["k_norm"], self.inv_freq, kc, vc, Hq, eps,
                                   max_kv, row_seq=row_seq, out=b["attn"], ws=ws, seq_rows=seq_rows,
                                   key_chunk=key_chunk)
             else:
-                ops.qkv_rope_append(b["qkv"], pos, lw["q_norm"], lw["k_norm"], self.inv_freq, kc, vc, Hq, Hkv, hd,
-                                    c.rope_dim, eps, q_out=b["q"], row_seq=row_seq, **pg)
+                if not qkv_rope:
+                    ops.qkv_rope_append(b["qkv"], pos, lw["q_norm"], lw["k_norm"], self.inv_freq, kc, vc, Hq, Hkv,
+                                        hd, c.rope_dim, eps, q_out=b["q"], row_seq=row_seq, **pg)
                 ops.attention(b["q"], kc, vc, pos, causal=True, max_kv=max_kv, row_seq=row_seq, out=b["attn"],
                               ws=ws, seq_rows=seq_rows, key_chunk=key_chunk, **pg)
             ops.gemm(b["attn"], lw["w_o"], ops.EPI_RESIDUAL, residual=h, out=h, ws=ws, sumsq_out=ss)
@@ -512,11 +528,17 @@ class DraftModel:
                 if l + 1 < len(self.layers):
                     pending.append(qkv_op(self.layers[l + 1]))
             return chain_head(pending, h, ss, self.target.lm_head_w, self.norm_w, eps, head, b, ws)
+        qkv_rope = qkv_rope_ok(ws, hd, hd)
         for l, lw in enumerate(self.layers):
             kc, vc = cache.layer(l)
-            ops.gemm(h, lw["w_qkv"], out=b["qkv"], ws=ws, norm_w=lw["in_norm"], sumsq_in=ss, eps=eps)
-            ops.qkv_rope_append(b["qkv"], pos, lw["q_norm"], lw["k_norm"], self.inv_freq, kc, vc, Hq, Hkv, hd, hd,
-                                eps, q_out=b["q"], row_seq=row_seq, **cache.paging)
+            if qkv_rope:  # QKV projection + q/k norm + RoPE + append in one call (same bits)
+                ops.gemm_qkv_rope(h, lw["w_qkv"], b["qkv"], pos, lw["q_norm"], lw["k_norm"], self.inv_freq, kc, vc,
+                                  b["q"], Hq, Hkv, hd, eps, norm_w=lw["in_norm"], sumsq_in=ss, row_seq=row_seq,
+                                  ws=ws, **cache.paging)
+            else:
+                ops.gemm(h, lw["w_qkv"], out=b["qkv"], ws=ws, norm_w=lw["in_norm"], sumsq_in=ss, eps=eps)
+                ops.qkv_rope_append(b["qkv"], pos, lw["q_norm"], lw["k_norm"], self.inv_freq, kc, vc, Hq, Hkv, hd,
+                                    hd, eps, q_out=b["q"], row_seq=row_seq, **cache.paging)
             ops.attention(b["q"], kc, vc, pos, causal=causal, max_kv=max_kv, kv_len=kv_len, row_seq=row_seq,
                           seq_rows=seq_rows, key_chunk=key_chunk, out=b["attn"], ws=ws, **cache.paging)
             ops.gemm(b["attn"], lw["w_o"], ops.EPI_RESIDUAL, residual=h, out=h, ws=ws, sumsq_out=ss)

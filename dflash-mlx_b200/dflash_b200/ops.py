@@ -309,6 +309,39 @@ def qkv_rope_append(qkv: torch.Tensor, pos: torch.Tensor, q_norm: torch.Tensor, 
     return q_out
 
 
+def gemm_qkv_rope(x: torch.Tensor, w: PackedWeight | torch.Tensor, qkv: torch.Tensor, pos: torch.Tensor, q_norm: torch.Tensor,
+                  k_norm: torch.Tensor, inv_freq: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                  q_out: torch.Tensor, Hq: int, Hkv: int, hd: int, eps: float, norm_w: torch.Tensor | None = None,
+                  sumsq_in: torch.Tensor | None = None, row_seq: torch.Tensor | None = None,
+                  ws: Workspace | None = None, page_table: torch.Tensor | None = None, page_size: int = 0) -> None:
+    """The QKV projection (input RMSNorm fused when norm_w is given) into ``qkv``, then the
+    q/k head norm + RoPE (full rotary) + cache append of qkv_rope_append, as one call
+    (dfl_gemm_qkv_rope): the same bits as gemm() followed by qkv_rope_append()."""
+    if isinstance(w, torch.Tensor):  # convenience for tests: pack on the fly
+        w = PackedWeight(w)
+    _need_cuda(x, qkv, pos, q_norm, k_norm, inv_freq, k_cache, v_cache, q_out, norm_w, sumsq_in, row_seq, page_table)
+    M, K = x.shape
+    N = (Hq + 2 * Hkv) * hd
+    if tuple(w.shape) != (N, K) or qkv.shape[0] < M or qkv.shape[1] < N:
+        raise ValueError(f"gemm_qkv_rope shape mismatch x{tuple(x.shape)} w{tuple(w.shape)} qkv{tuple(qkv.shape)}")
+    if k_cache.dim() != 4 or k_cache.stride(3) != 1 or k_cache.stride(2) != hd:
+        raise ValueError("k_cache must be a [seq, Hkv, cap, hd] view (or a page pool)")
+    ws = ws or workspace(x.device)
+    if ws.wide:
+        raise ValueError("gemm_qkv_rope runs the M <= 16 weight-streaming forms only")
+    ws.ensure_gemm(int(_lib.query("dfl_gemm_workspace_bytes", M, N, K, EPI_STORE)))
+    n_parts = 0
+    if norm_w is not None:
+        if sumsq_in is None or sumsq_in.dtype != torch.float32 or not sumsq_in.is_contiguous():
+            raise ValueError("the fused RMSNorm needs contiguous fp32 sumsq_in partials [M, K/32]")
+        n_parts = sumsq_in.shape[1]
+    _lib.call("dfl_gemm_qkv_rope", _ptr(x), _row_stride(x), _ptr(w), M, K, _ptr(norm_w), _ptr(sumsq_in), n_parts,
+              float(eps), _ptr(qkv), _row_stride(qkv), _ptr(pos), _ptr(row_seq), _ptr(q_norm), _ptr(k_norm),
+              _ptr(inv_freq), _ptr(q_out), _ptr(k_cache), _ptr(v_cache), k_cache.stride(0), k_cache.stride(1),
+              _ptr(page_table), page_table.stride(0) if page_table is not None else 0, int(page_size), Hq, Hkv, hd,
+              _ptr(ws.gemm), ws.gemm.numel(), _stream())
+
+
 def attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, pos: torch.Tensor, causal: bool,
               max_kv: int, kv_len: torch.Tensor | None = None, row_seq: torch.Tensor | None = None,
               scale: float | None = None, out: torch.Tensor | None = None, ws: Workspace | None = None,

@@ -108,10 +108,12 @@ class SpecSession:
         # batch size alone so that a batch's plain decode and its speculative decode
         # use the same arithmetic: attention splits keys every 1024 positions (a batch
         # already fills the SMs; long splits cut the partial-result traffic) instead of
-        # every 128, and every GEMM runs whole-K tensor-core tiles (weights read once for
-        # all rows) instead of the M <= 16 weight-streaming split-K form
+        # every 64 (one 64-key block per CTA: the most SMs on a single stream's keys,
+        # measured fastest on B200 at config 3's contexts), and every GEMM runs whole-K
+        # tensor-core tiles (weights read once for all rows) instead of the M <= 16
+        # weight-streaming split-K form
         self.batched = batch >= 4
-        self.key_chunk = 1024 if self.batched else 128
+        self.key_chunk = 1024 if self.batched else 64
         self.out_cap = self.cap
         self.max_steps = max_steps or (max_total + 1)
         # under 16 sequences, weights with few 128-row tiles also split K (fixed ranges)

@@ -247,6 +247,25 @@ int dfl_qkv_rope_append_paged(const void* qkv, int64_t ldqkv, int q_stride, cons
                               void* k_pages, void* v_pages, int64_t page_stride, int64_t head_stride,
                               const int32_t* page_table, int64_t pt_stride, int page_size, int M, int Hq, int Hkv,
                               int hd, int rot_dim, float eps, int do_q, void* stream);
+/* The QKV projection of a decoder layer with the q/k head norm + RoPE + KV append fused
+ * into it: dfl_gemm_bf16 (store epilogue; input RMSNorm prologue when norm_w is given)
+ * writing the projection rows qkv [M][(Hq + 2 Hkv) * hd] (row stride ldqkv), then
+ * dfl_qkv_rope_append over them (q_stride = rot_dim = hd, eps for the input norm and the
+ * head norms, as Qwen3's rms_norm_eps), with the same bits as those two calls. For the
+ * weight-streaming cluster form (M <= 16, head_dim 128: one output tile per head) the
+ * append runs inside the GEMM launch after the tile's split-K reduction; otherwise the
+ * two kernels run. page_table (nullable) as dfl_qkv_rope_append_paged. Replaces the
+ * q/k/v projections + q_norm/k_norm + rope + KVCache.update_and_fetch of mlx-lm qwen3
+ * Attention (driven from adapters.py:611-631) and of draft.py:118-147. */
+int dfl_gemm_qkv_rope(const void* x, int64_t ldx, const void* w_packed, int M, int K, const void* norm_w,
+                      const float* sumsq_in, int n_parts, float eps, void* qkv, int64_t ldqkv, const int32_t* pos,
+                      const int32_t* row_seq, const void* q_norm, const void* k_norm, const float* inv_freq,
+                      void* q_out, void* k_cache, void* v_cache, int64_t seq_stride, int64_t head_stride,
+                      const int32_t* page_table, int64_t pt_stride, int page_size, int Hq, int Hkv, int hd,
+                      void* workspace, size_t workspace_bytes, void* stream);
+/* Kernel launches one dfl_gemm_qkv_rope call of this shape makes (1: the append inside the
+ * GEMM launch; 2: GEMM + append kernel), -1 for a bad shape. */
+int dfl_gemm_qkv_rope_launches(int M, int K, int Hq, int Hkv, int hd);
 int dfl_attention_paged(const void* q, const void* k_pages, const void* v_pages, int64_t page_stride,
                         int64_t head_stride, const int32_t* page_table, int64_t pt_stride, int page_size,
                         const int32_t* pos, const int32_t* row_seq, const int32_t* kv_len, int seq_rows, int M, int Hq,

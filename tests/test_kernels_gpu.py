@@ -658,3 +658,70 @@ def test_gemm_chain_ops_with_fewer_units_than_ctas(N, K):
     assert d.max().item() <= 2 ** -7 * y1.float().abs().max().item(), d.max().item()
     assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
     assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("case", ["qwen3_4b", "qwen3_4b_paged", "two_seqs", "rows_20", "hd64"])
+def test_gemm_qkv_rope_matches_separate_calls(case):
+    """dfl_gemm_qkv_rope (the QKV projection with the q/k head norm + RoPE + cache append
+    after its split-K reduction, in the GEMM launch) against dfl_gemm_bf16 followed by
+    dfl_qkv_rope_append on the same inputs: projection rows, q and both caches bit for
+    bit. At the Qwen3-4B verify shape the append kernel must not run (the fused form);
+    20 rows (two row tiles) and head_dim 64 take the two-kernel form inside the call."""
+    from dflash_b200.weights import rope_inv_freq
+    ops = _ops()
+    H, Hq, Hkv, hd, M = 2560, 32, 8, 128, 16
+    if case == "rows_20":
+        M = 20
+    if case == "hd64":
+        H, Hq, Hkv, hd = 256, 4, 2, 64
+    n_seq = 2 if case == "two_seqs" else 1
+    N = (Hq + 2 * Hkv) * hd
+    x = _rand((M, H), 1.0, 60).to(DEV)
+    w = ops.PackedWeight(_rand((N, H), 0.02, 61).to(DEV))
+    in_norm = (1.0 + 0.1 * _rand((H,), 1.0, 62).float()).bfloat16().to(DEV)
+    qn, kn = _rand((hd,), 1.0, 63).to(DEV), _rand((hd,), 1.0, 64).to(DEV)
+    ss = (x.float() ** 2).reshape(M, H // 32, 32).sum(-1).contiguous()
+    inv = rope_inv_freq(hd, 1e6).to(DEV)
+    if n_seq == 2:
+        pos = torch.tensor(list(range(300, 308)) + list(range(811, 819)), dtype=torch.int32, device=DEV)
+        row_seq = torch.tensor([0] * 8 + [1] * 8, dtype=torch.int32, device=DEV)
+    else:
+        pos = torch.arange(1000, 1000 + M, dtype=torch.int32, device=DEV)
+        pos[3] = -1  # a skipped row
+        row_seq = None
+    cap = 1152
+    paged = case == "qwen3_4b_paged"
+    pg = {}
+    if paged:
+        n_pages = cap // 64
+        perm = torch.randperm(n_pages, generator=torch.Generator().manual_seed(65)).to(torch.int32).to(DEV)
+        pg = {"page_table": perm.view(1, -1), "page_size": 64}
+
+    def caches():
+        shape = (cap // 64, Hkv, 64, hd) if paged else (n_seq, Hkv, cap, hd)
+        return torch.zeros(shape, dtype=torch.bfloat16, device=DEV), torch.zeros(shape, dtype=torch.bfloat16,
+                                                                                   device=DEV)
+
+    kc0, vc0 = caches()
+    qkv0 = torch.zeros((M, N), dtype=torch.bfloat16, device=DEV)
+    ops.gemm(x, w, out=qkv0, norm_w=in_norm, sumsq_in=ss)
+    q0 = ops.qkv_rope_append(qkv0, pos, qn, kn, inv, kc0, vc0, Hq, Hkv, hd, hd, 1e-6, row_seq=row_seq, **pg)
+    kc1, vc1 = caches()
+    qkv1 = torch.zeros((M, N), dtype=torch.bfloat16, device=DEV)
+    q1 = torch.zeros((M, Hq, hd), dtype=torch.bfloat16, device=DEV)
+    q1[3] = q0[3]  # the skipped row is left as it was
+    from torch.profiler import ProfilerActivity, profile
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        ops.gemm_qkv_rope(x, w, qkv1, pos, qn, kn, inv, kc1, vc1, q1, Hq, Hkv, hd, 1e-6, norm_w=in_norm, sumsq_in=ss,
+                          row_seq=row_seq, **pg)
+        torch.cuda.synchronize()
+    names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+    assert ops.device_error() == 0
+    assert torch.equal(qkv1, qkv0)
+    assert torch.equal(q1, q0)
+    assert torch.equal(kc1, kc0) and torch.equal(vc1, vc0)
+    assert kc1.abs().sum().item() > 0
+    appended = any("qkv_rope_append" in n for n in names)
+    print(case, "kernels:", sorted(set(n[:40] for n in names)))
+    if names:
+        assert appended == (case in ("rows_20", "hd64")), names

@@ -141,15 +141,15 @@ int gemm(Ctx* c, const void* x, int64_t ldx, const void* w, int M, int N, int K,
 size_t kv_layer_elems(const Ctx* c, int hkv, int hd) { return (size_t)c->B * hkv * c->cap * hd; }
 
 // The QKV projection (input RMSNorm fused) and the q/k head norm + RoPE + cache append of
-// one decoder layer: one dfl_gemm_qkv_rope call on the M <= 16 GEMM forms when
-// DFLASH_B200_FUSED_QKV_ROPE=1 (the Python host's model.qkv_rope_ok rule), else the two
+// one decoder layer: one dfl_gemm_qkv_rope call on the M <= 16 GEMM forms unless
+// DFLASH_B200_FUSED_QKV_ROPE=0 (the Python host's model.qkv_rope_ok rule), else the two
 // calls; both give the same bits.
 bool fused_qkv_rope(const Ctx* c, int hd, int rot_dim) {
-  static const bool on = [] {
+  static const bool off = [] {
     const char* e = std::getenv("DFLASH_B200_FUSED_QKV_ROPE");
-    return e && e[0] == '1';
+    return e && e[0] == '0';
   }();
-  return on && !c->batched && rot_dim == hd;
+  return !off && !c->batched && rot_dim == hd;
 }
 
 int qkv_rope(Ctx* c, const void* x, const float* ss, int H, const dfl_layer_weights& w, int M, int Hq, int Hkv, int hd,

@@ -88,9 +88,8 @@ def gemm_chain_enabled() -> bool:
 def qkv_rope_ok(ws, hd: int, rot_dim: int) -> bool:
     """Whether a decoder layer's QKV projection takes the fused q/k norm + RoPE + append
     call (ops.gemm_qkv_rope: the same bits as the separate calls): full rotary, the M <= 16
-    GEMM forms (not a wide workspace), and DFLASH_B200_FUSED_QKV_ROPE=1 (opt-in: measured
-    slower than the separate append kernel in the Qwen3-4B step)."""
-    if os.environ.get("DFLASH_B200_FUSED_QKV_ROPE", "0") != "1":
+    GEMM forms (not a wide workspace), unless DFLASH_B200_FUSED_QKV_ROPE=0."""
+    if os.environ.get("DFLASH_B200_FUSED_QKV_ROPE", "1") == "0":
         return False
     return rot_dim == hd and not (ws is not None and ws.wide)
 

@@ -442,7 +442,9 @@ __global__ void __launch_bounds__(256) attn_chunk_kernel(AttnArgs a) {
 // Merge the chunk partials of one (row, head) in chunk order. One warp per
 // (row, head): lane c holds chunk c's (max, sum) so the global max and the
 // denominator are warp reductions; the output accumulates chunk by chunk in
-// order, eight chunks' loads in flight at a time (four at head_dim 256).
+// order, eight chunks' loads in flight at a time (four at head_dim 256). The first
+// 32 chunks' (max, sum) and the first eight chunks' outputs are loaded together with
+// the row's key range, before it is known which of them the row uses.
 template <int HD>
 __global__ void attn_combine_kernel(AttnArgs a) {
   grid_dependency_launch_dependents();
@@ -451,23 +453,37 @@ __global__ void attn_combine_kernel(AttnArgs a) {
   const long long item = (long long)blockIdx.x * (blockDim.x >> 5) + warp;
   if (item >= (long long)a.M * a.Hq) return;
   const int m = (int)(item / a.Hq), h = (int)(item % a.Hq);
+  constexpr int PER = HD / 32;
+  constexpr int FL = HD <= 128 ? 8 : 4;  // chunks' loads in flight
+  const long long cstride = (long long)a.M * a.Hq;  // between one chunk's partials and the next's
+  const float2* ml_row = a.part_ml + (long long)m * a.Hq + h;
+  const float* po_row = a.part_o + ((long long)m * a.Hq + h) * HD;
+  // Loads that do not depend on the row's key range go out with the range's own loads:
+  // the first 32 chunks' (max, sum) and the first FL chunks' partial outputs (only the
+  // row's own chunks are used below).
+  const int pre_ml = min(32, a.n_chunks), pre_o = min(FL, a.n_chunks);
+  const float2 ml0 = lane < pre_ml ? ml_row[lane * cstride] : make_float2(-INFINITY, 0.f);
+  float v0[FL][PER];
+#pragma unroll
+  for (int u = 0; u < FL; ++u)
+#pragma unroll
+    for (int i = 0; i < PER; ++i) v0[u][i] = u < pre_o ? po_row[u * cstride * HD + lane + 32 * i] : 0.f;
   const int lim = row_limit(a, m);
   if (lim <= 0) return;
   const int nch = min((lim + a.key_chunk - 1) / a.key_chunk, a.n_chunks);
-  constexpr int PER = HD / 32;
   float acc[PER];
 #pragma unroll
   for (int i = 0; i < PER; ++i) acc[i] = 0.f;
   float den = 0.f;
-  // global max over all chunks
-  float mmax = -INFINITY;
-  for (int c = lane; c < nch; c += 32) mmax = fmaxf(mmax, a.part_ml[((long long)c * a.M + m) * a.Hq + h].x);
+  // global max over the row's chunks
+  float mmax = lane < nch ? ml0.x : -INFINITY;
+  for (int c = lane + 32; c < nch; c += 32) mmax = fmaxf(mmax, ml_row[c * cstride].x);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffffu, mmax, o));
   const float mu = mmax == -INFINITY ? 0.f : mmax;
   for (int c0 = 0; c0 < nch; c0 += 32) {
     const int c = c0 + lane;
-    const float2 ml = c < nch ? a.part_ml[((long long)c * a.M + m) * a.Hq + h] : make_float2(-INFINITY, 0.f);
+    const float2 ml = c >= nch ? make_float2(-INFINITY, 0.f) : (c0 == 0 ? ml0 : ml_row[c * cstride]);
     const float w = c < nch ? exp2f(ml.x - mu) : 0.f;
     float dl = w * ml.y;
 #pragma unroll
@@ -475,14 +491,23 @@ __global__ void attn_combine_kernel(AttnArgs a) {
     den += dl;
     const int n = min(32, nch - c0);
     int j = 0;
-    constexpr int FL = HD <= 128 ? 8 : 4;  // chunks' loads in flight
+    if (c0 == 0) {  // the prefetched chunks, in order
+#pragma unroll
+      for (int u = 0; u < FL; ++u)
+        if (u < n) {
+          const float wj = __shfl_sync(0xffffffffu, w, u);
+#pragma unroll
+          for (int i = 0; i < PER; ++i) acc[i] += wj * v0[u][i];
+        }
+      j = min(FL, n);
+    }
     for (; j + FL <= n; j += FL) {
       float v[FL][PER];
       float wj[FL];
 #pragma unroll
       for (int u = 0; u < FL; ++u) {
         wj[u] = __shfl_sync(0xffffffffu, w, j + u);
-        const float* po = a.part_o + (((long long)(c0 + j + u) * a.M + m) * a.Hq + h) * HD;
+        const float* po = po_row + (long long)(c0 + j + u) * cstride * HD;
 #pragma unroll
         for (int i = 0; i < PER; ++i) v[u][i] = po[lane + 32 * i];
       }
@@ -493,7 +518,7 @@ __global__ void attn_combine_kernel(AttnArgs a) {
     }
     for (; j < n; ++j) {
       const float wj = __shfl_sync(0xffffffffu, w, j);
-      const float* po = a.part_o + (((long long)(c0 + j) * a.M + m) * a.Hq + h) * HD;
+      const float* po = po_row + (long long)(c0 + j) * cstride * HD;
 #pragma unroll
       for (int i = 0; i < PER; ++i) acc[i] += wj * po[lane + 32 * i];
     }

@@ -49,6 +49,50 @@ __device__ __forceinline__ int warp_row_argmax(const float2* part, int n_tiles, 
   return best.i;
 }
 
+// Argmax of rows first .. first + n - 1 of the per-tile partials by the whole block: each
+// row gets nw = warps / n warps (at least one), warp `sub` of a row takes every nw-th run
+// of 32 partials with sixteen loads per lane in flight, and the warps' pairs meet in shared
+// memory. The (value desc, index asc) order is total, so the split does not change the
+// result. Every thread of the block must call it; out[k] gets row first + k's index.
+__device__ __forceinline__ void block_rows_argmax(const float2* part, int n_tiles, int first, int n, int* out) {
+  __shared__ ArgmaxPair pairs[32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, warps = blockDim.x >> 5;
+  const int nw = max(1, warps / n);
+  for (int k0 = 0; k0 < n; k0 += warps / nw) {
+    const int k = k0 + warp / nw, sub = warp % nw;
+    ArgmaxPair best{-INFINITY, 0x7fffffff};
+    if (k < n && warp / nw < warps / nw) {
+      const float2* row = part + (long long)(first + k) * n_tiles;
+      const int step = 32 * nw;
+      int j = sub * 32 + lane;
+      for (; j + 15 * step < n_tiles; j += 16 * step) {
+        float2 p[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) p[u] = row[j + u * step];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) best = better(best, ArgmaxPair{p[u].x, __float_as_int(p[u].y)});
+      }
+      for (; j < n_tiles; j += step) {
+        const float2 p = row[j];
+        best = better(best, ArgmaxPair{p.x, __float_as_int(p.y)});
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        ArgmaxPair other{__shfl_xor_sync(0xffffffffu, best.v, o), __shfl_xor_sync(0xffffffffu, best.i, o)};
+        best = better(best, other);
+      }
+    }
+    if (lane == 0) pairs[warp] = best;
+    __syncthreads();
+    if (threadIdx.x < warps / nw && k0 + (int)threadIdx.x < n) {
+      ArgmaxPair b = pairs[threadIdx.x * nw];
+      for (int u = 1; u < nw; ++u) b = better(b, pairs[threadIdx.x * nw + u]);
+      out[k0 + threadIdx.x] = b.i;
+    }
+    __syncthreads();
+  }
+}
+
 __global__ void argmax_reduce_kernel(const float2* __restrict__ part, int M, int n_tiles, int* __restrict__ out) {
   grid_dependency_launch_dependents();
   grid_dependency_wait();
@@ -93,17 +137,20 @@ __global__ void draft_commit_kernel(dfl_seq_state* st, const float2* __restrict_
   grid_dependency_wait();
   const int b = blockIdx.x;
   if (b >= B) return;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __shared__ int post[64];
   const dfl_seq_state s = st[b];
-  for (int i = 1 + warp; i < bs; i += blockDim.x >> 5) {
-    const int r = b * bs + i;
-    int tok = warp_row_argmax(part + (long long)r * n_tiles, n_tiles, lane);
+  block_rows_argmax(part, n_tiles, b * bs + 1, bs - 1, post);  // also under injection: the same work as a real step
+  __syncthreads();
+  for (int i = 1 + (int)threadIdx.x; i < bs; i += blockDim.x) {
+    int tok;
     if (inject_tokens) {
       const int L = inject_len[(long long)b * inject_len_stride + s.steps];
       tok = (i - 1 < L) ? inject_tokens[(long long)b * inject_stride + s.start + i]
                         : inject_noise[(long long)b * noise_stride + (long long)s.steps * bs + i];
+    } else {
+      tok = post[i - 1];
     }
-    if (lane == 0) block[r] = tok;
+    block[b * bs + i] = tok;
   }
   __syncthreads();
   if (threadIdx.x == 0 && !s.finished) {
@@ -123,15 +170,9 @@ __global__ void verify_accept_kernel(dfl_seq_state* st, const float2* __restrict
   __shared__ int post[64];
   const int b = blockIdx.x;
   if (b >= B) return;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int i = warp; i < bs; i += blockDim.x >> 5) {
-    const int r = b * bs + i;
-    const int tok = warp_row_argmax(part + (long long)r * n_tiles, n_tiles, lane);
-    if (lane == 0) {
-      post[i] = tok;
-      if (posterior) posterior[r] = tok;
-    }
-  }
+  block_rows_argmax(part, n_tiles, b * bs, bs, post);
+  if (posterior)
+    for (int i = threadIdx.x; i < bs; i += blockDim.x) posterior[b * bs + i] = post[i];
   __syncthreads();
   if (threadIdx.x != 0) return;
   dfl_seq_state s = st[b];
@@ -303,7 +344,7 @@ extern "C" int dfl_draft_commit(dfl_seq_state* state, const void* partials, int 
   const float2* p = static_cast<const float2*>(partials);
   long long is = inject_stride, ils = inject_len_stride, ns = noise_stride;
   void* args[] = {&state, &p, &n_tiles, &block, &bs, &inject_tokens, &is, &inject_len, &ils, &inject_noise, &ns, &B};
-  return launch_simple((const void*)draft_commit_kernel, dim3(B), dim3(512), args, as_stream(stream),
+  return launch_simple((const void*)draft_commit_kernel, dim3(B), dim3(1024), args, as_stream(stream),
                        "dfl_draft_commit");
 }
 
@@ -320,6 +361,6 @@ extern "C" int dfl_verify_accept(dfl_seq_state* state, const void* partials, int
   long long os = out_stride, ls = log_stride;
   void* args[] = {&state, &p, &n_tiles, &block, &bs, &out_tokens, &os, &posterior, &stop_ids, &n_stop, &accept_log,
                   &ls, &B};
-  return launch_simple((const void*)verify_accept_kernel, dim3(B), dim3(512), args, as_stream(stream),
+  return launch_simple((const void*)verify_accept_kernel, dim3(B), dim3(1024), args, as_stream(stream),
                        "dfl_verify_accept");
 }

@@ -545,7 +545,13 @@ def main():
         return int(q("dfl_gemm_qkv_rope_launches", rows, c.hidden_size, c.num_attention_heads,
                      c.num_key_value_heads, c.head_dim))
     qkv_t, qkv_d = qkv_launches(tcfg), qkv_launches(dcfg)
-    draft_launches = 1 + (2 + n_layers_d) + 1 + (3 + qkv_d + att_d) * n_layers_d + 1 + 1
+    # draft context rows: fc, then the stacked K/V projection with every layer's append fused
+    # (one launch) or followed by one append launch per layer
+    ingest_fused = qkv_rope_ok(sess.ws, dcfg.head_dim, dcfg.head_dim) and int(q(
+        "dfl_gemm_qkv_rope_launches", rows, dcfg.hidden_size, 0, n_layers_d * dcfg.num_key_value_heads,
+        dcfg.head_dim)) == 1
+    ingest = 2 + (0 if ingest_fused else n_layers_d)
+    draft_launches = 1 + ingest + 1 + (3 + qkv_d + att_d) * n_layers_d + 1 + 1
     verify_launches = 1 + (3 + qkv_t + att_t) * n_layers_t + 1 + 1
     launches_step = draft_launches + verify_launches
     if rank == 0:

@@ -287,6 +287,16 @@ int draft_ingest(Ctx* c, const __nv_bfloat16* taps, const int* pos, int M, const
   } else {
     TRY(gemm(c, taps, (int64_t)ntaps * H, d.fc, M, H, ntaps * H, DFL_EPI_STORE, nullptr, 0, c->dfc, H, nullptr, 0,
              nullptr, nullptr, nullptr, c->dss_ctx, d.eps, s));
+    if (fused_qkv_rope(c, hd, hd) && d.n_layers <= 16) {
+      // hidden_norm, every layer's k/v projection and k_norm + RoPE + append: one call
+      std::vector<const void*> kn(d.n_layers);
+      for (int l = 0; l < d.n_layers; ++l) kn[l] = c->dl[l].k_norm;
+      return dfl_gemm_kv_append_layers(c->dfc, H, d.w_ctx_kv, M, H, d.hidden_norm, c->dss_ctx, H / 32, d.eps, c->dkvp,
+                                       nkv, pos, row_seq, kn.data(), c->d_inv_freq, c->dk, c->dv,
+                                       (int64_t)kv_layer_elems(c, Hkv, hd), (int64_t)Hkv * c->cap * hd,
+                                       (int64_t)c->cap * hd, nullptr, 0, 0, d.n_layers, Hkv, hd, c->gemm_ws,
+                                       c->gemm_ws_bytes, s);
+    }
     TRY(gemm(c, c->dfc, H, d.w_ctx_kv, M, nkv, H, DFL_EPI_STORE, nullptr, 0, c->dkvp, nkv, nullptr, 0, nullptr,
              d.hidden_norm, c->dss_ctx, nullptr, d.eps, s));
   }

@@ -112,6 +112,8 @@ constexpr int TC_PART_FLOATS = TC_BM * TC_NT;  // one partial tile
 constexpr uint32_t TC_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TC_BM >> 3) << 17) |
                               ((uint32_t)(TC_NT >> 4) << 24);
 
+constexpr int TC_KV_LAYERS_MAX = 16;  // layers one fused context K/V projection may append
+
 struct TcArgs {
   const unsigned char* wt;  // pre-tiled weights: unit u at wt + u * TC_W_BYTES
   const __nv_bfloat16* res;
@@ -137,6 +139,10 @@ struct TcArgs {
   // head_dim 128 = one column tile per head, M <= 16): rope_on selects it
   int rope_on;
   QkvArgs rope;
+  // several layers' context-row K/V in one projection (rope.Hq = 0): 2 Hkv column tiles per
+  // layer, layer l's k_norm weight at rope_k_norm[l]; 0 = one layer
+  int rope_layer_heads;
+  const __nv_bfloat16* rope_k_norm[TC_KV_LAYERS_MAX];
 };
 
 // tcgen05 helpers (descriptors, MMA issue, commit, fences, TMEM loads): tcgen05.cuh
@@ -776,7 +782,10 @@ __global__ void __launch_bounds__(TC_THREADS, DFL_TC_MINB)
     cluster_arrive();
     cluster_wait();
     float* buf = reinterpret_cast<float*>(smem) + warp * 128;
-    for (int m = r + S * warp; m < a.M; m += S * (TC_THREADS / 32)) qkv_rope_row(a.rope, m, nt, lane, buf);
+    const int lh = a.rope_layer_heads;
+    const int layer = lh ? nt / lh : 0, head = lh ? nt % lh : nt;
+    const __nv_bfloat16* knl = lh ? a.rope_k_norm[layer] : nullptr;
+    for (int m = r + S * warp; m < a.M; m += S * (TC_THREADS / 32)) qkv_rope_row(a.rope, m, head, lane, buf, layer, knl);
   }
   tc_fence_before();
   __syncthreads();
@@ -1645,7 +1654,8 @@ static int gemm_bf16_impl(const void* x, int64_t ldx, const void* w_packed, int 
                           const void* residual, int64_t ldr, void* y, int64_t ldy, void* y2, int64_t ldy2,
                           void* argmax_partials, const void* norm_w, const float* sumsq_in, int n_parts, float eps,
                           float* sumsq_out, void* workspace, size_t workspace_bytes, void* stream,
-                          const QkvArgs* rope = nullptr, bool* fused = nullptr) {
+                          const QkvArgs* rope = nullptr, bool* fused = nullptr, int rope_layers = 0,
+                          const void* const* rope_k_norms = nullptr) {
   if (fused) *fused = false;
   if (M == 0) return DFL_OK;
   const void* w = w_packed;
@@ -1721,6 +1731,12 @@ static int gemm_bf16_impl(const void* x, int64_t ldx, const void* w_packed, int 
   a.rope_on = rope && p.S && p.m_tiles == 1 && epilogue == DFL_EPI_STORE;
   if (a.rope_on) a.rope = *rope;
   else memset(&a.rope, 0, sizeof(a.rope));
+  a.rope_layer_heads = 0;
+  memset(a.rope_k_norm, 0, sizeof(a.rope_k_norm));
+  if (a.rope_on && rope_layers > 0) {
+    a.rope_layer_heads = 2 * rope->Hkv;
+    for (int l = 0; l < rope_layers; ++l) a.rope_k_norm[l] = static_cast<const __nv_bfloat16*>(rope_k_norms[l]);
+  }
   if (fused) *fused = a.rope_on;
 
   cudaLaunchConfig_t cfg = {};
@@ -1857,8 +1873,83 @@ extern "C" int dfl_gemm_qkv_rope(const void* x, int64_t ldx, const void* w_packe
                              seq_stride, head_stride, M, Hq, Hkv, hd, hd, eps, 1, stream);
 }
 
+extern "C" int dfl_gemm_kv_append_layers(const void* x, int64_t ldx, const void* w_packed, int M, int K,
+                                         const void* norm_w, const float* sumsq_in, int n_parts, float eps, void* kv,
+                                         int64_t ldkv, const int32_t* pos, const int32_t* row_seq,
+                                         const void* const* k_norms, const float* inv_freq, void* k_cache,
+                                         void* v_cache, int64_t layer_stride, int64_t seq_stride,
+                                         int64_t head_stride, const int32_t* page_table, int64_t pt_stride,
+                                         int page_size, int n_layers, int Hkv, int hd, void* workspace,
+                                         size_t workspace_bytes, void* stream) {
+  if (M == 0) return DFL_OK;
+  if (!pos || !k_norms || !inv_freq || !k_cache || !v_cache || n_layers <= 0 || n_layers > TC_KV_LAYERS_MAX ||
+      Hkv <= 0 || hd <= 0) {
+    set_error("dfl_gemm_kv_append_layers: null pointer, bad head geometry or more than %d layers", TC_KV_LAYERS_MAX);
+    return DFL_ERR_INVALID;
+  }
+  for (int l = 0; l < n_layers; ++l)
+    if (!k_norms[l]) {
+      set_error("dfl_gemm_kv_append_layers: null k_norm of layer %d", l);
+      return DFL_ERR_INVALID;
+    }
+  QkvArgs r;
+  memset(&r, 0, sizeof(r));
+  r.qkv = static_cast<const __nv_bfloat16*>(kv);
+  r.ldqkv = ldkv;
+  r.q_stride = hd;
+  r.pos = pos;
+  r.row_seq = row_seq;
+  r.k_norm = static_cast<const __nv_bfloat16*>(k_norms[0]);
+  r.q_norm = r.k_norm;
+  r.inv_freq = inv_freq;
+  r.k_cache = static_cast<__nv_bfloat16*>(k_cache);
+  r.v_cache = static_cast<__nv_bfloat16*>(v_cache);
+  r.seq_stride = seq_stride;
+  r.head_stride = head_stride;
+  r.M = M;
+  r.Hq = 0;
+  r.Hkv = Hkv;
+  r.hd = hd;
+  r.rot_dim = hd;
+  r.eps = eps;
+  r.do_q = 0;
+  r.page_table = page_table;
+  r.pt_stride = pt_stride;
+  r.page_shift = 0;
+  r.layer_stride = layer_stride;
+  if (page_table) {
+    if (page_size < 64 || (page_size & (page_size - 1)) || pt_stride <= 0) {
+      set_error("dfl_gemm_kv_append_layers: page_size must be a power of two >= 64 (got %d)", page_size);
+      return DFL_ERR_INVALID;
+    }
+    while ((1 << r.page_shift) < page_size) ++r.page_shift;
+  }
+  const int per = 2 * Hkv * hd;
+  bool fused = false;
+  const int st = gemm_bf16_impl(x, ldx, w_packed, M, n_layers * per, K, DFL_EPI_STORE, nullptr, 0, kv, ldkv, nullptr, 0,
+                                nullptr, norm_w, sumsq_in, n_parts, eps, nullptr, workspace, workspace_bytes, stream,
+                                hd == TC_NT ? &r : nullptr, &fused, n_layers, k_norms);
+  if (st != DFL_OK || fused) return st;
+  // another GEMM form: one append launch per layer (the same arithmetic)
+  char* kb = static_cast<char*>(k_cache);
+  char* vb = static_cast<char*>(v_cache);
+  for (int l = 0; l < n_layers; ++l) {
+    const void* kvl = static_cast<const char*>(kv) + (size_t)l * per * 2;
+    void* kl = kb + (size_t)l * layer_stride * 2;
+    void* vl = vb + (size_t)l * layer_stride * 2;
+    const int s = page_table
+                      ? dfl_qkv_rope_append_paged(kvl, ldkv, hd, pos, row_seq, k_norms[l], k_norms[l], inv_freq,
+                                                  nullptr, kl, vl, seq_stride, head_stride, page_table, pt_stride,
+                                                  page_size, M, 0, Hkv, hd, hd, eps, 0, stream)
+                      : dfl_qkv_rope_append(kvl, ldkv, hd, pos, row_seq, k_norms[l], k_norms[l], inv_freq, nullptr,
+                                            kl, vl, seq_stride, head_stride, M, 0, Hkv, hd, hd, eps, 0, stream);
+    if (s != DFL_OK) return s;
+  }
+  return DFL_OK;
+}
+
 extern "C" int dfl_gemm_qkv_rope_launches(int M, int K, int Hq, int Hkv, int hd) {
-  if (M <= 0 || K <= 0 || K % TC_BK || Hq <= 0 || Hkv <= 0 || hd <= 0) return -1;
+  if (M <= 0 || K <= 0 || K % TC_BK || Hq < 0 || Hkv <= 0 || hd <= 0) return -1;
   const TcPlan p = tc_plan(M, (Hq + 2 * Hkv) * hd, K);
   return (hd == TC_NT && p.S && p.m_tiles == 1) ? 1 : 2;
 }

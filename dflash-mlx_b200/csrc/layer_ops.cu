@@ -193,6 +193,7 @@ static int qkv_rope_append_impl(const void* qkv, int64_t ldqkv, int q_stride, co
   a.page_table = page_table;
   a.pt_stride = pt_stride;
   a.page_shift = 0;
+  a.layer_stride = 0;
   if (page_table) {
     if (page_size < 64 || (page_size & (page_size - 1)) || pt_stride <= 0) {
       set_error("dfl_qkv_rope_append_paged: page_size must be a power of two >= 64 (got %d)", page_size);

@@ -36,6 +36,7 @@ struct QkvArgs {
   const int* page_table;  // nullable: contiguous [seq][Hkv][cap][hd] caches
   long long pt_stride;
   int page_shift;         // log2(page_size)
+  long long layer_stride; // multi-layer append: elements between consecutive layers' caches
 };
 
 // element offset of (sequence, kv head, position) in a contiguous or paged cache
@@ -48,15 +49,20 @@ __device__ __forceinline__ long long kv_offset(const int* pt, long long pt_strid
 
 // One (row, head) of the q/k head norm + RoPE + append, by one warp; buf: hd floats of
 // this warp's shared memory. Shared by qkv_rope_append_kernel and the fused epilogue of
-// the QKV projection (gemm_tc.cu), so both give the same bits.
-__device__ __forceinline__ void qkv_rope_row(const QkvArgs& a, int row, int head, int lane, float* buf) {
+// the QKV projection (gemm_tc.cu), so both give the same bits. layer > 0 (the stacked K/V
+// projection of several layers' context rows): the row's columns of that layer, its
+// k_norm weight k_norm_l and its caches (layer * layer_stride further on).
+__device__ __forceinline__ void qkv_rope_row(const QkvArgs& a, int row, int head, int lane, float* buf, int layer = 0,
+                                             const __nv_bfloat16* k_norm_l = nullptr) {
   const int p = a.pos[row];
   if (p < 0) return;
   const int seq = a.row_seq ? a.row_seq[row] : 0;
   const __nv_bfloat16* src;
   const __nv_bfloat16* nw = nullptr;
   __nv_bfloat16* dst;
-  const __nv_bfloat16* qkv_row = a.qkv + (long long)row * a.ldqkv;
+  const long long lcache = (long long)layer * a.layer_stride;
+  const __nv_bfloat16* qkv_row =
+      a.qkv + (long long)row * a.ldqkv + (long long)layer * (a.Hq * a.q_stride + 2 * a.Hkv * a.hd);
   if (head < a.Hq) {
     if (!a.do_q) return;
     src = qkv_row + (long long)head * a.q_stride;
@@ -65,12 +71,14 @@ __device__ __forceinline__ void qkv_rope_row(const QkvArgs& a, int row, int head
   } else if (head < a.Hq + a.Hkv) {
     const int kh = head - a.Hq;
     src = qkv_row + (long long)a.Hq * a.q_stride + (long long)kh * a.hd;
-    nw = a.k_norm;
-    dst = a.k_cache + kv_offset(a.page_table, a.pt_stride, a.page_shift, a.seq_stride, a.head_stride, seq, kh, p, a.hd);
+    nw = k_norm_l ? k_norm_l : a.k_norm;
+    dst = a.k_cache + lcache +
+          kv_offset(a.page_table, a.pt_stride, a.page_shift, a.seq_stride, a.head_stride, seq, kh, p, a.hd);
   } else {
     const int vh = head - a.Hq - a.Hkv;
     src = qkv_row + (long long)a.Hq * a.q_stride + (long long)(a.Hkv + vh) * a.hd;
-    dst = a.v_cache + kv_offset(a.page_table, a.pt_stride, a.page_shift, a.seq_stride, a.head_stride, seq, vh, p, a.hd);
+    dst = a.v_cache + lcache +
+          kv_offset(a.page_table, a.pt_stride, a.page_shift, a.seq_stride, a.head_stride, seq, vh, p, a.hd);
     for (int i = lane; i < a.hd; i += 32) dst[i] = src[i];
     return;
   }

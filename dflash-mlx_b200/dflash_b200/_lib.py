@@ -59,6 +59,10 @@ SIGNATURES: dict[str, tuple] = {
                                   c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                   c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_int64, c_int, c_int, c_int, c_int,
                                   c_void_p, c_size_t, c_void_p]),
+    "dfl_gemm_kv_append_layers": (c_int, [c_void_p, c_int64, c_void_p, c_int, c_int, c_void_p, c_void_p, c_int,
+                                          c_float, c_void_p, c_int64, c_void_p, c_void_p, POINTER(c_void_p),
+                                          c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p,
+                                          c_int64, c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "dfl_gemm_qkv_rope_launches": (c_int, [c_int, c_int, c_int, c_int, c_int]),
     "dfl_qkv_rope_append": (c_int, [c_void_p, c_int64, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                     c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int, c_int, c_int, c_int, c_int,

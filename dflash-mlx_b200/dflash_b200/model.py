@@ -484,6 +484,14 @@ class DraftModel:
                                          sumsq_in=b["ss"], eps=c.rms_norm_eps)], ws)
         else:
             ops.gemm(taps, self.fc, out=b["fc"], ws=ws, sumsq_out=b["ss"])
+            if qkv_rope_ok(ws, hd, hd) and len(self.layers) <= ops.KV_LAYERS_MAX:
+                # hidden_norm, the stacked k/v projection of every layer and each layer's
+                # k_norm + RoPE + append: one call (the same bits as the calls below)
+                ops.gemm_kv_append_layers(b["fc"], self.w_ctx_kv, b["kv"], pos, [lw["k_norm"] for lw in self.layers],
+                                          self.inv_freq, cache.k, cache.v, Hkv, hd, c.rms_norm_eps,
+                                          norm_w=self.hidden_norm, sumsq_in=b["ss"], row_seq=row_seq, ws=ws,
+                                          **cache.paging)
+                return
             # hidden_norm fused into the stacked k/v projection of every layer
             ops.gemm(b["fc"], self.w_ctx_kv, out=b["kv"], ws=ws, norm_w=self.hidden_norm, sumsq_in=b["ss"],
                      eps=c.rms_norm_eps)

@@ -15,6 +15,7 @@ from . import _lib
 
 EPI_STORE, EPI_RESIDUAL, EPI_SILU_MUL, EPI_ARGMAX, EPI_STORE_F32, EPI_PARTIALS = 0, 1, 2, 3, 4, 5
 ATTN_CHUNK = 128
+KV_LAYERS_MAX = 16  # layers one dfl_gemm_kv_append_layers call appends
 
 
 def _stream() -> int:
@@ -339,6 +340,43 @@ def gemm_qkv_rope(x: torch.Tensor, w: PackedWeight | torch.Tensor, qkv: torch.Te
               float(eps), _ptr(qkv), _row_stride(qkv), _ptr(pos), _ptr(row_seq), _ptr(q_norm), _ptr(k_norm),
               _ptr(inv_freq), _ptr(q_out), _ptr(k_cache), _ptr(v_cache), k_cache.stride(0), k_cache.stride(1),
               _ptr(page_table), page_table.stride(0) if page_table is not None else 0, int(page_size), Hq, Hkv, hd,
+              _ptr(ws.gemm), ws.gemm.numel(), _stream())
+
+
+def gemm_kv_append_layers(x: torch.Tensor, w: PackedWeight | torch.Tensor, kv: torch.Tensor, pos: torch.Tensor,
+                          k_norms: list[torch.Tensor], inv_freq: torch.Tensor, k_cache: torch.Tensor,
+                          v_cache: torch.Tensor, Hkv: int, hd: int, eps: float, norm_w: torch.Tensor | None = None,
+                          sumsq_in: torch.Tensor | None = None, row_seq: torch.Tensor | None = None,
+                          ws: Workspace | None = None, page_table: torch.Tensor | None = None,
+                          page_size: int = 0) -> None:
+    """The stacked K/V projection of every layer's context rows (input RMSNorm fused when
+    norm_w is given) into ``kv``, then each layer's k_norm + RoPE + append into
+    k_cache[l] / v_cache[l] (caches [L, ...], one layer per leading index), as one call
+    (dfl_gemm_kv_append_layers): the same bits as gemm() and a qkv_rope_append() per layer."""
+    if isinstance(w, torch.Tensor):  # convenience for tests: pack on the fly
+        w = PackedWeight(w)
+    _need_cuda(x, kv, pos, inv_freq, k_cache, v_cache, norm_w, sumsq_in, row_seq, page_table, *k_norms)
+    M, K = x.shape
+    L = len(k_norms)
+    N = L * 2 * Hkv * hd
+    if tuple(w.shape) != (N, K) or kv.shape[0] < M or kv.shape[1] < N or k_cache.shape[0] < L:
+        raise ValueError(f"gemm_kv_append_layers shape mismatch x{tuple(x.shape)} w{tuple(w.shape)} kv{tuple(kv.shape)}")
+    if k_cache.dim() != 5 or k_cache.stride(4) != 1 or k_cache.stride(3) != hd or k_cache.stride() != v_cache.stride():
+        raise ValueError("k_cache / v_cache must be [L, seq, Hkv, cap, hd] (or [L, pages, Hkv, page_size, hd]) alike")
+    ws = ws or workspace(x.device)
+    if ws.wide:
+        raise ValueError("gemm_kv_append_layers runs the M <= 16 weight-streaming forms only")
+    ws.ensure_gemm(int(_lib.query("dfl_gemm_workspace_bytes", M, N, K, EPI_STORE)))
+    n_parts = 0
+    if norm_w is not None:
+        if sumsq_in is None or sumsq_in.dtype != torch.float32 or not sumsq_in.is_contiguous():
+            raise ValueError("the fused RMSNorm needs contiguous fp32 sumsq_in partials [M, K/32]")
+        n_parts = sumsq_in.shape[1]
+    norms = (ctypes.c_void_p * L)(*[t.data_ptr() for t in k_norms])
+    _lib.call("dfl_gemm_kv_append_layers", _ptr(x), _row_stride(x), _ptr(w), M, K, _ptr(norm_w), _ptr(sumsq_in),
+              n_parts, float(eps), _ptr(kv), _row_stride(kv), _ptr(pos), _ptr(row_seq), norms, _ptr(inv_freq),
+              _ptr(k_cache), _ptr(v_cache), k_cache.stride(0), k_cache.stride(1), k_cache.stride(2),
+              _ptr(page_table), page_table.stride(0) if page_table is not None else 0, int(page_size), L, Hkv, hd,
               _ptr(ws.gemm), ws.gemm.numel(), _stream())
 
 

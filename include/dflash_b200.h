@@ -263,8 +263,27 @@ int dfl_gemm_qkv_rope(const void* x, int64_t ldx, const void* w_packed, int M, i
                       void* q_out, void* k_cache, void* v_cache, int64_t seq_stride, int64_t head_stride,
                       const int32_t* page_table, int64_t pt_stride, int page_size, int Hq, int Hkv, int hd,
                       void* workspace, size_t workspace_bytes, void* stream);
+/* The draft's context rows (draft.py:118-147 for every DFlashDecoderLayer: k_proj / v_proj
+ * of the context, k_norm, RoPE at the rows' positions, append to each layer's cache) for
+ * n_layers layers at once: one GEMM over the stacked per-layer K/V weights
+ * [n_layers * 2 * Hkv * hd, K] writing kv (layer l's columns at l * 2 * Hkv * hd), then layer
+ * l's k_norm (k_norms[l], a host array of device pointers) + RoPE + append into
+ * k_cache / v_cache + l * layer_stride elements. At M <= 16 rows and head_dim 128 the
+ * appends run inside the GEMM launch; otherwise one append launch per layer follows. The
+ * same bits as dfl_gemm_bf16 + dfl_qkv_rope_append(_paged) per layer (Hq = 0, do_q = 0).
+ * n_layers <= 16. */
+int dfl_gemm_kv_append_layers(const void* x, int64_t ldx, const void* w_packed, int M, int K, const void* norm_w,
+                              const float* sumsq_in, int n_parts, float eps, void* kv, int64_t ldkv,
+                              const int32_t* pos, const int32_t* row_seq, const void* const* k_norms,
+                              const float* inv_freq, void* k_cache, void* v_cache, int64_t layer_stride,
+                              int64_t seq_stride, int64_t head_stride, const int32_t* page_table, int64_t pt_stride,
+                              int page_size, int n_layers, int Hkv, int hd, void* workspace, size_t workspace_bytes,
+                              void* stream);
+
 /* Kernel launches one dfl_gemm_qkv_rope call of this shape makes (1: the append inside the
- * GEMM launch; 2: GEMM + append kernel), -1 for a bad shape. */
+ * GEMM launch; 2: GEMM + append kernel), -1 for a bad shape. With Hq = 0 and Hkv = n_layers x
+ * the layer's kv heads it answers for dfl_gemm_kv_append_layers (1: fused; 2: GEMM + one
+ * append launch per layer). */
 int dfl_gemm_qkv_rope_launches(int M, int K, int Hq, int Hkv, int hd);
 int dfl_attention_paged(const void* q, const void* k_pages, const void* v_pages, int64_t page_stride,
                         int64_t head_stride, const int32_t* page_table, int64_t pt_stride, int page_size,

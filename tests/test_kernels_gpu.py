@@ -725,3 +725,53 @@ def test_gemm_qkv_rope_matches_separate_calls(case):
     print(case, "kernels:", sorted(set(n[:40] for n in names)))
     if names:
         assert appended == (case in ("rows_20", "hd64")), names
+
+
+@pytest.mark.parametrize("case", ["draft_4b", "draft_4b_paged", "rows_20"])
+def test_gemm_kv_append_layers_matches_separate_calls(case):
+    """dfl_gemm_kv_append_layers (the draft's stacked context K/V projection with every
+    layer's k_norm + RoPE + append after the split-K reduction, in the GEMM launch) against
+    dfl_gemm_bf16 followed by one dfl_qkv_rope_append per layer: projection rows and every
+    layer's caches bit for bit. 20 rows take the per-layer append launches inside the call."""
+    from dflash_b200.weights import rope_inv_freq
+    ops = _ops()
+    L, H, Hkv, hd = 5, 2560, 8, 128
+    M = 20 if case == "rows_20" else 16
+    per = 2 * Hkv * hd
+    N = L * per
+    x = _rand((M, H), 1.0, 70).to(DEV)
+    w = ops.PackedWeight(_rand((N, H), 0.02, 71).to(DEV))
+    hn = (1.0 + 0.1 * _rand((H,), 1.0, 72).float()).bfloat16().to(DEV)
+    kns = [_rand((hd,), 1.0, 73 + l).to(DEV) for l in range(L)]
+    ss = (x.float() ** 2).reshape(M, H // 32, 32).sum(-1).contiguous()
+    inv = rope_inv_freq(hd, 1e6).to(DEV)
+    pos = torch.arange(700, 700 + M, dtype=torch.int32, device=DEV)
+    pos[5] = -1
+    cap = 1024
+    paged = case == "draft_4b_paged"
+    pg = {}
+    if paged:
+        perm = torch.randperm(cap // 64, generator=torch.Generator().manual_seed(79)).to(torch.int32).to(DEV)
+        pg = {"page_table": perm.view(1, -1), "page_size": 64}
+    shape = (L, cap // 64, Hkv, 64, hd) if paged else (L, 1, Hkv, cap, hd)
+    kc0, vc0 = torch.zeros(shape, dtype=torch.bfloat16, device=DEV), torch.zeros(shape, dtype=torch.bfloat16, device=DEV)
+    kv0 = torch.zeros((M, N), dtype=torch.bfloat16, device=DEV)
+    ops.gemm(x, w, out=kv0, norm_w=hn, sumsq_in=ss)
+    for l in range(L):
+        ops.qkv_rope_append(kv0[:, l * per:(l + 1) * per], pos, kns[l], kns[l], inv, kc0[l], vc0[l], 0, Hkv, hd, hd,
+                            1e-6, do_q=False, **pg)
+    kc1, vc1 = torch.zeros_like(kc0), torch.zeros_like(vc0)
+    kv1 = torch.zeros((M, N), dtype=torch.bfloat16, device=DEV)
+    from torch.profiler import ProfilerActivity, profile
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        ops.gemm_kv_append_layers(x, w, kv1, pos, kns, inv, kc1, vc1, Hkv, hd, 1e-6, norm_w=hn, sumsq_in=ss, **pg)
+        torch.cuda.synchronize()
+    names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+    assert ops.device_error() == 0
+    assert torch.equal(kv1, kv0)
+    assert torch.equal(kc1, kc0) and torch.equal(vc1, vc0)
+    assert kc1.abs().sum().item() > 0
+    n_append = sum("qkv_rope_append" in n for n in names)
+    print(case, "append launches:", n_append)
+    if names:
+        assert n_append == (L if case == "rows_20" else 0), names

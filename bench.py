@@ -69,6 +69,13 @@ def parse_args():
 
 
 # ---------------------------------------------------------------------------
+def draft_taps(layers: int) -> list[int]:
+    """The draft's tap layers: five evenly spaced ones at full depth, else the first and the
+    last (distinct) for the shallow profiling targets."""
+    from dflash_b200.config import evenly_spaced_layers
+    return evenly_spaced_layers(layers, 5) if layers >= 8 else sorted({0, layers - 1} if layers < 3 else {1, layers - 1})
+
+
 def geometric_p(tau: float, cap: int) -> float:
     """p with E[min(G, cap)] = tau for G ~ Geometric(p) on {1, 2, ...}."""
     lo, hi = 1e-6, 1.0
@@ -156,12 +163,11 @@ def measured_peaks() -> tuple[float, float, str]:
 
 # ---------------------------------------------------------------------------
 def build_models(args, device):
-    from dflash_b200.config import DraftConfig, TargetConfig, evenly_spaced_layers
+    from dflash_b200.config import DraftConfig, TargetConfig
     from dflash_b200.model import DraftModel, TargetModel
     from dflash_b200.weights import random_draft_weights, random_target_weights
     tcfg = TargetConfig(num_hidden_layers=args.layers)
-    dcfg = DraftConfig(target_layer_ids=evenly_spaced_layers(args.layers, 5) if args.layers >= 8
-                       else [1, args.layers - 1])
+    dcfg = DraftConfig(target_layer_ids=draft_taps(args.layers))
     tw = random_target_weights(tcfg, args.seed, device=device)
     dw = random_draft_weights(dcfg, args.seed, device=device)
     target = TargetModel(tcfg, tw, device)
@@ -292,30 +298,31 @@ def run_reference(args, world: int, rank: int) -> None:
     if rank != 0:
         return
     from oracle import dflash_oracle as O
-    from dflash_b200.config import DraftConfig, TargetConfig, evenly_spaced_layers
+    from dflash_b200.config import DraftConfig, TargetConfig
     from dflash_b200.weights import random_draft_weights, random_target_weights
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     t_setup = time.perf_counter()
     tcfg = TargetConfig(num_hidden_layers=args.layers)
-    dcfg = DraftConfig(target_layer_ids=evenly_spaced_layers(args.layers, 5) if args.layers >= 8
-                       else [1, args.layers - 1])
+    dcfg = DraftConfig(target_layer_ids=draft_taps(args.layers))
     tw = _fp32_weights(random_target_weights(tcfg, args.seed))
     dw = _fp32_weights(random_draft_weights(dcfg, args.seed))
     ot = O.OracleTarget(tcfg, tw)
     od = O.OracleDraft(dcfg, dw, ot)
     bs = dcfg.block_size
     n_steps = max(1, min(args.steps, args.cpu_steps))
-    lengths, noise = injection_plan(n_steps + 4, bs, args.tau, tcfg.vocab_size, args.seed)
+    n_warm = max(0, min(args.warmup, args.cpu_steps))  # untimed steps first, as the GPU arm
+    total = n_warm + n_steps
+    lengths, noise = injection_plan(total + 4, bs, args.tau, tcfg.vocab_size, args.seed)
     g = torch.Generator().manual_seed(args.seed)
     prompt = torch.randint(0, tcfg.vocab_size, (args.prompt_len,), generator=g).tolist()
     P = len(prompt)
-    cap = P + bs * (n_steps + 4)
+    cap = P + bs * (total + 4)
     tcache, dcache = ot.make_cache(cap), od.make_cache(cap)
     logits, hidden = ot.forward_with_hidden_states(prompt, tcache, dcfg.target_layer_ids)
     out = prompt + [int(O.argmax_first(logits[-1]))]
     # the target's greedy continuation, far enough for every injected prefix (untimed)
-    need = P + 1 + sum(int(x) + 1 for x in lengths[:n_steps]) + bs
+    need = P + 1 + sum(int(x) + 1 for x in lengths[:total]) + bs
     gcache = ot.make_cache(need + 1)
     for c, src in zip(gcache, tcache):
         c.k[:, :P] = src.k[:, :P]
@@ -329,7 +336,9 @@ def run_reference(args, world: int, rank: int) -> None:
     setup_s = time.perf_counter() - t_setup
     start, accepted = P, 0
     t0 = time.perf_counter()
-    for s in range(n_steps):
+    for s in range(total):
+        if s == n_warm:  # the timed steps start here
+            t0, accepted = time.perf_counter(), 0
         block = [out[start]] + [dcfg.mask_token_id] * (bs - 1)
         dh = od(ot.embed_tokens(block), hidden, dcache)
         O.argmax_first(ot.lm_head_logits(dh[1:]))
@@ -350,11 +359,11 @@ def run_reference(args, world: int, rank: int) -> None:
         accepted += acc
     dt = time.perf_counter() - t0
     value = accepted / dt
-    sample = (f"{n_steps} speculative steps (draft + 16-token verify + accept) of the config-3 workload from "
-              f"context {P}, {dt:.1f} s timed ({setup_s:.0f} s untimed set-up: seeded weights, prefill and the "
-              f"greedy trace behind the injected drafts, all on the CPU)")
+    sample = (f"{n_steps} speculative steps (draft + 16-token verify + accept) of the config-3 workload after "
+              f"{n_warm} untimed ones from context {P}, {dt:.1f} s timed ({setup_s:.0f} s untimed set-up: seeded "
+              f"weights, prefill and the greedy trace behind the injected drafts, all on the CPU)")
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": n_steps,
-            "warmup": 0, "ms_per_step": dt / n_steps * 1e3, "higher_is_better": True, "impl": "reference",
+            "warmup": n_warm, "ms_per_step": dt / n_steps * 1e3, "higher_is_better": True, "impl": "reference",
             "scaling": "weak", "dtype": "bf16",
             "data": "synthetic (random-init weights, random prompt, oracle-injected drafts)",
             "config": {"workload": f"config3: Qwen3-4B-shaped target ({args.layers} layers) + 5-layer DFlash draft, "

@@ -95,3 +95,28 @@ def test_step_abi_rejects_bad_arguments_without_a_device():
     for fn in ("dfl_draft_step", "dfl_verify_step", "dfl_rollback"):
         assert getattr(lib, fn)(None, None) == 1
     assert lib.dfl_ctx_destroy(None) == 0
+
+
+def test_fused_projection_appends_reject_bad_arguments_without_a_device():
+    """dfl_gemm_qkv_rope and dfl_gemm_kv_append_layers check their pointers, head geometry and
+    layer count (at most 16) before any CUDA call; the launch-count query answers on the
+    host for both (Hq = 0 with the layers' kv heads for the multi-layer form)."""
+    import ctypes
+    from dflash_b200 import _lib
+    from dflash_b200._lib import DFlashKernelError
+    d = ctypes.c_void_p(16)  # never dereferenced
+    with pytest.raises(DFlashKernelError) as e:  # null positions
+        _lib.call("dfl_gemm_qkv_rope", d, 2560, d, 16, 2560, None, None, 0, 1e-6, d, 6144, None, None, d, d, d, d, d,
+                  d, 0, 0, None, 0, 0, 32, 8, 128, d, 1 << 20, None)
+    assert e.value.status == 1
+    norms = (ctypes.c_void_p * 17)(*([16] * 17))
+    with pytest.raises(DFlashKernelError) as e:  # 17 layers
+        _lib.call("dfl_gemm_kv_append_layers", d, 2560, d, 16, 2560, None, None, 0, 1e-6, d, 17 * 2048, d, None,
+                  norms, d, d, d, 0, 0, 0, None, 0, 0, 17, 8, 128, d, 1 << 20, None)
+    assert e.value.status == 1 and "16 layers" in str(e.value)
+    lib = _lib.load()
+    assert lib.dfl_gemm_qkv_rope_launches(16, 2560, 32, 8, 128) == 1  # cluster form, one row tile
+    assert lib.dfl_gemm_qkv_rope_launches(20, 2560, 32, 8, 128) == 2  # two row tiles
+    assert lib.dfl_gemm_qkv_rope_launches(16, 256, 4, 2, 64) == 2  # head_dim 64
+    assert lib.dfl_gemm_qkv_rope_launches(16, 2560, 0, 40, 128) == 1  # five layers' context K/V
+    assert lib.dfl_gemm_qkv_rope_launches(16, 100, 32, 8, 128) == -1

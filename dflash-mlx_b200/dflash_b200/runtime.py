@@ -309,6 +309,13 @@ class SpecSession:
 
     def capture(self) -> None:
         """Captures the draft half and the verify half of a step as two CUDA graphs."""
+        # the step's activation buffers exist before the capture: one first made inside it
+        # would put its zero fill into the graph, to run again at every replay
+        M = self.B * self.bs
+        self.target.buffers(M)
+        if self.draft is not None:
+            for kind in ("ctx", "blk"):
+                self.draft.buffers(M, kind)
         s = torch.cuda.Stream(device=self.dev)
         s.wait_stream(torch.cuda.current_stream(self.dev))
         parts = [self._draft_kernels]

@@ -43,7 +43,15 @@ struct TpArgs {
   long long slab_stride;  // elements between a rank's K-range partial slabs
   int n_slabs;
   int rank, n_ranks, M, H;
+  // nullable: also write xn = RMSNorm(h) * norm_w (the next projection's input), so that
+  // projection needs no norm pass of its own
+  const __nv_bfloat16* norm_w;
+  __nv_bfloat16* xn;
+  long long ldxn;
+  float eps;
 };
+
+constexpr int TP_NORM_MAX_H = 8192;  // row width the norm-folding form holds in shared memory
 
 __device__ __forceinline__ void st_release_sys(int* p, int v) {
   asm volatile("st.release.sys.global.s32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
@@ -54,7 +62,48 @@ __device__ __forceinline__ int ld_acquire_sys(const int* p) {
   return v;
 }
 
+// Row m, columns c0 .. c0 + 7 (one lane): the sum over ranks (rank order, then slab order)
+// of the partials, h <- bf16(h + bf16(sum)), the tap copy; returns the lane's sum of squares
+// of the new h values.
+__device__ __forceinline__ float reduce_span(const TpArgs& a, int m, int c0) {
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  for (int j = 0; j < a.n_ranks; ++j)  // rank order, then slab order: the same sum on every rank
+    for (int sl = 0; sl < a.n_slabs; ++sl) {
+      const float4* pp =
+          reinterpret_cast<const float4*>(a.parts[j] + sl * a.slab_stride + (long long)m * a.H + c0);
+      const float4 p0 = __ldcg(pp), p1 = __ldcg(pp + 1);
+      acc[0] += p0.x;
+      acc[1] += p0.y;
+      acc[2] += p0.z;
+      acc[3] += p0.w;
+      acc[4] += p1.x;
+      acc[5] += p1.y;
+      acc[6] += p1.z;
+      acc[7] += p1.w;
+    }
+  __nv_bfloat16* hp = a.h + (long long)m * a.ldh + c0;
+  const uint4 hv = *reinterpret_cast<const uint4*>(hp);
+  const __nv_bfloat16* hb = reinterpret_cast<const __nv_bfloat16*>(&hv);
+  uint32_t pk[4];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; i += 2) {
+    const float y0 = bf2f(hb[i]) + round_bf16(acc[i]);
+    const float y1 = bf2f(hb[i + 1]) + round_bf16(acc[i + 1]);
+    pk[i / 2] = pack_bf16x2(y0, y1);
+    const float q0 = round_bf16(y0), q1 = round_bf16(y1);
+    ss += q0 * q0 + q1 * q1;
+  }
+  const uint4 out = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+  *reinterpret_cast<uint4*>(hp) = out;
+  if (a.tap) *reinterpret_cast<uint4*>(a.tap + (long long)m * a.ldtap + c0) = out;
+  return ss;
+}
+
 // one warp per (row, 256-column span): lane owns 8 consecutive columns
+template <bool NORM>
 __global__ void __launch_bounds__(256) tp_reduce_residual_kernel(TpArgs a) {
   grid_dependency_launch_dependents();
   grid_dependency_wait();
@@ -80,50 +129,56 @@ __global__ void __launch_bounds__(256) tp_reduce_residual_kernel(TpArgs a) {
     s_ok = ok;
   }
   __syncthreads();
-  if (s_ok) {
+  if (!NORM && s_ok) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int spans = a.H / 256;
     const long long item = (long long)blockIdx.x * (blockDim.x >> 5) + warp;
     for (long long it = item; it < (long long)a.M * spans; it += (long long)gridDim.x * (blockDim.x >> 5)) {
       const int m = (int)(it / spans), c0 = (int)(it % spans) * 256 + lane * 8;
-      float acc[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-      for (int j = 0; j < a.n_ranks; ++j)  // rank order, then slab order: the same sum on every rank
-        for (int sl = 0; sl < a.n_slabs; ++sl) {
-          const float4* pp =
-              reinterpret_cast<const float4*>(a.parts[j] + sl * a.slab_stride + (long long)m * a.H + c0);
-          const float4 p0 = __ldcg(pp), p1 = __ldcg(pp + 1);
-          acc[0] += p0.x;
-          acc[1] += p0.y;
-          acc[2] += p0.z;
-          acc[3] += p0.w;
-          acc[4] += p1.x;
-          acc[5] += p1.y;
-          acc[6] += p1.z;
-          acc[7] += p1.w;
-        }
-      __nv_bfloat16* hp = a.h + (long long)m * a.ldh + c0;
-      const uint4 hv = *reinterpret_cast<const uint4*>(hp);
-      const __nv_bfloat16* hb = reinterpret_cast<const __nv_bfloat16*>(&hv);
-      uint32_t pk[4];
-      float ss = 0.f;
-#pragma unroll
-      for (int i = 0; i < 8; i += 2) {
-        const float y0 = bf2f(hb[i]) + round_bf16(acc[i]);
-        const float y1 = bf2f(hb[i + 1]) + round_bf16(acc[i + 1]);
-        pk[i / 2] = pack_bf16x2(y0, y1);
-        const float q0 = round_bf16(y0), q1 = round_bf16(y1);
-        ss += q0 * q0 + q1 * q1;
-      }
-      const uint4 out = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-      *reinterpret_cast<uint4*>(hp) = out;
-      if (a.tap) *reinterpret_cast<uint4*>(a.tap + (long long)m * a.ldtap + c0) = out;
+      float ss = reduce_span(a, m, c0);
       if (a.sumsq_out) {  // four lanes cover one 32-column group
         ss += __shfl_xor_sync(0xffffffffu, ss, 1);
         ss += __shfl_xor_sync(0xffffffffu, ss, 2);
         if ((lane & 3) == 0) a.sumsq_out[(long long)m * (a.H / 32) + c0 / 32] = ss;
       }
+    }
+  }
+  if (NORM && s_ok) {
+    // one row at a time per CTA: the row's spans, its 32-column sums of squares into shared
+    // memory, their sum in column order (the norm prologue's order), then xn
+    __shared__ float s_part[TP_NORM_MAX_H / 32];
+    __shared__ float s_inv;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, warps = blockDim.x >> 5;
+    const int spans = a.H / 256, n_parts = a.H / 32;
+    for (int m = blockIdx.x; m < a.M; m += gridDim.x) {
+      for (int sp = warp; sp < spans; sp += warps) {
+        const int c0 = sp * 256 + lane * 8;
+        float ss = reduce_span(a, m, c0);
+        ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+        ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+        if ((lane & 3) == 0) {
+          s_part[c0 / 32] = ss;
+          if (a.sumsq_out) a.sumsq_out[(long long)m * n_parts + c0 / 32] = ss;
+        }
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        float ss = 0.f;
+        for (int p = 0; p < n_parts; ++p) ss += s_part[p];
+        s_inv = rsqrtf(ss / (float)a.H + a.eps);
+      }
+      __syncthreads();
+      const float inv = s_inv;
+      for (int k = threadIdx.x * 8; k < a.H; k += blockDim.x * 8) {
+        uint4 xv = *reinterpret_cast<const uint4*>(a.h + (long long)m * a.ldh + k);
+        const uint4 wv = *reinterpret_cast<const uint4*>(a.norm_w + k);
+        __nv_bfloat16* xe = reinterpret_cast<__nv_bfloat16*>(&xv);
+        const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) xe[e] = f2bf(bf2f(we[e]) * (bf2f(xe[e]) * inv));
+        *reinterpret_cast<uint4*>(a.xn + (long long)m * a.ldxn + k) = xv;
+      }
+      __syncthreads();
     }
   }
   // the last CTA advances the call counter for the next launch
@@ -192,9 +247,10 @@ extern "C" int dfl_tp_free(void* ptr) {
   return DFL_OK;
 }
 
-extern "C" int dfl_tp_reduce_residual(const void* const* parts, int* const* flags, int* epoch, int* done, int rank,
-                                      int n_ranks, int n_slabs, int64_t slab_stride, void* h, int64_t ldh, void* tap,
-                                      int64_t ldtap, float* sumsq_out, int M, int H, void* stream) {
+static int tp_reduce_impl(const void* const* parts, int* const* flags, int* epoch, int* done, int rank, int n_ranks,
+                          int n_slabs, int64_t slab_stride, void* h, int64_t ldh, void* tap, int64_t ldtap,
+                          float* sumsq_out, int M, int H, const void* norm_w, float eps, void* xn, int64_t ldxn,
+                          void* stream) {
   if (M == 0) return DFL_OK;
   if (!parts || !flags || !epoch || !done || !h || n_ranks < 1 || n_ranks > TP_MAX_RANKS || rank < 0 ||
       rank >= n_ranks || M < 0 || H <= 0 || n_slabs < 1 || (n_slabs > 1 && slab_stride < (long long)M * H) ||
@@ -225,7 +281,11 @@ extern "C" int dfl_tp_reduce_residual(const void* const* parts, int* const* flag
   a.n_ranks = n_ranks;
   a.M = M;
   a.H = H;
-  const long long items = (long long)M * (H / 256);
+  a.norm_w = static_cast<const __nv_bfloat16*>(norm_w);
+  a.xn = static_cast<__nv_bfloat16*>(xn);
+  a.ldxn = ldxn;
+  a.eps = eps;
+  const long long items = norm_w ? (long long)M * 8 : (long long)M * (H / 256);  // norm form: a row per CTA
   int blocks = (int)((items + 7) / 8);
   if (blocks > 148) blocks = 148;  // every CTA waits on the flags: keep the grid resident
   cudaLaunchAttribute attr[1];
@@ -237,10 +297,31 @@ extern "C" int dfl_tp_reduce_residual(const void* const* parts, int* const* flag
   cfg.stream = as_stream(stream);
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, tp_reduce_residual_kernel, a);
+  cudaError_t e = norm_w ? cudaLaunchKernelEx(&cfg, tp_reduce_residual_kernel<true>, a)
+                         : cudaLaunchKernelEx(&cfg, tp_reduce_residual_kernel<false>, a);
   if (e != cudaSuccess) {
     set_error("dfl_tp_reduce_residual: launch failed: %s", cudaGetErrorString(e));
     return DFL_ERR_CUDA;
   }
   return DFL_OK;
+}
+
+extern "C" int dfl_tp_reduce_residual(const void* const* parts, int* const* flags, int* epoch, int* done, int rank,
+                                      int n_ranks, int n_slabs, int64_t slab_stride, void* h, int64_t ldh, void* tap,
+                                      int64_t ldtap, float* sumsq_out, int M, int H, void* stream) {
+  return tp_reduce_impl(parts, flags, epoch, done, rank, n_ranks, n_slabs, slab_stride, h, ldh, tap, ldtap, sumsq_out,
+                        M, H, nullptr, 0.f, nullptr, 0, stream);
+}
+
+extern "C" int dfl_tp_reduce_residual_norm(const void* const* parts, int* const* flags, int* epoch, int* done,
+                                           int rank, int n_ranks, int n_slabs, int64_t slab_stride, void* h,
+                                           int64_t ldh, void* tap, int64_t ldtap, float* sumsq_out, int M, int H,
+                                           const void* norm_w, float eps, void* xn, int64_t ldxn, void* stream) {
+  if (M > 0 && (!norm_w || !xn || H > TP_NORM_MAX_H || ldxn % 8 || ldxn < H)) {
+    set_error("dfl_tp_reduce_residual_norm: needs norm_w, xn (row stride >= H, multiple of 8) and H <= %d",
+              TP_NORM_MAX_H);
+    return DFL_ERR_INVALID;
+  }
+  return tp_reduce_impl(parts, flags, epoch, done, rank, n_ranks, n_slabs, slab_stride, h, ldh, tap, ldtap, sumsq_out,
+                        M, H, norm_w, eps, xn, ldxn, stream);
 }

@@ -47,6 +47,9 @@ SIGNATURES: dict[str, tuple] = {
     "dfl_tp_free": (c_int, [c_void_p]),
     "dfl_tp_reduce_residual": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int64,
                                        c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int, c_int, c_void_p]),
+    "dfl_tp_reduce_residual_norm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int64,
+                                            c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int, c_int, c_void_p,
+                                            c_float, c_void_p, c_int64, c_void_p]),
     "dfl_packed_weight_bytes": (c_size_t, [c_int, c_int]),
     "dfl_gemm_noalloc_scratch_bytes": (c_size_t, []),
     "dfl_gemm_bf16_noalloc": (c_int, [c_void_p, c_int64, c_void_p, c_int, c_int, c_int, c_int, c_void_p, c_int64,

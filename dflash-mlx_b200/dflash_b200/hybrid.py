@@ -170,18 +170,29 @@ class HybridTargetModel:
                 "gon": torch.empty((M, self.vd), **bf),
                 "argmax": torch.empty((M, ops.argmax_tiles(c.vocab_size), 2), dtype=torch.float32, device=dev),
                 "ss": torch.zeros((M, H // 32), dtype=torch.float32, device=dev),
+                "xtp": torch.empty((M, H), **bf),  # tensor parallel: the all-sum's normed rows
             }
             self._bufs[M] = b
         return b
 
-    def _gdn_layer(self, lw, h, ss, b, cache: HybridCache, gi: int, seqs: slice, T: int, verify: bool, ws):
-        """One GDN layer over rows [B_s * T] (sequences `seqs` of the cache, T tokens each)."""
+    def _normed_gemm(self, h, xn, w, norm_w, ss, ws, epilogue=ops.EPI_STORE, out=None):
+        """A projection of RMSNorm(h) * norm_w: from the all-sum's normed rows ``xn`` when
+        tensor parallelism produced them (the same bits), else with the GEMM's own norm."""
+        eps = self.cfg.rms_norm_eps
+        if xn is not None:
+            return ops.gemm(xn, w, epilogue, out=out, ws=ws)
+        return ops.gemm(h, w, epilogue, out=out, ws=ws, norm_w=norm_w, sumsq_in=ss, eps=eps)
+
+    def _gdn_layer(self, lw, h, ss, b, cache: HybridCache, gi: int, seqs: slice, T: int, verify: bool, ws,
+                   xn=None, next_norm=None):
+        """One GDN layer over rows [B_s * T] (sequences `seqs` of the cache, T tokens each);
+        returns the all-sum's normed rows for ``next_norm`` under tensor parallelism."""
         c = self.cfg
         eps = c.rms_norm_eps
         Bs = (seqs.stop - seqs.start)
         M = Bs * T
         proj = b["proj"]
-        ops.gemm(h, lw["w_in"], out=proj, ws=ws, norm_w=lw["in_norm"], sumsq_in=ss, eps=eps)
+        self._normed_gemm(h, xn, lw["w_in"], lw["in_norm"], ss, ws, out=proj)
         win = cache.window[gi][seqs]
         replay = verify and cache.mode == "replay"
         if replay:
@@ -211,21 +222,28 @@ class HybridTargetModel:
                                b["gbeta"].view(Bs, T, self.Hv), st, state_out=st, o=o.view(Bs, T, self.Hv, self.Dv))
         z = proj[:, self.C:self.C + self.vd]
         ops.gated_rmsnorm(b["go"], z, lw["gnorm"], self.Hv, self.Dv, eps, out=b["gon"])
-        self._row_parallel(b["gon"], lw["w_out"], h, ss, None, ws, parity=0)
+        return self._row_parallel(b["gon"], lw["w_out"], h, ss, None, ws, parity=0, next_norm=next_norm,
+                                  xn_out=b["xtp"])
 
-    def _row_parallel(self, x, w, h, ss, tap, ws, parity: int) -> None:
+    def _row_parallel(self, x, w, h, ss, tap, ws, parity: int, next_norm=None, xn_out=None):
         """h <- h + x @ w.T (out_proj / o_proj / down_proj): fused residual epilogue on one
-        GPU; with tensor parallelism this rank's partial, then the all-sum + residual."""
+        GPU; with tensor parallelism this rank's partial, then the all-sum + residual, which
+        also writes RMSNorm(h) * next_norm into ``xn_out`` for the projection that follows
+        (returned; None on one GPU, where that projection norms its own input)."""
         if self.tp is None:
             ops.gemm(x, w, ops.EPI_RESIDUAL, residual=h, out=h, out2=tap, ws=ws, sumsq_out=ss)
-            return
+            return None
         M = x.shape[0]
         # one fp32 partial per rank: a split-K GEMM sums its K ranges locally first, so
         # the peers read one slab each over NVLink (handing them the unsummed K-range
         # slabs, DFL_EPI_PARTIALS, saves that launch but multiplies the NVLink bytes by
         # the split: slower from 2 ranks on, 0.7x at 4)
         ops.gemm(x, w, ops.EPI_STORE_F32, out=self.tp.partial(parity, M), ws=ws)
-        self.tp.reduce_residual(parity, h, tap, ss, M)
+        if next_norm is None or xn_out is None:
+            self.tp.reduce_residual(parity, h, tap, ss, M)
+            return None
+        self.tp.reduce_residual(parity, h, tap, ss, M, norm_w=next_norm, eps=self.cfg.rms_norm_eps, xn=xn_out[:M])
+        return xn_out[:M]
 
     def forward(self, tokens: torch.Tensor, pos: torch.Tensor, cache: HybridCache, max_kv: int,
                 layer_ids: list[int] | None = None, taps_out: torch.Tensor | None = None,
@@ -248,30 +266,36 @@ class HybridTargetModel:
         tap_col = {lid: i for i, lid in enumerate(sorted(layer_ids or []))}
         h, ss, eps = b["h"], b["ss"], c.rms_norm_eps
         ops.embed(tokens, self.embed_w, out=h, sumsq_out=ss)
+        xn = None  # tensor parallel: the all-sum's normed rows for the next projection
         for l, lw in enumerate(self.layers):
             if self.kinds[l] == "gdn":
-                self._gdn_layer(lw, h, ss, b, cache, self.gdn_index[l], seqs, T, verify, ws)
+                xn = self._gdn_layer(lw, h, ss, b, cache, self.gdn_index[l], seqs, T, verify, ws, xn=xn,
+                                     next_norm=lw["post_norm"])
             else:
                 kc, vc = cache.kv.layer(self.attn_index[l])
-                ops.gemm(h, lw["w_qkv"], out=b["qkv"], ws=ws, norm_w=lw["in_norm"], sumsq_in=ss, eps=eps)
+                self._normed_gemm(h, xn, lw["w_qkv"], lw["in_norm"], ss, ws, out=b["qkv"])
                 qkv = b["qkv"][:, :(2 * Hq + 2 * Hkv) * hd]
                 ops.qkv_rope_append(qkv, pos, lw["q_norm"], lw["k_norm"], self.inv_freq, kc, vc, Hq, Hkv, hd,
                                     c.rope_dim, eps, q_out=b["q"], row_seq=row_seq, q_stride=2 * hd)
                 ops.attention(b["q"], kc, vc, pos, causal=True, max_kv=max_kv, row_seq=row_seq, out=b["attn"],
                               seq_rows=seq_rows or T, key_chunk=key_chunk,
                               ws=ws, gate=qkv[:, hd:], gate_head_stride=2 * hd)
-                self._row_parallel(b["attn"], lw["w_o"], h, ss, None, ws, parity=0)
-            ops.gemm(h, lw["w_gu"], ops.EPI_SILU_MUL, out=b["act"], ws=ws, norm_w=lw["post_norm"], sumsq_in=ss,
-                     eps=eps)
+                xn = self._row_parallel(b["attn"], lw["w_o"], h, ss, None, ws, parity=0, next_norm=lw["post_norm"],
+                                        xn_out=b["xtp"])
+            self._normed_gemm(h, xn, lw["w_gu"], lw["post_norm"], ss, ws, ops.EPI_SILU_MUL, out=b["act"])
             tap = None
             if l in tap_col and taps_out is not None:
                 i = tap_col[l]
                 tap = taps_out[:, i * H:(i + 1) * H]
-            self._row_parallel(b["act"], lw["w_down"], h, ss, tap, ws, parity=1)
+            nxt = self.layers[l + 1]["in_norm"] if l + 1 < len(self.layers) else (
+                self.norm_w if head != "hidden" else None)
+            xn = self._row_parallel(b["act"], lw["w_down"], h, ss, tap, ws, parity=1, next_norm=nxt, xn_out=b["xtp"])
         if head == "hidden":
             return ops.rmsnorm(h, self.norm_w, eps, out=b["xn"])
         if head == "logits":
-            return ops.gemm(h, self.lm_head_w, ws=ws, norm_w=self.norm_w, sumsq_in=ss, eps=eps)
+            return self._normed_gemm(h, xn, self.lm_head_w, self.norm_w, ss, ws)
+        if xn is not None:
+            return ops.gemm(xn, self.lm_head_w, ops.EPI_ARGMAX, argmax_partials=b["argmax"], ws=ws)
         return ops.gemm(h, self.lm_head_w, ops.EPI_ARGMAX, argmax_partials=b["argmax"], ws=ws, norm_w=self.norm_w,
                         sumsq_in=ss, eps=eps)
 

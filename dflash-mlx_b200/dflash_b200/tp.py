@@ -174,15 +174,20 @@ class TPComm:
         return v.view(M, self.hidden) if slabs == 1 else v.view(slabs, M, self.hidden)
 
     def reduce_residual(self, parity: int, h: torch.Tensor, tap: torch.Tensor | None, sumsq_out: torch.Tensor | None,
-                        M: int, slabs: int = 1) -> None:
+                        M: int, slabs: int = 1, norm_w: torch.Tensor | None = None, eps: float = 0.0,
+                        xn: torch.Tensor | None = None) -> None:
         """h[:M] <- h + sum over ranks (and K-range slabs) of the parity slot; tap copy;
-        row sums of squares."""
+        row sums of squares; with norm_w, also xn = RMSNorm(h) * norm_w (the next
+        projection's input, the same bits as that projection's own norm)."""
         from .ops import _ptr, _row_stride, _stream
-        _lib.call("dfl_tp_reduce_residual", self.parts_arr[parity], self.flags_arr,
-                  self.counters.data_ptr(), self.counters.data_ptr() + 4, self.rank, self.size, slabs,
-                  M * self.hidden, _ptr(h),
-                  _row_stride(h), _ptr(tap), _row_stride(tap) if tap is not None else 0, _ptr(sumsq_out), M,
-                  self.hidden, _stream())
+        args = (self.parts_arr[parity], self.flags_arr, self.counters.data_ptr(), self.counters.data_ptr() + 4,
+                self.rank, self.size, slabs, M * self.hidden, _ptr(h), _row_stride(h), _ptr(tap),
+                _row_stride(tap) if tap is not None else 0, _ptr(sumsq_out), M, self.hidden)
+        if norm_w is None:
+            _lib.call("dfl_tp_reduce_residual", *args, _stream())
+        else:
+            _lib.call("dfl_tp_reduce_residual_norm", *args, _ptr(norm_w), float(eps), _ptr(xn), _row_stride(xn),
+                      _stream())
 
     def close(self) -> None:
         for j, p in enumerate(self.peers):

@@ -162,6 +162,14 @@ int dfl_tp_free(void* ptr);
 int dfl_tp_reduce_residual(const void* const* parts, int* const* flags, int* epoch, int* done, int rank, int n_ranks,
                            int n_slabs, int64_t slab_stride, void* h, int64_t ldh, void* tap, int64_t ldtap,
                            float* sumsq_out, int M, int H, void* stream);
+/* dfl_tp_reduce_residual that also writes xn = RMSNorm(h) * norm_w (row stride ldxn, the
+ * input RMSNorm of the projection that follows: the reference's post_attention_layernorm /
+ * next layer's input_layernorm after the all-reduce, custom_qwen35_model.py:810), each CTA
+ * taking whole rows; the same bits as the GEMM's own norm from sumsq_out. H <= 8192. */
+int dfl_tp_reduce_residual_norm(const void* const* parts, int* const* flags, int* epoch, int* done, int rank,
+                                int n_ranks, int n_slabs, int64_t slab_stride, void* h, int64_t ldh, void* tap,
+                                int64_t ldtap, float* sumsq_out, int M, int H, const void* norm_w, float eps, void* xn,
+                                int64_t ldxn, void* stream);
 
 /* Reads (and optionally clears) the device error record: non-zero when a kernel's
  * bounded wait gave up (the kernel returned instead of hanging). Synchronises

@@ -120,3 +120,17 @@ def test_fused_projection_appends_reject_bad_arguments_without_a_device():
     assert lib.dfl_gemm_qkv_rope_launches(16, 256, 4, 2, 64) == 2  # head_dim 64
     assert lib.dfl_gemm_qkv_rope_launches(16, 2560, 0, 40, 128) == 1  # five layers' context K/V
     assert lib.dfl_gemm_qkv_rope_launches(16, 100, 32, 8, 128) == -1
+
+
+def test_tp_all_sum_norm_rejects_bad_arguments_without_a_device():
+    """dfl_tp_reduce_residual_norm needs the norm weight, an output for the normed rows and a
+    row width its shared memory holds (H <= 8192); it says so before any CUDA call."""
+    import ctypes
+    from dflash_b200 import _lib
+    from dflash_b200._lib import DFlashKernelError
+    d = ctypes.c_void_p(16)  # never dereferenced
+    for norm_w, xn, H in ((None, d, 512), (d, None, 512), (d, d, 16384)):
+        with pytest.raises(DFlashKernelError) as e:
+            _lib.call("dfl_tp_reduce_residual_norm", d, d, d, d, 0, 1, 1, 0, d, H, None, 0, None, 4, H, norm_w, 1e-6,
+                      xn, H, None)
+        assert e.value.status == 1 and "8192" in str(e.value)

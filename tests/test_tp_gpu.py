@@ -72,3 +72,47 @@ def test_tp_all_sum_wait_gives_up_and_reports(lib):
     assert lib.dfl_device_error(ctypes.byref(code), 1, stream) == 0 and code.value == 0
     ref = (h0.float() + part0.to(torch.bfloat16).float()).to(torch.bfloat16)
     assert torch.equal(h, ref)
+
+
+@pytest.mark.parametrize("M", [128, 16])
+def test_tp_all_sum_norm_rows_equal_the_projection_norm(lib, M):
+    """One GPU, one rank: dfl_tp_reduce_residual_norm gives the same h, tap and sums of
+    squares as dfl_tp_reduce_residual, and its normed rows fed to a projection without a
+    norm give the same bits as that projection norming h itself (wide form at 128 rows,
+    weight-streaming form at 16), the claim that lets the tensor-parallel forward skip the
+    projection's norm pass."""
+    from dflash_b200 import ops
+    from dflash_b200.tp import TPComm
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    dev = torch.device("cuda")
+    H, N = 5120, 2048
+    g = torch.Generator(device=dev).manual_seed(5)
+    h0 = torch.randn((M, H), generator=g, device=dev).bfloat16()
+    part = torch.randn((M, H), generator=g, device=dev) * 0.5
+    nw = (1.0 + 0.1 * torch.randn((H,), generator=g, device=dev)).bfloat16()
+    w = ops.PackedWeight((torch.randn((N, H), generator=g, device=dev) * 0.02).bfloat16())
+    comm = TPComm(0, 1, dev, max_rows=M, hidden=H)
+    try:
+        outs = []
+        for with_norm in (False, True):
+            h = h0.clone()
+            tap = torch.empty_like(h)
+            ss = torch.empty((M, H // 32), dtype=torch.float32, device=dev)
+            xn = torch.empty_like(h)
+            comm.partial(0, M).copy_(part)
+            if with_norm:
+                comm.reduce_residual(0, h, tap, ss, M, norm_w=nw, eps=1e-6, xn=xn)
+            else:
+                comm.reduce_residual(0, h, tap, ss, M)
+            torch.cuda.synchronize()
+            outs.append((h, tap, ss, xn))
+        assert ops.device_error() == 0
+        (h_a, tap_a, ss_a, _), (h_b, tap_b, ss_b, xn_b) = outs
+        assert torch.equal(h_a, h_b) and torch.equal(tap_a, tap_b) and torch.equal(ss_a, ss_b)
+        ws = ops.Workspace(dev, wide=M > 16)
+        y_norm = ops.gemm(h_a, w, ws=ws, norm_w=nw, sumsq_in=ss_a, eps=1e-6)
+        y_rows = ops.gemm(xn_b, w, ws=ws)
+        assert torch.equal(y_norm, y_rows)
+    finally:
+        comm.close()

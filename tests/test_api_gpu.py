@@ -122,3 +122,25 @@ def test_openai_batching_runner_concurrent_requests(gen):
         assert got[i].text == want[i].text and got[i].completion_tokens == want[i].completion_tokens
         assert got[i].finish_reason == want[i].finish_reason
         assert got[i].prompt_tokens == want[i].prompt_tokens
+
+
+@pytest.mark.parametrize("n", [0, 1, 2])
+def test_short_generations_follow_the_reference_limits(gen, n):
+    """max_new_tokens 0, 1, 2 (runtime.py:376-404, 517-521): no generated token at 0 (and no
+    token event), else exactly the first n tokens of the plain greedy decode; the stream's
+    token events reassemble them and the last event is the finished one."""
+    prompt = list(range(9, 30))
+    plain = gen.generate_from_tokens(prompt, max_new_tokens=5, speculative_tokens=1)
+    res = gen.generate_from_tokens(prompt, max_new_tokens=n)
+    assert res.generated_tokens == plain.generated_tokens[:n]
+    assert res.metrics["num_output_tokens"] == n
+    events = list(gen.stream_from_tokens(prompt, max_new_tokens=n))
+    assert [t for e in events for t in e.token_ids] == plain.generated_tokens[:n]
+    assert events[-1].finished
+
+
+def test_one_token_prompt_is_lossless(gen):
+    res = gen.generate_from_tokens([17], max_new_tokens=24)
+    plain = gen.generate_from_tokens([17], max_new_tokens=24, speculative_tokens=1)
+    assert res.output_tokens == plain.output_tokens
+    assert len(res.generated_tokens) == 24

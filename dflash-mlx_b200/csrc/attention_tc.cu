@@ -14,9 +14,9 @@
 // The running maximum is rescaled lazily: O and the row sum are rescaled only when a
 // row's maximum grows by more than 8 (log2 units) over the one the exponentials use, and
 // the final division and the chunk merge use that maximum -- exact, and the same for a
-// row whatever other rows share the tile. V arrives from the cache key-major ([key][dim]);
-// two warps transpose each block into the K-major [dim][key] image the MMA reads.
-// Warp roles: 0 TMA producer, 1 MMA issuer, 2-3 V transpose, 4-5 softmax and epilogue.
+// row whatever other rows share the tile. V arrives from the cache as [key][dim] and the
+// P V product reads it so, as an MN-major B operand (no transpose).
+// Warp roles: 0 TMA producer, 1 MMA issuer, 2-3 idle, 4-5 softmax and epilogue.
 // K/V come through 3-D tensor maps (dims, key rows, (sequence or page) x kv head planes),
 // so a block past a head's last row reads zeros instead of another head's keys. Every
 // wait is bounded (device error 320-329).
@@ -36,16 +36,16 @@ constexpr int AT_UNIT = 128 * 128;        // one [128 rows x 128 B] swizzled uni
 constexpr int AT_OFF_Q = 0;               // 2 units: dims 0-63, 64-127
 constexpr int AT_OFF_K = 2 * AT_UNIT;     // 2 stages x 2 halves x [64 keys x 128 B]
 constexpr int AT_OFF_V = 4 * AT_UNIT;     // 2 stages x 2 halves x [64 keys x 128 B]
-constexpr int AT_OFF_VT = 6 * AT_UNIT;    // 2 buffers x [128 dims x 64 keys]
-constexpr int AT_OFF_P = 8 * AT_UNIT;     // high unit, low unit
-constexpr int AT_OFF_BAR = 10 * AT_UNIT;
+constexpr int AT_OFF_P = 6 * AT_UNIT;     // high unit, low unit
+constexpr int AT_OFF_BAR = 8 * AT_UNIT;
 constexpr int AT_NBAR = 24;
 constexpr int AT_SMEM = AT_OFF_BAR + AT_NBAR * 8 + 16 + 1024;
 constexpr int AT_THREADS = 192;
 constexpr uint32_t AT_TMEM_COLS = 256;    // S double buffer (2 x 64) + O (128)
 // kind::f16, A = B = bf16, D = f32, K-major; M = 128; N = 64 (S) or 128 (O)
 constexpr uint32_t AT_IDESC_S = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(64 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-constexpr uint32_t AT_IDESC_O = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(128 >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
+constexpr uint32_t AT_IDESC_O = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((uint32_t)(128 >> 3) << 17) |
+                                  ((uint32_t)(128 >> 4) << 24);  // B (V) MN-major
 constexpr float AT_RESCALE = 8.f;         // lazy rescale threshold (log2 units)
 
 struct AttnTcArgs {
@@ -91,9 +91,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1) attn_tc_kernel(const __grid_con
   uint64_t* k_full = bars;       // [2]
   uint64_t* k_empty = bars + 2;  // [2]
   uint64_t* v_full = bars + 4;   // [2]
-  uint64_t* v_empty = bars + 6;  // [2] 64 transposer arrivals
-  uint64_t* vt_full = bars + 8;  // [2] 64 transposer arrivals
-  uint64_t* vt_free = bars + 10; // [2] MMA commit
+  uint64_t* v_empty = bars + 6;  // [2] MMA commit (the P V products read the stage)
   uint64_t* s_full = bars + 12;  // [2] MMA commit
   uint64_t* s_free = bars + 14;  // [2] 64 softmax arrivals
   uint64_t* p_full = bars + 16;  // 64 softmax arrivals
@@ -167,9 +165,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1) attn_tc_kernel(const __grid_con
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
       mbar_init(&v_full[s], 1);
-      mbar_init(&v_empty[s], 64);
-      mbar_init(&vt_full[s], 64);
-      mbar_init(&vt_free[s], 1);
+      mbar_init(&v_empty[s], 1);
       mbar_init(&s_full[s], 1);
       mbar_init(&s_free[s], 64);
     }
@@ -226,17 +222,20 @@ __global__ void __launch_bounds__(AT_THREADS, 1) attn_tc_kernel(const __grid_con
       const uint32_t q0 = smem_u32(smem + AT_OFF_Q);
       auto mma2 = [&](int j) -> bool {  // O += P V for block j (high, then low part of P)
         if (!mbar_wait(p_full, j & 1, 322, a.err)) return false;
-        if (!mbar_wait(&vt_full[j & 1], (j >> 1) & 1, 323, a.err)) return false;
+        if (!mbar_wait(&v_full[j & 1], (j >> 1) & 1, 323, a.err)) return false;
         tc_fence_after();
-        const uint32_t vt = smem_u32(smem + AT_OFF_VT + (j & 1) * AT_UNIT);
+        // V as loaded, [key][dim] in two 64-dim halves of 8 KB: MN-major B, atoms of 8 keys x
+        // 64 dims (1 KB) -- the next 8 keys 1 KB on, the next 64 dims 8 KB on; 16 keys a step
+        const uint32_t vb = smem_u32(smem + AT_OFF_V + (j & 1) * 2 * 8192);
         for (int part = 0; part < 2; ++part) {
           const uint32_t p0 = smem_u32(smem + AT_OFF_P + part * AT_UNIT);
 #pragma unroll
           for (int kk = 0; kk < AT_KB / 16; ++kk)
-            tc_mma(t_o, sw128_desc(p0) + 2 * kk, sw128_desc(vt) + 2 * kk, AT_IDESC_O, (j > 0 || part > 0 || kk > 0) ? 1u : 0u);
+            tc_mma(t_o, sw128_desc(p0) + 2 * kk, sw128_mn_desc(vb + kk * 2048, 8192, 1024), AT_IDESC_O,
+                   (j > 0 || part > 0 || kk > 0) ? 1u : 0u);
         }
         tc_commit(p_free);
-        tc_commit(&vt_free[j & 1]);
+        tc_commit(&v_empty[j & 1]);
         return true;
       };
       bool ok = true;
@@ -259,36 +258,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1) attn_tc_kernel(const __grid_con
     }
     __syncwarp();
   } else if (warp < 4) {
-    // ---------------- V transpose: [key][dim] (two 64-dim halves) -> [dim][key] ----------------
-    const int t = threadIdx.x - 64;  // 0..63: dims t and t + 64
-    for (int i = 0; i < n_blocks; ++i) {
-      const int s = i & 1;
-      if (!mbar_wait(&v_full[s], (i >> 1) & 1, 326, a.err)) break;
-      if (!mbar_wait(&vt_free[s], ((i >> 1) & 1) ^ 1, 327, a.err)) break;
-      const unsigned char* vs = smem + AT_OFF_V + s * 2 * 8192;
-      unsigned char* vt = smem + AT_OFF_VT + s * AT_UNIT;
-#pragma unroll
-      for (int dd = 0; dd < 2; ++dd) {
-        const int d = t + dd * 64;
-        const unsigned char* half = vs + dd * 8192;
-        const int dc = (d & 63) >> 3, de = (d & 7) * 2;
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {  // keys 8c .. 8c + 7
-          uint16_t e[8];
-#pragma unroll
-          for (int k = 0; k < 8; ++k) e[k] = *reinterpret_cast<const uint16_t*>(half + sw_off(8 * c + k, dc) + de);
-          uint4 v;
-          v.x = (uint32_t)e[0] | ((uint32_t)e[1] << 16);
-          v.y = (uint32_t)e[2] | ((uint32_t)e[3] << 16);
-          v.z = (uint32_t)e[4] | ((uint32_t)e[5] << 16);
-          v.w = (uint32_t)e[6] | ((uint32_t)e[7] << 16);
-          *reinterpret_cast<uint4*>(vt + sw_off(d, c)) = v;
-        }
-      }
-      fence_proxy_async_smem();
-      mbar_arrive(&v_empty[s]);
-      mbar_arrive(&vt_full[s]);
-    }
+    // warps 2-3: idle (the P V product reads V as loaded, MN-major)
   } else {
     // ---------------- softmax (one thread per row, TMEM lanes 0-63) and epilogue ----------------
     const int r = threadIdx.x - 128;  // row of the MMA tile: head hl = r / 16, token tr = r % 16

@@ -14,6 +14,15 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   const uint32_t hi = (1024u >> 4) | (1u << 14) | (2u << 29);
   return ((uint64_t)hi << 32) | lo;
 }
+// MN-major, 128-byte-swizzle descriptor (an operand whose MN dimension is contiguous, as a
+// V tile read from the cache as [key][dim] is for P V): swizzle atoms of 8 K-rows x 64
+// elements (1 KB); lbo = byte offset between atoms along MN, sbo = between 8-row groups
+// along K.
+__device__ __forceinline__ uint64_t sw128_mn_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  const uint32_t lo = ((saddr >> 4) & 0x3FFFu) | (((lbo >> 4) & 0x3FFFu) << 16);
+  const uint32_t hi = ((sbo >> 4) & 0x3FFFu) | (1u << 14) | (2u << 29);
+  return ((uint64_t)hi << 32) | lo;
+}
 __device__ __forceinline__ void tc_mma(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
   asm volatile(
       "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"

@@ -7,8 +7,9 @@
 // x 16 rows form the rows 0 .. 16G-1 of a 128-row MMA tile (the rest zero). Per 64-key
 // block of the chunk:
 //   S = Q K^T       tcgen05.mma, M = 128 rows, N = 64 keys, K = 128 dims, into TMEM
-//   P = exp2(S - m) softmax warps, one thread per row (TMEM lane), written to shared
-//                   memory as a bf16 high part and a bf16 low part (about 16 significant
+//   P = exp2(S - m) softmax warps, one thread per row (TMEM lane), written to one of two
+//                   shared-memory buffers (the next block's softmax overlaps this block's
+//                   P V) as a bf16 high part and a bf16 low part (about 16 significant
 //                   bits: the reference's fp32 softmax weights, not a single bf16 rounding)
 //   O += P V        tcgen05.mma, N = 128 dims, K = 64 keys, twice (high, low), in TMEM
 // The running maximum is rescaled lazily: O and the row sum are rescaled only when a
@@ -36,8 +37,8 @@ constexpr int AT_UNIT = 128 * 128;        // one [128 rows x 128 B] swizzled uni
 constexpr int AT_OFF_Q = 0;               // 2 units: dims 0-63, 64-127
 constexpr int AT_OFF_K = 2 * AT_UNIT;     // 2 stages x 2 halves x [64 keys x 128 B]
 constexpr int AT_OFF_V = 4 * AT_UNIT;     // 2 stages x 2 halves x [64 keys x 128 B]
-constexpr int AT_OFF_P = 6 * AT_UNIT;     // high unit, low unit
-constexpr int AT_OFF_BAR = 8 * AT_UNIT;
+constexpr int AT_OFF_P = 6 * AT_UNIT;     // 2 buffers x (high unit, low unit)
+constexpr int AT_OFF_BAR = 10 * AT_UNIT;
 constexpr int AT_NBAR = 24;
 constexpr int AT_SMEM = AT_OFF_BAR + AT_NBAR * 8 + 16 + 1024;
 constexpr int AT_THREADS = 192;
@@ -94,8 +95,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1) attn_tc_kernel(const __grid_con
   uint64_t* v_empty = bars + 6;  // [2] MMA commit (the P V products read the stage)
   uint64_t* s_full = bars + 12;  // [2] MMA commit
   uint64_t* s_free = bars + 14;  // [2] 64 softmax arrivals
-  uint64_t* p_full = bars + 16;  // 64 softmax arrivals
-  uint64_t* p_free = bars + 17;  // MMA commit (also: O complete up to that block)
+  uint64_t* p_full = bars + 16;  // [2] 64 softmax arrivals
+  uint64_t* p_free = bars + 18;  // [2] MMA commit (also: O complete up to that block)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + AT_OFF_BAR + AT_NBAR * 8);
 
   __shared__ int s_lim[16];
@@ -155,7 +156,7 @@ __global__ void __launch_bounds__(AT_THREADS, 1) attn_tc_kernel(const __grid_con
         v = *reinterpret_cast<const uint4*>(a.q + ((long long)(m0 + r) * a.Hq + kvh * G + hl) * AT_HD + c * 8);
       *reinterpret_cast<uint4*>(smem + AT_OFF_Q + (c >> 3) * AT_UNIT + sw_off(row, c & 7)) = v;
     }
-    for (int idx = threadIdx.x; idx < 2 * 64 * 8; idx += AT_THREADS) {  // P rows 64-127, both units
+    for (int idx = threadIdx.x; idx < 4 * 64 * 8; idx += AT_THREADS) {  // P rows 64-127, all four units
       const int u = idx / 512, rr = 64 + (idx % 512) / 8, c = idx % 8;
       *reinterpret_cast<uint4*>(smem + AT_OFF_P + u * AT_UNIT + sw_off(rr, c)) = make_uint4(0, 0, 0, 0);
     }
@@ -169,8 +170,10 @@ __global__ void __launch_bounds__(AT_THREADS, 1) attn_tc_kernel(const __grid_con
       mbar_init(&s_full[s], 1);
       mbar_init(&s_free[s], 64);
     }
-    mbar_init(p_full, 64);
-    mbar_init(p_free, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&p_full[s], 64);
+      mbar_init(&p_free[s], 1);
+    }
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -221,20 +224,20 @@ __global__ void __launch_bounds__(AT_THREADS, 1) attn_tc_kernel(const __grid_con
     if (lane == 0) {
       const uint32_t q0 = smem_u32(smem + AT_OFF_Q);
       auto mma2 = [&](int j) -> bool {  // O += P V for block j (high, then low part of P)
-        if (!mbar_wait(p_full, j & 1, 322, a.err)) return false;
+        if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, 322, a.err)) return false;
         if (!mbar_wait(&v_full[j & 1], (j >> 1) & 1, 323, a.err)) return false;
         tc_fence_after();
         // V as loaded, [key][dim] in two 64-dim halves of 8 KB: MN-major B, atoms of 8 keys x
         // 64 dims (1 KB) -- the next 8 keys 1 KB on, the next 64 dims 8 KB on; 16 keys a step
         const uint32_t vb = smem_u32(smem + AT_OFF_V + (j & 1) * 2 * 8192);
         for (int part = 0; part < 2; ++part) {
-          const uint32_t p0 = smem_u32(smem + AT_OFF_P + part * AT_UNIT);
+          const uint32_t p0 = smem_u32(smem + AT_OFF_P + ((j & 1) * 2 + part) * AT_UNIT);
 #pragma unroll
           for (int kk = 0; kk < AT_KB / 16; ++kk)
             tc_mma(t_o, sw128_desc(p0) + 2 * kk, sw128_mn_desc(vb + kk * 2048, 8192, 1024), AT_IDESC_O,
                    (j > 0 || part > 0 || kk > 0) ? 1u : 0u);
         }
-        tc_commit(p_free);
+        tc_commit(&p_free[j & 1]);
         tc_commit(&v_empty[j & 1]);
         return true;
       };
@@ -285,8 +288,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1) attn_tc_kernel(const __grid_con
         sv[c] = (key < lim && key < k_end) ? sv[c] * a.scale_log2 : -INFINITY;
         mx = fmaxf(mx, sv[c]);
       }
-      // P of the previous block has been read and O is complete up to it
-      if (i > 0 && !mbar_wait(p_free, (i - 1) & 1, 329, a.err)) { ok = false; break; }
+      // P buffer i & 1 is free once the P V product of block i - 2 has read it
+      if (i > 1 && !mbar_wait(&p_free[i & 1], ((i - 2) >> 1) & 1, 329, a.err)) { ok = false; break; }
       // tcgen05.ld / st are warp-collective: the warp rescales O together whenever any of
       // its rows needs it, rows that do not with factor 1 (exact)
       const bool resc = mx > m_used + AT_RESCALE || (m_used == -INFINITY && mx > -INFINITY);
@@ -296,6 +299,8 @@ __global__ void __launch_bounds__(AT_THREADS, 1) attn_tc_kernel(const __grid_con
         m_used = mx;
       }
       if (i > 0 && __any_sync(0xffffffffu, resc)) {
+        // O must be complete up to block i - 1 before it is rescaled
+        if (!mbar_wait(&p_free[(i - 1) & 1], ((i - 1) >> 1) & 1, 330, a.err)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int q8 = 0; q8 < 8; ++q8) {
@@ -320,16 +325,18 @@ __global__ void __launch_bounds__(AT_THREADS, 1) attn_tc_kernel(const __grid_con
           hi[u] = pack_bf16x2(h0, h1);
           lo[u] = pack_bf16x2(p0 - h0, p1 - h1);
         }
-        *reinterpret_cast<uint4*>(smem + AT_OFF_P + sw_off(r, c8)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        *reinterpret_cast<uint4*>(smem + AT_OFF_P + AT_UNIT + sw_off(r, c8)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        unsigned char* pb = smem + AT_OFF_P + (i & 1) * 2 * AT_UNIT;
+        *reinterpret_cast<uint4*>(pb + sw_off(r, c8)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4*>(pb + AT_UNIT + sw_off(r, c8)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
       }
       l += ps;
       fence_proxy_async_smem();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[i & 1]);
     }
     // epilogue: O of this row once the last P V product completed (every thread of the warp
     // loads its TMEM lane -- the loads are warp-collective -- and valid rows store)
-    if (__all_sync(0xffffffffu, ok) && mbar_wait(p_free, (n_blocks - 1) & 1, 329, a.err)) {
+    if (__all_sync(0xffffffffu, ok) &&
+        mbar_wait(&p_free[(n_blocks - 1) & 1], ((n_blocks - 1) >> 1) & 1, 329, a.err)) {
       tc_fence_after();
       const bool store = real && lim > k_begin && m0 + tr < a.M;
       const int m = m0 + tr, h = kvh * G + hl;
